@@ -1,0 +1,176 @@
+// Kernel parameter blocks and launchers of the verify-step backend.
+//
+// Data layout in HBM (one model):
+//   * weights: every quantized matrix is repacked at load into "pair tiles"
+//     of 32 rows x KT columns laid out in mma-fragment order (see qgemv.cu);
+//     the byte count equals the GGUF byte count (same bits per weight).
+//   * residual stream h: f32 [M][H].
+//   * activation operand of every GEMV: f16 (bf16 for BF16 models) values in
+//     m16n8k16 B-fragment order, plus per-16 / per-32 column sums of those
+//     rounded values (xsum16 / xsum32) used to cancel the code offsets.
+//   * KV cache: f16 (bf16 for BF16 models) [layer][kv_head][t][head_dim], K and
+//     V in separate arenas; rows beyond the live length hold finite stale data.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace specb200 {
+
+// Error bits reported through the per-model device error word.
+enum DevError : unsigned {
+  DEV_ERR_MBAR_TIMEOUT = 1u << 0,   // an mbarrier wait gave up
+  DEV_ERR_BAD_ARGUMENT = 1u << 1,   // a kernel saw an out-of-range index
+};
+
+// GGML type ids (public GGUF specification) of the weight formats handled.
+enum WFmt : int { WF_F32 = 0, WF_F16 = 1, WF_Q8_0 = 8, WF_Q4_K = 12, WF_Q5_K = 13, WF_Q6_K = 14, WF_BF16 = 30 };
+
+// Columns per tile and bytes per 16-row tile of each repacked format.
+__host__ __device__ constexpr int fmt_kt(int f) { return f == WF_Q8_0 ? 128 : (f == WF_BF16 ? 128 : 256); }
+__host__ __device__ constexpr int fmt_tile_bytes(int f) {
+  return f == WF_Q4_K ? 2304 : f == WF_Q5_K ? 2816 : f == WF_Q6_K ? 3360 : f == WF_Q8_0 ? 2176 : f == WF_BF16 ? 4096 : 0;
+}
+__host__ __device__ constexpr int fmt_pair_bytes(int f) { return 2 * fmt_tile_bytes(f); }
+__host__ __device__ constexpr int fmt_stages(int f) { return f == WF_Q6_K || f == WF_Q5_K ? 2 : 3; }
+__host__ __device__ constexpr int fmt_block_elems(int f) {
+  return (f == WF_Q4_K || f == WF_Q5_K || f == WF_Q6_K) ? 256 : f == WF_Q8_0 ? 32 : 1;
+}
+__host__ __device__ constexpr int fmt_block_bytes(int f) {
+  return f == WF_Q4_K ? 144 : f == WF_Q5_K ? 176 : f == WF_Q6_K ? 210 : f == WF_Q8_0 ? 34 : f == WF_F32 ? 4 : 2;
+}
+
+constexpr int kGemvWarps = 4;          // warps per CTA
+constexpr int kGroupRows = 128;        // rows per CTA (4 warps x 32 rows)
+constexpr int kMaxRows = 64;           // max activation rows (M) per forward
+constexpr int kSsStride = 64;          // stride of per-group sum-of-squares slots
+
+// Epilogue applied by the CTA that owns the final sum of a 128-row group.
+enum Epi : int {
+  EPI_STORE = 0,   // out[m*ld + n] = rinv[m]*y + bias[n]
+  EPI_QKV = 1,     // bias, RoPE, q -> qbuf, k/v -> cache
+  EPI_RESID = 2,   // h += y; per-group sum of squares; next operand fragments
+  EPI_SILU = 3,    // silu(gate) * up -> next operand fragments
+};
+
+struct WSeg {                // one weight segment (one format)
+  const uint8_t* w = nullptr;  // pair tiles
+  int fmt = 0;
+  int groups = 0;              // 128-row groups in this segment
+  int k_tiles = 0;             // K / KT
+  int tiles_per_split = 0;     // k_tiles / S
+};
+
+struct QmvParams {
+  WSeg seg[2];
+  int n_rows = 0;        // total output rows (both segments)
+  int K = 0;
+  int S = 1;             // K splits (grid.y)
+  int M = 1;
+  // activation operand
+  const uint32_t* xfrag = nullptr;
+  const float* xsum16 = nullptr;
+  const float* xsum32 = nullptr;
+  // rinv of an RMSNorm folded into this GEMV's input (null = none)
+  const float* ss_in = nullptr;
+  int ss_groups = 0;
+  float ss_inv_dim = 0.f;
+  float eps = 0.f;
+  // split-K scratch
+  float* part = nullptr;
+  int* counters = nullptr;
+  unsigned* err = nullptr;
+  // epilogue
+  int epi = EPI_STORE;
+  float* out = nullptr;
+  int ld_out = 0;
+  const float* bias = nullptr;
+  // EPI_QKV
+  int n_q_heads = 0, n_kv_heads = 0, head_dim = 0;
+  int rope_interleaved = 0;       // 1: pairs (2i,2i+1) (rope_i); 0: pairs (i, i+d/2)
+  const float* rope_cos = nullptr;  // [ctx][head_dim/2]
+  const float* rope_sin = nullptr;
+  const int* positions = nullptr;   // [M] RoPE positions
+  const int* kv_slots = nullptr;    // [M] cache rows to write
+  void* qbuf = nullptr;             // [n_kv][M*G][head_dim] (f16 / bf16)
+  void* kcache = nullptr;           // layer base [n_kv][t_max][head_dim]
+  void* vcache = nullptr;
+  int t_max = 0;
+  // EPI_RESID / EPI_SILU: next operand
+  float* h = nullptr;               // residual [M][H]
+  float* ss_out = nullptr;          // [groups][kSsStride]
+  const float* next_norm = nullptr; // norm weight folded into the next operand (null: plain)
+  uint32_t* next_frag = nullptr;
+  float* next_xsum16 = nullptr;
+  float* next_xsum32 = nullptr;
+  int act_bf16 = 0;                 // operand dtype: 0 f16, 1 bf16
+};
+
+// Launch one fused GEMV.  `nt` = ceil(M/8) selects the instantiation.
+cudaError_t launch_qmv(const QmvParams& p, cudaStream_t stream, bool pdl);
+
+// Repack raw GGUF blocks (device, row-major [N][K/be][bb]) into pair tiles.
+cudaError_t launch_repack(const uint8_t* raw, int fmt, int N, int K, uint8_t* tiles, cudaStream_t s);
+
+// ---- embedding gather --------------------------------------------------
+struct EmbedParams {
+  const uint8_t* table = nullptr;  // raw GGUF rows [V][H]
+  int fmt = 0;
+  int H = 0, V = 0, M = 0;
+  const int* tokens = nullptr;     // [M]
+  float* h = nullptr;              // [M][H]
+  float* ss_out = nullptr;         // [H/128][kSsStride]
+  const float* norm = nullptr;     // first layer's attn_norm
+  uint32_t* frag = nullptr;
+  float* xsum16 = nullptr;
+  float* xsum32 = nullptr;
+  int act_bf16 = 0;
+  unsigned* err = nullptr;
+};
+cudaError_t launch_embed(const EmbedParams& p, int nt, cudaStream_t s, bool pdl);
+
+// ---- attention ----------------------------------------------------------
+struct AttnParams {
+  const void* q = nullptr;         // [n_kv][R][hd], R = M*G, row r = m*G + g
+  const void* kcache = nullptr;    // layer base [n_kv][t_max][hd]
+  const void* vcache = nullptr;
+  int n_kv = 0, G = 0, hd = 0, M = 0, t_max = 0;
+  const int* step = nullptr;       // device: [0] = prefix length P, [1] = total keys P + n
+  const unsigned long long* anc = nullptr;  // [M] ancestor bitmask over the n new keys
+  float scale_log2 = 0.f;          // log2(e) / sqrt(hd)
+  int chunk = 64;                  // keys per split (aligned to absolute positions)
+  int max_splits = 0;
+  float* part_o = nullptr;         // [n_kv][max_splits][R][hd]
+  float* part_ml = nullptr;        // [n_kv][max_splits][R][2]
+  // combine output: O-proj operand fragments
+  uint32_t* frag = nullptr;
+  float* xsum16 = nullptr;
+  float* xsum32 = nullptr;
+  int act_bf16 = 0;
+  unsigned* err = nullptr;
+};
+cudaError_t launch_attention(const AttnParams& p, int nt, cudaStream_t s, bool pdl);
+
+// ---- KV reorder (commit accepted path) -----------------------------------
+// src_rows/dst_rows: device int[n]; tmp: device scratch of layers*2*n_kv*n*hd halves.
+cudaError_t launch_kv_gather(void* kcache, void* vcache, int layers, int n_kv, int t_max, int hd,
+                             const int* src_rows, const int* dst_rows, int n, void* tmp, cudaStream_t s);
+
+// ---- plain f32 activations -> GEMV operand (fragments + column sums) ------
+cudaError_t launch_make_operand(const float* x, int M, int K, int nt, uint32_t* frag, float* xsum16, float* xsum32,
+                                int bf16, cudaStream_t s);
+
+// ---- final hidden rows (for hidden-state outputs) ------------------------
+cudaError_t launch_final_hidden(const float* h, const float* ss, int groups, float inv_dim, float eps,
+                                const float* norm, int M, int H, float* out, cudaStream_t s);
+
+// ---- acceptance helpers ---------------------------------------------------
+cudaError_t launch_row_argmax(const float* logits, int rows, int V, int* out_idx, float* out_val,
+                              cudaStream_t s);
+
+// ---- synthetic weight generation (seeded N(0, sigma) then quantized) -------
+cudaError_t launch_synth_quant(uint8_t* raw, int fmt, int rows, int K, uint64_t seed, float sigma,
+                               int row_offset, cudaStream_t s);
+cudaError_t launch_synth_vec(float* out, int n, uint64_t seed, float base, float sigma, cudaStream_t s);
+
+}  // namespace specb200

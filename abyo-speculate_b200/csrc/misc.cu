@@ -1,0 +1,429 @@
+// Small kernels around the verify step: embedding gather-dequant, KV-cache
+// reorder (accepted-path commit), final-norm hidden rows, row argmax, and the
+// seeded on-device generator for synthetic quantized weights.
+#include "common.cuh"
+#include "kernels.cuh"
+
+#include <math.h>
+
+namespace specb200 {
+
+namespace {
+
+SPEC_DEV float h2f16(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+SPEC_DEV uint16_t rd_u16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+SPEC_DEV void k4_sm(const uint8_t* q, int j, int& sc, int& m) {
+  if (j < 4) {
+    sc = q[j] & 63;
+    m = q[j + 4] & 63;
+  } else {
+    sc = (q[j + 4] & 0xF) | ((q[j - 4] >> 6) << 4);
+    m = (q[j + 4] >> 4) | ((q[j] >> 6) << 4);
+  }
+}
+
+// Element k of a GGUF row, with the same f32 operation order as the GGUF
+// reference decode (no fused multiply-add), so the embedding rows are
+// bit-identical to a host dequantization.
+SPEC_DEV float deq_elem(const uint8_t* row, int fmt, int k) {
+  switch (fmt) {
+    case WF_Q4_K:
+    case WF_Q5_K: {
+      const int bb = fmt == WF_Q4_K ? 144 : 176;
+      const uint8_t* b = row + (size_t)(k >> 8) * bb;
+      const int kk = k & 255, c = kk >> 6, l = kk & 31, hi = (kk & 63) >> 5;
+      int sc, m;
+      k4_sm(b + 4, 2 * c + hi, sc, m);
+      const float d = h2f16(rd_u16(b)), dmin = h2f16(rd_u16(b + 2));
+      const float d1 = __fmul_rn(d, (float)sc), m1 = __fmul_rn(dmin, (float)m);
+      int q;
+      if (fmt == WF_Q4_K) {
+        const uint8_t byte = b[16 + 32 * c + l];
+        q = hi ? (byte >> 4) : (byte & 15);
+      } else {
+        const uint8_t byte = b[48 + 32 * c + l];
+        q = (hi ? (byte >> 4) : (byte & 15)) + (((b[16 + l] >> (2 * c + hi)) & 1) ? 16 : 0);
+      }
+      return __fsub_rn(__fmul_rn(d1, (float)q), m1);
+    }
+    case WF_Q6_K: {
+      const uint8_t* b = row + (size_t)(k >> 8) * 210;
+      const int kk = k & 255, n = kk >> 7, r = kk & 127, j = r >> 5, l = r & 31;
+      const uint8_t lb = b[64 * n + l + (j & 1) * 32];
+      const int lo = (j < 2) ? (lb & 15) : (lb >> 4);
+      const int hi = (b[128 + 32 * n + l] >> (2 * j)) & 3;
+      const int q = (lo | (hi << 4)) - 32;
+      const int is = l / 16;
+      const float d = h2f16(rd_u16(b + 208));
+      const float sc = (float)(int8_t)b[192 + 8 * n + is + 2 * j];
+      return __fmul_rn(__fmul_rn(d, sc), (float)q);
+    }
+    case WF_Q8_0: {
+      const uint8_t* b = row + (size_t)(k >> 5) * 34;
+      return __fmul_rn(h2f16(rd_u16(b)), (float)(int8_t)b[2 + (k & 31)]);
+    }
+    case WF_F32:
+      return reinterpret_cast<const float*>(row)[k];
+    case WF_F16:
+      return h2f16(reinterpret_cast<const uint16_t*>(row)[k]);
+    case WF_BF16: {
+      const uint32_t bits = (uint32_t)reinterpret_cast<const uint16_t*>(row)[k] << 16;
+      return __uint_as_float(bits);
+    }
+  }
+  return 0.f;
+}
+
+SPEC_DEV void frag_store_m(uint32_t* frag, int nt_total, int m, int k, uint16_t bits) {
+  const int s = k >> 4, kk = k & 15, nt = m >> 3, g = m & 7;
+  const int t = (kk & 7) >> 1, slot = kk >> 3, lo = kk & 1;
+  const size_t hidx = ((size_t)((s * nt_total + nt) * 32 + g * 4 + t)) * 4 + slot * 2 + lo;
+  reinterpret_cast<uint16_t*>(frag)[hidx] = bits;
+}
+
+// grid (H/128, M), 128 threads: one column each.
+__global__ void __launch_bounds__(128) embed_kernel(const __grid_constant__ EmbedParams p, int nt_total) {
+  __shared__ float s_red[4];
+  pdl_launch_dependents();
+  pdl_wait();
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int grp = blockIdx.x, m = blockIdx.y;
+  const int n = grp * 128 + tid;
+  const int tok = p.tokens[m];
+  float v = 0.f;
+  if (tok >= 0 && tok < p.V) {
+    const size_t row_bytes = (size_t)(p.H / fmt_block_elems(p.fmt)) * fmt_block_bytes(p.fmt);
+    v = deq_elem(p.table + (size_t)tok * row_bytes, p.fmt, n);
+  } else if (tid == 0) {
+    atomicOr(p.err, DEV_ERR_BAD_ARGUMENT);
+  }
+  p.h[(size_t)m * p.H + n] = v;
+  const float sq = warp_sum(v * v);
+  if (lane == 0) s_red[warp] = sq;
+  // operand of the first GEMV: f16/bf16(h * attn_norm)
+  const float x = p.norm ? v * p.norm[n] : v;
+  float back;
+  uint16_t bits;
+  if (p.act_bf16) {
+    const __nv_bfloat16 b = __float2bfloat16_rn(x);
+    back = __bfloat162float(b);
+    bits = __bfloat16_as_ushort(b);
+  } else {
+    const __half h = __float2half_rn(x);
+    back = __half2float(h);
+    bits = __half_as_ushort(h);
+  }
+  frag_store_m(p.frag, nt_total, m, n, bits);
+  float s16 = back;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
+  const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 16);
+  const int w16 = 8 * nt_total;
+  if ((lane & 15) == 0) p.xsum16[(size_t)(n >> 4) * w16 + m] = s16;
+  if (lane == 0) p.xsum32[(size_t)(n >> 5) * w16 + m] = s32;
+  __syncthreads();
+  if (tid == 0) p.ss_out[grp * kSsStride + m] = s_red[0] + s_red[1] + s_red[2] + s_red[3];
+}
+
+// Reorder: for every (layer, arena K/V, kv head) copy rows src[i] -> tmp, then
+// tmp -> dst[i].  One CTA per (layer*2 + arena, kv head).
+__global__ void kv_gather_kernel(uint16_t* kcache, uint16_t* vcache, int n_kv, int t_max, int hd,
+                                 const int* src, const int* dst, int n, uint16_t* tmp) {
+  const int la = blockIdx.x, h = blockIdx.y;
+  const int layer = la >> 1, arena = la & 1;
+  uint16_t* base = (arena ? vcache : kcache) + ((size_t)layer * n_kv + h) * t_max * hd;
+  uint16_t* tb = tmp + ((size_t)la * n_kv + h) * (size_t)n * hd;
+  for (int i = threadIdx.x; i < n * hd; i += blockDim.x) {
+    const int r = i / hd, d = i % hd;
+    tb[i] = base[(size_t)src[r] * hd + d];
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < n * hd; i += blockDim.x) {
+    const int r = i / hd, d = i % hd;
+    base[(size_t)dst[r] * hd + d] = tb[i];
+  }
+}
+
+__global__ void final_hidden_kernel(const float* h, const float* ss, int groups, float inv_dim, float eps,
+                                    const float* norm, int H, float* out) {
+  const int m = blockIdx.x;
+  float ms = 0.f;
+  for (int q = 0; q < groups; ++q) ms += ss[q * kSsStride + m];
+  const float r = 1.f / sqrtf(ms * inv_dim + eps);
+  for (int n = threadIdx.x; n < H; n += blockDim.x) out[(size_t)m * H + n] = h[(size_t)m * H + n] * r * norm[n];
+}
+
+// First-max argmax (strict '>' scan order), one CTA per row.
+__global__ void row_argmax_kernel(const float* logits, int V, int* out_idx, float* out_val) {
+  const int row = blockIdx.x;
+  const float* x = logits + (size_t)row * V;
+  float bv = -INFINITY;
+  int bi = V;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = x[i];
+    if (v > bv) {
+      bv = v;
+      bi = i;
+    }
+  }
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  if (lane == 0) {
+    sv[warp] = bv;
+    si[warp] = bi;
+  }
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = blockDim.x / 32;
+    bv = lane < nw ? sv[lane] : -INFINITY;
+    bi = lane < nw ? si[lane] : V;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    if (lane == 0) {
+      out_idx[row] = bi >= V ? 0 : bi;
+      if (out_val) out_val[row] = bv;
+    }
+  }
+}
+
+// ---- seeded synthetic weights --------------------------------------------
+SPEC_DEV uint64_t splitmix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+SPEC_DEV float gauss(uint64_t seed, uint64_t idx) {
+  const uint64_t r = splitmix64(seed ^ splitmix64(idx));
+  const float u1 = ((float)(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+  const float u2 = ((float)((r >> 16) & 0xFFFFFF) + 0.5f) * (1.0f / 16777216.0f);
+  return sqrtf(-2.f * logf(u1)) * cospif(2.f * u2);
+}
+
+SPEC_DEV uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
+
+// One thread per block of the row-major [rows][K] matrix.
+__global__ void synth_quant_kernel(uint8_t* raw, int fmt, int rows, int K, uint64_t seed, float sigma,
+                                   int row_offset) {
+  const int be = fmt_block_elems(fmt), bb = fmt_block_bytes(fmt);
+  const int nbr = K / be;
+  const size_t blk = (size_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (blk >= (size_t)rows * nbr) return;
+  const int r = (int)(blk / nbr), c = (int)(blk % nbr);
+  uint8_t* out = raw + blk * bb;
+  const uint64_t base = ((uint64_t)(r + row_offset) * (uint64_t)K) + (uint64_t)c * be;
+  if (fmt == WF_Q8_0) {
+    float x[32], amax = 0.f;
+    for (int i = 0; i < 32; ++i) {
+      x[i] = sigma * gauss(seed, base + i);
+      amax = fmaxf(amax, fabsf(x[i]));
+    }
+    const uint16_t db = f2h_bits(amax / 127.f);
+    const float d = h2f16(db);
+    out[0] = db & 0xff;
+    out[1] = db >> 8;
+    for (int i = 0; i < 32; ++i) {
+      const float q = d > 0.f ? rintf(x[i] / d) : 0.f;
+      out[2 + i] = (uint8_t)(int8_t)fminf(fmaxf(q, -127.f), 127.f);
+    }
+    return;
+  }
+  if (fmt == WF_BF16 || fmt == WF_F16 || fmt == WF_F32) {
+    const float x = sigma * gauss(seed, base);
+    if (fmt == WF_BF16) {
+      const uint16_t b = __bfloat16_as_ushort(__float2bfloat16_rn(x));
+      out[0] = b & 0xff;
+      out[1] = b >> 8;
+    } else if (fmt == WF_F16) {
+      const uint16_t b = f2h_bits(x);
+      out[0] = b & 0xff;
+      out[1] = b >> 8;
+    } else {
+      *reinterpret_cast<float*>(out) = x;
+    }
+    return;
+  }
+  float x[256];
+  for (int i = 0; i < 256; ++i) x[i] = sigma * gauss(seed, base + i);
+  for (int i = 0; i < bb; ++i) out[i] = 0;
+  if (fmt == WF_Q6_K) {
+    float scale[16], dmax = 0.f;
+    for (int s = 0; s < 16; ++s) {
+      float am = 0.f;
+      for (int i = 0; i < 16; ++i) am = fmaxf(am, fabsf(x[16 * s + i]));
+      scale[s] = am / 31.f;
+      dmax = fmaxf(dmax, scale[s]);
+    }
+    const uint16_t db = f2h_bits(dmax / 127.f);
+    const float d = h2f16(db);
+    out[208] = db & 0xff;
+    out[209] = db >> 8;
+    for (int s = 0; s < 16; ++s) {
+      const int sc = d > 0.f ? (int)fminf(fmaxf(rintf(scale[s] / d), 0.f), 127.f) : 0;
+      out[192 + s] = (uint8_t)(int8_t)sc;
+      const float se = d * (float)sc;
+      for (int i = 0; i < 16; ++i) {
+        const int k = 16 * s + i;
+        int q = se > 0.f ? (int)fminf(fmaxf(rintf(x[k] / se), -32.f), 31.f) : 0;
+        q += 32;
+        const int n = k >> 7, rr = k & 127, j = rr >> 5, l = rr & 31;
+        uint8_t& lb = out[64 * n + l + (j & 1) * 32];
+        lb |= (j < 2) ? (q & 15) : ((q & 15) << 4);
+        out[128 + 32 * n + l] |= (uint8_t)(((q >> 4) & 3) << (2 * j));
+      }
+    }
+    return;
+  }
+  // Q4_K / Q5_K
+  const int levels = fmt == WF_Q4_K ? 15 : 31;
+  float scale[8], mins[8], smax = 0.f, mmax = 0.f;
+  for (int s = 0; s < 8; ++s) {
+    float lo = 0.f, hi = -INFINITY;
+    for (int i = 0; i < 32; ++i) {
+      lo = fminf(lo, x[32 * s + i]);
+      hi = fmaxf(hi, x[32 * s + i]);
+    }
+    scale[s] = (hi - lo) / levels;
+    mins[s] = -lo;
+    smax = fmaxf(smax, scale[s]);
+    mmax = fmaxf(mmax, mins[s]);
+  }
+  const uint16_t db = f2h_bits(smax / 63.f), dmb = f2h_bits(mmax / 63.f);
+  const float d = h2f16(db), dm = h2f16(dmb);
+  out[0] = db & 0xff;
+  out[1] = db >> 8;
+  out[2] = dmb & 0xff;
+  out[3] = dmb >> 8;
+  int sc[8], mq[8];
+  for (int s = 0; s < 8; ++s) {
+    sc[s] = d > 0.f ? (int)fminf(fmaxf(rintf(scale[s] / d), 0.f), 63.f) : 0;
+    mq[s] = dm > 0.f ? (int)fminf(fmaxf(rintf(mins[s] / dm), 0.f), 63.f) : 0;
+  }
+  uint8_t* sp = out + 4;
+  for (int j = 0; j < 4; ++j) {
+    sp[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+    sp[j + 4] = (uint8_t)((mq[j] & 63) | ((mq[j + 4] >> 4) << 6));
+    sp[j + 8] = (uint8_t)((sc[j + 4] & 15) | ((mq[j + 4] & 15) << 4));
+  }
+  const int qoff = fmt == WF_Q4_K ? 16 : 48;
+  for (int k = 0; k < 256; ++k) {
+    const int s = k >> 5;
+    const float se = d * (float)sc[s], ce = dm * (float)mq[s];
+    int q = se > 0.f ? (int)fminf(fmaxf(rintf((x[k] + ce) / se), 0.f), (float)levels) : 0;
+    const int c = k >> 6, l = k & 31, hi = (k & 63) >> 5;
+    out[qoff + 32 * c + l] |= (uint8_t)((q & 15) << (hi ? 4 : 0));
+    if (fmt == WF_Q5_K && (q >> 4)) out[16 + l] |= (uint8_t)(1u << (2 * c + hi));
+  }
+}
+
+// grid (ceil(K/128), M): f32 row-major activations -> operand fragments.
+__global__ void __launch_bounds__(128) make_operand_kernel(const float* x, int K, int nt_total, uint32_t* frag,
+                                                           float* xs16, float* xs32, int bf16) {
+  const int lane = threadIdx.x & 31;
+  const int m = blockIdx.y;
+  const int k = blockIdx.x * 128 + threadIdx.x;
+  if (blockIdx.x * 128 + (threadIdx.x & ~31) >= K) return;  // whole warp out of range
+  const float v = x[(size_t)m * K + k];
+  float back;
+  uint16_t bits;
+  if (bf16) {
+    const __nv_bfloat16 b = __float2bfloat16_rn(v);
+    back = __bfloat162float(b);
+    bits = __bfloat16_as_ushort(b);
+  } else {
+    const __half h = __float2half_rn(v);
+    back = __half2float(h);
+    bits = __half_as_ushort(h);
+  }
+  frag_store_m(frag, nt_total, m, k, bits);
+  float s16 = back;
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
+  const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 16);
+  const int w16 = 8 * nt_total;
+  if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m] = s16;
+  if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = s32;
+}
+
+__global__ void synth_vec_kernel(float* out, int n, uint64_t seed, float base, float sigma) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = base + sigma * gauss(seed, (uint64_t)i);
+}
+
+}  // namespace
+
+cudaError_t launch_embed(const EmbedParams& p, int nt, cudaStream_t s, bool pdl) {
+  if (p.H % 128 || p.M < 1 || p.M > kMaxRows) return cudaErrorInvalidValue;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.H / 128, p.M, 1);
+  cfg.blockDim = dim3(128, 1, 1);
+  cfg.stream = s;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, embed_kernel, p, nt);
+}
+
+cudaError_t launch_kv_gather(void* kcache, void* vcache, int layers, int n_kv, int t_max, int hd, const int* src,
+                             const int* dst, int n, void* tmp, cudaStream_t s) {
+  if (n <= 0) return cudaSuccess;
+  kv_gather_kernel<<<dim3(layers * 2, n_kv), 256, 0, s>>>(reinterpret_cast<uint16_t*>(kcache),
+                                                           reinterpret_cast<uint16_t*>(vcache), n_kv, t_max, hd, src,
+                                                           dst, n, reinterpret_cast<uint16_t*>(tmp));
+  return cudaGetLastError();
+}
+
+cudaError_t launch_make_operand(const float* x, int M, int K, int nt, uint32_t* frag, float* xsum16, float* xsum32,
+                                int bf16, cudaStream_t s) {
+  if (K % 32 || M < 1 || M > kMaxRows) return cudaErrorInvalidValue;
+  make_operand_kernel<<<dim3((K + 127) / 128, M), 128, 0, s>>>(x, K, nt, frag, xsum16, xsum32, bf16);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_final_hidden(const float* h, const float* ss, int groups, float inv_dim, float eps,
+                                const float* norm, int M, int H, float* out, cudaStream_t s) {
+  final_hidden_kernel<<<M, 256, 0, s>>>(h, ss, groups, inv_dim, eps, norm, H, out);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_row_argmax(const float* logits, int rows, int V, int* out_idx, float* out_val, cudaStream_t s) {
+  row_argmax_kernel<<<rows, 1024, 0, s>>>(logits, V, out_idx, out_val);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_synth_quant(uint8_t* raw, int fmt, int rows, int K, uint64_t seed, float sigma, int row_offset,
+                               cudaStream_t s) {
+  const int be = fmt_block_elems(fmt);
+  if (be == 0 || K % be) return cudaErrorInvalidValue;
+  const size_t blocks = (size_t)rows * (K / be);
+  const int th = 128;
+  synth_quant_kernel<<<(unsigned)((blocks + th - 1) / th), th, 0, s>>>(raw, fmt, rows, K, seed, sigma, row_offset);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_synth_vec(float* out, int n, uint64_t seed, float base, float sigma, cudaStream_t s) {
+  synth_vec_kernel<<<(n + 255) / 256, 256, 0, s>>>(out, n, seed, base, sigma);
+  return cudaGetLastError();
+}
+
+}  // namespace specb200

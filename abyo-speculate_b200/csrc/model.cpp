@@ -1,0 +1,1772 @@
+// Host runtime and C ABI of the verify-step backend.
+//
+// Mirrors the observable protocol of the reference decoders:
+//   crates/speculate/src/model/quantized_llama.rs (LlamaQuantDecoder)
+//   crates/speculate/src/model/quantized_qwen2.rs (Qwen2QuantDecoder)
+//   crates/speculate/src/model/llama.rs           (BF16 LlamaDecoder)
+// with history / cache_len / cached-last-logits bookkeeping identical to
+// theirs, and the model math of quantized_llama_local.rs /
+// quantized_qwen2_local.rs / llama_local.rs executed by this library's CUDA
+// kernels (qgemv.cu, attention.cu, misc.cu).
+#include "model.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include <algorithm>
+#include <memory>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "../../include/spec_b200.h"
+#include "gguf.h"
+
+using namespace specb200;
+
+namespace specb200 {
+
+int choose_split(int groups, int k_tiles_gcd, int num_sms) {
+  const char* env = getenv("SPEC_B200_SPLIT");
+  if (env) {
+    const int s = atoi(env);
+    if (s > 0 && k_tiles_gcd % s == 0) return s;
+  }
+  // Smallest divisor of the tile count that gives at least one CTA per SM,
+  // keeping >= 2 tiles per warp where possible.
+  int best = 1;
+  for (int s = 1; s <= k_tiles_gcd; ++s) {
+    if (k_tiles_gcd % s) continue;
+    if (k_tiles_gcd / s < 2 && s > 1) break;
+    best = s;
+    if ((long)groups * s >= num_sms) break;
+  }
+  return best;
+}
+
+}  // namespace specb200
+
+namespace {
+
+thread_local std::string g_load_error;
+
+std::string cuda_msg(cudaError_t e, const char* what) {
+  return std::string(what) + ": " + cudaGetErrorString(e);
+}
+
+int gcd_int(int a, int b) { return b == 0 ? a : gcd_int(b, a % b); }
+
+uint16_t f2bf_bits(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+float half_bits_to_float(uint16_t h) {
+  const uint32_t sign = (uint32_t)(h >> 15) << 31;
+  uint32_t exp = (h >> 10) & 0x1f, man = h & 0x3ff, bits;
+  if (exp == 0) {
+    if (man == 0) {
+      bits = sign;
+    } else {
+      int e = -1;
+      do {
+        man <<= 1;
+        ++e;
+      } while (!(man & 0x400));
+      bits = sign | ((uint32_t)(127 - 15 - e) << 23) | ((man & 0x3ff) << 13);
+    }
+  } else if (exp == 31) {
+    bits = sign | 0x7f800000u | (man << 13);
+  } else {
+    bits = sign | ((exp + 112) << 23) | (man << 13);
+  }
+  float f;
+  memcpy(&f, &bits, 4);
+  return f;
+}
+
+float bf_round(float f) {
+  uint32_t u = (uint32_t)f2bf_bits(f) << 16;
+  float r;
+  memcpy(&r, &u, 4);
+  return r;
+}
+
+}  // namespace
+
+struct spec_model {
+  ModelCfg cfg;
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  std::string err;
+  bool use_graphs = true;
+
+  std::vector<Layer> layers;
+  Mat lm;
+  uint8_t* embed_raw = nullptr;
+  int embed_fmt = 0;
+  float* out_norm = nullptr;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+
+  int t_max = 0;
+  void* kcache = nullptr;
+  void* vcache = nullptr;
+  size_t kv_layer_elems = 0;
+
+  float* h = nullptr;
+  float* ss = nullptr;
+  uint32_t* xa = nullptr;
+  float* xa16 = nullptr;
+  float* xa32 = nullptr;
+  uint32_t* xb = nullptr;
+  float* xb16 = nullptr;
+  float* xb32 = nullptr;
+  uint32_t* xc = nullptr;
+  float* xc16 = nullptr;
+  float* xc32 = nullptr;
+  void* qbuf = nullptr;
+  float* part_o = nullptr;
+  float* part_ml = nullptr;
+  int attn_chunk = 64, attn_max_splits = 1;
+  float* gemv_part = nullptr;
+  int* counters = nullptr;
+  float* logits = nullptr;
+  float* last_row = nullptr;
+  float* hidden_out = nullptr;
+  float* collect = nullptr;
+  unsigned* err_dev = nullptr;
+  StepDev* step_dev = nullptr;
+  StepDev* step_host = nullptr;
+  float* logits_host = nullptr;
+  float* hidden_host = nullptr;
+  unsigned* err_host = nullptr;
+  int* idx_dev = nullptr;
+  int* idx_host = nullptr;
+  void* kv_tmp = nullptr;
+  int* argmax_dev = nullptr;
+  int* argmax_host = nullptr;
+  float* op_in = nullptr;  // f32 staging for apply_lm_head
+
+  std::vector<uint32_t> history;
+  int cache_len = 0;
+  bool last_valid = false;
+
+  struct GraphEntry {
+    cudaGraphExec_t exec = nullptr;
+    int runs = 0;
+  };
+  std::map<int, GraphEntry> graphs;
+  cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+  float last_ms = 0.f;
+  std::vector<void*> dev_allocs;
+  std::vector<void*> host_allocs;
+  int64_t weight_bytes = 0;
+
+  ~spec_model() {
+    cudaSetDevice(device);
+    if (stream) cudaStreamSynchronize(stream);
+    for (auto& kv : graphs)
+      if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    for (void* p : dev_allocs) cudaFree(p);
+    for (void* p : host_allocs) cudaFreeHost(p);
+    if (ev0) cudaEventDestroy(ev0);
+    if (ev1) cudaEventDestroy(ev1);
+    if (stream) cudaStreamDestroy(stream);
+  }
+
+  int fail(int code, const std::string& msg) {
+    err = msg;
+    return code;
+  }
+
+  template <class T>
+  cudaError_t dalloc(T** p, size_t bytes) {
+    void* q = nullptr;
+    cudaError_t e = cudaMalloc(&q, bytes ? bytes : 16);
+    if (e != cudaSuccess) return e;
+    dev_allocs.push_back(q);
+    *p = static_cast<T*>(q);
+    return cudaMemsetAsync(q, 0, bytes ? bytes : 16, stream);
+  }
+  template <class T>
+  cudaError_t halloc(T** p, size_t bytes) {
+    void* q = nullptr;
+    cudaError_t e = cudaMallocHost(&q, bytes ? bytes : 16);
+    if (e != cudaSuccess) return e;
+    host_allocs.push_back(q);
+    memset(q, 0, bytes ? bytes : 16);
+    *p = static_cast<T*>(q);
+    return cudaSuccess;
+  }
+};
+
+namespace {
+
+int kv_elem_bytes(const ModelCfg&) { return 2; }
+
+// ---------------------------------------------------------------------------
+// Weight building
+// ---------------------------------------------------------------------------
+
+// Copies `rows` raw rows of `row_bytes` from src (host or device) into a
+// device destination with an optional destination pitch (for interleaving).
+cudaError_t copy_rows(void* dst, size_t dst_pitch, const Part& p, size_t row_bytes, int row0, int rows,
+                      cudaStream_t s) {
+  const uint8_t* src = p.src + (size_t)row0 * row_bytes;
+  const cudaMemcpyKind kind = p.on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice;
+  if (dst_pitch == row_bytes) return cudaMemcpyAsync(dst, src, (size_t)rows * row_bytes, kind, s);
+  return cudaMemcpy2DAsync(dst, dst_pitch, src, row_bytes, row_bytes, rows, kind, s);
+}
+
+// Build a fused matrix from parts (all of K columns).  interleave64 fuses
+// exactly two same-format parts as [a 64 rows | b 64 rows] per 128-row group
+// (the gate/up layout consumed by the SiLU epilogue).
+int build_mat(spec_model* m, const std::vector<Part>& parts, int K, bool interleave64, Mat& out) {
+  // Format runs -> segments.
+  struct Run {
+    int fmt;
+    std::vector<int> idx;
+    int rows;
+  };
+  std::vector<Run> runs;
+  for (int i = 0; i < (int)parts.size(); ++i) {
+    if (runs.empty() || runs.back().fmt != parts[i].fmt || interleave64) {
+      if (interleave64 && !runs.empty()) {
+        if (runs.back().fmt != parts[i].fmt) return m->fail(SPEC_ERR_UNSUPPORTED, "gate/up formats differ");
+        runs.back().idx.push_back(i);
+        runs.back().rows += parts[i].rows;
+        continue;
+      }
+      runs.push_back({parts[i].fmt, {i}, parts[i].rows});
+    } else {
+      runs.back().idx.push_back(i);
+      runs.back().rows += parts[i].rows;
+    }
+  }
+  if (runs.size() > 2) return m->fail(SPEC_ERR_UNSUPPORTED, "more than two weight formats in one fused matrix");
+  out.K = K;
+  out.N = 0;
+  int64_t total = 0;
+  for (auto& r : runs) {
+    if (fmt_tile_bytes(r.fmt) == 0)
+      return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported weight format " + std::to_string(r.fmt));
+    if (K % fmt_kt(r.fmt)) return m->fail(SPEC_ERR_UNSUPPORTED, "K not a multiple of the tile width");
+    if (r.rows % kGroupRows) return m->fail(SPEC_ERR_UNSUPPORTED, "segment rows not a multiple of 128");
+    total += (int64_t)(r.rows / 16) * (K / fmt_kt(r.fmt)) * fmt_tile_bytes(r.fmt);
+    out.N += r.rows;
+  }
+  cudaError_t e = m->dalloc(&out.tiles, (size_t)total);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, "weight alloc"));
+  out.bytes = total;
+  m->weight_bytes += total;
+  int64_t off = 0;
+  int kgcd = 0;
+  for (size_t si = 0; si < runs.size(); ++si) {
+    const Run& r = runs[si];
+    const size_t row_bytes = (size_t)(K / fmt_block_elems(r.fmt)) * fmt_block_bytes(r.fmt);
+    uint8_t* staging = nullptr;
+    e = cudaMalloc(&staging, row_bytes * r.rows);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, "staging alloc"));
+    if (interleave64) {
+      const Part& a = parts[r.idx[0]];
+      const Part& b = parts[r.idx[1]];
+      if (a.rows != b.rows || a.rows % 64) {
+        cudaFree(staging);
+        return m->fail(SPEC_ERR_UNSUPPORTED, "gate/up shapes differ");
+      }
+      e = copy_rows(staging, 128 * row_bytes, a, 64 * row_bytes, 0, a.rows / 64, m->stream);
+      if (e == cudaSuccess)
+        e = copy_rows(staging + 64 * row_bytes, 128 * row_bytes, b, 64 * row_bytes, 0, b.rows / 64, m->stream);
+    } else {
+      size_t o = 0;
+      for (int pi : r.idx) {
+        e = copy_rows(staging + o, row_bytes, parts[pi], row_bytes, 0, parts[pi].rows, m->stream);
+        if (e != cudaSuccess) break;
+        o += row_bytes * parts[pi].rows;
+      }
+    }
+    if (e == cudaSuccess) e = launch_repack(staging, r.fmt, r.rows, K, out.tiles + off, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    cudaFree(staging);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "weight upload/repack"));
+    WSeg& sg = out.seg[si];
+    sg.w = out.tiles + off;
+    sg.fmt = r.fmt;
+    sg.groups = r.rows / kGroupRows;
+    sg.k_tiles = K / fmt_kt(r.fmt);
+    kgcd = kgcd ? gcd_int(kgcd, sg.k_tiles) : sg.k_tiles;
+    off += (int64_t)(r.rows / 16) * sg.k_tiles * fmt_tile_bytes(r.fmt);
+  }
+  if (runs.size() == 1) out.seg[1] = WSeg{};
+  const int groups = out.seg[0].groups + out.seg[1].groups;
+  out.S = choose_split(groups, kgcd, m->num_sms);
+  for (int si = 0; si < 2; ++si)
+    if (out.seg[si].groups) out.seg[si].tiles_per_split = out.seg[si].k_tiles / out.S;
+  return SPEC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Buffers and tables
+// ---------------------------------------------------------------------------
+int alloc_runtime(spec_model* m) {
+  const ModelCfg& c = m->cfg;
+  const int H = c.hidden, F = c.ffn, V = c.vocab, hd = c.head_dim;
+  const int G = c.n_heads / c.n_kv;
+  cudaError_t e = cudaSuccess;
+#define ALLOC(ptr, bytes)                                                  \
+  do {                                                                     \
+    e = m->dalloc(&(ptr), (bytes));                                        \
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, #ptr)); \
+  } while (0)
+#define HALLOC(ptr, bytes)                                                 \
+  do {                                                                     \
+    e = m->halloc(&(ptr), (bytes));                                        \
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, #ptr)); \
+  } while (0)
+  m->kv_layer_elems = (size_t)c.n_kv * m->t_max * hd;
+  ALLOC(m->kcache, m->kv_layer_elems * c.n_layers * kv_elem_bytes(c));
+  ALLOC(m->vcache, m->kv_layer_elems * c.n_layers * kv_elem_bytes(c));
+  ALLOC(m->h, (size_t)kMaxRows * H * 4);
+  const int groups_h = H / kGroupRows;
+  ALLOC(m->ss, (size_t)groups_h * kSsStride * 4);
+  const int Kq = c.n_heads * hd;
+  auto frag_bytes = [](int K) { return (size_t)K * kMaxRows * 2; };
+  ALLOC(m->xa, frag_bytes(H));
+  ALLOC(m->xa16, (size_t)(H / 16) * kMaxRows * 4);
+  ALLOC(m->xa32, (size_t)(H / 32) * kMaxRows * 4);
+  ALLOC(m->xb, frag_bytes(Kq));
+  ALLOC(m->xb16, (size_t)(Kq / 16) * kMaxRows * 4);
+  ALLOC(m->xb32, (size_t)(Kq / 32) * kMaxRows * 4);
+  ALLOC(m->xc, frag_bytes(F));
+  ALLOC(m->xc16, (size_t)(F / 16) * kMaxRows * 4);
+  ALLOC(m->xc32, (size_t)(F / 32) * kMaxRows * 4);
+  ALLOC(m->qbuf, (size_t)c.n_heads * kMaxRows * hd * 2);
+  m->attn_chunk = m->t_max <= 4096 ? 64 : (m->t_max <= 16384 ? 128 : 256);
+  m->attn_max_splits = (m->t_max + m->attn_chunk - 1) / m->attn_chunk;
+  const size_t R = (size_t)kMaxRows * G;
+  ALLOC(m->part_o, (size_t)c.n_kv * m->attn_max_splits * R * hd * 4);
+  ALLOC(m->part_ml, (size_t)c.n_kv * m->attn_max_splits * R * 2 * 4);
+  size_t part = 0;
+  int max_groups = 0;
+  auto acc_mat = [&](const Mat& mt) {
+    const int g = mt.seg[0].groups + mt.seg[1].groups;
+    max_groups = std::max(max_groups, g);
+    if (mt.S > 1) part = std::max(part, (size_t)mt.S * g * kGroupRows * kMaxRows);
+  };
+  for (auto& L : m->layers) {
+    acc_mat(L.qkv);
+    acc_mat(L.o);
+    acc_mat(L.gu);
+    acc_mat(L.down);
+  }
+  acc_mat(m->lm);
+  ALLOC(m->gemv_part, part * 4);
+  ALLOC(m->counters, (size_t)max_groups * 4);
+  ALLOC(m->logits, (size_t)kMaxRows * V * 4);
+  ALLOC(m->last_row, (size_t)V * 4);
+  ALLOC(m->hidden_out, (size_t)kMaxRows * H * 4);
+  ALLOC(m->err_dev, 16);
+  ALLOC(m->step_dev, sizeof(StepDev));
+  ALLOC(m->idx_dev, 4 * (size_t)(m->t_max + 64) * 2);
+  ALLOC(m->kv_tmp, (size_t)c.n_layers * 2 * c.n_kv * kMaxRows * hd * 2);
+  ALLOC(m->argmax_dev, kMaxRows * 4);
+  ALLOC(m->op_in, (size_t)kMaxRows * H * 4);
+  HALLOC(m->step_host, sizeof(StepDev));
+  HALLOC(m->logits_host, (size_t)kMaxRows * V * 4);
+  HALLOC(m->hidden_host, (size_t)kMaxRows * H * 4);
+  HALLOC(m->err_host, 16);
+  HALLOC(m->idx_host, 4 * (size_t)(m->t_max + 64) * 2);
+  HALLOC(m->argmax_host, kMaxRows * 4);
+#undef ALLOC
+#undef HALLOC
+  e = cudaEventCreate(&m->ev0);
+  if (e == cudaSuccess) e = cudaEventCreate(&m->ev1);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "events"));
+  return SPEC_OK;
+}
+
+// RoPE tables exactly as precomput_freqs_cis (quantized_llama_local.rs:189-205):
+// theta_i = 1 / base^(2i/d) in f32, angle = pos * theta_i (single f32
+// product), cos/sin in f32.  Llama-3 frequency scaling follows
+// llama_local.rs:47-75; the BF16 model casts the tables to bf16 (:95-96).
+int build_rope(spec_model* m) {
+  const ModelCfg& c = m->cfg;
+  const int half = c.head_dim / 2;
+  std::vector<float> inv(half);
+  for (int i = 0; i < half; ++i) inv[i] = 1.0f / powf(c.rope_theta, (float)(2 * i) / (float)c.head_dim);
+  if (c.rope_scaled) {
+    const float pi = 3.14159265358979323846f;
+    const float low_wavelen = (float)c.rs_orig / c.rs_low;
+    const float high_wavelen = (float)c.rs_orig / c.rs_high;
+    for (int i = 0; i < half; ++i) {
+      const float freq = inv[i];
+      const float wavelen = 2.f * pi / freq;
+      if (wavelen < high_wavelen) {
+      } else if (wavelen > low_wavelen) {
+        inv[i] = freq / c.rs_factor;
+      } else {
+        const float smooth = ((float)c.rs_orig / wavelen - c.rs_low) / (c.rs_high - c.rs_low);
+        inv[i] = (1.f - smooth) * freq / c.rs_factor + smooth * freq;
+      }
+    }
+  }
+  const size_t n = (size_t)m->t_max * half;
+  std::vector<float> cs(n), sn(n);
+  for (int p = 0; p < m->t_max; ++p)
+    for (int i = 0; i < half; ++i) {
+      const float a = (float)p * inv[i];
+      float cv = cosf(a), sv = sinf(a);
+      if (c.rope_tables_bf16) {
+        cv = bf_round(cv);
+        sv = bf_round(sv);
+      }
+      cs[(size_t)p * half + i] = cv;
+      sn[(size_t)p * half + i] = sv;
+    }
+  cudaError_t e = m->dalloc(&m->rope_cos, n * 4);
+  if (e == cudaSuccess) e = m->dalloc(&m->rope_sin, n * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(m->rope_cos, cs.data(), n * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMemcpy(m->rope_sin, sn.data(), n * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "rope tables"));
+  return SPEC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// Forward
+// ---------------------------------------------------------------------------
+enum : int { F_LOGITS = 1, F_HIDDEN = 2 };
+
+QmvParams base_params(spec_model* m, const Mat& mt, int M) {
+  QmvParams p;
+  p.seg[0] = mt.seg[0];
+  p.seg[1] = mt.seg[1];
+  p.n_rows = mt.N;
+  p.K = mt.K;
+  p.S = mt.S;
+  p.M = M;
+  p.part = m->gemv_part;
+  p.counters = m->counters;
+  p.err = m->err_dev;
+  p.act_bf16 = m->cfg.bf16 ? 1 : 0;
+  return p;
+}
+
+struct ProfRec {
+  std::vector<cudaEvent_t> ev;  // ev[0] before the first kernel, ev[i+1] after kernel i
+  std::vector<int> kind;
+  std::vector<int64_t> bytes;
+};
+
+// Kernel kinds reported by spec_profile_forward.
+enum : int { K_EMBED = 0, K_QKV = 1, K_ATTN = 2, K_ATTN_COMBINE = 3, K_O = 4, K_GATE_UP = 5, K_DOWN = 6, K_LM = 7 };
+
+cudaError_t prof_mark(ProfRec* pr, cudaStream_t s, int kind, int64_t bytes) {
+  if (!pr) return cudaSuccess;
+  cudaEvent_t e;
+  cudaError_t err = cudaEventCreate(&e);
+  if (err != cudaSuccess) return err;
+  pr->ev.push_back(e);
+  pr->kind.push_back(kind);
+  pr->bytes.push_back(bytes);
+  return cudaEventRecord(e, s);
+}
+
+cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<int>* collect,
+                            ProfRec* pr = nullptr) {
+  const ModelCfg& c = m->cfg;
+  const int H = c.hidden, hd = c.head_dim, G = c.n_heads / c.n_kv;
+  const int nt = (M + 7) / 8;
+  cudaStream_t s = m->stream;
+  cudaError_t e = cudaMemcpyAsync(m->step_dev, m->step_host, sizeof(StepDev), cudaMemcpyHostToDevice, s);
+  if (e != cudaSuccess) return e;
+  EmbedParams ep;
+  ep.table = m->embed_raw;
+  ep.fmt = m->embed_fmt;
+  ep.H = H;
+  ep.V = c.vocab;
+  ep.M = M;
+  ep.tokens = m->step_dev->tokens;
+  ep.h = m->h;
+  ep.ss_out = m->ss;
+  ep.norm = m->layers[0].attn_norm;
+  ep.frag = m->xa;
+  ep.xsum16 = m->xa16;
+  ep.xsum32 = m->xa32;
+  ep.act_bf16 = c.bf16 ? 1 : 0;
+  ep.err = m->err_dev;
+  if (pr) {
+    cudaEvent_t e0;
+    if ((e = cudaEventCreate(&e0)) != cudaSuccess) return e;
+    pr->ev.push_back(e0);
+    if ((e = cudaEventRecord(e0, s)) != cudaSuccess) return e;
+  }
+  const bool pdl = pr == nullptr;
+  e = launch_embed(ep, nt, s, false);
+  if (e != cudaSuccess) return e;
+  if ((e = prof_mark(pr, s, K_EMBED, (int64_t)M * H * 8)) != cudaSuccess) return e;
+  const float inv_h = 1.f / (float)H;
+  const int64_t step_keys = (int64_t)m->step_host->step[1];
+  const int groups_h = H / kGroupRows;
+  for (int l = 0; l < c.n_layers; ++l) {
+    const Layer& L = m->layers[l];
+    uint8_t* kc = static_cast<uint8_t*>(m->kcache) + (size_t)l * m->kv_layer_elems * 2;
+    uint8_t* vc = static_cast<uint8_t*>(m->vcache) + (size_t)l * m->kv_layer_elems * 2;
+    {  // q/k/v projection + bias + RoPE + KV append
+      QmvParams p = base_params(m, L.qkv, M);
+      p.xfrag = m->xa;
+      p.xsum16 = m->xa16;
+      p.xsum32 = m->xa32;
+      p.ss_in = m->ss;
+      p.ss_groups = groups_h;
+      p.ss_inv_dim = inv_h;
+      p.eps = c.eps;
+      p.epi = EPI_QKV;
+      p.bias = L.bqkv;
+      p.n_q_heads = c.n_heads;
+      p.n_kv_heads = c.n_kv;
+      p.head_dim = hd;
+      p.rope_interleaved = c.rope_interleaved ? 1 : 0;
+      p.rope_cos = m->rope_cos;
+      p.rope_sin = m->rope_sin;
+      p.positions = m->step_dev->positions;
+      p.kv_slots = m->step_dev->slots;
+      p.qbuf = m->qbuf;
+      p.kcache = kc;
+      p.vcache = vc;
+      p.t_max = m->t_max;
+      if ((e = launch_qmv(p, s, pdl)) != cudaSuccess) return e;
+      if ((e = prof_mark(pr, s, K_QKV, L.qkv.bytes)) != cudaSuccess) return e;
+    }
+    {  // attention
+      AttnParams a;
+      a.q = m->qbuf;
+      a.kcache = kc;
+      a.vcache = vc;
+      a.n_kv = c.n_kv;
+      a.G = G;
+      a.hd = hd;
+      a.M = M;
+      a.t_max = m->t_max;
+      a.step = m->step_dev->step;
+      a.anc = m->step_dev->anc;
+      a.scale_log2 = 1.4426950408889634f / sqrtf((float)hd);
+      a.chunk = m->attn_chunk;
+      a.max_splits = m->attn_max_splits;
+      a.part_o = m->part_o;
+      a.part_ml = m->part_ml;
+      a.frag = m->xb;
+      a.xsum16 = m->xb16;
+      a.xsum32 = m->xb32;
+      a.act_bf16 = c.bf16 ? 1 : 0;
+      a.err = m->err_dev;
+      if ((e = launch_attention(a, nt, s, pdl)) != cudaSuccess) return e;
+      if ((e = prof_mark(pr, s, K_ATTN, step_keys * c.n_kv * hd * 2 * 2)) != cudaSuccess) return e;
+    }
+    {  // o projection + residual; next operand = ffn_norm(h)
+      QmvParams p = base_params(m, L.o, M);
+      p.xfrag = m->xb;
+      p.xsum16 = m->xb16;
+      p.xsum32 = m->xb32;
+      p.epi = EPI_RESID;
+      p.h = m->h;
+      p.ss_out = m->ss;
+      p.next_norm = L.ffn_norm;
+      p.next_frag = m->xa;
+      p.next_xsum16 = m->xa16;
+      p.next_xsum32 = m->xa32;
+      if ((e = launch_qmv(p, s, pdl)) != cudaSuccess) return e;
+      if ((e = prof_mark(pr, s, K_O, L.o.bytes)) != cudaSuccess) return e;
+    }
+    {  // gate/up + SiLU
+      QmvParams p = base_params(m, L.gu, M);
+      p.xfrag = m->xa;
+      p.xsum16 = m->xa16;
+      p.xsum32 = m->xa32;
+      p.ss_in = m->ss;
+      p.ss_groups = groups_h;
+      p.ss_inv_dim = inv_h;
+      p.eps = c.eps;
+      p.epi = EPI_SILU;
+      p.next_frag = m->xc;
+      p.next_xsum16 = m->xc16;
+      p.next_xsum32 = m->xc32;
+      if ((e = launch_qmv(p, s, pdl)) != cudaSuccess) return e;
+      if ((e = prof_mark(pr, s, K_GATE_UP, L.gu.bytes)) != cudaSuccess) return e;
+    }
+    {  // down + residual; next operand = next attn_norm(h) or output_norm(h)
+      QmvParams p = base_params(m, L.down, M);
+      p.xfrag = m->xc;
+      p.xsum16 = m->xc16;
+      p.xsum32 = m->xc32;
+      p.epi = EPI_RESID;
+      p.h = m->h;
+      p.ss_out = m->ss;
+      p.next_norm = (l + 1 < c.n_layers) ? m->layers[l + 1].attn_norm : m->out_norm;
+      p.next_frag = m->xa;
+      p.next_xsum16 = m->xa16;
+      p.next_xsum32 = m->xa32;
+      if ((e = launch_qmv(p, s, pdl)) != cudaSuccess) return e;
+      if ((e = prof_mark(pr, s, K_DOWN, L.down.bytes)) != cudaSuccess) return e;
+    }
+    if (collect) {
+      for (size_t ci = 0; ci < collect->size(); ++ci)
+        if ((*collect)[ci] == l) {
+          e = cudaMemcpyAsync(m->collect + ci * (size_t)M * H, m->h, (size_t)M * H * 4, cudaMemcpyDeviceToDevice, s);
+          if (e != cudaSuccess) return e;
+        }
+    }
+  }
+  if (flags & F_LOGITS) {
+    QmvParams p = base_params(m, m->lm, M);
+    p.xfrag = m->xa;
+    p.xsum16 = m->xa16;
+    p.xsum32 = m->xa32;
+    p.ss_in = m->ss;
+    p.ss_groups = groups_h;
+    p.ss_inv_dim = inv_h;
+    p.eps = c.eps;
+    p.epi = EPI_STORE;
+    p.out = m->logits;
+    p.ld_out = c.vocab;
+    if ((e = launch_qmv(p, s, pdl)) != cudaSuccess) return e;
+    if ((e = prof_mark(pr, s, K_LM, m->lm.bytes)) != cudaSuccess) return e;
+    e = cudaMemcpyAsync(m->last_row, m->logits + (size_t)(M - 1) * c.vocab, (size_t)c.vocab * 4,
+                        cudaMemcpyDeviceToDevice, s);
+    if (e != cudaSuccess) return e;
+  }
+  if (flags & F_HIDDEN) {
+    e = launch_final_hidden(m->h, m->ss, groups_h, inv_h, c.eps, m->out_norm, M, H, m->hidden_out, s);
+    if (e != cudaSuccess) return e;
+  }
+  return cudaSuccess;
+}
+
+// Runs one forward of M rows described by m->step_host.  Graph-replayed per
+// (M, flags) after a first eager run.
+int run_forward(spec_model* m, int M, int flags, const std::vector<int>* collect = nullptr) {
+  cudaError_t e = cudaSuccess;
+  const int key = M | (flags << 8);
+  const bool graphable = m->use_graphs && collect == nullptr;
+  e = cudaEventRecord(m->ev0, m->stream);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "event"));
+  auto& ge = m->graphs[key];
+  if (graphable && ge.exec) {
+    e = cudaGraphLaunch(ge.exec, m->stream);
+  } else if (graphable && ge.runs >= 1) {
+    cudaGraph_t g = nullptr;
+    e = cudaStreamBeginCapture(m->stream, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+      const cudaError_t ee = enqueue_forward(m, M, flags, nullptr);
+      e = cudaStreamEndCapture(m->stream, &g);
+      if (ee != cudaSuccess) e = ee;
+    }
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&ge.exec, g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (e == cudaSuccess) e = cudaGraphLaunch(ge.exec, m->stream);
+    if (e != cudaSuccess) {
+      // Capture unsupported here: fall back to eager launches for good.
+      cudaGetLastError();
+      if (ge.exec) cudaGraphExecDestroy(ge.exec);
+      ge.exec = nullptr;
+      m->use_graphs = false;
+      e = enqueue_forward(m, M, flags, nullptr);
+    }
+  } else {
+    e = enqueue_forward(m, M, flags, collect);
+  }
+  ge.runs++;
+  if (e == cudaSuccess) e = cudaEventRecord(m->ev1, m->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->err_host, m->err_dev, 4, cudaMemcpyDeviceToHost, m->stream);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "forward launch"));
+  return SPEC_OK;
+}
+
+int finish(spec_model* m) {
+  cudaError_t e = cudaStreamSynchronize(m->stream);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "forward"));
+  cudaEventElapsedTime(&m->last_ms, m->ev0, m->ev1);
+  if (*m->err_host) {
+    const unsigned bits = *m->err_host;
+    *m->err_host = 0;
+    cudaMemsetAsync(m->err_dev, 0, 4, m->stream);
+    cudaStreamSynchronize(m->stream);
+    if (bits & DEV_ERR_MBAR_TIMEOUT) return m->fail(SPEC_ERR_TIMEOUT, "a device wait gave up (mbarrier timeout)");
+    return m->fail(SPEC_ERR_INVALID, "a kernel rejected an index (token id out of range?)");
+  }
+  return SPEC_OK;
+}
+
+void fill_step_causal(spec_model* m, const uint32_t* toks, int M, int P) {
+  StepDev* st = m->step_host;
+  for (int i = 0; i < M; ++i) {
+    st->tokens[i] = (int)toks[i];
+    st->positions[i] = P + i;
+    st->slots[i] = P + i;
+    st->anc[i] = (i == 63) ? ~0ull : ((1ull << (i + 1)) - 1ull);
+  }
+  st->step[0] = P;
+  st->step[1] = P + M;
+}
+
+// forward_advance_logits (quantized_llama.rs:137-158): forwards `n` tokens
+// at cache_len, chunked by kMaxRows; when rows_out != nullptr it receives
+// all n logits rows.  On success cache_len += n and the last row is cached.
+int forward_advance(spec_model* m, const uint32_t* ids, int n, float* rows_out, bool want_logits = true) {
+  if (n <= 0) return m->fail(SPEC_ERR_INVALID, "forward_advance with empty tokens");
+  if (m->cache_len + n > m->t_max)
+    return m->fail(SPEC_ERR_INVALID, "KV capacity exceeded (" + std::to_string(m->cache_len + n) + " > " +
+                                         std::to_string(m->t_max) + ")");
+  for (int i = 0; i < n; ++i)
+    if (ids[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  const int start = m->cache_len;
+  int done = 0;
+  while (done < n) {
+    const int M = std::min(kMaxRows, n - done);
+    fill_step_causal(m, ids + done, M, start + done);
+    const bool last_chunk = done + M == n;
+    const int flags = (rows_out || (last_chunk && want_logits)) ? F_LOGITS : 0;
+    int rc = run_forward(m, M, flags);
+    if (rc == SPEC_OK && rows_out) {
+      cudaMemcpyAsync(m->logits_host, m->logits, (size_t)M * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+    }
+    if (rc == SPEC_OK) rc = finish(m);
+    if (rc != SPEC_OK) {
+      m->cache_len = start;  // KV rows beyond cache_len are ignored: state unchanged
+      return rc;
+    }
+    if (rows_out) memcpy(rows_out + (size_t)done * m->cfg.vocab, m->logits_host, (size_t)M * m->cfg.vocab * 4);
+    done += M;
+  }
+  m->cache_len = start + n;
+  m->last_valid = want_logits;
+  return SPEC_OK;
+}
+
+int copy_last_row(spec_model* m, float* out) {
+  cudaError_t e = cudaMemcpy(out, m->last_row, (size_t)m->cfg.vocab * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "copy logits"));
+  return SPEC_OK;
+}
+
+// Tree helpers (crates/speculate/src/tree.rs:38-74, 125-133, 149-158).
+int check_tree(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n) {
+  if (n <= 0) return m->fail(SPEC_ERR_INVALID, "DraftTree must have at least a root");
+  if (n > kMaxRows) return m->fail(SPEC_ERR_UNSUPPORTED, "tree larger than SPEC_MAX_ROWS nodes");
+  for (int i = 1; i < n; ++i)
+    if (parents[i] < 0 || parents[i] >= i)
+      return m->fail(SPEC_ERR_INVALID, "node " + std::to_string(i) + " has parent index " +
+                                           std::to_string(parents[i]) + ", which is not strictly smaller");
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  return SPEC_OK;
+}
+
+void fill_step_tree(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, int prefix) {
+  StepDev* st = m->step_host;
+  for (int i = 0; i < n; ++i) {
+    int d = 0;
+    unsigned long long anc = 1ull << i;
+    for (int cur = i; cur != 0; cur = parents[cur]) {
+      ++d;
+      anc |= 1ull << parents[cur];
+    }
+    st->tokens[i] = (int)tokens[i];
+    st->positions[i] = prefix + d;
+    st->slots[i] = prefix + i;
+    st->anc[i] = anc | 1ull;  // the root is everyone's ancestor
+  }
+  st->step[0] = prefix;
+  st->step[1] = prefix + n;
+}
+
+int tree_forward(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, int prefix, int flags) {
+  if (prefix + n > m->t_max) return m->fail(SPEC_ERR_INVALID, "KV capacity exceeded");
+  fill_step_tree(m, tokens, parents, n, prefix);
+  int rc = run_forward(m, n, flags);
+  return rc;
+}
+
+}  // namespace
+
+// ===========================================================================
+// Model construction
+// ===========================================================================
+namespace {
+
+int init_device(spec_model* m, const spec_load_opts* opts) {
+  m->device = opts ? opts->device : 0;
+  m->use_graphs = opts ? (opts->use_graphs != 0) : true;
+  if (getenv("SPEC_B200_NO_GRAPHS")) m->use_graphs = false;
+  cudaError_t e = cudaSetDevice(m->device);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "cudaSetDevice"));
+  cudaDeviceProp prop;
+  e = cudaGetDeviceProperties(&prop, m->device);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "device properties"));
+  if (prop.major < 10) return m->fail(SPEC_ERR_UNSUPPORTED, std::string("needs an sm_100 GPU, found ") + prop.name);
+  m->num_sms = prop.multiProcessorCount;
+  e = cudaStreamCreateWithFlags(&m->stream, cudaStreamNonBlocking);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "stream"));
+  return SPEC_OK;
+}
+
+int upload_vec(spec_model* m, float** dst, const float* src, int n) {
+  cudaError_t e = m->dalloc(dst, (size_t)n * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(*dst, src, (size_t)n * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "upload vector"));
+  return SPEC_OK;
+}
+
+int finalize_model(spec_model* m, const spec_load_opts* opts, int ctx_len) {
+  int want = opts && opts->max_ctx > 0 ? opts->max_ctx : std::min(ctx_len > 0 ? ctx_len : 4096, 4096);
+  m->t_max = want;
+  int rc = alloc_runtime(m);
+  if (rc == SPEC_OK) rc = build_rope(m);
+  if (rc == SPEC_OK) {
+    cudaError_t e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "init"));
+  }
+  return rc;
+}
+
+int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) {
+  GgufFile f;
+  std::string err = f.open(path);
+  if (!err.empty()) return m->fail(SPEC_ERR_IO, err);
+  std::string arch;
+  if (!f.get_str("general.architecture", arch)) return m->fail(SPEC_ERR_IO, "missing general.architecture");
+  ModelCfg& c = m->cfg;
+  if (arch == "llama") c.arch = 0;
+  else if (arch == "qwen2") c.arch = 1;
+  else return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported architecture " + arch);
+  auto need_u32 = [&](const std::string& k, int& out) -> bool {
+    uint32_t v;
+    if (!f.get_u32(arch + "." + k, v)) {
+      m->fail(SPEC_ERR_IO, "cannot find " + arch + "." + k + " in GGUF metadata");
+      return false;
+    }
+    out = (int)v;
+    return true;
+  };
+  if (!need_u32("attention.head_count", c.n_heads) || !need_u32("attention.head_count_kv", c.n_kv) ||
+      !need_u32("embedding_length", c.hidden) || !need_u32("context_length", c.ctx_len) ||
+      !need_u32("block_count", c.n_layers))
+    return SPEC_ERR_IO;
+  if (!f.get_f32(arch + ".attention.layer_norm_rms_epsilon", c.eps))
+    return m->fail(SPEC_ERR_IO, "cannot find " + arch + ".attention.layer_norm_rms_epsilon in GGUF metadata");
+  if (!f.get_f32(arch + ".rope.freq_base", c.rope_theta)) c.rope_theta = 10000.f;
+  c.head_dim = c.hidden / c.n_heads;
+  c.has_bias = c.arch == 1;
+  c.rope_interleaved = c.arch == 0;
+  std::string style;
+  if (f.get_str("speculate_b200.rope_style", style) && style == "half") c.rope_interleaved = false;
+  std::string rs;
+  if (f.get_str(arch + ".rope.scaling.type", rs) && rs == "llama3") {
+    c.rope_scaled = true;
+    f.get_f32(arch + ".rope.scaling.factor", c.rs_factor);
+    f.get_f32(arch + ".rope.scaling.low_freq_factor", c.rs_low);
+    f.get_f32(arch + ".rope.scaling.high_freq_factor", c.rs_high);
+    uint32_t o;
+    if (f.get_u32(arch + ".rope.scaling.original_context_length", o)) c.rs_orig = (int)o;
+  }
+  const GgufValue* toks = f.get("tokenizer.ggml.tokens");
+  const GgufTensor* te = f.tensor("token_embd.weight");
+  if (!te || te->dims.size() != 2) return m->fail(SPEC_ERR_IO, "missing token_embd.weight");
+  c.vocab = toks ? (int)toks->arr_len : (int)te->dims[1];
+  if ((int)te->dims[1] < c.vocab) return m->fail(SPEC_ERR_IO, "token_embd has fewer rows than the vocabulary");
+  const GgufTensor* g0 = f.tensor("blk.0.ffn_gate.weight");
+  if (!g0) return m->fail(SPEC_ERR_IO, "missing blk.0.ffn_gate.weight");
+  c.ffn = (int)g0->dims[1];
+  c.bf16 = te->type == WF_BF16 || g0->type == WF_BF16;
+  c.rope_tables_bf16 = c.bf16 && c.arch == 0;
+  if (c.hidden % kGroupRows || c.ffn % kGroupRows || (c.head_dim != 64 && c.head_dim != 128) ||
+      c.n_heads % c.n_kv)
+    return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported model shape");
+
+  auto part_of = [&](const std::string& name, int K, Part& p) -> bool {
+    const GgufTensor* t = f.tensor(name);
+    if (!t) {
+      m->fail(SPEC_ERR_IO, "cannot find tensor " + name);
+      return false;
+    }
+    if (t->dims.size() != 2 || (int)t->dims[0] != K) {
+      m->fail(SPEC_ERR_IO, "tensor " + name + " has an unexpected shape");
+      return false;
+    }
+    p.src = f.data(*t);
+    p.on_device = false;
+    p.fmt = t->type;
+    p.rows = (int)t->dims[1];
+    return true;
+  };
+  auto vec_of = [&](const std::string& name, int n, float** dst) -> int {
+    const GgufTensor* t = f.tensor(name);
+    if (!t) return m->fail(SPEC_ERR_IO, "cannot find tensor " + name);
+    uint64_t cnt = 1;
+    for (auto d : t->dims) cnt *= d;
+    if ((int)cnt != n) return m->fail(SPEC_ERR_IO, "tensor " + name + " has an unexpected size");
+    std::vector<float> tmp(n);
+    const uint8_t* src = f.data(*t);
+    if (t->type == WF_F32) {
+      memcpy(tmp.data(), src, (size_t)n * 4);
+    } else if (t->type == WF_F16 || t->type == WF_BF16) {
+      for (int i = 0; i < n; ++i) {
+        uint16_t b;
+        memcpy(&b, src + 2 * i, 2);
+        if (t->type == WF_BF16) {
+          uint32_t u = (uint32_t)b << 16;
+          memcpy(&tmp[i], &u, 4);
+        } else {
+          tmp[i] = half_bits_to_float(b);
+        }
+      }
+    } else {
+      return m->fail(SPEC_ERR_UNSUPPORTED, "norm/bias tensor " + name + " must be F32/F16/BF16");
+    }
+    return upload_vec(m, dst, tmp.data(), n);
+  };
+  const int H = c.hidden, F = c.ffn, hd = c.head_dim;
+  m->layers.resize(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    const std::string pre = "blk." + std::to_string(l) + ".";
+    Layer& L = m->layers[l];
+    Part q, k, v, o, g, u, d;
+    if (!part_of(pre + "attn_q.weight", H, q) || !part_of(pre + "attn_k.weight", H, k) ||
+        !part_of(pre + "attn_v.weight", H, v) || !part_of(pre + "attn_output.weight", c.n_heads * hd, o) ||
+        !part_of(pre + "ffn_gate.weight", H, g) || !part_of(pre + "ffn_up.weight", H, u) ||
+        !part_of(pre + "ffn_down.weight", F, d))
+      return SPEC_ERR_IO;
+    if (q.rows != c.n_heads * hd || k.rows != c.n_kv * hd || v.rows != c.n_kv * hd || o.rows != H ||
+        g.rows != F || u.rows != F || d.rows != H)
+      return m->fail(SPEC_ERR_IO, "layer " + std::to_string(l) + " has inconsistent shapes");
+    int rc = build_mat(m, {q, k, v}, H, false, L.qkv);
+    if (rc == SPEC_OK) rc = build_mat(m, {o}, c.n_heads * hd, false, L.o);
+    if (rc == SPEC_OK) rc = build_mat(m, {g, u}, H, true, L.gu);
+    if (rc == SPEC_OK) rc = build_mat(m, {d}, F, false, L.down);
+    if (rc == SPEC_OK) rc = vec_of(pre + "attn_norm.weight", H, &L.attn_norm);
+    if (rc == SPEC_OK) rc = vec_of(pre + "ffn_norm.weight", H, &L.ffn_norm);
+    if (rc == SPEC_OK && c.has_bias) {
+      std::vector<float> b((size_t)(c.n_heads + 2 * c.n_kv) * hd);
+      float* tmpd = nullptr;
+      const char* names[3] = {"attn_q.bias", "attn_k.bias", "attn_v.bias"};
+      const int lens[3] = {c.n_heads * hd, c.n_kv * hd, c.n_kv * hd};
+      size_t off = 0;
+      for (int i = 0; i < 3 && rc == SPEC_OK; ++i) {
+        const GgufTensor* t = f.tensor(pre + names[i]);
+        if (!t || t->type != WF_F32 || (int)(t->nbytes / 4) != lens[i]) {
+          rc = m->fail(SPEC_ERR_IO, "cannot find F32 tensor " + pre + names[i]);
+          break;
+        }
+        memcpy(b.data() + off, f.data(*t), (size_t)lens[i] * 4);
+        off += lens[i];
+      }
+      if (rc == SPEC_OK) rc = upload_vec(m, &tmpd, b.data(), (int)b.size());
+      L.bqkv = tmpd;
+    }
+    if (rc != SPEC_OK) return rc;
+  }
+  int rc = vec_of("output_norm.weight", H, &m->out_norm);
+  if (rc != SPEC_OK) return rc;
+  // Embedding table stays in its GGUF layout for the gather.
+  m->embed_fmt = te->type;
+  if (fmt_block_elems(te->type) == 0 || H % fmt_block_elems(te->type))
+    return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported token_embd format");
+  {
+    cudaError_t e = m->dalloc(&m->embed_raw, te->nbytes);
+    if (e == cudaSuccess) e = cudaMemcpy(m->embed_raw, f.data(*te), te->nbytes, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, "embedding upload"));
+  }
+  Part outp;
+  const GgufTensor* ot = f.tensor("output.weight");
+  if (ot) {
+    if (!part_of("output.weight", H, outp)) return SPEC_ERR_IO;
+  } else {  // tied weights (quantized_llama_local.rs:249-252)
+    if (!part_of("token_embd.weight", H, outp)) return SPEC_ERR_IO;
+  }
+  if (outp.rows < c.vocab) return m->fail(SPEC_ERR_IO, "output.weight has fewer rows than the vocabulary");
+  if (c.vocab % kGroupRows) return m->fail(SPEC_ERR_UNSUPPORTED, "vocabulary not a multiple of 128");
+  outp.rows = c.vocab;
+  rc = build_mat(m, {outp}, H, false, m->lm);
+  if (rc != SPEC_OK) return rc;
+  return finalize_model(m, opts, c.ctx_len);
+}
+
+}  // namespace
+
+// ===========================================================================
+// Synthetic models
+// ===========================================================================
+namespace {
+
+int mix_type(int mix, bool is_output, bool is_v_or_down, int layer, int K) {
+  if (mix == 3) return WF_BF16;
+  if (mix == 2) return WF_Q8_0;
+  int base;
+  if (is_output) base = WF_Q6_K;
+  else if (mix == 0) base = (layer >= 0 && layer % 2 == 0 && is_v_or_down) ? WF_Q6_K : WF_Q4_K;
+  else base = WF_Q5_K;
+  if (K % 256) return WF_Q8_0;
+  return base;
+}
+
+uint64_t mix64(uint64_t x) {
+  x += 0x9E3779B97F4A7C15ull;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ull;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBull;
+  return x ^ (x >> 31);
+}
+
+// Raw GGUF blocks for one seeded tensor, generated on the device.
+int synth_part(spec_model* m, std::vector<void*>& temps, int fmt, int rows, int K, uint64_t seed, Part& p) {
+  const size_t bytes = (size_t)rows * (K / fmt_block_elems(fmt)) * fmt_block_bytes(fmt);
+  void* buf = nullptr;
+  cudaError_t e = cudaMalloc(&buf, bytes);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, "synthetic staging"));
+  temps.push_back(buf);
+  e = launch_synth_quant(static_cast<uint8_t*>(buf), fmt, rows, K, seed, 0.02f, 0, m->stream);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "synthetic weights"));
+  p.src = static_cast<const uint8_t*>(buf);
+  p.on_device = true;
+  p.fmt = fmt;
+  p.rows = rows;
+  return SPEC_OK;
+}
+
+int synth_vec(spec_model* m, float** dst, int n, uint64_t seed, float base) {
+  cudaError_t e = m->dalloc(dst, (size_t)n * 4);
+  if (e == cudaSuccess) e = launch_synth_vec(*dst, n, seed, base, 0.02f, m->stream);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "synthetic vector"));
+  return SPEC_OK;
+}
+
+int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, const spec_load_opts* opts) {
+  ModelCfg& c = m->cfg;
+  c.arch = d->arch;
+  c.n_layers = d->n_layers;
+  c.hidden = d->hidden;
+  c.n_heads = d->n_heads;
+  c.n_kv = d->n_kv_heads;
+  c.ffn = d->ffn;
+  c.vocab = d->vocab;
+  c.rope_theta = d->rope_theta;
+  c.eps = d->eps;
+  c.head_dim = c.hidden / c.n_heads;
+  c.has_bias = c.arch == 1;
+  c.bf16 = d->quant_mix == 3;
+  c.rope_interleaved = c.arch == 0 && !d->rope_half;
+  c.rope_tables_bf16 = c.bf16 && c.arch == 0;
+  c.ctx_len = 131072;
+  if (c.bf16 && c.arch == 0) {  // Llama-3.1 frequency scaling for the BF16 checkpoint shape
+    c.rope_scaled = true;
+  }
+  if (c.n_layers <= 0 || c.hidden % kGroupRows || c.ffn % kGroupRows || c.vocab % kGroupRows ||
+      (c.head_dim != 64 && c.head_dim != 128) || c.n_heads % c.n_kv)
+    return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported synthetic model shape");
+  const int H = c.hidden, F = c.ffn, hd = c.head_dim;
+  uint64_t tid = 0;
+  auto tseed = [&]() { return mix64(seed * 0x100000001B3ull + (++tid)); };
+  m->layers.resize(c.n_layers);
+  for (int l = 0; l < c.n_layers; ++l) {
+    Layer& L = m->layers[l];
+    std::vector<void*> temps;
+    Part q, k, v, o, g, u, dn;
+    const int mix = d->quant_mix;
+    int rc = synth_part(m, temps, mix_type(mix, false, false, l, H), c.n_heads * hd, H, tseed(), q);
+    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, H), c.n_kv * hd, H, tseed(), k);
+    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, true, l, H), c.n_kv * hd, H, tseed(), v);
+    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, c.n_heads * hd), H, c.n_heads * hd, tseed(), o);
+    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, H), F, H, tseed(), g);
+    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, H), F, H, tseed(), u);
+    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, true, l, F), H, F, tseed(), dn);
+    if (rc == SPEC_OK) rc = build_mat(m, {q, k, v}, H, false, L.qkv);
+    if (rc == SPEC_OK) rc = build_mat(m, {o}, c.n_heads * hd, false, L.o);
+    if (rc == SPEC_OK) rc = build_mat(m, {g, u}, H, true, L.gu);
+    if (rc == SPEC_OK) rc = build_mat(m, {dn}, F, false, L.down);
+    if (rc == SPEC_OK) rc = synth_vec(m, &L.attn_norm, H, tseed(), 1.f);
+    if (rc == SPEC_OK) rc = synth_vec(m, &L.ffn_norm, H, tseed(), 1.f);
+    if (rc == SPEC_OK && c.has_bias) rc = synth_vec(m, &L.bqkv, (c.n_heads + 2 * c.n_kv) * hd, tseed(), 0.f);
+    cudaStreamSynchronize(m->stream);
+    for (void* t : temps) cudaFree(t);
+    if (rc != SPEC_OK) return rc;
+  }
+  int rc = synth_vec(m, &m->out_norm, H, tseed(), 1.f);
+  if (rc != SPEC_OK) return rc;
+  {
+    std::vector<void*> temps;
+    Part ep, op;
+    m->embed_fmt = mix_type(d->quant_mix, false, false, -1, H);
+    rc = synth_part(m, temps, m->embed_fmt, c.vocab, H, tseed(), ep);
+    if (rc == SPEC_OK) {
+      const size_t bytes = (size_t)c.vocab * (H / fmt_block_elems(m->embed_fmt)) * fmt_block_bytes(m->embed_fmt);
+      cudaError_t e = m->dalloc(&m->embed_raw, bytes);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(m->embed_raw, ep.src, bytes, cudaMemcpyDeviceToDevice, m->stream);
+      if (e != cudaSuccess) rc = m->fail(SPEC_ERR_OOM, cuda_msg(e, "embedding"));
+    }
+    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(d->quant_mix, true, false, -1, H), c.vocab, H, tseed(), op);
+    if (rc == SPEC_OK) rc = build_mat(m, {op}, H, false, m->lm);
+    cudaStreamSynchronize(m->stream);
+    for (void* t : temps) cudaFree(t);
+    if (rc != SPEC_OK) return rc;
+  }
+  return finalize_model(m, opts, c.ctx_len);
+}
+
+}  // namespace
+
+// ===========================================================================
+// C ABI
+// ===========================================================================
+extern "C" {
+
+int spec_load_gguf(const char* path, const spec_load_opts* opts, spec_model** out) {
+  if (!out || !path) {
+    g_load_error = "null argument";
+    return SPEC_ERR_INVALID;
+  }
+  *out = nullptr;
+  std::unique_ptr<spec_model> m(new (std::nothrow) spec_model());
+  if (!m) return SPEC_ERR_OOM;
+  int rc = init_device(m.get(), opts);
+  if (rc == SPEC_OK) rc = load_from_gguf(m.get(), path, opts);
+  if (rc != SPEC_OK) {
+    g_load_error = m->err;
+    return rc;
+  }
+  *out = m.release();
+  return SPEC_OK;
+}
+
+int spec_create_synthetic(const spec_model_desc* desc, uint64_t seed, const spec_load_opts* opts,
+                          spec_model** out) {
+  if (!out || !desc) {
+    g_load_error = "null argument";
+    return SPEC_ERR_INVALID;
+  }
+  *out = nullptr;
+  std::unique_ptr<spec_model> m(new (std::nothrow) spec_model());
+  if (!m) return SPEC_ERR_OOM;
+  int rc = init_device(m.get(), opts);
+  if (rc == SPEC_OK) rc = create_synthetic(m.get(), desc, seed, opts);
+  if (rc != SPEC_OK) {
+    g_load_error = m->err;
+    return rc;
+  }
+  *out = m.release();
+  return SPEC_OK;
+}
+
+void spec_free(spec_model* m) { delete m; }
+
+const char* spec_last_error(const spec_model* m) { return m ? m->err.c_str() : g_load_error.c_str(); }
+
+int spec_vocab_size(const spec_model* m) { return m ? m->cfg.vocab : 0; }
+int spec_hidden_size(const spec_model* m) { return m ? m->cfg.hidden : 0; }
+int spec_num_layers(const spec_model* m) { return m ? m->cfg.n_layers : 0; }
+int spec_history_len(const spec_model* m) { return m ? (int)m->history.size() : 0; }
+int spec_history(const spec_model* m, uint32_t* out, int cap) {
+  if (!m) return 0;
+  const int n = (int)m->history.size();
+  if (out && cap > 0) memcpy(out, m->history.data(), (size_t)std::min(cap, n) * 4);
+  return n;
+}
+int spec_kv_len(const spec_model* m) { return m ? m->cache_len : 0; }
+int spec_max_ctx(const spec_model* m) { return m ? m->t_max : 0; }
+
+int spec_reset(spec_model* m) {
+  if (!m) return SPEC_ERR_INVALID;
+  m->history.clear();
+  m->cache_len = 0;
+  m->last_valid = false;
+  return SPEC_OK;
+}
+
+int spec_observe(spec_model* m, const uint32_t* ids, int n) {
+  if (!m || (n > 0 && !ids) || n < 0) return SPEC_ERR_INVALID;
+  if (n == 0) return SPEC_OK;
+  cudaSetDevice(m->device);
+  int rc = forward_advance(m, ids, n, nullptr);
+  if (rc != SPEC_OK) return rc;
+  m->history.insert(m->history.end(), ids, ids + n);
+  return SPEC_OK;
+}
+
+int spec_next_logits(spec_model* m, float* out) {
+  if (!m || !out) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "next_logits called with empty history");
+  if (m->last_valid) return copy_last_row(m, out);
+  const uint32_t last = m->history.back();
+  const int saved = m->cache_len;
+  const int target = (int)m->history.size() - 1;
+  if (target > m->cache_len) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
+  m->cache_len = target;
+  int rc = forward_advance(m, &last, 1, nullptr);
+  if (rc != SPEC_OK) {
+    m->cache_len = saved;
+    return rc;
+  }
+  return copy_last_row(m, out);
+}
+
+int spec_batched_logits(spec_model* m, const uint32_t* drafts, int k, float* out) {
+  if (!m || !out || k < 0 || (k > 0 && !drafts)) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (k == 0) return spec_next_logits(m, out);
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "batched_logits with empty history");
+  std::vector<uint32_t> combined(k + 1);
+  combined[0] = m->history.back();
+  memcpy(combined.data() + 1, drafts, (size_t)k * 4);
+  const int saved = m->cache_len;
+  const int target = (int)m->history.size() - 1;
+  if (target > m->cache_len) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
+  const bool saved_valid = m->last_valid;
+  m->cache_len = target;
+  int rc = forward_advance(m, combined.data(), k + 1, out);
+  if (rc != SPEC_OK) {
+    m->cache_len = saved;
+    m->last_valid = saved_valid;
+    return rc;
+  }
+  m->history.insert(m->history.end(), drafts, drafts + k);
+  return SPEC_OK;
+}
+
+int spec_rollback_to(spec_model* m, int len) {
+  if (!m || len < 0) return SPEC_ERR_INVALID;
+  if (len > (int)m->history.size())
+    return m->fail(SPEC_ERR_CACHE_ROLLBACK, "rollback target " + std::to_string(len) + " > history length " +
+                                                std::to_string(m->history.size()));
+  if (len > m->cache_len)
+    return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate_kv_cache_to(" + std::to_string(len) + ") exceeds " +
+                                                std::to_string(m->cache_len));
+  m->history.resize(len);
+  m->last_valid = false;
+  m->cache_len = len;
+  return SPEC_OK;
+}
+
+int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out) {
+  if (!m || !tokens || !parents || !out) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
+  int rc = check_tree(m, tokens, parents, n);
+  if (rc != SPEC_OK) return rc;
+  const uint32_t last = m->history.back();
+  if (tokens[0] != last)
+    return m->fail(SPEC_ERR_INVALID, "tree root (" + std::to_string(tokens[0]) +
+                                         ") must equal last committed token (" + std::to_string(last) + ")");
+  const int pre = m->cache_len;
+  if (pre < 1) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty cache");
+  const int prefix = pre - 1;
+  rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS);
+  if (rc == SPEC_OK)
+    cudaMemcpyAsync(m->logits_host, m->logits, (size_t)n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+  if (rc == SPEC_OK) rc = finish(m);
+  if (rc != SPEC_OK) return rc;
+  memcpy(out, m->logits_host, (size_t)n * m->cfg.vocab * 4);
+  // Restore (quantized_llama.rs:306-323): truncate to prefix and re-forward
+  // the root; its logits replace row 0 and become the cached next logits.
+  m->cache_len = prefix;
+  rc = forward_advance(m, &last, 1, nullptr);
+  if (rc != SPEC_OK) {
+    m->cache_len = pre;
+    return rc;
+  }
+  return copy_last_row(m, out);
+}
+
+int spec_tree_logits_keep_kv(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
+                             float* logits_out, float* hidden_out) {
+  if (!m || !tokens || !parents) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  m->last_valid = false;
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
+  int rc = check_tree(m, tokens, parents, n);
+  if (rc != SPEC_OK) return rc;
+  const uint32_t last = m->history.back();
+  if (tokens[0] != last)
+    return m->fail(SPEC_ERR_INVALID, "tree root (" + std::to_string(tokens[0]) +
+                                         ") must equal last committed token (" + std::to_string(last) + ")");
+  const int pre = m->cache_len;
+  if (pre < 1) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty cache");
+  const int prefix = pre - 1;
+  rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS | F_HIDDEN);
+  if (rc == SPEC_OK && logits_out)
+    cudaMemcpyAsync(m->logits_host, m->logits, (size_t)n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+  if (rc == SPEC_OK && hidden_out)
+    cudaMemcpyAsync(m->hidden_host, m->hidden_out, (size_t)n * m->cfg.hidden * 4, cudaMemcpyDeviceToHost, m->stream);
+  if (rc == SPEC_OK) rc = finish(m);
+  if (rc != SPEC_OK) return rc;
+  m->cache_len = prefix + n;
+  if (logits_out) memcpy(logits_out, m->logits_host, (size_t)n * m->cfg.vocab * 4);
+  if (hidden_out) memcpy(hidden_out, m->hidden_host, (size_t)n * m->cfg.hidden * 4);
+  return SPEC_OK;
+}
+
+int spec_commit_tree_path(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
+                          const int32_t* accepted, int n_acc) {
+  if (!m || !tokens || !parents || !accepted) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  m->last_valid = false;
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "commit_tree_path with empty history");
+  int rc = check_tree(m, tokens, parents, n);
+  if (rc != SPEC_OK) return rc;
+  if (n_acc < 1 || accepted[0] != 0) return m->fail(SPEC_ERR_INVALID, "accepted path must start at the root (0)");
+  const int prefix = (int)m->history.size() - 1;
+  for (int i = 0; i < n_acc; ++i) {
+    if (accepted[i] < 0 || accepted[i] >= n) return m->fail(SPEC_ERR_INVALID, "accepted index out of range");
+    if (prefix + accepted[i] >= m->cache_len)
+      return m->fail(SPEC_ERR_INVALID, "accepted node is not in the KV cache");
+  }
+  // keep = [0..prefix) ++ [prefix + ti]: the prefix is the identity, so only
+  // the accepted tree rows move (quantized_llama.rs:426-433).
+  int nmove = 0;
+  for (int i = 0; i < n_acc; ++i) {
+    const int src = prefix + accepted[i], dst = prefix + i;
+    if (src != dst) {
+      m->idx_host[nmove] = src;
+      m->idx_host[kMaxRows + nmove] = dst;
+      ++nmove;
+    }
+  }
+  if (nmove > 0) {
+    cudaError_t e = cudaMemcpyAsync(m->idx_dev, m->idx_host, 2 * kMaxRows * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess)
+      e = launch_kv_gather(m->kcache, m->vcache, m->cfg.n_layers, m->cfg.n_kv, m->t_max, m->cfg.head_dim, m->idx_dev,
+                           m->idx_dev + kMaxRows, nmove, m->kv_tmp, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "kv reorder"));
+  }
+  m->cache_len = prefix + n_acc;
+  for (int i = 1; i < n_acc; ++i) m->history.push_back(tokens[accepted[i]]);
+  return SPEC_OK;
+}
+
+int spec_last_hidden_state(spec_model* m, float* out) {
+  if (!m || !out) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "last_hidden_state with empty history");
+  const uint32_t last = m->history.back();
+  const int target = (int)m->history.size() - 1;
+  if (target > m->cache_len) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
+  const int saved = m->cache_len;
+  fill_step_causal(m, &last, 1, target);
+  int rc = run_forward(m, 1, F_HIDDEN);
+  if (rc == SPEC_OK)
+    cudaMemcpyAsync(m->hidden_host, m->hidden_out, (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost, m->stream);
+  if (rc == SPEC_OK) rc = finish(m);
+  if (rc != SPEC_OK) {
+    m->cache_len = saved;
+    return rc;
+  }
+  m->cache_len = target + 1;
+  memcpy(out, m->hidden_host, (size_t)m->cfg.hidden * 4);
+  return SPEC_OK;
+}
+
+int spec_observe_returning_last_hidden(spec_model* m, const uint32_t* ids, int n, float* hidden_out) {
+  if (!m || !ids || !hidden_out) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (n <= 0) return m->fail(SPEC_ERR_INVALID, "observe_returning_last_hidden with empty ids");
+  for (int i = 0; i < n; ++i)
+    if (ids[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  const int start = m->cache_len;
+  if (start + n > m->t_max) return m->fail(SPEC_ERR_INVALID, "KV capacity exceeded");
+  int done = 0;
+  while (done < n) {
+    const int M = std::min(kMaxRows, n - done);
+    fill_step_causal(m, ids + done, M, start + done);
+    const bool last = done + M == n;
+    int rc = run_forward(m, M, last ? F_HIDDEN : 0);
+    if (rc == SPEC_OK && last)
+      cudaMemcpyAsync(m->hidden_host, m->hidden_out + (size_t)(M - 1) * m->cfg.hidden, (size_t)m->cfg.hidden * 4,
+                      cudaMemcpyDeviceToHost, m->stream);
+    if (rc == SPEC_OK) rc = finish(m);
+    if (rc != SPEC_OK) {
+      m->cache_len = start;
+      return rc;
+    }
+    done += M;
+  }
+  m->cache_len = start + n;
+  m->history.insert(m->history.end(), ids, ids + n);
+  // The forward ran without the LM head, so no next-token logits are cached.
+  m->last_valid = false;
+  memcpy(hidden_out, m->hidden_host, (size_t)m->cfg.hidden * 4);
+  return SPEC_OK;
+}
+
+int spec_apply_lm_head(spec_model* m, const float* hidden, int rows, float* out) {
+  if (!m || !hidden || !out || rows < 0) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  const int H = m->cfg.hidden, V = m->cfg.vocab;
+  for (int r0 = 0; r0 < rows; r0 += kMaxRows) {
+    const int M = std::min(kMaxRows, rows - r0);
+    const int nt = (M + 7) / 8;
+    cudaError_t e = cudaMemcpyAsync(m->op_in, hidden + (size_t)r0 * H, (size_t)M * H * 4, cudaMemcpyHostToDevice,
+                                    m->stream);
+    if (e == cudaSuccess)
+      e = launch_make_operand(m->op_in, M, H, nt, m->xa, m->xa16, m->xa32, m->cfg.bf16 ? 1 : 0, m->stream);
+    QmvParams p = base_params(m, m->lm, M);
+    p.xfrag = m->xa;
+    p.xsum16 = m->xa16;
+    p.xsum32 = m->xa32;
+    p.epi = EPI_STORE;
+    p.out = m->logits;
+    p.ld_out = V;
+    if (e == cudaSuccess) e = launch_qmv(p, m->stream, false);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out + (size_t)r0 * V, m->logits, (size_t)M * V * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "apply_lm_head"));
+  }
+  return SPEC_OK;
+}
+
+int spec_embed_tokens(spec_model* m, const uint32_t* ids, int n, float* out) {
+  if (!m || !ids || !out || n < 0) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  const int H = m->cfg.hidden;
+  for (int i = 0; i < n; ++i)
+    if (ids[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  for (int r0 = 0; r0 < n; r0 += kMaxRows) {
+    const int M = std::min(kMaxRows, n - r0);
+    for (int i = 0; i < M; ++i) m->step_host->tokens[i] = (int)ids[r0 + i];
+    cudaError_t e = cudaMemcpyAsync(m->step_dev, m->step_host, sizeof(StepDev), cudaMemcpyHostToDevice, m->stream);
+    EmbedParams ep;
+    ep.table = m->embed_raw;
+    ep.fmt = m->embed_fmt;
+    ep.H = H;
+    ep.V = m->cfg.vocab;
+    ep.M = M;
+    ep.tokens = m->step_dev->tokens;
+    ep.h = m->op_in;
+    ep.ss_out = m->ss;
+    ep.norm = nullptr;
+    ep.frag = m->xb;  // scratch operand; not consumed
+    ep.xsum16 = m->xb16;
+    ep.xsum32 = m->xb32;
+    ep.act_bf16 = m->cfg.bf16 ? 1 : 0;
+    ep.err = m->err_dev;
+    if (e == cudaSuccess) e = launch_embed(ep, (M + 7) / 8, m->stream, false);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(out + (size_t)r0 * H, m->op_in, (size_t)M * H * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "embed_tokens"));
+  }
+  return SPEC_OK;
+}
+
+int spec_last_hidden_states_multi(spec_model* m, const int32_t* layers, int n_sel, float* final_out,
+                                  float* layer_outs) {
+  if (!m || !final_out || n_sel < 0 || (n_sel > 0 && (!layers || !layer_outs))) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "last_hidden_states_multi with empty history");
+  for (int i = 0; i < n_sel; ++i)
+    if (layers[i] < 0 || layers[i] >= m->cfg.n_layers)
+      return m->fail(SPEC_ERR_INVALID, "collect_layers[" + std::to_string(i) + "] = " + std::to_string(layers[i]) +
+                                           " out of range (n_layers=" + std::to_string(m->cfg.n_layers) + ")");
+  const int H = m->cfg.hidden;
+  if (!m->collect) {
+    cudaError_t e = m->dalloc(&m->collect, (size_t)m->cfg.n_layers * H * 4);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, "collect buffer"));
+  }
+  const uint32_t last = m->history.back();
+  const int target = (int)m->history.size() - 1;
+  if (target > m->cache_len) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
+  std::vector<int> sel(layers, layers + n_sel);
+  fill_step_causal(m, &last, 1, target);
+  const int saved = m->cache_len;
+  int rc = run_forward(m, 1, F_HIDDEN, &sel);
+  if (rc == SPEC_OK)
+    cudaMemcpyAsync(m->hidden_host, m->hidden_out, (size_t)H * 4, cudaMemcpyDeviceToHost, m->stream);
+  if (rc == SPEC_OK) rc = finish(m);
+  if (rc != SPEC_OK) {
+    m->cache_len = saved;
+    return rc;
+  }
+  memcpy(final_out, m->hidden_host, (size_t)H * 4);
+  if (n_sel > 0) {
+    cudaError_t e = cudaMemcpy(layer_outs, m->collect, (size_t)n_sel * H * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "collect copy"));
+  }
+  m->cache_len = target + 1;
+  return SPEC_OK;
+}
+
+int spec_verify_greedy(spec_model* m, const uint32_t* drafts, int k, int* n_accepted, uint32_t* next_token,
+                       int32_t* argmax_out) {
+  if (!m || !n_accepted || !next_token || k < 0 || (k > 0 && !drafts)) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "batched_logits with empty history");
+  if (k + 1 > kMaxRows) return m->fail(SPEC_ERR_UNSUPPORTED, "k+1 exceeds SPEC_MAX_ROWS");
+  for (int i = 0; i < k; ++i)
+    if (drafts[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  const int saved = m->cache_len;
+  const int target = (int)m->history.size() - 1;
+  if (target > m->cache_len) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
+  if (target + k + 1 > m->t_max) return m->fail(SPEC_ERR_INVALID, "KV capacity exceeded");
+  std::vector<uint32_t> combined(k + 1);
+  combined[0] = m->history.back();
+  if (k) memcpy(combined.data() + 1, drafts, (size_t)k * 4);
+  fill_step_causal(m, combined.data(), k + 1, target);
+  int rc = run_forward(m, k + 1, F_LOGITS);
+  if (rc == SPEC_OK) {
+    cudaError_t e = launch_row_argmax(m->logits, k + 1, m->cfg.vocab, m->argmax_dev, nullptr, m->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(m->argmax_host, m->argmax_dev, (size_t)(k + 1) * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "argmax"));
+  }
+  if (rc == SPEC_OK) rc = finish(m);
+  if (rc != SPEC_OK) {
+    m->cache_len = saved;
+    return rc;
+  }
+  m->cache_len = target + k + 1;
+  m->last_valid = true;
+  m->history.insert(m->history.end(), drafts, drafts + k);
+  int acc = 0;
+  while (acc < k && (uint32_t)m->argmax_host[acc] == drafts[acc]) ++acc;
+  *n_accepted = acc;
+  *next_token = (uint32_t)m->argmax_host[acc];
+  if (argmax_out) memcpy(argmax_out, m->argmax_host, (size_t)(k + 1) * 4);
+  return SPEC_OK;
+}
+
+int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
+                            int32_t* best_path, int* path_len, uint32_t* bonus) {
+  if (!m || !tokens || !parents || !best_path || !path_len || !bonus) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  m->last_valid = false;
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
+  int rc = check_tree(m, tokens, parents, n);
+  if (rc != SPEC_OK) return rc;
+  if (tokens[0] != m->history.back()) return m->fail(SPEC_ERR_INVALID, "tree root must equal last committed token");
+  const int pre = m->cache_len;
+  if (pre < 1) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty cache");
+  const int prefix = pre - 1;
+  rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS);
+  if (rc == SPEC_OK) {
+    cudaError_t e = launch_row_argmax(m->logits, n, m->cfg.vocab, m->argmax_dev, nullptr, m->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(m->argmax_host, m->argmax_dev, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "argmax"));
+  }
+  if (rc == SPEC_OK) rc = finish(m);
+  if (rc != SPEC_OK) return rc;
+  m->cache_len = prefix + n;
+  // eagle.rs:618-661: walk every root-to-leaf path (leaves in index order),
+  // count leading matches, keep the first longest.
+  std::vector<char> is_leaf(n, 1);
+  for (int i = 1; i < n; ++i) is_leaf[parents[i]] = 0;
+  std::vector<int> best = {0};
+  for (int leaf = 0; leaf < n; ++leaf) {
+    if (!is_leaf[leaf]) continue;
+    std::vector<int> chain;
+    for (int cur = leaf;; cur = parents[cur]) {
+      chain.push_back(cur);
+      if (cur == 0) break;
+    }
+    std::reverse(chain.begin(), chain.end());
+    int accepted = 0;
+    for (size_t w = 0; w + 1 < chain.size(); ++w) {
+      if ((uint32_t)m->argmax_host[chain[w]] == tokens[chain[w + 1]]) ++accepted;
+      else break;
+    }
+    if (accepted + 1 > (int)best.size()) best.assign(chain.begin(), chain.begin() + accepted + 1);
+  }
+  for (size_t i = 0; i < best.size(); ++i) best_path[i] = best[i];
+  *path_len = (int)best.size();
+  *bonus = (uint32_t)m->argmax_host[best.back()];
+  return SPEC_OK;
+}
+
+float spec_last_forward_ms(const spec_model* m) { return m ? m->last_ms : 0.f; }
+
+}  // extern "C"
+
+struct spec_qweight {
+  std::unique_ptr<spec_model> ctx;
+  Mat mat;
+  uint32_t* frag = nullptr;
+  float* x16 = nullptr;
+  float* x32 = nullptr;
+  float* y = nullptr;
+  void* flush = nullptr;
+  size_t flush_bytes = 0;
+  int last_M = 0;
+};
+
+extern "C" {
+
+int spec_qweight_upload(int ggml_type, const void* gguf_blocks, int n_rows, int k_cols, int device,
+                        spec_qweight** out) {
+  if (!out || !gguf_blocks || n_rows <= 0 || k_cols <= 0) return SPEC_ERR_INVALID;
+  *out = nullptr;
+  std::unique_ptr<spec_qweight> w(new (std::nothrow) spec_qweight());
+  if (!w) return SPEC_ERR_OOM;
+  w->ctx.reset(new spec_model());
+  spec_model* m = w->ctx.get();
+  spec_load_opts o = {};
+  o.device = device;
+  int rc = init_device(m, &o);
+  if (rc != SPEC_OK) {
+    g_load_error = m->err;
+    return rc;
+  }
+  Part p;
+  p.src = static_cast<const uint8_t*>(gguf_blocks);
+  p.on_device = false;
+  p.fmt = ggml_type;
+  p.rows = n_rows;
+  if (fmt_tile_bytes(ggml_type) == 0 || k_cols % fmt_kt(ggml_type) || n_rows % kGroupRows) {
+    g_load_error = "unsupported format or shape (rows must be a multiple of 128, K of the tile width)";
+    return SPEC_ERR_UNSUPPORTED;
+  }
+  rc = build_mat(m, {p}, k_cols, false, w->mat);
+  cudaError_t e = cudaSuccess;
+  const int groups = w->mat.seg[0].groups;
+  if (rc == SPEC_OK) e = m->dalloc(&w->frag, (size_t)k_cols * kMaxRows * 2);
+  if (e == cudaSuccess && rc == SPEC_OK) e = m->dalloc(&w->x16, (size_t)(k_cols / 16) * kMaxRows * 4);
+  if (e == cudaSuccess && rc == SPEC_OK) e = m->dalloc(&w->x32, (size_t)(k_cols / 32) * kMaxRows * 4);
+  if (e == cudaSuccess && rc == SPEC_OK) e = m->dalloc(&w->y, (size_t)n_rows * kMaxRows * 4);
+  if (e == cudaSuccess && rc == SPEC_OK)
+    e = m->dalloc(&m->gemv_part, (size_t)w->mat.S * groups * kGroupRows * kMaxRows * 4);
+  if (e == cudaSuccess && rc == SPEC_OK) e = m->dalloc(&m->counters, (size_t)groups * 4);
+  if (e == cudaSuccess && rc == SPEC_OK) e = m->dalloc(&m->err_dev, 16);
+  if (e == cudaSuccess && rc == SPEC_OK) e = cudaStreamSynchronize(m->stream);
+  if (rc == SPEC_OK && e != cudaSuccess) rc = m->fail(SPEC_ERR_OOM, cuda_msg(e, "qweight buffers"));
+  if (rc != SPEC_OK) {
+    g_load_error = m->err;
+    return rc;
+  }
+  *out = w.release();
+  return SPEC_OK;
+}
+
+void spec_qweight_free(spec_qweight* w) {
+  if (!w) return;
+  if (w->flush) {
+    cudaSetDevice(w->ctx->device);
+    cudaFree(w->flush);
+  }
+  delete w;
+}
+
+int64_t spec_qweight_bytes(const spec_qweight* w) { return w ? w->mat.bytes : 0; }
+
+static int qmatmul_enqueue(spec_qweight* w, int M, float* y_dev, cudaStream_t s) {
+  spec_model* m = w->ctx.get();
+  QmvParams p = base_params(m, w->mat, M);
+  p.act_bf16 = w->mat.seg[0].fmt == WF_BF16 ? 1 : 0;
+  p.xfrag = w->frag;
+  p.xsum16 = w->x16;
+  p.xsum32 = w->x32;
+  p.epi = EPI_STORE;
+  p.out = y_dev;
+  p.ld_out = w->mat.N;
+  cudaError_t e = launch_qmv(p, s, false);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "qmatmul launch"));
+  return SPEC_OK;
+}
+
+int spec_qmatmul(spec_qweight* w, const float* x_dev, int M, float* y_dev, void* stream) {
+  if (!w || !x_dev || !y_dev || M < 1 || M > kMaxRows) return SPEC_ERR_INVALID;
+  spec_model* m = w->ctx.get();
+  cudaSetDevice(m->device);
+  cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
+  const int nt = (M + 7) / 8;
+  cudaError_t e = launch_make_operand(x_dev, M, w->mat.K, nt, w->frag, w->x16, w->x32,
+                                      w->mat.seg[0].fmt == WF_BF16 ? 1 : 0, s);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "operand"));
+  w->last_M = M;
+  int rc = qmatmul_enqueue(w, M, y_dev, s);
+  if (rc != SPEC_OK) return rc;
+  if (!stream) {
+    e = cudaStreamSynchronize(s);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "qmatmul"));
+  }
+  return SPEC_OK;
+}
+
+int spec_qmatmul_time(spec_qweight* w, int M, int iters, int flush_l2, float* avg_ms) {
+  if (!w || !avg_ms || iters < 1 || M != w->last_M) return SPEC_ERR_INVALID;
+  spec_model* m = w->ctx.get();
+  cudaSetDevice(m->device);
+  cudaError_t e = cudaSuccess;
+  if (flush_l2 && !w->flush) {
+    w->flush_bytes = (size_t)512 << 20;
+    e = cudaMalloc(&w->flush, w->flush_bytes);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, "flush buffer"));
+  }
+  if (!m->ev0) {
+    e = cudaEventCreate(&m->ev0);
+    if (e == cudaSuccess) e = cudaEventCreate(&m->ev1);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "events"));
+  }
+  double total = 0.0;
+  for (int i = 0; i < iters; ++i) {
+    if (flush_l2) e = cudaMemsetAsync(w->flush, i & 0xff, w->flush_bytes, m->stream);
+    if (e == cudaSuccess) e = cudaEventRecord(m->ev0, m->stream);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "time"));
+    int rc = qmatmul_enqueue(w, M, w->y, m->stream);
+    if (rc != SPEC_OK) return rc;
+    e = cudaEventRecord(m->ev1, m->stream);
+    if (e == cudaSuccess) e = cudaEventSynchronize(m->ev1);
+    float ms = 0.f;
+    if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, m->ev0, m->ev1);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "time"));
+    total += ms;
+  }
+  *avg_ms = (float)(total / iters);
+  return SPEC_OK;
+}
+
+void* spec_cuda_stream(const spec_model* m) { return m ? static_cast<void*>(m->stream) : nullptr; }
+
+int spec_profile_forward(spec_model* m, const uint32_t* drafts, int k, float* ms_out, int* kind_out,
+                         int64_t* bytes_out, int cap) {
+  if (!m || k < 0 || (k > 0 && !drafts) || !ms_out || !kind_out || !bytes_out) return -SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (m->history.empty()) return -m->fail(SPEC_ERR_INVALID, "profile with empty history");
+  const int target = (int)m->history.size() - 1;
+  if (target > m->cache_len || target + k + 1 > m->t_max) return -m->fail(SPEC_ERR_INVALID, "bad cache state");
+  std::vector<uint32_t> combined(k + 1);
+  combined[0] = m->history.back();
+  if (k) memcpy(combined.data() + 1, drafts, (size_t)k * 4);
+  fill_step_causal(m, combined.data(), k + 1, target);
+  ProfRec pr;
+  cudaError_t e = enqueue_forward(m, k + 1, F_LOGITS, nullptr, &pr);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+  int n = 0;
+  if (e == cudaSuccess) {
+    for (size_t i = 0; i + 1 < pr.ev.size() && n < cap; ++i, ++n) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, pr.ev[i], pr.ev[i + 1]);
+      ms_out[n] = ms;
+      kind_out[n] = pr.kind[i];
+      bytes_out[n] = pr.bytes[i];
+    }
+  }
+  for (cudaEvent_t ev : pr.ev) cudaEventDestroy(ev);
+  // The forward rewrote KV rows [target, target + k]; the decoder's logical
+  // state (history, cache_len) is unchanged and later forwards overwrite them.
+  m->last_valid = false;
+  if (e != cudaSuccess) return -m->fail(SPEC_ERR_CUDA, cuda_msg(e, "profile"));
+  return n;
+}
+
+int spec_kernels_per_forward(const spec_model* m, int rows) {
+  (void)rows;
+  if (!m) return 0;
+  // embed + per layer (qkv, attn split, attn combine, o, gate/up, down) + lm_head
+  return 1 + 6 * m->cfg.n_layers + 1;
+}
+
+int64_t spec_weight_bytes(const spec_model* m) { return m ? m->weight_bytes : 0; }
+
+}  // extern "C"

@@ -1,0 +1,62 @@
+// Host-side model runtime of the verify-step backend (internal header).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <map>
+#include <string>
+#include <vector>
+
+#include "kernels.cuh"
+
+namespace specb200 {
+
+struct ModelCfg {
+  int arch = 0;  // 0 llama, 1 qwen2
+  int n_layers = 0, hidden = 0, n_heads = 0, n_kv = 0, head_dim = 0, ffn = 0, vocab = 0, ctx_len = 0;
+  float eps = 1e-5f, rope_theta = 10000.f;
+  bool rope_interleaved = true;  // GGUF Llama: rope_i; Qwen2 and BF16 Llama: rotate-half
+  bool bf16 = false;             // BF16 weights: bf16 activations and KV
+  bool has_bias = false;         // Qwen2 q/k/v biases
+  bool rope_scaled = false;      // Llama-3.1 frequency scaling
+  float rs_factor = 8.f, rs_low = 1.f, rs_high = 4.f;
+  int rs_orig = 8192;
+  bool rope_tables_bf16 = false; // BF16 model: cos/sin rounded to bf16
+};
+
+struct Mat {
+  uint8_t* tiles = nullptr;
+  WSeg seg[2];
+  int N = 0, K = 0, S = 1;
+  int64_t bytes = 0;
+};
+
+struct Layer {
+  Mat qkv, o, gu, down;
+  float* attn_norm = nullptr;
+  float* ffn_norm = nullptr;
+  float* bqkv = nullptr;
+};
+
+// Per-forward dynamic parameters, copied host -> device once per forward.
+struct StepDev {
+  int tokens[kMaxRows];
+  int positions[kMaxRows];
+  int slots[kMaxRows];
+  unsigned long long anc[kMaxRows];
+  int step[2];  // P (keys before the new rows), P + M
+  int pad[2];
+};
+
+// Source of one weight part while building a fused matrix.
+struct Part {
+  const uint8_t* src = nullptr;  // raw GGUF rows
+  bool on_device = false;
+  int fmt = 0;
+  int rows = 0;
+};
+
+int choose_split(int groups, int k_tiles_gcd, int num_sms);
+
+}  // namespace specb200

@@ -1,0 +1,276 @@
+"""``B200Decoder``: the reference's Decoder / TreeDecoder surface over the C ABI.
+
+Method names, argument meaning, return shapes and error classes follow the
+traits in crates/speculate/src/model/mod.rs:39-236 as implemented by
+``LlamaQuantDecoder`` (crates/speculate/src/model/quantized_llama.rs),
+``Qwen2QuantDecoder`` (quantized_qwen2.rs) and the BF16 ``LlamaDecoder``
+(llama.rs).  Where the trait returns ``Vec<f32>`` this returns a 1-D float32
+numpy array; ``Vec<Vec<f32>>`` becomes a 2-D array (rows x vocab); candle
+tensors (hidden states) become float32 arrays.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import List, Optional, Sequence, Tuple
+
+import numpy as np
+
+from . import _lib
+from .tree import DraftTree
+
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.uint32).reshape(-1))
+
+
+def _ptr(a: np.ndarray, ct):
+    return a.ctypes.data_as(ctypes.POINTER(ct))
+
+
+class B200Decoder:
+    """One model resident on one B200; stateful like the reference decoders."""
+
+    def __init__(self, handle: ctypes.c_void_p, eos_token_ids: Sequence[int] = ()):
+        self._lib = _lib.load()
+        self._h = handle
+        self._eos = [int(t) for t in eos_token_ids]
+        self._vocab = self._lib.spec_vocab_size(self._h)
+        self._hidden = self._lib.spec_hidden_size(self._h)
+
+    # ---- construction ----------------------------------------------------
+    @classmethod
+    def from_gguf(cls, path: str, device: int = 0, max_ctx: int = 0, use_graphs: bool = True,
+                  eos_token_ids: Sequence[int] = ()) -> "B200Decoder":
+        """LlamaQuantDecoder::from_gguf / Qwen2QuantDecoder::from_gguf (quantized_llama.rs:57-97)."""
+        lib = _lib.load()
+        opts = _lib.LoadOpts(device, max_ctx, 1 if use_graphs else 0)
+        h = ctypes.c_void_p()
+        _lib.check(lib.spec_load_gguf(path.encode(), ctypes.byref(opts), ctypes.byref(h)), None)
+        return cls(h, eos_token_ids)
+
+    @classmethod
+    def synthetic(cls, arch: str, n_layers: int, hidden: int, n_heads: int, n_kv_heads: int, ffn: int,
+                  vocab: int, rope_theta: float, eps: float, quant_mix: str = "Q4_K_M", seed: int = 0,
+                  device: int = 0, max_ctx: int = 0, use_graphs: bool = True, rope_half: bool = False,
+                  eos_token_ids: Sequence[int] = ()) -> "B200Decoder":
+        """A seeded synthetic model whose weights are generated on the device."""
+        lib = _lib.load()
+        mixes = {"Q4_K_M": 0, "Q5_K": 1, "Q8_0": 2, "BF16": 3}
+        d = _lib.ModelDesc(0 if arch == "llama" else 1, n_layers, hidden, n_heads, n_kv_heads, ffn, vocab,
+                           rope_theta, eps, mixes[quant_mix], 1 if rope_half else 0)
+        opts = _lib.LoadOpts(device, max_ctx, 1 if use_graphs else 0)
+        h = ctypes.c_void_p()
+        _lib.check(lib.spec_create_synthetic(ctypes.byref(d), seed, ctypes.byref(opts), ctypes.byref(h)), None)
+        return cls(h, eos_token_ids)
+
+    def close(self) -> None:
+        if self._h:
+            self._lib.spec_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def _check(self, rc: int) -> None:
+        _lib.check(rc, self._h)
+
+    # ---- Decoder -------------------------------------------------------------
+    def vocab_size(self) -> int:
+        return self._vocab
+
+    def hidden_size(self) -> int:
+        return self._hidden
+
+    def history(self) -> List[int]:
+        n = self._lib.spec_history_len(self._h)
+        buf = np.zeros(max(n, 1), dtype=np.uint32)
+        self._lib.spec_history(self._h, _ptr(buf, ctypes.c_uint32), n)
+        return [int(x) for x in buf[:n]]
+
+    def history_len(self) -> int:
+        return self._lib.spec_history_len(self._h)
+
+    def kv_len(self) -> int:
+        """The reference decoder's `cache_len`."""
+        return self._lib.spec_kv_len(self._h)
+
+    def eos_token_ids(self) -> List[int]:
+        return list(self._eos)
+
+    def reset(self) -> None:
+        self._check(self._lib.spec_reset(self._h))
+
+    def observe(self, ids: Sequence[int]) -> None:
+        a = _u32(ids)
+        self._check(self._lib.spec_observe(self._h, _ptr(a, ctypes.c_uint32), a.size))
+
+    def next_logits(self) -> np.ndarray:
+        out = np.empty(self._vocab, dtype=np.float32)
+        self._check(self._lib.spec_next_logits(self._h, _ptr(out, ctypes.c_float)))
+        return out
+
+    def batched_logits(self, drafts: Sequence[int]) -> np.ndarray:
+        a = _u32(drafts)
+        out = np.empty((a.size + 1, self._vocab), dtype=np.float32)
+        self._check(self._lib.spec_batched_logits(self._h, _ptr(a, ctypes.c_uint32), a.size,
+                                                  _ptr(out, ctypes.c_float)))
+        return out
+
+    def rollback_to(self, length: int) -> None:
+        self._check(self._lib.spec_rollback_to(self._h, int(length)))
+
+    # ---- TreeDecoder -----------------------------------------------------------
+    @staticmethod
+    def _tree_arrays(tree: DraftTree) -> Tuple[np.ndarray, np.ndarray]:
+        return _u32(tree.tokens()), np.ascontiguousarray(np.asarray(tree.parents(), dtype=np.int32))
+
+    def tree_logits(self, tree: DraftTree) -> np.ndarray:
+        t, p = self._tree_arrays(tree)
+        out = np.empty((t.size, self._vocab), dtype=np.float32)
+        self._check(self._lib.spec_tree_logits(self._h, _ptr(t, ctypes.c_uint32), _ptr(p, ctypes.c_int32), t.size,
+                                               _ptr(out, ctypes.c_float)))
+        return out
+
+    def tree_logits_keep_kv(self, tree: DraftTree) -> Tuple[np.ndarray, np.ndarray]:
+        t, p = self._tree_arrays(tree)
+        lo = np.empty((t.size, self._vocab), dtype=np.float32)
+        hi = np.empty((t.size, self._hidden), dtype=np.float32)
+        self._check(self._lib.spec_tree_logits_keep_kv(self._h, _ptr(t, ctypes.c_uint32), _ptr(p, ctypes.c_int32),
+                                                       t.size, _ptr(lo, ctypes.c_float), _ptr(hi, ctypes.c_float)))
+        return lo, hi
+
+    def commit_tree_path(self, tree: DraftTree, accepted: Sequence[int]) -> None:
+        t, p = self._tree_arrays(tree)
+        a = np.ascontiguousarray(np.asarray(accepted, dtype=np.int32))
+        self._check(self._lib.spec_commit_tree_path(self._h, _ptr(t, ctypes.c_uint32), _ptr(p, ctypes.c_int32),
+                                                    t.size, _ptr(a, ctypes.c_int32), a.size))
+
+    def last_hidden_state(self) -> np.ndarray:
+        out = np.empty(self._hidden, dtype=np.float32)
+        self._check(self._lib.spec_last_hidden_state(self._h, _ptr(out, ctypes.c_float)))
+        return out
+
+    def observe_returning_last_hidden(self, ids: Sequence[int]) -> np.ndarray:
+        a = _u32(ids)
+        out = np.empty(self._hidden, dtype=np.float32)
+        self._check(self._lib.spec_observe_returning_last_hidden(self._h, _ptr(a, ctypes.c_uint32), a.size,
+                                                                 _ptr(out, ctypes.c_float)))
+        return out
+
+    def apply_lm_head(self, hidden: np.ndarray) -> np.ndarray:
+        h = np.ascontiguousarray(np.asarray(hidden, dtype=np.float32))
+        lead = h.shape[:-1]
+        h2 = h.reshape(-1, self._hidden)
+        out = np.empty((h2.shape[0], self._vocab), dtype=np.float32)
+        self._check(self._lib.spec_apply_lm_head(self._h, _ptr(h2, ctypes.c_float), h2.shape[0],
+                                                 _ptr(out, ctypes.c_float)))
+        return out.reshape(*lead, self._vocab)
+
+    def embed_tokens(self, ids: Sequence[int]) -> np.ndarray:
+        a = _u32(ids)
+        out = np.empty((a.size, self._hidden), dtype=np.float32)
+        self._check(self._lib.spec_embed_tokens(self._h, _ptr(a, ctypes.c_uint32), a.size, _ptr(out, ctypes.c_float)))
+        return out
+
+    def last_hidden_states_multi(self, layers: Sequence[int]) -> Tuple[np.ndarray, List[np.ndarray]]:
+        sel = np.ascontiguousarray(np.asarray(layers, dtype=np.int32))
+        fin = np.empty(self._hidden, dtype=np.float32)
+        outs = np.empty((max(sel.size, 1), self._hidden), dtype=np.float32)
+        self._check(self._lib.spec_last_hidden_states_multi(self._h, _ptr(sel, ctypes.c_int32), sel.size,
+                                                            _ptr(fin, ctypes.c_float), _ptr(outs, ctypes.c_float)))
+        return fin, [outs[i].copy() for i in range(sel.size)]
+
+    def num_hidden_layers(self) -> int:
+        return self._lib.spec_num_layers(self._h)
+
+    # ---- device-side acceptance ----------------------------------------------------
+    def verify_greedy(self, drafts: Sequence[int]) -> Tuple[int, int, np.ndarray]:
+        """Batched verify + device argmax + temperature-0 accept walk.
+
+        Returns (n_accepted, next_token, row_argmax)."""
+        a = _u32(drafts)
+        n_acc = ctypes.c_int()
+        nxt = ctypes.c_uint32()
+        am = np.empty(a.size + 1, dtype=np.int32)
+        self._check(self._lib.spec_verify_greedy(self._h, _ptr(a, ctypes.c_uint32), a.size, ctypes.byref(n_acc),
+                                                 ctypes.byref(nxt), _ptr(am, ctypes.c_int32)))
+        return n_acc.value, nxt.value, am
+
+    def verify_tree_greedy(self, tree: DraftTree) -> Tuple[List[int], int]:
+        """Tree verify (KV kept) + device argmax + eagle.rs:618-661 path walk."""
+        t, p = self._tree_arrays(tree)
+        best = np.empty(t.size, dtype=np.int32)
+        plen = ctypes.c_int()
+        bonus = ctypes.c_uint32()
+        self._check(self._lib.spec_verify_tree_greedy(self._h, _ptr(t, ctypes.c_uint32), _ptr(p, ctypes.c_int32),
+                                                      t.size, _ptr(best, ctypes.c_int32), ctypes.byref(plen),
+                                                      ctypes.byref(bonus)))
+        return [int(x) for x in best[:plen.value]], bonus.value
+
+    # ---- diagnostics -----------------------------------------------------------------
+    def last_forward_ms(self) -> float:
+        return float(self._lib.spec_last_forward_ms(self._h))
+
+    def cuda_stream(self) -> int:
+        """cudaStream_t (as an int) the library runs this model's forwards on."""
+        return int(self._lib.spec_cuda_stream(self._h) or 0)
+
+    def profile_forward(self, drafts: Sequence[int]):
+        """Per-kernel (kind, ms, bytes) of one eager verify forward."""
+        a = _u32(drafts)
+        cap = 4096
+        ms = np.zeros(cap, dtype=np.float32)
+        kind = np.zeros(cap, dtype=np.int32)
+        nb = np.zeros(cap, dtype=np.int64)
+        n = self._lib.spec_profile_forward(self._h, _ptr(a, ctypes.c_uint32), a.size, _ptr(ms, ctypes.c_float),
+                                           _ptr(kind, ctypes.c_int), nb.ctypes.data_as(ctypes.POINTER(ctypes.c_int64)),
+                                           cap)
+        if n < 0:
+            self._check(-n)
+        return kind[:n].copy(), ms[:n].copy(), nb[:n].copy()
+
+    def kernels_per_forward(self, rows: int) -> int:
+        return int(self._lib.spec_kernels_per_forward(self._h, rows))
+
+    def weight_bytes(self) -> int:
+        return int(self._lib.spec_weight_bytes(self._h))
+
+
+class QWeight:
+    """Standalone dequant-matmul (candle ``QMatMul::forward``) over device buffers."""
+
+    def __init__(self, ggml_type: int, blocks: np.ndarray, n_rows: int, k_cols: int, device: int = 0):
+        self._lib = _lib.load()
+        b = np.ascontiguousarray(blocks)
+        h = ctypes.c_void_p()
+        _lib.check(self._lib.spec_qweight_upload(int(ggml_type), b.ctypes.data, n_rows, k_cols, device,
+                                                 ctypes.byref(h)), None)
+        self._h = h
+        self.n_rows, self.k_cols = n_rows, k_cols
+
+    def matmul(self, x_dev_ptr: int, m: int, y_dev_ptr: int, stream: Optional[int] = None) -> None:
+        _lib.check(self._lib.spec_qmatmul(self._h, ctypes.c_void_p(x_dev_ptr), m, ctypes.c_void_p(y_dev_ptr),
+                                          ctypes.c_void_p(stream) if stream else None), None)
+
+    def time_ms(self, m: int, iters: int, flush_l2: bool = True) -> float:
+        out = ctypes.c_float()
+        _lib.check(self._lib.spec_qmatmul_time(self._h, m, iters, 1 if flush_l2 else 0, ctypes.byref(out)), None)
+        return out.value
+
+    def nbytes(self) -> int:
+        return int(self._lib.spec_qweight_bytes(self._h))
+
+    def close(self) -> None:
+        if self._h:
+            self._lib.spec_qweight_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

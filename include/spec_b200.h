@@ -1,0 +1,196 @@
+/*
+ * spec_b200.h -- C ABI of the B200 verify-step backend.
+ *
+ * A drop-in replacement, for the target-model verify step, of the decoders
+ * behind abyo-speculate's `Decoder` / `TreeDecoder` traits
+ * (crates/speculate/src/model/mod.rs:39-108 and :118-236) as implemented by
+ * `LlamaQuantDecoder` (crates/speculate/src/model/quantized_llama.rs),
+ * `Qwen2QuantDecoder` (crates/speculate/src/model/quantized_qwen2.rs) and the
+ * BF16 `LlamaDecoder` (crates/speculate/src/model/llama.rs).  Every tensor op
+ * runs in this library's own sm_100a CUDA kernels.
+ *
+ * Conventions
+ *  - Plain pointers and sizes only.  The caller owns every host buffer; the
+ *    library owns all device memory.  "Rows" of logits are `vocab_size` f32.
+ *  - Every function returns a status (SPEC_OK = 0).  On error the decoder
+ *    state (history, KV length, cached logits) is unchanged, matching the
+ *    trait contract at crates/speculate/src/model/mod.rs:35-38.  No function
+ *    aborts or throws across the ABI.  `spec_last_error` gives the message.
+ *  - A handle is used by one thread at a time (the trait methods take
+ *    `&mut self`; the engine holds `Box<dyn TreeDecoder + Send>`,
+ *    crates/speculate/src/engine.rs:97).
+ */
+#ifndef SPEC_B200_H
+#define SPEC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes.  Mapping onto crates/speculate/src/error.rs:10-51:
+ *   SPEC_ERR_INVALID        -> Error::Sampling (bad argument / protocol misuse)
+ *   SPEC_ERR_CACHE_ROLLBACK -> Error::CacheRollback
+ *   SPEC_ERR_UNSUPPORTED    -> Error::UnsupportedMethod
+ *   SPEC_ERR_IO             -> Error::Io (GGUF open / parse)
+ *   SPEC_ERR_CUDA, _OOM, _TIMEOUT -> Error::Other / Error::Candle           */
+#define SPEC_OK 0
+#define SPEC_ERR_INVALID 1
+#define SPEC_ERR_CACHE_ROLLBACK 2
+#define SPEC_ERR_UNSUPPORTED 3
+#define SPEC_ERR_IO 4
+#define SPEC_ERR_CUDA 5
+#define SPEC_ERR_OOM 6
+#define SPEC_ERR_TIMEOUT 7
+
+/* Largest number of rows (k+1 verify rows, tree nodes, observe chunk) one
+ * forward processes; longer observes are chunked internally. */
+#define SPEC_MAX_ROWS 64
+
+typedef struct spec_model spec_model;
+
+typedef struct spec_load_opts {
+  int device;     /* CUDA device ordinal */
+  int max_ctx;    /* KV capacity in tokens; 0 = min(GGUF context_length, 4096) */
+  int use_graphs; /* 1 = replay one CUDA graph per row count (default), 0 = eager */
+  int reserved[5];
+} spec_load_opts;
+
+/* Shape of a seeded synthetic model (weights generated on the device). */
+typedef struct spec_model_desc {
+  int arch;       /* 0 = llama, 1 = qwen2 */
+  int n_layers, hidden, n_heads, n_kv_heads, ffn, vocab;
+  float rope_theta;
+  float eps;
+  int quant_mix;  /* 0 = Q4_K_M, 1 = Q5_K, 2 = Q8_0, 3 = BF16 */
+  int rope_half;  /* llama only: 1 = rotate-half RoPE (BF16 checkpoints), 0 = interleaved */
+  int reserved[6];
+} spec_model_desc;
+
+/* ---- lifetime -------------------------------------------------------------
+ * Replaces LlamaQuantDecoder::from_gguf (quantized_llama.rs:57-97) and
+ * Qwen2QuantDecoder::from_gguf (quantized_qwen2.rs) -> ModelWeights::from_gguf
+ * (quantized_llama_local.rs:217-308, quantized_qwen2_local.rs:210-300).       */
+int spec_load_gguf(const char* path, const spec_load_opts* opts, spec_model** out);
+/* Synthetic model: seeded N(0, 0.02) weights quantized on the device. */
+int spec_create_synthetic(const spec_model_desc* desc, uint64_t seed, const spec_load_opts* opts,
+                          spec_model** out);
+void spec_free(spec_model* m);
+/* Message of the last error on `m`; with m == NULL, of the last failed
+ * load on the calling thread. */
+const char* spec_last_error(const spec_model* m);
+
+/* ---- shape / state queries -------------------------------------------------
+ * Decoder::vocab_size, ::history, ::history_len (model/mod.rs:41-50);
+ * TreeDecoder::num_hidden_layers (mod.rs:177-182).                           */
+int spec_vocab_size(const spec_model* m);
+int spec_hidden_size(const spec_model* m);
+int spec_num_layers(const spec_model* m);
+int spec_history_len(const spec_model* m);
+/* Copies min(cap, history_len) tokens; returns the full history length. */
+int spec_history(const spec_model* m, uint32_t* out, int cap);
+/* Current KV length (the reference decoder's `cache_len`). */
+int spec_kv_len(const spec_model* m);
+int spec_max_ctx(const spec_model* m);
+
+/* ---- Decoder (model/mod.rs:39-108) ---------------------------------------- */
+/* Decoder::reset (mod.rs:52-53; quantized_llama.rs:512-517). */
+int spec_reset(spec_model* m);
+/* Decoder::observe (mod.rs:55-56; quantized_llama.rs:519-526). */
+int spec_observe(spec_model* m, const uint32_t* ids, int n);
+/* Decoder::next_logits (mod.rs:58-60; quantized_llama.rs:528-551); out: V f32. */
+int spec_next_logits(spec_model* m, float* out);
+/* Decoder::batched_logits (mod.rs:62-74; quantized_llama.rs:553-583);
+ * out: (k+1) x V f32.  Afterwards history += drafts. */
+int spec_batched_logits(spec_model* m, const uint32_t* drafts, int k, float* out);
+/* Decoder::rollback_to (mod.rs:76-80; quantized_llama.rs:585-599). */
+int spec_rollback_to(spec_model* m, int len);
+
+/* ---- TreeDecoder (model/mod.rs:118-236) ------------------------------------
+ * A draft tree is (tokens[n], parents[n]) in BFS order with parents[0]
+ * ignored and parents[i] < i (crates/speculate/src/tree.rs:38-74).          */
+/* TreeDecoder::tree_logits (mod.rs:135-144; quantized_llama.rs:262-325);
+ * out: n x V.  History and KV are restored. */
+int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out);
+/* TreeDecoder::tree_logits_keep_kv (mod.rs:196-210; quantized_llama.rs:341-394);
+ * logits_out: n x V (may be NULL), hidden_out: n x hidden (may be NULL).
+ * KV is left holding the prefix plus all n tree nodes. */
+int spec_tree_logits_keep_kv(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
+                             float* logits_out, float* hidden_out);
+/* TreeDecoder::commit_tree_path (mod.rs:223-235; quantized_llama.rs:409-440).
+ * accepted: node indices root-first (accepted[0] == 0). */
+int spec_commit_tree_path(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
+                          const int32_t* accepted, int n_acc);
+/* TreeDecoder::last_hidden_state (mod.rs:127-133; quantized_llama.rs:193-212). */
+int spec_last_hidden_state(spec_model* m, float* out);
+/* TreeDecoder::observe_returning_last_hidden (mod.rs:212-221; quantized_llama.rs:174-191). */
+int spec_observe_returning_last_hidden(spec_model* m, const uint32_t* ids, int n, float* hidden_out);
+/* TreeDecoder::apply_lm_head (mod.rs:146-156; quantized_llama.rs:112-121):
+ * rows x hidden f32 -> rows x V f32. */
+int spec_apply_lm_head(spec_model* m, const float* hidden, int rows, float* out);
+/* TreeDecoder::embed_tokens (mod.rs:184-194; quantized_llama_local.rs:328-330). */
+int spec_embed_tokens(spec_model* m, const uint32_t* ids, int n, float* out);
+/* TreeDecoder::last_hidden_states_multi (mod.rs:158-175; quantized_llama.rs:221-249):
+ * final_out: hidden f32; layer_outs: n_sel x hidden f32 (residual after layer). */
+int spec_last_hidden_states_multi(spec_model* m, const int32_t* layers, int n_sel, float* final_out,
+                                  float* layer_outs);
+
+/* ---- device-side acceptance ------------------------------------------------
+ * Greedy (temperature 0) vanilla verify: one batched forward of [last]+drafts
+ * (same protocol and state change as spec_batched_logits), then the argmax of
+ * every row on the device (first-max tie break, crates/speculate/src/
+ * sampling/tokens.rs:25-36) and the accept walk of methods/vanilla.rs:312-343
+ * at temperature 0.  Writes n_accepted (0..k) and the token that follows
+ * them (the argmax of row n_accepted).  Row argmaxes go to argmax_out[k+1]
+ * when it is non-NULL.  Only (k+1) ints cross to the host. */
+int spec_verify_greedy(spec_model* m, const uint32_t* drafts, int k, int* n_accepted, uint32_t* next_token,
+                       int32_t* argmax_out);
+/* Greedy tree acceptance of methods/eagle.rs:618-661 over a tree forward
+ * (spec_tree_logits_keep_kv semantics, KV kept): best_path receives the
+ * accepted node indices root-first (capacity n), *path_len its length, and
+ * *bonus the argmax of the deepest accepted node. */
+int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
+                            int32_t* best_path, int* path_len, uint32_t* bonus);
+
+/* ---- diagnostics -------------------------------------------------------- */
+/* Device time (ms, CUDA events) of the most recent forward. */
+float spec_last_forward_ms(const spec_model* m);
+/* The CUDA stream (cudaStream_t) every forward of `m` runs on, for callers
+ * that bracket calls with their own CUDA events. */
+void* spec_cuda_stream(const spec_model* m);
+/* One eager verify forward of [last] + drafts (the spec_batched_logits
+ * protocol, but the decoder's history / KV length are left unchanged and the
+ * cached next logits are dropped), with a CUDA event after every kernel.
+ * Writes per-kernel device ms, kind (0 embed, 1 qkv, 2 attention,
+ * 4 o-proj, 5 gate/up, 6 down, 7 lm_head) and algorithmic bytes (packed
+ * weights, or KV bytes for attention); returns the number of kernels, or a
+ * negated status on error. */
+int spec_profile_forward(spec_model* m, const uint32_t* drafts, int k, float* ms_out, int* kind_out,
+                         int64_t* bytes_out, int cap);
+/* Number of kernel launches one forward of `rows` rows performs. */
+int spec_kernels_per_forward(const spec_model* m, int rows);
+/* Total weight bytes streamed by one forward (packed weights, all layers + head). */
+int64_t spec_weight_bytes(const spec_model* m);
+
+/* ---- standalone dequant-matmul (QMatMul::forward, candle 0.8.4) -----------
+ * y[M][N] = x[M][K] . W^T on device buffers, for the microbench and tests.
+ * W is uploaded once from raw GGUF blocks (row-major [N][K/blk]).           */
+typedef struct spec_qweight spec_qweight;
+int spec_qweight_upload(int ggml_type, const void* gguf_blocks, int n_rows, int k_cols, int device,
+                        spec_qweight** out);
+void spec_qweight_free(spec_qweight* w);
+/* x_dev: M x K f32 (device), y_dev: M x N f32 (device); stream may be NULL. */
+int spec_qmatmul(spec_qweight* w, const float* x_dev, int M, float* y_dev, void* stream);
+/* Weight bytes of the packed matrix (equal to the GGUF byte count). */
+int64_t spec_qweight_bytes(const spec_qweight* w);
+/* Average device ms of the dequant kernel over `iters` launches of the last
+ * spec_qmatmul shape (CUDA events on the launching stream). */
+int spec_qmatmul_time(spec_qweight* w, int M, int iters, int flush_l2, float* avg_ms);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPEC_B200_H */

@@ -1,0 +1,221 @@
+"""Decoder / TreeDecoder parity through the C ABI against the oracle (GPU).
+
+Bars (north star): logits max-abs <= 2e-2 vs the oracle; decisions, history,
+KV lengths bit-exact; batched rows bit-identical to sequential rows
+(M-invariance) and tree row 0 bit-identical to next_logits.
+"""
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+TOL = 2e-2
+MODELS = ["llama_q4km", "llama_hd128", "qwen_q4km", "qwen_q5k", "qwen_q80", "llama_bf16"]
+
+
+def _pair(pkg, oracle, path, max_ctx=512):
+    dec = pkg.B200Decoder.from_gguf(path, max_ctx=max_ctx)
+    om = oracle.OracleModel(path, max_ctx=max_ctx)
+    return dec, oracle.OracleDecoder(om)
+
+
+def _prompt(vocab, n, seed):
+    return np.random.default_rng(seed).integers(0, vocab, size=n).tolist()
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_observe_next_and_batched_logits(pkg, oracle, tiny_gguf, name):
+    dec, ref = _pair(pkg, oracle, tiny_gguf(name))
+    prompt = _prompt(dec.vocab_size(), 37, 1)
+    dec.observe(prompt)
+    ref.observe(prompt)
+    assert np.abs(dec.next_logits() - ref.next_logits()).max() <= TOL
+    drafts = _prompt(dec.vocab_size(), 4, 2)
+    a = dec.batched_logits(drafts)
+    b = ref.batched_logits(drafts)
+    assert a.shape == (5, dec.vocab_size())
+    assert np.abs(a - b).max() <= TOL
+    assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+    # rollback + re-observe, as the vanilla loop does (vanilla.rs:358-362)
+    dec.rollback_to(len(prompt) + 2)
+    ref.rollback_to(len(prompt) + 2)
+    dec.observe([5])
+    ref.observe([5])
+    assert np.abs(dec.next_logits() - ref.next_logits()).max() <= TOL
+    assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+
+
+@pytest.mark.parametrize("name", ["llama_q4km", "qwen_q4km", "llama_bf16"])
+def test_long_observe_chunks(pkg, oracle, tiny_gguf, name):
+    dec, ref = _pair(pkg, oracle, tiny_gguf(name))
+    prompt = _prompt(dec.vocab_size(), 150, 3)  # > 64 rows: chunked forwards
+    dec.observe(prompt)
+    ref.observe(prompt)
+    assert np.abs(dec.next_logits() - ref.next_logits()).max() <= TOL
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_batched_equals_sequential_bitwise(pkg, tiny_gguf, name):
+    path = tiny_gguf(name)
+    a = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    b = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    prompt = _prompt(a.vocab_size(), 20, 4)
+    drafts = _prompt(a.vocab_size(), 8, 5)
+    a.observe(prompt)
+    rows = a.batched_logits(drafts)
+    b.observe(prompt)
+    seq = [b.next_logits()]
+    for d in drafts:
+        b.observe([d])
+        seq.append(b.next_logits())
+    for i in range(len(seq)):
+        assert np.array_equal(rows[i].view(np.uint32), seq[i].view(np.uint32)), f"row {i}"
+
+
+def _tree(pkg, root, vocab, seed):
+    rng = np.random.default_rng(seed)
+    nodes = [(0, root)]
+    for i in range(1, 12):
+        nodes.append((int(rng.integers(0, i)), int(rng.integers(0, vocab))))
+    return pkg.DraftTree.from_parent_table(nodes)
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_tree_logits_and_restore(pkg, oracle, tiny_gguf, name):
+    dec, ref = _pair(pkg, oracle, tiny_gguf(name))
+    prompt = _prompt(dec.vocab_size(), 30, 6)
+    dec.observe(prompt)
+    ref.observe(prompt)
+    nxt = dec.next_logits()
+    tree = _tree(pkg, prompt[-1], dec.vocab_size(), 7)
+    a = dec.tree_logits(tree)
+    b = ref.tree_logits(tree.tokens(), tree.parents())
+    assert np.abs(a - b).max() <= TOL
+    assert np.array_equal(a[0].view(np.uint32), nxt.view(np.uint32))
+    assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+    assert np.array_equal(dec.next_logits().view(np.uint32), nxt.view(np.uint32))
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_tree_keep_kv_commit_path(pkg, oracle, tiny_gguf, name):
+    dec, ref = _pair(pkg, oracle, tiny_gguf(name))
+    prompt = _prompt(dec.vocab_size(), 25, 8)
+    dec.observe(prompt)
+    ref.observe(prompt)
+    tree = _tree(pkg, prompt[-1], dec.vocab_size(), 9)
+    lo, hi = dec.tree_logits_keep_kv(tree)
+    rlo, rhi = ref.tree_logits_keep_kv(tree.tokens(), tree.parents())
+    assert np.abs(lo - rlo).max() <= TOL
+    assert np.abs(hi - rhi).max() <= TOL
+    assert dec.kv_len() == ref.cache_len
+    path = max(tree.paths(), key=len)
+    dec.commit_tree_path(tree, path)
+    ref.commit_tree_path(tree.tokens(), tree.parents(), path)
+    assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+    dec.observe([3])
+    ref.observe([3])
+    assert np.abs(dec.next_logits() - ref.next_logits()).max() <= TOL
+
+
+def test_commit_equals_linear_replay_bitwise(pkg, tiny_gguf):
+    """Committing a tree path leaves exactly the KV a plain replay would."""
+    path = tiny_gguf("llama_q4km")
+    a = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    b = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    prompt = _prompt(a.vocab_size(), 25, 10)
+    a.observe(prompt)
+    b.observe(prompt)
+    tree = _tree(pkg, prompt[-1], a.vocab_size(), 11)
+    a.tree_logits_keep_kv(tree)
+    chain = max(tree.paths(), key=len)
+    a.commit_tree_path(tree, chain)
+    b.observe([tree.token_at(i) for i in chain[1:]])
+    a.observe([7])
+    b.observe([7])
+    assert a.history() == b.history()
+    assert np.array_equal(a.next_logits().view(np.uint32), b.next_logits().view(np.uint32))
+
+
+@pytest.mark.parametrize("name", ["llama_q4km", "qwen_q80", "llama_bf16"])
+def test_hidden_embed_lm_head(pkg, oracle, tiny_gguf, name):
+    dec, ref = _pair(pkg, oracle, tiny_gguf(name))
+    ids = _prompt(dec.vocab_size(), 9, 12)
+    emb = dec.embed_tokens(ids)
+    assert np.array_equal(emb, ref.m.embed(ids).astype(np.float32))
+    dec.observe(ids)
+    ref.observe(ids)
+    h = dec.last_hidden_state()
+    rh, _ = ref.m.forward([ids[-1]], [len(ids) - 1], [len(ids) - 1], len(ids) - 1, [1])
+    assert np.abs(h - rh[0]).max() <= TOL
+    lo = dec.apply_lm_head(h[None])
+    assert np.abs(lo[0] - ref.m.lm_head(h[None].astype(np.float64))[0]).max() <= TOL
+    fin, mids = dec.last_hidden_states_multi([0, 1])
+    assert np.abs(fin - h).max() <= 1e-5 and len(mids) == 2
+    hid = dec.observe_returning_last_hidden([4, 5])
+    rh2, _ = ref.m.forward([4, 5], [len(ids), len(ids) + 1], [len(ids), len(ids) + 1], len(ids), [1, 3])
+    assert np.abs(hid - rh2[-1]).max() <= TOL
+
+
+@pytest.mark.parametrize("name", ["llama_q4km", "qwen_q4km"])
+def test_verify_greedy_decisions(pkg, accept, tiny_gguf, name):
+    path = tiny_gguf(name)
+    a = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    b = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    prompt = _prompt(a.vocab_size(), 16, 13)
+    a.observe(prompt)
+    b.observe(prompt)
+    # drafts = the model's own greedy continuation, one token corrupted
+    cont = []
+    for _ in range(4):
+        t = accept.argmax_first(b.next_logits())
+        cont.append(t)
+        b.observe([t])
+    b.rollback_to(len(prompt))
+    drafts = cont[:2] + [(cont[2] + 1) % a.vocab_size()] + cont[3:]
+    n_acc, nxt, am = a.verify_greedy(drafts)
+    rows = b.batched_logits(drafts)
+    exp_acc, exp_next = accept.greedy_linear_accept(rows, drafts)
+    assert (n_acc, nxt) == (exp_acc, exp_next) and n_acc == 2
+    assert list(am) == [accept.argmax_first(r) for r in rows]
+    assert a.history() == b.history() and a.kv_len() == b.kv_len()
+
+
+def test_verify_tree_greedy(pkg, accept, tiny_gguf):
+    path = tiny_gguf("llama_q4km")
+    a = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    b = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    prompt = _prompt(a.vocab_size(), 16, 14)
+    a.observe(prompt)
+    b.observe(prompt)
+    g1 = accept.argmax_first(b.next_logits())
+    b.observe([g1])
+    g2 = accept.argmax_first(b.next_logits())
+    b.rollback_to(len(prompt))
+    tree = pkg.DraftTree.from_parent_table([(0, prompt[-1]), (0, (g1 + 1) % 1024), (0, g1), (2, g2), (2, 5)])
+    best, bonus = a.verify_tree_greedy(tree)
+    rows, _ = b.tree_logits_keep_kv(tree)
+    eb, ebonus = accept.greedy_tree_accept(tree.tokens(), tree.parents(), rows)
+    assert (best, bonus) == (eb, ebonus) and best[:3] == [0, 2, 3]
+    assert a.kv_len() == b.kv_len()
+
+
+def test_error_behaviour(pkg, tiny_gguf):
+    dec = pkg.B200Decoder.from_gguf(tiny_gguf("llama_q4km"), max_ctx=128)
+    with pytest.raises(pkg.SamplingError):
+        dec.next_logits()  # empty history
+    dec.observe([1, 2, 3])
+    with pytest.raises(pkg.CacheRollbackError):
+        dec.rollback_to(4)
+    with pytest.raises(pkg.SamplingError):
+        dec.observe([10 ** 6])  # token out of range; state unchanged
+    assert dec.history() == [1, 2, 3] and dec.kv_len() == 3
+    with pytest.raises(pkg.SamplingError):
+        dec.tree_logits(pkg.DraftTree.linear(9, [1]))  # root != last committed
+    with pytest.raises(pkg.SamplingError):
+        dec.observe(list(range(200)))  # exceeds KV capacity
+    assert dec.kv_len() == 3
+    with pytest.raises(pkg.IoError):
+        pkg.B200Decoder.from_gguf("/nonexistent/model.gguf")
+    dec.reset()
+    assert dec.history() == [] and dec.kv_len() == 0
