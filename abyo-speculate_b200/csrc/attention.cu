@@ -243,8 +243,12 @@ SPEC_DEV void frag_store_a(uint32_t* frag, int nt_total, int m, int k, uint16_t 
   reinterpret_cast<uint16_t*>(frag)[hidx] = bits;
 }
 
-// One warp per (kv head, row r): merge the splits in order and emit the
-// O-projection operand for columns (kv*G + g)*hd + [0, hd).
+// One warp per (kv head, row r): merge the splits and emit the O-projection
+// operand for columns (kv*G + g)*hd + [0, hd).  Split weights are formed with
+// lane-strided partial sums and a fixed butterfly; the output rows are
+// accumulated in split order.  Splits past a row's last visible key carry
+// weight exactly 0, so the result does not depend on how many rows share the
+// call.
 template <int HD>
 __global__ void __launch_bounds__(128) attn_combine_kernel(const __grid_constant__ AttnParams p, int nt_total) {
   pdl_launch_dependents();
@@ -257,28 +261,51 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const __grid_constant
   const int m = r / p.G, gq = r % p.G;
   const int Ttot = p.step[1];
   const int ns = (Ttot + p.chunk - 1) / p.chunk;
+  const size_t base0 = (size_t)kvh * p.max_splits * R + r;  // + s * R
   float mx = -INFINITY;
-  for (int s = 0; s < ns; ++s) {
-    const size_t base = ((size_t)kvh * p.max_splits + s) * R + r;
-    mx = fmaxf(mx, p.part_ml[base * 2]);
+  for (int s = lane; s < ns; s += 32) mx = fmaxf(mx, __ldcg(p.part_ml + (base0 + (size_t)s * R) * 2));
+  mx = warp_max(mx);
+  float lsum = 0.f;
+  for (int s = lane; s < ns; s += 32) {
+    const float2 ml = __ldcg(reinterpret_cast<const float2*>(p.part_ml + (base0 + (size_t)s * R) * 2));
+    const float w = (ml.x == -INFINITY) ? 0.f : exp2f(ml.x - mx);
+    lsum += w * ml.y;
   }
-  float L = 0.f;
-  float acc[HD / 32];
+  lsum = warp_sum(lsum);
+  constexpr int C = HD / 32;
+  float acc[C];
 #pragma unroll
-  for (int c = 0; c < HD / 32; ++c) acc[c] = 0.f;
-  for (int s = 0; s < ns; ++s) {
-    const size_t base = ((size_t)kvh * p.max_splits + s) * R + r;
-    const float ms = p.part_ml[base * 2];
-    const float w = (ms == -INFINITY) ? 0.f : exp2f(ms - mx);
-    L += w * p.part_ml[base * 2 + 1];
-    const float* po = p.part_o + base * HD;
+  for (int c = 0; c < C; ++c) acc[c] = 0.f;
+  for (int s0 = 0; s0 < ns; s0 += 32) {
+    float wl = 0.f;
+    if (s0 + lane < ns) {
+      const float msv = __ldcg(p.part_ml + (base0 + (size_t)(s0 + lane) * R) * 2);
+      wl = (msv == -INFINITY) ? 0.f : exp2f(msv - mx);
+    }
+    const int cnt = ns - s0 < 32 ? ns - s0 : 32;
+    for (int j0 = 0; j0 < cnt; j0 += 8) {
+      float v[8][C];
 #pragma unroll
-    for (int c = 0; c < HD / 32; ++c) acc[c] += w * po[c * 32 + lane];
+      for (int q = 0; q < 8; ++q)
+        if (j0 + q < cnt) {
+          const float* po = p.part_o + (base0 + (size_t)(s0 + j0 + q) * R) * HD;
+#pragma unroll
+          for (int c = 0; c < C; ++c) v[q][c] = __ldcg(po + c * 32 + lane);
+        }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float w = __shfl_sync(0xffffffffu, wl, (j0 + q) & 31);
+        if (j0 + q < cnt) {
+#pragma unroll
+          for (int c = 0; c < C; ++c) acc[c] += w * v[q][c];
+        }
+      }
+    }
   }
-  const float inv = (L > 0.f) ? 1.f / L : 0.f;
+  const float inv = (lsum > 0.f) ? 1.f / lsum : 0.f;
   const int head = kvh * p.G + gq;
 #pragma unroll
-  for (int c = 0; c < HD / 32; ++c) {
+  for (int c = 0; c < C; ++c) {
     const int k = head * HD + c * 32 + lane;
     const float v = acc[c] * inv;
     float back;

@@ -44,6 +44,12 @@ constexpr int kGemvWarps = 4;          // warps per CTA
 constexpr int kGroupRows = 128;        // rows per CTA (4 warps x 32 rows)
 constexpr int kMaxRows = 64;           // max activation rows (M) per forward
 constexpr int kSsStride = 64;          // stride of per-group sum-of-squares slots
+constexpr int kMaxSsGroups = 64;       // hidden size <= 64 * 128
+
+// Number of 8-row fragment columns (n-tiles) the kernels use for M rows: the
+// GEMV is instantiated for 1, 2, 4 and 8, and every producer of an operand
+// must lay it out for the same count.
+__host__ __device__ constexpr int nt_for_rows(int M) { return M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; }
 
 // Epilogue applied by the CTA that owns the final sum of a 128-row group.
 enum Epi : int {
@@ -106,8 +112,12 @@ struct QmvParams {
   int act_bf16 = 0;                 // operand dtype: 0 f16, 1 bf16
 };
 
-// Launch one fused GEMV.  `nt` = ceil(M/8) selects the instantiation.
+// Launch one fused GEMV (persistent grid sized to occupancy); the
+// instantiation is picked by nt_for_rows(p.M).
 cudaError_t launch_qmv(const QmvParams& p, cudaStream_t stream, bool pdl);
+// Resident CTAs per SM of the GEMV for a (segment 0, segment 1) format pair
+// (on the current device).
+int qmv_ctas_per_sm(int fa, int fb);
 
 // Repack raw GGUF blocks (device, row-major [N][K/be][bb]) into pair tiles.
 cudaError_t launch_repack(const uint8_t* raw, int fmt, int N, int K, uint8_t* tiles, cudaStream_t s);

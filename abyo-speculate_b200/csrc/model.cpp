@@ -28,20 +28,29 @@ using namespace specb200;
 
 namespace specb200 {
 
-int choose_split(int groups, int k_tiles_gcd, int num_sms) {
+int choose_split(int groups, int k_tiles_gcd, int max_ctas) {
   const char* env = getenv("SPEC_B200_SPLIT");
   if (env) {
     const int s = atoi(env);
     if (s > 0 && k_tiles_gcd % s == 0) return s;
   }
-  // Smallest divisor of the tile count that gives at least one CTA per SM,
-  // keeping >= 2 tiles per warp where possible.
+  // The GEMV grid is persistent (max_ctas resident CTAs, each taking work
+  // units round-robin), so a split S gives groups*S units of k_tiles/S tiles
+  // per warp.  Score = load balance of the last round x per-unit overhead
+  // (about half a tile of epilogue per unit); pick the best divisor.
   int best = 1;
+  double best_score = -1.0;
   for (int s = 1; s <= k_tiles_gcd; ++s) {
     if (k_tiles_gcd % s) continue;
-    if (k_tiles_gcd / s < 2 && s > 1) break;
-    best = s;
-    if ((long)groups * s >= num_sms) break;
+    const double units = (double)groups * s;
+    const double rounds = units / max_ctas;
+    const double balance = rounds / ceil(rounds);
+    const double tps = (double)k_tiles_gcd / s;
+    const double score = balance * tps / (tps + 0.5);
+    if (score > best_score + 1e-9) {
+      best_score = score;
+      best = s;
+    }
   }
   return best;
 }
@@ -304,7 +313,8 @@ int build_mat(spec_model* m, const std::vector<Part>& parts, int K, bool interle
   }
   if (runs.size() == 1) out.seg[1] = WSeg{};
   const int groups = out.seg[0].groups + out.seg[1].groups;
-  out.S = choose_split(groups, kgcd, m->num_sms);
+  const int fa = out.seg[0].fmt, fb = out.seg[1].groups ? out.seg[1].fmt : fa;
+  out.S = choose_split(groups, kgcd, qmv_ctas_per_sm(fa, fb) * m->num_sms);
   for (int si = 0; si < 2; ++si)
     if (out.seg[si].groups) out.seg[si].tiles_per_split = out.seg[si].k_tiles / out.S;
   return SPEC_OK;
@@ -346,7 +356,9 @@ int alloc_runtime(spec_model* m) {
   ALLOC(m->xc16, (size_t)(F / 16) * kMaxRows * 4);
   ALLOC(m->xc32, (size_t)(F / 32) * kMaxRows * 4);
   ALLOC(m->qbuf, (size_t)c.n_heads * kMaxRows * hd * 2);
-  m->attn_chunk = m->t_max <= 4096 ? 64 : (m->t_max <= 16384 ? 128 : 256);
+  // Keys per attention split (fixed per model: splits are aligned to absolute
+  // key positions, which keeps every row's arithmetic independent of M).
+  m->attn_chunk = m->t_max <= 8192 ? 128 : 256;
   m->attn_max_splits = (m->t_max + m->attn_chunk - 1) / m->attn_chunk;
   const size_t R = (size_t)kMaxRows * G;
   ALLOC(m->part_o, (size_t)c.n_kv * m->attn_max_splits * R * hd * 4);
@@ -480,7 +492,7 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
                             ProfRec* pr = nullptr) {
   const ModelCfg& c = m->cfg;
   const int H = c.hidden, hd = c.head_dim, G = c.n_heads / c.n_kv;
-  const int nt = (M + 7) / 8;
+  const int nt = nt_for_rows(M);
   cudaStream_t s = m->stream;
   cudaError_t e = cudaMemcpyAsync(m->step_dev, m->step_host, sizeof(StepDev), cudaMemcpyHostToDevice, s);
   if (e != cudaSuccess) return e;
@@ -884,7 +896,7 @@ int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) 
   c.bf16 = te->type == WF_BF16 || g0->type == WF_BF16;
   c.rope_tables_bf16 = c.bf16 && c.arch == 0;
   if (c.hidden % kGroupRows || c.ffn % kGroupRows || (c.head_dim != 64 && c.head_dim != 128) ||
-      c.n_heads % c.n_kv)
+      c.n_heads % c.n_kv || c.hidden / kGroupRows > kMaxSsGroups)
     return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported model shape");
 
   auto part_of = [&](const std::string& name, int K, Part& p) -> bool {
@@ -1064,6 +1076,7 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
     c.rope_scaled = true;
   }
   if (c.n_layers <= 0 || c.hidden % kGroupRows || c.ffn % kGroupRows || c.vocab % kGroupRows ||
+      c.hidden / kGroupRows > kMaxSsGroups ||
       (c.head_dim != 64 && c.head_dim != 128) || c.n_heads % c.n_kv)
     return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported synthetic model shape");
   const int H = c.hidden, F = c.ffn, hd = c.head_dim;
@@ -1406,7 +1419,7 @@ int spec_apply_lm_head(spec_model* m, const float* hidden, int rows, float* out)
   const int H = m->cfg.hidden, V = m->cfg.vocab;
   for (int r0 = 0; r0 < rows; r0 += kMaxRows) {
     const int M = std::min(kMaxRows, rows - r0);
-    const int nt = (M + 7) / 8;
+    const int nt = nt_for_rows(M);
     cudaError_t e = cudaMemcpyAsync(m->op_in, hidden + (size_t)r0 * H, (size_t)M * H * 4, cudaMemcpyHostToDevice,
                                     m->stream);
     if (e == cudaSuccess)
@@ -1452,7 +1465,7 @@ int spec_embed_tokens(spec_model* m, const uint32_t* ids, int n, float* out) {
     ep.xsum32 = m->xb32;
     ep.act_bf16 = m->cfg.bf16 ? 1 : 0;
     ep.err = m->err_dev;
-    if (e == cudaSuccess) e = launch_embed(ep, (M + 7) / 8, m->stream, false);
+    if (e == cudaSuccess) e = launch_embed(ep, nt_for_rows(M), m->stream, false);
     if (e == cudaSuccess)
       e = cudaMemcpyAsync(out + (size_t)r0 * H, m->op_in, (size_t)M * H * 4, cudaMemcpyDeviceToHost, m->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
@@ -1679,7 +1692,7 @@ int spec_qmatmul(spec_qweight* w, const float* x_dev, int M, float* y_dev, void*
   spec_model* m = w->ctx.get();
   cudaSetDevice(m->device);
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
-  const int nt = (M + 7) / 8;
+  const int nt = nt_for_rows(M);
   cudaError_t e = launch_make_operand(x_dev, M, w->mat.K, nt, w->frag, w->x16, w->x32,
                                       w->mat.seg[0].fmt == WF_BF16 ? 1 : 0, s);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "operand"));

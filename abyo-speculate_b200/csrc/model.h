@@ -57,6 +57,6 @@ struct Part {
   int rows = 0;
 };
 
-int choose_split(int groups, int k_tiles_gcd, int num_sms);
+int choose_split(int groups, int k_tiles_gcd, int max_ctas);
 
 }  // namespace specb200

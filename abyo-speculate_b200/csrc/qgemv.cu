@@ -31,36 +31,31 @@
 #include "common.cuh"
 #include "kernels.cuh"
 
+#include <stdlib.h>
+
 namespace specb200 {
 
 namespace {
 
+// ---------------------------------------------------------------------------
+// Static tile geometry per format / n-tile count.
+// ---------------------------------------------------------------------------
+template <int F, int NT>
+struct Geo {
+  static constexpr int KT = fmt_kt(F);
+  static constexpr int KS = KT / 16;                        // k-steps per tile
+  static constexpr int PAIR = fmt_pair_bytes(F);            // weight bytes per pair tile
+  static constexpr int XFRAG = KS * NT * 256;               // operand fragments per tile
+  static constexpr int X32 = (F == WF_BF16) ? 0 : (KT / 32) * 8 * NT * 4;
+  static constexpr int X16 = (F == WF_BF16) ? 0 : KS * 8 * NT * 4;
+  static constexpr int XB = XFRAG + X32 + X16;              // operand bytes per tile
+};
+
+constexpr int kWStages = 2;      // weight ring stages per warp
+constexpr int kXStages = 2;      // operand ring stages per CTA
+constexpr int kScratch = 2048;   // per-warp decoded-scale scratch (bytes)
+
 SPEC_DEV float h2f_bits(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xffffu))); }
-
-// ---------------------------------------------------------------------------
-// Activation operand access
-// ---------------------------------------------------------------------------
-template <int NT>
-SPEC_DEV void load_b(const QmvParams& p, int ks, int lane, uint32_t (&b)[NT][2]) {
-  const int g = lane >> 2;
-#pragma unroll
-  for (int nt = 0; nt < NT; ++nt) {
-    if (nt * 8 + g < p.M) {
-      const uint2 v = __ldg(reinterpret_cast<const uint2*>(p.xfrag) + ((size_t)ks * NT + nt) * 32 + lane);
-      b[nt][0] = v.x;
-      b[nt][1] = v.y;
-    } else {
-      b[nt][0] = 0u;
-      b[nt][1] = 0u;
-    }
-  }
-}
-
-template <int NT>
-SPEC_DEV float2 load_xs(const float* xs, int blk, int nt, int lane) {
-  const int t = lane & 3;
-  return __ldg(reinterpret_cast<const float2*>(xs + (size_t)blk * (8 * NT) + nt * 8 + 2 * t));
-}
 
 // Q4_K / Q5_K: unpack sub-block b's 6-bit (scale, min) from the 12 packed
 // bytes held in m.y (bytes 0-3), m.z (4-7), m.w (8-11).
@@ -86,131 +81,108 @@ SPEC_DEV void a_from_nibbles(uint32_t w, uint32_t (&a)[4]) {
   a[3] = lop3_and_or(w >> 12, 0x000F000Fu, 0x64006400u);
 }
 
-template <int NT>
-SPEC_DEV void mma_sub(const uint32_t (&a)[4], const uint32_t (&b)[NT][2], int nt, float c0, float c1, float (&d)[4]) {
-  mma_f16(d, a[0], a[1], a[2], a[3], b[nt][0], b[nt][1], c0, c1, c0, c1);
-}
-template <int NT>
-SPEC_DEV void mma_acc(const uint32_t (&a)[4], const uint32_t (&b)[NT][2], int nt, float (&d)[4]) {
-  mma_f16(d, a[0], a[1], a[2], a[3], b[nt][0], b[nt][1], d[0], d[1], d[2], d[3]);
-}
-
 // ---------------------------------------------------------------------------
-// Per-format pair-tile processing.  `tp` = pair tile in shared memory,
-// `ks0` = global k-step (16 columns) of the tile's first column.
+// Cooperative scale decode: lane l decodes row l of the pair tile (rows
+// 0-15 = tile 0, 16-31 = tile 1) into the warp's scratch, laid out so that
+// lane (g, t) later reads rows g and g+8 with one vector load.
 // ---------------------------------------------------------------------------
-template <int NT>
-SPEC_DEV void tile_q4k(const uint8_t* tp, int ks0, const QmvParams& p, int lane, float (&acc)[2][NT][4]) {
-  constexpr int TB = 2304;
-  const int g = lane >> 2;
-  uint4 meta[2][2];
+template <int F>
+SPEC_DEV void decode_scales(const uint8_t* tp, float* scr, int lane) {
+  constexpr int TB = fmt_tile_bytes(F);
+  const int rt = lane >> 4, ri = lane & 15;
+  if constexpr (F == WF_Q4_K || F == WF_Q5_K) {
+    constexpr int MO = (F == WF_Q4_K) ? 2048 : 2560;
+    const uint4 m = *reinterpret_cast<const uint4*>(tp + rt * TB + MO + ri * 16);
+    const float d = h2f_bits(m.x), dm = h2f_bits(m.x >> 16);
 #pragma unroll
-  for (int rt = 0; rt < 2; ++rt) {
-    meta[rt][0] = *reinterpret_cast<const uint4*>(tp + rt * TB + 2048 + g * 16);
-    meta[rt][1] = *reinterpret_cast<const uint4*>(tp + rt * TB + 2048 + (g + 8) * 16);
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    uint32_t bq[4][NT][2];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) load_b<NT>(p, ks0 + 4 * j + i, lane, bq[i]);
-    float2 xs[2][NT];
-#pragma unroll
-    for (int sb = 0; sb < 2; ++sb)
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) xs[sb][nt] = load_xs<NT>(p.xsum32, ks0 / 2 + 2 * j + sb, nt, lane);
-#pragma unroll
-    for (int rt = 0; rt < 2; ++rt) {
-      const uint4 qw = *reinterpret_cast<const uint4*>(tp + rt * TB + j * 512 + lane * 16);
-      const uint32_t wv[4] = {qw.x, qw.y, qw.z, qw.w};
-#pragma unroll
-      for (int sb = 0; sb < 2; ++sb) {
-        const int b = 2 * j + sb;
-        float s[2], c[2];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          int sc, mn;
-          k4_scale_min(meta[rt][r], b, sc, mn);
-          s[r] = h2f_bits(meta[rt][r].x) * (float)sc;
-          c[r] = h2f_bits(meta[rt][r].x >> 16) * (float)mn;
-        }
-        uint32_t a0[4], a1[4];
-        a_from_nibbles(wv[2 * sb], a0);
-        a_from_nibbles(wv[2 * sb + 1], a1);
-#pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const float c0 = -1024.f * xs[sb][nt].x, c1 = -1024.f * xs[sb][nt].y;
-          float d[4];
-          mma_sub<NT>(a0, bq[2 * sb], nt, c0, c1, d);
-          mma_acc<NT>(a1, bq[2 * sb + 1], nt, d);
-          float* ac = acc[rt][nt];
-          ac[0] = fmaf(s[0], d[0], fmaf(-c[0], xs[sb][nt].x, ac[0]));
-          ac[1] = fmaf(s[0], d[1], fmaf(-c[0], xs[sb][nt].y, ac[1]));
-          ac[2] = fmaf(s[1], d[2], fmaf(-c[1], xs[sb][nt].x, ac[2]));
-          ac[3] = fmaf(s[1], d[3], fmaf(-c[1], xs[sb][nt].y, ac[3]));
-        }
-      }
+    for (int sb = 0; sb < 8; ++sb) {
+      int sc, mn;
+      k4_scale_min(m, sb, sc, mn);
+      *reinterpret_cast<float2*>(scr + ((rt * 8 + sb) * 8 + (ri & 7)) * 4 + (ri >> 3) * 2) =
+          make_float2(d * (float)sc, dm * (float)mn);
     }
+  } else if constexpr (F == WF_Q6_K) {
+    const uint4 sv = *reinterpret_cast<const uint4*>(tp + rt * TB + 3072 + ri * 16);
+    const float d = h2f_bits(*reinterpret_cast<const uint16_t*>(tp + rt * TB + 3328 + ri * 2));
+    const uint32_t w4[4] = {sv.x, sv.y, sv.z, sv.w};
+#pragma unroll
+    for (int b = 0; b < 16; ++b)
+      scr[((rt * 16 + b) * 8 + (ri & 7)) * 2 + (ri >> 3)] = d * (float)(int8_t)((w4[b >> 2] >> (8 * (b & 3))) & 0xff);
+  } else if constexpr (F == WF_Q8_0) {
+    const uint2 dv = *reinterpret_cast<const uint2*>(tp + rt * TB + 2048 + ri * 8);
+    const uint32_t w2[2] = {dv.x, dv.y};
+#pragma unroll
+    for (int b = 0; b < 4; ++b)
+      scr[((rt * 4 + b) * 8 + (ri & 7)) * 2 + (ri >> 3)] = h2f_bits(w2[b >> 1] >> (16 * (b & 1)));
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Per-format pair-tile compute.  tp: weights (shared), xs: operand stage
+// (shared; fragments, then xsum32, then xsum16), scr: decoded scales.
+// ---------------------------------------------------------------------------
+template <int NT>
+SPEC_DEV void load_bfrag(const uint8_t* xs, int kk, int lane, uint32_t (&b)[NT][2]) {
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const uint2 v = *reinterpret_cast<const uint2*>(xs + (kk * NT + nt) * 256 + lane * 8);
+    b[nt][0] = v.x;
+    b[nt][1] = v.y;
   }
 }
 
 template <int NT>
-SPEC_DEV void tile_q5k(const uint8_t* tp, int ks0, const QmvParams& p, int lane, float (&acc)[2][NT][4]) {
-  constexpr int TB = 2816;
+SPEC_DEV float2 load_sum(const uint8_t* base, int blk, int nt, int lane) {
+  return *reinterpret_cast<const float2*>(base + ((blk * NT + nt) * 8 + 2 * (lane & 3)) * 4);
+}
+
+template <int NT>
+SPEC_DEV void tile_q45k(const uint8_t* tp, const uint8_t* xs, const float* scr, int lane, bool q5,
+                        float (&acc)[2][NT][4]) {
+  const int TB = q5 ? 2816 : 2304;
   const int g = lane >> 2;
-  uint4 meta[2][2];
+  const uint8_t* x32 = xs + 16 * NT * 256;
 #pragma unroll
-  for (int rt = 0; rt < 2; ++rt) {
-    meta[rt][0] = *reinterpret_cast<const uint4*>(tp + rt * TB + 2560 + g * 16);
-    meta[rt][1] = *reinterpret_cast<const uint4*>(tp + rt * TB + 2560 + (g + 8) * 16);
-  }
-#pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < 4; ++j) {  // 4 k-steps = 2 sub-blocks of 32
     uint32_t bq[4][NT][2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) load_b<NT>(p, ks0 + 4 * j + i, lane, bq[i]);
-    float2 xs[2][NT];
+    for (int i = 0; i < 4; ++i) load_bfrag<NT>(xs, 4 * j + i, lane, bq[i]);
+    float2 xsum[2][NT];
 #pragma unroll
     for (int sb = 0; sb < 2; ++sb)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) xs[sb][nt] = load_xs<NT>(p.xsum32, ks0 / 2 + 2 * j + sb, nt, lane);
+      for (int nt = 0; nt < NT; ++nt) xsum[sb][nt] = load_sum<NT>(x32, 2 * j + sb, nt, lane);
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt) {
       const uint4 qw = *reinterpret_cast<const uint4*>(tp + rt * TB + j * 512 + lane * 16);
-      const uint32_t hw = *reinterpret_cast<const uint32_t*>(tp + rt * TB + 2048 + j * 128 + lane * 4);
       const uint32_t wv[4] = {qw.x, qw.y, qw.z, qw.w};
+      uint32_t hw = 0;
+      if (q5) hw = *reinterpret_cast<const uint32_t*>(tp + rt * TB + 2048 + j * 128 + lane * 4);
 #pragma unroll
       for (int sb = 0; sb < 2; ++sb) {
-        const int b = 2 * j + sb;
-        float s[2], c[2];
-#pragma unroll
-        for (int r = 0; r < 2; ++r) {
-          int sc, mn;
-          k4_scale_min(meta[rt][r], b, sc, mn);
-          s[r] = h2f_bits(meta[rt][r].x) * (float)sc;
-          c[r] = h2f_bits(meta[rt][r].x >> 16) * (float)mn;
-        }
+        const float4 sc = *reinterpret_cast<const float4*>(scr + ((rt * 8 + 2 * j + sb) * 8 + g) * 4);
         uint32_t a[2][4];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const int i = 2 * sb + h;  // k-step within the group of 4
+          const int i = 2 * sb + h;
+          a_from_nibbles(wv[i], a[h]);
+          if (q5) {
 #pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            const uint32_t base = lop3_and_or(wv[i] >> (4 * jj), 0x000F000Fu, 0x64006400u);
-            a[h][jj] = lop3_or_and(base, shift_signed(hw, 4 * i + jj - 4), 0x00100010u);
+            for (int jj = 0; jj < 4; ++jj) a[h][jj] = lop3_or_and(a[h][jj], shift_signed(hw, 4 * i + jj - 4), 0x00100010u);
           }
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const float c0 = -1024.f * xs[sb][nt].x, c1 = -1024.f * xs[sb][nt].y;
+          const float c0 = -1024.f * xsum[sb][nt].x, c1 = -1024.f * xsum[sb][nt].y;
           float d[4];
-          mma_sub<NT>(a[0], bq[2 * sb], nt, c0, c1, d);
-          mma_acc<NT>(a[1], bq[2 * sb + 1], nt, d);
+          mma_f16(d, a[0][0], a[0][1], a[0][2], a[0][3], bq[2 * sb][nt][0], bq[2 * sb][nt][1], c0, c1, c0, c1);
+          mma_f16(d, a[1][0], a[1][1], a[1][2], a[1][3], bq[2 * sb + 1][nt][0], bq[2 * sb + 1][nt][1], d[0], d[1],
+                  d[2], d[3]);
           float* ac = acc[rt][nt];
-          ac[0] = fmaf(s[0], d[0], fmaf(-c[0], xs[sb][nt].x, ac[0]));
-          ac[1] = fmaf(s[0], d[1], fmaf(-c[0], xs[sb][nt].y, ac[1]));
-          ac[2] = fmaf(s[1], d[2], fmaf(-c[1], xs[sb][nt].x, ac[2]));
-          ac[3] = fmaf(s[1], d[3], fmaf(-c[1], xs[sb][nt].y, ac[3]));
+          ac[0] = fmaf(sc.x, d[0], fmaf(-sc.y, xsum[sb][nt].x, ac[0]));
+          ac[1] = fmaf(sc.x, d[1], fmaf(-sc.y, xsum[sb][nt].y, ac[1]));
+          ac[2] = fmaf(sc.z, d[2], fmaf(-sc.w, xsum[sb][nt].x, ac[2]));
+          ac[3] = fmaf(sc.z, d[3], fmaf(-sc.w, xsum[sb][nt].y, ac[3]));
         }
       }
     }
@@ -218,56 +190,49 @@ SPEC_DEV void tile_q5k(const uint8_t* tp, int ks0, const QmvParams& p, int lane,
 }
 
 template <int NT>
-SPEC_DEV void tile_q6k(const uint8_t* tp, int ks0, const QmvParams& p, int lane, float (&acc)[2][NT][4]) {
+SPEC_DEV void tile_q6k(const uint8_t* tp, const uint8_t* xs, const float* scr, int lane, float (&acc)[2][NT][4]) {
   constexpr int TB = 3360;
   const int g = lane >> 2;
-  uint4 scl[2][2];
-  float dd[2][2];
-#pragma unroll
-  for (int rt = 0; rt < 2; ++rt) {
-    scl[rt][0] = *reinterpret_cast<const uint4*>(tp + rt * TB + 3072 + g * 16);
-    scl[rt][1] = *reinterpret_cast<const uint4*>(tp + rt * TB + 3072 + (g + 8) * 16);
-    dd[rt][0] = h2f_bits(*reinterpret_cast<const uint16_t*>(tp + rt * TB + 3328 + g * 2));
-    dd[rt][1] = h2f_bits(*reinterpret_cast<const uint16_t*>(tp + rt * TB + 3328 + (g + 8) * 2));
-  }
+  const uint8_t* x16 = xs + 16 * NT * 256 + 8 * 8 * NT * 4;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
     uint32_t bq[4][NT][2];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) load_b<NT>(p, ks0 + 4 * j + i, lane, bq[i]);
-    float2 xs[4][NT];
+    for (int i = 0; i < 4; ++i) load_bfrag<NT>(xs, 4 * j + i, lane, bq[i]);
+    float2 xsum[4][NT];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
-      for (int nt = 0; nt < NT; ++nt) xs[i][nt] = load_xs<NT>(p.xsum16, ks0 + 4 * j + i, nt, lane);
+      for (int nt = 0; nt < NT; ++nt) xsum[i][nt] = load_sum<NT>(x16, 4 * j + i, nt, lane);
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt) {
       const uint4 qw = *reinterpret_cast<const uint4*>(tp + rt * TB + j * 512 + lane * 16);
+      const uint32_t hw0 = *reinterpret_cast<const uint32_t*>(tp + rt * TB + 2048 + (2 * j) * 128 + lane * 4);
+      const uint32_t hw1 = *reinterpret_cast<const uint32_t*>(tp + rt * TB + 2048 + (2 * j + 1) * 128 + lane * 4);
       const uint32_t wv[4] = {qw.x, qw.y, qw.z, qw.w};
+      const uint32_t hws[2] = {hw0, hw1};
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int ksl = 4 * j + i;  // k-step within the superblock = sub-block index
-        const uint32_t hw = *reinterpret_cast<const uint32_t*>(tp + rt * TB + 2048 + (ksl >> 1) * 128 + lane * 4);
-        const int ip = ksl & 1;
+        const int ksl = 4 * j + i;
+        const uint32_t hw = hws[i >> 1];
+        const int ip = i & 1;
         uint32_t a[4];
 #pragma unroll
         for (int jj = 0; jj < 4; ++jj) {
           const uint32_t base = lop3_and_or(wv[i] >> (4 * jj), 0x000F000Fu, 0x64006400u);
           a[jj] = lop3_or_and(base, shift_signed(hw, 2 * (4 * ip + jj) - 4), 0x00300030u);
         }
-        const uint32_t sw0 = (ksl < 4 ? scl[rt][0].x : ksl < 8 ? scl[rt][0].y : ksl < 12 ? scl[rt][0].z : scl[rt][0].w);
-        const uint32_t sw1 = (ksl < 4 ? scl[rt][1].x : ksl < 8 ? scl[rt][1].y : ksl < 12 ? scl[rt][1].z : scl[rt][1].w);
-        const float s0 = dd[rt][0] * (float)(int8_t)((sw0 >> (8 * (ksl & 3))) & 0xff);
-        const float s1 = dd[rt][1] * (float)(int8_t)((sw1 >> (8 * (ksl & 3))) & 0xff);
+        const float2 sc = *reinterpret_cast<const float2*>(scr + ((rt * 16 + ksl) * 8 + g) * 2);
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           float d[4];
-          mma_sub<NT>(a, bq[i], nt, -1056.f * xs[i][nt].x, -1056.f * xs[i][nt].y, d);
+          const float c0 = -1056.f * xsum[i][nt].x, c1 = -1056.f * xsum[i][nt].y;
+          mma_f16(d, a[0], a[1], a[2], a[3], bq[i][nt][0], bq[i][nt][1], c0, c1, c0, c1);
           float* ac = acc[rt][nt];
-          ac[0] = fmaf(s0, d[0], ac[0]);
-          ac[1] = fmaf(s0, d[1], ac[1]);
-          ac[2] = fmaf(s1, d[2], ac[2]);
-          ac[3] = fmaf(s1, d[3], ac[3]);
+          ac[0] = fmaf(sc.x, d[0], ac[0]);
+          ac[1] = fmaf(sc.x, d[1], ac[1]);
+          ac[2] = fmaf(sc.y, d[2], ac[2]);
+          ac[3] = fmaf(sc.y, d[3], ac[3]);
         }
       }
     }
@@ -275,22 +240,22 @@ SPEC_DEV void tile_q6k(const uint8_t* tp, int ks0, const QmvParams& p, int lane,
 }
 
 template <int NT>
-SPEC_DEV void tile_q80(const uint8_t* tp, int ks0, const QmvParams& p, int lane, float (&acc)[2][NT][4]) {
+SPEC_DEV void tile_q80(const uint8_t* tp, const uint8_t* xs, const float* scr, int lane, float (&acc)[2][NT][4]) {
   constexpr int TB = 2176;
   const int g = lane >> 2;
+  const uint8_t* x32 = xs + 8 * NT * 256;
 #pragma unroll
   for (int j = 0; j < 4; ++j) {  // one Q8_0 block (32 columns) per j
     uint32_t bq[2][NT][2];
 #pragma unroll
-    for (int i = 0; i < 2; ++i) load_b<NT>(p, ks0 + 2 * j + i, lane, bq[i]);
-    float2 xs[NT];
+    for (int i = 0; i < 2; ++i) load_bfrag<NT>(xs, 2 * j + i, lane, bq[i]);
+    float2 xsum[NT];
 #pragma unroll
-    for (int nt = 0; nt < NT; ++nt) xs[nt] = load_xs<NT>(p.xsum32, ks0 / 2 + j, nt, lane);
+    for (int nt = 0; nt < NT; ++nt) xsum[nt] = load_sum<NT>(x32, j, nt, lane);
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt) {
       const uint4 qw = *reinterpret_cast<const uint4*>(tp + rt * TB + j * 512 + lane * 16);
-      const float s0 = h2f_bits(*reinterpret_cast<const uint16_t*>(tp + rt * TB + 2048 + (g * 4 + j) * 2));
-      const float s1 = h2f_bits(*reinterpret_cast<const uint16_t*>(tp + rt * TB + 2048 + ((g + 8) * 4 + j) * 2));
+      const float2 sc = *reinterpret_cast<const float2*>(scr + ((rt * 4 + j) * 8 + g) * 2);
       const uint32_t w[4] = {qw.x ^ 0x80808080u, qw.y ^ 0x80808080u, qw.z ^ 0x80808080u, qw.w ^ 0x80808080u};
       uint32_t a[2][4];
 #pragma unroll
@@ -303,25 +268,26 @@ SPEC_DEV void tile_q80(const uint8_t* tp, int ks0, const QmvParams& p, int lane,
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         float d[4];
-        mma_sub<NT>(a[0], bq[0], nt, -1152.f * xs[nt].x, -1152.f * xs[nt].y, d);
-        mma_acc<NT>(a[1], bq[1], nt, d);
+        const float c0 = -1152.f * xsum[nt].x, c1 = -1152.f * xsum[nt].y;
+        mma_f16(d, a[0][0], a[0][1], a[0][2], a[0][3], bq[0][nt][0], bq[0][nt][1], c0, c1, c0, c1);
+        mma_f16(d, a[1][0], a[1][1], a[1][2], a[1][3], bq[1][nt][0], bq[1][nt][1], d[0], d[1], d[2], d[3]);
         float* ac = acc[rt][nt];
-        ac[0] = fmaf(s0, d[0], ac[0]);
-        ac[1] = fmaf(s0, d[1], ac[1]);
-        ac[2] = fmaf(s1, d[2], ac[2]);
-        ac[3] = fmaf(s1, d[3], ac[3]);
+        ac[0] = fmaf(sc.x, d[0], ac[0]);
+        ac[1] = fmaf(sc.x, d[1], ac[1]);
+        ac[2] = fmaf(sc.y, d[2], ac[2]);
+        ac[3] = fmaf(sc.y, d[3], ac[3]);
       }
     }
   }
 }
 
 template <int NT>
-SPEC_DEV void tile_bf16(const uint8_t* tp, int ks0, const QmvParams& p, int lane, float (&acc)[2][NT][4]) {
+SPEC_DEV void tile_bf16(const uint8_t* tp, const uint8_t* xs, int lane, float (&acc)[2][NT][4]) {
   constexpr int TB = 4096;
 #pragma unroll
   for (int s = 0; s < 8; ++s) {
     uint32_t bq[NT][2];
-    load_b<NT>(p, ks0 + s, lane, bq);
+    load_bfrag<NT>(xs, s, lane, bq);
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt) {
       const uint4 a = *reinterpret_cast<const uint4*>(tp + rt * TB + s * 512 + lane * 16);
@@ -340,78 +306,17 @@ SPEC_DEV void tile_bf16(const uint8_t* tp, int ks0, const QmvParams& p, int lane
 }
 
 template <int F, int NT>
-SPEC_DEV void process_tile(const uint8_t* tp, int ks0, const QmvParams& p, int lane, float (&acc)[2][NT][4]) {
-  if constexpr (F == WF_Q4_K) tile_q4k<NT>(tp, ks0, p, lane, acc);
-  else if constexpr (F == WF_Q5_K) tile_q5k<NT>(tp, ks0, p, lane, acc);
-  else if constexpr (F == WF_Q6_K) tile_q6k<NT>(tp, ks0, p, lane, acc);
-  else if constexpr (F == WF_Q8_0) tile_q80<NT>(tp, ks0, p, lane, acc);
-  else tile_bf16<NT>(tp, ks0, p, lane, acc);
-}
-
-// ---------------------------------------------------------------------------
-// Per-warp streaming loop over this warp's pair tiles.
-// ---------------------------------------------------------------------------
-template <int F, int NT>
-SPEC_DEV void gemv_segment(const QmvParams& p, const WSeg& sg, int group_in_seg, int split, uint8_t* smem,
-                           uint64_t* bars, float (&acc)[2][NT][4]) {
-  constexpr int PAIR = fmt_pair_bytes(F);
-  constexpr int ST = fmt_stages(F);
-  constexpr int KSTEPS = fmt_kt(F) / 16;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int rowpair = group_in_seg * kGemvWarps + warp;
-  const int kt0 = split * sg.tiles_per_split;
-  const int cnt = sg.tiles_per_split;
-  const uint8_t* src = sg.w + ((size_t)rowpair * sg.k_tiles + kt0) * PAIR;
-  uint8_t* ring = smem + (size_t)warp * ST * PAIR;
-  uint64_t* bar = bars + warp * 4;
-
-  if (lane == 0) {
-#pragma unroll
-    for (int s = 0; s < ST; ++s) mbar_init(&bar[s], 1);
-    fence_mbar_init();
-  }
-  __syncwarp();
-  if (lane == 0) {
-    const int n0 = cnt < ST ? cnt : ST;
-    for (int i = 0; i < n0; ++i) {
-      mbar_arrive_expect_tx(&bar[i], PAIR);
-      tma_bulk_g2s(ring + i * PAIR, src + (size_t)i * PAIR, PAIR, &bar[i]);
-    }
-  }
-  // Everything above touches only weights; activations come from the
-  // previous kernel.
-  pdl_wait();
-
-#pragma unroll
-  for (int rt = 0; rt < 2; ++rt)
-#pragma unroll
-    for (int nt = 0; nt < NT; ++nt)
-#pragma unroll
-      for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
-
-  int done = 0;
-  bool ok = true;
-  for (int i = 0; i < cnt; ++i) {
-    const int slot = i % ST;
-    const uint32_t par = (uint32_t)((i / ST) & 1);
-    if (!mbar_wait_bounded(&bar[slot], par, p.err)) {
-      ok = false;
-      break;
-    }
-    process_tile<F, NT>(ring + slot * PAIR, (kt0 + i) * KSTEPS, p, lane, acc);
+SPEC_DEV void process_tile(const uint8_t* tp, const uint8_t* xs, float* scr, int lane, float (&acc)[2][NT][4]) {
+  if constexpr (F != WF_BF16) {
+    decode_scales<F>(tp, scr, lane);
     __syncwarp();
-    if (lane == 0 && i + ST < cnt) {
-      mbar_arrive_expect_tx(&bar[slot], PAIR);
-      tma_bulk_g2s(ring + slot * PAIR, src + (size_t)(i + ST) * PAIR, PAIR, &bar[slot]);
-    }
-    done = i + 1;
   }
-  if (!ok) {
-    // Drain whatever copies are still in flight (bounded) before the CTA
-    // may exit and release its shared memory.
-    const int issued = (cnt < done + ST) ? cnt : done + ST;
-    for (int i = done; i < issued; ++i) mbar_wait_bounded(&bar[i % ST], (uint32_t)((i / ST) & 1), nullptr);
-  }
+  if constexpr (F == WF_Q4_K) tile_q45k<NT>(tp, xs, scr, lane, false, acc);
+  else if constexpr (F == WF_Q5_K) tile_q45k<NT>(tp, xs, scr, lane, true, acc);
+  else if constexpr (F == WF_Q6_K) tile_q6k<NT>(tp, xs, scr, lane, acc);
+  else if constexpr (F == WF_Q8_0) tile_q80<NT>(tp, xs, scr, lane, acc);
+  else tile_bf16<NT>(tp, xs, lane, acc);
+  __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
@@ -455,6 +360,9 @@ SPEC_DEV void emit_operand_warp(uint32_t* frag, float* xs16, float* xs32, int nt
 // ---------------------------------------------------------------------------
 // Split-K reduction and fused epilogues.
 // ---------------------------------------------------------------------------
+// Barrier among the 128 consumer threads only (the producer warp runs ahead).
+SPEC_DEV void consumer_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
 template <int NT>
 SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, float (&acc)[2][NT][4], float* ys) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -463,10 +371,12 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
   __shared__ float s_rinv[kMaxRows];
   __shared__ float s_red[kGemvWarps][kMaxRows];
   const int M = p.M;
+  const int n_groups = p.seg[0].groups + p.seg[1].groups;
+  consumer_sync();  // all warps are done with their scale scratch (aliased by ys)
 
   if (p.S > 1) {
     const size_t per = (size_t)kGroupRows * 8 * NT;
-    float* mine = p.part + ((size_t)split * gridDim.x + group) * per;
+    float* mine = p.part + ((size_t)split * n_groups + group) * per;
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
@@ -474,14 +384,14 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
         __stcg(reinterpret_cast<float4*>(mine + ((size_t)((warp * 2 + rt) * NT + nt) * 32 + lane) * 4),
                make_float4(acc[rt][nt][0], acc[rt][nt][1], acc[rt][nt][2], acc[rt][nt][3]));
     __threadfence();
-    __syncthreads();
+    consumer_sync();
     if (tid == 0) {
       const int prev = atomicAdd(&p.counters[group], 1);
       s_last = (prev == p.S - 1);
       if (s_last) p.counters[group] = 0;
     }
-    __syncthreads();
-    if (!s_last) return;
+    consumer_sync();
+    if (!s_last) return;  // uniform across the CTA
     __threadfence();
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt)
@@ -489,21 +399,37 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
-    for (int s = 0; s < p.S; ++s) {
-      const float* ps = p.part + ((size_t)s * gridDim.x + group) * per;
+    // Sum the splits in index order; loads of 4 splits are issued together.
+    for (int s0 = 0; s0 < p.S; s0 += 4) {
+      float4 v[4][2][NT];
 #pragma unroll
-      for (int rt = 0; rt < 2; ++rt)
+      for (int q = 0; q < 4; ++q) {
+        if (s0 + q < p.S) {
+          const float* ps = p.part + ((size_t)(s0 + q) * n_groups + group) * per;
 #pragma unroll
-        for (int nt = 0; nt < NT; ++nt) {
-          const float4 v = __ldcg(reinterpret_cast<const float4*>(ps + ((size_t)((warp * 2 + rt) * NT + nt) * 32 + lane) * 4));
-          acc[rt][nt][0] += v.x;
-          acc[rt][nt][1] += v.y;
-          acc[rt][nt][2] += v.z;
-          acc[rt][nt][3] += v.w;
+          for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt)
+              v[q][rt][nt] =
+                  __ldcg(reinterpret_cast<const float4*>(ps + ((size_t)((warp * 2 + rt) * NT + nt) * 32 + lane) * 4));
         }
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        if (s0 + q < p.S) {
+#pragma unroll
+          for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              acc[rt][nt][0] += v[q][rt][nt].x;
+              acc[rt][nt][1] += v[q][rt][nt].y;
+              acc[rt][nt][2] += v[q][rt][nt].z;
+              acc[rt][nt][3] += v[q][rt][nt].w;
+            }
+        }
+      }
     }
   }
-  __syncthreads();  // every warp is done with its TMA ring: reuse as ys
 #pragma unroll
   for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
@@ -514,20 +440,30 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
         const int col = nt * 8 + 2 * t + (i & 1);
         if (col < M) ys[col * kGroupRows + row] = acc[rt][nt][i];
       }
-  if (tid < M) {
-    float r = 1.f;
-    if (p.ss_in) {
-      float ms = 0.f;
-      for (int q = 0; q < p.ss_groups; ++q) ms += p.ss_in[q * kSsStride + tid];
-      r = 1.f / sqrtf(ms * p.ss_inv_dim + p.eps);
+  if (p.ss_in) {
+    // Per-group sums of squares of the residual rows -> RMSNorm scale.  All
+    // 128 threads fetch the [ss_groups][M] table into shared memory at once;
+    // thread m then adds its column in group order.
+    float* sst = ys + M * kGroupRows;
+    const int n_ss = p.ss_groups * M;
+    for (int i = tid; i < n_ss; i += kGemvWarps * 32) {
+      const int q = i / M, m = i - q * M;
+      sst[i] = __ldcg(p.ss_in + q * kSsStride + m);
     }
-    s_rinv[tid] = r;
+    consumer_sync();
+    if (tid < M) {
+      float ms = 0.f;
+      for (int q = 0; q < p.ss_groups; ++q) ms += sst[q * M + tid];
+      s_rinv[tid] = 1.f / sqrtf(ms * p.ss_inv_dim + p.eps);
+    }
+  } else if (tid < M) {
+    s_rinv[tid] = 1.f;
   }
-  __syncthreads();
+  consumer_sync();
 
   const int n0 = group * kGroupRows;
   if (p.epi == EPI_STORE) {
-    for (int idx = tid; idx < M * kGroupRows; idx += blockDim.x) {
+    for (int idx = tid; idx < M * kGroupRows; idx += kGemvWarps * 32) {
       const int m = idx / kGroupRows, j = idx % kGroupRows, n = n0 + j;
       float v = ys[m * kGroupRows + j] * s_rinv[m];
       if (p.bias) v += p.bias[n];
@@ -536,7 +472,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
   } else if (p.epi == EPI_QKV) {
     const int hd = p.head_dim, nq = p.n_q_heads, nkv = p.n_kv_heads;
     const int G = nq / nkv, R = M * G, half = hd / 2;
-    for (int idx = tid; idx < M * kGroupRows; idx += blockDim.x) {
+    for (int idx = tid; idx < M * kGroupRows; idx += kGemvWarps * 32) {
       const int m = idx / kGroupRows, j = idx % kGroupRows, n = n0 + j;
       const int d = n % hd, head = n / hd;
       float x = ys[m * kGroupRows + j] * s_rinv[m];
@@ -575,17 +511,30 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
   } else if (p.epi == EPI_RESID) {
     const int H = p.n_rows;
     const int n = n0 + tid;  // 128 threads, one column each
-    for (int m = 0; m < M; ++m) {
-      const float hv = p.h[(size_t)m * H + n] + ys[m * kGroupRows + tid];
-      p.h[(size_t)m * H + n] = hv;
-      const float sq = warp_sum(hv * hv);
-      if (lane == 0) s_red[warp][m] = sq;
-      if (p.next_frag) {
-        const float v = p.next_norm ? hv * p.next_norm[n] : hv;
-        emit_operand_warp(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m, n, v, p.act_bf16, lane);
+    // Issue every row's residual load before using any of them.
+    for (int m0 = 0; m0 < M; m0 += 8) {
+      float hv[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q)
+        if (m0 + q < M) hv[q] = __ldcg(p.h + (size_t)(m0 + q) * H + n);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int m = m0 + q;
+        if (m < M) {
+          const float v = hv[q] + ys[m * kGroupRows + tid];
+          p.h[(size_t)m * H + n] = v;
+          ys[m * kGroupRows + tid] = v;
+        }
       }
     }
-    __syncthreads();
+    const float nw = p.next_norm ? __ldg(p.next_norm + n) : 1.f;
+    for (int m = 0; m < M; ++m) {
+      const float hv = ys[m * kGroupRows + tid];
+      const float sq = warp_sum(hv * hv);
+      if (lane == 0) s_red[warp][m] = sq;
+      if (p.next_frag) emit_operand_warp(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m, n, hv * nw, p.act_bf16, lane);
+    }
+    consumer_sync();
     if (tid < M) {
       float ss = 0.f;
 #pragma unroll
@@ -603,25 +552,174 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
       }
     }
   }
+  consumer_sync();  // ys aliases the scale scratch of the next unit
 }
 
+SPEC_DEV void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+constexpr int kProducerWarp = kGemvWarps;  // warp 4
+constexpr int kStageBudget = 106 * 1024;   // ring bytes per CTA (2 CTAs / SM)
+
 template <int FA, int FB, int NT>
-__global__ void __launch_bounds__(128) qmv_kernel(const __grid_constant__ QmvParams p) {
+struct KGeo {
+  static constexpr int PA = Geo<FA, NT>::PAIR, PB = Geo<FB, NT>::PAIR;
+  static constexpr int XA = Geo<FA, NT>::XB, XB = Geo<FB, NT>::XB;
+  static constexpr int PAIRMAX = PA > PB ? PA : PB;
+  static constexpr int XBMAX = XA > XB ? XA : XB;
+  static constexpr int STAGE = kGemvWarps * PAIRMAX + XBMAX;  // one k-tile of one unit
+  static constexpr int D0 = kStageBudget / STAGE;
+  static constexpr int D = D0 < 2 ? 2 : (D0 > 6 ? 6 : D0);     // ring depth
+  static constexpr int RING = D * STAGE;
+  static constexpr int SCR = kGemvWarps * kScratch;
+  static constexpr int YS = (8 * NT * kGroupRows + kMaxSsGroups * 8 * NT) * 4;  // ys + ss table
+  static constexpr int TAIL = SCR > YS ? SCR : YS;
+  static constexpr int SMEM = RING + TAIL;
+};
+
+// Persistent, warp-specialized GEMV.  CTA c takes work units c, c+G, c+2G, ...
+// (unit = 128-row group x K split; segment-0 units first).  Warp 4 is the
+// producer: one lane walks the CTA's tile sequence and, for every k-tile,
+// fills one ring stage with four pair tiles (one per consumer warp) and the
+// matching operand tile using TMA bulk copies, up to D stages ahead.  Warps
+// 0-3 consume: decode scales, run the tensor-core tile, release the stage.
+template <int FA, int FB, int NT>
+__global__ void __launch_bounds__(160) qmv_kernel(const __grid_constant__ QmvParams p) {
+  using KG = KGeo<FA, FB, NT>;
+  constexpr int D = KG::D;
   extern __shared__ __align__(128) uint8_t smem[];
-  __shared__ __align__(8) uint64_t bars[kGemvWarps * 4];
+  __shared__ __align__(8) uint64_t full[D];
+  __shared__ __align__(8) uint64_t empty[D];
   pdl_launch_dependents();
-  const int group = blockIdx.x, split = blockIdx.y;
-  float acc[2][NT][4];
-  if constexpr (FA == FB) {
-    const int seg = group < p.seg[0].groups ? 0 : 1;
-    gemv_segment<FA, NT>(p, p.seg[seg], seg ? group - p.seg[0].groups : group, split, smem, bars, acc);
-  } else {
-    if (group < p.seg[0].groups)
-      gemv_segment<FA, NT>(p, p.seg[0], group, split, smem, bars, acc);
-    else
-      gemv_segment<FB, NT>(p, p.seg[1], group - p.seg[0].groups, split, smem, bars, acc);
+  uint8_t* ring = smem;
+  float* tail = reinterpret_cast<float*>(smem + KG::RING);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  const int S = p.S;
+  const int unitsA = p.seg[0].groups * S, unitsB = p.seg[1].groups * S, U = unitsA + unitsB;
+  const int G = gridDim.x, c = blockIdx.x;
+  const int my_units = U > c ? (U - c + G - 1) / G : 0;
+  const int kA = unitsA > c ? (unitsA - c + G - 1) / G : 0;
+  const int cntA = p.seg[0].tiles_per_split, cntB = p.seg[1].tiles_per_split;
+  const int total = kA * cntA + (my_units - kA) * cntB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < D; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kGemvWarps);
+    }
   }
-  reduce_and_epilogue<NT>(p, group, split, acc, reinterpret_cast<float*>(smem));
+  fence_mbar_init();
+  __syncthreads();
+
+  if (warp == kProducerWarp) {
+    if (lane == 0) {
+      auto locate = [&](int pos, int& seg, int& u_in, int& local) {
+        if (pos < kA * cntA) {
+          const int k = pos / cntA;
+          local = pos - k * cntA;
+          u_in = c + k * G;
+          seg = 0;
+        } else {
+          const int q = pos - kA * cntA;
+          const int k = q / cntB;
+          local = q - k * cntB;
+          u_in = c + (kA + k) * G - unitsA;
+          seg = 1;
+        }
+      };
+      auto issue_w = [&](int pos) {
+        int seg, u_in, local;
+        locate(pos, seg, u_in, local);
+        const WSeg& sg = p.seg[seg];
+        const int grp = u_in / S, split = u_in - grp * S;
+        const int pair = seg ? KG::PB : KG::PA;
+        const int xb = seg ? KG::XB : KG::XA;
+        const int st = pos % D;
+        mbar_arrive_expect_tx(&full[st], kGemvWarps * pair + xb);
+        uint8_t* dst = ring + (size_t)st * KG::STAGE;
+        const size_t kt = (size_t)split * sg.tiles_per_split + local;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w)
+          tma_bulk_g2s(dst + w * KG::PAIRMAX, sg.w + ((size_t)(grp * kGemvWarps + w) * sg.k_tiles + kt) * pair, pair,
+                       &full[st]);
+      };
+      auto issue_x = [&](int pos) {
+        int seg, u_in, local;
+        locate(pos, seg, u_in, local);
+        const WSeg& sg = p.seg[seg];
+        const int grp = u_in / S, split = u_in - grp * S;
+        const int ksf = (seg ? fmt_kt(FB) : fmt_kt(FA)) / 16;
+        const int ks0 = (split * sg.tiles_per_split + local) * ksf;
+        const int xf = ksf * NT * 256;
+        const int x32 = seg ? Geo<FB, NT>::X32 : Geo<FA, NT>::X32;
+        const int x16 = seg ? Geo<FB, NT>::X16 : Geo<FA, NT>::X16;
+        const int st = pos % D;
+        uint8_t* dst = ring + (size_t)st * KG::STAGE + kGemvWarps * KG::PAIRMAX;
+        tma_bulk_g2s(dst, reinterpret_cast<const uint8_t*>(p.xfrag) + (size_t)ks0 * NT * 256, xf, &full[st]);
+        if (x32) tma_bulk_g2s(dst + xf, p.xsum32 + (size_t)(ks0 / 2) * 8 * NT, x32, &full[st]);
+        if (x16) tma_bulk_g2s(dst + xf + x32, p.xsum16 + (size_t)ks0 * 8 * NT, x16, &full[st]);
+      };
+      const int pre = total < D ? total : D;
+      for (int pos = 0; pos < pre; ++pos) issue_w(pos);
+      // Weights above do not depend on the previous kernel; operands do.
+      pdl_wait();
+      for (int pos = 0; pos < pre; ++pos) issue_x(pos);
+      bool ok = true;
+      for (int pos = pre; pos < total && ok; ++pos) {
+        ok = mbar_wait_bounded(&empty[pos % D], (uint32_t)(((pos / D) - 1) & 1), p.err);
+        if (ok) {
+          issue_w(pos);
+          issue_x(pos);
+        }
+      }
+      // Every issued copy must land before this CTA can retire.
+      for (int pos = total - pre; pos < total; ++pos)
+        if (pos >= 0) mbar_wait_bounded(&full[pos % D], (uint32_t)((pos / D) & 1), nullptr);
+    }
+    return;
+  }
+
+  // ---- consumers ----
+  pdl_wait();
+  float* scr = tail + warp * (kScratch / 4);
+  float acc[2][NT][4];
+  bool ok = true;
+  int pos = 0;
+  for (int k = 0; k < my_units; ++k) {
+    const int unit = c + k * G;
+    const int seg = unit < unitsA ? 0 : 1;
+    const int u_in = seg ? unit - unitsA : unit;
+    const int grp = u_in / S, split = u_in - grp * S;
+    const int cnt = seg ? cntB : cntA;
+#pragma unroll
+    for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
+    for (int local = 0; local < cnt; ++local, ++pos) {
+      const int st = pos % D;
+      if (ok) ok = mbar_wait_bounded(&full[st], (uint32_t)((pos / D) & 1), p.err);
+      if (ok) {
+        const uint8_t* stage = ring + (size_t)st * KG::STAGE;
+        const uint8_t* tp = stage + warp * KG::PAIRMAX;
+        const uint8_t* xs = stage + kGemvWarps * KG::PAIRMAX;
+        if constexpr (FA == FB) {
+          process_tile<FA, NT>(tp, xs, scr, lane, acc);
+        } else {
+          if (seg == 0) process_tile<FA, NT>(tp, xs, scr, lane, acc);
+          else process_tile<FB, NT>(tp, xs, scr, lane, acc);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+    }
+    const int ggrp = (seg ? p.seg[0].groups : 0) + grp;
+    reduce_and_epilogue<NT>(p, ggrp, split, acc, tail);
+    consumer_sync();
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -784,19 +882,34 @@ __global__ void repack_kernel(const uint8_t* raw, int fmt, int N, int K, uint8_t
 
 template <int FA, int FB, int NT>
 cudaError_t launch_inst(const QmvParams& p, cudaStream_t stream, bool pdl) {
-  constexpr int ringA = kGemvWarps * fmt_stages(FA) * fmt_pair_bytes(FA);
-  constexpr int ringB = kGemvWarps * fmt_stages(FB) * fmt_pair_bytes(FB);
-  constexpr int ysb = kMaxRows * kGroupRows * 4;
-  constexpr int smem = ringA > ringB ? (ringA > ysb ? ringA : ysb) : (ringB > ysb ? ringB : ysb);
-  static bool attr_set = false;
-  if (!attr_set) {
+  constexpr int smem = KGeo<FA, FB, NT>::SMEM;
+  static int blocks_per_sm[16] = {0};
+  static int num_sms[16] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 16) return cudaErrorInvalidDevice;
+  if (!blocks_per_sm[dev]) {
     cudaError_t e = cudaFuncSetAttribute(qmv_kernel<FA, FB, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    attr_set = true;
+    int bps = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, qmv_kernel<FA, FB, NT>, (kGemvWarps + 1) * 32, smem);
+    if (e != cudaSuccess) return e;
+    int sms = 0;
+    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    num_sms[dev] = sms;
+    blocks_per_sm[dev] = bps > 0 ? bps : 1;
   }
+  const int units = (p.seg[0].groups + p.seg[1].groups) * p.S;
+  int grid = blocks_per_sm[dev] * num_sms[dev];
+  if (const char* env = getenv("SPEC_B200_GEMV_CTAS_PER_SM")) {
+    const int v = atoi(env);
+    if (v > 0 && v < blocks_per_sm[dev]) grid = v * num_sms[dev];
+  }
+  if (grid > units) grid = units;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(p.seg[0].groups + p.seg[1].groups, p.S, 1);
-  cfg.blockDim = dim3(kGemvWarps * 32, 1, 1);
+  cfg.gridDim = dim3(grid, 1, 1);
+  cfg.blockDim = dim3((kGemvWarps + 1) * 32, 1, 1);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = stream;
   cudaLaunchAttribute attr[1];
@@ -809,14 +922,38 @@ cudaError_t launch_inst(const QmvParams& p, cudaStream_t stream, bool pdl) {
 
 template <int FA, int FB>
 cudaError_t launch_nt(const QmvParams& p, cudaStream_t s, bool pdl) {
-  const int nt = (p.M + 7) / 8;
-  if (nt <= 1) return launch_inst<FA, FB, 1>(p, s, pdl);
-  if (nt <= 2) return launch_inst<FA, FB, 2>(p, s, pdl);
-  if (nt <= 4) return launch_inst<FA, FB, 4>(p, s, pdl);
+  const int nt = nt_for_rows(p.M);
+  if (nt == 1) return launch_inst<FA, FB, 1>(p, s, pdl);
+  if (nt == 2) return launch_inst<FA, FB, 2>(p, s, pdl);
+  if (nt == 4) return launch_inst<FA, FB, 4>(p, s, pdl);
   return launch_inst<FA, FB, 8>(p, s, pdl);
 }
 
 }  // namespace
+
+namespace {
+template <int FA, int FB>
+int ctas_per_sm_inst() {
+  int bps = 0;
+  constexpr int smem = KGeo<FA, FB, 1>::SMEM;
+  if (cudaFuncSetAttribute(qmv_kernel<FA, FB, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
+    return 4;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, qmv_kernel<FA, FB, 1>, (kGemvWarps + 1) * 32, smem) !=
+      cudaSuccess)
+    return 4;
+  return bps > 0 ? bps : 1;
+}
+}  // namespace
+
+int qmv_ctas_per_sm(int fa, int fb) {
+  if (fa == WF_Q4_K && fb == WF_Q4_K) return ctas_per_sm_inst<WF_Q4_K, WF_Q4_K>();
+  if (fa == WF_Q4_K && fb == WF_Q6_K) return ctas_per_sm_inst<WF_Q4_K, WF_Q6_K>();
+  if (fa == WF_Q6_K && fb == WF_Q6_K) return ctas_per_sm_inst<WF_Q6_K, WF_Q6_K>();
+  if (fa == WF_Q5_K && fb == WF_Q5_K) return ctas_per_sm_inst<WF_Q5_K, WF_Q5_K>();
+  if (fa == WF_Q8_0 && fb == WF_Q8_0) return ctas_per_sm_inst<WF_Q8_0, WF_Q8_0>();
+  if (fa == WF_BF16 && fb == WF_BF16) return ctas_per_sm_inst<WF_BF16, WF_BF16>();
+  return 4;
+}
 
 cudaError_t launch_qmv(const QmvParams& p, cudaStream_t s, bool pdl) {
   if (p.M < 1 || p.M > kMaxRows) return cudaErrorInvalidValue;
