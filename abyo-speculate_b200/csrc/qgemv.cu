@@ -91,16 +91,25 @@ SPEC_DEV void decode_scales(const uint8_t* tp, float* scr, int lane) {
   constexpr int TB = fmt_tile_bytes(F);
   const int rt = lane >> 4, ri = lane & 15;
   if constexpr (F == WF_Q4_K || F == WF_Q5_K) {
+    // scr layout (floats): [0,256) s[rt][sb][g][row g | row g+8];
+    // [256,384) m as f16 A-fragment words [rt][g][t][row g | row g+8];
+    // [384,416) dmin[rt][row].
     constexpr int MO = (F == WF_Q4_K) ? 2048 : 2560;
     const uint4 m = *reinterpret_cast<const uint4*>(tp + rt * TB + MO + ri * 16);
     const float d = h2f_bits(m.x), dm = h2f_bits(m.x >> 16);
+    int mv[8];
 #pragma unroll
     for (int sb = 0; sb < 8; ++sb) {
-      int sc, mn;
-      k4_scale_min(m, sb, sc, mn);
-      *reinterpret_cast<float2*>(scr + ((rt * 8 + sb) * 8 + (ri & 7)) * 4 + (ri >> 3) * 2) =
-          make_float2(d * (float)sc, dm * (float)mn);
+      int sc;
+      k4_scale_min(m, sb, sc, mv[sb]);
+      scr[((rt * 8 + sb) * 8 + (ri & 7)) * 2 + (ri >> 3)] = d * (float)sc;
     }
+    uint32_t* mw = reinterpret_cast<uint32_t*>(scr + 256);
+#pragma unroll
+    for (int t = 0; t < 4; ++t)
+      mw[((rt * 8 + (ri & 7)) * 4 + t) * 2 + (ri >> 3)] =
+          pack_half2(__int2half_rn(mv[2 * t]), __int2half_rn(mv[2 * t + 1]));
+    scr[384 + rt * 16 + ri] = dm * 64.f;
   } else if constexpr (F == WF_Q6_K) {
     const uint4 sv = *reinterpret_cast<const uint4*>(tp + rt * TB + 3072 + ri * 16);
     const float d = h2f_bits(*reinterpret_cast<const uint16_t*>(tp + rt * TB + 3328 + ri * 2));
@@ -136,12 +145,27 @@ SPEC_DEV float2 load_sum(const uint8_t* base, int blk, int nt, int lane) {
   return *reinterpret_cast<const float2*>(base + ((blk * NT + nt) * 8 + 2 * (lane & 3)) * 4);
 }
 
+// Q4_K / Q5_K.  Per sub-block b the tensor core returns D_b = sum(q * x)
+// (its accumulator is seeded with -1024 * xsum_b to cancel the code offset);
+// acc += s_b * D_b.  The min term sum_b m_b * xsum_b is one more exact mma per
+// 16-row tile and superblock: A = the 6-bit mins (exact in f16), B = the
+// sub-block sums / 64 split into f16 hi + lo parts; acc -= 64 * dmin * D_min.
 template <int NT>
 SPEC_DEV void tile_q45k(const uint8_t* tp, const uint8_t* xs, const float* scr, int lane, bool q5,
                         float (&acc)[2][NT][4]) {
   const int TB = q5 ? 2816 : 2304;
-  const int g = lane >> 2;
+  const int g = lane >> 2, t = lane & 3;
   const uint8_t* x32 = xs + 16 * NT * 256;
+  // B operand of the min-term mma: rows k = sub-blocks 2t, 2t+1; column g.
+  uint32_t bh[NT], bl[NT];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) {
+    const float v0 = reinterpret_cast<const float*>(x32)[(2 * t) * 8 * NT + nt * 8 + g] * (1.f / 64.f);
+    const float v1 = reinterpret_cast<const float*>(x32)[(2 * t + 1) * 8 * NT + nt * 8 + g] * (1.f / 64.f);
+    const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
+    bh[nt] = pack_half2(h0, h1);
+    bl[nt] = pack_half2(__float2half_rn(v0 - __half2float(h0)), __float2half_rn(v1 - __half2float(h1)));
+  }
 #pragma unroll
   for (int j = 0; j < 4; ++j) {  // 4 k-steps = 2 sub-blocks of 32
     uint32_t bq[4][NT][2];
@@ -160,7 +184,7 @@ SPEC_DEV void tile_q45k(const uint8_t* tp, const uint8_t* xs, const float* scr, 
       if (q5) hw = *reinterpret_cast<const uint32_t*>(tp + rt * TB + 2048 + j * 128 + lane * 4);
 #pragma unroll
       for (int sb = 0; sb < 2; ++sb) {
-        const float4 sc = *reinterpret_cast<const float4*>(scr + ((rt * 8 + 2 * j + sb) * 8 + g) * 4);
+        const float2 sc = *reinterpret_cast<const float2*>(scr + ((rt * 8 + 2 * j + sb) * 8 + g) * 2);
         uint32_t a[2][4];
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
@@ -179,12 +203,29 @@ SPEC_DEV void tile_q45k(const uint8_t* tp, const uint8_t* xs, const float* scr, 
           mma_f16(d, a[1][0], a[1][1], a[1][2], a[1][3], bq[2 * sb + 1][nt][0], bq[2 * sb + 1][nt][1], d[0], d[1],
                   d[2], d[3]);
           float* ac = acc[rt][nt];
-          ac[0] = fmaf(sc.x, d[0], fmaf(-sc.y, xsum[sb][nt].x, ac[0]));
-          ac[1] = fmaf(sc.x, d[1], fmaf(-sc.y, xsum[sb][nt].y, ac[1]));
-          ac[2] = fmaf(sc.z, d[2], fmaf(-sc.w, xsum[sb][nt].x, ac[2]));
-          ac[3] = fmaf(sc.z, d[3], fmaf(-sc.w, xsum[sb][nt].y, ac[3]));
+          ac[0] = fmaf(sc.x, d[0], ac[0]);
+          ac[1] = fmaf(sc.x, d[1], ac[1]);
+          ac[2] = fmaf(sc.y, d[2], ac[2]);
+          ac[3] = fmaf(sc.y, d[3], ac[3]);
         }
       }
+    }
+  }
+  const uint32_t* mw = reinterpret_cast<const uint32_t*>(scr + 256);
+#pragma unroll
+  for (int rt = 0; rt < 2; ++rt) {
+    const uint2 am = *reinterpret_cast<const uint2*>(mw + ((rt * 8 + g) * 4 + t) * 2);
+    const float dm0 = scr[384 + rt * 16 + g], dm1 = scr[384 + rt * 16 + g + 8];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      float d[4];
+      mma_f16(d, am.x, am.y, 0u, 0u, bh[nt], 0u, 0.f, 0.f, 0.f, 0.f);
+      mma_f16(d, am.x, am.y, 0u, 0u, bl[nt], 0u, d[0], d[1], d[2], d[3]);
+      float* ac = acc[rt][nt];
+      ac[0] = fmaf(-dm0, d[0], ac[0]);
+      ac[1] = fmaf(-dm0, d[1], ac[1]);
+      ac[2] = fmaf(-dm1, d[2], ac[2]);
+      ac[3] = fmaf(-dm1, d[3], ac[3]);
     }
   }
 }
@@ -399,11 +440,12 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
-    // Sum the splits in index order; loads of 4 splits are issued together.
-    for (int s0 = 0; s0 < p.S; s0 += 4) {
-      float4 v[4][2][NT];
+    // Sum the splits in index order; the loads of SB splits are issued together.
+    constexpr int SB = NT == 1 ? 4 : (NT == 2 ? 2 : 1);
+    for (int s0 = 0; s0 < p.S; s0 += SB) {
+      float4 v[SB][2][NT];
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < SB; ++q) {
         if (s0 + q < p.S) {
           const float* ps = p.part + ((size_t)(s0 + q) * n_groups + group) * per;
 #pragma unroll
@@ -415,7 +457,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
         }
       }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < SB; ++q) {
         if (s0 + q < p.S) {
 #pragma unroll
           for (int rt = 0; rt < 2; ++rt)
@@ -560,7 +602,7 @@ SPEC_DEV void mbar_arrive(uint64_t* bar) {
 }
 
 constexpr int kProducerWarp = kGemvWarps;  // warp 4
-constexpr int kStageBudget = 106 * 1024;   // ring bytes per CTA (2 CTAs / SM)
+constexpr int kStageBudget = 48 * 1024;    // ring bytes per CTA (4 CTAs / SM at M <= 8)
 
 template <int FA, int FB, int NT>
 struct KGeo {
@@ -585,7 +627,7 @@ struct KGeo {
 // matching operand tile using TMA bulk copies, up to D stages ahead.  Warps
 // 0-3 consume: decode scales, run the tensor-core tile, release the stage.
 template <int FA, int FB, int NT>
-__global__ void __launch_bounds__(160) qmv_kernel(const __grid_constant__ QmvParams p) {
+__global__ void __launch_bounds__(160, NT == 1 ? 4 : (NT == 2 ? 3 : (NT == 4 ? 2 : 1))) qmv_kernel(const __grid_constant__ QmvParams p) {
   using KG = KGeo<FA, FB, NT>;
   constexpr int D = KG::D;
   extern __shared__ __align__(128) uint8_t smem[];
