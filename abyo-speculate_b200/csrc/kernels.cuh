@@ -112,12 +112,41 @@ struct QmvParams {
   int act_bf16 = 0;                 // operand dtype: 0 f16, 1 bf16
 };
 
-// Launch one fused GEMV (persistent grid sized to occupancy); the
-// instantiation is picked by nt_for_rows(p.M).
-cudaError_t launch_qmv(const QmvParams& p, cudaStream_t stream, bool pdl);
-// Resident CTAs per SM of the GEMV for a (segment 0, segment 1) format pair
-// (on the current device).
-int qmv_ctas_per_sm(int fa, int fb);
+// ---- persistent multi-op GEMV kernel -------------------------------------
+// One launch runs a schedule of GEMV ops.  Every CTA walks the same op list
+// and takes units c, c+G, c+2G, ... of each op.  A producer warp streams the
+// weight tiles of all its units, across op boundaries, through a TMA ring;
+// the activation tile of a stage is only fetched once the op it depends on
+// has completed (device-side completion counter), so weight streaming never
+// waits on the previous op.
+struct alignas(16) FwdOp {
+  QmvParams q;
+  int dep = -1;  // op (index in this launch) whose completion gates this op; -1: the previous kernel
+};
+
+// Bit set of weight formats one kernel instantiation handles.
+enum FmtSet : int { FS_Q4K = 1, FS_Q5K = 2, FS_Q6K = 4, FS_Q80 = 8, FS_BF16 = 16 };
+__host__ __device__ constexpr int fmt_bit(int f) {
+  return f == WF_Q4_K ? FS_Q4K : f == WF_Q5_K ? FS_Q5K : f == WF_Q6_K ? FS_Q6K : f == WF_Q8_0 ? FS_Q80 : f == WF_BF16 ? FS_BF16 : 0;
+}
+
+constexpr int kMaxLaunchOps = 8;  // ops per forward-kernel launch
+
+struct FwdParams {
+  const FwdOp* ops = nullptr;  // device array (16-byte aligned)
+  int n_ops = 0;
+  int* done = nullptr;         // [n_ops] completion counters, zero at launch
+  unsigned* err = nullptr;
+  int l2_ahead = 0;            // stages of this CTA's weights prefetched into L2 ahead of the ring
+};
+
+// The instantiation is picked by (format set, nt_for_rows(M)); all ops of
+// one launch must share M and have formats inside `fmt_set`.
+cudaError_t launch_fwd(const FwdParams& p, int fmt_set, int M, cudaStream_t stream, bool pdl);
+// Resident CTAs per SM of the instantiation for `fmt_set` at M <= 8.
+int fwd_ctas_per_sm(int fmt_set);
+// The format sets instantiated (a model's formats must fit in one).
+int fwd_fmt_set_for(int fmt_bits);
 
 // Repack raw GGUF blocks (device, row-major [N][K/be][bb]) into pair tiles.
 cudaError_t launch_repack(const uint8_t* raw, int fmt, int N, int K, uint8_t* tiles, cudaStream_t s);

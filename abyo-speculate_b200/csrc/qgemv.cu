@@ -51,8 +51,6 @@ struct Geo {
   static constexpr int XB = XFRAG + X32 + X16;              // operand bytes per tile
 };
 
-constexpr int kWStages = 2;      // weight ring stages per warp
-constexpr int kXStages = 2;      // operand ring stages per CTA
 constexpr int kScratch = 2048;   // per-warp decoded-scale scratch (bytes)
 
 SPEC_DEV float h2f_bits(uint32_t bits16) { return __half2float(__ushort_as_half((unsigned short)(bits16 & 0xffffu))); }
@@ -404,8 +402,11 @@ SPEC_DEV void emit_operand_warp(uint32_t* frag, float* xs16, float* xs32, int nt
 // Barrier among the 128 consumer threads only (the producer warp runs ahead).
 SPEC_DEV void consumer_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Sums the K splits of a 128-row group (the CTA that delivers the last split
+// does it) and runs the fused epilogue; that CTA then bumps `done`.
 template <int NT>
-SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, float (&acc)[2][NT][4], float* ys) {
+SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, float (&acc)[2][NT][4], float* ys,
+                                  int* done) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   __shared__ int s_last;
@@ -595,6 +596,10 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
     }
   }
   consumer_sync();  // ys aliases the scale scratch of the next unit
+  if (done && tid == 0) {
+    __threadfence();
+    atomicAdd(done, 1);
+  }
 }
 
 SPEC_DEV void mbar_arrive(uint64_t* bar) {
@@ -602,49 +607,152 @@ SPEC_DEV void mbar_arrive(uint64_t* bar) {
 }
 
 constexpr int kProducerWarp = kGemvWarps;  // warp 4
-constexpr int kStageBudget = 48 * 1024;    // ring bytes per CTA (4 CTAs / SM at M <= 8)
+constexpr int kStageBudget = 64 * 1024;    // ring bytes per CTA (3 CTAs / SM at M <= 8)
 
-template <int FA, int FB, int NT>
-struct KGeo {
-  static constexpr int PA = Geo<FA, NT>::PAIR, PB = Geo<FB, NT>::PAIR;
-  static constexpr int XA = Geo<FA, NT>::XB, XB = Geo<FB, NT>::XB;
-  static constexpr int PAIRMAX = PA > PB ? PA : PB;
-  static constexpr int XBMAX = XA > XB ? XA : XB;
-  static constexpr int STAGE = kGemvWarps * PAIRMAX + XBMAX;  // one k-tile of one unit
+template <int SET, int F, int NT>
+struct GeoIf {
+  static constexpr bool on = (SET & fmt_bit(F)) != 0;
+  static constexpr int PAIR = on ? Geo<F, NT>::PAIR : 0;
+  static constexpr int XB = on ? Geo<F, NT>::XB : 0;
+};
+constexpr int cmax(int a, int b) { return a > b ? a : b; }
+
+template <int SET, int NT>
+struct FGeo {
+  static constexpr int PAIRMAX =
+      cmax(cmax(cmax(GeoIf<SET, WF_Q4_K, NT>::PAIR, GeoIf<SET, WF_Q5_K, NT>::PAIR),
+                cmax(GeoIf<SET, WF_Q6_K, NT>::PAIR, GeoIf<SET, WF_Q8_0, NT>::PAIR)),
+           GeoIf<SET, WF_BF16, NT>::PAIR);
+  static constexpr int XBMAX = cmax(cmax(cmax(GeoIf<SET, WF_Q4_K, NT>::XB, GeoIf<SET, WF_Q5_K, NT>::XB),
+                                         cmax(GeoIf<SET, WF_Q6_K, NT>::XB, GeoIf<SET, WF_Q8_0, NT>::XB)),
+                                    GeoIf<SET, WF_BF16, NT>::XB);
+  static constexpr int STAGE = kGemvWarps * PAIRMAX + XBMAX;
   static constexpr int D0 = kStageBudget / STAGE;
-  static constexpr int D = D0 < 2 ? 2 : (D0 > 6 ? 6 : D0);     // ring depth
+  static constexpr int D = D0 < 2 ? 2 : (D0 > 6 ? 6 : D0);
   static constexpr int RING = D * STAGE;
   static constexpr int SCR = kGemvWarps * kScratch;
-  static constexpr int YS = (8 * NT * kGroupRows + kMaxSsGroups * 8 * NT) * 4;  // ys + ss table
+  static constexpr int YS = (8 * NT * kGroupRows + kMaxSsGroups * 8 * NT) * 4;
   static constexpr int TAIL = SCR > YS ? SCR : YS;
   static constexpr int SMEM = RING + TAIL;
 };
 
-// Persistent, warp-specialized GEMV.  CTA c takes work units c, c+G, c+2G, ...
-// (unit = 128-row group x K split; segment-0 units first).  Warp 4 is the
-// producer: one lane walks the CTA's tile sequence and, for every k-tile,
-// fills one ring stage with four pair tiles (one per consumer warp) and the
-// matching operand tile using TMA bulk copies, up to D stages ahead.  Warps
-// 0-3 consume: decode scales, run the tensor-core tile, release the stage.
-template <int FA, int FB, int NT>
-__global__ void __launch_bounds__(160, NT == 1 ? 4 : (NT == 2 ? 3 : (NT == 4 ? 2 : 1))) qmv_kernel(const __grid_constant__ QmvParams p) {
-  using KG = KGeo<FA, FB, NT>;
-  constexpr int D = KG::D;
+// Walks (op, unit, tile) for CTA c in schedule order.
+struct SeqIt {
+  int op = 0, k = 0, local = 0, cnt = 0, unit = 0;
+  bool valid = false;
+};
+
+SPEC_DEV int op_units(const QmvParams& q) { return (q.seg[0].groups + q.seg[1].groups) * q.S; }
+
+SPEC_DEV void seq_settle(const FwdParams& P, int c, int G, SeqIt& it) {
+  // Move to the first (op, k) with a unit for this CTA, starting at it.op / it.k.
+  while (it.op < P.n_ops) {
+    const QmvParams& q = P.ops[it.op].q;
+    const int u = c + it.k * G;
+    if (u < op_units(q)) {
+      const int unitsA = q.seg[0].groups * q.S;
+      it.unit = u;
+      it.cnt = u < unitsA ? q.seg[0].tiles_per_split : q.seg[1].tiles_per_split;
+      it.valid = true;
+      return;
+    }
+    ++it.op;
+    it.k = 0;
+    it.local = 0;
+  }
+  it.valid = false;
+}
+SPEC_DEV void seq_begin(const FwdParams& P, int c, int G, SeqIt& it) {
+  it = SeqIt{};
+  seq_settle(P, c, G, it);
+}
+SPEC_DEV void seq_next(const FwdParams& P, int c, int G, SeqIt& it) {
+  if (++it.local < it.cnt) return;
+  it.local = 0;
+  ++it.k;
+  seq_settle(P, c, G, it);
+}
+
+SPEC_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+SPEC_DEV int ld_acquire(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+SPEC_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+SPEC_DEV bool op_inputs_ready(const FwdParams& P, int op) {
+  const int dep = P.ops[op].dep;
+  if (dep < 0) return true;
+  const QmvParams& d = P.ops[dep].q;
+  return ld_acquire(P.done + dep) >= d.seg[0].groups + d.seg[1].groups;
+}
+
+template <int SET, int NT>
+SPEC_DEV void process_any(int fmt, const uint8_t* tp, const uint8_t* xs, float* scr, int lane,
+                          float (&acc)[2][NT][4]) {
+  if constexpr ((SET & FS_Q4K) != 0) {
+    if (fmt == WF_Q4_K) return process_tile<WF_Q4_K, NT>(tp, xs, scr, lane, acc);
+  }
+  if constexpr ((SET & FS_Q6K) != 0) {
+    if (fmt == WF_Q6_K) return process_tile<WF_Q6_K, NT>(tp, xs, scr, lane, acc);
+  }
+  if constexpr ((SET & FS_Q5K) != 0) {
+    if (fmt == WF_Q5_K) return process_tile<WF_Q5_K, NT>(tp, xs, scr, lane, acc);
+  }
+  if constexpr ((SET & FS_Q80) != 0) {
+    if (fmt == WF_Q8_0) return process_tile<WF_Q8_0, NT>(tp, xs, scr, lane, acc);
+  }
+  if constexpr ((SET & FS_BF16) != 0) {
+    if (fmt == WF_BF16) return process_tile<WF_BF16, NT>(tp, xs, scr, lane, acc);
+  }
+}
+
+SPEC_DEV int x32_bytes(int fmt, int NT) { return fmt == WF_BF16 ? 0 : (fmt_kt(fmt) / 32) * 8 * NT * 4; }
+SPEC_DEV int x16_bytes(int fmt, int NT) { return fmt == WF_BF16 ? 0 : (fmt_kt(fmt) / 16) * 8 * NT * 4; }
+
+// Persistent, warp-specialized multi-op GEMV (see FwdOp).  Warp 4 lane 0 is
+// the producer: it keeps a weight cursor up to D stages ahead of the
+// consumers (never blocked by op dependencies) and an operand cursor that
+// fills each stage's activation tile once that stage's op has its inputs.
+// Warps 0-3 consume stages, run the per-unit split-K epilogue and publish
+// op completion.
+template <int SET, int NT>
+__global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2 : 1)))
+    fwd_kernel(const __grid_constant__ FwdParams Pg) {
+  using FG = FGeo<SET, NT>;
+  constexpr int D = FG::D;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[D];
   __shared__ __align__(8) uint64_t empty[D];
+  __shared__ __align__(16) FwdOp s_ops[kMaxLaunchOps];
   pdl_launch_dependents();
+  // Op descriptors live in shared memory for the whole launch (the producer
+  // walks them per tile).  They were uploaded long before this launch.
+  {
+    const int n = Pg.n_ops < kMaxLaunchOps ? Pg.n_ops : kMaxLaunchOps;
+    const int4* src = reinterpret_cast<const int4*>(Pg.ops);
+    int4* dst = reinterpret_cast<int4*>(s_ops);
+    const int words = n * (int)(sizeof(FwdOp) / sizeof(int4));
+    for (int i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
+  }
+  FwdParams P = Pg;
+  P.ops = s_ops;
   uint8_t* ring = smem;
-  float* tail = reinterpret_cast<float*>(smem + KG::RING);
+  float* tail = reinterpret_cast<float*>(smem + FG::RING);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  const int S = p.S;
-  const int unitsA = p.seg[0].groups * S, unitsB = p.seg[1].groups * S, U = unitsA + unitsB;
   const int G = gridDim.x, c = blockIdx.x;
-  const int my_units = U > c ? (U - c + G - 1) / G : 0;
-  const int kA = unitsA > c ? (unitsA - c + G - 1) / G : 0;
-  const int cntA = p.seg[0].tiles_per_split, cntB = p.seg[1].tiles_per_split;
-  const int total = kA * cntA + (my_units - kA) * cntB;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < D; ++s) {
@@ -657,68 +765,118 @@ __global__ void __launch_bounds__(160, NT == 1 ? 4 : (NT == 2 ? 3 : (NT == 4 ? 2
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
-      auto locate = [&](int pos, int& seg, int& u_in, int& local) {
-        if (pos < kA * cntA) {
-          const int k = pos / cntA;
-          local = pos - k * cntA;
-          u_in = c + k * G;
-          seg = 0;
-        } else {
-          const int q = pos - kA * cntA;
-          const int k = q / cntB;
-          local = q - k * cntB;
-          u_in = c + (kA + k) * G - unitsA;
-          seg = 1;
-        }
+      auto wbytes = [&](const SeqIt& it, int& pair, int& xb, int& fmt) {
+        const QmvParams& q = P.ops[it.op].q;
+        const int seg = it.unit < q.seg[0].groups * q.S ? 0 : 1;
+        fmt = q.seg[seg].fmt;
+        pair = fmt_pair_bytes(fmt);
+        xb = (fmt_kt(fmt) / 16) * NT * 256 + x32_bytes(fmt, NT) + x16_bytes(fmt, NT);
+        return seg;
       };
-      auto issue_w = [&](int pos) {
-        int seg, u_in, local;
-        locate(pos, seg, u_in, local);
-        const WSeg& sg = p.seg[seg];
-        const int grp = u_in / S, split = u_in - grp * S;
-        const int pair = seg ? KG::PB : KG::PA;
-        const int xb = seg ? KG::XB : KG::XA;
+      auto issue_w = [&](const SeqIt& it, int pos) {
+        int pair, xb, fmt;
+        const int seg = wbytes(it, pair, xb, fmt);
+        const QmvParams& q = P.ops[it.op].q;
+        const WSeg& sg = q.seg[seg];
+        const int u_in = seg ? it.unit - q.seg[0].groups * q.S : it.unit;
+        const int grp = u_in / q.S, split = u_in - grp * q.S;
         const int st = pos % D;
         mbar_arrive_expect_tx(&full[st], kGemvWarps * pair + xb);
-        uint8_t* dst = ring + (size_t)st * KG::STAGE;
-        const size_t kt = (size_t)split * sg.tiles_per_split + local;
+        uint8_t* dst = ring + (size_t)st * FG::STAGE;
+        const size_t kt = (size_t)split * sg.tiles_per_split + it.local;
 #pragma unroll
         for (int w = 0; w < kGemvWarps; ++w)
-          tma_bulk_g2s(dst + w * KG::PAIRMAX, sg.w + ((size_t)(grp * kGemvWarps + w) * sg.k_tiles + kt) * pair, pair,
+          tma_bulk_g2s(dst + w * FG::PAIRMAX, sg.w + ((size_t)(grp * kGemvWarps + w) * sg.k_tiles + kt) * pair, pair,
                        &full[st]);
       };
-      auto issue_x = [&](int pos) {
-        int seg, u_in, local;
-        locate(pos, seg, u_in, local);
-        const WSeg& sg = p.seg[seg];
-        const int grp = u_in / S, split = u_in - grp * S;
-        const int ksf = (seg ? fmt_kt(FB) : fmt_kt(FA)) / 16;
-        const int ks0 = (split * sg.tiles_per_split + local) * ksf;
-        const int xf = ksf * NT * 256;
-        const int x32 = seg ? Geo<FB, NT>::X32 : Geo<FA, NT>::X32;
-        const int x16 = seg ? Geo<FB, NT>::X16 : Geo<FA, NT>::X16;
+      auto issue_x = [&](const SeqIt& it, int pos) {
+        int pair, xb, fmt;
+        const int seg = wbytes(it, pair, xb, fmt);
+        const QmvParams& q = P.ops[it.op].q;
+        const WSeg& sg = q.seg[seg];
+        const int u_in = seg ? it.unit - q.seg[0].groups * q.S : it.unit;
+        const int grp = u_in / q.S, split = u_in - grp * q.S;
+        const int ksf = fmt_kt(fmt) / 16;
+        const int ks0 = (split * sg.tiles_per_split + it.local) * ksf;
+        const int xf = ksf * NT * 256, x32 = x32_bytes(fmt, NT), x16 = x16_bytes(fmt, NT);
         const int st = pos % D;
-        uint8_t* dst = ring + (size_t)st * KG::STAGE + kGemvWarps * KG::PAIRMAX;
-        tma_bulk_g2s(dst, reinterpret_cast<const uint8_t*>(p.xfrag) + (size_t)ks0 * NT * 256, xf, &full[st]);
-        if (x32) tma_bulk_g2s(dst + xf, p.xsum32 + (size_t)(ks0 / 2) * 8 * NT, x32, &full[st]);
-        if (x16) tma_bulk_g2s(dst + xf + x32, p.xsum16 + (size_t)ks0 * 8 * NT, x16, &full[st]);
+        uint8_t* dst = ring + (size_t)st * FG::STAGE + kGemvWarps * FG::PAIRMAX;
+        tma_bulk_g2s(dst, reinterpret_cast<const uint8_t*>(q.xfrag) + (size_t)ks0 * NT * 256, xf, &full[st]);
+        if (x32) tma_bulk_g2s(dst + xf, q.xsum32 + (size_t)(ks0 / 2) * 8 * NT, x32, &full[st]);
+        if (x16) tma_bulk_g2s(dst + xf + x32, q.xsum16 + (size_t)ks0 * 8 * NT, x16, &full[st]);
       };
-      const int pre = total < D ? total : D;
-      for (int pos = 0; pos < pre; ++pos) issue_w(pos);
-      // Weights above do not depend on the previous kernel; operands do.
-      pdl_wait();
-      for (int pos = 0; pos < pre; ++pos) issue_x(pos);
-      bool ok = true;
-      for (int pos = pre; pos < total && ok; ++pos) {
-        ok = mbar_wait_bounded(&empty[pos % D], (uint32_t)(((pos / D) - 1) & 1), p.err);
-        if (ok) {
-          issue_w(pos);
-          issue_x(pos);
+      // L2 run-ahead: stage `pi` of this CTA's weight stream is prefetched
+      // into L2 while the ring is still `l2_ahead` stages behind, so HBM keeps
+      // streaming while ops wait on their inputs (and before pdl_wait, while
+      // the previous kernel still runs).
+      auto issue_pf = [&](const SeqIt& it) {
+        int pair, xb, fmt;
+        const int seg = wbytes(it, pair, xb, fmt);
+        const QmvParams& q = P.ops[it.op].q;
+        const WSeg& sg = q.seg[seg];
+        const int u_in = seg ? it.unit - q.seg[0].groups * q.S : it.unit;
+        const int grp = u_in / q.S, split = u_in - grp * q.S;
+        const size_t kt = (size_t)split * sg.tiles_per_split + it.local;
+#pragma unroll
+        for (int w = 0; w < kGemvWarps; ++w)
+          tma_prefetch_l2(sg.w + ((size_t)(grp * kGemvWarps + w) * sg.k_tiles + kt) * pair, pair);
+      };
+      SeqIt wi, xi, pi;
+      seq_begin(P, c, G, wi);
+      xi = wi;
+      pi = wi;
+      int wpos = 0, xpos = 0, ppos = 0;
+      const int ahead = P.l2_ahead;
+      for (; pi.valid && ppos < D + ahead; ++ppos) {
+        if (ppos >= D) issue_pf(pi);
+        seq_next(P, c, G, pi);
+      }
+      for (; wi.valid && wpos < D; ++wpos) {  // weights only depend on nothing
+        issue_w(wi, wpos);
+        seq_next(P, c, G, wi);
+      }
+      pdl_wait();  // operands and counters come from the previous kernel
+      int ready_op = -1;
+      unsigned long long t_idle = 0;
+      while (xi.valid) {
+        bool progressed = false;
+        if (xpos < wpos) {
+          if (xi.op <= ready_op || op_inputs_ready(P, xi.op)) {
+            if (xi.op > ready_op) {
+              ready_op = xi.op;
+              fence_proxy_async_global();
+            }
+            issue_x(xi, xpos);
+            seq_next(P, c, G, xi);
+            ++xpos;
+            progressed = true;
+          }
+        }
+        if (wi.valid && mbar_test_wait(&empty[wpos % D], (uint32_t)(((wpos / D) - 1) & 1))) {
+          issue_w(wi, wpos);
+          seq_next(P, c, G, wi);
+          ++wpos;
+          progressed = true;
+          if (pi.valid && ppos < wpos + D + ahead) {
+            issue_pf(pi);
+            seq_next(P, c, G, pi);
+            ++ppos;
+          }
+        }
+        if (progressed) {
+          t_idle = 0;
+        } else {
+          const unsigned long long now = global_timer_ns();
+          if (t_idle == 0) t_idle = now;
+          else if (now - t_idle > kMbarTimeoutNs) {
+            atomicOr(P.err, DEV_ERR_MBAR_TIMEOUT);
+            break;
+          }
         }
       }
       // Every issued copy must land before this CTA can retire.
-      for (int pos = total - pre; pos < total; ++pos)
-        if (pos >= 0) mbar_wait_bounded(&full[pos % D], (uint32_t)((pos / D) & 1), nullptr);
+      const int first = wpos > D ? wpos - D : 0;
+      for (int pos = first; pos < wpos; ++pos) mbar_wait_bounded(&full[pos % D], (uint32_t)((pos / D) & 1), nullptr);
     }
     return;
   }
@@ -729,12 +887,17 @@ __global__ void __launch_bounds__(160, NT == 1 ? 4 : (NT == 2 ? 3 : (NT == 4 ? 2
   float acc[2][NT][4];
   bool ok = true;
   int pos = 0;
-  for (int k = 0; k < my_units; ++k) {
-    const int unit = c + k * G;
-    const int seg = unit < unitsA ? 0 : 1;
-    const int u_in = seg ? unit - unitsA : unit;
-    const int grp = u_in / S, split = u_in - grp * S;
-    const int cnt = seg ? cntB : cntA;
+  SeqIt it;
+  seq_begin(P, c, G, it);
+  while (it.valid) {
+    const int op = it.op;
+    const QmvParams& q = P.ops[op].q;
+    const int unitsA = q.seg[0].groups * q.S;
+    const int seg = it.unit < unitsA ? 0 : 1;
+    const int u_in = seg ? it.unit - unitsA : it.unit;
+    const int grp = u_in / q.S, split = u_in - grp * q.S;
+    const int fmt = q.seg[seg].fmt;
+    const int cnt = it.cnt;
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
@@ -743,24 +906,31 @@ __global__ void __launch_bounds__(160, NT == 1 ? 4 : (NT == 2 ? 3 : (NT == 4 ? 2
         for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
     for (int local = 0; local < cnt; ++local, ++pos) {
       const int st = pos % D;
-      if (ok) ok = mbar_wait_bounded(&full[st], (uint32_t)((pos / D) & 1), p.err);
+      if (ok) ok = mbar_wait_bounded(&full[st], (uint32_t)((pos / D) & 1), P.err);
       if (ok) {
-        const uint8_t* stage = ring + (size_t)st * KG::STAGE;
-        const uint8_t* tp = stage + warp * KG::PAIRMAX;
-        const uint8_t* xs = stage + kGemvWarps * KG::PAIRMAX;
-        if constexpr (FA == FB) {
-          process_tile<FA, NT>(tp, xs, scr, lane, acc);
-        } else {
-          if (seg == 0) process_tile<FA, NT>(tp, xs, scr, lane, acc);
-          else process_tile<FB, NT>(tp, xs, scr, lane, acc);
-        }
+        const uint8_t* stage = ring + (size_t)st * FG::STAGE;
+        process_any<SET, NT>(fmt, stage + warp * FG::PAIRMAX, stage + kGemvWarps * FG::PAIRMAX, scr, lane, acc);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
     }
-    const int ggrp = (seg ? p.seg[0].groups : 0) + grp;
-    reduce_and_epilogue<NT>(p, ggrp, split, acc, tail);
+    // The epilogue reads activations / norms of earlier ops: acquire them.
+    if (threadIdx.x == 0 && P.ops[op].dep >= 0) {
+      const int dep = P.ops[op].dep;
+      const QmvParams& d = P.ops[dep].q;
+      const unsigned long long t0 = global_timer_ns();
+      while (ld_acquire(P.done + dep) < d.seg[0].groups + d.seg[1].groups) {
+        if (global_timer_ns() - t0 > kMbarTimeoutNs) {
+          atomicOr(P.err, DEV_ERR_MBAR_TIMEOUT);
+          break;
+        }
+      }
+    }
     consumer_sync();
+    reduce_and_epilogue<NT>(q, (seg ? q.seg[0].groups : 0) + grp, split, acc, tail, P.done + op);
+    consumer_sync();
+    it.local = cnt - 1;
+    seq_next(P, c, G, it);
   }
 }
 
@@ -864,14 +1034,13 @@ __global__ void repack_kernel(const uint8_t* raw, int fmt, int N, int K, uint8_t
   }
   // K-quants: low nibbles in A-fragment order.
   for (int s = 0; s < 16; ++s) {
-    uint32_t w = 0, hw = 0;
+    uint32_t w = 0;
     for (int p = 0; p < 8; ++p) {
       int row, col;
       nib_pos(p, g, t, row, col);
       const uint8_t* rowp = raw + (size_t)(r0 + row) * row_bytes;
       const int k = kbase + 16 * s + col;
       w |= (uint32_t)code_at(rowp, fmt, k) << (4 * p);
-      (void)hw;
     }
     *reinterpret_cast<uint32_t*>(out + (s >> 2) * 512 + lane * 16 + (s & 3) * 4) = w;
   }
@@ -922,90 +1091,107 @@ __global__ void repack_kernel(const uint8_t* raw, int fmt, int N, int K, uint8_t
   }
 }
 
-template <int FA, int FB, int NT>
-cudaError_t launch_inst(const QmvParams& p, cudaStream_t stream, bool pdl) {
-  constexpr int smem = KGeo<FA, FB, NT>::SMEM;
-  static int blocks_per_sm[16] = {0};
-  static int num_sms[16] = {0};
+template <int SET, int NT>
+struct FwdInst {
+  struct Occ {
+    int bps[16] = {0};
+    int sms[16] = {0};
+  };
+  static Occ& occ() {
+    static Occ o;
+    return o;
+  }
+  static cudaError_t prepare(int dev) {
+    int* bps = occ().bps;
+    int* sms = occ().sms;
+    if (bps[dev]) return cudaSuccess;
+    constexpr int smem = FGeo<SET, NT>::SMEM;
+    cudaError_t e = cudaFuncSetAttribute(fwd_kernel<SET, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    int b = 0;
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fwd_kernel<SET, NT>, (kGemvWarps + 1) * 32, smem);
+    if (e != cudaSuccess) return e;
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return e;
+    sms[dev] = n;
+    bps[dev] = b > 0 ? b : 1;
+    return cudaSuccess;
+  }
+  static cudaError_t launch(const FwdParams& p, cudaStream_t stream, bool pdl) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= 16) return cudaErrorInvalidDevice;
+    cudaError_t e = prepare(dev);
+    if (e != cudaSuccess) return e;
+    const int* bps = occ().bps;
+    const int* sms = occ().sms;
+    int grid = bps[dev] * sms[dev];
+    if (const char* env = getenv("SPEC_B200_GEMV_CTAS_PER_SM")) {
+      const int v = atoi(env);
+      if (v > 0 && v < bps[dev]) grid = v * sms[dev];
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid, 1, 1);
+    cfg.blockDim = dim3((kGemvWarps + 1) * 32, 1, 1);
+    cfg.dynamicSmemBytes = FGeo<SET, NT>::SMEM;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, fwd_kernel<SET, NT>, p);
+  }
+};
+
+template <int SET>
+cudaError_t launch_set(const FwdParams& p, int M, cudaStream_t s, bool pdl) {
+  const int nt = nt_for_rows(M);
+  if (nt == 1) return FwdInst<SET, 1>::launch(p, s, pdl);
+  if (nt == 2) return FwdInst<SET, 2>::launch(p, s, pdl);
+  if (nt == 4) return FwdInst<SET, 4>::launch(p, s, pdl);
+  return FwdInst<SET, 8>::launch(p, s, pdl);
+}
+
+// Instantiated format sets: GGUF K-quant mixes (with the Q8_0 fallback for
+// K % 256 != 0) and BF16.
+constexpr int kSetK4 = FS_Q4K | FS_Q6K | FS_Q80;
+constexpr int kSetK5 = FS_Q5K | FS_Q6K | FS_Q80;
+constexpr int kSetBF = FS_BF16;
+
+}  // namespace
+
+int fwd_fmt_set_for(int bits) {
+  if ((bits & ~kSetK4) == 0) return kSetK4;
+  if ((bits & ~kSetK5) == 0) return kSetK5;
+  if ((bits & ~kSetBF) == 0) return kSetBF;
+  return 0;
+}
+
+int fwd_ctas_per_sm(int set) {
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 16) return cudaErrorInvalidDevice;
-  if (!blocks_per_sm[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(qmv_kernel<FA, FB, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    int bps = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, qmv_kernel<FA, FB, NT>, (kGemvWarps + 1) * 32, smem);
-    if (e != cudaSuccess) return e;
-    int sms = 0;
-    e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (e != cudaSuccess) return e;
-    num_sms[dev] = sms;
-    blocks_per_sm[dev] = bps > 0 ? bps : 1;
+  cudaError_t e = cudaErrorInvalidValue;
+  if (set == kSetK4) {
+    e = FwdInst<kSetK4, 1>::prepare(dev);
+    if (e == cudaSuccess) return FwdInst<kSetK4, 1>::occ().bps[dev];
+  } else if (set == kSetK5) {
+    e = FwdInst<kSetK5, 1>::prepare(dev);
+    if (e == cudaSuccess) return FwdInst<kSetK5, 1>::occ().bps[dev];
+  } else if (set == kSetBF) {
+    e = FwdInst<kSetBF, 1>::prepare(dev);
+    if (e == cudaSuccess) return FwdInst<kSetBF, 1>::occ().bps[dev];
   }
-  const int units = (p.seg[0].groups + p.seg[1].groups) * p.S;
-  int grid = blocks_per_sm[dev] * num_sms[dev];
-  if (const char* env = getenv("SPEC_B200_GEMV_CTAS_PER_SM")) {
-    const int v = atoi(env);
-    if (v > 0 && v < blocks_per_sm[dev]) grid = v * num_sms[dev];
-  }
-  if (grid > units) grid = units;
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(grid, 1, 1);
-  cfg.blockDim = dim3((kGemvWarps + 1) * 32, 1, 1);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, qmv_kernel<FA, FB, NT>, p);
+  return 3;
 }
 
-template <int FA, int FB>
-cudaError_t launch_nt(const QmvParams& p, cudaStream_t s, bool pdl) {
-  const int nt = nt_for_rows(p.M);
-  if (nt == 1) return launch_inst<FA, FB, 1>(p, s, pdl);
-  if (nt == 2) return launch_inst<FA, FB, 2>(p, s, pdl);
-  if (nt == 4) return launch_inst<FA, FB, 4>(p, s, pdl);
-  return launch_inst<FA, FB, 8>(p, s, pdl);
-}
-
-}  // namespace
-
-namespace {
-template <int FA, int FB>
-int ctas_per_sm_inst() {
-  int bps = 0;
-  constexpr int smem = KGeo<FA, FB, 1>::SMEM;
-  if (cudaFuncSetAttribute(qmv_kernel<FA, FB, 1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess)
-    return 4;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&bps, qmv_kernel<FA, FB, 1>, (kGemvWarps + 1) * 32, smem) !=
-      cudaSuccess)
-    return 4;
-  return bps > 0 ? bps : 1;
-}
-}  // namespace
-
-int qmv_ctas_per_sm(int fa, int fb) {
-  if (fa == WF_Q4_K && fb == WF_Q4_K) return ctas_per_sm_inst<WF_Q4_K, WF_Q4_K>();
-  if (fa == WF_Q4_K && fb == WF_Q6_K) return ctas_per_sm_inst<WF_Q4_K, WF_Q6_K>();
-  if (fa == WF_Q6_K && fb == WF_Q6_K) return ctas_per_sm_inst<WF_Q6_K, WF_Q6_K>();
-  if (fa == WF_Q5_K && fb == WF_Q5_K) return ctas_per_sm_inst<WF_Q5_K, WF_Q5_K>();
-  if (fa == WF_Q8_0 && fb == WF_Q8_0) return ctas_per_sm_inst<WF_Q8_0, WF_Q8_0>();
-  if (fa == WF_BF16 && fb == WF_BF16) return ctas_per_sm_inst<WF_BF16, WF_BF16>();
-  return 4;
-}
-
-cudaError_t launch_qmv(const QmvParams& p, cudaStream_t s, bool pdl) {
-  if (p.M < 1 || p.M > kMaxRows) return cudaErrorInvalidValue;
-  const int fa = p.seg[0].fmt, fb = p.seg[1].groups ? p.seg[1].fmt : fa;
-  if (fa == WF_Q4_K && fb == WF_Q4_K) return launch_nt<WF_Q4_K, WF_Q4_K>(p, s, pdl);
-  if (fa == WF_Q4_K && fb == WF_Q6_K) return launch_nt<WF_Q4_K, WF_Q6_K>(p, s, pdl);
-  if (fa == WF_Q6_K && fb == WF_Q6_K) return launch_nt<WF_Q6_K, WF_Q6_K>(p, s, pdl);
-  if (fa == WF_Q5_K && fb == WF_Q5_K) return launch_nt<WF_Q5_K, WF_Q5_K>(p, s, pdl);
-  if (fa == WF_Q8_0 && fb == WF_Q8_0) return launch_nt<WF_Q8_0, WF_Q8_0>(p, s, pdl);
-  if (fa == WF_BF16 && fb == WF_BF16) return launch_nt<WF_BF16, WF_BF16>(p, s, pdl);
+cudaError_t launch_fwd(const FwdParams& p, int fmt_set, int M, cudaStream_t s, bool pdl) {
+  if (M < 1 || M > kMaxRows || p.n_ops < 1 || p.n_ops > kMaxLaunchOps) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(p.ops) % 16) return cudaErrorMisalignedAddress;
+  if (fmt_set == kSetK4) return launch_set<kSetK4>(p, M, s, pdl);
+  if (fmt_set == kSetK5) return launch_set<kSetK5>(p, M, s, pdl);
+  if (fmt_set == kSetBF) return launch_set<kSetBF>(p, M, s, pdl);
   return cudaErrorNotSupported;
 }
 

@@ -45,9 +45,8 @@ CFG = dict(arch="llama", n_layers=32, hidden=4096, n_heads=32, n_kv_heads=8, ffn
            rope_theta=5e5, eps=1e-5)
 K_DRAFT = 4
 KV_LEN = 2048
-KIND_NAMES = {0: "embed", 1: "qkv_gemv", 2: "attention", 3: "attn_combine", 4: "o_gemv", 5: "gate_up_gemv",
-              6: "down_gemv", 7: "lm_head_gemv"}
-GEMV_KINDS = (1, 4, 5, 6, 7)
+KIND_NAMES = {0: "embed", 2: "attention (split + combine)", 8: "fwd_kernel (persistent multi-op GEMV)"}
+GEMV_KINDS = (8,)
 
 
 def dist_env():
@@ -325,7 +324,7 @@ def run_b200(args, ws, rank, local, dist):
                             if dev_us else None, "peak_gbs": peak},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "kernel": "qmv_kernel (all GEMV launches of one verify forward)",
+                     "kernel": "fwd_kernel (all persistent multi-op GEMV launches of one verify forward)",
                      "peak_kind": peak_kind},
         "kernels": per_kind,
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": 1296 + 4 * K_DRAFT,

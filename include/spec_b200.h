@@ -163,9 +163,10 @@ void* spec_cuda_stream(const spec_model* m);
 /* One eager verify forward of [last] + drafts (the spec_batched_logits
  * protocol, but the decoder's history / KV length are left unchanged and the
  * cached next logits are dropped), with a CUDA event after every kernel.
- * Writes per-kernel device ms, kind (0 embed, 1 qkv, 2 attention,
- * 4 o-proj, 5 gate/up, 6 down, 7 lm_head) and algorithmic bytes (packed
- * weights, or KV bytes for attention); returns the number of kernels, or a
+ * Writes per-launch device ms, kind (0 embed, 2 attention split+combine,
+ * 8 one persistent multi-op GEMV launch: a layer's o-proj, gate/up and down
+ * plus the next layer's qkv, or the LM head) and algorithmic bytes (packed
+ * weights, or KV bytes for attention); returns the number of launches, or a
  * negated status on error. */
 int spec_profile_forward(spec_model* m, const uint32_t* drafts, int k, float* ms_out, int* kind_out,
                          int64_t* bytes_out, int cap);
