@@ -125,6 +125,8 @@ SIGNATURES = [
     ("spec_qmatmul", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     ("spec_qweight_bytes", ctypes.c_int64, [ctypes.c_void_p]),
     ("spec_qmatmul_time", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, c_f32_p]),
+    ("spec_qmatmul_noalloc", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
 ]
 
 _lib: Optional[ctypes.CDLL] = None

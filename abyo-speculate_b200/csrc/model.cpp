@@ -1872,6 +1872,33 @@ static int qmatmul_enqueue(spec_qweight* w, int M, float* y_dev, cudaStream_t s)
   return SPEC_OK;
 }
 
+}  // extern "C"
+
+namespace specb200 {
+
+bool qweight_launch_desc(spec_qweight* w, int M, float* y_dev, QmatmulLaunch* out) {
+  if (!w || !out) return false;
+  spec_model* m = w->ctx.get();
+  QmvParams p = base_params(m, w->mat, M);
+  p.part = nullptr;
+  p.counters = nullptr;
+  p.act_bf16 = w->mat.seg[0].fmt == WF_BF16 ? 1 : 0;
+  p.epi = EPI_STORE;
+  p.out = y_dev;
+  p.ld_out = w->mat.N;
+  out->p = p;
+  out->fmt_set = m->fmt_set ? m->fmt_set : fwd_fmt_set_for(m->fmt_bits);
+  out->device = m->device;
+  out->stream = m->stream;
+  return true;
+}
+
+void set_thread_error(const char* msg) { g_load_error = msg; }
+
+}  // namespace specb200
+
+extern "C" {
+
 int spec_qmatmul(spec_qweight* w, const float* x_dev, int M, float* y_dev, void* stream) {
   if (!w || !x_dev || !y_dev || M < 1 || M > kMaxRows) return SPEC_ERR_INVALID;
   spec_model* m = w->ctx.get();

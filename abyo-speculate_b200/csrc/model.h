@@ -59,4 +59,25 @@ struct Part {
 
 int choose_split(int groups, int k_tiles_gcd, int max_ctas);
 
+// What a launch path that brings its own scratch needs to run one standalone
+// matmul of an uploaded weight (spec_qweight).  Filling it allocates nothing.
+struct QmatmulLaunch {
+  QmvParams p;           // weight segments, rows, splits, M, output; scratch pointers null
+  int fmt_set = 0;       // forward-kernel format set of the weight
+  int device = 0;
+  cudaStream_t stream = nullptr;  // the weight's own stream
+};
+
+}  // namespace specb200
+
+struct spec_qweight;
+
+namespace specb200 {
+
+// Fills `out` for y[M][N] = x[M][K] . W^T into y_dev.  Returns false for a
+// null weight.
+bool qweight_launch_desc(spec_qweight* w, int M, float* y_dev, QmatmulLaunch* out);
+// Sets the message spec_last_error(NULL) returns on this thread (error paths).
+void set_thread_error(const char* msg);
+
 }  // namespace specb200

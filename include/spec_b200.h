@@ -190,6 +190,40 @@ int64_t spec_qweight_bytes(const spec_qweight* w);
  * spec_qmatmul shape (CUDA events on the launching stream). */
 int spec_qmatmul_time(spec_qweight* w, int M, int iters, int flush_l2, float* avg_ms);
 
+/* ---- no-allocation matmul (no counterpart in the reference) ---------------
+ * spec_qmatmul_noalloc: the spec_qmatmul contract (same arguments, result
+ * within the same tolerance; it runs the same kernel), but the call
+ * allocates no memory.  spec_qmatmul allocates a descriptor slot and pinned
+ * staging on its first call; this entry point keeps every piece of per-call
+ * scratch (operand fragments and column sums, split-K partials and counters,
+ * the op descriptor) in one file-scope device array of
+ * SPEC_NOALLOC_SCRATCH_BYTES per device.  It is for callers that cannot
+ * allocate:
+ *   - a serving runtime that reserves nearly all device memory up front
+ *     (weights, KV pages), where a late cudaMalloc fails or forces eviction;
+ *   - a latency-critical loop that must not meet the device-wide
+ *     synchronisation that cudaFree (and at times cudaMalloc) implies;
+ *   - code running inside an allocator or memory-pool callback, where
+ *     re-entering the allocator deadlocks.
+ * Limits and rules:
+ *   - a call needs about 2.4*K*m8 bytes of operand (m8 = M rounded up to
+ *     8, 16, 32 or 64) plus, when the weight's K is split S ways across
+ *     CTAs, S*N*4*m8 bytes of partials; a shape needing more than
+ *     SPEC_NOALLOC_SCRATCH_BYTES returns SPEC_ERR_INVALID (message via
+ *     spec_last_error(NULL)) and launches nothing;
+ *   - the first call on a device looks the array up (cudaGetSymbolAddress)
+ *     with that device current; make that first call before any stream
+ *     capture begins;
+ *   - every call on a device shares the one array: calls on the same stream
+ *     are ordered, but calls that overlap in time (different streams, or
+ *     several host threads) race on it and corrupt each other's results;
+ *   - each call zeroes the counters it uses (an async memset on `stream`)
+ *     and rewrites everything else it reads before reading it;
+ *   - stream may be NULL (the weight's own stream, synchronised on return).
+ * Error messages are thread-local (spec_last_error(NULL)). */
+#define SPEC_NOALLOC_SCRATCH_BYTES (16u << 20)
+int spec_qmatmul_noalloc(spec_qweight* w, const float* x_dev, int M, float* y_dev, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
