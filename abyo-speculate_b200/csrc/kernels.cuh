@@ -23,6 +23,11 @@ enum DevError : unsigned {
   DEV_ERR_BAD_ARGUMENT = 1u << 1,   // a kernel saw an out-of-range index
 };
 
+// The error word is err[0]; a wait that gives up also records where, once:
+// err[1] = site | op << 8 | cta << 16, err[2] = stage / ring position,
+// err[3] = the counter value it last saw.
+enum WaitSite : unsigned { WAIT_CONSUMER_FULL = 1, WAIT_CONSUMER_DEP = 2, WAIT_PRODUCER_IDLE = 3 };
+
 // GGML type ids (public GGUF specification) of the weight formats handled.
 enum WFmt : int { WF_F32 = 0, WF_F16 = 1, WF_Q8_0 = 8, WF_Q4_K = 12, WF_Q5_K = 13, WF_Q6_K = 14, WF_BF16 = 30 };
 
@@ -64,14 +69,19 @@ struct WSeg {                // one weight segment (one format)
   int fmt = 0;
   int groups = 0;              // 128-row groups in this segment
   int k_tiles = 0;             // K / KT
-  int tiles_per_split = 0;     // k_tiles / S
 };
 
 struct QmvParams {
   WSeg seg[2];
   int n_rows = 0;        // total output rows (both segments)
   int K = 0;
-  int S = 1;             // K splits (grid.y)
+  // Work split (stream-K): the op's stages (one k-tile of one 128-row group;
+  // segment 0's groups first, each group's k-tiles in order) are cut into
+  // `chunks` contiguous runs, chunk i = [i*stages/chunks, (i+1)*stages/chunks).
+  // The cut depends on the matrix only, never on M or the grid, so every
+  // row's f32 summation order is fixed.
+  int stages = 0;
+  int chunks = 1;
   int M = 1;
   // activation operand
   const uint32_t* xfrag = nullptr;
@@ -82,7 +92,8 @@ struct QmvParams {
   int ss_groups = 0;
   float ss_inv_dim = 0.f;
   float eps = 0.f;
-  // split-K scratch
+  // split-K scratch: partial sums, slot (chunk + group) x [128 rows][8*NT]
+  // (chunks + groups slots), and one arrival counter per group (zero between ops)
   float* part = nullptr;
   int* counters = nullptr;
   unsigned* err = nullptr;
@@ -114,7 +125,7 @@ struct QmvParams {
 
 // ---- persistent multi-op GEMV kernel -------------------------------------
 // One launch runs a schedule of GEMV ops.  Every CTA walks the same op list
-// and takes units c, c+G, c+2G, ... of each op.  A producer warp streams the
+// and takes chunks c, c+G, c+2G, ... of each op.  A producer warp streams the
 // weight tiles of all its units, across op boundaries, through a TMA ring;
 // the activation tile of a stage is only fetched once the op it depends on
 // has completed (device-side completion counter), so weight streaming never

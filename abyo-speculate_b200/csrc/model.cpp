@@ -28,31 +28,13 @@ using namespace specb200;
 
 namespace specb200 {
 
-int choose_split(int groups, int k_tiles_gcd, int max_ctas) {
-  const char* env = getenv("SPEC_B200_SPLIT");
-  if (env) {
-    const int s = atoi(env);
-    if (s > 0 && k_tiles_gcd % s == 0) return s;
+int choose_chunks(int stages, int resident_ctas) {
+  int c = resident_ctas;
+  if (const char* env = getenv("SPEC_B200_CHUNKS")) {
+    const int v = atoi(env);
+    if (v > 0) c = v;
   }
-  // The GEMV grid is persistent (max_ctas resident CTAs, each taking work
-  // units round-robin), so a split S gives groups*S units of k_tiles/S tiles
-  // per warp.  Score = load balance of the last round x per-unit overhead
-  // (about half a tile of epilogue per unit); pick the best divisor.
-  int best = 1;
-  double best_score = -1.0;
-  for (int s = 1; s <= k_tiles_gcd; ++s) {
-    if (k_tiles_gcd % s) continue;
-    const double units = (double)groups * s;
-    const double rounds = units / max_ctas;
-    const double balance = rounds / ceil(rounds);
-    const double tps = (double)k_tiles_gcd / s;
-    const double score = balance * tps / (tps + 0.5);
-    if (score > best_score + 1e-9) {
-      best_score = score;
-      best = s;
-    }
-  }
-  return best;
+  return std::max(1, std::min(c, stages));
 }
 
 }  // namespace specb200
@@ -189,7 +171,8 @@ struct spec_model {
     FwdOp* solo = nullptr;  // the same ops with dep = -1, for one-op launches
   };
   std::map<int, Schedule> schedules;
-  int l2_ahead = 4;                 // weight stages each CTA prefetches into L2 ahead of its ring
+  int l2_ahead = 0;                 // weight stages each CTA prefetches into L2 ahead of its ring (SPEC_B200_L2_AHEAD)
+  bool use_pdl = true;              // programmatic dependent launch between forward kernels
   FwdOp* single_op = nullptr;       // device slot for one-op launches
   FwdOp* single_op_host = nullptr;  // pinned staging
   int* single_done = nullptr;
@@ -336,9 +319,10 @@ int build_mat(spec_model* m, const std::vector<Part>& parts, int K, bool interle
   m->fmt_bits |= bits;
   const int set = fwd_fmt_set_for(bits);
   if (!set) return m->fail(SPEC_ERR_UNSUPPORTED, "weight format combination not supported by the forward kernel");
-  out.S = choose_split(groups, kgcd, fwd_ctas_per_sm(set) * m->num_sms);
-  for (int si = 0; si < 2; ++si)
-    if (out.seg[si].groups) out.seg[si].tiles_per_split = out.seg[si].k_tiles / out.S;
+  out.stages = out.seg[0].groups * out.seg[0].k_tiles + out.seg[1].groups * out.seg[1].k_tiles;
+  out.chunks = choose_chunks(out.stages, fwd_ctas_per_sm(set) * m->num_sms);
+  (void)groups;
+  (void)kgcd;
   return SPEC_OK;
 }
 
@@ -390,7 +374,7 @@ int alloc_runtime(spec_model* m) {
   auto acc_mat = [&](const Mat& mt) {
     const int g = mt.seg[0].groups + mt.seg[1].groups;
     max_groups = std::max(max_groups, g);
-    if (mt.S > 1) part = std::max(part, (size_t)mt.S * g * kGroupRows * kMaxRows);
+    part = std::max(part, (size_t)partial_slots(mt) * kGroupRows * kMaxRows);
   };
   for (auto& L : m->layers) {
     acc_mat(L.qkv);
@@ -481,7 +465,8 @@ QmvParams base_params(spec_model* m, const Mat& mt, int M) {
   p.seg[1] = mt.seg[1];
   p.n_rows = mt.N;
   p.K = mt.K;
-  p.S = mt.S;
+  p.stages = mt.stages;
+  p.chunks = mt.chunks;
   p.M = M;
   p.part = m->gemv_part;
   p.counters = m->counters;
@@ -743,7 +728,7 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
     pr->ev.push_back(e0);
     if ((e = cudaEventRecord(e0, s)) != cudaSuccess) return e;
   }
-  const bool pdl = pr == nullptr;
+  const bool pdl = pr == nullptr && m->use_pdl;
   e = launch_embed(ep, nt, s, false);
   if (e != cudaSuccess) return e;
   if ((e = prof_mark(pr, s, K_EMBED, (int64_t)M * H * 8)) != cudaSuccess) return e;
@@ -846,7 +831,7 @@ int run_forward(spec_model* m, int M, int flags, const std::vector<int>* collect
   }
   ge.runs++;
   if (e == cudaSuccess) e = cudaEventRecord(m->ev1, m->stream);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(m->err_host, m->err_dev, 4, cudaMemcpyDeviceToHost, m->stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(m->err_host, m->err_dev, 16, cudaMemcpyDeviceToHost, m->stream);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "forward launch"));
   return SPEC_OK;
 }
@@ -856,11 +841,17 @@ int finish(spec_model* m) {
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "forward"));
   cudaEventElapsedTime(&m->last_ms, m->ev0, m->ev1);
   if (*m->err_host) {
-    const unsigned bits = *m->err_host;
-    *m->err_host = 0;
-    cudaMemsetAsync(m->err_dev, 0, 4, m->stream);
+    const unsigned bits = m->err_host[0], where = m->err_host[1], pos = m->err_host[2], seen = m->err_host[3];
+    for (int i = 0; i < 4; ++i) m->err_host[i] = 0;
+    cudaMemsetAsync(m->err_dev, 0, 16, m->stream);
     cudaStreamSynchronize(m->stream);
-    if (bits & DEV_ERR_MBAR_TIMEOUT) return m->fail(SPEC_ERR_TIMEOUT, "a device wait gave up (mbarrier timeout)");
+    if (bits & DEV_ERR_MBAR_TIMEOUT) {
+      char msg[192];
+      snprintf(msg, sizeof msg,
+               "a device wait gave up (mbarrier timeout): site %u op %u cta %u, stage/pos %u (0x%x), counter %d",
+               where & 0xffu, (where >> 8) & 0xffu, where >> 16, pos, pos, (int)seen);
+      return m->fail(SPEC_ERR_TIMEOUT, msg);
+    }
     return m->fail(SPEC_ERR_INVALID, "a kernel rejected an index (token id out of range?)");
   }
   return SPEC_OK;
@@ -967,6 +958,7 @@ int init_device(spec_model* m, const spec_load_opts* opts) {
   m->device = opts ? opts->device : 0;
   m->use_graphs = opts ? (opts->use_graphs != 0) : true;
   if (getenv("SPEC_B200_NO_GRAPHS")) m->use_graphs = false;
+  if (getenv("SPEC_B200_NO_PDL")) m->use_pdl = false;
   if (const char* env = getenv("SPEC_B200_L2_AHEAD")) m->l2_ahead = atoi(env);
   cudaError_t e = cudaSetDevice(m->device);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "cudaSetDevice"));
@@ -1808,7 +1800,7 @@ int spec_qweight_upload(int ggml_type, const void* gguf_blocks, int n_rows, int 
   if (e == cudaSuccess && rc == SPEC_OK) e = m->dalloc(&w->x32, (size_t)(k_cols / 32) * kMaxRows * 4);
   if (e == cudaSuccess && rc == SPEC_OK) e = m->dalloc(&w->y, (size_t)n_rows * kMaxRows * 4);
   if (e == cudaSuccess && rc == SPEC_OK)
-    e = m->dalloc(&m->gemv_part, (size_t)w->mat.S * groups * kGroupRows * kMaxRows * 4);
+    e = m->dalloc(&m->gemv_part, (size_t)partial_slots(w->mat) * kGroupRows * kMaxRows * 4);
   if (e == cudaSuccess && rc == SPEC_OK) e = m->dalloc(&m->counters, (size_t)groups * 4);
   if (e == cudaSuccess && rc == SPEC_OK) e = m->dalloc(&m->err_dev, 16);
   if (e == cudaSuccess && rc == SPEC_OK) e = cudaStreamSynchronize(m->stream);

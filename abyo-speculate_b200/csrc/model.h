@@ -28,7 +28,9 @@ struct ModelCfg {
 struct Mat {
   uint8_t* tiles = nullptr;
   WSeg seg[2];
-  int N = 0, K = 0, S = 1;
+  int N = 0, K = 0;
+  int stages = 0;  // (group, k-tile) stages of the GEMV
+  int chunks = 1;  // stream-K chunks (fixed per matrix)
   int64_t bytes = 0;
 };
 
@@ -57,7 +59,12 @@ struct Part {
   int rows = 0;
 };
 
-int choose_split(int groups, int k_tiles_gcd, int max_ctas);
+// Stream-K chunk count for a GEMV of `stages` stages: one chunk per resident
+// CTA of the 1-8 row instantiation (SPEC_B200_CHUNKS overrides), at most one
+// per stage.
+int choose_chunks(int stages, int resident_ctas);
+// Partial-sum slots a matrix's split reduction needs (chunks + groups).
+inline int partial_slots(const Mat& m) { return m.chunks + m.seg[0].groups + m.seg[1].groups; }
 
 // What a launch path that brings its own scratch needs to run one standalone
 // matmul of an uploaded weight (spec_qweight).  Filling it allocates nothing.

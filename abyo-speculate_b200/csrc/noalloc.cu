@@ -32,7 +32,7 @@ struct Layout {
   size_t zero_begin, zero_end;  // [counters + done] must be zero at launch
 };
 
-Layout plan(int K, int nt, int groups, int S) {
+Layout plan(int K, int nt, int groups, int chunks) {
   Layout L;
   size_t o = 0;
   L.desc = o;
@@ -50,7 +50,7 @@ Layout plan(int K, int nt, int groups, int S) {
   L.x32 = o;
   o = align_up(o + (size_t)(K / 32) * 8 * nt * 4);
   L.part = o;
-  if (S > 1) o = align_up(o + (size_t)S * groups * kGroupRows * 8 * nt * 4);
+  if (chunks > 1) o = align_up(o + (size_t)(chunks + groups) * kGroupRows * 8 * nt * 4);
   L.total = o;
   return L;
 }
@@ -101,11 +101,11 @@ extern "C" int spec_qmatmul_noalloc(spec_qweight* w, const float* x_dev, int M, 
   }
   const int nt = nt_for_rows(M);
   const int groups = q.p.seg[0].groups + q.p.seg[1].groups;
-  const Layout L = plan(q.p.K, nt, groups, q.p.S);
+  const Layout L = plan(q.p.K, nt, groups, q.p.chunks);
   if (L.total > kNoAllocBytes) {
     set_thread_error(
         "spec_qmatmul_noalloc: this shape needs more scratch than SPEC_NOALLOC_SCRATCH_BYTES "
-        "(operand K*16*ceil8(M) + split partials); use spec_qmatmul");
+        "(operand plus split-K partials); use spec_qmatmul");
     return SPEC_ERR_INVALID;
   }
   uint8_t* base = nullptr;

@@ -21,10 +21,12 @@
 //        acc += s_row * D - c_row * xsum.
 //    Products q*x are exact in the tensor core (q <= 63, x f16), so the only
 //    roundings are the f16 activations and f32 accumulation.
-//  * K is split into S fixed chunks; partial sums go to scratch and the last
-//    CTA of a 128-row group adds them in split order 0..S-1, then runs the
-//    fused epilogue.  Nothing depends on M except which fragment columns are
-//    live, so row r's result is bit-identical for any M (batched == sequential).
+//  * Work is split stream-K style: an op's (group, k-tile) stages are cut into
+//    a fixed number of contiguous chunks, one per resident CTA.  A group cut
+//    across chunks leaves one partial per piece; the CTA delivering the last
+//    piece adds them in chunk order, then runs the fused epilogue.  The cut
+//    depends only on the matrix, so row r's result is bit-identical for any
+//    M (batched == sequential).
 //  * Programmatic dependent launch: a CTA issues its first weight copies, then
 //    waits for the previous kernel (griddepcontrol.wait) before touching
 //    activations, so weight streaming overlaps the predecessor's tail.
@@ -402,23 +404,25 @@ SPEC_DEV void emit_operand_warp(uint32_t* frag, float* xs16, float* xs32, int nt
 // Barrier among the 128 consumer threads only (the producer warp runs ahead).
 SPEC_DEV void consumer_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-// Sums the K splits of a 128-row group (the CTA that delivers the last split
-// does it) and runs the fused epilogue; that CTA then bumps `done`.
+// Finishes one piece (the part of a 128-row group inside one chunk).  A
+// group that lies in one chunk goes straight to the fused epilogue.  A group
+// cut across chunks i0..i1 leaves one partial per piece in slot (chunk +
+// group); the CTA that delivers the last piece sums the slots in chunk order
+// and runs the epilogue.  The CTA that ran the epilogue bumps `done`.
 template <int NT>
-SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, float (&acc)[2][NT][4], float* ys,
-                                  int* done) {
+SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0, int i1, float (&acc)[2][NT][4],
+                                  float* ys, int* done) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   __shared__ int s_last;
   __shared__ float s_rinv[kMaxRows];
   __shared__ float s_red[kGemvWarps][kMaxRows];
   const int M = p.M;
-  const int n_groups = p.seg[0].groups + p.seg[1].groups;
   consumer_sync();  // all warps are done with their scale scratch (aliased by ys)
 
-  if (p.S > 1) {
+  if (i0 != i1) {
     const size_t per = (size_t)kGroupRows * 8 * NT;
-    float* mine = p.part + ((size_t)split * n_groups + group) * per;
+    float* mine = p.part + (size_t)(own + group) * per;
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
@@ -429,7 +433,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
     consumer_sync();
     if (tid == 0) {
       const int prev = atomicAdd(&p.counters[group], 1);
-      s_last = (prev == p.S - 1);
+      s_last = (prev == i1 - i0);
       if (s_last) p.counters[group] = 0;
     }
     consumer_sync();
@@ -441,14 +445,14 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
-    // Sum the splits in index order; the loads of SB splits are issued together.
+    // Sum the pieces in chunk order; the loads of SB pieces are issued together.
     constexpr int SB = NT == 1 ? 4 : (NT == 2 ? 2 : 1);
-    for (int s0 = 0; s0 < p.S; s0 += SB) {
+    for (int s0 = i0; s0 <= i1; s0 += SB) {
       float4 v[SB][2][NT];
 #pragma unroll
       for (int q = 0; q < SB; ++q) {
-        if (s0 + q < p.S) {
-          const float* ps = p.part + ((size_t)(s0 + q) * n_groups + group) * per;
+        if (s0 + q <= i1) {
+          const float* ps = p.part + (size_t)(s0 + q + group) * per;
 #pragma unroll
           for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
@@ -459,7 +463,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int split, floa
       }
 #pragma unroll
       for (int q = 0; q < SB; ++q) {
-        if (s0 + q < p.S) {
+        if (s0 + q <= i1) {
 #pragma unroll
           for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
@@ -636,29 +640,49 @@ struct FGeo {
   static constexpr int SMEM = RING + TAIL;
 };
 
-// Walks (op, unit, tile) for CTA c in schedule order.
+// Stage s of an op: segment, group (within the segment and overall), k-tile.
+struct StageLoc {
+  int seg, lgrp, grp, kt, gstart;  // gstart: stage index of the group's first k-tile
+};
+SPEC_DEV StageLoc locate(const QmvParams& q, int s) {
+  StageLoc L;
+  const int a = q.seg[0].groups * q.seg[0].k_tiles;
+  L.seg = s < a ? 0 : 1;
+  const int r = L.seg ? s - a : s;
+  const int kt = q.seg[L.seg].k_tiles;
+  L.lgrp = r / kt;
+  L.kt = r - L.lgrp * kt;
+  L.grp = (L.seg ? q.seg[0].groups : 0) + L.lgrp;
+  L.gstart = s - L.kt;
+  return L;
+}
+SPEC_DEV int chunk_start(const QmvParams& q, int i) { return (int)(((long long)i * q.stages) / q.chunks); }
+// Chunk holding stage s: the largest i with chunk_start(i) <= s.
+SPEC_DEV int chunk_of(const QmvParams& q, int s) { return (int)(((long long)(s + 1) * q.chunks - 1) / q.stages); }
+
+// Walks (op, chunk, stage) for CTA c in schedule order: chunks c, c+G, ...
 struct SeqIt {
-  int op = 0, k = 0, local = 0, cnt = 0, unit = 0;
+  int op = 0, k = 0, s = 0, s_end = 0;
   bool valid = false;
 };
 
-SPEC_DEV int op_units(const QmvParams& q) { return (q.seg[0].groups + q.seg[1].groups) * q.S; }
-
 SPEC_DEV void seq_settle(const FwdParams& P, int c, int G, SeqIt& it) {
-  // Move to the first (op, k) with a unit for this CTA, starting at it.op / it.k.
+  // Move to the first non-empty chunk at or after (it.op, it.k).
   while (it.op < P.n_ops) {
     const QmvParams& q = P.ops[it.op].q;
-    const int u = c + it.k * G;
-    if (u < op_units(q)) {
-      const int unitsA = q.seg[0].groups * q.S;
-      it.unit = u;
-      it.cnt = u < unitsA ? q.seg[0].tiles_per_split : q.seg[1].tiles_per_split;
-      it.valid = true;
-      return;
+    const int i = c + it.k * G;
+    if (i < q.chunks) {
+      it.s = chunk_start(q, i);
+      it.s_end = chunk_start(q, i + 1);
+      if (it.s < it.s_end) {
+        it.valid = true;
+        return;
+      }
+      ++it.k;
+      continue;
     }
     ++it.op;
     it.k = 0;
-    it.local = 0;
   }
   it.valid = false;
 }
@@ -667,8 +691,7 @@ SPEC_DEV void seq_begin(const FwdParams& P, int c, int G, SeqIt& it) {
   seq_settle(P, c, G, it);
 }
 SPEC_DEV void seq_next(const FwdParams& P, int c, int G, SeqIt& it) {
-  if (++it.local < it.cnt) return;
-  it.local = 0;
+  if (++it.s < it.s_end) return;
   ++it.k;
   seq_settle(P, c, G, it);
 }
@@ -683,6 +706,15 @@ SPEC_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
       : "r"(smem_u32(bar)), "r"(parity)
       : "memory");
   return ok != 0;
+}
+
+// Records where a bounded wait gave up (first one wins), then flags it.
+SPEC_DEV void wait_gave_up(unsigned* err, unsigned site, int op, int where, int seen) {
+  if (atomicCAS(err + 1, 0u, site | ((unsigned)op << 8) | ((unsigned)blockIdx.x << 16)) == 0u) {
+    err[2] = (unsigned)where;
+    err[3] = (unsigned)seen;
+  }
+  atomicOr(err, DEV_ERR_MBAR_TIMEOUT);
 }
 
 SPEC_DEV int ld_acquire(const int* p) {
@@ -737,7 +769,12 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
   __shared__ __align__(8) uint64_t full[D];
   __shared__ __align__(8) uint64_t empty[D];
   __shared__ __align__(16) FwdOp s_ops[kMaxLaunchOps];
-  pdl_launch_dependents();
+  // No griddepcontrol.launch_dependents here: the kernels after this one
+  // (attention, then the next forward kernel) are only scheduled as its CTAs
+  // exit.  Letting them launch while these persistent CTAs still wait on one
+  // another lost a split-K group's completion on B200 (a bounded wait fired);
+  // the next forward kernel still overlaps attention through the attention
+  // kernels' own early trigger.
   // Op descriptors live in shared memory for the whole launch (the producer
   // walks them per tile).  They were uploaded long before this launch.
   {
@@ -765,39 +802,26 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
-      auto wbytes = [&](const SeqIt& it, int& pair, int& xb, int& fmt) {
-        const QmvParams& q = P.ops[it.op].q;
-        const int seg = it.unit < q.seg[0].groups * q.S ? 0 : 1;
-        fmt = q.seg[seg].fmt;
-        pair = fmt_pair_bytes(fmt);
-        xb = (fmt_kt(fmt) / 16) * NT * 256 + x32_bytes(fmt, NT) + x16_bytes(fmt, NT);
-        return seg;
-      };
       auto issue_w = [&](const SeqIt& it, int pos) {
-        int pair, xb, fmt;
-        const int seg = wbytes(it, pair, xb, fmt);
         const QmvParams& q = P.ops[it.op].q;
-        const WSeg& sg = q.seg[seg];
-        const int u_in = seg ? it.unit - q.seg[0].groups * q.S : it.unit;
-        const int grp = u_in / q.S, split = u_in - grp * q.S;
+        const StageLoc L = locate(q, it.s);
+        const WSeg& sg = q.seg[L.seg];
+        const int fmt = sg.fmt, pair = fmt_pair_bytes(fmt);
+        const int xb = (fmt_kt(fmt) / 16) * NT * 256 + x32_bytes(fmt, NT) + x16_bytes(fmt, NT);
         const int st = pos % D;
         mbar_arrive_expect_tx(&full[st], kGemvWarps * pair + xb);
         uint8_t* dst = ring + (size_t)st * FG::STAGE;
-        const size_t kt = (size_t)split * sg.tiles_per_split + it.local;
 #pragma unroll
         for (int w = 0; w < kGemvWarps; ++w)
-          tma_bulk_g2s(dst + w * FG::PAIRMAX, sg.w + ((size_t)(grp * kGemvWarps + w) * sg.k_tiles + kt) * pair, pair,
-                       &full[st]);
+          tma_bulk_g2s(dst + w * FG::PAIRMAX,
+                       sg.w + ((size_t)(L.lgrp * kGemvWarps + w) * sg.k_tiles + L.kt) * pair, pair, &full[st]);
       };
       auto issue_x = [&](const SeqIt& it, int pos) {
-        int pair, xb, fmt;
-        const int seg = wbytes(it, pair, xb, fmt);
         const QmvParams& q = P.ops[it.op].q;
-        const WSeg& sg = q.seg[seg];
-        const int u_in = seg ? it.unit - q.seg[0].groups * q.S : it.unit;
-        const int grp = u_in / q.S, split = u_in - grp * q.S;
+        const StageLoc L = locate(q, it.s);
+        const int fmt = q.seg[L.seg].fmt;
         const int ksf = fmt_kt(fmt) / 16;
-        const int ks0 = (split * sg.tiles_per_split + it.local) * ksf;
+        const int ks0 = L.kt * ksf;
         const int xf = ksf * NT * 256, x32 = x32_bytes(fmt, NT), x16 = x16_bytes(fmt, NT);
         const int st = pos % D;
         uint8_t* dst = ring + (size_t)st * FG::STAGE + kGemvWarps * FG::PAIRMAX;
@@ -810,16 +834,13 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
       // streaming while ops wait on their inputs (and before pdl_wait, while
       // the previous kernel still runs).
       auto issue_pf = [&](const SeqIt& it) {
-        int pair, xb, fmt;
-        const int seg = wbytes(it, pair, xb, fmt);
         const QmvParams& q = P.ops[it.op].q;
-        const WSeg& sg = q.seg[seg];
-        const int u_in = seg ? it.unit - q.seg[0].groups * q.S : it.unit;
-        const int grp = u_in / q.S, split = u_in - grp * q.S;
-        const size_t kt = (size_t)split * sg.tiles_per_split + it.local;
+        const StageLoc L = locate(q, it.s);
+        const WSeg& sg = q.seg[L.seg];
+        const int pair = fmt_pair_bytes(sg.fmt);
 #pragma unroll
         for (int w = 0; w < kGemvWarps; ++w)
-          tma_prefetch_l2(sg.w + ((size_t)(grp * kGemvWarps + w) * sg.k_tiles + kt) * pair, pair);
+          tma_prefetch_l2(sg.w + ((size_t)(L.lgrp * kGemvWarps + w) * sg.k_tiles + L.kt) * pair, pair);
       };
       SeqIt wi, xi, pi;
       seq_begin(P, c, G, wi);
@@ -869,7 +890,8 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
           const unsigned long long now = global_timer_ns();
           if (t_idle == 0) t_idle = now;
           else if (now - t_idle > kMbarTimeoutNs) {
-            atomicOr(P.err, DEV_ERR_MBAR_TIMEOUT);
+            const int dep = P.ops[xi.op].dep;
+            wait_gave_up(P.err, WAIT_PRODUCER_IDLE, xi.op, xpos | (wpos << 16), dep >= 0 ? ld_acquire(P.done + dep) : -1);
             break;
           }
         }
@@ -886,50 +908,64 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
   float* scr = tail + warp * (kScratch / 4);
   float acc[2][NT][4];
   bool ok = true;
-  int pos = 0;
+  int pos = 0, acq_op = -1;
   SeqIt it;
   seq_begin(P, c, G, it);
   while (it.valid) {
     const int op = it.op;
     const QmvParams& q = P.ops[op].q;
-    const int unitsA = q.seg[0].groups * q.S;
-    const int seg = it.unit < unitsA ? 0 : 1;
-    const int u_in = seg ? it.unit - unitsA : it.unit;
-    const int grp = u_in / q.S, split = u_in - grp * q.S;
-    const int fmt = q.seg[seg].fmt;
-    const int cnt = it.cnt;
+    const int own = c + it.k * G;
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
-    for (int local = 0; local < cnt; ++local, ++pos) {
+    for (int s = it.s; s < it.s_end; ++s, ++pos) {
+      const StageLoc L = locate(q, s);
+      const int kts = q.seg[L.seg].k_tiles;
       const int st = pos % D;
-      if (ok) ok = mbar_wait_bounded(&full[st], (uint32_t)((pos / D) & 1), P.err);
+      if (ok) {
+        ok = mbar_wait_bounded(&full[st], (uint32_t)((pos / D) & 1), nullptr);
+        if (!ok) wait_gave_up(P.err, WAIT_CONSUMER_FULL, op, s, pos);
+      }
       if (ok) {
         const uint8_t* stage = ring + (size_t)st * FG::STAGE;
-        process_any<SET, NT>(fmt, stage + warp * FG::PAIRMAX, stage + kGemvWarps * FG::PAIRMAX, scr, lane, acc);
+        process_any<SET, NT>(q.seg[L.seg].fmt, stage + warp * FG::PAIRMAX, stage + kGemvWarps * FG::PAIRMAX, scr,
+                             lane, acc);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
-    }
-    // The epilogue reads activations / norms of earlier ops: acquire them.
-    if (threadIdx.x == 0 && P.ops[op].dep >= 0) {
-      const int dep = P.ops[op].dep;
-      const QmvParams& d = P.ops[dep].q;
-      const unsigned long long t0 = global_timer_ns();
-      while (ld_acquire(P.done + dep) < d.seg[0].groups + d.seg[1].groups) {
-        if (global_timer_ns() - t0 > kMbarTimeoutNs) {
-          atomicOr(P.err, DEV_ERR_MBAR_TIMEOUT);
-          break;
+      if (L.kt == kts - 1 || s == it.s_end - 1) {  // end of a piece
+        // The epilogue reads activations / norms of earlier ops: acquire them
+        // (once per op).
+        if (threadIdx.x == 0 && op > acq_op) {
+          acq_op = op;
+          const int dep = P.ops[op].dep;
+          if (dep >= 0) {
+            const QmvParams& d = P.ops[dep].q;
+            const unsigned long long t0 = global_timer_ns();
+            int seen;
+            while ((seen = ld_acquire(P.done + dep)) < d.seg[0].groups + d.seg[1].groups) {
+              if (global_timer_ns() - t0 > kMbarTimeoutNs) {
+                wait_gave_up(P.err, WAIT_CONSUMER_DEP, op, s, seen);
+                break;
+              }
+            }
+          }
         }
+        const int i0 = chunk_of(q, L.gstart), i1 = chunk_of(q, L.gstart + kts - 1);
+        reduce_and_epilogue<NT>(q, L.grp, own, i0, i1, acc, tail, P.done + op);
+        consumer_sync();
+#pragma unroll
+        for (int rt = 0; rt < 2; ++rt)
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
       }
     }
-    consumer_sync();
-    reduce_and_epilogue<NT>(q, (seg ? q.seg[0].groups : 0) + grp, split, acc, tail, P.done + op);
-    consumer_sync();
-    it.local = cnt - 1;
+    it.s = it.s_end - 1;
     seq_next(P, c, G, it);
   }
 }

@@ -207,8 +207,9 @@ int spec_qmatmul_time(spec_qweight* w, int M, int iters, int flush_l2, float* av
  *     re-entering the allocator deadlocks.
  * Limits and rules:
  *   - a call needs about 2.4*K*m8 bytes of operand (m8 = M rounded up to
- *     8, 16, 32 or 64) plus, when the weight's K is split S ways across
- *     CTAs, S*N*4*m8 bytes of partials; a shape needing more than
+ *     8, 16, 32 or 64) plus, when the weight's work is cut into C > 1
+ *     chunks (C <= resident CTAs, 444 on a B200 at M <= 8),
+ *     (C + N/128)*512*m8 bytes of partials; a shape needing more than
  *     SPEC_NOALLOC_SCRATCH_BYTES returns SPEC_ERR_INVALID (message via
  *     spec_last_error(NULL)) and launches nothing;
  *   - the first call on a device looks the array up (cudaGetSymbolAddress)
