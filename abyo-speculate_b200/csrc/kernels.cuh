@@ -215,8 +215,10 @@ cudaError_t launch_final_hidden(const float* h, const float* ss, int groups, flo
                                 const float* norm, int M, int H, float* out, cudaStream_t s);
 
 // ---- acceptance helpers ---------------------------------------------------
+// Per-row argmax (first-max tie break).  slots / counters: kMaxRows each,
+// zero before the first call; every call leaves them zero again.
 cudaError_t launch_row_argmax(const float* logits, int rows, int V, int* out_idx, float* out_val,
-                              cudaStream_t s);
+                              unsigned long long* slots, int* counters, cudaStream_t s);
 
 // ---- synthetic weight generation (seeded N(0, sigma) then quantized) -------
 cudaError_t launch_synth_quant(uint8_t* raw, int fmt, int rows, int K, uint64_t seed, float sigma,

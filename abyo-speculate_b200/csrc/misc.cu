@@ -155,51 +155,53 @@ __global__ void final_hidden_kernel(const float* h, const float* ss, int groups,
 }
 
 // First-max argmax (strict '>' scan order), one CTA per row.
-__global__ void row_argmax_kernel(const float* logits, int V, int* out_idx, float* out_val) {
-  const int row = blockIdx.x;
+// Row argmax with the first-max tie break (a sequential scan with strict >):
+// every (row, chunk) CTA folds its slice into one 64-bit key (order-preserving
+// float bits, then the complemented index, so a larger key is a larger value
+// or, on a tie, a smaller index) and merges it with atomicMax; the CTA that
+// arrives last for a row decodes the key and clears the slot and counter for
+// the next call.  The max of a set of keys does not depend on arrival order.
+// NaN entries are skipped; a row of only NaN yields index 0.
+SPEC_DEV unsigned long long argmax_key(float v, int i) {
+  unsigned u = __float_as_uint(v);
+  u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  return ((unsigned long long)u << 32) | (unsigned)(~i);
+}
+SPEC_DEV float argmax_key_value(unsigned long long k) {
+  unsigned u = (unsigned)(k >> 32);
+  u = (u & 0x80000000u) ? (u & 0x7fffffffu) : ~u;
+  return __uint_as_float(u);
+}
+
+__global__ void __launch_bounds__(256) row_argmax_kernel(const float* logits, int V, int per_cta,
+                                                         unsigned long long* slots, int* counters, int* out_idx,
+                                                         float* out_val) {
+  const int row = blockIdx.y;
   const float* x = logits + (size_t)row * V;
-  float bv = -INFINITY;
-  int bi = V;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = x[i];
-    if (v > bv) {
-      bv = v;
-      bi = i;
-    }
+  const int start = blockIdx.x * per_cta, end = min(V, start + per_cta);
+  unsigned long long best = 0ull;
+  for (int i = start + threadIdx.x; i < end; i += blockDim.x) {
+    const float v = __ldg(x + i);
+    if (v == v) best = max(best, argmax_key(v, i));
   }
-  __shared__ float sv[32];
-  __shared__ int si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) best = max(best, __shfl_xor_sync(0xffffffffu, best, o));
+  __shared__ unsigned long long sb[8];
+  __shared__ bool s_last;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) {
-    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ov > bv || (ov == bv && oi < bi)) {
-      bv = ov;
-      bi = oi;
-    }
-  }
-  if (lane == 0) {
-    sv[warp] = bv;
-    si[warp] = bi;
-  }
+  if (lane == 0) sb[warp] = best;
   __syncthreads();
-  if (warp == 0) {
-    const int nw = blockDim.x / 32;
-    bv = lane < nw ? sv[lane] : -INFINITY;
-    bi = lane < nw ? si[lane] : V;
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ov > bv || (ov == bv && oi < bi)) {
-        bv = ov;
-        bi = oi;
-      }
-    }
-    if (lane == 0) {
-      out_idx[row] = bi >= V ? 0 : bi;
-      if (out_val) out_val[row] = bv;
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) best = max(best, sb[w]);
+    atomicMax(slots + row, best);
+    __threadfence();
+    s_last = atomicAdd(counters + row, 1) == (int)gridDim.x - 1;
+    if (s_last) {
+      __threadfence();
+      const unsigned long long k = atomicExch(slots + row, 0ull);
+      counters[row] = 0;
+      out_idx[row] = k ? (int)(~(unsigned)(k & 0xffffffffull)) : 0;
+      if (out_val) out_val[row] = k ? argmax_key_value(k) : -INFINITY;
     }
   }
 }
@@ -406,8 +408,12 @@ cudaError_t launch_final_hidden(const float* h, const float* ss, int groups, flo
   return cudaGetLastError();
 }
 
-cudaError_t launch_row_argmax(const float* logits, int rows, int V, int* out_idx, float* out_val, cudaStream_t s) {
-  row_argmax_kernel<<<rows, 1024, 0, s>>>(logits, V, out_idx, out_val);
+cudaError_t launch_row_argmax(const float* logits, int rows, int V, int* out_idx, float* out_val,
+                              unsigned long long* slots, int* counters, cudaStream_t s) {
+  if (rows < 1 || rows > kMaxRows || V < 1) return cudaErrorInvalidValue;
+  const int per_cta = 2048;
+  row_argmax_kernel<<<dim3((V + per_cta - 1) / per_cta, rows), 256, 0, s>>>(logits, V, per_cta, slots, counters,
+                                                                           out_idx, out_val);
   return cudaGetLastError();
 }
 

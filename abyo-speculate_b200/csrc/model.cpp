@@ -140,6 +140,8 @@ struct spec_model {
   int* idx_host = nullptr;
   void* kv_tmp = nullptr;
   int* argmax_dev = nullptr;
+  unsigned long long* argmax_slots = nullptr;  // row argmax scratch (self-clearing)
+  int* argmax_counters = nullptr;
   int* argmax_host = nullptr;
   float* op_in = nullptr;  // f32 staging for apply_lm_head
 
@@ -393,6 +395,8 @@ int alloc_runtime(spec_model* m) {
   ALLOC(m->idx_dev, 4 * (size_t)(m->t_max + 64) * 2);
   ALLOC(m->kv_tmp, (size_t)c.n_layers * 2 * c.n_kv * kMaxRows * hd * 2);
   ALLOC(m->argmax_dev, kMaxRows * 4);
+  ALLOC(m->argmax_slots, kMaxRows * 8);
+  ALLOC(m->argmax_counters, kMaxRows * 4);
   ALLOC(m->op_in, (size_t)kMaxRows * H * 4);
   HALLOC(m->step_host, sizeof(StepDev));
   HALLOC(m->logits_host, (size_t)kMaxRows * V * 4);
@@ -1677,7 +1681,8 @@ int spec_verify_greedy(spec_model* m, const uint32_t* drafts, int k, int* n_acce
   fill_step_causal(m, combined.data(), k + 1, target);
   int rc = run_forward(m, k + 1, F_LOGITS);
   if (rc == SPEC_OK) {
-    cudaError_t e = launch_row_argmax(m->logits, k + 1, m->cfg.vocab, m->argmax_dev, nullptr, m->stream);
+    cudaError_t e = launch_row_argmax(m->logits, k + 1, m->cfg.vocab, m->argmax_dev, nullptr,
+                                      m->argmax_slots, m->argmax_counters, m->stream);
     if (e == cudaSuccess)
       e = cudaMemcpyAsync(m->argmax_host, m->argmax_dev, (size_t)(k + 1) * 4, cudaMemcpyDeviceToHost, m->stream);
     if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "argmax"));
@@ -1712,7 +1717,8 @@ int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t
   const int prefix = pre - 1;
   rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS);
   if (rc == SPEC_OK) {
-    cudaError_t e = launch_row_argmax(m->logits, n, m->cfg.vocab, m->argmax_dev, nullptr, m->stream);
+    cudaError_t e = launch_row_argmax(m->logits, n, m->cfg.vocab, m->argmax_dev, nullptr,
+                                      m->argmax_slots, m->argmax_counters, m->stream);
     if (e == cudaSuccess)
       e = cudaMemcpyAsync(m->argmax_host, m->argmax_dev, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream);
     if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "argmax"));
