@@ -111,6 +111,9 @@ SIGNATURES = [
     ("spec_embed_tokens", ctypes.c_int, [ctypes.c_void_p, c_u32_p, ctypes.c_int, c_f32_p]),
     ("spec_last_hidden_states_multi", ctypes.c_int, [ctypes.c_void_p, c_i32_p, ctypes.c_int, c_f32_p, c_f32_p]),
     ("spec_verify_greedy", ctypes.c_int, [ctypes.c_void_p, c_u32_p, ctypes.c_int, c_int_p, c_u32_p, c_i32_p]),
+    ("spec_verify_rejection", ctypes.c_int,
+     [ctypes.c_void_p, c_u32_p, ctypes.c_int, c_f32_p, ctypes.c_float, c_f32_p, ctypes.c_int, ctypes.c_int, c_u32_p,
+      c_int_p, c_int_p]),
     ("spec_verify_tree_greedy", ctypes.c_int,
      [ctypes.c_void_p, c_u32_p, c_i32_p, ctypes.c_int, c_i32_p, c_int_p, c_u32_p]),
     ("spec_last_forward_ms", ctypes.c_float, [ctypes.c_void_p]),

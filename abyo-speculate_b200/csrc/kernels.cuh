@@ -89,6 +89,13 @@ struct QmvParams {
   const float* xsum32 = nullptr;
   // rinv of an RMSNorm folded into this GEMV's input (null = none)
   const float* ss_in = nullptr;
+  // The input operand was emitted pre-scaled by the rinv of this table (the
+  // previous residual's); the epilogue undoes it (null = not pre-scaled).
+  const float* ss_pre = nullptr;
+  // EPI_RESID: scale the emitted next operand by the rinv of this table (the
+  // residual before this op's update), keeping f16 operands O(1) however large
+  // the residual grows (null = no scaling).
+  const float* ss_scale = nullptr;
   int ss_groups = 0;
   float ss_inv_dim = 0.f;
   float eps = 0.f;
@@ -215,6 +222,19 @@ cudaError_t launch_final_hidden(const float* h, const float* ss, int groups, flo
                                 const float* norm, int M, int H, float* out, cudaStream_t s);
 
 // ---- acceptance helpers ---------------------------------------------------
+// ---- rejection-sampling acceptance (accept.cu) ----------------------------
+enum RejError : int { REJ_OK = 0, REJ_ERR_SOFTMAX = 1, REJ_ERR_ADJUSTED = 2, REJ_ERR_UNIFORMS = 3, REJ_ERR_DISTRIBUTION = 4 };
+struct RejStep {
+  int k = 0, n_uniforms = 0, budget = 1, pad = 0;
+  int drafts[kMaxRows];
+  float uniforms[kMaxRows + 1];
+};
+// rows: [k+1][V] target logits, overwritten with the target probabilities;
+// q: [k][V] draft probabilities; r: [V] scratch; out: [4 + kMaxRows] ints,
+// zero at launch: n_commits, uniforms used, status (RejError), -, commits.
+cudaError_t launch_rejection(float* rows, const float* q, float* r, const RejStep* st, int k, int V,
+                             float temperature, int* out, cudaStream_t s);
+
 // Per-row argmax (first-max tie break).  slots / counters: kMaxRows each,
 // zero before the first call; every call leaves them zero again.
 cudaError_t launch_row_argmax(const float* logits, int rows, int V, int* out_idx, float* out_val,

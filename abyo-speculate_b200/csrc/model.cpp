@@ -11,6 +11,8 @@
 #include "model.h"
 
 #include <math.h>
+
+#include <cmath>
 #include <stdio.h>
 #include <stdlib.h>
 #include <string.h>
@@ -141,6 +143,13 @@ struct spec_model {
   void* kv_tmp = nullptr;
   int* argmax_dev = nullptr;
   unsigned long long* argmax_slots = nullptr;  // row argmax scratch (self-clearing)
+  float* rej_q = nullptr;                      // [kMaxRows-1][V] draft probabilities
+  float* rej_q_host = nullptr;                 // pinned staging for rej_q
+  float* rej_r = nullptr;                      // [V] adjusted distribution
+  RejStep* rej_step_dev = nullptr;
+  RejStep* rej_step_host = nullptr;            // pinned
+  int* rej_out_dev = nullptr;                  // [4 + kMaxRows]
+  int* rej_out_host = nullptr;                 // pinned
   int* argmax_counters = nullptr;
   int* argmax_host = nullptr;
   float* op_in = nullptr;  // f32 staging for apply_lm_head
@@ -351,7 +360,10 @@ int alloc_runtime(spec_model* m) {
   ALLOC(m->vcache, m->kv_layer_elems * c.n_layers * kv_elem_bytes(c));
   ALLOC(m->h, (size_t)kMaxRows * H * 4);
   const int groups_h = H / kGroupRows;
-  ALLOC(m->ss, (size_t)groups_h * kSsStride * 4);
+  // Two sum-of-squares tables: ss0 = residual after embed / after each down
+  // projection, ss1 = after each o-projection (each residual epilogue scales
+  // its emitted operand by the other table's rinv).
+  ALLOC(m->ss, (size_t)2 * groups_h * kSsStride * 4);
   const int Kq = c.n_heads * hd;
   auto frag_bytes = [](int K) { return (size_t)K * kMaxRows * 2; };
   ALLOC(m->xa, frag_bytes(H));
@@ -396,6 +408,13 @@ int alloc_runtime(spec_model* m) {
   ALLOC(m->kv_tmp, (size_t)c.n_layers * 2 * c.n_kv * kMaxRows * hd * 2);
   ALLOC(m->argmax_dev, kMaxRows * 4);
   ALLOC(m->argmax_slots, kMaxRows * 8);
+  ALLOC(m->rej_q, (size_t)(kMaxRows - 1) * V * 4);
+  HALLOC(m->rej_q_host, (size_t)(kMaxRows - 1) * V * 4);
+  ALLOC(m->rej_r, (size_t)V * 4);
+  ALLOC(m->rej_step_dev, sizeof(RejStep));
+  HALLOC(m->rej_step_host, sizeof(RejStep));
+  ALLOC(m->rej_out_dev, (4 + kMaxRows) * 4);
+  HALLOC(m->rej_out_host, (4 + kMaxRows) * 4);
   ALLOC(m->argmax_counters, kMaxRows * 4);
   ALLOC(m->op_in, (size_t)kMaxRows * H * 4);
   HALLOC(m->step_host, sizeof(StepDev));
@@ -504,6 +523,10 @@ cudaError_t prof_mark(ProfRec* pr, cudaStream_t s, int kind, int64_t bytes) {
 enum : int { K_FWD = 8 };
 
 // GEMV op descriptors of one layer (QKV; O; gate/up; down) for M rows.
+// The two sum-of-squares tables (see alloc_runtime).
+float* ss0(spec_model* m) { return m->ss; }
+float* ss1(spec_model* m) { return m->ss + (size_t)(m->cfg.hidden / kGroupRows) * kSsStride; }
+
 FwdOp op_qkv(spec_model* m, int l, int M) {
   const ModelCfg& c = m->cfg;
   const Layer& L = m->layers[l];
@@ -513,7 +536,8 @@ FwdOp op_qkv(spec_model* m, int l, int M) {
   p.xfrag = m->xa;
   p.xsum16 = m->xa16;
   p.xsum32 = m->xa32;
-  p.ss_in = m->ss;
+  p.ss_in = ss0(m);
+  p.ss_pre = l > 0 ? ss1(m) : nullptr;  // layer 0's operand comes from embed, unscaled
   p.ss_groups = c.hidden / kGroupRows;
   p.ss_inv_dim = 1.f / (float)c.hidden;
   p.eps = c.eps;
@@ -534,6 +558,7 @@ FwdOp op_qkv(spec_model* m, int l, int M) {
   return o;
 }
 FwdOp op_o(spec_model* m, int l, int M) {
+  const ModelCfg& c = m->cfg;
   FwdOp o;
   QmvParams& p = o.q;
   p = base_params(m, m->layers[l].o, M);
@@ -542,7 +567,11 @@ FwdOp op_o(spec_model* m, int l, int M) {
   p.xsum32 = m->xb32;
   p.epi = EPI_RESID;
   p.h = m->h;
-  p.ss_out = m->ss;
+  p.ss_out = ss1(m);
+  p.ss_scale = ss0(m);  // residual before this update: embed's or the previous down's
+  p.ss_groups = c.hidden / kGroupRows;
+  p.ss_inv_dim = 1.f / (float)c.hidden;
+  p.eps = c.eps;
   p.next_norm = m->layers[l].ffn_norm;
   p.next_frag = m->xa;
   p.next_xsum16 = m->xa16;
@@ -557,7 +586,8 @@ FwdOp op_gu(spec_model* m, int l, int M) {
   p.xfrag = m->xa;
   p.xsum16 = m->xa16;
   p.xsum32 = m->xa32;
-  p.ss_in = m->ss;
+  p.ss_in = ss1(m);
+  p.ss_pre = ss0(m);
   p.ss_groups = c.hidden / kGroupRows;
   p.ss_inv_dim = 1.f / (float)c.hidden;
   p.eps = c.eps;
@@ -577,7 +607,11 @@ FwdOp op_down(spec_model* m, int l, int M) {
   p.xsum32 = m->xc32;
   p.epi = EPI_RESID;
   p.h = m->h;
-  p.ss_out = m->ss;
+  p.ss_out = ss0(m);
+  p.ss_scale = ss1(m);  // residual before this update: the o-projection's
+  p.ss_groups = c.hidden / kGroupRows;
+  p.ss_inv_dim = 1.f / (float)c.hidden;
+  p.eps = c.eps;
   p.next_norm = (l + 1 < c.n_layers) ? m->layers[l + 1].attn_norm : m->out_norm;
   p.next_frag = m->xa;
   p.next_xsum16 = m->xa16;
@@ -592,7 +626,8 @@ FwdOp op_lm(spec_model* m, int M, float* out) {
   p.xfrag = m->xa;
   p.xsum16 = m->xa16;
   p.xsum32 = m->xa32;
-  p.ss_in = m->ss;
+  p.ss_in = ss0(m);
+  p.ss_pre = ss1(m);
   p.ss_groups = c.hidden / kGroupRows;
   p.ss_inv_dim = 1.f / (float)c.hidden;
   p.eps = c.eps;
@@ -1700,6 +1735,74 @@ int spec_verify_greedy(spec_model* m, const uint32_t* drafts, int k, int* n_acce
   *n_accepted = acc;
   *next_token = (uint32_t)m->argmax_host[acc];
   if (argmax_out) memcpy(argmax_out, m->argmax_host, (size_t)(k + 1) * 4);
+  return SPEC_OK;
+}
+
+int spec_verify_rejection(spec_model* m, const uint32_t* drafts, int k, const float* draft_probs,
+                          float temperature, const float* uniforms, int n_uniforms, int budget, uint32_t* commits,
+                          int* n_commits, int* n_uniforms_used) {
+  if (!m || !commits || !n_commits || k < 0 || (k > 0 && (!drafts || !draft_probs)) || n_uniforms < 0 ||
+      (n_uniforms > 0 && !uniforms))
+    return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (!std::isfinite(temperature) || temperature < 0.f) return m->fail(SPEC_ERR_INVALID, "invalid temperature");
+  if (budget < 1) return m->fail(SPEC_ERR_INVALID, "token budget must be >= 1");
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "batched_logits with empty history");
+  if (k + 1 > kMaxRows) return m->fail(SPEC_ERR_UNSUPPORTED, "k+1 exceeds SPEC_MAX_ROWS");
+  const int V = m->cfg.vocab;
+  for (int i = 0; i < k; ++i)
+    if (drafts[i] >= (uint32_t)V) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  const int saved = m->cache_len;
+  const int target = (int)m->history.size() - 1;
+  if (target > m->cache_len) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
+  if (target + k + 1 > m->t_max) return m->fail(SPEC_ERR_INVALID, "KV capacity exceeded");
+  std::vector<uint32_t> combined(k + 1);
+  combined[0] = m->history.back();
+  if (k) memcpy(combined.data() + 1, drafts, (size_t)k * 4);
+  // Stage the round's inputs before the forward (every call ends with its
+  // stream drained, so the pinned slots are free) so their upload overlaps it.
+  RejStep* st = m->rej_step_host;
+  st->k = k;
+  st->budget = budget;
+  st->n_uniforms = std::min(n_uniforms, kMaxRows + 1);
+  for (int i = 0; i < k; ++i) st->drafts[i] = (int)drafts[i];
+  for (int i = 0; i < st->n_uniforms; ++i) st->uniforms[i] = uniforms[i];
+  if (k) memcpy(m->rej_q_host, draft_probs, (size_t)k * V * 4);
+  cudaError_t e0 = cudaSuccess;
+  if (k) e0 = cudaMemcpyAsync(m->rej_q, m->rej_q_host, (size_t)k * V * 4, cudaMemcpyHostToDevice, m->stream);
+  if (e0 == cudaSuccess)
+    e0 = cudaMemcpyAsync(m->rej_step_dev, st, sizeof(RejStep), cudaMemcpyHostToDevice, m->stream);
+  if (e0 != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e0, "rejection inputs"));
+  fill_step_causal(m, combined.data(), k + 1, target);
+  int rc = run_forward(m, k + 1, F_LOGITS);
+  if (rc == SPEC_OK) {
+    cudaError_t e = cudaSuccess;
+    if (e == cudaSuccess) e = cudaMemsetAsync(m->rej_out_dev, 0, (4 + kMaxRows) * 4, m->stream);
+    if (e == cudaSuccess)
+      e = launch_rejection(m->logits, m->rej_q, m->rej_r, m->rej_step_dev, k, V, temperature, m->rej_out_dev,
+                           m->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(m->rej_out_host, m->rej_out_dev, (4 + kMaxRows) * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "rejection sampling"));
+  }
+  if (rc == SPEC_OK) rc = finish(m);
+  if (rc == SPEC_OK && m->rej_out_host[2] != REJ_OK) {
+    static const char* msgs[] = {"", "softmax produced non-positive sum", "adjusted distribution has non-positive mass",
+                                 "not enough uniforms for the round", "invalid distribution"};
+    const int st = m->rej_out_host[2];
+    rc = m->fail(SPEC_ERR_INVALID, st > 0 && st < 5 ? msgs[st] : "sampling error");
+  }
+  if (rc != SPEC_OK) {
+    m->cache_len = saved;
+    return rc;
+  }
+  m->cache_len = target + k + 1;
+  m->last_valid = true;
+  m->history.insert(m->history.end(), drafts, drafts + k);
+  const int n = m->rej_out_host[0];
+  for (int i = 0; i < n; ++i) commits[i] = (uint32_t)m->rej_out_host[4 + i];
+  *n_commits = n;
+  if (n_uniforms_used) *n_uniforms_used = m->rej_out_host[1];
   return SPEC_OK;
 }
 

@@ -487,21 +487,31 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
         const int col = nt * 8 + 2 * t + (i & 1);
         if (col < M) ys[col * kGroupRows + row] = acc[rt][nt][i];
       }
-  if (p.ss_in) {
+  if (p.ss_in || p.ss_scale) {
     // Per-group sums of squares of the residual rows -> RMSNorm scale.  All
-    // 128 threads fetch the [ss_groups][M] table into shared memory at once;
+    // 128 threads fetch the [ss_groups][M] tables into shared memory at once;
     // thread m then adds its column in group order.
     float* sst = ys + M * kGroupRows;
     const int n_ss = p.ss_groups * M;
+    const float* t0 = p.ss_in ? p.ss_in : p.ss_scale;
+    const float* t1 = p.ss_in ? p.ss_pre : nullptr;
     for (int i = tid; i < n_ss; i += kGemvWarps * 32) {
       const int q = i / M, m = i - q * M;
-      sst[i] = __ldcg(p.ss_in + q * kSsStride + m);
+      sst[i] = __ldcg(t0 + q * kSsStride + m);
+      if (t1) sst[n_ss + i] = __ldcg(t1 + q * kSsStride + m);
     }
     consumer_sync();
     if (tid < M) {
       float ms = 0.f;
       for (int q = 0; q < p.ss_groups; ++q) ms += sst[q * M + tid];
-      s_rinv[tid] = 1.f / sqrtf(ms * p.ss_inv_dim + p.eps);
+      float r = 1.f / sqrtf(ms * p.ss_inv_dim + p.eps);
+      if (t1) {  // undo the pre-scale the operand was emitted with: x (1/r_pre) r
+        float mp = 0.f;
+        for (int q = 0; q < p.ss_groups; ++q) mp += sst[n_ss + q * M + tid];
+        r *= sqrtf(mp * p.ss_inv_dim + p.eps);
+      }
+      // EPI_RESID (ss_scale): s_rinv is the pre-scale of the emitted operand.
+      s_rinv[tid] = r;
     }
   } else if (tid < M) {
     s_rinv[tid] = 1.f;
@@ -579,7 +589,9 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       const float hv = ys[m * kGroupRows + tid];
       const float sq = warp_sum(hv * hv);
       if (lane == 0) s_red[warp][m] = sq;
-      if (p.next_frag) emit_operand_warp(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m, n, hv * nw, p.act_bf16, lane);
+      // s_rinv[m] = rinv of the residual before this update (or 1).
+      if (p.next_frag)
+        emit_operand_warp(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m, n, hv * nw * s_rinv[m], p.act_bf16, lane);
     }
     consumer_sync();
     if (tid < M) {
@@ -635,7 +647,7 @@ struct FGeo {
   static constexpr int D = D0 < 2 ? 2 : (D0 > 6 ? 6 : D0);
   static constexpr int RING = D * STAGE;
   static constexpr int SCR = kGemvWarps * kScratch;
-  static constexpr int YS = (8 * NT * kGroupRows + kMaxSsGroups * 8 * NT) * 4;
+  static constexpr int YS = (8 * NT * kGroupRows + 2 * kMaxSsGroups * 8 * NT) * 4;
   static constexpr int TAIL = SCR > YS ? SCR : YS;
   static constexpr int SMEM = RING + TAIL;
 };

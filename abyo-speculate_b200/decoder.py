@@ -200,6 +200,28 @@ class B200Decoder:
                                                  ctypes.byref(nxt), _ptr(am, ctypes.c_int32)))
         return n_acc.value, nxt.value, am
 
+    def verify_rejection(self, drafts: Sequence[int], draft_probs: np.ndarray, temperature: float,
+                         uniforms: Sequence[float], budget: Optional[int] = None) -> Tuple[List[int], int]:
+        """Batched verify + the rejection-sampling round of vanilla.rs:172-210
+        on the device.  draft_probs: k x V float32 draft distributions;
+        uniforms: the round's gen::<f32>() draws in the reference order.
+
+        Returns (committed tokens, uniforms used)."""
+        a = _u32(drafts)
+        q = np.ascontiguousarray(draft_probs, dtype=np.float32).reshape(a.size, -1) if a.size else \
+            np.zeros((0, self.vocab_size()), dtype=np.float32)
+        u = np.ascontiguousarray(uniforms, dtype=np.float32)
+        commits = np.empty(a.size + 1, dtype=np.uint32)
+        n = ctypes.c_int()
+        used = ctypes.c_int()
+        b = a.size + 1 if budget is None else int(budget)
+        self._check(self._lib.spec_verify_rejection(self._h, _ptr(a, ctypes.c_uint32), a.size,
+                                                    _ptr(q, ctypes.c_float), float(temperature),
+                                                    _ptr(u, ctypes.c_float), u.size, b,
+                                                    _ptr(commits, ctypes.c_uint32), ctypes.byref(n),
+                                                    ctypes.byref(used)))
+        return [int(x) for x in commits[: n.value]], used.value
+
     def verify_tree_greedy(self, tree: DraftTree) -> Tuple[List[int], int]:
         """Tree verify (KV kept) + device argmax + eagle.rs:618-661 path walk."""
         t, p = self._tree_arrays(tree)

@@ -247,17 +247,17 @@ def layer_tensor_shapes(spec: ModelSpec) -> List[Tuple[str, Tuple[int, int]]]:
     ]
 
 
-def synth_tensors(spec: ModelSpec, seed: int) -> Dict[str, Tuple[np.ndarray, int]]:
+def synth_tensors(spec: ModelSpec, seed: int, sigma: float = 0.02) -> Dict[str, Tuple[np.ndarray, int]]:
     """All model tensors as name -> (raw GGUF data, ggml type), seeded.
 
-    Weight matrices are N(0, 0.02) before quantization; norms 1 + N(0, 0.02);
-    Qwen2 q/k/v biases N(0, 0.02) in F32.
+    Weight matrices are N(0, sigma) (default 0.02) before quantization; norms
+    1 + N(0, 0.02); Qwen2 q/k/v biases N(0, 0.02) in F32.
     """
     rng = np.random.default_rng(seed)
     out: Dict[str, Tuple[np.ndarray, int]] = {}
 
     def mat(name: str, shape: Tuple[int, int], layer: Optional[int]) -> None:
-        w = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
+        w = rng.standard_normal(shape, dtype=np.float32) * np.float32(sigma)
         qt = tensor_qtype(spec, name, shape[1], layer)
         out[name] = (quantize(w, qt), qt)
 
@@ -282,7 +282,7 @@ def synth_tensors(spec: ModelSpec, seed: int) -> Dict[str, Tuple[np.ndarray, int
 
 
 def write_gguf(path: str, spec: ModelSpec, seed: int, rope_style: Optional[str] = None,
-               llama3_scaling: bool = False) -> Dict[str, Tuple[np.ndarray, int]]:
+               llama3_scaling: bool = False, sigma: float = 0.02) -> Dict[str, Tuple[np.ndarray, int]]:
     """Write a synthetic GGUF for ``spec`` and return its tensors.
 
     ``rope_style="half"`` marks a Llama whose q/k use rotate-half RoPE (the
@@ -292,7 +292,7 @@ def write_gguf(path: str, spec: ModelSpec, seed: int, rope_style: Optional[str] 
     """
     import gguf
 
-    tensors = synth_tensors(spec, seed)
+    tensors = synth_tensors(spec, seed, sigma)
     arch = spec.arch
     w = gguf.GGUFWriter(path, arch)
     w.add_uint32(f"{arch}.attention.head_count", spec.n_heads)

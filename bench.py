@@ -271,6 +271,29 @@ def run_b200(args, ws, rank, local, dist):
     ms = e0.elapsed_time(e1)
     barrier(dist)
     ms_max = max_over_ranks(dist, ms)
+    # Seeded temperature-1.0 rejection-sampling round on the device
+    # (spec_verify_rejection): same forward, then the vanilla.rs round over
+    # the 5 rows with draft distributions and uniforms from the host.
+    rj_rng = np.random.default_rng(11 + rank)
+    V = CFG["vocab"]
+    rj_q = rj_rng.random((K_DRAFT, V), dtype=np.float32)
+    rj_q /= rj_q.sum(axis=1, keepdims=True, dtype=np.float32)
+    rj_u = rj_rng.random((max(args.steps, 1) + args.warmup, K_DRAFT + 1)).astype(np.float32)
+    for i in range(args.warmup):
+        dec.verify_rejection(drafts_all[i], rj_q, 1.0, rj_u[i])
+        dec.rollback_to(KV_LEN)
+    barrier(dist)
+    torch.cuda.synchronize()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(stream)
+    rj_commits = 0
+    for i in range(args.steps):
+        c, _ = dec.verify_rejection(drafts_all[args.warmup + i], rj_q, 1.0, rj_u[args.warmup + i])
+        rj_commits += len(c)
+        dec.rollback_to(KV_LEN)
+    r1.record(stream)
+    torch.cuda.synchronize()
+    rj_ms = max_over_ranks(dist, r0.elapsed_time(r1))
     # e2e: host drafts in, host logits rows out (spec_batched_logits)
     barrier(dist)
     torch.cuda.synchronize()
@@ -337,6 +360,10 @@ def run_b200(args, ws, rank, local, dist):
         "kernels": per_kind,
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": 1296 + 4 * K_DRAFT,
                 "d2h_bytes_per_step": (K_DRAFT + 1) * CFG["vocab"] * 4 + 4},
+        "rejection_t1": {"value": round(ws * args.steps / (rj_ms / 1e3), 3), "unit": UNIT,
+                         "verify_us": round(rj_ms / args.steps * 1e3, 2),
+                         "mean_commits": round(rj_commits / max(args.steps, 1), 3),
+                         "note": "spec_verify_rejection, temperature 1.0, seeded draft distributions and uniforms"},
         "gpu_launches": launches_per_step * args.steps,
         "clocks": sampler.summary(),
     }

@@ -153,6 +153,28 @@ int spec_verify_greedy(spec_model* m, const uint32_t* drafts, int k, int* n_acce
  * *bonus the argmax of the deepest accepted node. */
 int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
                             int32_t* best_path, int* path_len, uint32_t* bonus);
+/* Rejection-sampling vanilla round (methods/vanilla.rs:172-210 steps 3-4) on
+ * the device: one batched forward of [last]+drafts (same protocol and state
+ * change as spec_batched_logits), then, with the reference's float32
+ * operations in its order (sampling/tokens.rs:14-55 and :99-120,
+ * vanilla.rs:59-106):
+ *   for i < k: p = softmax_t(target row i); accept drafts[i] iff
+ *     q_i[x] <= 0 or u <= min(p[x] / q_i[x], 1) with the next uniform;
+ *     on the first rejection, commit a sample (next uniform) of
+ *     norm(max(p - q_i, 0)) and stop;
+ *   if all k were accepted and fewer than `budget` tokens are committed,
+ *     commit a bonus sample (next uniform) of softmax_t(target row k).
+ * A commit that reaches `budget` (the round's max_new - generated) ends the
+ * round, as the reference's loop does.  draft_probs: k x V f32 (the draft
+ * distributions q_i, host); uniforms: the round's gen::<f32>() draws in the
+ * reference order (at most k + 1 are used).  Writes the committed tokens to
+ * commits (capacity k + 1), their count, and the number of uniforms used.
+ * temperature 0 is the one-hot argmax distribution.  Errors of the
+ * reference's sampling (invalid temperature, non-positive softmax or adjusted
+ * mass, too few uniforms) return SPEC_ERR_INVALID with the state unchanged. */
+int spec_verify_rejection(spec_model* m, const uint32_t* drafts, int k, const float* draft_probs,
+                          float temperature, const float* uniforms, int n_uniforms, int budget, uint32_t* commits,
+                          int* n_commits, int* n_uniforms_used);
 
 /* ---- diagnostics -------------------------------------------------------- */
 /* Device time (ms, CUDA events) of the most recent forward. */

@@ -70,8 +70,11 @@ def softmax_with_temperature(logits: np.ndarray, temperature: float) -> np.ndarr
         out[argmax_first_fast(logits)] = 1.0
         return out
     inv_t = np.float32(1.0) / np.float32(temperature)
-    mx = np.float32(np.max(logits))
-    out = np.exp((logits - mx) * inv_t).astype(np.float32)
+    finite = logits[~np.isnan(logits)]  # fold(NEG_INFINITY, f32::max) skips NaN
+    mx = np.float32(np.max(finite)) if finite.size else np.float32(-np.inf)
+    # f32::exp is modelled as the correctly rounded exp of the f32 argument
+    # (exp in double, one rounding to f32).
+    out = np.exp(((logits - mx) * inv_t).astype(np.float64)).astype(np.float32)
     s = seq_sum_f32(out)
     if not (s > 0) or not np.isfinite(s):
         raise SamplingError(f"softmax produced non-positive sum: {s}")

@@ -55,7 +55,11 @@ TINY_SPECS = {
                      rope_theta=1e6, eps=1e-6, quant_mix="Q8_0"),
     "llama_bf16": dict(arch="llama", n_layers=2, hidden=256, n_heads=2, n_kv_heads=1, ffn=512, vocab=1024,
                        rope_theta=5e5, eps=1e-5, quant_mix="BF16"),
+    # Large weights: the residual stream passes the f16 range by layer 1.
+    "llama_hot": dict(arch="llama", n_layers=3, hidden=256, n_heads=4, n_kv_heads=2, ffn=512, vocab=1024,
+                      rope_theta=5e5, eps=1e-5, quant_mix="Q4_K_M"),
 }
+TINY_SIGMA = {"llama_hot": 2.0}
 
 
 def make_tiny_gguf(synth_mod, name: str, out_dir: str, seed: int = 1234) -> str:
@@ -65,6 +69,8 @@ def make_tiny_gguf(synth_mod, name: str, out_dir: str, seed: int = 1234) -> str:
         extra = {}
         if spec.quant_mix == "BF16":
             extra = {"rope_style": "half", "llama3_scaling": True}
+        if name in TINY_SIGMA:
+            extra["sigma"] = TINY_SIGMA[name]
         synth_mod.write_gguf(path, spec, seed, **extra)
     return path
 

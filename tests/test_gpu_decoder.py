@@ -219,3 +219,23 @@ def test_error_behaviour(pkg, tiny_gguf):
         pkg.B200Decoder.from_gguf("/nonexistent/model.gguf")
     dec.reset()
     assert dec.history() == [] and dec.kv_len() == 0
+
+
+def test_large_residual_stays_finite(pkg, oracle, tiny_gguf):
+    """Weights N(0, 2): the residual stream passes the f16 range by layer 1.
+
+    The operands of the GEMVs after each residual update are emitted
+    pre-scaled by the previous residual's RMS, so they stay O(1); logits must be
+    finite and match the float64 oracle within 1 % of their range (the f16
+    operand rounding is relative, and these logits are large)."""
+    dec, ref = _pair(pkg, oracle, tiny_gguf("llama_hot"))
+    prompt = _prompt(dec.vocab_size(), 21, 4)
+    dec.observe(prompt)
+    ref.observe(prompt)
+    h = dec.last_hidden_states_multi([0, 1, 2])[1]
+    assert np.abs(np.asarray(h)).max() > 65504.0  # the stress actually happened
+    drafts = _prompt(dec.vocab_size(), 4, 5)
+    a = dec.batched_logits(drafts)
+    b = ref.batched_logits(drafts)
+    assert np.isfinite(a).all()
+    assert np.abs(a - b).max() <= 1e-2 * np.abs(b).max()
