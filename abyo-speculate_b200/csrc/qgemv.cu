@@ -404,6 +404,19 @@ SPEC_DEV void emit_operand_warp(uint32_t* frag, float* xs16, float* xs32, int nt
 // Barrier among the 128 consumer threads only (the producer warp runs ahead).
 SPEC_DEV void consumer_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
+// Arrival on a split counter: release (this CTA's partial stores, ordered
+// before it by the preceding barrier) and acquire (the other pieces'
+// partials, for the CTA that arrives last).
+SPEC_DEV int atom_add_acq_rel(int* ptr, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(ptr), "r"(v) : "memory");
+  return old;
+}
+// Completion count of an op: release of this CTA's epilogue writes.
+SPEC_DEV void red_add_release(int* ptr, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+
 // Finishes one piece (the part of a 128-row group inside one chunk).  A
 // group that lies in one chunk goes straight to the fused epilogue.  A group
 // cut across chunks i0..i1 leaves one partial per piece in slot (chunk +
@@ -418,7 +431,32 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
   __shared__ float s_rinv[kMaxRows];
   __shared__ float s_red[kGemvWarps][kMaxRows];
   const int M = p.M;
+  const int H = p.n_rows, n0 = group * kGroupRows;
   consumer_sync();  // all warps are done with their scale scratch (aliased by ys)
+
+  // Loads of the epilogue that do not depend on the split reduction are
+  // issued first, so their latency overlaps the partial-sum round trips: the
+  // sum-of-squares tables (into sst) and, for EPI_RESID at M <= 8, this
+  // thread's residual column and norm weight.
+  float* sst = ys + M * kGroupRows;
+  const int n_ss = p.ss_groups * M;
+  const float* ss_t1 = p.ss_in ? p.ss_pre : nullptr;
+  if (p.ss_in || p.ss_scale) {
+    const float* t0 = p.ss_in ? p.ss_in : p.ss_scale;
+    for (int i = tid; i < n_ss; i += kGemvWarps * 32) {
+      const int q = i / M, m = i - q * M;
+      sst[i] = __ldcg(t0 + q * kSsStride + m);
+      if (ss_t1) sst[n_ss + i] = __ldcg(ss_t1 + q * kSsStride + m);
+    }
+  }
+  const bool resid_pre = p.epi == EPI_RESID && M <= 8;
+  float hpre[8];
+  float nwpre = 1.f;
+  if (resid_pre) {
+#pragma unroll
+    for (int m = 0; m < 8; ++m) hpre[m] = m < M ? __ldcg(p.h + (size_t)m * H + n0 + tid) : 0.f;
+    if (p.next_norm) nwpre = __ldg(p.next_norm + n0 + tid);
+  }
 
   if (i0 != i1) {
     const size_t per = (size_t)kGroupRows * 8 * NT;
@@ -429,16 +467,14 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       for (int nt = 0; nt < NT; ++nt)
         __stcg(reinterpret_cast<float4*>(mine + ((size_t)((warp * 2 + rt) * NT + nt) * 32 + lane) * 4),
                make_float4(acc[rt][nt][0], acc[rt][nt][1], acc[rt][nt][2], acc[rt][nt][3]));
-    __threadfence();
     consumer_sync();
     if (tid == 0) {
-      const int prev = atomicAdd(&p.counters[group], 1);
+      const int prev = atom_add_acq_rel(&p.counters[group], 1);
       s_last = (prev == i1 - i0);
       if (s_last) p.counters[group] = 0;
     }
     consumer_sync();
     if (!s_last) return;  // uniform across the CTA
-    __threadfence();
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
@@ -488,24 +524,14 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
         if (col < M) ys[col * kGroupRows + row] = acc[rt][nt][i];
       }
   if (p.ss_in || p.ss_scale) {
-    // Per-group sums of squares of the residual rows -> RMSNorm scale.  All
-    // 128 threads fetch the [ss_groups][M] tables into shared memory at once;
-    // thread m then adds its column in group order.
-    float* sst = ys + M * kGroupRows;
-    const int n_ss = p.ss_groups * M;
-    const float* t0 = p.ss_in ? p.ss_in : p.ss_scale;
-    const float* t1 = p.ss_in ? p.ss_pre : nullptr;
-    for (int i = tid; i < n_ss; i += kGemvWarps * 32) {
-      const int q = i / M, m = i - q * M;
-      sst[i] = __ldcg(t0 + q * kSsStride + m);
-      if (t1) sst[n_ss + i] = __ldcg(t1 + q * kSsStride + m);
-    }
+    // Per-group sums of squares of the residual rows (fetched into sst above)
+    // -> RMSNorm scale: thread m adds its column in group order.
     consumer_sync();
     if (tid < M) {
       float ms = 0.f;
       for (int q = 0; q < p.ss_groups; ++q) ms += sst[q * M + tid];
       float r = 1.f / sqrtf(ms * p.ss_inv_dim + p.eps);
-      if (t1) {  // undo the pre-scale the operand was emitted with: x (1/r_pre) r
+      if (ss_t1) {  // undo the pre-scale the operand was emitted with: x (1/r_pre) r
         float mp = 0.f;
         for (int q = 0; q < p.ss_groups; ++q) mp += sst[n_ss + q * M + tid];
         r *= sqrtf(mp * p.ss_inv_dim + p.eps);
@@ -518,7 +544,6 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
   }
   consumer_sync();
 
-  const int n0 = group * kGroupRows;
   if (p.epi == EPI_STORE) {
     for (int idx = tid; idx < M * kGroupRows; idx += kGemvWarps * 32) {
       const int m = idx / kGroupRows, j = idx % kGroupRows, n = n0 + j;
@@ -566,14 +591,16 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       }
     }
   } else if (p.epi == EPI_RESID) {
-    const int H = p.n_rows;
     const int n = n0 + tid;  // 128 threads, one column each
-    // Issue every row's residual load before using any of them.
+    // Issue every row's residual load before using any of them (prefetched
+    // above at M <= 8).
     for (int m0 = 0; m0 < M; m0 += 8) {
       float hv[8];
 #pragma unroll
-      for (int q = 0; q < 8; ++q)
-        if (m0 + q < M) hv[q] = __ldcg(p.h + (size_t)(m0 + q) * H + n);
+      for (int q = 0; q < 8; ++q) {
+        if (resid_pre) hv[q] = hpre[q];
+        else if (m0 + q < M) hv[q] = __ldcg(p.h + (size_t)(m0 + q) * H + n);
+      }
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
         const int m = m0 + q;
@@ -584,7 +611,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
         }
       }
     }
-    const float nw = p.next_norm ? __ldg(p.next_norm + n) : 1.f;
+    const float nw = resid_pre ? nwpre : (p.next_norm ? __ldg(p.next_norm + n) : 1.f);
     for (int m = 0; m < M; ++m) {
       const float hv = ys[m * kGroupRows + tid];
       const float sq = warp_sum(hv * hv);
@@ -612,10 +639,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
     }
   }
   consumer_sync();  // ys aliases the scale scratch of the next unit
-  if (done && tid == 0) {
-    __threadfence();
-    atomicAdd(done, 1);
-  }
+  if (done && tid == 0) red_add_release(done, 1);
 }
 
 SPEC_DEV void mbar_arrive(uint64_t* bar) {
