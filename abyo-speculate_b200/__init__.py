@@ -8,10 +8,10 @@ mirror of the reference's Decoder / TreeDecoder interface.
 
 from ._lib import (CacheRollbackError, DeviceError, IoError, SamplingError, SpecError,  # noqa: F401
                    UnsupportedMethodError, LIB_PATH, MAX_ROWS, load)
-from .decoder import B200Decoder, QWeight  # noqa: F401
+from .decoder import B200Decoder, QWeight, exchange_tp_handles  # noqa: F401
 from .tree import DraftTree  # noqa: F401
 
 __all__ = [
     "B200Decoder", "QWeight", "DraftTree", "SpecError", "SamplingError", "CacheRollbackError",
-    "UnsupportedMethodError", "IoError", "DeviceError", "LIB_PATH", "MAX_ROWS", "load",
+    "UnsupportedMethodError", "IoError", "DeviceError", "LIB_PATH", "MAX_ROWS", "load", "exchange_tp_handles",
 ]

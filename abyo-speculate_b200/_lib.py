@@ -72,7 +72,7 @@ c_f32_p = ctypes.POINTER(ctypes.c_float)
 
 class LoadOpts(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("max_ctx", ctypes.c_int), ("use_graphs", ctypes.c_int),
-                ("reserved", ctypes.c_int * 5)]
+                ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int), ("reserved", ctypes.c_int * 3)]
 
 
 class ModelDesc(ctypes.Structure):
@@ -128,6 +128,9 @@ SIGNATURES = [
     ("spec_qmatmul", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
     ("spec_qweight_bytes", ctypes.c_int64, [ctypes.c_void_p]),
     ("spec_qmatmul_time", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, c_f32_p]),
+    ("spec_tp_handle", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]),
+    ("spec_tp_connect", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int]),
+    ("spec_tp_size", ctypes.c_int, [ctypes.c_void_p]),
     ("spec_qmatmul_noalloc", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]),
 ]

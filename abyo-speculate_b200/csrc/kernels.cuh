@@ -26,7 +26,7 @@ enum DevError : unsigned {
 // The error word is err[0]; a wait that gives up also records where, once:
 // err[1] = site | op << 8 | cta << 16, err[2] = stage / ring position,
 // err[3] = the counter value it last saw.
-enum WaitSite : unsigned { WAIT_CONSUMER_FULL = 1, WAIT_CONSUMER_DEP = 2, WAIT_PRODUCER_IDLE = 3 };
+enum WaitSite : unsigned { WAIT_CONSUMER_FULL = 1, WAIT_CONSUMER_DEP = 2, WAIT_PRODUCER_IDLE = 3, WAIT_TP_PEERS = 4 };
 
 // GGML type ids (public GGUF specification) of the weight formats handled.
 enum WFmt : int { WF_F32 = 0, WF_F16 = 1, WF_Q8_0 = 8, WF_Q4_K = 12, WF_Q5_K = 13, WF_Q6_K = 14, WF_BF16 = 30 };
@@ -50,6 +50,7 @@ constexpr int kGroupRows = 128;        // rows per CTA (4 warps x 32 rows)
 constexpr int kMaxRows = 64;           // max activation rows (M) per forward
 constexpr int kSsStride = 64;          // stride of per-group sum-of-squares slots
 constexpr int kMaxSsGroups = 64;       // hidden size <= 64 * 128
+constexpr int kTpSlot = kMaxRows * 128;  // floats per (source rank, group) receive slot
 
 // Number of 8-row fragment columns (n-tiles) the kernels use for M rows: the
 // GEMV is instantiated for 1, 2, 4 and 8, and every producer of an operand
@@ -96,6 +97,15 @@ struct QmvParams {
   // residual before this op's update), keeping f16 operands O(1) however large
   // the residual grows (null = no scaling).
   const float* ss_scale = nullptr;
+  // Tensor parallelism (EPI_RESID of the row-parallel o / down projections):
+  // after this rank's split reduction, the group's sum is stored into every
+  // rank's receive slot over NVLink, and the ranks' sums are added in rank
+  // order before the residual update, the same way on every rank.
+  int tp_size = 1, tp_rank = 0;
+  float* const* tp_recv = nullptr;       // [tp_size] device: rank r's receive set
+  int* const* tp_cnt = nullptr;          // [tp_size] device: rank r's arrival counters for this set
+  const float* tp_recv_local = nullptr;  // this rank's receive set [src rank][group][kTpSlot]
+  int* tp_cnt_local = nullptr;           // this rank's counters [group]
   int ss_groups = 0;
   float ss_inv_dim = 0.f;
   float eps = 0.f;

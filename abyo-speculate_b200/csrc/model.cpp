@@ -182,6 +182,14 @@ struct spec_model {
     FwdOp* solo = nullptr;  // the same ops with dep = -1, for one-op launches
   };
   std::map<int, Schedule> schedules;
+  int tp_rank = 0, tp_size = 1;     // tensor-parallel position (1 = whole model on this GPU)
+  // Tensor-parallel receive buffer (exported to the other ranks by CUDA IPC):
+  // two sets (o, down), each [tp_size][groups][kTpSlot] floats + [groups] counters.
+  uint8_t* tp_buf = nullptr;
+  size_t tp_set_bytes = 0, tp_recv_bytes = 0;
+  void** tp_ptrs_dev = nullptr;     // [set][kind: recv, cnt][rank] device pointers
+  std::vector<void*> tp_peer_bases; // opened IPC mappings (closed at free)
+  bool tp_connected = false;
   int l2_ahead = 0;                 // weight stages each CTA prefetches into L2 ahead of its ring (SPEC_B200_L2_AHEAD)
   bool use_pdl = true;              // programmatic dependent launch between forward kernels
   FwdOp* single_op = nullptr;       // device slot for one-op launches
@@ -193,6 +201,7 @@ struct spec_model {
     if (stream) cudaStreamSynchronize(stream);
     for (auto& kv : graphs)
       if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    for (void* p : tp_peer_bases) cudaIpcCloseMemHandle(p);
     for (void* p : dev_allocs) cudaFree(p);
     for (void* p : host_allocs) cudaFreeHost(p);
     if (ev0) cudaEventDestroy(ev0);
@@ -399,6 +408,12 @@ int alloc_runtime(spec_model* m) {
   acc_mat(m->lm);
   ALLOC(m->gemv_part, part * 4);
   ALLOC(m->counters, (size_t)max_groups * 4);
+  if (m->tp_size > 1) {
+    m->tp_recv_bytes = (size_t)m->tp_size * groups_h * kTpSlot * 4;
+    m->tp_set_bytes = m->tp_recv_bytes + (((size_t)groups_h * 4 + 255) / 256) * 256;
+    ALLOC(m->tp_buf, 2 * m->tp_set_bytes);
+    ALLOC(m->tp_ptrs_dev, (size_t)2 * 2 * m->tp_size * sizeof(void*));
+  }
   ALLOC(m->logits, (size_t)kMaxRows * V * 4);
   ALLOC(m->last_row, (size_t)V * 4);
   ALLOC(m->hidden_out, (size_t)kMaxRows * H * 4);
@@ -522,11 +537,23 @@ cudaError_t prof_mark(ProfRec* pr, cudaStream_t s, int kind, int64_t bytes) {
 // multi-op GEMV launch).
 enum : int { K_FWD = 8 };
 
-// GEMV op descriptors of one layer (QKV; O; gate/up; down) for M rows.
+// Points a row-parallel op's epilogue at its tensor-parallel receive set.
+void set_tp(spec_model* m, QmvParams& p, int set) {
+  if (m->tp_size <= 1) return;
+  p.tp_size = m->tp_size;
+  p.tp_rank = m->tp_rank;
+  void** base = m->tp_ptrs_dev + (size_t)set * 2 * m->tp_size;
+  p.tp_recv = reinterpret_cast<float* const*>(base);
+  p.tp_cnt = reinterpret_cast<int* const*>(base + m->tp_size);
+  p.tp_recv_local = reinterpret_cast<const float*>(m->tp_buf + set * m->tp_set_bytes);
+  p.tp_cnt_local = reinterpret_cast<int*>(m->tp_buf + set * m->tp_set_bytes + m->tp_recv_bytes);
+}
+
 // The two sum-of-squares tables (see alloc_runtime).
 float* ss0(spec_model* m) { return m->ss; }
 float* ss1(spec_model* m) { return m->ss + (size_t)(m->cfg.hidden / kGroupRows) * kSsStride; }
 
+// GEMV op descriptors of one layer (QKV; O; gate/up; down) for M rows.
 FwdOp op_qkv(spec_model* m, int l, int M) {
   const ModelCfg& c = m->cfg;
   const Layer& L = m->layers[l];
@@ -576,6 +603,7 @@ FwdOp op_o(spec_model* m, int l, int M) {
   p.next_frag = m->xa;
   p.next_xsum16 = m->xa16;
   p.next_xsum32 = m->xa32;
+  set_tp(m, p, 0);
   return o;
 }
 FwdOp op_gu(spec_model* m, int l, int M) {
@@ -616,6 +644,7 @@ FwdOp op_down(spec_model* m, int l, int M) {
   p.next_frag = m->xa;
   p.next_xsum16 = m->xa16;
   p.next_xsum32 = m->xa32;
+  set_tp(m, p, 1);
   return o;
 }
 FwdOp op_lm(spec_model* m, int M, float* out) {
@@ -838,6 +867,8 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
 // Runs one forward of M rows described by m->step_host.  Graph-replayed per
 // (M, flags) after a first eager run.
 int run_forward(spec_model* m, int M, int flags, const std::vector<int>* collect = nullptr) {
+  if (m->tp_size > 1 && !m->tp_connected)
+    return m->fail(SPEC_ERR_INVALID, "tensor-parallel handle used before spec_tp_connect");
   cudaError_t e = cudaSuccess;
   const int key = M | (flags << 8);
   const bool graphable = m->use_graphs && collect == nullptr;
@@ -995,6 +1026,9 @@ namespace {
 
 int init_device(spec_model* m, const spec_load_opts* opts) {
   m->device = opts ? opts->device : 0;
+  m->tp_size = (opts && opts->tp_size > 1) ? opts->tp_size : 1;
+  m->tp_rank = m->tp_size > 1 ? opts->tp_rank : 0;
+  if (m->tp_rank < 0 || m->tp_rank >= m->tp_size) return m->fail(SPEC_ERR_INVALID, "tp_rank outside [0, tp_size)");
   m->use_graphs = opts ? (opts->use_graphs != 0) : true;
   if (getenv("SPEC_B200_NO_GRAPHS")) m->use_graphs = false;
   if (getenv("SPEC_B200_NO_PDL")) m->use_pdl = false;
@@ -1030,6 +1064,93 @@ int finalize_model(spec_model* m, const spec_load_opts* opts, int ctx_len) {
     if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "init"));
   }
   return rc;
+}
+
+size_t raw_row_bytes(int fmt, int K) { return (size_t)(K / fmt_block_elems(fmt)) * fmt_block_bytes(fmt); }
+
+// Rows [row0, row0 + rows) of a part (a view, no copy).
+Part part_rows(const Part& p, int K, int row0, int rows) {
+  Part q = p;
+  q.src = p.src + (size_t)row0 * raw_row_bytes(p.fmt, K);
+  q.rows = rows;
+  return q;
+}
+
+// Columns [k0, k0 + kn) of every row of a part, gathered into a device buffer
+// (whole GGUF blocks; k0 and kn must be multiples of the block width).
+int part_cols(spec_model* m, std::vector<void*>& temps, const Part& p, int K, int k0, int kn, Part& out) {
+  const int be = fmt_block_elems(p.fmt);
+  if (be == 0 || k0 % be || kn % be) return m->fail(SPEC_ERR_UNSUPPORTED, "tensor-parallel column split inside a block");
+  const size_t full = raw_row_bytes(p.fmt, K), width = raw_row_bytes(p.fmt, kn), off = raw_row_bytes(p.fmt, k0);
+  void* buf = nullptr;
+  cudaError_t e = cudaMalloc(&buf, width * p.rows);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, "shard staging"));
+  temps.push_back(buf);
+  e = cudaMemcpy2DAsync(buf, width, p.src + off, full, width, p.rows,
+                        p.on_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, m->stream);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "shard copy"));
+  out = p;
+  out.src = static_cast<const uint8_t*>(buf);
+  out.on_device = true;
+  return SPEC_OK;
+}
+
+// Checks that the model splits into tp_size tensor-parallel shards: whole q
+// and kv heads per rank, FFN slices of whole 128-row groups, and column
+// splits on tile boundaries.
+int check_tp_shape(spec_model* m, int nq, int nkv, int hd, int F) {
+  const int N = m->tp_size;
+  if (N == 1) return SPEC_OK;
+  if (nq % N || nkv % N || F % N || (F / N) % kGroupRows || ((nq / N) * hd) % 256 || (F / N) % 256 ||
+      ((nkv / N) * hd) % kGroupRows)
+    return m->fail(SPEC_ERR_UNSUPPORTED, "model does not split into tp_size tensor-parallel shards");
+  return SPEC_OK;
+}
+
+// The tensor-parallel shard of one layer for this rank: q/k/v rows of the
+// rank's heads and gate/up rows of its FFN slice (column-parallel), the
+// o-projection's columns of its heads and the down projection's columns of
+// its FFN slice (row-parallel; their outputs are summed across ranks).
+// nq, nkv and F are the whole model's.
+int shard_layer(spec_model* m, std::vector<void*>& temps, int nq, int nkv, int hd, int H, int F, Part& q, Part& k,
+                Part& v, Part& o, Part& g, Part& u, Part& d) {
+  const int N = m->tp_size, r = m->tp_rank;
+  if (N == 1) return SPEC_OK;
+  const int nql = nq / N, nkvl = nkv / N, Fl = F / N;
+  q = part_rows(q, H, r * nql * hd, nql * hd);
+  k = part_rows(k, H, r * nkvl * hd, nkvl * hd);
+  v = part_rows(v, H, r * nkvl * hd, nkvl * hd);
+  g = part_rows(g, H, r * Fl, Fl);
+  u = part_rows(u, H, r * Fl, Fl);
+  Part o2, d2;
+  int rc = part_cols(m, temps, o, nq * hd, r * nql * hd, nql * hd, o2);
+  if (rc == SPEC_OK) rc = part_cols(m, temps, d, F, r * Fl, Fl, d2);
+  if (rc != SPEC_OK) return rc;
+  o = o2;
+  d = d2;
+  return SPEC_OK;
+}
+
+// This rank's slice [q heads | k heads | v heads] of a full q/k/v bias.
+std::vector<float> shard_qkv_bias(const spec_model* m, const std::vector<float>& full, int nq, int nkv, int hd) {
+  const int N = m->tp_size, r = m->tp_rank;
+  if (N == 1) return full;
+  const int nql = nq / N, nkvl = nkv / N;
+  std::vector<float> out;
+  out.insert(out.end(), full.begin() + (size_t)r * nql * hd, full.begin() + (size_t)(r + 1) * nql * hd);
+  const size_t kb = (size_t)nq * hd, vb = kb + (size_t)nkv * hd;
+  out.insert(out.end(), full.begin() + kb + (size_t)r * nkvl * hd, full.begin() + kb + (size_t)(r + 1) * nkvl * hd);
+  out.insert(out.end(), full.begin() + vb + (size_t)r * nkvl * hd, full.begin() + vb + (size_t)(r + 1) * nkvl * hd);
+  return out;
+}
+
+// After the shards are built, the model's head and FFN counts are this
+// rank's (hidden size, vocabulary and head size are whole).
+void set_local_dims(spec_model* m) {
+  ModelCfg& c = m->cfg;
+  c.n_heads /= m->tp_size;
+  c.n_kv /= m->tp_size;
+  c.ffn /= m->tp_size;
 }
 
 int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) {
@@ -1085,6 +1206,7 @@ int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) 
   if (c.hidden % kGroupRows || c.ffn % kGroupRows || (c.head_dim != 64 && c.head_dim != 128) ||
       c.n_heads % c.n_kv || c.hidden / kGroupRows > kMaxSsGroups)
     return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported model shape");
+  if (int rc0 = check_tp_shape(m, c.n_heads, c.n_kv, c.head_dim, c.ffn)) return rc0;
 
   auto part_of = [&](const std::string& name, int K, Part& p) -> bool {
     const GgufTensor* t = f.tensor(name);
@@ -1142,10 +1264,15 @@ int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) 
     if (q.rows != c.n_heads * hd || k.rows != c.n_kv * hd || v.rows != c.n_kv * hd || o.rows != H ||
         g.rows != F || u.rows != F || d.rows != H)
       return m->fail(SPEC_ERR_IO, "layer " + std::to_string(l) + " has inconsistent shapes");
-    int rc = build_mat(m, {q, k, v}, H, false, L.qkv);
-    if (rc == SPEC_OK) rc = build_mat(m, {o}, c.n_heads * hd, false, L.o);
+    std::vector<void*> temps;
+    int rc = shard_layer(m, temps, c.n_heads, c.n_kv, hd, H, F, q, k, v, o, g, u, d);
+    const int Kl_o = c.n_heads / m->tp_size * hd, Fl = F / m->tp_size;
+    if (rc == SPEC_OK) rc = build_mat(m, {q, k, v}, H, false, L.qkv);
+    if (rc == SPEC_OK) rc = build_mat(m, {o}, Kl_o, false, L.o);
     if (rc == SPEC_OK) rc = build_mat(m, {g, u}, H, true, L.gu);
-    if (rc == SPEC_OK) rc = build_mat(m, {d}, F, false, L.down);
+    if (rc == SPEC_OK) rc = build_mat(m, {d}, Fl, false, L.down);
+    cudaStreamSynchronize(m->stream);
+    for (void* t : temps) cudaFree(t);
     if (rc == SPEC_OK) rc = vec_of(pre + "attn_norm.weight", H, &L.attn_norm);
     if (rc == SPEC_OK) rc = vec_of(pre + "ffn_norm.weight", H, &L.ffn_norm);
     if (rc == SPEC_OK && c.has_bias) {
@@ -1163,7 +1290,10 @@ int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) 
         memcpy(b.data() + off, f.data(*t), (size_t)lens[i] * 4);
         off += lens[i];
       }
-      if (rc == SPEC_OK) rc = upload_vec(m, &tmpd, b.data(), (int)b.size());
+      if (rc == SPEC_OK) {
+        std::vector<float> bl = shard_qkv_bias(m, b, c.n_heads, c.n_kv, hd);
+        rc = upload_vec(m, &tmpd, bl.data(), (int)bl.size());
+      }
       L.bqkv = tmpd;
     }
     if (rc != SPEC_OK) return rc;
@@ -1191,6 +1321,7 @@ int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) 
   outp.rows = c.vocab;
   rc = build_mat(m, {outp}, H, false, m->lm);
   if (rc != SPEC_OK) return rc;
+  set_local_dims(m);
   return finalize_model(m, opts, c.ctx_len);
 }
 
@@ -1266,6 +1397,7 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
       c.hidden / kGroupRows > kMaxSsGroups ||
       (c.head_dim != 64 && c.head_dim != 128) || c.n_heads % c.n_kv)
     return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported synthetic model shape");
+  if (int rc0 = check_tp_shape(m, c.n_heads, c.n_kv, c.head_dim, c.ffn)) return rc0;
   const int H = c.hidden, F = c.ffn, hd = c.head_dim;
   uint64_t tid = 0;
   auto tseed = [&]() { return mix64(seed * 0x100000001B3ull + (++tid)); };
@@ -1282,13 +1414,29 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, H), F, H, tseed(), g);
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, H), F, H, tseed(), u);
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, true, l, F), H, F, tseed(), dn);
+    if (rc == SPEC_OK) rc = shard_layer(m, temps, c.n_heads, c.n_kv, hd, H, F, q, k, v, o, g, u, dn);
+    const int Kl_o = c.n_heads / m->tp_size * hd, Fl = F / m->tp_size;
     if (rc == SPEC_OK) rc = build_mat(m, {q, k, v}, H, false, L.qkv);
-    if (rc == SPEC_OK) rc = build_mat(m, {o}, c.n_heads * hd, false, L.o);
+    if (rc == SPEC_OK) rc = build_mat(m, {o}, Kl_o, false, L.o);
     if (rc == SPEC_OK) rc = build_mat(m, {g, u}, H, true, L.gu);
-    if (rc == SPEC_OK) rc = build_mat(m, {dn}, F, false, L.down);
+    if (rc == SPEC_OK) rc = build_mat(m, {dn}, Fl, false, L.down);
     if (rc == SPEC_OK) rc = synth_vec(m, &L.attn_norm, H, tseed(), 1.f);
     if (rc == SPEC_OK) rc = synth_vec(m, &L.ffn_norm, H, tseed(), 1.f);
-    if (rc == SPEC_OK && c.has_bias) rc = synth_vec(m, &L.bqkv, (c.n_heads + 2 * c.n_kv) * hd, tseed(), 0.f);
+    if (rc == SPEC_OK && c.has_bias) {
+      const int nb = (c.n_heads + 2 * c.n_kv) * hd;
+      float* full = nullptr;
+      rc = synth_vec(m, &full, nb, tseed(), 0.f);
+      if (rc == SPEC_OK && m->tp_size > 1) {
+        std::vector<float> h(nb);
+        cudaError_t e = cudaMemcpyAsync(h.data(), full, (size_t)nb * 4, cudaMemcpyDeviceToHost, m->stream);
+        if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+        if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "bias shard"));
+        std::vector<float> b = shard_qkv_bias(m, h, c.n_heads, c.n_kv, hd);
+        if (rc == SPEC_OK) rc = upload_vec(m, &L.bqkv, b.data(), (int)b.size());
+      } else {
+        L.bqkv = full;
+      }
+    }
     cudaStreamSynchronize(m->stream);
     for (void* t : temps) cudaFree(t);
     if (rc != SPEC_OK) return rc;
@@ -1312,6 +1460,7 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
     for (void* t : temps) cudaFree(t);
     if (rc != SPEC_OK) return rc;
   }
+  set_local_dims(m);
   return finalize_model(m, opts, c.ctx_len);
 }
 
@@ -1360,6 +1509,54 @@ int spec_create_synthetic(const spec_model_desc* desc, uint64_t seed, const spec
 }
 
 void spec_free(spec_model* m) { delete m; }
+
+int spec_tp_handle(spec_model* m, void* out, int cap) {
+  if (!m || !out) return -SPEC_ERR_INVALID;
+  if (m->tp_size <= 1 || !m->tp_buf) return -m->fail(SPEC_ERR_INVALID, "not a tensor-parallel handle");
+  if (cap < (int)sizeof(cudaIpcMemHandle_t)) return -m->fail(SPEC_ERR_INVALID, "handle buffer too small");
+  cudaSetDevice(m->device);
+  // The zeroed counters must be in place before any peer can write to them.
+  cudaError_t e = cudaStreamSynchronize(m->stream);
+  if (e != cudaSuccess) return -m->fail(SPEC_ERR_CUDA, cuda_msg(e, "stream"));
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, m->tp_buf);
+  if (e != cudaSuccess) return -m->fail(SPEC_ERR_CUDA, cuda_msg(e, "cudaIpcGetMemHandle"));
+  memcpy(out, &h, sizeof h);
+  return (int)sizeof h;
+}
+
+int spec_tp_connect(spec_model* m, const void* handles, int n) {
+  if (!m || !handles) return SPEC_ERR_INVALID;
+  if (m->tp_size <= 1 || n != m->tp_size) return m->fail(SPEC_ERR_INVALID, "handle count differs from tp_size");
+  if (m->tp_connected) return m->fail(SPEC_ERR_INVALID, "already connected");
+  cudaSetDevice(m->device);
+  std::vector<uint8_t*> base(n);
+  for (int r = 0; r < n; ++r) {
+    if (r == m->tp_rank) {
+      base[r] = m->tp_buf;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const uint8_t*>(handles) + (size_t)r * sizeof h, sizeof h);
+    void* ptr = nullptr;
+    const cudaError_t e = cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "cudaIpcOpenMemHandle"));
+    m->tp_peer_bases.push_back(ptr);
+    base[r] = static_cast<uint8_t*>(ptr);
+  }
+  std::vector<void*> ptrs((size_t)2 * 2 * n);
+  for (int set = 0; set < 2; ++set)
+    for (int r = 0; r < n; ++r) {
+      ptrs[((size_t)set * 2 + 0) * n + r] = base[r] + set * m->tp_set_bytes;
+      ptrs[((size_t)set * 2 + 1) * n + r] = base[r] + set * m->tp_set_bytes + m->tp_recv_bytes;
+    }
+  const cudaError_t e = cudaMemcpy(m->tp_ptrs_dev, ptrs.data(), ptrs.size() * sizeof(void*), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "peer pointer table"));
+  m->tp_connected = true;
+  return SPEC_OK;
+}
+
+int spec_tp_size(const spec_model* m) { return m ? m->tp_size : 0; }
 
 const char* spec_last_error(const spec_model* m) { return m ? m->err.c_str() : g_load_error.c_str(); }
 

@@ -416,6 +416,15 @@ SPEC_DEV int atom_add_acq_rel(int* ptr, int v) {
 SPEC_DEV void red_add_release(int* ptr, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
+// Arrival on another GPU's counter (system scope, after fence.sc.sys).
+SPEC_DEV void red_add_release_sys(int* ptr, int v) {
+  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+SPEC_DEV int ld_acquire_sys(const int* ptr) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
 
 // Finishes one piece (the part of a 128-row group inside one chunk).  A
 // group that lies in one chunk goes straight to the fused epilogue.  A group
@@ -523,6 +532,54 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
         const int col = nt * 8 + 2 * t + (i & 1);
         if (col < M) ys[col * kGroupRows + row] = acc[rt][nt][i];
       }
+  if (p.tp_size > 1) {
+    // Tensor parallelism: this rank's sum of the group goes to every rank's
+    // receive slot; once all ranks' sums are here, they are added in rank
+    // order (the same arithmetic on every rank, so h stays identical).
+    consumer_sync();
+    const int ng = p.seg[0].groups + p.seg[1].groups;
+    const int n4 = M * (kGroupRows / 4);
+    const size_t slot4 = kTpSlot / 4;
+    const float4* ys4c = reinterpret_cast<const float4*>(ys);
+    for (int r = 0; r < p.tp_size; ++r) {
+      float4* dst = reinterpret_cast<float4*>(p.tp_recv[r]) + ((size_t)p.tp_rank * ng + group) * slot4;
+      for (int e = tid; e < n4; e += kGemvWarps * 32) dst[e] = ys4c[e];
+    }
+    consumer_sync();
+    if (tid == 0) {
+      __threadfence_system();
+      for (int r = 0; r < p.tp_size; ++r) red_add_release_sys(p.tp_cnt[r] + group, 1);
+      const unsigned long long t0 = global_timer_ns();
+      int seen;
+      while ((seen = ld_acquire_sys(p.tp_cnt_local + group)) < p.tp_size) {
+        if (global_timer_ns() - t0 > kMbarTimeoutNs) {
+          atomicOr(p.err, DEV_ERR_MBAR_TIMEOUT);
+          if (atomicCAS(p.err + 1, 0u, WAIT_TP_PEERS | ((unsigned)group << 8) | ((unsigned)blockIdx.x << 16)) == 0u) {
+            p.err[2] = (unsigned)group;
+            p.err[3] = (unsigned)seen;
+          }
+          break;
+        }
+      }
+      // This slot's next use is the next op of the same set, which no rank
+      // reaches before every rank has finished this op.
+      p.tp_cnt_local[group] = 0;
+    }
+    consumer_sync();
+    const float4* rl = reinterpret_cast<const float4*>(p.tp_recv_local);
+    float4* ys4 = reinterpret_cast<float4*>(ys);
+    for (int e = tid; e < n4; e += kGemvWarps * 32) {
+      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+      for (int r = 0; r < p.tp_size; ++r) {
+        const float4 v = __ldcg(rl + ((size_t)r * ng + group) * slot4 + e);
+        sum.x += v.x;
+        sum.y += v.y;
+        sum.z += v.z;
+        sum.w += v.w;
+      }
+      ys4[e] = sum;
+    }
+  }
   if (p.ss_in || p.ss_scale) {
     // Per-group sums of squares of the residual rows (fetched into sst above)
     // -> RMSNorm scale: thread m adds its column in group order.

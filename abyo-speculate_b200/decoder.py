@@ -28,6 +28,17 @@ def _ptr(a: np.ndarray, ct):
     return a.ctypes.data_as(ctypes.POINTER(ct))
 
 
+def exchange_tp_handles(mine: bytes, group=None) -> List[bytes]:
+    """All ranks' tensor-parallel handles in rank order (torch.distributed
+    all_gather_object over `group`; works with the gloo and nccl backends)."""
+    import torch.distributed as dist
+    out: List[Optional[bytes]] = [None] * dist.get_world_size(group)
+    dist.all_gather_object(out, bytes(mine), group=group)
+    if any(h is None or len(h) != len(mine) for h in out):
+        raise _lib.SpecError(_lib.SPEC_ERR_INVALID, "tensor-parallel handle exchange returned a malformed handle")
+    return [bytes(h) for h in out]
+
+
 class B200Decoder:
     """One model resident on one B200; stateful like the reference decoders."""
 
@@ -41,10 +52,13 @@ class B200Decoder:
     # ---- construction ----------------------------------------------------
     @classmethod
     def from_gguf(cls, path: str, device: int = 0, max_ctx: int = 0, use_graphs: bool = True,
-                  eos_token_ids: Sequence[int] = ()) -> "B200Decoder":
-        """LlamaQuantDecoder::from_gguf / Qwen2QuantDecoder::from_gguf (quantized_llama.rs:57-97)."""
+                  eos_token_ids: Sequence[int] = (), tp_rank: int = 0, tp_size: int = 1) -> "B200Decoder":
+        """LlamaQuantDecoder::from_gguf / Qwen2QuantDecoder::from_gguf (quantized_llama.rs:57-97).
+
+        With tp_size > 1 the handle holds rank tp_rank's tensor-parallel shard;
+        call tp_connect() on every rank before the first forward."""
         lib = _lib.load()
-        opts = _lib.LoadOpts(device, max_ctx, 1 if use_graphs else 0)
+        opts = _lib.LoadOpts(device, max_ctx, 1 if use_graphs else 0, tp_rank, tp_size)
         h = ctypes.c_void_p()
         _lib.check(lib.spec_load_gguf(path.encode(), ctypes.byref(opts), ctypes.byref(h)), None)
         return cls(h, eos_token_ids)
@@ -53,16 +67,39 @@ class B200Decoder:
     def synthetic(cls, arch: str, n_layers: int, hidden: int, n_heads: int, n_kv_heads: int, ffn: int,
                   vocab: int, rope_theta: float, eps: float, quant_mix: str = "Q4_K_M", seed: int = 0,
                   device: int = 0, max_ctx: int = 0, use_graphs: bool = True, rope_half: bool = False,
-                  eos_token_ids: Sequence[int] = ()) -> "B200Decoder":
-        """A seeded synthetic model whose weights are generated on the device."""
+                  eos_token_ids: Sequence[int] = (), tp_rank: int = 0, tp_size: int = 1) -> "B200Decoder":
+        """A seeded synthetic model whose weights are generated on the device
+        (the same weights for every tp_size; a tensor-parallel rank keeps its shard)."""
         lib = _lib.load()
         mixes = {"Q4_K_M": 0, "Q5_K": 1, "Q8_0": 2, "BF16": 3}
         d = _lib.ModelDesc(0 if arch == "llama" else 1, n_layers, hidden, n_heads, n_kv_heads, ffn, vocab,
                            rope_theta, eps, mixes[quant_mix], 1 if rope_half else 0)
-        opts = _lib.LoadOpts(device, max_ctx, 1 if use_graphs else 0)
+        opts = _lib.LoadOpts(device, max_ctx, 1 if use_graphs else 0, tp_rank, tp_size)
         h = ctypes.c_void_p()
         _lib.check(lib.spec_create_synthetic(ctypes.byref(d), seed, ctypes.byref(opts), ctypes.byref(h)), None)
         return cls(h, eos_token_ids)
+
+    # ---- tensor parallelism ------------------------------------------------
+    def tp_size(self) -> int:
+        return int(self._lib.spec_tp_size(self._h))
+
+    def tp_handle(self) -> bytes:
+        """This rank's receive-buffer handle (CUDA IPC), to be shared with every rank."""
+        buf = ctypes.create_string_buffer(256)
+        n = self._lib.spec_tp_handle(self._h, buf, 256)
+        if n < 0:
+            self._check(-n)
+        return buf.raw[:n]
+
+    def tp_connect(self, handles: Sequence[bytes]) -> None:
+        """Maps every rank's receive buffer (handles in rank order)."""
+        blob = b"".join(handles)
+        self._check(self._lib.spec_tp_connect(self._h, blob, len(handles)))
+
+    def tp_connect_group(self, group=None) -> None:
+        """Exchanges handles over a torch.distributed process group, then connects."""
+        handles = exchange_tp_handles(self.tp_handle(), group)
+        self.tp_connect(handles)
 
     def close(self) -> None:
         if self._h:

@@ -55,7 +55,9 @@ typedef struct spec_load_opts {
   int device;     /* CUDA device ordinal */
   int max_ctx;    /* KV capacity in tokens; 0 = min(GGUF context_length, 4096) */
   int use_graphs; /* 1 = replay one CUDA graph per row count (default), 0 = eager */
-  int reserved[5];
+  int tp_rank;    /* tensor-parallel rank of this handle (0 when tp_size <= 1) */
+  int tp_size;    /* tensor-parallel ranks (0 or 1 = a whole model on one GPU); see spec_tp_* */
+  int reserved[3];
 } spec_load_opts;
 
 /* Shape of a seeded synthetic model (weights generated on the device). */
@@ -78,6 +80,21 @@ int spec_load_gguf(const char* path, const spec_load_opts* opts, spec_model** ou
 int spec_create_synthetic(const spec_model_desc* desc, uint64_t seed, const spec_load_opts* opts,
                           spec_model** out);
 void spec_free(spec_model* m);
+
+/* ---- tensor parallelism (one process per GPU) ----------------------------
+ * No counterpart in the reference (candle runs the model on one device).  A
+ * handle loaded with tp_size > 1 holds rank tp_rank's shard: its q/kv heads
+ * and FFN slice (column-parallel q/k/v and gate/up, row-parallel o and down,
+ * KV cache of its heads; embedding, norms and LM head whole).  The sums of
+ * the row-parallel projections are exchanged inside the forward kernel over
+ * NVLink peer memory.  Before the first forward every rank exports its
+ * receive buffer (spec_tp_handle: writes an opaque handle, returns its byte
+ * count or a negated status) and connects to all ranks' handles, given in
+ * rank order (spec_tp_connect).  Every rank must then make the same calls
+ * with the same arguments; results are identical on all ranks. */
+int spec_tp_handle(spec_model* m, void* out, int cap);
+int spec_tp_connect(spec_model* m, const void* handles, int n);
+int spec_tp_size(const spec_model* m);
 /* Message of the last error on `m`; with m == NULL, of the last failed
  * load on the calling thread. */
 const char* spec_last_error(const spec_model* m);
