@@ -50,7 +50,9 @@ constexpr int kGroupRows = 128;        // rows per CTA (4 warps x 32 rows)
 constexpr int kMaxRows = 64;           // max activation rows (M) per forward
 constexpr int kSsStride = 64;          // stride of per-group sum-of-squares slots
 constexpr int kMaxSsGroups = 64;       // hidden size <= 64 * 128
-constexpr int kTpSlot = kMaxRows * 128;  // floats per (source rank, group) receive slot
+constexpr int kTpSlot = kMaxRows * 128;  // words per (source rank, group) receive slot
+constexpr int kTpMaxLayers = 256;        // tp_tag = 2 x layer + set stays below 512
+__host__ __device__ inline unsigned tp_flag_of(unsigned epoch, int tag) { return (epoch << 9) | (unsigned)tag; }
 
 // Number of 8-row fragment columns (n-tiles) the kernels use for M rows: the
 // GEMV is instantiated for 1, 2, 4 and 8, and every producer of an operand
@@ -100,12 +102,15 @@ struct QmvParams {
   // Tensor parallelism (EPI_RESID of the row-parallel o / down projections):
   // after this rank's split reduction, the group's sum is stored into every
   // rank's receive slot over NVLink, and the ranks' sums are added in rank
-  // order before the residual update, the same way on every rank.
+  // order before the residual update, the same way on every rank.  Each
+  // 8-byte slot word carries a value (low half) and the flag of its use
+  // (high half: tp_flag_of(*tp_epoch, tp_tag)), so a reader needs no fence
+  // or counter: a word is ready when its flag is the current one.
   int tp_size = 1, tp_rank = 0;
-  float* const* tp_recv = nullptr;       // [tp_size] device: rank r's receive set
-  int* const* tp_cnt = nullptr;          // [tp_size] device: rank r's arrival counters for this set
-  const float* tp_recv_local = nullptr;  // this rank's receive set [src rank][group][kTpSlot]
-  int* tp_cnt_local = nullptr;           // this rank's counters [group]
+  int tp_tag = 0;                                    // 2 x layer + set: distinct within one forward
+  const unsigned* tp_epoch = nullptr;                // forward counter, identical on every rank
+  unsigned long long* const* tp_recv = nullptr;      // [tp_size] device: rank r's receive set
+  const unsigned long long* tp_recv_local = nullptr; // this rank's set [src rank][group][kTpSlot]
   int ss_groups = 0;
   float ss_inv_dim = 0.f;
   float eps = 0.f;

@@ -184,10 +184,11 @@ struct spec_model {
   std::map<int, Schedule> schedules;
   int tp_rank = 0, tp_size = 1;     // tensor-parallel position (1 = whole model on this GPU)
   // Tensor-parallel receive buffer (exported to the other ranks by CUDA IPC):
-  // two sets (o, down), each [tp_size][groups][kTpSlot] floats + [groups] counters.
+  // two sets (o, down), each [tp_size][groups][kTpSlot] flagged 8-byte words.
   uint8_t* tp_buf = nullptr;
-  size_t tp_set_bytes = 0, tp_recv_bytes = 0;
-  void** tp_ptrs_dev = nullptr;     // [set][kind: recv, cnt][rank] device pointers
+  size_t tp_set_bytes = 0;
+  void** tp_ptrs_dev = nullptr;     // [set][rank] device pointers to every rank's sets
+  unsigned tp_epoch = 0;            // forwards run (the same count on every rank)
   std::vector<void*> tp_peer_bases; // opened IPC mappings (closed at free)
   bool tp_connected = false;
   int l2_ahead = 0;                 // weight stages each CTA prefetches into L2 ahead of its ring (SPEC_B200_L2_AHEAD)
@@ -409,10 +410,9 @@ int alloc_runtime(spec_model* m) {
   ALLOC(m->gemv_part, part * 4);
   ALLOC(m->counters, (size_t)max_groups * 4);
   if (m->tp_size > 1) {
-    m->tp_recv_bytes = (size_t)m->tp_size * groups_h * kTpSlot * 4;
-    m->tp_set_bytes = m->tp_recv_bytes + (((size_t)groups_h * 4 + 255) / 256) * 256;
+    m->tp_set_bytes = (size_t)m->tp_size * groups_h * kTpSlot * 8;
     ALLOC(m->tp_buf, 2 * m->tp_set_bytes);
-    ALLOC(m->tp_ptrs_dev, (size_t)2 * 2 * m->tp_size * sizeof(void*));
+    ALLOC(m->tp_ptrs_dev, (size_t)2 * m->tp_size * sizeof(void*));
   }
   ALLOC(m->logits, (size_t)kMaxRows * V * 4);
   ALLOC(m->last_row, (size_t)V * 4);
@@ -538,15 +538,14 @@ cudaError_t prof_mark(ProfRec* pr, cudaStream_t s, int kind, int64_t bytes) {
 enum : int { K_FWD = 8 };
 
 // Points a row-parallel op's epilogue at its tensor-parallel receive set.
-void set_tp(spec_model* m, QmvParams& p, int set) {
+void set_tp(spec_model* m, QmvParams& p, int layer, int set) {
   if (m->tp_size <= 1) return;
   p.tp_size = m->tp_size;
   p.tp_rank = m->tp_rank;
-  void** base = m->tp_ptrs_dev + (size_t)set * 2 * m->tp_size;
-  p.tp_recv = reinterpret_cast<float* const*>(base);
-  p.tp_cnt = reinterpret_cast<int* const*>(base + m->tp_size);
-  p.tp_recv_local = reinterpret_cast<const float*>(m->tp_buf + set * m->tp_set_bytes);
-  p.tp_cnt_local = reinterpret_cast<int*>(m->tp_buf + set * m->tp_set_bytes + m->tp_recv_bytes);
+  p.tp_tag = 2 * layer + set;
+  p.tp_epoch = &m->step_dev->tp_epoch;
+  p.tp_recv = reinterpret_cast<unsigned long long* const*>(m->tp_ptrs_dev + (size_t)set * m->tp_size);
+  p.tp_recv_local = reinterpret_cast<const unsigned long long*>(m->tp_buf + set * m->tp_set_bytes);
 }
 
 // The two sum-of-squares tables (see alloc_runtime).
@@ -603,7 +602,7 @@ FwdOp op_o(spec_model* m, int l, int M) {
   p.next_frag = m->xa;
   p.next_xsum16 = m->xa16;
   p.next_xsum32 = m->xa32;
-  set_tp(m, p, 0);
+  set_tp(m, p, l, 0);
   return o;
 }
 FwdOp op_gu(spec_model* m, int l, int M) {
@@ -644,7 +643,7 @@ FwdOp op_down(spec_model* m, int l, int M) {
   p.next_frag = m->xa;
   p.next_xsum16 = m->xa16;
   p.next_xsum32 = m->xa32;
-  set_tp(m, p, 1);
+  set_tp(m, p, l, 1);
   return o;
 }
 FwdOp op_lm(spec_model* m, int M, float* out) {
@@ -869,6 +868,7 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
 int run_forward(spec_model* m, int M, int flags, const std::vector<int>* collect = nullptr) {
   if (m->tp_size > 1 && !m->tp_connected)
     return m->fail(SPEC_ERR_INVALID, "tensor-parallel handle used before spec_tp_connect");
+  m->step_host->tp_epoch = ++m->tp_epoch;
   cudaError_t e = cudaSuccess;
   const int key = M | (flags << 8);
   const bool graphable = m->use_graphs && collect == nullptr;
@@ -1098,9 +1098,10 @@ int part_cols(spec_model* m, std::vector<void*>& temps, const Part& p, int K, in
 // Checks that the model splits into tp_size tensor-parallel shards: whole q
 // and kv heads per rank, FFN slices of whole 128-row groups, and column
 // splits on tile boundaries.
-int check_tp_shape(spec_model* m, int nq, int nkv, int hd, int F) {
+int check_tp_shape(spec_model* m, int nq, int nkv, int hd, int F, int n_layers) {
   const int N = m->tp_size;
   if (N == 1) return SPEC_OK;
+  if (n_layers > kTpMaxLayers) return m->fail(SPEC_ERR_UNSUPPORTED, "too many layers for tensor parallelism");
   if (nq % N || nkv % N || F % N || (F / N) % kGroupRows || ((nq / N) * hd) % 256 || (F / N) % 256 ||
       ((nkv / N) * hd) % kGroupRows)
     return m->fail(SPEC_ERR_UNSUPPORTED, "model does not split into tp_size tensor-parallel shards");
@@ -1206,7 +1207,7 @@ int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) 
   if (c.hidden % kGroupRows || c.ffn % kGroupRows || (c.head_dim != 64 && c.head_dim != 128) ||
       c.n_heads % c.n_kv || c.hidden / kGroupRows > kMaxSsGroups)
     return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported model shape");
-  if (int rc0 = check_tp_shape(m, c.n_heads, c.n_kv, c.head_dim, c.ffn)) return rc0;
+  if (int rc0 = check_tp_shape(m, c.n_heads, c.n_kv, c.head_dim, c.ffn, c.n_layers)) return rc0;
 
   auto part_of = [&](const std::string& name, int K, Part& p) -> bool {
     const GgufTensor* t = f.tensor(name);
@@ -1397,7 +1398,7 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
       c.hidden / kGroupRows > kMaxSsGroups ||
       (c.head_dim != 64 && c.head_dim != 128) || c.n_heads % c.n_kv)
     return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported synthetic model shape");
-  if (int rc0 = check_tp_shape(m, c.n_heads, c.n_kv, c.head_dim, c.ffn)) return rc0;
+  if (int rc0 = check_tp_shape(m, c.n_heads, c.n_kv, c.head_dim, c.ffn, c.n_layers)) return rc0;
   const int H = c.hidden, F = c.ffn, hd = c.head_dim;
   uint64_t tid = 0;
   auto tseed = [&]() { return mix64(seed * 0x100000001B3ull + (++tid)); };
@@ -1544,12 +1545,9 @@ int spec_tp_connect(spec_model* m, const void* handles, int n) {
     m->tp_peer_bases.push_back(ptr);
     base[r] = static_cast<uint8_t*>(ptr);
   }
-  std::vector<void*> ptrs((size_t)2 * 2 * n);
+  std::vector<void*> ptrs((size_t)2 * n);
   for (int set = 0; set < 2; ++set)
-    for (int r = 0; r < n; ++r) {
-      ptrs[((size_t)set * 2 + 0) * n + r] = base[r] + set * m->tp_set_bytes;
-      ptrs[((size_t)set * 2 + 1) * n + r] = base[r] + set * m->tp_set_bytes + m->tp_recv_bytes;
-    }
+    for (int r = 0; r < n; ++r) ptrs[(size_t)set * n + r] = base[r] + set * m->tp_set_bytes;
   const cudaError_t e = cudaMemcpy(m->tp_ptrs_dev, ptrs.data(), ptrs.size() * sizeof(void*), cudaMemcpyHostToDevice);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "peer pointer table"));
   m->tp_connected = true;

@@ -48,7 +48,8 @@ struct StepDev {
   int slots[kMaxRows];
   unsigned long long anc[kMaxRows];
   int step[2];  // P (keys before the new rows), P + M
-  int pad[2];
+  unsigned tp_epoch;  // forward counter (tensor parallelism: flags of the exchanged words)
+  int pad;
 };
 
 // Source of one weight part while building a fused matrix.

@@ -417,12 +417,12 @@ SPEC_DEV void red_add_release(int* ptr, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
 // Arrival on another GPU's counter (system scope, after fence.sc.sys).
-SPEC_DEV void red_add_release_sys(int* ptr, int v) {
-  asm volatile("red.release.sys.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+SPEC_DEV void st_relaxed_sys_u64(unsigned long long* ptr, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
 }
-SPEC_DEV int ld_acquire_sys(const int* ptr) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+SPEC_DEV unsigned long long ld_relaxed_sys_u64(const unsigned long long* ptr) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
   return v;
 }
 
@@ -534,50 +534,45 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       }
   if (p.tp_size > 1) {
     // Tensor parallelism: this rank's sum of the group goes to every rank's
-    // receive slot; once all ranks' sums are here, they are added in rank
-    // order (the same arithmetic on every rank, so h stays identical).
+    // receive slot as flagged words (peers first, this rank last); then each
+    // thread waits for its elements' words from every rank and adds them in
+    // rank order (the same arithmetic on every rank, so h stays identical).
+    // Each thread reads back only the elements it stored, so ys needs no
+    // barrier between the two loops.
     consumer_sync();
     const int ng = p.seg[0].groups + p.seg[1].groups;
-    const int n4 = M * (kGroupRows / 4);
-    const size_t slot4 = kTpSlot / 4;
-    const float4* ys4c = reinterpret_cast<const float4*>(ys);
-    for (int r = 0; r < p.tp_size; ++r) {
-      float4* dst = reinterpret_cast<float4*>(p.tp_recv[r]) + ((size_t)p.tp_rank * ng + group) * slot4;
-      for (int e = tid; e < n4; e += kGemvWarps * 32) dst[e] = ys4c[e];
+    const int n = M * kGroupRows;
+    const unsigned flag = tp_flag_of(*p.tp_epoch, p.tp_tag);
+    const unsigned long long hi = (unsigned long long)flag << 32;
+    for (int i = 1; i <= p.tp_size; ++i) {
+      const int r = (p.tp_rank + i) % p.tp_size;
+      unsigned long long* dst = p.tp_recv[r] + ((size_t)p.tp_rank * ng + group) * kTpSlot;
+      for (int e = tid; e < n; e += kGemvWarps * 32) st_relaxed_sys_u64(dst + e, hi | __float_as_uint(ys[e]));
     }
-    consumer_sync();
-    if (tid == 0) {
-      __threadfence_system();
-      for (int r = 0; r < p.tp_size; ++r) red_add_release_sys(p.tp_cnt[r] + group, 1);
-      const unsigned long long t0 = global_timer_ns();
-      int seen;
-      while ((seen = ld_acquire_sys(p.tp_cnt_local + group)) < p.tp_size) {
-        if (global_timer_ns() - t0 > kMbarTimeoutNs) {
-          atomicOr(p.err, DEV_ERR_MBAR_TIMEOUT);
-          if (atomicCAS(p.err + 1, 0u, WAIT_TP_PEERS | ((unsigned)group << 8) | ((unsigned)blockIdx.x << 16)) == 0u) {
-            p.err[2] = (unsigned)group;
-            p.err[3] = (unsigned)seen;
-          }
-          break;
-        }
-      }
-      // This slot's next use is the next op of the same set, which no rank
-      // reaches before every rank has finished this op.
-      p.tp_cnt_local[group] = 0;
-    }
-    consumer_sync();
-    const float4* rl = reinterpret_cast<const float4*>(p.tp_recv_local);
-    float4* ys4 = reinterpret_cast<float4*>(ys);
-    for (int e = tid; e < n4; e += kGemvWarps * 32) {
-      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+    bool live = true;
+    const unsigned long long t0 = global_timer_ns();
+    for (int e = tid; e < n; e += kGemvWarps * 32) {
+      float sum = 0.f;
       for (int r = 0; r < p.tp_size; ++r) {
-        const float4 v = __ldcg(rl + ((size_t)r * ng + group) * slot4 + e);
-        sum.x += v.x;
-        sum.y += v.y;
-        sum.z += v.z;
-        sum.w += v.w;
+        const unsigned long long* src = p.tp_recv_local + ((size_t)r * ng + group) * kTpSlot + e;
+        unsigned long long w = ld_relaxed_sys_u64(src);
+        for (unsigned spin = 0; live && (unsigned)(w >> 32) != flag; ++spin) {
+          if ((spin & 255u) == 255u &&
+              ((*(volatile unsigned*)p.err & DEV_ERR_MBAR_TIMEOUT) || global_timer_ns() - t0 > kMbarTimeoutNs)) {
+            live = false;
+            atomicOr(p.err, DEV_ERR_MBAR_TIMEOUT);
+            if (atomicCAS(p.err + 1, 0u, WAIT_TP_PEERS | ((unsigned)group << 8) | ((unsigned)blockIdx.x << 16)) ==
+                0u) {
+              p.err[2] = (unsigned)r;
+              p.err[3] = (unsigned)(w >> 32);
+            }
+            break;
+          }
+          w = ld_relaxed_sys_u64(src);
+        }
+        sum += __uint_as_float((unsigned)w);
       }
-      ys4[e] = sum;
+      ys[e] = sum;
     }
   }
   if (p.ss_in || p.ss_scale) {

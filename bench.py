@@ -10,9 +10,12 @@ the library's stream over K back-to-back device-side greedy verifies
 whole forward, device argmax, k+1 ints back).  `e2e` = the same metric through
 spec_batched_logits with host draft tokens in and the 5 x 128256 f32 logits
 rows copied back to host every step (the reference-facing Decoder call).
-Multi-GPU: one process per GPU, each rank an independent replica of the
-verify step (the path is measured per replica here; no collective), time =
-max over ranks, value = all ranks' steps / that time.
+Multi-GPU: one process per GPU, time = max over ranks.  By default each rank
+is an independent replica of the verify step (no collective; value = all
+ranks' steps / that time).  `--tp T` shards each model over T GPUs instead
+(tensor parallelism: each rank holds its heads and FFN slice, the o and down
+outputs are summed across the T ranks inside the GEMV epilogue over NVLink);
+the N GPUs then run N/T such models and value = their steps / the time.
 
 `--impl reference` times the reference's CPU path for the same workload.  The
 reference is Rust over candle and cannot be built here (no cargo/rustc, candle
@@ -236,13 +239,35 @@ def run_reference(args, ws, rank):
 # ---------------------------------------------------------------------------
 # B200 arm
 # ---------------------------------------------------------------------------
+def tp_groups(dist, ws, tp):
+    """Tensor-parallel groups of consecutive ranks; every rank creates every
+    group (torch.distributed requires it) and keeps its own."""
+    if tp <= 1:
+        return None
+    mine = None
+    rank = dist.get_rank()
+    for g0 in range(0, ws, tp):
+        grp = dist.new_group(list(range(g0, g0 + tp)))
+        if g0 <= rank < g0 + tp:
+            mine = grp
+    return mine
+
+
 def run_b200(args, ws, rank, local, dist):
     import torch
     pkg = importlib.import_module("abyo-speculate_b200")
     torch.cuda.set_device(local)
     cfg = dict(CFG, n_layers=args.layers)
-    dec = pkg.B200Decoder.synthetic(**cfg, quant_mix="Q4_K_M", seed=1234, device=local, max_ctx=4096)
-    rng = np.random.default_rng(7 + rank)
+    tp = args.tp
+    if tp < 1 or ws % tp:
+        raise SystemExit(f"--tp {tp} must divide the number of ranks ({ws})")
+    models = ws // tp
+    dec = pkg.B200Decoder.synthetic(**cfg, quant_mix="Q4_K_M", seed=1234, device=local, max_ctx=4096,
+                                    tp_rank=rank % tp, tp_size=tp)
+    if tp > 1:
+        dec.tp_connect_group(tp_groups(dist, ws, tp))
+    replica = rank // tp  # the ranks of one tensor-parallel model see the same inputs
+    rng = np.random.default_rng(7 + replica)
     prompt = rng.integers(0, CFG["vocab"], size=KV_LEN).tolist()
     dec.observe(prompt)
     drafts_all = rng.integers(0, CFG["vocab"], size=(max(args.steps, 1) + args.warmup + 8, K_DRAFT)).astype(np.uint32)
@@ -274,7 +299,7 @@ def run_b200(args, ws, rank, local, dist):
     # Seeded temperature-1.0 rejection-sampling round on the device
     # (spec_verify_rejection): same forward, then the vanilla.rs round over
     # the 5 rows with draft distributions and uniforms from the host.
-    rj_rng = np.random.default_rng(11 + rank)
+    rj_rng = np.random.default_rng(11 + replica)
     V = CFG["vocab"]
     rj_q = rj_rng.random((K_DRAFT, V), dtype=np.float32)
     rj_q /= rj_q.sum(axis=1, keepdims=True, dtype=np.float32)
@@ -324,15 +349,15 @@ def run_b200(args, ws, rank, local, dist):
     if rank != 0:
         return
     launches_per_step = dec.kernels_per_forward(K_DRAFT + 1) + 1  # + device argmax
-    value = ws * args.steps / (ms_max / 1e3)
-    e2e_value = ws * args.steps / (e2e_ms / 1e3)
+    value = models * args.steps / (ms_max / 1e3)
+    e2e_value = models * args.steps / (e2e_ms / 1e3)
     # DRAM bytes per launch of the dominant kernel, from the committed ncu
     # capture of one verify layer launch (dram__bytes_read + dram__bytes_write).
     traffic, traffic_alg = None, None
-    tp = os.path.join(ROOT, "profiles", "traffic.json")
-    if os.path.exists(tp):
+    tpath = os.path.join(ROOT, "profiles", "traffic.json")
+    if os.path.exists(tpath):
         try:
-            rec = json.load(open(tp))
+            rec = json.load(open(tpath))
             traffic, traffic_alg = rec.get("dram_bytes_per_launch"), rec.get("algorithmic_bytes_per_launch")
         except Exception:
             traffic = None
@@ -343,7 +368,7 @@ def run_b200(args, ws, rank, local, dist):
         "config": {"workload": "Llama-3-8B-shaped Q4_K_M verify step, k=4 (5 rows), 2048-token KV, batch 1"
                    + ("" if args.layers == CFG["n_layers"] else f" ({args.layers} of 32 layers: profiling case)"),
                    "rows": K_DRAFT + 1, "kv_len": KV_LEN, "quant_mix": "Q4_K_M (Q6_K v/down on even layers, Q6_K head)",
-                   "parallelism": f"replicas x{ws}", "l2": "weights 4.6 GB >> 126 MB L2 (no flush needed)",
+                   "parallelism": f"replicas x{ws}" if tp == 1 else f"tp{tp} x {models} replicas", "l2": "weights 4.6 GB >> 126 MB L2 (no flush needed)",
                    "weights": "seeded N(0,0.02), quantized on device"},
         "verify_us": round(ms_max / args.steps * 1e3, 2),
         "verify_us_device": round(dev_us, 2) if dev_us else None,
@@ -360,7 +385,7 @@ def run_b200(args, ws, rank, local, dist):
         "kernels": per_kind,
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": 1296 + 4 * K_DRAFT,
                 "d2h_bytes_per_step": (K_DRAFT + 1) * CFG["vocab"] * 4 + 4},
-        "rejection_t1": {"value": round(ws * args.steps / (rj_ms / 1e3), 3), "unit": UNIT,
+        "rejection_t1": {"value": round(models * args.steps / (rj_ms / 1e3), 3), "unit": UNIT,
                          "verify_us": round(rj_ms / args.steps * 1e3, 2),
                          "mean_commits": round(rj_commits / max(args.steps, 1), 3),
                          "note": "spec_verify_rejection, temperature 1.0, seeded draft distributions and uniforms"},
@@ -381,6 +406,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--reference-budget", type=float, default=120.0)
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel ranks per model (divides --gpus); 1 = one whole model per GPU")
     ap.add_argument("--layers", type=int, default=CFG["n_layers"],
                     help="transformer layers of the synthetic target (32 = the benchmark; fewer only for ncu captures)")
     args = ap.parse_args()
