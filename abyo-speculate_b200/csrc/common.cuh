@@ -96,6 +96,23 @@ SPEC_DEV void tma_bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
       : "memory");
 }
 
+// The same copy with an L2 cache-policy hint (e.g. evict_first for weights
+// streamed once per forward, so they do not push activations, partial sums
+// and norm tables out of L2).
+SPEC_DEV void tma_bulk_g2s_hint(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
+                                uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+          smem_u32(smem_dst)),
+      "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+SPEC_DEV uint64_t l2_policy_evict_first() {
+  uint64_t pol;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+  return pol;
+}
+
 // L2 prefetch of a contiguous range (no shared memory, no registers).
 SPEC_DEV void tma_prefetch_l2(const void* gmem_src, uint32_t bytes) {
   asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes) : "memory");

@@ -171,6 +171,13 @@ struct FwdParams {
   int* done = nullptr;         // [n_ops] completion counters, zero at launch
   unsigned* err = nullptr;
   int l2_ahead = 0;            // stages of this CTA's weights prefetched into L2 ahead of the ring
+  // Per-group completion flags [n_ops][flag_stride]: a group's epilogue
+  // stores *epoch (this forward's number) into its flag, so a stage of the
+  // next op waits only for the groups that produce its K range, not for the
+  // whole op.  Null: an op waits for its dependency's `done` count.
+  int* gflags = nullptr;
+  int flag_stride = 0;
+  const unsigned* epoch = nullptr;
 };
 
 // The instantiation is picked by (format set, nt_for_rows(M)); all ops of

@@ -128,6 +128,8 @@ struct spec_model {
   int attn_chunk = 64, attn_max_splits = 1;
   float* gemv_part = nullptr;
   int* counters = nullptr;
+  size_t part_set = 0;   // floats per partial set (two sets)
+  int counter_set = 0;   // counters per set (two sets); also the flag stride
   float* logits = nullptr;
   float* last_row = nullptr;
   float* hidden_out = nullptr;
@@ -180,6 +182,7 @@ struct spec_model {
     std::vector<int64_t> launch_bytes;
     std::vector<FwdOp> host_ops;
     FwdOp* solo = nullptr;  // the same ops with dep = -1, for one-op launches
+    int* gflags = nullptr;  // [n_ops][flag_stride] per-group completion flags
   };
   std::map<int, Schedule> schedules;
   int tp_rank = 0, tp_size = 1;     // tensor-parallel position (1 = whole model on this GPU)
@@ -188,7 +191,7 @@ struct spec_model {
   uint8_t* tp_buf = nullptr;
   size_t tp_set_bytes = 0;
   void** tp_ptrs_dev = nullptr;     // [set][rank] device pointers to every rank's sets
-  unsigned tp_epoch = 0;            // forwards run (the same count on every rank)
+  unsigned epoch = 0;               // forwards run (the same count on every tensor-parallel rank)
   std::vector<void*> tp_peer_bases; // opened IPC mappings (closed at free)
   bool tp_connected = false;
   int l2_ahead = 0;                 // weight stages each CTA prefetches into L2 ahead of its ring (SPEC_B200_L2_AHEAD)
@@ -407,8 +410,13 @@ int alloc_runtime(spec_model* m) {
     acc_mat(L.down);
   }
   acc_mat(m->lm);
-  ALLOC(m->gemv_part, part * 4);
-  ALLOC(m->counters, (size_t)max_groups * 4);
+  // Two sets of split-K partials and arrival counters, used by alternate ops
+  // of a launch: with per-group dependencies, op i+1 can start while op i
+  // still reduces; op i+2 starts only after op i is complete.
+  m->part_set = part;
+  m->counter_set = max_groups;
+  ALLOC(m->gemv_part, 2 * part * 4);
+  ALLOC(m->counters, (size_t)2 * max_groups * 4);
   if (m->tp_size > 1) {
     m->tp_set_bytes = (size_t)m->tp_size * groups_h * kTpSlot * 8;
     ALLOC(m->tp_buf, 2 * m->tp_set_bytes);
@@ -543,7 +551,7 @@ void set_tp(spec_model* m, QmvParams& p, int layer, int set) {
   p.tp_size = m->tp_size;
   p.tp_rank = m->tp_rank;
   p.tp_tag = 2 * layer + set;
-  p.tp_epoch = &m->step_dev->tp_epoch;
+  p.tp_epoch = &m->step_dev->epoch;
   p.tp_recv = reinterpret_cast<unsigned long long* const*>(m->tp_ptrs_dev + (size_t)set * m->tp_size);
   p.tp_recv_local = reinterpret_cast<const unsigned long long*>(m->tp_buf + set * m->tp_set_bytes);
 }
@@ -681,6 +689,10 @@ int get_schedule(spec_model* m, int M, int flags, spec_model::Schedule** out) {
   auto add = [&](FwdOp o, int64_t bytes) {
     const int first = sc.launches.back().first;
     o.dep = (int)ops.size() == first ? -1 : (int)ops.size() - 1 - first;
+    if (((int)ops.size() - first) & 1) {
+      o.q.part += m->part_set;
+      o.q.counters += m->counter_set;
+    }
     ops.push_back(o);
     sc.launches.back().second = (int)ops.size();
     sc.launch_bytes.back() += bytes;
@@ -699,6 +711,7 @@ int get_schedule(spec_model* m, int M, int flags, spec_model::Schedule** out) {
   sc.host_ops = ops;
   cudaError_t e = m->dalloc(&sc.ops, sizeof(FwdOp) * ops.size());
   if (e == cudaSuccess) e = m->dalloc(&sc.done, sizeof(int) * ops.size());
+  if (e == cudaSuccess) e = m->dalloc(&sc.gflags, sizeof(int) * ops.size() * m->counter_set);
   if (e == cudaSuccess) e = cudaMemcpy(sc.ops, ops.data(), sizeof(FwdOp) * ops.size(), cudaMemcpyHostToDevice);
   if (e == cudaSuccess) {
     std::vector<FwdOp> solo = ops;
@@ -720,6 +733,9 @@ cudaError_t launch_slice(spec_model* m, const spec_model::Schedule& sc, int li, 
   fp.done = sc.done + sc.launches[li].first;
   fp.err = m->err_dev;
   fp.l2_ahead = m->l2_ahead;
+  fp.gflags = sc.gflags + (size_t)sc.launches[li].first * m->counter_set;
+  fp.flag_stride = m->counter_set;
+  fp.epoch = &m->step_dev->epoch;
   return launch_fwd(fp, m->fmt_set, M, m->stream, pdl);
 }
 
@@ -868,7 +884,7 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
 int run_forward(spec_model* m, int M, int flags, const std::vector<int>* collect = nullptr) {
   if (m->tp_size > 1 && !m->tp_connected)
     return m->fail(SPEC_ERR_INVALID, "tensor-parallel handle used before spec_tp_connect");
-  m->step_host->tp_epoch = ++m->tp_epoch;
+  m->step_host->epoch = ++m->epoch;
   cudaError_t e = cudaSuccess;
   const int key = M | (flags << 8);
   const bool graphable = m->use_graphs && collect == nullptr;

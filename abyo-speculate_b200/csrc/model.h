@@ -48,7 +48,7 @@ struct StepDev {
   int slots[kMaxRows];
   unsigned long long anc[kMaxRows];
   int step[2];  // P (keys before the new rows), P + M
-  unsigned tp_epoch;  // forward counter (tensor parallelism: flags of the exchanged words)
+  unsigned epoch;  // forward counter: value of this forward's completion flags and exchanged words
   int pad;
 };
 

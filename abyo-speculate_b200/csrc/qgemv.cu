@@ -417,6 +417,22 @@ SPEC_DEV void red_add_release(int* ptr, int v) {
   asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
 // Arrival on another GPU's counter (system scope, after fence.sc.sys).
+SPEC_DEV void cp_async4(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+SPEC_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+SPEC_DEV void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+SPEC_DEV void st_relaxed_gpu(int* ptr, int v) {
+  asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
+SPEC_DEV int ld_relaxed_gpu(const int* ptr) {
+  int v;
+  asm volatile("ld.relaxed.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(ptr) : "memory");
+  return v;
+}
+SPEC_DEV void red_add_relaxed(int* ptr, int v) {
+  asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
+}
 SPEC_DEV void st_relaxed_sys_u64(unsigned long long* ptr, unsigned long long v) {
   asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
 }
@@ -433,7 +449,7 @@ SPEC_DEV unsigned long long ld_relaxed_sys_u64(const unsigned long long* ptr) {
 // and runs the epilogue.  The CTA that ran the epilogue bumps `done`.
 template <int NT>
 SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0, int i1, float (&acc)[2][NT][4],
-                                  float* ys, int* done) {
+                                  float* ys, int* done, int* gflag = nullptr, unsigned epoch = 0) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int g = lane >> 2, t = lane & 3;
   __shared__ int s_last;
@@ -444,28 +460,40 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
   consumer_sync();  // all warps are done with their scale scratch (aliased by ys)
 
   // Loads of the epilogue that do not depend on the split reduction are
-  // issued first, so their latency overlaps the partial-sum round trips: the
-  // sum-of-squares tables (into sst) and, for EPI_RESID at M <= 8, this
-  // thread's residual column and norm weight.
+  // issued (by the CTA that runs the epilogue only) before the partial sums,
+  // so their latency overlaps the partial-sum round trips: the sum-of-squares
+  // tables and the rows' positions / cache slots go to shared memory by
+  // cp.async (no registers held), and for EPI_RESID at M <= 8 this thread's
+  // residual column and norm weight go to registers.
+  // EPI_QKV's row positions / cache slots share s_red's storage (EPI_RESID only).
+  int* s_pos = reinterpret_cast<int*>(&s_red[0][0]);
+  int* s_slot = s_pos + kMaxRows;
   float* sst = ys + M * kGroupRows;
   const int n_ss = p.ss_groups * M;
   const float* ss_t1 = p.ss_in ? p.ss_pre : nullptr;
-  if (p.ss_in || p.ss_scale) {
-    const float* t0 = p.ss_in ? p.ss_in : p.ss_scale;
-    for (int i = tid; i < n_ss; i += kGemvWarps * 32) {
-      const int q = i / M, m = i - q * M;
-      sst[i] = __ldcg(t0 + q * kSsStride + m);
-      if (ss_t1) sst[n_ss + i] = __ldcg(ss_t1 + q * kSsStride + m);
-    }
-  }
+  const float* ss_t0 = p.ss_in ? p.ss_in : p.ss_scale;
   const bool resid_pre = p.epi == EPI_RESID && M <= 8;
   float hpre[8];
   float nwpre = 1.f;
-  if (resid_pre) {
+  auto epi_loads = [&]() {
+    if (ss_t0) {
+      for (int i = tid; i < n_ss; i += kGemvWarps * 32) {
+        const int q = i / M, m = i - q * M;
+        cp_async4(sst + i, ss_t0 + q * kSsStride + m);
+        if (ss_t1) cp_async4(sst + n_ss + i, ss_t1 + q * kSsStride + m);
+      }
+    }
+    if (p.epi == EPI_QKV && tid < M) {
+      cp_async4(s_pos + tid, p.positions + tid);
+      cp_async4(s_slot + tid, p.kv_slots + tid);
+    }
+    if (resid_pre) {
 #pragma unroll
-    for (int m = 0; m < 8; ++m) hpre[m] = m < M ? __ldcg(p.h + (size_t)m * H + n0 + tid) : 0.f;
-    if (p.next_norm) nwpre = __ldg(p.next_norm + n0 + tid);
-  }
+      for (int m = 0; m < 8; ++m) hpre[m] = m < M ? __ldcg(p.h + (size_t)m * H + n0 + tid) : 0.f;
+      if (p.next_norm) nwpre = __ldg(p.next_norm + n0 + tid);
+    }
+  };
+  if (i0 == i1) epi_loads();
 
   if (i0 != i1) {
     const size_t per = (size_t)kGroupRows * 8 * NT;
@@ -484,6 +512,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
     }
     consumer_sync();
     if (!s_last) return;  // uniform across the CTA
+    epi_loads();
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
@@ -575,21 +604,27 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       ys[e] = sum;
     }
   }
-  if (p.ss_in || p.ss_scale) {
-    // Per-group sums of squares of the residual rows (fetched into sst above)
-    // -> RMSNorm scale: thread m adds its column in group order.
+  cp_async_wait_all();  // sst, s_pos, s_slot
+  if (ss_t0) {
+    // Per-group sums of squares of the residual rows -> RMSNorm scale: warp w
+    // takes rows w, w+4, ...; lane l adds groups l, l+32, ..., then a fixed
+    // butterfly (the same order for every M).
     consumer_sync();
-    if (tid < M) {
-      float ms = 0.f;
-      for (int q = 0; q < p.ss_groups; ++q) ms += sst[q * M + tid];
-      float r = 1.f / sqrtf(ms * p.ss_inv_dim + p.eps);
-      if (ss_t1) {  // undo the pre-scale the operand was emitted with: x (1/r_pre) r
-        float mp = 0.f;
-        for (int q = 0; q < p.ss_groups; ++q) mp += sst[n_ss + q * M + tid];
-        r *= sqrtf(mp * p.ss_inv_dim + p.eps);
+    for (int m = warp; m < M; m += kGemvWarps) {
+      float ms = 0.f, mp = 0.f;
+      for (int q = lane; q < p.ss_groups; q += 32) {
+        ms += sst[q * M + m];
+        if (ss_t1) mp += sst[n_ss + q * M + m];
       }
-      // EPI_RESID (ss_scale): s_rinv is the pre-scale of the emitted operand.
-      s_rinv[tid] = r;
+      ms = warp_sum(ms);
+      if (ss_t1) mp = warp_sum(mp);
+      if (lane == 0) {
+        float r = 1.f / sqrtf(ms * p.ss_inv_dim + p.eps);
+        // undo the pre-scale the operand was emitted with: x (1/r_pre) r
+        if (ss_t1) r *= sqrtf(mp * p.ss_inv_dim + p.eps);
+        // EPI_RESID (ss_scale): s_rinv is the pre-scale of the emitted operand.
+        s_rinv[m] = r;
+      }
     }
   } else if (tid < M) {
     s_rinv[tid] = 1.f;
@@ -624,7 +659,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
         }
         float y = ys[m * kGroupRows + jp] * s_rinv[m];
         if (p.bias) y += p.bias[n0 + jp];
-        const int pos = p.positions[m];
+        const int pos = s_pos[m];
         const float cs = p.rope_cos[(size_t)pos * half + ci], sn = p.rope_sin[(size_t)pos * half + ci];
         const bool first = p.rope_interleaved ? ((d & 1) == 0) : (d < half);
         out = first ? (x * cs - y * sn) : (y * sn + x * cs);
@@ -636,10 +671,10 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
         reinterpret_cast<uint16_t*>(p.qbuf)[((size_t)kvh * R + r) * hd + d] = bits;
       } else if (!is_v) {
         const int kvh = head - nq;
-        reinterpret_cast<uint16_t*>(p.kcache)[((size_t)kvh * p.t_max + p.kv_slots[m]) * hd + d] = bits;
+        reinterpret_cast<uint16_t*>(p.kcache)[((size_t)kvh * p.t_max + s_slot[m]) * hd + d] = bits;
       } else {
         const int kvh = head - nq - nkv;
-        reinterpret_cast<uint16_t*>(p.vcache)[((size_t)kvh * p.t_max + p.kv_slots[m]) * hd + d] = bits;
+        reinterpret_cast<uint16_t*>(p.vcache)[((size_t)kvh * p.t_max + s_slot[m]) * hd + d] = bits;
       }
     }
   } else if (p.epi == EPI_RESID) {
@@ -691,7 +726,15 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
     }
   }
   consumer_sync();  // ys aliases the scale scratch of the next unit
-  if (done && tid == 0) red_add_release(done, 1);
+  if (done && tid == 0) {
+    if (gflag) {  // one release fence covers the group flag and the op count
+      fence_acq_rel_gpu();
+      st_relaxed_gpu(gflag + group, (int)epoch);
+      red_add_relaxed(done, 1);
+    } else {
+      red_add_release(done, 1);
+    }
+  }
 }
 
 SPEC_DEV void mbar_arrive(uint64_t* bar) {
@@ -874,6 +917,9 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
   }
   FwdParams P = Pg;
   P.ops = s_ops;
+  // This forward's number (the host writes it before the first kernel of
+  // the forward; it does not change while the forward runs).
+  const unsigned epoch = P.epoch ? *P.epoch : 0u;
   uint8_t* ring = smem;
   float* tail = reinterpret_cast<float*>(smem + FG::RING);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -890,6 +936,8 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
+      // Weights are read once per forward: evict them from L2 first.
+      const uint64_t wpol = l2_policy_evict_first();
       auto issue_w = [&](const SeqIt& it, int pos) {
         const QmvParams& q = P.ops[it.op].q;
         const StageLoc L = locate(q, it.s);
@@ -901,8 +949,9 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
         uint8_t* dst = ring + (size_t)st * FG::STAGE;
 #pragma unroll
         for (int w = 0; w < kGemvWarps; ++w)
-          tma_bulk_g2s(dst + w * FG::PAIRMAX,
-                       sg.w + ((size_t)(L.lgrp * kGemvWarps + w) * sg.k_tiles + L.kt) * pair, pair, &full[st]);
+          tma_bulk_g2s_hint(dst + w * FG::PAIRMAX,
+                            sg.w + ((size_t)(L.lgrp * kGemvWarps + w) * sg.k_tiles + L.kt) * pair, pair, &full[st],
+                            wpol);
       };
       auto issue_x = [&](const SeqIt& it, int pos) {
         const QmvParams& q = P.ops[it.op].q;
@@ -946,15 +995,39 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
       }
       pdl_wait();  // operands and counters come from the previous kernel
       int ready_op = -1;
+      // Stage readiness with per-group flags: the groups of the dependency
+      // that produce this stage's K range (128 output rows per group, 64
+      // activations per group after the SiLU epilogue) must carry this
+      // forward's epoch.  The dependency's `done` count is read alongside;
+      // once it is full, the rest of the op needs no more checks.
+      auto stage_ready = [&](const SeqIt& it) -> bool {
+        const int dep = P.ops[it.op].dep;
+        if (dep < 0) return true;
+        const QmvParams& d = P.ops[dep].q;
+        const int dgroups = d.seg[0].groups + d.seg[1].groups;
+        if (!P.gflags) return ld_acquire(P.done + dep) >= dgroups;
+        const QmvParams& q = P.ops[it.op].q;
+        const StageLoc L = locate(q, it.s);
+        const int KT = fmt_kt(q.seg[L.seg].fmt);
+        const int cpg = d.epi == EPI_SILU ? kGroupRows / 2 : kGroupRows;
+        const int g0 = (L.kt * KT) / cpg, g1 = (L.kt * KT + KT - 1) / cpg;
+        const int* fl = P.gflags + (size_t)dep * P.flag_stride;
+        const int all = ld_relaxed_gpu(P.done + dep);
+        bool ok = true;
+        for (int g = g0; g <= g1; ++g) ok &= ld_relaxed_gpu(fl + g) == (int)epoch;
+        if (all >= dgroups) {
+          ok = true;
+          ready_op = it.op;
+        }
+        if (ok) fence_acq_rel_gpu();
+        return ok;
+      };
       unsigned long long t_idle = 0;
       while (xi.valid) {
         bool progressed = false;
         if (xpos < wpos) {
-          if (xi.op <= ready_op || op_inputs_ready(P, xi.op)) {
-            if (xi.op > ready_op) {
-              ready_op = xi.op;
-              fence_proxy_async_global();
-            }
+          if (xi.op <= ready_op || stage_ready(xi)) {
+            fence_proxy_async_global();
             issue_x(xi, xpos);
             seq_next(P, c, G, xi);
             ++xpos;
@@ -996,7 +1069,7 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
   float* scr = tail + warp * (kScratch / 4);
   float acc[2][NT][4];
   bool ok = true;
-  int pos = 0, acq_op = -1;
+  int pos = 0;
   SeqIt it;
   seq_begin(P, c, G, it);
   while (it.valid) {
@@ -1025,25 +1098,15 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
       if (L.kt == kts - 1 || s == it.s_end - 1) {  // end of a piece
-        // The epilogue reads activations / norms of earlier ops: acquire them
-        // (once per op).
-        if (threadIdx.x == 0 && op > acq_op) {
-          acq_op = op;
-          const int dep = P.ops[op].dep;
-          if (dep >= 0) {
-            const QmvParams& d = P.ops[dep].q;
-            const unsigned long long t0 = global_timer_ns();
-            int seen;
-            while ((seen = ld_acquire(P.done + dep)) < d.seg[0].groups + d.seg[1].groups) {
-              if (global_timer_ns() - t0 > kMbarTimeoutNs) {
-                wait_gave_up(P.err, WAIT_CONSUMER_DEP, op, s, seen);
-                break;
-              }
-            }
-          }
-        }
+        // What the epilogue reads of earlier ops (norm tables, residual) is
+        // ordered before it without a wait here: a group is reduced only
+        // after every K stage of it ran, each stage's inputs were acquired
+        // by its CTA's producer (flags or count, then the mbarrier hand-off),
+        // and the split arrivals release / acquire those CTAs' work.  Every
+        // K stage of a group covers every group of the dependency.
         const int i0 = chunk_of(q, L.gstart), i1 = chunk_of(q, L.gstart + kts - 1);
-        reduce_and_epilogue<NT>(q, L.grp, own, i0, i1, acc, tail, P.done + op);
+        reduce_and_epilogue<NT>(q, L.grp, own, i0, i1, acc, tail, P.done + op,
+                                P.gflags ? P.gflags + (size_t)op * P.flag_stride : nullptr, epoch);
         consumer_sync();
 #pragma unroll
         for (int rt = 0; rt < 2; ++rt)
