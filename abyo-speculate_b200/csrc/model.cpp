@@ -1584,7 +1584,11 @@ int spec_history(const spec_model* m, uint32_t* out, int cap) {
   if (out && cap > 0) memcpy(out, m->history.data(), (size_t)std::min(cap, n) * 4);
   return n;
 }
-int spec_kv_len(const spec_model* m) { return m ? m->cache_len : 0; }
+// The logical KV length: a pending last token (lazy observe) counts.
+int spec_kv_len(const spec_model* m) {
+  if (!m) return 0;
+  return m->cache_len + (m->cache_len == (int)m->history.size() - 1 ? 1 : 0);
+}
 int spec_max_ctx(const spec_model* m) { return m ? m->t_max : 0; }
 
 int spec_reset(spec_model* m) {
@@ -1595,13 +1599,33 @@ int spec_reset(spec_model* m) {
   return SPEC_OK;
 }
 
+// Lazy observe: the KV rows of every new token but the last are computed
+// now; the last token stays pending (cache_len == history - 1) and its row is
+// computed by the next call that needs it -- next_logits, batched_logits, a
+// tree or verify forward -- which recompute the last committed token anyway
+// (quantized_llama.rs:561-569 truncates and replays it).  So the M=1 forward
+// that vanilla SD's observe runs after each round (vanilla.rs:358-360) is
+// folded into the next verify.  Rows are bit-identical either way: every
+// row's arithmetic is independent of the rows batched with it.
 int spec_observe(spec_model* m, const uint32_t* ids, int n) {
   if (!m || (n > 0 && !ids) || n < 0) return SPEC_ERR_INVALID;
   if (n == 0) return SPEC_OK;
   cudaSetDevice(m->device);
-  int rc = forward_advance(m, ids, n, nullptr);
-  if (rc != SPEC_OK) return rc;
+  for (int i = 0; i < n; ++i)
+    if (ids[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  const int size = (int)m->history.size();
+  if (size + n > m->t_max)
+    return m->fail(SPEC_ERR_INVALID, "KV capacity exceeded (" + std::to_string(size + n) + " > " +
+                                         std::to_string(m->t_max) + ")");
+  std::vector<uint32_t> todo;
+  if (size > 0 && m->cache_len == size - 1) todo.push_back(m->history.back());
+  todo.insert(todo.end(), ids, ids + n - 1);
+  if (!todo.empty()) {
+    const int rc = forward_advance(m, todo.data(), (int)todo.size(), nullptr, false);
+    if (rc != SPEC_OK) return rc;
+  }
   m->history.insert(m->history.end(), ids, ids + n);
+  m->last_valid = false;
   return SPEC_OK;
 }
 
@@ -1651,12 +1675,15 @@ int spec_rollback_to(spec_model* m, int len) {
   if (len > (int)m->history.size())
     return m->fail(SPEC_ERR_CACHE_ROLLBACK, "rollback target " + std::to_string(len) + " > history length " +
                                                 std::to_string(m->history.size()));
-  if (len > m->cache_len)
+  const int logical = spec_kv_len(m);
+  if (len > logical)
     return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate_kv_cache_to(" + std::to_string(len) + ") exceeds " +
-                                                std::to_string(m->cache_len));
+                                                std::to_string(logical));
+  const bool keep_valid = m->last_valid && len == (int)m->history.size() && m->cache_len == len;
   m->history.resize(len);
-  m->last_valid = false;
-  m->cache_len = len;
+  m->last_valid = keep_valid;
+  // A pending last token (cache_len == len - 1) stays pending.
+  m->cache_len = std::min(m->cache_len, len);
   return SPEC_OK;
 }
 
@@ -1670,9 +1697,11 @@ int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* paren
   if (tokens[0] != last)
     return m->fail(SPEC_ERR_INVALID, "tree root (" + std::to_string(tokens[0]) +
                                          ") must equal last committed token (" + std::to_string(last) + ")");
+  // The root is the last committed token, at position history - 1 (its KV
+  // row may still be pending after a lazy observe; the tree forward writes it).
   const int pre = m->cache_len;
-  if (pre < 1) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty cache");
-  const int prefix = pre - 1;
+  const int prefix = (int)m->history.size() - 1;
+  if (prefix > pre) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
   rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS);
   if (rc == SPEC_OK)
     cudaMemcpyAsync(m->logits_host, m->logits, (size_t)n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
@@ -1702,9 +1731,11 @@ int spec_tree_logits_keep_kv(spec_model* m, const uint32_t* tokens, const int32_
   if (tokens[0] != last)
     return m->fail(SPEC_ERR_INVALID, "tree root (" + std::to_string(tokens[0]) +
                                          ") must equal last committed token (" + std::to_string(last) + ")");
+  // The root is the last committed token, at position history - 1 (its KV
+  // row may still be pending after a lazy observe; the tree forward writes it).
   const int pre = m->cache_len;
-  if (pre < 1) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty cache");
-  const int prefix = pre - 1;
+  const int prefix = (int)m->history.size() - 1;
+  if (prefix > pre) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
   rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS | F_HIDDEN);
   if (rc == SPEC_OK && logits_out)
     cudaMemcpyAsync(m->logits_host, m->logits, (size_t)n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
@@ -1785,6 +1816,13 @@ int spec_observe_returning_last_hidden(spec_model* m, const uint32_t* ids, int n
   if (n <= 0) return m->fail(SPEC_ERR_INVALID, "observe_returning_last_hidden with empty ids");
   for (int i = 0; i < n; ++i)
     if (ids[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  // A pending last token (lazy observe) goes first.
+  std::vector<uint32_t> all;
+  if (!m->history.empty() && m->cache_len == (int)m->history.size() - 1) all.push_back(m->history.back());
+  all.insert(all.end(), ids, ids + n);
+  const int n_new = n;
+  n = (int)all.size();
+  ids = all.data();
   const int start = m->cache_len;
   if (start + n > m->t_max) return m->fail(SPEC_ERR_INVALID, "KV capacity exceeded");
   int done = 0;
@@ -1804,7 +1842,7 @@ int spec_observe_returning_last_hidden(spec_model* m, const uint32_t* ids, int n
     done += M;
   }
   m->cache_len = start + n;
-  m->history.insert(m->history.end(), ids, ids + n);
+  m->history.insert(m->history.end(), ids + (n - n_new), ids + n);
   // The forward ran without the LM head, so no next-token logits are cached.
   m->last_valid = false;
   memcpy(hidden_out, m->hidden_host, (size_t)m->cfg.hidden * 4);
@@ -2026,9 +2064,11 @@ int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t
   int rc = check_tree(m, tokens, parents, n);
   if (rc != SPEC_OK) return rc;
   if (tokens[0] != m->history.back()) return m->fail(SPEC_ERR_INVALID, "tree root must equal last committed token");
+  // The root is the last committed token, at position history - 1 (its KV
+  // row may still be pending after a lazy observe; the tree forward writes it).
   const int pre = m->cache_len;
-  if (pre < 1) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty cache");
-  const int prefix = pre - 1;
+  const int prefix = (int)m->history.size() - 1;
+  if (prefix > pre) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
   rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS);
   if (rc == SPEC_OK) {
     cudaError_t e = launch_row_argmax(m->logits, n, m->cfg.vocab, m->argmax_dev, nullptr,

@@ -48,6 +48,10 @@ CFG = dict(arch="llama", n_layers=32, hidden=4096, n_heads=32, n_kv_heads=8, ffn
            rope_theta=5e5, eps=1e-5)
 K_DRAFT = 4
 KV_LEN = 2048
+# BASELINE.json configs[1] draft: Llama-3.2-1B-shaped Q4_K_M.
+CFG_DRAFT = dict(arch="llama", n_layers=16, hidden=2048, n_heads=32, n_kv_heads=8, ffn=8192, vocab=128256,
+                 rope_theta=5e5, eps=1e-5)
+SD_NEW_TOKENS = 128
 KIND_NAMES = {0: "embed", 2: "attention (split + combine)", 8: "fwd_kernel (persistent multi-op GEMV)"}
 GEMV_KINDS = (8,)
 
@@ -253,6 +257,32 @@ def tp_groups(dist, ws, tp):
     return mine
 
 
+def run_sd_greedy(pkg, target, prompt, local):
+    """Generated tokens/s of greedy vanilla SD (k=4) with the configs[1] draft,
+    through the trait calls of vanilla.rs's round (abyo-speculate_b200/sd_loop.py).
+    Wall-clock over whole rounds (every call synchronises), prefill excluded.
+    Random-init target and draft agree on almost nothing, so rounds commit
+    about one token each; the per-round time is the informative figure."""
+    sd = importlib.import_module("abyo-speculate_b200.sd_loop")
+    draft = pkg.B200Decoder.synthetic(**CFG_DRAFT, quant_mix="Q4_K_M", seed=4321, device=local, max_ctx=4096)
+    target.rollback_to(KV_LEN)
+    draft.observe(prompt)
+    for _ in range(3):  # warm-up rounds (graph capture of the M=1 and M=5 forwards)
+        sd.vanilla_greedy_round(target, draft, K_DRAFT)
+    target.rollback_to(KV_LEN)
+    draft.rollback_to(KV_LEN)
+    t0 = time.perf_counter()
+    toks, acc = sd.vanilla_greedy_generate(target, draft, prompt, SD_NEW_TOKENS, K_DRAFT, observe_prompt=False)
+    el = time.perf_counter() - t0
+    target.rollback_to(KV_LEN)
+    draft.close()
+    return {"tok_per_s": round(len(toks) / el, 2), "tokens": len(toks), "rounds": len(acc),
+            "ms_per_round": round(el / len(acc) * 1e3, 3), "mean_accepted": round(float(np.mean(acc)), 3),
+            "k": K_DRAFT, "draft": "Llama-3.2-1B-shaped Q4_K_M (16 layers, hidden 2048, 32/8 heads, FFN 8192)",
+            "note": "greedy vanilla SD, 2048-token prompt, wall clock per round incl. host calls; "
+                    "random-init models accept ~0 drafts"}
+
+
 def run_b200(args, ws, rank, local, dist):
     import torch
     pkg = importlib.import_module("abyo-speculate_b200")
@@ -330,6 +360,7 @@ def run_b200(args, ws, rank, local, dist):
     f1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(dist, f0.elapsed_time(f1))
+    sd_block = run_sd_greedy(pkg, dec, prompt, local) if (tp == 1 and not args.no_sd) else None
     # per-kernel profile of one eager verify forward (roofline)
     kinds, kms, kbytes = dec.profile_forward(drafts_all[0].tolist())
     dec.rollback_to(KV_LEN)
@@ -389,6 +420,7 @@ def run_b200(args, ws, rank, local, dist):
                          "verify_us": round(rj_ms / args.steps * 1e3, 2),
                          "mean_commits": round(rj_commits / max(args.steps, 1), 3),
                          "note": "spec_verify_rejection, temperature 1.0, seeded draft distributions and uniforms"},
+        "sd_greedy": sd_block,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": sampler.summary(),
     }
@@ -406,6 +438,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--reference-budget", type=float, default=120.0)
+    ap.add_argument("--no-sd", action="store_true", help="skip the greedy SD-loop tokens/s measurement")
     ap.add_argument("--tp", type=int, default=1,
                     help="tensor-parallel ranks per model (divides --gpus); 1 = one whole model per GPU")
     ap.add_argument("--layers", type=int, default=CFG["n_layers"],

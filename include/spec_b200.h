@@ -108,14 +108,20 @@ int spec_num_layers(const spec_model* m);
 int spec_history_len(const spec_model* m);
 /* Copies min(cap, history_len) tokens; returns the full history length. */
 int spec_history(const spec_model* m, uint32_t* out, int cap);
-/* Current KV length (the reference decoder's `cache_len`). */
+/* Current KV length (the reference decoder's `cache_len`).  A token that
+ * spec_observe left pending (see below) counts. */
 int spec_kv_len(const spec_model* m);
 int spec_max_ctx(const spec_model* m);
 
 /* ---- Decoder (model/mod.rs:39-108) ---------------------------------------- */
 /* Decoder::reset (mod.rs:52-53; quantized_llama.rs:512-517). */
 int spec_reset(spec_model* m);
-/* Decoder::observe (mod.rs:55-56; quantized_llama.rs:519-526). */
+/* Decoder::observe (mod.rs:55-56; quantized_llama.rs:519-526).  Lazy: the KV
+ * rows of all but the last new token are computed now; the last one is
+ * computed inside the next call that needs it (next_logits, batched_logits,
+ * tree or verify forwards recompute the last committed token anyway), so the
+ * observe after a vanilla SD round costs no forward of its own.  Observable
+ * results (logits, history, KV length, errors) are those of an eager observe. */
 int spec_observe(spec_model* m, const uint32_t* ids, int n);
 /* Decoder::next_logits (mod.rs:58-60; quantized_llama.rs:528-551); out: V f32. */
 int spec_next_logits(spec_model* m, float* out);

@@ -239,3 +239,41 @@ def test_large_residual_stays_finite(pkg, oracle, tiny_gguf):
     b = ref.batched_logits(drafts)
     assert np.isfinite(a).all()
     assert np.abs(a - b).max() <= 1e-2 * np.abs(b).max()
+
+
+def test_lazy_observe_matches_eager(pkg, oracle, tiny_gguf):
+    """observe leaves its last token pending; every observable result is the
+    eager decoder's: KV length, rollback bounds, logits of the vanilla round
+    protocol (batched verify, rollback, observe of the commits), hidden
+    states after a pending token."""
+    dec, ref = _pair(pkg, oracle, tiny_gguf("llama_q4km"))
+    prompt = _prompt(dec.vocab_size(), 20, 21)
+    dec.observe(prompt)
+    ref.observe(prompt)
+    assert dec.kv_len() == ref.cache_len == 20
+    dec.rollback_to(20)  # no-op at the logical length
+    ref.rollback_to(20)
+    for rnd in range(3):  # vanilla.rs:285-369 round shape, k = 3
+        drafts = _prompt(dec.vocab_size(), 3, 30 + rnd)
+        pre = len(dec.history())
+        a = dec.batched_logits(drafts)
+        b = ref.batched_logits(drafts)
+        assert np.abs(a - b).max() <= TOL
+        acc = rnd % 3
+        commits = drafts[:acc] + [int(np.argmax(a[acc]))]
+        dec.rollback_to(pre + acc)
+        ref.rollback_to(pre + acc)
+        dec.observe(commits[acc:])
+        ref.observe(commits[acc:])
+        assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+    assert np.abs(dec.next_logits() - ref.next_logits()).max() <= TOL
+    # a pending token ahead of observe_returning_last_hidden
+    dec.observe([7, 8])
+    ref.observe([7, 8])
+    h = dec.observe_returning_last_hidden([9])
+    n = len(ref.history)
+    rh, _ = ref.m.forward([9], [n], [n], n, [1])
+    ref.observe([9])
+    assert np.abs(h - rh[-1]).max() <= TOL
+    assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+    assert np.abs(dec.next_logits() - ref.next_logits()).max() <= TOL
