@@ -257,6 +257,49 @@ def tp_groups(dist, ws, tp):
     return mine
 
 
+MICRO_SHAPES = [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336), (128256, 4096)]
+MICRO_ROWS = [1, 5, 8, 16, 32, 64]
+
+
+def run_microbench(pkg, local):
+    """the standalone dequant-matmul (spec_qmatmul,
+    the same persistent kernel as one op) for Q4_K and Q6_K at every (N, K)
+    and M; L2 flushed (512 MB memset) before each timed launch.  Weights: a
+    1024-row block of seeded N(0,0.02) floats quantized by the GGUF writer,
+    tiled down the rows (timing does not depend on the values; every row
+    still has its own address, so DRAM traffic is that of the full matrix).
+    GB/s = packed weight bytes / launch time (CUDA events, launch overhead
+    included)."""
+    import torch
+    gs = importlib.import_module("abyo-speculate_b200.gguf_synth")
+    peak, _ = measured_peaks()
+    rng = np.random.default_rng(5)
+    rows = []
+    for fmt, fname in ((12, "Q4_K"), (14, "Q6_K")):
+        base = {}
+        for N, K in MICRO_SHAPES:
+            if K not in base:
+                w = rng.standard_normal((1024, K), dtype=np.float32) * np.float32(0.02)
+                base[K] = gs.quantize(w, fmt).view(np.uint8).reshape(1024, -1)
+            blk = np.tile(base[K], ((N + 1023) // 1024, 1))[:N]
+            qw = pkg.QWeight(fmt, blk, N, K, device=local)
+            for M in MICRO_ROWS:
+                x = torch.randn(M, K, device=f"cuda:{local}")
+                y = torch.empty(M, N, device=f"cuda:{local}")
+                qw.matmul(x.data_ptr(), M, y.data_ptr())
+                torch.cuda.synchronize()
+                ms = qw.time_ms(M, 10, flush_l2=True)
+                gbs = qw.nbytes() / (ms * 1e-3) / 1e9
+                rows.append({"fmt": fname, "N": N, "K": K, "M": M, "us": round(ms * 1e3, 2), "GB_s": round(gbs, 1),
+                             "frac": round(gbs / peak, 4)})
+            qw.close()
+    big = [r for r in rows if r["N"] == 128256]
+    return {"peak_gbs": peak, "rows": rows,
+            "best_frac": max(r["frac"] for r in rows), "lm_head_q6k_m5_frac": next(
+                (r["frac"] for r in big if r["fmt"] == "Q6_K" and r["M"] == 5), None),
+            "note": "spec_qmatmul, f32 x in / f32 y out at the ABI (f16 operand inside), one launch per timing"}
+
+
 def run_sd_greedy(pkg, target, prompt, local):
     """Generated tokens/s of greedy vanilla SD (k=4) with the configs[1] draft,
     through the trait calls of vanilla.rs's round (abyo-speculate_b200/sd_loop.py).
@@ -361,6 +404,7 @@ def run_b200(args, ws, rank, local, dist):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(dist, f0.elapsed_time(f1))
     sd_block = run_sd_greedy(pkg, dec, prompt, local) if (tp == 1 and not args.no_sd) else None
+    micro = run_microbench(pkg, local) if (rank == 0 and not args.no_microbench) else None
     # per-kernel profile of one eager verify forward (roofline)
     kinds, kms, kbytes = dec.profile_forward(drafts_all[0].tolist())
     dec.rollback_to(KV_LEN)
@@ -421,6 +465,7 @@ def run_b200(args, ws, rank, local, dist):
                          "mean_commits": round(rj_commits / max(args.steps, 1), 3),
                          "note": "spec_verify_rejection, temperature 1.0, seeded draft distributions and uniforms"},
         "sd_greedy": sd_block,
+        "dequant_microbench": micro,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": sampler.summary(),
     }
@@ -439,6 +484,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--reference-budget", type=float, default=120.0)
     ap.add_argument("--no-sd", action="store_true", help="skip the greedy SD-loop tokens/s measurement")
+    ap.add_argument("--no-microbench", action="store_true", help="skip the dequant-matmul microbench (configs[2])")
     ap.add_argument("--tp", type=int, default=1,
                     help="tensor-parallel ranks per model (divides --gpus); 1 = one whole model per GPU")
     ap.add_argument("--layers", type=int, default=CFG["n_layers"],
