@@ -398,6 +398,36 @@ SPEC_DEV void emit_operand_warp(uint32_t* frag, float* xs16, float* xs32, int nt
   if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = s32;
 }
 
+// emit_operand_warp for rows 0..M-1 (M <= 8) of one column at once; the
+// rows' shuffle chains are independent, so they overlap.  Same arithmetic per
+// row as emit_operand_warp.
+SPEC_DEV void emit_rows_warp8(uint32_t* frag, float* xs16, float* xs32, int nt_total, int M, int k, const float (&v)[8],
+                              int bf16, int lane) {
+  float s16[8];
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    float back = 0.f;
+    if (m < M) {
+      const uint16_t bits = round_act(v[m], bf16, back);
+      frag_store(frag, nt_total, m, k, bits);
+    }
+    s16[m] = back;
+  }
+#pragma unroll
+  for (int o = 8; o > 0; o >>= 1)
+#pragma unroll
+    for (int m = 0; m < 8; ++m) s16[m] += __shfl_xor_sync(0xffffffffu, s16[m], o);
+  const int w16 = 8 * nt_total;
+#pragma unroll
+  for (int m = 0; m < 8; ++m) {
+    const float s32 = s16[m] + __shfl_xor_sync(0xffffffffu, s16[m], 16);
+    if (m < M) {
+      if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m] = s16[m];
+      if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = s32;
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Split-K reduction and fused epilogues.
 // ---------------------------------------------------------------------------
@@ -699,13 +729,39 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       }
     }
     const float nw = resid_pre ? nwpre : (p.next_norm ? __ldg(p.next_norm + n) : 1.f);
-    for (int m = 0; m < M; ++m) {
-      const float hv = ys[m * kGroupRows + tid];
-      const float sq = warp_sum(hv * hv);
-      if (lane == 0) s_red[warp][m] = sq;
-      // s_rinv[m] = rinv of the residual before this update (or 1).
-      if (p.next_frag)
-        emit_operand_warp(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m, n, hv * nw * s_rinv[m], p.act_bf16, lane);
+    // s_rinv[m] = rinv of the residual before this update (or 1).
+    if (M <= 8) {
+      // All rows at once: their shuffle chains are independent and overlap.
+      float hv[8], sq[8];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        hv[m] = m < M ? ys[m * kGroupRows + tid] : 0.f;
+        sq[m] = hv[m] * hv[m];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+        for (int m = 0; m < 8; ++m) sq[m] += __shfl_xor_sync(0xffffffffu, sq[m], o);
+      if (lane == 0) {
+#pragma unroll
+        for (int m = 0; m < 8; ++m)
+          if (m < M) s_red[warp][m] = sq[m];
+      }
+      if (p.next_frag) {
+        float v[8];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) v[m] = m < M ? hv[m] * nw * s_rinv[m] : 0.f;
+        emit_rows_warp8(p.next_frag, p.next_xsum16, p.next_xsum32, NT, M, n, v, p.act_bf16, lane);
+      }
+    } else {
+      for (int m = 0; m < M; ++m) {
+        const float hv = ys[m * kGroupRows + tid];
+        const float sq = warp_sum(hv * hv);
+        if (lane == 0) s_red[warp][m] = sq;
+        if (p.next_frag)
+          emit_operand_warp(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m, n, hv * nw * s_rinv[m], p.act_bf16,
+                            lane);
+      }
     }
     consumer_sync();
     if (tid < M) {
