@@ -1003,11 +1003,9 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
         const int st = pos % D;
         mbar_arrive_expect_tx(&full[st], kGemvWarps * pair + xb);
         uint8_t* dst = ring + (size_t)st * FG::STAGE;
-#pragma unroll
-        for (int w = 0; w < kGemvWarps; ++w)
-          tma_bulk_g2s_hint(dst + w * FG::PAIRMAX,
-                            sg.w + ((size_t)(L.lgrp * kGemvWarps + w) * sg.k_tiles + L.kt) * pair, pair, &full[st],
-                            wpol);
+        // The stage's 4 pair tiles are contiguous in HBM: one bulk copy.
+        tma_bulk_g2s_hint(dst, sg.w + ((size_t)L.lgrp * sg.k_tiles + L.kt) * kGemvWarps * pair, kGemvWarps * pair,
+                          &full[st], wpol);
       };
       auto issue_x = [&](const SeqIt& it, int pos) {
         const QmvParams& q = P.ops[it.op].q;
@@ -1031,9 +1029,7 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
         const StageLoc L = locate(q, it.s);
         const WSeg& sg = q.seg[L.seg];
         const int pair = fmt_pair_bytes(sg.fmt);
-#pragma unroll
-        for (int w = 0; w < kGemvWarps; ++w)
-          tma_prefetch_l2(sg.w + ((size_t)(L.lgrp * kGemvWarps + w) * sg.k_tiles + L.kt) * pair, pair);
+        tma_prefetch_l2(sg.w + ((size_t)L.lgrp * sg.k_tiles + L.kt) * kGemvWarps * pair, kGemvWarps * pair);
       };
       SeqIt wi, xi, pi;
       seq_begin(P, c, G, wi);
@@ -1148,8 +1144,9 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
       }
       if (ok) {
         const uint8_t* stage = ring + (size_t)st * FG::STAGE;
-        process_any<SET, NT>(q.seg[L.seg].fmt, stage + warp * FG::PAIRMAX, stage + kGemvWarps * FG::PAIRMAX, scr,
-                             lane, acc);
+        const int fmt = q.seg[L.seg].fmt;
+        process_any<SET, NT>(fmt, stage + warp * fmt_pair_bytes(fmt), stage + kGemvWarps * FG::PAIRMAX, scr, lane,
+                             acc);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&empty[st]);
@@ -1231,7 +1228,10 @@ __global__ void repack_kernel(const uint8_t* raw, int fmt, int N, int K, uint8_t
   const int be = fmt_block_elems(fmt), bb = fmt_block_bytes(fmt);
   const size_t row_bytes = (size_t)(K / be) * bb;
   const int k_tiles = K / KT;
-  uint8_t* out = tiles + (((size_t)(rt16 >> 1) * k_tiles + kt) * 2 + (rt16 & 1)) * TB;
+  // Layout [group][k-tile][warp][16-row tile]: the 4 pair tiles of one
+  // stage (128 rows x one k-tile) are contiguous, so a stage is one bulk copy.
+  const int pair = rt16 >> 1;
+  uint8_t* out = tiles + (((((size_t)(pair >> 2) * k_tiles + kt) * kGemvWarps + (pair & 3)) * 2) + (rt16 & 1)) * TB;
   const int r0 = rt16 * 16;
   const int kbase = kt * KT;
   if (fmt == WF_BF16) {
