@@ -210,6 +210,154 @@ def cpu_baseline_block(budget_s: float = 20.0):
                       f"full head: {v * 1e3:.1f} ms per verify"}
 
 
+# ---- the other BASELINE.json configs (opt-in: --config cfg1|cfg4|cfg5) ----------
+CFG1_TARGET = dict(arch="qwen2", n_layers=24, hidden=896, n_heads=14, n_kv_heads=2, ffn=4864, vocab=151936,
+                   rope_theta=1e6, eps=1e-6)
+CFG1_DRAFT = dict(CFG1_TARGET, n_layers=2)
+CFG4_TARGET = dict(arch="llama", n_layers=32, hidden=4096, n_heads=32, n_kv_heads=8, ffn=14336, vocab=128256,
+                   rope_theta=5e5, eps=1e-5)
+CFG5_TARGET = dict(arch="qwen2", n_layers=28, hidden=3584, n_heads=28, n_kv_heads=4, ffn=18944, vocab=152064,
+                   rope_theta=1e6, eps=1e-6)
+
+
+def _event_ms(stream, fn, steps):
+    import torch
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for i in range(steps):
+        fn(i)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1)
+
+
+def random_tree(rng, root, n, depth, topk, vocab):
+    """configs[3] draft tree: BFS levels, each node's parent drawn from the
+    previous level, at most `topk` children per parent, `depth` levels below
+    the root, `n` nodes in all (root included); parent < child."""
+    nodes = [(-1, root)]
+    levels = [[0]]
+    per_level = [(n - 1) // depth + (1 if i < (n - 1) % depth else 0) for i in range(depth)]
+    for d in range(depth):
+        cur, kids = [], {}
+        for _ in range(per_level[d]):
+            choices = [p for p in levels[-1] if kids.get(p, 0) < topk]
+            p = int(rng.choice(choices))
+            kids[p] = kids.get(p, 0) + 1
+            nodes.append((p, int(rng.integers(0, vocab))))
+            cur.append(len(nodes) - 1)
+        levels.append(cur)
+    return nodes
+
+
+def run_config(args, ws, rank, local, dist):
+    import torch
+    pkg = importlib.import_module("abyo-speculate_b200")
+    sd = importlib.import_module("abyo-speculate_b200.sd_loop")
+    torch.cuda.set_device(local)
+    rng = np.random.default_rng(17)
+    out = {"impl": "b200", "n_gpus": ws, "data": "synthetic", "higher_is_better": True, "steps": args.steps,
+           "warmup": args.warmup}
+    if args.config == "cfg1":
+        tgt = pkg.B200Decoder.synthetic(**CFG1_TARGET, quant_mix="Q4_K_M", seed=11, device=local, max_ctx=1024)
+        drf = pkg.B200Decoder.synthetic(**CFG1_DRAFT, quant_mix="Q4_K_M", seed=12, device=local, max_ctx=1024)
+        prompt = rng.integers(0, CFG1_TARGET["vocab"], size=128).tolist()
+        for _ in range(args.warmup):
+            sd.vanilla_greedy_generate(tgt, drf, prompt, 16, K_DRAFT)
+        t0 = time.perf_counter()
+        n_tok = 0
+        for _ in range(max(1, args.steps // 50)):
+            toks, acc = sd.vanilla_greedy_generate(tgt, drf, prompt, 128, K_DRAFT)
+            n_tok += len(toks)
+        el = time.perf_counter() - t0
+        tgt.rollback_to(128)
+        stream = torch.cuda.ExternalStream(tgt.cuda_stream(), device=f"cuda:{local}")
+        dr = rng.integers(0, CFG1_TARGET["vocab"], size=(args.steps + 8, K_DRAFT)).astype(np.uint32)
+
+        def verify(i):
+            tgt.verify_greedy(dr[i])
+            tgt.rollback_to(128)
+        for i in range(args.warmup):
+            verify(i)
+        ms = _event_ms(stream, verify, args.steps)
+        out.update({"metric": "vanilla SD greedy tok/s, Qwen2.5-0.5B-shaped Q4_K_M target + 2-layer draft, k=4",
+                    "value": round(n_tok / el, 2), "unit": "tok/s",
+                    "config": {"workload": "configs[0]: prompt 128 uniform ids, 128 new tokens, greedy, batch 1",
+                               "k": K_DRAFT, "quant_mix": "Q4_K_M (Q8_0 where K=896 is not a multiple of 256)"},
+                    "verify_us": round(ms / args.steps * 1e3, 2),
+                    "note": "wall clock per generation incl. prefill of target and draft"})
+    elif args.config == "cfg4":
+        T = 4096
+        tgt = pkg.B200Decoder.synthetic(**CFG4_TARGET, quant_mix="BF16", seed=13, device=local, max_ctx=T + 128,
+                                        rope_half=True)
+        prompt = rng.integers(0, CFG4_TARGET["vocab"], size=T).tolist()
+        tgt.observe(prompt)
+        trees = []
+        for i in range(args.steps + args.warmup):
+            nodes = random_tree(rng, prompt[-1], 60, 6, 10, CFG4_TARGET["vocab"])
+            trees.append(pkg.DraftTree.from_parent_table([(max(p, 0), t) for p, t in nodes]))
+        stream = torch.cuda.ExternalStream(tgt.cuda_stream(), device=f"cuda:{local}")
+        acc_len = []
+
+        def step(i):
+            tr = trees[i]
+            best, bonus = tgt.verify_tree_greedy(tr)
+            # a random root-to-leaf path stands for the accepted one (configs[3])
+            par = tr.parents()
+            leaf = int(rng.integers(1, len(par)))
+            path = [leaf]
+            while par[path[-1]] > 0:
+                path.append(par[path[-1]])
+            path = [0] + path[::-1]
+            tgt.commit_tree_path(tr, path)
+            acc_len.append(len(path))
+            tgt.rollback_to(T)
+        for i in range(args.warmup):
+            step(i)
+        acc_len.clear()
+        ms = _event_ms(stream, lambda i: step(args.warmup + i), args.steps)
+        out.update({"metric": "EAGLE tree verify steps/s (60-node tree, tree forward + device argmax + accepted-path KV reorder)",
+                    "value": round(args.steps / (ms / 1e3), 3), "unit": "tree verify steps/s",
+                    "ms_per_step": round(ms / args.steps, 3), "dtype": "bf16",
+                    "config": {"workload": "configs[3]: Llama-3.1-8B-shaped BF16 target, 60-node tree (depth 6, "
+                                           "top-k <= 10), 4096-token KV, random accepted root-to-leaf path",
+                               "mean_path_len": round(float(np.mean(acc_len)), 2)}})
+    elif args.config == "cfg5":
+        T = 16384
+        k = 8
+        tp = args.tp
+        res = {}
+        for mix in ("Q5_K", "Q8_0"):
+            dec = pkg.B200Decoder.synthetic(**CFG5_TARGET, quant_mix=mix, seed=15, device=local, max_ctx=T + 64,
+                                            rope_half=True, tp_rank=rank % tp, tp_size=tp)
+            if tp > 1:
+                dec.tp_connect_group(tp_groups(dist, ws, tp))
+            prng = np.random.default_rng(19 + rank // tp)
+            prompt = prng.integers(0, CFG5_TARGET["vocab"], size=T).tolist()
+            dec.observe(prompt)
+            dr = prng.integers(0, CFG5_TARGET["vocab"], size=(args.steps + args.warmup, k)).astype(np.uint32)
+            stream = torch.cuda.ExternalStream(dec.cuda_stream(), device=f"cuda:{local}")
+
+            def verify(i, dec=dec, dr=dr):
+                dec.verify_greedy(dr[i])
+                dec.rollback_to(T)
+            for i in range(args.warmup):
+                verify(i)
+            barrier(dist)
+            ms = max_over_ranks(dist, _event_ms(stream, lambda i: verify(args.warmup + i), args.steps))
+            res[mix] = {"verify_us": round(ms / args.steps * 1e3, 2),
+                        "verify_steps_per_s": round((ws // tp) * args.steps / (ms / 1e3), 3),
+                        "weight_gb_per_rank": round(dec.weight_bytes() / 1e9, 3)}
+            dec.close()
+        out.update({"metric": "verify steps/s, Qwen2.5-7B-shaped target, k=8 (9 rows), 16384-token KV",
+                    "value": res["Q5_K"]["verify_steps_per_s"], "unit": "verify steps/s", "variants": res,
+                    "config": {"workload": "configs[4]: Qwen2.5-7B-shaped Q5_K and Q8_0 verify, k=8, 16K KV",
+                               "parallelism": f"tp{tp} x {ws // tp} replicas" if tp > 1 else f"replicas x{ws}"}})
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
 def run_reference(args, ws, rank):
     if rank != 0:
         return
@@ -483,6 +631,9 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--reference-budget", type=float, default=120.0)
+    ap.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg4", "cfg5"],
+                    help="BASELINE.json config: cfg2 (default, the headline line), cfg1 = configs[0] SD loop, "
+                         "cfg4 = configs[3] BF16 tree verify, cfg5 = configs[4] Qwen2.5-7B k=8 16K KV")
     ap.add_argument("--no-sd", action="store_true", help="skip the greedy SD-loop tokens/s measurement")
     ap.add_argument("--no-microbench", action="store_true", help="skip the dequant-matmul microbench (configs[2])")
     ap.add_argument("--tp", type=int, default=1,
@@ -498,7 +649,10 @@ def main():
         return
     dist = init_dist(ws)
     try:
-        run_b200(args, ws, rank, local, dist)
+        if args.config != "cfg2":
+            run_config(args, ws, rank, local, dist)
+        else:
+            run_b200(args, ws, rank, local, dist)
     finally:
         if dist is not None:
             dist.destroy_process_group()
