@@ -26,8 +26,11 @@ TP_SPECS = {
                         rope_theta=1e6, eps=1e-6, quant_mix="Q8_0"),
     "llama_tp4": dict(arch="llama", n_layers=2, hidden=2048, n_heads=16, n_kv_heads=4, ffn=4096, vocab=1024,
                       rope_theta=5e5, eps=1e-5, quant_mix="Q4_K_M"),
+    # Llama-3-8B's head layout (32 q / 8 kv heads of 128): 8 ranks hold one kv head each.
+    "llama_tp8": dict(arch="llama", n_layers=2, hidden=4096, n_heads=32, n_kv_heads=8, ffn=4096, vocab=1024,
+                      rope_theta=5e5, eps=1e-5, quant_mix="Q4_K_M"),
 }
-CASES = [("llama_tp", 2), ("qwen_tp_q80", 2), ("llama_tp4", 2), ("llama_tp4", 4)]
+CASES = [("llama_tp", 2), ("qwen_tp_q80", 2), ("llama_tp4", 2), ("llama_tp4", 4), ("llama_tp8", 8)]
 
 
 def _prompt(vocab, n, seed):
