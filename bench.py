@@ -617,7 +617,7 @@ def run_b200(args, ws, rank, local, dist):
         "gpu_launches": launches_per_step * args.steps,
         "clocks": sampler.summary(),
     }
-    if not args.no_cpu_baseline:
+    if not args.no_cpu_baseline and ws == 1:  # rank 0 at N=1 only
         out["cpu_baseline"] = cpu_baseline_block(args.cpu_budget)
     print(json.dumps(out), flush=True)
 
