@@ -262,6 +262,14 @@ cudaError_t launch_rejection(float* rows, const float* q, float* r, const RejSte
 cudaError_t launch_row_argmax(const float* logits, int rows, int V, int* out_idx, float* out_val,
                               unsigned long long* slots, int* counters, cudaStream_t s);
 
+// Per-row top-k (k <= kMaxTopK): ids[rows][k], vals[rows][k] in descending
+// value order, ties by ascending index (methods/medusa.rs:477-487); part:
+// scratch of rows * kTopKMaxChunks * k keys.  V <= kTopKMaxChunks * 4096.
+constexpr int kMaxTopK = 64;
+constexpr int kTopKMaxChunks = 64;
+cudaError_t launch_row_topk(const float* logits, int rows, int V, int k, unsigned long long* part, int* ids,
+                            float* vals, cudaStream_t s);
+
 // ---- synthetic weight generation (seeded N(0, sigma) then quantized) -------
 cudaError_t launch_synth_quant(uint8_t* raw, int fmt, int rows, int K, uint64_t seed, float sigma,
                                int row_offset, cudaStream_t s);

@@ -161,9 +161,11 @@ __global__ void final_hidden_kernel(const float* h, const float* ss, int groups,
 // or, on a tie, a smaller index) and merges it with atomicMax; the CTA that
 // arrives last for a row decodes the key and clears the slot and counter for
 // the next call.  The max of a set of keys does not depend on arrival order.
-// NaN entries are skipped; a row of only NaN yields index 0.
+// NaN entries are skipped; a row of only NaN yields index 0.  -0.0 keys as
+// +0.0 (the reference's `>` treats them as equal, so the lower index wins).
 SPEC_DEV unsigned long long argmax_key(float v, int i) {
   unsigned u = __float_as_uint(v);
+  if (u == 0x80000000u) u = 0u;
   u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
   return ((unsigned long long)u << 32) | (unsigned)(~i);
 }
@@ -203,6 +205,78 @@ __global__ void __launch_bounds__(256) row_argmax_kernel(const float* logits, in
       out_idx[row] = k ? (int)(~(unsigned)(k & 0xffffffffull)) : 0;
       if (out_val) out_val[row] = k ? argmax_key_value(k) : -INFINITY;
     }
+  }
+}
+
+// ---- top-k over a logits row (methods/medusa.rs:477-487) ------------------
+// Values descending, ties by ascending index: exactly the order of the
+// argmax keys above, so the top k of a row are its k largest keys (NaN
+// entries key as 0, below every value).  Stage 1: each CTA stages a chunk's
+// keys in shared memory and extracts its k largest in k rounds of "largest
+// key below the previous one"; stage 2 does the same over the chunks'
+// candidates.  Keys are unique (the index is part of them), so each round
+// is one block-wide max.
+constexpr int kTopKChunk = 4096;
+
+SPEC_DEV unsigned long long block_max_u64(unsigned long long v, unsigned long long* sb) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = max(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  if (lane == 0) sb[warp] = v;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < (int)(blockDim.x >> 5); ++w) v = max(v, sb[w]);
+    sb[0] = v;
+  }
+  __syncthreads();
+  v = sb[0];
+  __syncthreads();
+  return v;
+}
+
+__global__ void __launch_bounds__(256) topk_chunk_kernel(const float* logits, int V, int k, unsigned long long* part) {
+  __shared__ unsigned long long keys[kTopKChunk];
+  __shared__ unsigned long long sb[8];
+  const int row = blockIdx.y, chunk = blockIdx.x;
+  const int start = chunk * kTopKChunk, n = min(kTopKChunk, V - start);
+  const float* x = logits + (size_t)row * V + start;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const float v = __ldg(x + i);
+    keys[i] = v == v ? argmax_key(v, start + i) : 0ull;
+  }
+  __syncthreads();
+  unsigned long long* out = part + ((size_t)row * gridDim.x + chunk) * k;
+  unsigned long long prev = ~0ull;
+  for (int r = 0; r < k; ++r) {
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const unsigned long long kk = keys[i];
+      if (kk < prev && kk > best) best = kk;
+    }
+    best = block_max_u64(best, sb);
+    if (threadIdx.x == 0) out[r] = best;
+    prev = best;
+  }
+}
+
+__global__ void __launch_bounds__(256) topk_merge_kernel(const unsigned long long* part, int chunks, int k,
+                                                         int* ids, float* vals) {
+  __shared__ unsigned long long sb[8];
+  const int row = blockIdx.x, n = chunks * k;
+  const unsigned long long* c = part + (size_t)row * n;
+  unsigned long long prev = ~0ull;
+  for (int r = 0; r < k; ++r) {
+    unsigned long long best = 0ull;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const unsigned long long kk = c[i];
+      if (kk < prev && kk > best) best = kk;
+    }
+    best = block_max_u64(best, sb);
+    if (threadIdx.x == 0) {
+      ids[row * k + r] = best ? (int)(~(unsigned)(best & 0xffffffffull)) : -1;
+      vals[row * k + r] = best ? argmax_key_value(best) : __int_as_float(0x7fc00000);
+    }
+    prev = best;
   }
 }
 
@@ -414,6 +488,18 @@ cudaError_t launch_row_argmax(const float* logits, int rows, int V, int* out_idx
   const int per_cta = 2048;
   row_argmax_kernel<<<dim3((V + per_cta - 1) / per_cta, rows), 256, 0, s>>>(logits, V, per_cta, slots, counters,
                                                                            out_idx, out_val);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_row_topk(const float* logits, int rows, int V, int k, unsigned long long* part, int* ids,
+                            float* vals, cudaStream_t s) {
+  if (rows < 1 || rows > kMaxRows || V < 1 || k < 1 || k > kMaxTopK || k > V) return cudaErrorInvalidValue;
+  const int chunks = (V + kTopKChunk - 1) / kTopKChunk;
+  if (chunks > kTopKMaxChunks) return cudaErrorInvalidValue;
+  topk_chunk_kernel<<<dim3(chunks, rows), 256, 0, s>>>(logits, V, k, part);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  topk_merge_kernel<<<rows, 256, 0, s>>>(part, chunks, k, ids, vals);
   return cudaGetLastError();
 }
 

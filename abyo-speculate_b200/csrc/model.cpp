@@ -145,6 +145,9 @@ struct spec_model {
   void* kv_tmp = nullptr;
   int* argmax_dev = nullptr;
   unsigned long long* argmax_slots = nullptr;  // row argmax scratch (self-clearing)
+  unsigned long long* topk_part = nullptr;     // row top-k scratch (allocated on first use)
+  int* topk_ids = nullptr;
+  float* topk_vals = nullptr;
   float* rej_q = nullptr;                      // [kMaxRows-1][V] draft probabilities
   float* rej_q_host = nullptr;                 // pinned staging for rej_q
   float* rej_r = nullptr;                      // [V] adjusted distribution
@@ -1872,6 +1875,44 @@ int spec_apply_lm_head(spec_model* m, const float* hidden, int rows, float* out)
       e = cudaMemcpyAsync(out + (size_t)r0 * V, m->logits, (size_t)M * V * 4, cudaMemcpyDeviceToHost, m->stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
     if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "apply_lm_head"));
+  }
+  return SPEC_OK;
+}
+
+int spec_apply_lm_head_topk(spec_model* m, const float* hidden, int rows, int k, int32_t* ids_out, float* vals_out) {
+  if (!m || !hidden || !ids_out || rows < 0) return SPEC_ERR_INVALID;
+  if (k < 1 || k > kMaxTopK || k > m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "top-k size out of range");
+  cudaSetDevice(m->device);
+  const int H = m->cfg.hidden, V = m->cfg.vocab;
+  cudaError_t e = cudaSuccess;
+  if (!m->topk_part) {
+    e = m->dalloc(&m->topk_part, (size_t)kMaxRows * kTopKMaxChunks * kMaxTopK * 8);
+    if (e == cudaSuccess) e = m->dalloc(&m->topk_ids, (size_t)kMaxRows * kMaxTopK * 4);
+    if (e == cudaSuccess) e = m->dalloc(&m->topk_vals, (size_t)kMaxRows * kMaxTopK * 4);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, "top-k scratch"));
+  }
+  for (int r0 = 0; r0 < rows; r0 += kMaxRows) {
+    const int M = std::min(kMaxRows, rows - r0);
+    const int nt = nt_for_rows(M);
+    e = cudaMemcpyAsync(m->op_in, hidden + (size_t)r0 * H, (size_t)M * H * 4, cudaMemcpyHostToDevice, m->stream);
+    if (e == cudaSuccess)
+      e = launch_make_operand(m->op_in, M, H, nt, m->xa, m->xa16, m->xa32, m->cfg.bf16 ? 1 : 0, m->stream);
+    QmvParams p = base_params(m, m->lm, M);
+    p.xfrag = m->xa;
+    p.xsum16 = m->xa16;
+    p.xsum32 = m->xa32;
+    p.epi = EPI_STORE;
+    p.out = m->logits;
+    p.ld_out = V;
+    if (e == cudaSuccess) e = enqueue_single(m, p, m->stream);
+    if (e == cudaSuccess) e = launch_row_topk(m->logits, M, V, k, m->topk_part, m->topk_ids, m->topk_vals, m->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(ids_out + (size_t)r0 * k, m->topk_ids, (size_t)M * k * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess && vals_out)
+      e = cudaMemcpyAsync(vals_out + (size_t)r0 * k, m->topk_vals, (size_t)M * k * 4, cudaMemcpyDeviceToHost,
+                          m->stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "apply_lm_head_topk"));
   }
   return SPEC_OK;
 }

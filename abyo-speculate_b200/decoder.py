@@ -207,6 +207,18 @@ class B200Decoder:
                                                  _ptr(out, ctypes.c_float)))
         return out.reshape(*lead, self._vocab)
 
+    def apply_lm_head_topk(self, hidden: np.ndarray, k: int) -> Tuple[np.ndarray, np.ndarray]:
+        """apply_lm_head then medusa.rs:477-487 top_k_indices, the top-k on
+        the device.  Returns (ids [..., k] int32, logits [..., k] f32)."""
+        h = np.ascontiguousarray(np.asarray(hidden, dtype=np.float32))
+        lead = h.shape[:-1]
+        h2 = h.reshape(-1, self._hidden)
+        ids = np.empty((h2.shape[0], k), dtype=np.int32)
+        vals = np.empty((h2.shape[0], k), dtype=np.float32)
+        self._check(self._lib.spec_apply_lm_head_topk(self._h, _ptr(h2, ctypes.c_float), h2.shape[0], k,
+                                                      _ptr(ids, ctypes.c_int32), _ptr(vals, ctypes.c_float)))
+        return ids.reshape(*lead, k), vals.reshape(*lead, k)
+
     def embed_tokens(self, ids: Sequence[int]) -> np.ndarray:
         a = _u32(ids)
         out = np.empty((a.size, self._hidden), dtype=np.float32)

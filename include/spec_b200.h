@@ -153,6 +153,13 @@ int spec_observe_returning_last_hidden(spec_model* m, const uint32_t* ids, int n
 /* TreeDecoder::apply_lm_head (mod.rs:146-156; quantized_llama.rs:112-121):
  * rows x hidden f32 -> rows x V f32. */
 int spec_apply_lm_head(spec_model* m, const float* hidden, int rows, float* out);
+/* TreeDecoder::apply_lm_head followed by methods::medusa::top_k_indices
+ * (medusa.rs:477-487), as the EAGLE draft loop uses them (eagle.rs:549-566),
+ * with the top-k on the device: ids_out[rows][k] (and, when non-NULL,
+ * vals_out[rows][k]) in descending logit order, ties by ascending index.
+ * 1 <= k <= 64.  Only rows x k ids (and values) cross to the host instead of
+ * rows x V logits.  NaN logits rank below every number. */
+int spec_apply_lm_head_topk(spec_model* m, const float* hidden, int rows, int k, int32_t* ids_out, float* vals_out);
 /* TreeDecoder::embed_tokens (mod.rs:184-194; quantized_llama_local.rs:328-330). */
 int spec_embed_tokens(spec_model* m, const uint32_t* ids, int n, float* out);
 /* TreeDecoder::last_hidden_states_multi (mod.rs:158-175; quantized_llama.rs:221-249):

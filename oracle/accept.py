@@ -40,6 +40,19 @@ def argmax_first(row: np.ndarray) -> int:
     return bi
 
 
+def top_k_indices(logits, k: int):
+    """methods/medusa.rs:477-487: indices sorted by value descending, ties by
+    ascending index (a stable sort on the value), the first k.  NaN entries
+    rank last here (the reference's comparator calls them equal to
+    everything; the backend documents them as lowest)."""
+    r = np.asarray(logits, dtype=np.float32)
+    v = np.where(np.isnan(r), -np.inf, r).astype(np.float64)
+    v = np.where(v == 0.0, 0.0, v)  # -0.0 equals +0.0
+    nan_last = np.isnan(r).astype(np.int8)
+    order = np.lexsort((np.arange(r.size), -v, nan_last))
+    return [int(i) for i in order[:min(k, r.size)]]
+
+
 def argmax_first_fast(row: np.ndarray) -> int:
     r = np.asarray(row, dtype=np.float32)
     finite = ~np.isnan(r)

@@ -90,3 +90,11 @@ def test_greedy_tree_accept_first_longest(accept):
     rows2 = np.zeros((5, 10), dtype=np.float32)  # all ties -> argmax 0, nothing accepted
     best, bonus = accept.greedy_tree_accept(tokens, parents, rows2)
     assert best == [0] and bonus == 0
+
+
+def test_top_k_indices_order(accept):
+    """medusa.rs:477-487: value descending, ties by ascending index."""
+    row = np.array([0.5, 2.0, 2.0, -1.0, 2.0, 0.5, -0.0, 0.0, np.nan], dtype=np.float32)
+    assert accept.top_k_indices(row, 5) == [1, 2, 4, 0, 5]
+    assert accept.top_k_indices(row, 9) == [1, 2, 4, 0, 5, 6, 7, 3, 8]
+    assert accept.top_k_indices(row, 20) == [1, 2, 4, 0, 5, 6, 7, 3, 8]

@@ -277,3 +277,23 @@ def test_lazy_observe_matches_eager(pkg, oracle, tiny_gguf):
     assert np.abs(h - rh[-1]).max() <= TOL
     assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
     assert np.abs(dec.next_logits() - ref.next_logits()).max() <= TOL
+
+
+def test_apply_lm_head_topk(pkg, accept, tiny_gguf):
+    """Device top-k after the LM head == medusa.rs top_k_indices over the
+    same logits rows (ids and values), > 64 rows (chunked), all-tie rows."""
+    dec = pkg.B200Decoder.from_gguf(tiny_gguf("llama_q4km"), max_ctx=128)
+    rng = np.random.default_rng(31)
+    hid = rng.standard_normal((70, dec.hidden_size())).astype(np.float32)
+    hid[3] = 0.0  # every logit equal: ties resolve by ascending index
+    full = dec.apply_lm_head(hid)
+    for k in (1, 10, 64):
+        ids, vals = dec.apply_lm_head_topk(hid, k)
+        assert ids.shape == (70, k)
+        for r in range(70):
+            want = accept.top_k_indices(full[r], k)
+            assert ids[r].tolist() == want, (k, r)
+            assert np.array_equal(vals[r], full[r][want])
+    assert dec.apply_lm_head_topk(hid[3:4], 5)[0].tolist() == [[0, 1, 2, 3, 4]]
+    with pytest.raises(pkg.SamplingError):
+        dec.apply_lm_head_topk(hid[:1], 65)
