@@ -26,7 +26,9 @@ enum DevError : unsigned {
 // The error word is err[0]; a wait that gives up also records where, once:
 // err[1] = site | op << 8 | cta << 16, err[2] = stage / ring position,
 // err[3] = the counter value it last saw.
-enum WaitSite : unsigned { WAIT_CONSUMER_FULL = 1, WAIT_CONSUMER_DEP = 2, WAIT_PRODUCER_IDLE = 3, WAIT_TP_PEERS = 4 };
+// (Site 2 was the consumers' per-op dependency wait, which per-group flags
+// made unnecessary; the number stays retired.)
+enum WaitSite : unsigned { WAIT_CONSUMER_FULL = 1, WAIT_PRODUCER_IDLE = 3, WAIT_TP_PEERS = 4 };
 
 // GGML type ids (public GGUF specification) of the weight formats handled.
 enum WFmt : int { WF_F32 = 0, WF_F16 = 1, WF_Q8_0 = 8, WF_Q4_K = 12, WF_Q5_K = 13, WF_Q6_K = 14, WF_BF16 = 30 };

@@ -11,8 +11,9 @@
 //    m16n8k16 A-fragment order: lane (g,t) finds, in one 32-bit word per
 //    k-step, the 8 codes of rows g / g+8 at columns 2t, 2t+1, 2t+8, 2t+9.
 //    Two 16-row tiles form a "pair tile" (32 rows x KT columns); one warp owns
-//    a 32-row slice and streams its pair tiles with TMA bulk copies
-//    (cp.async.bulk -> shared, mbarrier completion) through a 2-3 stage ring.
+//    a 32-row slice.  Tiles are laid out [group][k-tile][warp], so one stage
+//    (128 rows x one k-tile) is a single TMA bulk copy (cp.async.bulk ->
+//    shared, mbarrier completion, L2 evict-first) into a 2-3 stage ring.
 //  * Codes become f16 with one LOP3 each (magic 0x6400: value = 1024 + q),
 //    feed mma.sync with the activation fragments, and the accumulator is
 //    seeded with -offset * (sum of the activations of that sub-block), so the
@@ -27,6 +28,9 @@
 //    piece adds them in chunk order, then runs the fused epilogue.  The cut
 //    depends only on the matrix, so row r's result is bit-identical for any
 //    M (batched == sequential).
+//  * Ops of one launch chain through per-group completion flags: a stage's
+//    activations are fetched once the groups of the previous op that produce
+//    its K range are done, so an op starts while the previous one finishes.
 //  * Programmatic dependent launch: a CTA issues its first weight copies, then
 //    waits for the previous kernel (griddepcontrol.wait) before touching
 //    activations, so weight streaming overlaps the predecessor's tail.
@@ -910,13 +914,6 @@ SPEC_DEV int ld_acquire(const int* p) {
   return v;
 }
 SPEC_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
-
-SPEC_DEV bool op_inputs_ready(const FwdParams& P, int op) {
-  const int dep = P.ops[op].dep;
-  if (dep < 0) return true;
-  const QmvParams& d = P.ops[dep].q;
-  return ld_acquire(P.done + dep) >= d.seg[0].groups + d.seg[1].groups;
-}
 
 template <int SET, int NT>
 SPEC_DEV void process_any(int fmt, const uint8_t* tp, const uint8_t* xs, float* scr, int lane,
