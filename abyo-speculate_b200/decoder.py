@@ -315,8 +315,16 @@ class QWeight:
     """Standalone dequant-matmul (candle ``QMatMul::forward``) over device buffers."""
 
     def __init__(self, ggml_type: int, blocks: np.ndarray, n_rows: int, k_cols: int, device: int = 0):
+        from .gguf_synth import BLOCK_BYTES, BLOCK_ELEMS
         self._lib = _lib.load()
         b = np.ascontiguousarray(blocks)
+        # The C entry point reads n_rows x (k_cols / block) blocks from the
+        # host pointer; check the buffer holds them before handing it over.
+        if int(ggml_type) in BLOCK_ELEMS and k_cols % BLOCK_ELEMS[int(ggml_type)] == 0:
+            need = n_rows * (k_cols // BLOCK_ELEMS[int(ggml_type)]) * BLOCK_BYTES[int(ggml_type)]
+            if b.nbytes < need:
+                raise _lib.SamplingError(_lib.SPEC_ERR_INVALID,
+                                         f"blocks hold {b.nbytes} bytes, {n_rows} x {k_cols} needs {need}")
         h = ctypes.c_void_p()
         _lib.check(self._lib.spec_qweight_upload(int(ggml_type), b.ctypes.data, n_rows, k_cols, device,
                                                  ctypes.byref(h)), None)

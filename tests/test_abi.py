@@ -44,3 +44,13 @@ def test_load_without_gpu_fails_cleanly(pkg):
         assert e.code in (4, 5)
     else:
         raise AssertionError("expected an error")
+
+
+def test_qweight_rejects_short_host_buffer(pkg):
+    """The C entry point reads n_rows x K/256 blocks from the host pointer;
+    the Python wrapper refuses a buffer that does not hold them (no device
+    call is made)."""
+    import numpy as np
+    import pytest
+    with pytest.raises(pkg.SamplingError):
+        pkg.QWeight(12, np.zeros((10, 144 * 16), np.uint8), 11, 4096)
