@@ -108,6 +108,8 @@ SIGNATURES = [
     ("spec_last_hidden_state", ctypes.c_int, [ctypes.c_void_p, c_f32_p]),
     ("spec_observe_returning_last_hidden", ctypes.c_int, [ctypes.c_void_p, c_u32_p, ctypes.c_int, c_f32_p]),
     ("spec_apply_lm_head", ctypes.c_int, [ctypes.c_void_p, c_f32_p, ctypes.c_int, c_f32_p]),
+    ("spec_sd_greedy_round", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_int)]),
     ("spec_apply_lm_head_topk", ctypes.c_int,
      [ctypes.c_void_p, c_f32_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_int32), c_f32_p]),
     ("spec_embed_tokens", ctypes.c_int, [ctypes.c_void_p, c_u32_p, ctypes.c_int, c_f32_p]),

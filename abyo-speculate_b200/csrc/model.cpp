@@ -2028,6 +2028,43 @@ int spec_verify_greedy(spec_model* m, const uint32_t* drafts, int k, int* n_acce
   return SPEC_OK;
 }
 
+// One greedy vanilla SD round (methods/vanilla.rs:285-369 at temperature 0)
+// over two handles, natively: k draft steps (device argmax of the draft's
+// next-token row, then a lazy observe), one target verify with the device
+// accept walk, then both handles roll back to the accepted prefix and
+// observe the token that follows it.  Same calls, same order and same
+// results as issuing them one by one through the ABI.
+int spec_sd_greedy_round(spec_model* target, spec_model* draft, int k, uint32_t* commits_out, int* n_out) {
+  if (!target || !draft || !commits_out || !n_out || k < 0 || k + 1 > kMaxRows) return SPEC_ERR_INVALID;
+  if (target->history.size() != draft->history.size())
+    return target->fail(SPEC_ERR_INVALID, "target and draft histories differ in length");
+  const int pre = (int)target->history.size();
+  uint32_t drafts[kMaxRows];
+  for (int i = 0; i < k; ++i) {
+    int acc;
+    uint32_t nxt;
+    int rc = spec_verify_greedy(draft, nullptr, 0, &acc, &nxt, nullptr);
+    if (rc == SPEC_OK) rc = spec_observe(draft, &nxt, 1);
+    if (rc != SPEC_OK) {
+      if (draft != target) target->err = draft->err;
+      return rc;
+    }
+    drafts[i] = nxt;
+  }
+  int n_acc = 0;
+  uint32_t bonus = 0;
+  int rc = spec_verify_greedy(target, drafts, k, &n_acc, &bonus, nullptr);
+  if (rc == SPEC_OK) rc = spec_rollback_to(target, pre + n_acc);
+  if (rc == SPEC_OK) rc = spec_observe(target, &bonus, 1);
+  if (rc == SPEC_OK) rc = spec_rollback_to(draft, pre + n_acc);
+  if (rc == SPEC_OK) rc = spec_observe(draft, &bonus, 1);
+  if (rc != SPEC_OK) return rc;
+  for (int i = 0; i < n_acc; ++i) commits_out[i] = drafts[i];
+  commits_out[n_acc] = bonus;
+  *n_out = n_acc + 1;
+  return SPEC_OK;
+}
+
 int spec_verify_rejection(spec_model* m, const uint32_t* drafts, int k, const float* draft_probs,
                           float temperature, const float* uniforms, int n_uniforms, int budget, uint32_t* commits,
                           int* n_commits, int* n_uniforms_used) {

@@ -11,7 +11,9 @@ and argmax:
           token that follows it                         vanilla.rs:358-362
 
 With lazy observe the post-round observes cost no forward; the next round's
-draft step and verify compute the pending token's KV row.
+draft step and verify compute the pending token's KV row.  The same round is
+also one native call (spec_sd_greedy_round), the default in
+vanilla_greedy_generate.
 """
 
 from __future__ import annotations
@@ -24,6 +26,15 @@ def greedy_next(dec) -> int:
     zero drafts: one forward of the pending token plus a device argmax)."""
     _, nxt, _ = dec.verify_greedy([])
     return int(nxt)
+
+
+def vanilla_greedy_round_native(target, draft, k: int) -> List[int]:
+    """The same round as one C call (spec_sd_greedy_round)."""
+    import ctypes
+    out = (ctypes.c_uint32 * (k + 1))()
+    n = ctypes.c_int()
+    target._check(target._lib.spec_sd_greedy_round(target._h, draft._h, k, out, ctypes.byref(n)))
+    return [int(out[i]) for i in range(n.value)]
 
 
 def vanilla_greedy_round(target, draft, k: int) -> List[int]:
@@ -44,7 +55,7 @@ def vanilla_greedy_round(target, draft, k: int) -> List[int]:
 
 
 def vanilla_greedy_generate(target, draft, prompt: Sequence[int], n_new: int, k: int,
-                            observe_prompt: bool = True) -> Tuple[List[int], List[int]]:
+                            observe_prompt: bool = True, native: bool = True) -> Tuple[List[int], List[int]]:
     """Generates at least n_new tokens; returns (tokens, accepted drafts per round)."""
     if observe_prompt:
         target.reset()
@@ -54,7 +65,7 @@ def vanilla_greedy_generate(target, draft, prompt: Sequence[int], n_new: int, k:
     out: List[int] = []
     accepted: List[int] = []
     while len(out) < n_new:
-        c = vanilla_greedy_round(target, draft, k)
+        c = (vanilla_greedy_round_native if native else vanilla_greedy_round)(target, draft, k)
         out.extend(c)
         accepted.append(len(c) - 1)
     return out, accepted

@@ -177,6 +177,14 @@ int spec_last_hidden_states_multi(spec_model* m, const int32_t* layers, int n_se
  * when it is non-NULL.  Only (k+1) ints cross to the host. */
 int spec_verify_greedy(spec_model* m, const uint32_t* drafts, int k, int* n_accepted, uint32_t* next_token,
                        int32_t* argmax_out);
+/* One greedy vanilla SD round over a target and a draft handle
+ * (methods/vanilla.rs:285-369 at temperature 0): k draft steps (device
+ * argmax + lazy observe), spec_verify_greedy on the target, then both roll
+ * back to the accepted prefix and observe the next token.  Writes the
+ * committed tokens (accepted drafts, then the next token) to commits_out
+ * (room for k+1) and their count to *n_out.  The histories must be equal on
+ * entry; they are equal again on return. */
+int spec_sd_greedy_round(spec_model* target, spec_model* draft, int k, uint32_t* commits_out, int* n_out);
 /* Greedy tree acceptance of methods/eagle.rs:618-661 over a tree forward
  * (spec_tree_logits_keep_kv semantics, KV kept): best_path receives the
  * accepted node indices root-first (capacity n), *path_len its length, and

@@ -25,14 +25,14 @@ def _greedy_plain(pkg, accept, path, prompt, n):
     return out
 
 
-@pytest.mark.parametrize("k", [1, 4])
-def test_sd_stream_equals_target_greedy(pkg, accept, tiny_gguf, k):
+@pytest.mark.parametrize("k,native", [(1, True), (4, True), (4, False)])
+def test_sd_stream_equals_target_greedy(pkg, accept, tiny_gguf, k, native):
     sd = importlib.import_module("abyo-speculate_b200.sd_loop")
     tpath, dpath = tiny_gguf("llama_q4km"), tiny_gguf("llama_hd128")
     prompt = np.random.default_rng(41).integers(0, 1024, size=24).tolist()
     target = pkg.B200Decoder.from_gguf(tpath, max_ctx=512)
     draft = pkg.B200Decoder.from_gguf(dpath, max_ctx=512)
-    toks, acc = sd.vanilla_greedy_generate(target, draft, prompt, 40, k)
+    toks, acc = sd.vanilla_greedy_generate(target, draft, prompt, 40, k, native=native)
     ref = _greedy_plain(pkg, accept, tpath, prompt, len(toks))
     assert toks == ref
     assert target.history() == prompt + toks and draft.history() == prompt + toks
