@@ -325,8 +325,8 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const __grid_constant
     for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
     const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 16);
     const int w16 = 8 * nt_total;
-    if ((lane & 15) == 0) p.xsum16[(size_t)(k >> 4) * w16 + m] = s16;
-    if (lane == 0) p.xsum32[(size_t)(k >> 5) * w16 + m] = s32;
+    if ((lane & 15) == 0) p.xsum16[(size_t)(k >> 4) * w16 + m] = kXSum16Seed * s16;
+    if (lane == 0) p.xsum32[(size_t)(k >> 5) * w16 + m] = kXSum32Seed * s32;
   }
 }
 

@@ -7,7 +7,9 @@
 //   * residual stream h: f32 [M][H].
 //   * activation operand of every GEMV: f16 (bf16 for BF16 models) values in
 //     m16n8k16 B-fragment order, plus per-16 / per-32 column sums of those
-//     rounded values (xsum16 / xsum32) used to cancel the code offsets.
+//     rounded values, stored already multiplied by the tiles' accumulator
+//     seeds: xsum16 = -1056 x (sum of 16), xsum32 = -1024 x (sum of 32)
+//     (kXSum16Seed / kXSum32Seed), so a tile loads its MMA's C operand.
 //   * KV cache: f16 (bf16 for BF16 models) [layer][kv_head][t][head_dim], K and
 //     V in separate arenas; rows beyond the live length hold finite stale data.
 #pragma once
@@ -52,6 +54,10 @@ constexpr int kGroupRows = 128;        // rows per CTA (4 warps x 32 rows)
 constexpr int kMaxRows = 64;           // max activation rows (M) per forward
 constexpr int kSsStride = 64;          // stride of per-group sum-of-squares slots
 constexpr int kMaxSsGroups = 64;       // hidden size <= 64 * 128
+// Seeds the operand column sums carry (see the layout note at the top):
+// Q6_K codes sit at 1024 + 32 + q, Q4_K/Q5_K codes at 1024 + q.
+constexpr float kXSum16Seed = -1056.f;
+constexpr float kXSum32Seed = -1024.f;
 constexpr int kTpSlot = kMaxRows * 128;  // words per (source rank, group) receive slot
 constexpr int kTpMaxLayers = 256;        // tp_tag = 2 x layer + set stays below 512
 __host__ __device__ inline unsigned tp_flag_of(unsigned epoch, int tag) { return (epoch << 9) | (unsigned)tag; }

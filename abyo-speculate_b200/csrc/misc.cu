@@ -120,8 +120,8 @@ __global__ void __launch_bounds__(128) embed_kernel(const __grid_constant__ Embe
   for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
   const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 16);
   const int w16 = 8 * nt_total;
-  if ((lane & 15) == 0) p.xsum16[(size_t)(n >> 4) * w16 + m] = s16;
-  if (lane == 0) p.xsum32[(size_t)(n >> 5) * w16 + m] = s32;
+  if ((lane & 15) == 0) p.xsum16[(size_t)(n >> 4) * w16 + m] = kXSum16Seed * s16;
+  if (lane == 0) p.xsum32[(size_t)(n >> 5) * w16 + m] = kXSum32Seed * s32;
   __syncthreads();
   if (tid == 0) p.ss_out[grp * kSsStride + m] = s_red[0] + s_red[1] + s_red[2] + s_red[3];
 }
@@ -435,8 +435,8 @@ __global__ void __launch_bounds__(128) make_operand_kernel(const float* x, int K
   for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
   const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 16);
   const int w16 = 8 * nt_total;
-  if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m] = s16;
-  if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = s32;
+  if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m] = kXSum16Seed * s16;
+  if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = kXSum32Seed * s32;
 }
 
 __global__ void synth_vec_kernel(float* out, int n, uint64_t seed, float base, float sigma) {

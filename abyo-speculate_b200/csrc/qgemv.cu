@@ -164,8 +164,9 @@ SPEC_DEV void tile_q45k(const uint8_t* tp, const uint8_t* xs, const float* scr, 
   uint32_t bh[NT], bl[NT];
 #pragma unroll
   for (int nt = 0; nt < NT; ++nt) {
-    const float v0 = reinterpret_cast<const float*>(x32)[(2 * t) * 8 * NT + nt * 8 + g] * (1.f / 64.f);
-    const float v1 = reinterpret_cast<const float*>(x32)[(2 * t + 1) * 8 * NT + nt * 8 + g] * (1.f / 64.f);
+    // x32 holds -1024 x the sums: x (-1/65536) = the sums / 64, exactly.
+    const float v0 = reinterpret_cast<const float*>(x32)[(2 * t) * 8 * NT + nt * 8 + g] * (-1.f / 65536.f);
+    const float v1 = reinterpret_cast<const float*>(x32)[(2 * t + 1) * 8 * NT + nt * 8 + g] * (-1.f / 65536.f);
     const __half h0 = __float2half_rn(v0), h1 = __float2half_rn(v1);
     bh[nt] = pack_half2(h0, h1);
     bl[nt] = pack_half2(__float2half_rn(v0 - __half2float(h0)), __float2half_rn(v1 - __half2float(h1)));
@@ -201,7 +202,7 @@ SPEC_DEV void tile_q45k(const uint8_t* tp, const uint8_t* xs, const float* scr, 
         }
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
-          const float c0 = -1024.f * xsum[sb][nt].x, c1 = -1024.f * xsum[sb][nt].y;
+          const float c0 = xsum[sb][nt].x, c1 = xsum[sb][nt].y;  // already -1024 x the sums
           float d[4];
           mma_f16(d, a[0][0], a[0][1], a[0][2], a[0][3], bq[2 * sb][nt][0], bq[2 * sb][nt][1], c0, c1, c0, c1);
           mma_f16(d, a[1][0], a[1][1], a[1][2], a[1][3], bq[2 * sb + 1][nt][0], bq[2 * sb + 1][nt][1], d[0], d[1],
@@ -271,7 +272,7 @@ SPEC_DEV void tile_q6k(const uint8_t* tp, const uint8_t* xs, const float* scr, i
 #pragma unroll
         for (int nt = 0; nt < NT; ++nt) {
           float d[4];
-          const float c0 = -1056.f * xsum[i][nt].x, c1 = -1056.f * xsum[i][nt].y;
+          const float c0 = xsum[i][nt].x, c1 = xsum[i][nt].y;  // already -1056 x the sums
           mma_f16(d, a[0], a[1], a[2], a[3], bq[i][nt][0], bq[i][nt][1], c0, c1, c0, c1);
           float* ac = acc[rt][nt];
           ac[0] = fmaf(sc.x, d[0], ac[0]);
@@ -313,7 +314,8 @@ SPEC_DEV void tile_q80(const uint8_t* tp, const uint8_t* xs, const float* scr, i
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
         float d[4];
-        const float c0 = -1152.f * xsum[nt].x, c1 = -1152.f * xsum[nt].y;
+        // -1152 x the sums = 1.125 x the stored -1024 x the sums (one rounding, as before)
+        const float c0 = 1.125f * xsum[nt].x, c1 = 1.125f * xsum[nt].y;
         mma_f16(d, a[0][0], a[0][1], a[0][2], a[0][3], bq[0][nt][0], bq[0][nt][1], c0, c1, c0, c1);
         mma_f16(d, a[1][0], a[1][1], a[1][2], a[1][3], bq[1][nt][0], bq[1][nt][1], d[0], d[1], d[2], d[3]);
         float* ac = acc[rt][nt];
@@ -398,8 +400,8 @@ SPEC_DEV void emit_operand_warp(uint32_t* frag, float* xs16, float* xs32, int nt
   for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
   const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 16);
   const int w16 = 8 * nt_total;
-  if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m] = s16;
-  if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = s32;
+  if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m] = kXSum16Seed * s16;
+  if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = kXSum32Seed * s32;
 }
 
 // emit_operand_warp for rows 0..M-1 (M <= 8) of one column at once; the
@@ -426,8 +428,8 @@ SPEC_DEV void emit_rows_warp8(uint32_t* frag, float* xs16, float* xs32, int nt_t
   for (int m = 0; m < 8; ++m) {
     const float s32 = s16[m] + __shfl_xor_sync(0xffffffffu, s16[m], 16);
     if (m < M) {
-      if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m] = s16[m];
-      if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = s32;
+      if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m] = kXSum16Seed * s16[m];
+      if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = kXSum32Seed * s32;
     }
   }
 }
