@@ -70,6 +70,13 @@ c_i32_p = ctypes.POINTER(ctypes.c_int32)
 c_f32_p = ctypes.POINTER(ctypes.c_float)
 
 
+class EagleWeights(ctypes.Structure):
+    """spec_eagle_weights (include/spec_b200.h)."""
+
+    _fields_ = [(n, ctypes.c_void_p) for n in ("fc", "q", "k", "v", "o", "gate", "up", "down", "post_norm")] + [
+        ("rope_theta", ctypes.c_float)]
+
+
 class LoadOpts(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("max_ctx", ctypes.c_int), ("use_graphs", ctypes.c_int),
                 ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int), ("reserved", ctypes.c_int * 3)]
@@ -108,6 +115,11 @@ SIGNATURES = [
     ("spec_last_hidden_state", ctypes.c_int, [ctypes.c_void_p, c_f32_p]),
     ("spec_observe_returning_last_hidden", ctypes.c_int, [ctypes.c_void_p, c_u32_p, ctypes.c_int, c_f32_p]),
     ("spec_apply_lm_head", ctypes.c_int, [ctypes.c_void_p, c_f32_p, ctypes.c_int, c_f32_p]),
+    ("spec_eagle_attach", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    ("spec_eagle_attach_synthetic", ctypes.c_int, [ctypes.c_void_p, ctypes.c_uint64]),
+    ("spec_eagle_draft", ctypes.c_int,
+     [ctypes.c_void_p, c_f32_p, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+      ctypes.POINTER(ctypes.c_int32), c_f32_p]),
     ("spec_sd_greedy_round", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_int)]),
     ("spec_apply_lm_head_topk", ctypes.c_int,

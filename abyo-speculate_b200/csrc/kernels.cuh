@@ -278,6 +278,14 @@ constexpr int kTopKMaxChunks = 64;
 cudaError_t launch_row_topk(const float* logits, int rows, int V, int k, unsigned long long* part, int* ids,
                             float* vals, cudaStream_t s);
 
+// ---- EAGLE draft block glue (methods/eagle.rs:390-427) -------------------
+cudaError_t launch_eagle_concat(const uint8_t* table, int fmt, int H, int V, const int* tok, const float* hidden,
+                                float* x2, unsigned* err, cudaStream_t s);
+cudaError_t launch_eagle_resid_norm(const float* t, const float* h, const float* w, int H, float eps, float* h2,
+                                    float* xn, cudaStream_t s);
+cudaError_t launch_eagle_add(const float* a, const float* b, float* out, int n, cudaStream_t s);
+cudaError_t launch_row_lse(const float* x, int V, float* out, cudaStream_t s);
+
 // ---- synthetic weight generation (seeded N(0, sigma) then quantized) -------
 cudaError_t launch_synth_quant(uint8_t* raw, int fmt, int rows, int K, uint64_t seed, float sigma,
                                int row_offset, cudaStream_t s);

@@ -280,6 +280,91 @@ __global__ void __launch_bounds__(256) topk_merge_kernel(const unsigned long lon
   }
 }
 
+// ---- EAGLE draft block glue (methods/eagle.rs:390-427) ----------------------
+// x2 = concat(hidden, embed(token)) with the token read from device memory
+// (the previous draft step's top-1), so a draft-depth loop runs without host
+// round trips.  grid (2H / 128), 128 threads.
+__global__ void __launch_bounds__(128) eagle_concat_kernel(const uint8_t* table, int fmt, int H, int V,
+                                                           const int* tok, const float* hidden, float* x2,
+                                                           unsigned* err) {
+  const int n = blockIdx.x * 128 + threadIdx.x;
+  if (n >= 2 * H) return;
+  if (n < H) {
+    x2[n] = hidden[n];
+    return;
+  }
+  const int t = *tok;
+  float v = 0.f;
+  if (t >= 0 && t < V) {
+    const size_t row_bytes = (size_t)(H / fmt_block_elems(fmt)) * fmt_block_bytes(fmt);
+    v = deq_elem(table + (size_t)t * row_bytes, fmt, n - H);
+  } else if (n == H) {
+    atomicOr(err, DEV_ERR_BAD_ARGUMENT);
+  }
+  x2[n] = v;
+}
+
+// h2 = t + h; xn = RMSNorm(h2) * w (post_attention_layernorm).  One CTA.
+__global__ void __launch_bounds__(256) eagle_resid_norm_kernel(const float* t, const float* h, const float* w, int H,
+                                                               float eps, float* h2, float* xn) {
+  __shared__ float red[8];
+  __shared__ float s_r;
+  float ss = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float v = t[i] + h[i];
+    h2[i] = v;
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) a += red[i];
+    s_r = 1.f / sqrtf(a / (float)H + eps);
+  }
+  __syncthreads();
+  const float r = s_r;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) xn[i] = h2[i] * r * w[i];
+}
+
+__global__ void eagle_add_kernel(const float* a, const float* b, float* out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) out[i] = a[i] + b[i];
+}
+
+// log(sum(exp(x - max))) + max over one row (NaN entries skipped).  One CTA.
+__global__ void __launch_bounds__(1024) row_lse_kernel(const float* x, int V, float* out) {
+  __shared__ float red[32];
+  __shared__ float s_m;
+  float m = -INFINITY;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) m = fmaxf(m, x[i]);
+  m = warp_max(m);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = -INFINITY;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) a = fmaxf(a, red[i]);
+    s_m = a;
+  }
+  __syncthreads();
+  const float mx = s_m;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float v = x[i];
+    if (v == v) s += expf(v - mx);
+  }
+  s = warp_sum(s);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = s;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float a = 0.f;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) a += red[i];
+    *out = logf(a) + mx;
+  }
+}
+
 // ---- seeded synthetic weights --------------------------------------------
 SPEC_DEV uint64_t splitmix64(uint64_t x) {
   x += 0x9E3779B97F4A7C15ull;
@@ -500,6 +585,25 @@ cudaError_t launch_row_topk(const float* logits, int rows, int V, int k, unsigne
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   topk_merge_kernel<<<rows, 256, 0, s>>>(part, chunks, k, ids, vals);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_eagle_concat(const uint8_t* table, int fmt, int H, int V, const int* tok, const float* hidden,
+                                float* x2, unsigned* err, cudaStream_t s) {
+  eagle_concat_kernel<<<(2 * H + 127) / 128, 128, 0, s>>>(table, fmt, H, V, tok, hidden, x2, err);
+  return cudaGetLastError();
+}
+cudaError_t launch_eagle_resid_norm(const float* t, const float* h, const float* w, int H, float eps, float* h2,
+                                    float* xn, cudaStream_t s) {
+  eagle_resid_norm_kernel<<<1, 256, 0, s>>>(t, h, w, H, eps, h2, xn);
+  return cudaGetLastError();
+}
+cudaError_t launch_eagle_add(const float* a, const float* b, float* out, int n, cudaStream_t s) {
+  eagle_add_kernel<<<(n + 255) / 256, 256, 0, s>>>(a, b, out, n);
+  return cudaGetLastError();
+}
+cudaError_t launch_row_lse(const float* x, int V, float* out, cudaStream_t s) {
+  row_lse_kernel<<<1, 1024, 0, s>>>(x, V, out);
   return cudaGetLastError();
 }
 

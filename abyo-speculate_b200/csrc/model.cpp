@@ -90,6 +90,8 @@ float bf_round(float f) {
 
 }  // namespace
 
+struct EagleHead;  // the EAGLE draft block attached to a target (spec_eagle_*)
+
 struct spec_model {
   ModelCfg cfg;
   int device = 0;
@@ -145,6 +147,7 @@ struct spec_model {
   void* kv_tmp = nullptr;
   int* argmax_dev = nullptr;
   unsigned long long* argmax_slots = nullptr;  // row argmax scratch (self-clearing)
+  std::shared_ptr<EagleHead> eagle;            // spec_eagle_attach*: device memory owned via dalloc
   unsigned long long* topk_part = nullptr;     // row top-k scratch (allocated on first use)
   int* topk_ids = nullptr;
   float* topk_vals = nullptr;
@@ -1914,6 +1917,390 @@ int spec_apply_lm_head_topk(spec_model* m, const float* hidden, int rows, int k,
     if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
     if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "apply_lm_head_topk"));
   }
+  return SPEC_OK;
+}
+
+// ---------------------------------------------------------------------------
+// EAGLE draft block on the device (methods/eagle.rs:100-427, 494-575)
+// ---------------------------------------------------------------------------
+constexpr int kEagleMaxSteps = 64;  // draft depth (KV rows of one round)
+
+struct EagleHead {
+  Mat fc, qkv, o, gu, down;  // BF16, the checkpoint's dtype
+  float* post_norm = nullptr;
+  float* rope_cos = nullptr;
+  float* rope_sin = nullptr;
+  void* kcache = nullptr;    // [n_kv][kEagleMaxSteps][hd] bf16
+  void* vcache = nullptr;
+  float *x2 = nullptr, *h = nullptr, *t = nullptr, *h2 = nullptr, *xn = nullptr, *t2 = nullptr, *out = nullptr,
+        *hin = nullptr, *logits = nullptr;
+  uint32_t *xa2 = nullptr, *xa = nullptr, *xl = nullptr, *xb = nullptr, *xc = nullptr;
+  float *xa2_16 = nullptr, *xa2_32 = nullptr, *xa16 = nullptr, *xa32 = nullptr, *xl16 = nullptr, *xl32 = nullptr,
+        *xb16 = nullptr, *xb32 = nullptr, *xc16 = nullptr, *xc32 = nullptr;
+  void* qbuf = nullptr;
+  float *part_o = nullptr, *part_ml = nullptr;
+  float* gpart = nullptr;
+  int* gcounters = nullptr;
+  FwdOp* ops = nullptr;  // fc, qkv, o, gu, down, lm
+  int* done = nullptr;
+  int* tok0 = nullptr;
+  int* step_dev = nullptr;   // {position, slot, keys before, keys after}
+  int* step_host = nullptr;  // pinned [kEagleMaxSteps][4]
+  unsigned long long* anc = nullptr;
+  int* ids = nullptr;
+  float* vals = nullptr;
+  float* lse = nullptr;
+  int* ids_host = nullptr;
+  float* vals_host = nullptr;
+  float* lse_host = nullptr;
+  int set_bf = 0;
+};
+
+namespace {
+
+enum : int { EOP_FC = 0, EOP_QKV, EOP_O, EOP_GU, EOP_DOWN, EOP_LM, EOP_N };
+
+// RoPE tables of the draft: eagle.rs:134-147 computes inv_freq in f32, then
+// positions and inv_freq in the checkpoint dtype (BF16), their product in
+// BF16, and cos/sin of that in BF16; the same roundings here.
+int eagle_rope(spec_model* m, EagleHead& e, float theta) {
+  const ModelCfg& c = m->cfg;
+  const int half = c.head_dim / 2, T = m->t_max + kEagleMaxSteps;
+  std::vector<float> cs((size_t)T * half), sn((size_t)T * half);
+  for (int i = 0; i < half; ++i) {
+    const float inv = bf_round(1.f / powf(theta, (float)(2 * i) / (float)c.head_dim));
+    for (int p = 0; p < T; ++p) {
+      const float a = bf_round(bf_round((float)p) * inv);
+      cs[(size_t)p * half + i] = bf_round(cosf(a));
+      sn[(size_t)p * half + i] = bf_round(sinf(a));
+    }
+  }
+  cudaError_t er = m->dalloc(&e.rope_cos, cs.size() * 4);
+  if (er == cudaSuccess) er = m->dalloc(&e.rope_sin, sn.size() * 4);
+  if (er == cudaSuccess) er = cudaMemcpy(e.rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
+  if (er == cudaSuccess) er = cudaMemcpy(e.rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+  if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "eagle rope tables"));
+  return SPEC_OK;
+}
+
+// Buffers and the six single-op descriptors, once the matrices exist.
+int eagle_finish(spec_model* m, EagleHead& e) {
+  const ModelCfg& c = m->cfg;
+  const int H = c.hidden, F = c.ffn, hd = c.head_dim, V = c.vocab, G = c.n_heads / c.n_kv;
+  const int Kq = c.n_heads * hd;
+  cudaError_t er = cudaSuccess;
+#define EALLOC(ptr, bytes)                                                     \
+  do {                                                                         \
+    if (er == cudaSuccess) er = m->dalloc(&(ptr), (bytes));                    \
+  } while (0)
+  const size_t kv = (size_t)c.n_kv * kEagleMaxSteps * hd * 2;
+  EALLOC(e.kcache, kv);
+  EALLOC(e.vcache, kv);
+  EALLOC(e.x2, (size_t)2 * H * 4);
+  EALLOC(e.h, (size_t)H * 4);
+  EALLOC(e.t, (size_t)H * 4);
+  EALLOC(e.h2, (size_t)H * 4);
+  EALLOC(e.xn, (size_t)H * 4);
+  EALLOC(e.t2, (size_t)H * 4);
+  EALLOC(e.out, (size_t)H * 4);
+  EALLOC(e.hin, (size_t)H * 4);
+  EALLOC(e.logits, (size_t)V * 4);
+  // operands of one row: K/16 k-steps x 256 bytes (NT = 1), column sums
+  auto frag = [&](uint32_t*& f, float*& s16, float*& s32, int K) {
+    EALLOC(f, (size_t)K * 16);
+    EALLOC(s16, (size_t)(K / 16) * 8 * 4);
+    EALLOC(s32, (size_t)(K / 32) * 8 * 4);
+  };
+  frag(e.xa2, e.xa2_16, e.xa2_32, 2 * H);
+  frag(e.xa, e.xa16, e.xa32, H);
+  frag(e.xl, e.xl16, e.xl32, H);
+  frag(e.xb, e.xb16, e.xb32, Kq);
+  frag(e.xc, e.xc16, e.xc32, F);
+  EALLOC(e.qbuf, (size_t)c.n_heads * hd * 2);
+  EALLOC(e.part_o, (size_t)c.n_kv * G * hd * 4);
+  EALLOC(e.part_ml, (size_t)c.n_kv * G * 2 * 4);
+  size_t part = 0;
+  int groups = 0;
+  for (const Mat* mt : {&e.fc, &e.qkv, &e.o, &e.gu, &e.down, &m->lm}) {
+    part = std::max(part, (size_t)partial_slots(*mt) * kGroupRows * 8);
+    groups = std::max(groups, mt->seg[0].groups + mt->seg[1].groups);
+  }
+  EALLOC(e.gpart, part * 4);
+  EALLOC(e.gcounters, (size_t)groups * 4);
+  EALLOC(e.ops, sizeof(FwdOp) * EOP_N);
+  EALLOC(e.done, sizeof(int) * EOP_N);
+  EALLOC(e.tok0, 16);
+  EALLOC(e.step_dev, 16);
+  EALLOC(e.anc, 8);
+  EALLOC(e.ids, (size_t)kEagleMaxSteps * kMaxTopK * 4);
+  EALLOC(e.vals, (size_t)kEagleMaxSteps * kMaxTopK * 4);
+  EALLOC(e.lse, (size_t)kEagleMaxSteps * 4);
+  if (!m->topk_part) EALLOC(m->topk_part, (size_t)kMaxRows * kTopKMaxChunks * kMaxTopK * 8);
+#undef EALLOC
+  if (er == cudaSuccess) er = m->halloc(&e.step_host, (size_t)kEagleMaxSteps * 16);
+  if (er == cudaSuccess) er = m->halloc(&e.ids_host, (size_t)kEagleMaxSteps * kMaxTopK * 4);
+  if (er == cudaSuccess) er = m->halloc(&e.vals_host, (size_t)kEagleMaxSteps * kMaxTopK * 4);
+  if (er == cudaSuccess) er = m->halloc(&e.lse_host, (size_t)kEagleMaxSteps * 4);
+  if (er != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(er, "eagle buffers"));
+  const unsigned long long one = 1ull;
+  er = cudaMemcpy(e.anc, &one, 8, cudaMemcpyHostToDevice);
+
+  auto base = [&](const Mat& mt) {
+    QmvParams p = base_params(m, mt, 1);
+    p.part = e.gpart;
+    p.counters = e.gcounters;
+    p.act_bf16 = 1;
+    return p;
+  };
+  FwdOp ops[EOP_N];
+  {  // fc: concat(hidden, embedding) -> h
+    QmvParams& p = ops[EOP_FC].q;
+    p = base(e.fc);
+    p.xfrag = e.xa2;
+    p.xsum16 = e.xa2_16;
+    p.xsum32 = e.xa2_32;
+    p.epi = EPI_STORE;
+    p.out = e.h;
+    p.ld_out = H;
+  }
+  {  // q, k, v with RoPE; K/V rows into the draft's cache (no input norm)
+    QmvParams& p = ops[EOP_QKV].q;
+    p = base(e.qkv);
+    p.xfrag = e.xa;
+    p.xsum16 = e.xa16;
+    p.xsum32 = e.xa32;
+    p.epi = EPI_QKV;
+    p.n_q_heads = c.n_heads;
+    p.n_kv_heads = c.n_kv;
+    p.head_dim = hd;
+    p.rope_interleaved = 0;  // candle_nn::rotary_emb::rope (rotate-half)
+    p.rope_cos = e.rope_cos;
+    p.rope_sin = e.rope_sin;
+    p.positions = e.step_dev;
+    p.kv_slots = e.step_dev + 1;
+    p.qbuf = e.qbuf;
+    p.kcache = e.kcache;
+    p.vcache = e.vcache;
+    p.t_max = kEagleMaxSteps;
+  }
+  {  // o_proj -> t
+    QmvParams& p = ops[EOP_O].q;
+    p = base(e.o);
+    p.xfrag = e.xb;
+    p.xsum16 = e.xb16;
+    p.xsum32 = e.xb32;
+    p.epi = EPI_STORE;
+    p.out = e.t;
+    p.ld_out = H;
+  }
+  {  // gate/up -> silu(g) * u as the down operand
+    QmvParams& p = ops[EOP_GU].q;
+    p = base(e.gu);
+    p.xfrag = e.xa;
+    p.xsum16 = e.xa16;
+    p.xsum32 = e.xa32;
+    p.epi = EPI_SILU;
+    p.next_frag = e.xc;
+    p.next_xsum16 = e.xc16;
+    p.next_xsum32 = e.xc32;
+  }
+  {  // down -> t2
+    QmvParams& p = ops[EOP_DOWN].q;
+    p = base(e.down);
+    p.xfrag = e.xc;
+    p.xsum16 = e.xc16;
+    p.xsum32 = e.xc32;
+    p.epi = EPI_STORE;
+    p.out = e.t2;
+    p.ld_out = H;
+  }
+  {  // the target's LM head -> logits row
+    QmvParams& p = ops[EOP_LM].q;
+    p = base(m->lm);
+    p.act_bf16 = c.bf16 ? 1 : 0;
+    p.xfrag = e.xl;
+    p.xsum16 = e.xl16;
+    p.xsum32 = e.xl32;
+    p.epi = EPI_STORE;
+    p.out = e.logits;
+    p.ld_out = V;
+  }
+  for (auto& op : ops) op.dep = -1;
+  if (er == cudaSuccess) er = cudaMemcpy(e.ops, ops, sizeof(ops), cudaMemcpyHostToDevice);
+  if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "eagle descriptors"));
+  e.set_bf = fwd_fmt_set_for(fmt_bit(WF_BF16));
+  return SPEC_OK;
+}
+
+int eagle_build(spec_model* m, const Part& fc, const Part& q, const Part& k, const Part& v, const Part& o,
+                const Part& g, const Part& u, const Part& d, float theta, std::shared_ptr<EagleHead>& out) {
+  const ModelCfg& c = m->cfg;
+  auto e = std::make_shared<EagleHead>();
+  const int saved_bits = m->fmt_bits;  // the draft's BF16 does not join the target's format set
+  int rc = build_mat(m, {fc}, 2 * c.hidden, false, e->fc);
+  if (rc == SPEC_OK) rc = build_mat(m, {q, k, v}, c.hidden, false, e->qkv);
+  if (rc == SPEC_OK) rc = build_mat(m, {o}, c.n_heads * c.head_dim, false, e->o);
+  if (rc == SPEC_OK) rc = build_mat(m, {g, u}, c.hidden, true, e->gu);
+  if (rc == SPEC_OK) rc = build_mat(m, {d}, c.ffn, false, e->down);
+  m->fmt_bits = saved_bits;
+  if (rc == SPEC_OK) rc = eagle_rope(m, *e, theta);
+  if (rc == SPEC_OK) rc = eagle_finish(m, *e);
+  if (rc == SPEC_OK) out = e;
+  return rc;
+}
+
+int eagle_check_target(spec_model* m) {
+  const ModelCfg& c = m->cfg;
+  if (m->tp_size > 1) return m->fail(SPEC_ERR_UNSUPPORTED, "EAGLE draft on a tensor-parallel handle");
+  if ((2 * c.hidden) % 128 || c.hidden % 128 || c.ffn % 128 || (c.n_heads * c.head_dim) % 128)
+    return m->fail(SPEC_ERR_UNSUPPORTED, "EAGLE draft shapes are not multiples of 128");
+  return SPEC_OK;
+}
+
+}  // namespace
+
+int spec_eagle_attach(spec_model* m, const spec_eagle_weights* w) {
+  if (!m || !w || !w->fc || !w->q || !w->k || !w->v || !w->o || !w->gate || !w->up || !w->down || !w->post_norm)
+    return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (int rc = eagle_check_target(m)) return rc;
+  const ModelCfg& c = m->cfg;
+  const int hd = c.head_dim;
+  auto host = [](const void* src, int rows) {
+    Part p;
+    p.src = static_cast<const uint8_t*>(src);
+    p.on_device = false;
+    p.fmt = WF_BF16;
+    p.rows = rows;
+    return p;
+  };
+  std::shared_ptr<EagleHead> e;
+  int rc = eagle_build(m, host(w->fc, c.hidden), host(w->q, c.n_heads * hd), host(w->k, c.n_kv * hd),
+                       host(w->v, c.n_kv * hd), host(w->o, c.hidden), host(w->gate, c.ffn), host(w->up, c.ffn),
+                       host(w->down, c.hidden), w->rope_theta > 0.f ? w->rope_theta : c.rope_theta, e);
+  if (rc != SPEC_OK) return rc;
+  cudaError_t er = m->dalloc(&e->post_norm, (size_t)c.hidden * 4);
+  if (er == cudaSuccess) er = cudaMemcpy(e->post_norm, w->post_norm, (size_t)c.hidden * 4, cudaMemcpyHostToDevice);
+  if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "eagle norm"));
+  m->eagle = e;
+  return SPEC_OK;
+}
+
+int spec_eagle_attach_synthetic(spec_model* m, uint64_t seed) {
+  if (!m) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (int rc = eagle_check_target(m)) return rc;
+  const ModelCfg& c = m->cfg;
+  const int H = c.hidden, hd = c.head_dim, F = c.ffn;
+  std::vector<void*> temps;
+  uint64_t st = seed * 0x9E3779B97F4A7C15ull + 0xEA61Eull;
+  auto tseed = [&]() { return st += 0x632BE59BD9B4E019ull; };
+  Part fc, q, k, v, o, g, u, d;
+  int rc = synth_part(m, temps, WF_BF16, H, 2 * H, tseed(), fc);
+  if (rc == SPEC_OK) rc = synth_part(m, temps, WF_BF16, c.n_heads * hd, H, tseed(), q);
+  if (rc == SPEC_OK) rc = synth_part(m, temps, WF_BF16, c.n_kv * hd, H, tseed(), k);
+  if (rc == SPEC_OK) rc = synth_part(m, temps, WF_BF16, c.n_kv * hd, H, tseed(), v);
+  if (rc == SPEC_OK) rc = synth_part(m, temps, WF_BF16, H, c.n_heads * hd, tseed(), o);
+  if (rc == SPEC_OK) rc = synth_part(m, temps, WF_BF16, F, H, tseed(), g);
+  if (rc == SPEC_OK) rc = synth_part(m, temps, WF_BF16, F, H, tseed(), u);
+  if (rc == SPEC_OK) rc = synth_part(m, temps, WF_BF16, H, F, tseed(), d);
+  std::shared_ptr<EagleHead> e;
+  if (rc == SPEC_OK) rc = eagle_build(m, fc, q, k, v, o, g, u, d, c.rope_theta, e);
+  if (rc == SPEC_OK) rc = synth_vec(m, &e->post_norm, H, tseed(), 1.f);
+  cudaStreamSynchronize(m->stream);
+  for (void* t : temps) cudaFree(t);
+  if (rc != SPEC_OK) return rc;
+  m->eagle = e;
+  return SPEC_OK;
+}
+
+int spec_eagle_draft(spec_model* m, const float* hidden, uint32_t root, int position, int depth, int k,
+                     int32_t* ids_out, float* logprobs_out) {
+  if (!m || !hidden || !ids_out || depth < 1) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  EagleHead* e = m->eagle.get();
+  if (!e) return m->fail(SPEC_ERR_INVALID, "no EAGLE draft attached (spec_eagle_attach)");
+  const ModelCfg& c = m->cfg;
+  const int H = c.hidden, V = c.vocab, G = c.n_heads / c.n_kv;
+  if (depth > kEagleMaxSteps) return m->fail(SPEC_ERR_UNSUPPORTED, "EAGLE draft depth above 64");
+  if (k < 1 || k > kMaxTopK || k > V) return m->fail(SPEC_ERR_INVALID, "top-k size out of range");
+  if (root >= (uint32_t)V) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  if (position < 0 || position + depth > m->t_max + kEagleMaxSteps)
+    return m->fail(SPEC_ERR_INVALID, "EAGLE draft position outside the RoPE table");
+  cudaStream_t s = m->stream;
+  for (int i = 0; i < depth; ++i) {
+    e->step_host[4 * i + 0] = position + i;  // RoPE position (eagle.rs:544: history_len + step)
+    e->step_host[4 * i + 1] = i;             // KV row: the cache holds this round only (draft.reset())
+    e->step_host[4 * i + 2] = i;             // keys before this row
+    e->step_host[4 * i + 3] = i + 1;
+  }
+  const int root_i = (int)root;
+  cudaError_t er = cudaMemcpyAsync(e->hin, hidden, (size_t)H * 4, cudaMemcpyHostToDevice, s);
+  if (er == cudaSuccess) er = cudaMemcpyAsync(e->tok0, &root_i, 4, cudaMemcpyHostToDevice, s);
+  if (er == cudaSuccess) er = cudaMemsetAsync(m->err_dev, 0, 16, s);
+  auto gemv = [&](int op, int set) {
+    FwdParams fp;
+    fp.ops = e->ops + op;
+    fp.n_ops = 1;
+    fp.done = e->done + op;
+    fp.err = m->err_dev;
+    return launch_fwd(fp, set, 1, s, false);
+  };
+  AttnParams a;
+  a.q = e->qbuf;
+  a.kcache = e->kcache;
+  a.vcache = e->vcache;
+  a.n_kv = c.n_kv;
+  a.G = G;
+  a.hd = c.head_dim;
+  a.M = 1;
+  a.t_max = kEagleMaxSteps;
+  a.step = e->step_dev + 2;
+  a.anc = e->anc;
+  a.scale_log2 = 1.4426950408889634f / sqrtf((float)c.head_dim);
+  a.chunk = kEagleMaxSteps;
+  a.max_splits = 1;
+  a.part_o = e->part_o;
+  a.part_ml = e->part_ml;
+  a.frag = e->xb;
+  a.xsum16 = e->xb16;
+  a.xsum32 = e->xb32;
+  a.act_bf16 = 1;
+  a.err = m->err_dev;
+  for (int i = 0; i < depth && er == cudaSuccess; ++i) {
+    const float* hid = i == 0 ? e->hin : e->out;
+    const int* tok = i == 0 ? e->tok0 : e->ids + (size_t)(i - 1) * k;  // previous step's top-1
+    er = cudaMemcpyAsync(e->step_dev, e->step_host + 4 * i, 16, cudaMemcpyHostToDevice, s);
+    if (er == cudaSuccess) er = launch_eagle_concat(m->embed_raw, m->embed_fmt, H, V, tok, hid, e->x2, m->err_dev, s);
+    if (er == cudaSuccess) er = launch_make_operand(e->x2, 1, 2 * H, 1, e->xa2, e->xa2_16, e->xa2_32, 1, s);
+    if (er == cudaSuccess) er = gemv(EOP_FC, e->set_bf);
+    if (er == cudaSuccess) er = launch_make_operand(e->h, 1, H, 1, e->xa, e->xa16, e->xa32, 1, s);
+    if (er == cudaSuccess) er = gemv(EOP_QKV, e->set_bf);
+    if (er == cudaSuccess) er = launch_attention(a, 1, s, false);
+    if (er == cudaSuccess) er = gemv(EOP_O, e->set_bf);
+    if (er == cudaSuccess) er = launch_eagle_resid_norm(e->t, e->h, e->post_norm, H, c.eps, e->h2, e->xn, s);
+    if (er == cudaSuccess) er = launch_make_operand(e->xn, 1, H, 1, e->xa, e->xa16, e->xa32, 1, s);
+    if (er == cudaSuccess) er = gemv(EOP_GU, e->set_bf);
+    if (er == cudaSuccess) er = gemv(EOP_DOWN, e->set_bf);
+    if (er == cudaSuccess) er = launch_eagle_add(e->t2, e->h2, e->out, H, s);
+    if (er == cudaSuccess) er = launch_make_operand(e->out, 1, H, 1, e->xl, e->xl16, e->xl32, c.bf16 ? 1 : 0, s);
+    if (er == cudaSuccess) er = gemv(EOP_LM, m->fmt_set);
+    if (er == cudaSuccess)
+      er = launch_row_topk(e->logits, 1, V, k, m->topk_part, e->ids + (size_t)i * k, e->vals + (size_t)i * k, s);
+    if (er == cudaSuccess) er = launch_row_lse(e->logits, V, e->lse + i, s);
+  }
+  if (er == cudaSuccess)
+    er = cudaMemcpyAsync(e->ids_host, e->ids, (size_t)depth * k * 4, cudaMemcpyDeviceToHost, s);
+  if (er == cudaSuccess)
+    er = cudaMemcpyAsync(e->vals_host, e->vals, (size_t)depth * k * 4, cudaMemcpyDeviceToHost, s);
+  if (er == cudaSuccess) er = cudaMemcpyAsync(e->lse_host, e->lse, (size_t)depth * 4, cudaMemcpyDeviceToHost, s);
+  if (er == cudaSuccess) er = cudaMemcpyAsync(m->err_host, m->err_dev, 16, cudaMemcpyDeviceToHost, s);
+  if (er == cudaSuccess) er = cudaStreamSynchronize(s);
+  if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "eagle draft"));
+  if (m->err_host[0]) return m->fail(SPEC_ERR_TIMEOUT, "device error during the EAGLE draft");
+  memcpy(ids_out, e->ids_host, (size_t)depth * k * 4);
+  if (logprobs_out)  // eagle.rs:557-559: logits[i] - lse
+    for (int i = 0; i < depth * k; ++i) logprobs_out[i] = e->vals_host[i] - e->lse_host[i / k];
   return SPEC_OK;
 }
 

@@ -219,6 +219,35 @@ class B200Decoder:
                                                       _ptr(ids, ctypes.c_int32), _ptr(vals, ctypes.c_float)))
         return ids.reshape(*lead, k), vals.reshape(*lead, k)
 
+    # ---- EAGLE draft on the device (methods/eagle.rs) ----------------------
+    def eagle_attach(self, weights: dict, rope_theta: float = 0.0) -> None:
+        """weights: 'fc', 'q', 'k', 'v', 'o', 'gate', 'up', 'down' as uint16 BF16
+        bit arrays [out, in]; 'post_norm' f32 [H]."""
+        keep = {}
+        ws = _lib.EagleWeights()
+        for name in ("fc", "q", "k", "v", "o", "gate", "up", "down"):
+            a = np.ascontiguousarray(weights[name], dtype=np.uint16)
+            keep[name] = a
+            setattr(ws, name, a.ctypes.data)
+        pn = np.ascontiguousarray(weights["post_norm"], dtype=np.float32)
+        keep["post_norm"] = pn
+        ws.post_norm = pn.ctypes.data
+        ws.rope_theta = float(rope_theta)
+        self._check(self._lib.spec_eagle_attach(self._h, ctypes.byref(ws)))
+
+    def eagle_attach_synthetic(self, seed: int = 0) -> None:
+        self._check(self._lib.spec_eagle_attach_synthetic(self._h, int(seed)))
+
+    def eagle_draft(self, hidden: np.ndarray, root: int, position: int, depth: int,
+                    k: int) -> Tuple[np.ndarray, np.ndarray]:
+        """eagle.rs:531-575 on the device: (ids [depth, k], log-probs [depth, k])."""
+        h = np.ascontiguousarray(np.asarray(hidden, dtype=np.float32).reshape(-1))
+        ids = np.empty((depth, k), dtype=np.int32)
+        lp = np.empty((depth, k), dtype=np.float32)
+        self._check(self._lib.spec_eagle_draft(self._h, _ptr(h, ctypes.c_float), int(root), int(position), depth, k,
+                                               _ptr(ids, ctypes.c_int32), _ptr(lp, ctypes.c_float)))
+        return ids, lp
+
     def embed_tokens(self, ids: Sequence[int]) -> np.ndarray:
         a = _u32(ids)
         out = np.empty((a.size, self._hidden), dtype=np.float32)

@@ -317,6 +317,16 @@ def run_config(args, ws, rank, local, dist):
             step(i)
         acc_len.clear()
         ms = _event_ms(stream, lambda i: step(args.warmup + i), args.steps)
+        # The EAGLE draft loop of a round (eagle.rs:531-575) on the device: a
+        # seeded BF16 draft block, depth 6, top-10 per step (configs[3]'s tree).
+        tgt.eagle_attach_synthetic(21)
+        hid = rng.standard_normal(CFG4_TARGET["hidden"]).astype(np.float32)
+        for _ in range(args.warmup):
+            tgt.eagle_draft(hid, prompt[-1], T, 6, 10)
+        dms = _event_ms(stream, lambda i: tgt.eagle_draft(hid, prompt[-1], T, 6, 10), args.steps)
+        out["eagle_draft"] = {"ms_per_round": round(dms / args.steps, 3), "depth": 6, "top_k": 10,
+                              "note": "spec_eagle_draft: draft block + target LM head + device top-k per step, "
+                                      "one host sync per round"}
         out.update({"metric": "EAGLE tree verify steps/s (60-node tree, tree forward + device argmax + accepted-path KV reorder)",
                     "value": round(args.steps / (ms / 1e3), 3), "unit": "tree verify steps/s",
                     "ms_per_step": round(ms / args.steps, 3), "dtype": "bf16",

@@ -167,6 +167,38 @@ int spec_embed_tokens(spec_model* m, const uint32_t* ids, int n, float* out);
 int spec_last_hidden_states_multi(spec_model* m, const int32_t* layers, int n_sel, float* final_out,
                                   float* layer_outs);
 
+/* ---- EAGLE draft on the device (methods/eagle.rs) ----------------------------
+ * The EAGLE draft block (eagle.rs:390-427): concat(target hidden, token
+ * embedding) -> fc -> one Llama block without input norm (RoPE rotate-half in
+ * the checkpoint's BF16, its own per-round KV cache) -> post-attention
+ * RMSNorm -> SiLU MLP, with shapes equal to a target layer.  Weights are BF16
+ * (row-major [out][in] bits), the norm f32; the token embedding is the
+ * target's.  rope_theta <= 0 takes the target's. */
+typedef struct spec_eagle_weights {
+  const uint16_t* fc;    /* [H][2H] */
+  const uint16_t* q;     /* [n_heads*hd][H] */
+  const uint16_t* k;     /* [n_kv*hd][H] */
+  const uint16_t* v;     /* [n_kv*hd][H] */
+  const uint16_t* o;     /* [H][n_heads*hd] */
+  const uint16_t* gate;  /* [F][H] */
+  const uint16_t* up;    /* [F][H] */
+  const uint16_t* down;  /* [H][F] */
+  const float* post_norm; /* [H] */
+  float rope_theta;
+} spec_eagle_weights;
+int spec_eagle_attach(spec_model* m, const spec_eagle_weights* w);
+/* Seeded N(0, 0.02) BF16 weights made on the device (benchmarks). */
+int spec_eagle_attach_synthetic(spec_model* m, uint64_t seed);
+/* One round's draft loop (eagle.rs:531-575) on the device: depth steps of the
+ * draft block, each followed by the target's LM head, a device top-k
+ * (medusa.rs:477-487 order) and log-softmax; the next step takes the top-1
+ * token and the draft's hidden row without leaving the device.  hidden: the
+ * target's last hidden row [H]; root: the last committed token; position: the
+ * target's history length.  Writes ids_out[depth][k] and (when non-NULL)
+ * logprobs_out[depth][k] = logit - logsumexp(row).  depth <= 64. */
+int spec_eagle_draft(spec_model* m, const float* hidden, uint32_t root, int position, int depth, int k,
+                     int32_t* ids_out, float* logprobs_out);
+
 /* ---- device-side acceptance ------------------------------------------------
  * Greedy (temperature 0) vanilla verify: one batched forward of [last]+drafts
  * (same protocol and state change as spec_batched_logits), then the argmax of
