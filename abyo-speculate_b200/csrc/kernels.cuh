@@ -30,7 +30,7 @@ enum DevError : unsigned {
 // err[3] = the counter value it last saw.
 // (Site 2 was the consumers' per-op dependency wait, which per-group flags
 // made unnecessary; the number stays retired.)
-enum WaitSite : unsigned { WAIT_CONSUMER_FULL = 1, WAIT_PRODUCER_IDLE = 3, WAIT_TP_PEERS = 4 };
+enum WaitSite : unsigned { WAIT_CONSUMER_FULL = 1, WAIT_PRODUCER_IDLE = 3, WAIT_TP_PEERS = 4, WAIT_ATTN_DEP = 5 };
 
 // GGML type ids (public GGUF specification) of the weight formats handled.
 enum WFmt : int { WF_F32 = 0, WF_F16 = 1, WF_Q8_0 = 8, WF_Q4_K = 12, WF_Q5_K = 13, WF_Q6_K = 14, WF_BF16 = 30 };
@@ -151,6 +151,15 @@ struct QmvParams {
   float* next_xsum16 = nullptr;
   float* next_xsum32 = nullptr;
   int act_bf16 = 0;                 // operand dtype: 0 f16, 1 bf16
+  // Attention ops (FwdOp::kind != OPK_GEMV) use qbuf / kcache / vcache /
+  // t_max / head counts above, next_frag / next_xsum* as the O-projection
+  // operand they emit, and these:
+  const int* attn_step = nullptr;                 // device: [0] prefix length P, [1] total keys
+  const unsigned long long* attn_anc = nullptr;   // [M] ancestor bitmask over the new keys
+  float* attn_o = nullptr;                        // split partials [n_kv][max_splits][R][hd]
+  float* attn_ml = nullptr;                       // [n_kv][max_splits][R][2]
+  float attn_scale_log2 = 0.f;                    // log2(e) / sqrt(hd)
+  int attn_chunk = 0, attn_max_splits = 0;        // keys per split; splits per KV head
 };
 
 // ---- persistent multi-op GEMV kernel -------------------------------------
@@ -160,9 +169,18 @@ struct QmvParams {
 // the activation tile of a stage is only fetched once the op it depends on
 // has completed (device-side completion counter), so weight streaming never
 // waits on the previous op.
+// Op kinds.  Attention ops come last in a launch, after every GEMV op: their
+// CTAs stage keys in the weight ring's shared memory once the ring is drained.
+//   OPK_ATTN_SPLIT: unit u = (split u / n_kv, KV head u % n_kv) of the split
+//     flash decode; waits for the QKV groups of its KV head (dep).
+//   OPK_ATTN_COMBINE: unit u = 4 merge items, one per warp; waits for every
+//     split unit (dep's done count).
+enum OpKind : int { OPK_GEMV = 0, OPK_ATTN_SPLIT = 1, OPK_ATTN_COMBINE = 2 };
+
 struct alignas(16) FwdOp {
   QmvParams q;
   int dep = -1;  // op (index in this launch) whose completion gates this op; -1: the previous kernel
+  int kind = OPK_GEMV;
 };
 
 // Bit set of weight formats one kernel instantiation handles.
@@ -186,6 +204,9 @@ struct FwdParams {
   int* gflags = nullptr;
   int flag_stride = 0;
   const unsigned* epoch = nullptr;
+  // Consumers that reach the launch's attention ops first signal the next
+  // kernel's programmatic launch (griddepcontrol.launch_dependents).
+  int trigger_after_gemv = 0;
 };
 
 // The instantiation is picked by (format set, nt_for_rows(M)); all ops of
@@ -195,6 +216,10 @@ cudaError_t launch_fwd(const FwdParams& p, int fmt_set, int M, cudaStream_t stre
 int fwd_ctas_per_sm(int fmt_set);
 // The format sets instantiated (a model's formats must fit in one).
 int fwd_fmt_set_for(int fmt_bits);
+// Keys per pass an attention split unit of the forward kernel stages for
+// (format set, M rows, head dim, keys per split); below kAttnKeyBlock,
+// attention does not fit the instantiation's ring and runs as its own kernels.
+int fwd_attn_keys_per_pass(int fmt_set, int M, int hd, int chunk);
 
 // Repack raw GGUF blocks (device, row-major [N][K/be][bb]) into pair tiles.
 cudaError_t launch_repack(const uint8_t* raw, int fmt, int N, int K, uint8_t* tiles, cudaStream_t s);
@@ -237,6 +262,10 @@ struct AttnParams {
   unsigned* err = nullptr;
 };
 cudaError_t launch_attention(const AttnParams& p, int nt, cudaStream_t s, bool pdl);
+// Keys per online-softmax step of a split; a split's chunk is a multiple.
+constexpr int kAttnKeyBlock = 32;
+// Merge items for R = M*G rows: one warp per (KV head, row, 32 head columns).
+__host__ __device__ constexpr int attn_combine_items(int n_kv, int R, int hd) { return n_kv * R * (hd / 32); }
 
 // ---- KV reorder (commit accepted path) -----------------------------------
 // src_rows/dst_rows: device int[n]; tmp: device scratch of layers*2*n_kv*n*hd halves.

@@ -189,6 +189,7 @@ struct spec_model {
     std::vector<FwdOp> host_ops;
     FwdOp* solo = nullptr;  // the same ops with dep = -1, for one-op launches
     int* gflags = nullptr;  // [n_ops][flag_stride] per-group completion flags
+    bool fused_attn = false;  // attention runs as ops of the forward kernel
   };
   std::map<int, Schedule> schedules;
   int tp_rank = 0, tp_size = 1;     // tensor-parallel position (1 = whole model on this GPU)
@@ -202,6 +203,8 @@ struct spec_model {
   bool tp_connected = false;
   int l2_ahead = 0;                 // weight stages each CTA prefetches into L2 ahead of its ring (SPEC_B200_L2_AHEAD)
   bool use_pdl = true;              // programmatic dependent launch between forward kernels
+  bool fused_attn = true;           // attention as ops of the forward kernel (else its own kernels)
+  bool attn_trigger = true;         // a launch's attention tail overlaps the next launch (PDL trigger)
   FwdOp* single_op = nullptr;       // device slot for one-op launches
   FwdOp* single_op_host = nullptr;  // pinned staging
   int* single_done = nullptr;
@@ -397,7 +400,10 @@ int alloc_runtime(spec_model* m) {
   ALLOC(m->qbuf, (size_t)c.n_heads * kMaxRows * hd * 2);
   // Keys per attention split (fixed per model: splits are aligned to absolute
   // key positions, which keeps every row's arithmetic independent of M).
-  m->attn_chunk = m->t_max <= 8192 ? 128 : 256;
+  // Short contexts take small splits (a split unit stages its keys in one
+  // pass and more units run at once), long ones larger splits (fewer
+  // partials to merge).
+  m->attn_chunk = m->t_max <= 4096 ? 64 : m->t_max <= 8192 ? 128 : 256;
   m->attn_max_splits = (m->t_max + m->attn_chunk - 1) / m->attn_chunk;
   const size_t R = (size_t)kMaxRows * G;
   ALLOC(m->part_o, (size_t)c.n_kv * m->attn_max_splits * R * hd * 4);
@@ -597,6 +603,50 @@ FwdOp op_qkv(spec_model* m, int l, int M) {
   p.t_max = m->t_max;
   return o;
 }
+// Layer l's attention as ops of the forward kernel, after its QKV op:
+// OPK_ATTN_SPLIT (one unit per (split, KV head)) and OPK_ATTN_COMBINE (four
+// merge items per unit, emitting the O-projection operand).
+FwdOp op_attn(spec_model* m, int l, int M, int kind) {
+  const ModelCfg& c = m->cfg;
+  FwdOp o;
+  o.kind = kind;
+  QmvParams& p = o.q;
+  p.M = M;
+  p.err = m->err_dev;
+  p.act_bf16 = c.bf16 ? 1 : 0;
+  p.n_q_heads = c.n_heads;
+  p.n_kv_heads = c.n_kv;
+  p.head_dim = c.head_dim;
+  p.qbuf = m->qbuf;
+  p.kcache = static_cast<uint8_t*>(m->kcache) + (size_t)l * m->kv_layer_elems * 2;
+  p.vcache = static_cast<uint8_t*>(m->vcache) + (size_t)l * m->kv_layer_elems * 2;
+  p.t_max = m->t_max;
+  p.attn_step = m->step_dev->step;
+  p.attn_anc = m->step_dev->anc;
+  p.attn_o = m->part_o;
+  p.attn_ml = m->part_ml;
+  p.attn_scale_log2 = 1.4426950408889634f / sqrtf((float)c.head_dim);
+  p.attn_chunk = m->attn_chunk;
+  p.attn_max_splits = m->attn_max_splits;
+  p.next_frag = m->xb;
+  p.next_xsum16 = m->xb16;
+  p.next_xsum32 = m->xb32;
+  const int R = M * (c.n_heads / c.n_kv);
+  p.stages = p.chunks = kind == OPK_ATTN_SPLIT
+                            ? c.n_kv * m->attn_max_splits
+                            : (attn_combine_items(c.n_kv, R, c.head_dim) + kGemvWarps - 1) / kGemvWarps;
+  return o;
+}
+
+// Whether attention runs inside the forward kernel for M rows: the split
+// unit's key / query staging must fit the weight ring of the instantiation.
+bool attn_fused(const spec_model* m, int M) {
+  if (!m->fused_attn) return false;
+  const int hd = m->cfg.head_dim;
+  if (hd != 64 && hd != 128) return false;
+  return fwd_attn_keys_per_pass(m->fmt_set, M, hd, m->attn_chunk) >= kAttnKeyBlock;
+}
+
 FwdOp op_o(spec_model* m, int l, int M) {
   const ModelCfg& c = m->cfg;
   FwdOp o;
@@ -695,7 +745,7 @@ int get_schedule(spec_model* m, int M, int flags, spec_model::Schedule** out) {
   auto add = [&](FwdOp o, int64_t bytes) {
     const int first = sc.launches.back().first;
     o.dep = (int)ops.size() == first ? -1 : (int)ops.size() - 1 - first;
-    if (((int)ops.size() - first) & 1) {
+    if (o.kind == OPK_GEMV && (((int)ops.size() - first) & 1)) {
       o.q.part += m->part_set;
       o.q.counters += m->counter_set;
     }
@@ -703,15 +753,27 @@ int get_schedule(spec_model* m, int M, int flags, spec_model::Schedule** out) {
     sc.launches.back().second = (int)ops.size();
     sc.launch_bytes.back() += bytes;
   };
+  if (!m->fmt_set) m->fmt_set = fwd_fmt_set_for(m->fmt_bits);
+  sc.fused_attn = attn_fused(m, M);
+  auto add_attn = [&](int l) {
+    if (!sc.fused_attn) return;
+    add(op_attn(m, l, M, OPK_ATTN_SPLIT), 0);
+    add(op_attn(m, l, M, OPK_ATTN_COMBINE), 0);
+  };
   begin_launch();
   add(op_qkv(m, 0, M), m->layers[0].qkv.bytes);
+  add_attn(0);
   for (int l = 0; l < c.n_layers; ++l) {
     begin_launch();
     add(op_o(m, l, M), m->layers[l].o.bytes);
     add(op_gu(m, l, M), m->layers[l].gu.bytes);
     add(op_down(m, l, M), m->layers[l].down.bytes);
-    if (l + 1 < c.n_layers) add(op_qkv(m, l + 1, M), m->layers[l + 1].qkv.bytes);
-    else if (flags & F_LOGITS) add(op_lm(m, M, m->logits), m->lm.bytes);
+    if (l + 1 < c.n_layers) {
+      add(op_qkv(m, l + 1, M), m->layers[l + 1].qkv.bytes);
+      add_attn(l + 1);
+    } else if (flags & F_LOGITS) {
+      add(op_lm(m, M, m->logits), m->lm.bytes);
+    }
   }
   sc.n_ops = (int)ops.size();
   sc.host_ops = ops;
@@ -742,6 +804,7 @@ cudaError_t launch_slice(spec_model* m, const spec_model::Schedule& sc, int li, 
   fp.gflags = sc.gflags + (size_t)sc.launches[li].first * m->counter_set;
   fp.flag_stride = m->counter_set;
   fp.epoch = &m->step_dev->epoch;
+  fp.trigger_after_gemv = (pdl && m->attn_trigger) ? 1 : 0;
   return launch_fwd(fp, m->fmt_set, M, m->stream, pdl);
 }
 
@@ -822,10 +885,14 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
   if (e != cudaSuccess) return e;
   if ((e = prof_mark(pr, s, K_EMBED, (int64_t)M * H * 8)) != cudaSuccess) return e;
   const int64_t step_keys = (int64_t)m->step_host->step[1];
+  // K and V bytes one layer's attention reads (counted in the forward
+  // kernel's launch when attention runs inside it).
+  const int64_t attn_bytes = step_keys * c.n_kv * hd * 2 * 2;
+  const int64_t fused_bytes = sc->fused_attn ? attn_bytes : 0;
   if ((e = launch_slice(m, *sc, 0, M, pdl)) != cudaSuccess) return e;
-  if ((e = prof_mark(pr, s, K_FWD, sc->launch_bytes[0])) != cudaSuccess) return e;
+  if ((e = prof_mark(pr, s, K_FWD, sc->launch_bytes[0] + fused_bytes)) != cudaSuccess) return e;
   for (int l = 0; l < c.n_layers; ++l) {
-    {  // attention of layer l
+    if (!sc->fused_attn) {  // attention of layer l as its own kernels
       AttnParams a;
       a.q = m->qbuf;
       a.kcache = static_cast<uint8_t*>(m->kcache) + (size_t)l * m->kv_layer_elems * 2;
@@ -848,7 +915,7 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
       a.act_bf16 = c.bf16 ? 1 : 0;
       a.err = m->err_dev;
       if ((e = launch_attention(a, nt, s, pdl)) != cudaSuccess) return e;
-      if ((e = prof_mark(pr, s, K_ATTN, step_keys * c.n_kv * hd * 2 * 2)) != cudaSuccess) return e;
+      if ((e = prof_mark(pr, s, K_ATTN, attn_bytes)) != cudaSuccess) return e;
     }
     if (collect) {
       // Collecting a layer's residual splits the launch after its down-proj.
@@ -871,7 +938,8 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
       }
     }
     if ((e = launch_slice(m, *sc, l + 1, M, pdl)) != cudaSuccess) return e;
-    if ((e = prof_mark(pr, s, K_FWD, sc->launch_bytes[l + 1])) != cudaSuccess) return e;
+    const bool has_attn = sc->fused_attn && l + 1 < c.n_layers;
+    if ((e = prof_mark(pr, s, K_FWD, sc->launch_bytes[l + 1] + (has_attn ? attn_bytes : 0))) != cudaSuccess) return e;
   }
   if (flags & F_LOGITS) {
     e = cudaMemcpyAsync(m->last_row, m->logits + (size_t)(M - 1) * c.vocab, (size_t)c.vocab * 4,
@@ -1054,6 +1122,8 @@ int init_device(spec_model* m, const spec_load_opts* opts) {
   m->use_graphs = opts ? (opts->use_graphs != 0) : true;
   if (getenv("SPEC_B200_NO_GRAPHS")) m->use_graphs = false;
   if (getenv("SPEC_B200_NO_PDL")) m->use_pdl = false;
+  if (getenv("SPEC_B200_ATTN_KERNELS")) m->fused_attn = false;
+  if (getenv("SPEC_B200_NO_ATTN_TRIGGER")) m->attn_trigger = false;
   if (const char* env = getenv("SPEC_B200_L2_AHEAD")) m->l2_ahead = atoi(env);
   cudaError_t e = cudaSetDevice(m->device);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "cudaSetDevice"));
@@ -2807,11 +2877,12 @@ int spec_profile_forward(spec_model* m, const uint32_t* drafts, int k, float* ms
 }
 
 int spec_kernels_per_forward(const spec_model* m, int rows) {
-  (void)rows;
   if (!m) return 0;
-  // embed + layer-0 qkv + per layer (attention split, combine, one multi-op
-  // GEMV launch for o / gate-up / down / next qkv or the LM head)
-  return 2 + 3 * m->cfg.n_layers;
+  // embed + layer-0 qkv (+ its attention) + per layer one multi-op launch
+  // (o / gate-up / down / next qkv and attention, or the LM head); with
+  // attention as its own kernels, a split and a combine launch per layer.
+  const bool fused = rows >= 1 && rows <= kMaxRows && attn_fused(m, rows);
+  return 2 + (fused ? 1 : 3) * m->cfg.n_layers;
 }
 
 int64_t spec_weight_bytes(const spec_model* m) { return m ? m->weight_bytes : 0; }

@@ -36,8 +36,11 @@
 //    activations, so weight streaming overlaps the predecessor's tail.
 #include "common.cuh"
 #include "kernels.cuh"
+#include "attn_core.cuh"
 
 #include <stdlib.h>
+
+#include <type_traits>
 
 namespace specb200 {
 
@@ -854,14 +857,21 @@ SPEC_DEV int chunk_start(const QmvParams& q, int i) { return (int)(((long long)i
 SPEC_DEV int chunk_of(const QmvParams& q, int s) { return (int)(((long long)(s + 1) * q.chunks - 1) / q.stages); }
 
 // Walks (op, chunk, stage) for CTA c in schedule order: chunks c, c+G, ...
+// The producer's walks skip the attention ops (no weight stream).
 struct SeqIt {
   int op = 0, k = 0, s = 0, s_end = 0;
   bool valid = false;
+  bool gemv_only = false;
 };
 
 SPEC_DEV void seq_settle(const FwdParams& P, int c, int G, SeqIt& it) {
   // Move to the first non-empty chunk at or after (it.op, it.k).
   while (it.op < P.n_ops) {
+    if (it.gemv_only && P.ops[it.op].kind != OPK_GEMV) {
+      ++it.op;
+      it.k = 0;
+      continue;
+    }
     const QmvParams& q = P.ops[it.op].q;
     const int i = c + it.k * G;
     if (i < q.chunks) {
@@ -879,8 +889,9 @@ SPEC_DEV void seq_settle(const FwdParams& P, int c, int G, SeqIt& it) {
   }
   it.valid = false;
 }
-SPEC_DEV void seq_begin(const FwdParams& P, int c, int G, SeqIt& it) {
+SPEC_DEV void seq_begin(const FwdParams& P, int c, int G, SeqIt& it, bool gemv_only) {
   it = SeqIt{};
+  it.gemv_only = gemv_only;
   seq_settle(P, c, G, it);
 }
 SPEC_DEV void seq_next(const FwdParams& P, int c, int G, SeqIt& it) {
@@ -939,6 +950,124 @@ SPEC_DEV void process_any(int fmt, const uint8_t* tp, const uint8_t* xs, float* 
 
 SPEC_DEV int x32_bytes(int fmt, int NT) { return fmt == WF_BF16 ? 0 : (fmt_kt(fmt) / 32) * 8 * NT * 4; }
 SPEC_DEV int x16_bytes(int fmt, int NT) { return fmt == WF_BF16 ? 0 : (fmt_kt(fmt) / 16) * 8 * NT * 4; }
+
+constexpr int kAttnParamBytes = 256;  // ring bytes an attention unit keeps its parameters in
+static_assert(sizeof(AttnParams) <= kAttnParamBytes, "AttnParams outgrew its ring slot");
+
+// Keys per pass an attention split unit stages in a ring of `ring` bytes
+// (a multiple of attn::kKeyBlock, at most the split's chunk).
+__host__ __device__ inline int attn_keys_per_pass(int ring, int hd, int chunk) {
+  const int kp = ((ring / (2 * (hd + 8)) - attn::kWarps * 16) / 2) & ~(attn::kKeyBlock - 1);
+  return kp < chunk ? kp : chunk;
+}
+
+// One unit of an attention op, run by the 4 consumer warps after every GEMV
+// stage of this CTA was consumed (the ring is drained and reused as the
+// key / query staging).  Split units wait for the QKV groups of their KV
+// head (per-group flags, or the dependency's done count) and count
+// themselves in `done`; combine units wait for every split unit.
+template <int NT>
+SPEC_DEV void attn_op_unit(const FwdOp* ops, int* done, const int* gflags, int flag_stride, unsigned* err, int op,
+                           int u, uint8_t* ring, int ring_bytes, unsigned epoch) {
+  const FwdOp& fo = ops[op];
+  const QmvParams& q = fo.q;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // The unit's parameters live in the last bytes of the ring (shared
+  // memory), not in registers.
+  ring_bytes -= kAttnParamBytes;
+  AttnParams* ap = reinterpret_cast<AttnParams*>(ring + ring_bytes);
+  consumer_sync();  // every warp is done with the ring (GEMV stages or the previous unit)
+  if (tid == 0) {
+    AttnParams& a = *ap;
+    a.q = q.qbuf;
+    a.kcache = q.kcache;
+    a.vcache = q.vcache;
+    a.n_kv = q.n_kv_heads;
+    a.G = q.n_q_heads / q.n_kv_heads;
+    a.hd = q.head_dim;
+    a.M = q.M;
+    a.t_max = q.t_max;
+    a.step = q.attn_step;
+    a.anc = q.attn_anc;
+    a.scale_log2 = q.attn_scale_log2;
+    a.chunk = q.attn_chunk;
+    a.max_splits = q.attn_max_splits;
+    a.part_o = q.attn_o;
+    a.part_ml = q.attn_ml;
+    a.frag = q.next_frag;
+    a.xsum16 = q.next_xsum16;
+    a.xsum32 = q.next_xsum32;
+    a.act_bf16 = q.act_bf16;
+    a.err = q.err;
+  }
+  consumer_sync();
+  const AttnParams& a = *ap;
+  const int dep = fo.dep;
+  if (fo.kind == OPK_ATTN_SPLIT) {
+    const int kvh = u % a.n_kv, split = u / a.n_kv;
+    auto wait_inputs = [&]() {
+      if (dep >= 0 && tid == 0) {
+        // The QKV groups holding this KV head's q rows, k rows and v rows.
+        const int hd = a.hd, G = a.G, nq = q.n_q_heads, nkv = a.n_kv;
+        const int r0[3] = {kvh * G * hd, nq * hd + kvh * hd, (nq + nkv) * hd + kvh * hd};
+        const int rn[3] = {G * hd, hd, hd};
+        const QmvParams& d = ops[dep].q;
+        const int dgroups = d.seg[0].groups + d.seg[1].groups;
+        const int* fl = gflags ? gflags + (size_t)dep * flag_stride : nullptr;
+        unsigned long long t0 = 0;
+        for (;;) {
+          bool ok = ld_relaxed_gpu(done + dep) >= dgroups;
+          if (!ok && fl) {
+            ok = true;
+            for (int j = 0; j < 3; ++j)
+              for (int g2 = r0[j] / kGroupRows; g2 <= (r0[j] + rn[j] - 1) / kGroupRows; ++g2)
+                ok &= ld_relaxed_gpu(fl + g2) == (int)epoch;
+          }
+          if (ok) break;
+          const unsigned long long now = global_timer_ns();
+          if (t0 == 0) {
+            t0 = now;
+          } else if (now - t0 > kMbarTimeoutNs) {
+            wait_gave_up(err, WAIT_ATTN_DEP, op, u, ld_relaxed_gpu(done + dep));
+            break;
+          }
+        }
+        fence_acq_rel_gpu();
+      }
+      consumer_sync();
+    };
+    const int kp = attn_keys_per_pass(ring_bytes, a.hd, a.chunk);
+    if (a.hd == 128) {
+      if (a.act_bf16) attn::split_unit<128, true>(a, split, kvh, ring, kp, wait_inputs);
+      else attn::split_unit<128, false>(a, split, kvh, ring, kp, wait_inputs);
+    } else {
+      if (a.act_bf16) attn::split_unit<64, true>(a, split, kvh, ring, kp, wait_inputs);
+      else attn::split_unit<64, false>(a, split, kvh, ring, kp, wait_inputs);
+    }
+    consumer_sync();  // every thread's partial stores are issued
+    if (tid == 0) {
+      fence_acq_rel_gpu();
+      red_add_relaxed(done + op, 1);
+    }
+  } else {
+    if (dep >= 0) {
+      const int need = ops[dep].q.chunks;  // every split unit
+      unsigned long long t0 = 0;
+      while (ld_acquire(done + dep) < need) {
+        const unsigned long long now = global_timer_ns();
+        if (t0 == 0) {
+          t0 = now;
+        } else if (now - t0 > kMbarTimeoutNs) {
+          if (lane == 0) wait_gave_up(err, WAIT_ATTN_DEP, op, u, ld_relaxed_gpu(done + dep));
+          break;
+        }
+      }
+    }
+    __syncwarp();
+    if (a.hd == 128) attn::combine_item<128>(a, NT, u * kGemvWarps + warp, lane);
+    else attn::combine_item<64>(a, NT, u * kGemvWarps + warp, lane);
+  }
+}
 
 // Persistent, warp-specialized multi-op GEMV (see FwdOp).  Warp 4 lane 0 is
 // the producer: it keeps a weight cursor up to D stages ahead of the
@@ -1031,7 +1160,7 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
         tma_prefetch_l2(sg.w + ((size_t)L.lgrp * sg.k_tiles + L.kt) * kGemvWarps * pair, kGemvWarps * pair);
       };
       SeqIt wi, xi, pi;
-      seq_begin(P, c, G, wi);
+      seq_begin(P, c, G, wi, true);
       xi = wi;
       pi = wi;
       int wpos = 0, xpos = 0, ppos = 0;
@@ -1122,9 +1251,10 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
   bool ok = true;
   int pos = 0;
   SeqIt it;
-  seq_begin(P, c, G, it);
+  seq_begin(P, c, G, it, false);
   while (it.valid) {
     const int op = it.op;
+    if (P.ops[op].kind != OPK_GEMV) break;  // the attention ops, below
     const QmvParams& q = P.ops[op].q;
     const int own = c + it.k * G;
 #pragma unroll
@@ -1168,6 +1298,23 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
             for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
       }
     }
+    it.s = it.s_end - 1;
+    seq_next(P, c, G, it);
+  }
+  // Attention ops follow every GEMV op of the launch: one chunk = one unit.
+  // Every GEMV piece of this CTA is done: the next forward kernel may be
+  // scheduled (its CTAs take the slots of CTAs that exit, stream their first
+  // weight stages, and wait for this grid's completion before reading
+  // anything it writes), so its launch overlaps the attention tail.
+  if (it.valid && Pg.trigger_after_gemv) pdl_launch_dependents();
+  static_assert(FG::RING % 16 == 0 && FG::RING > kAttnParamBytes, "ring too small for attention units");
+  while (it.valid) {
+    if (s_ops[it.op].kind == OPK_GEMV) {  // schedules put attention last: a GEMV op here is a bad schedule
+      if (threadIdx.x == 0) atomicOr(Pg.err, DEV_ERR_BAD_ARGUMENT);
+      break;
+    }
+    for (int u = it.s; u < it.s_end; ++u)
+      attn_op_unit<NT>(s_ops, Pg.done, Pg.gflags, Pg.flag_stride, Pg.err, it.op, u, ring, FG::RING, epoch);
     it.s = it.s_end - 1;
     seq_next(P, c, G, it);
   }
@@ -1403,6 +1550,20 @@ constexpr int kSetK5 = FS_Q5K | FS_Q6K | FS_Q80;
 constexpr int kSetBF = FS_BF16;
 
 }  // namespace
+
+int fwd_attn_keys_per_pass(int set, int M, int hd, int chunk) {
+  const int nt = nt_for_rows(M);
+  int ring = 0;
+  auto pick = [&](auto tag) {
+    constexpr int S = decltype(tag)::value;
+    ring = nt == 1 ? FGeo<S, 1>::RING : nt == 2 ? FGeo<S, 2>::RING : nt == 4 ? FGeo<S, 4>::RING : FGeo<S, 8>::RING;
+  };
+  if (set == kSetK4) pick(std::integral_constant<int, kSetK4>{});
+  else if (set == kSetK5) pick(std::integral_constant<int, kSetK5>{});
+  else if (set == kSetBF) pick(std::integral_constant<int, kSetBF>{});
+  else return 0;
+  return attn_keys_per_pass(ring - kAttnParamBytes, hd, chunk);
+}
 
 int fwd_fmt_set_for(int bits) {
   if ((bits & ~kSetK4) == 0) return kSetK4;

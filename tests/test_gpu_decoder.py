@@ -297,3 +297,35 @@ def test_apply_lm_head_topk(pkg, accept, tiny_gguf):
     assert dec.apply_lm_head_topk(hid[3:4], 5)[0].tolist() == [[0, 1, 2, 3, 4]]
     with pytest.raises(pkg.SamplingError):
         dec.apply_lm_head_topk(hid[:1], 65)
+
+
+@pytest.mark.parametrize("name", MODELS)
+def test_fused_attention_matches_attention_kernels(pkg, tiny_gguf, name, monkeypatch):
+    """Attention as ops of the forward kernel (the default) and as its own
+    kernels (SPEC_B200_ATTN_KERNELS, read at load) run the same arithmetic
+    (attn_core.cuh): logits must agree bit for bit, at M = 5 / 13 / 40 rows
+    (three forward-kernel instantiations) over a multi-split KV."""
+    path = tiny_gguf(name)
+    fused = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    monkeypatch.setenv("SPEC_B200_ATTN_KERNELS", "1")
+    sep = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    monkeypatch.delenv("SPEC_B200_ATTN_KERNELS")
+    v = fused.vocab_size()
+    prompt = _prompt(v, 300, 11)  # several 64-key splits; chunked observes
+    for d in (fused, sep):
+        d.observe(prompt)
+    assert np.array_equal(fused.next_logits(), sep.next_logits())
+    for k in (4, 12):
+        drafts = _prompt(v, k, 12 + k)
+        a, b = fused.batched_logits(drafts), sep.batched_logits(drafts)
+        assert np.array_equal(a, b), (k, float(np.abs(a - b).max()))
+        fused.rollback_to(len(prompt))
+        sep.rollback_to(len(prompt))
+    rng = np.random.default_rng(5)
+    edges = [(0, prompt[-1])] + [(int(rng.integers(0, i)), int(rng.integers(0, v))) for i in range(1, 40)]
+    tree = pkg.DraftTree.from_parent_table(edges)
+    a, b = fused.tree_logits(tree), sep.tree_logits(tree)
+    assert np.array_equal(a, b), float(np.abs(a - b).max())
+    assert fused.kernels_per_forward(5) < sep.kernels_per_forward(5)
+    fused.close()
+    sep.close()
