@@ -203,8 +203,9 @@ struct spec_model {
   bool tp_connected = false;
   int l2_ahead = 0;                 // weight stages each CTA prefetches into L2 ahead of its ring (SPEC_B200_L2_AHEAD)
   bool use_pdl = true;              // programmatic dependent launch between forward kernels
-  bool fused_attn = true;           // attention as ops of the forward kernel (else its own kernels)
+  bool fused_attn = false;          // attention as ops of the forward kernel (else its own kernels)
   bool attn_trigger = true;         // a launch's attention tail overlaps the next launch (PDL trigger)
+  bool attn_kernels_pdl = true;     // programmatic launch of the standalone attention kernels
   FwdOp* single_op = nullptr;       // device slot for one-op launches
   FwdOp* single_op_host = nullptr;  // pinned staging
   int* single_done = nullptr;
@@ -400,10 +401,12 @@ int alloc_runtime(spec_model* m) {
   ALLOC(m->qbuf, (size_t)c.n_heads * kMaxRows * hd * 2);
   // Keys per attention split (fixed per model: splits are aligned to absolute
   // key positions, which keeps every row's arithmetic independent of M).
-  // Short contexts take small splits (a split unit stages its keys in one
-  // pass and more units run at once), long ones larger splits (fewer
-  // partials to merge).
-  m->attn_chunk = m->t_max <= 4096 ? 64 : m->t_max <= 8192 ? 128 : 256;
+  // Long contexts take larger splits (fewer partials to merge).
+  m->attn_chunk = m->t_max <= 8192 ? 128 : 256;
+  if (const char* env = getenv("SPEC_B200_ATTN_CHUNK")) {  // tuning override: 64, 128 or 256 keys
+    const int v = atoi(env);
+    if (v == 64 || v == 128 || v == 256) m->attn_chunk = v;
+  }
   m->attn_max_splits = (m->t_max + m->attn_chunk - 1) / m->attn_chunk;
   const size_t R = (size_t)kMaxRows * G;
   ALLOC(m->part_o, (size_t)c.n_kv * m->attn_max_splits * R * hd * 4);
@@ -914,7 +917,11 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
       a.xsum32 = m->xb32;
       a.act_bf16 = c.bf16 ? 1 : 0;
       a.err = m->err_dev;
-      if ((e = launch_attention(a, nt, s, pdl)) != cudaSuccess) return e;
+      // 64-key splits launch 512+ small split CTAs; chained programmatically
+      // ahead of the next forward kernel they lost a GEMV group's completion
+      // on B200 (a bounded wait fired), so they run without the early launch.
+      const bool attn_pdl = pdl && m->attn_kernels_pdl && m->attn_chunk >= 128;
+      if ((e = launch_attention(a, nt, s, attn_pdl)) != cudaSuccess) return e;
       if ((e = prof_mark(pr, s, K_ATTN, attn_bytes)) != cudaSuccess) return e;
     }
     if (collect) {
@@ -1122,8 +1129,9 @@ int init_device(spec_model* m, const spec_load_opts* opts) {
   m->use_graphs = opts ? (opts->use_graphs != 0) : true;
   if (getenv("SPEC_B200_NO_GRAPHS")) m->use_graphs = false;
   if (getenv("SPEC_B200_NO_PDL")) m->use_pdl = false;
-  if (getenv("SPEC_B200_ATTN_KERNELS")) m->fused_attn = false;
+  if (getenv("SPEC_B200_FUSED_ATTN")) m->fused_attn = true;
   if (getenv("SPEC_B200_NO_ATTN_TRIGGER")) m->attn_trigger = false;
+  if (getenv("SPEC_B200_ATTN_KERNELS_NO_PDL")) m->attn_kernels_pdl = false;
   if (const char* env = getenv("SPEC_B200_L2_AHEAD")) m->l2_ahead = atoi(env);
   cudaError_t e = cudaSetDevice(m->device);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "cudaSetDevice"));

@@ -301,17 +301,17 @@ def test_apply_lm_head_topk(pkg, accept, tiny_gguf):
 
 @pytest.mark.parametrize("name", MODELS)
 def test_fused_attention_matches_attention_kernels(pkg, tiny_gguf, name, monkeypatch):
-    """Attention as ops of the forward kernel (the default) and as its own
-    kernels (SPEC_B200_ATTN_KERNELS, read at load) run the same arithmetic
+    """Attention as its own kernels (the default) and as ops of the forward
+    kernel (SPEC_B200_FUSED_ATTN, read at load) run the same arithmetic
     (attn_core.cuh): logits must agree bit for bit, at M = 5 / 13 / 40 rows
     (three forward-kernel instantiations) over a multi-split KV."""
     path = tiny_gguf(name)
-    fused = pkg.B200Decoder.from_gguf(path, max_ctx=512)
-    monkeypatch.setenv("SPEC_B200_ATTN_KERNELS", "1")
     sep = pkg.B200Decoder.from_gguf(path, max_ctx=512)
-    monkeypatch.delenv("SPEC_B200_ATTN_KERNELS")
+    monkeypatch.setenv("SPEC_B200_FUSED_ATTN", "1")
+    fused = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    monkeypatch.delenv("SPEC_B200_FUSED_ATTN")
     v = fused.vocab_size()
-    prompt = _prompt(v, 300, 11)  # several 64-key splits; chunked observes
+    prompt = _prompt(v, 300, 11)  # several 128-key splits; chunked observes
     for d in (fused, sep):
         d.observe(prompt)
     assert np.array_equal(fused.next_logits(), sep.next_logits())
