@@ -14,7 +14,9 @@
 //    a 32-row slice.  Tiles are laid out [group][k-tile][warp], so one stage
 //    (128 rows x one k-tile) is a single TMA bulk copy (cp.async.bulk ->
 //    shared, mbarrier completion, L2 evict-first) into a 2-3 stage ring.
-//  * Codes become f16 with one LOP3 each (magic 0x6400: value = 1024 + q),
+//  * Codes become f16 with one LOP3 each (magic 0x6400: value = 1024 + q;
+//    Q4_K / Q5_K rows g+8 take the high nibble in place, 1024 + 16q, with the
+//    1/16 folded into their sub-block scales),
 //    feed mma.sync with the activation fragments, and the accumulator is
 //    seeded with -offset * (sum of the activations of that sub-block), so the
 //    tensor core returns exactly sum(q * x) for the sub-block.  The sub-block
@@ -80,12 +82,16 @@ SPEC_DEV void k4_scale_min(const uint4& m, int b, int& sc, int& mn) {
 SPEC_DEV uint32_t shift_signed(uint32_t v, int delta) { return delta >= 0 ? (v >> delta) : (v << (-delta)); }
 
 // Four A registers (rows g/g+8, cols 2t..+1 / 2t+8..+9) from one word of
-// eight 4-bit codes: value = 1024 + code.
+// eight 4-bit codes.  Rows g (a[0], a[2]) hold 1024 + code; rows g+8 (a[1],
+// a[3]) are the high nibble of each byte masked in place, 1024 + 16 * code
+// (exact in f16: 16 * 15 < 1024).  That saves two shifts per word; the
+// sub-block scales of rows g+8 carry the 1/16 (decode_scales), which is exact.
 SPEC_DEV void a_from_nibbles(uint32_t w, uint32_t (&a)[4]) {
   a[0] = lop3_and_or(w, 0x000F000Fu, 0x64006400u);
-  a[1] = lop3_and_or(w >> 4, 0x000F000Fu, 0x64006400u);
-  a[2] = lop3_and_or(w >> 8, 0x000F000Fu, 0x64006400u);
-  a[3] = lop3_and_or(w >> 12, 0x000F000Fu, 0x64006400u);
+  a[1] = lop3_and_or(w, 0x00F000F0u, 0x64006400u);
+  const uint32_t w8 = w >> 8;
+  a[2] = lop3_and_or(w8, 0x000F000Fu, 0x64006400u);
+  a[3] = lop3_and_or(w8, 0x00F000F0u, 0x64006400u);
 }
 
 // ---------------------------------------------------------------------------
@@ -105,11 +111,13 @@ SPEC_DEV void decode_scales(const uint8_t* tp, float* scr, int lane) {
     const uint4 m = *reinterpret_cast<const uint4*>(tp + rt * TB + MO + ri * 16);
     const float d = h2f_bits(m.x), dm = h2f_bits(m.x >> 16);
     int mv[8];
+    // Rows 8-15 of the tile meet their codes as 16 * code (a_from_nibbles).
+    const float rs = (ri >> 3) ? 0.0625f : 1.f;
 #pragma unroll
     for (int sb = 0; sb < 8; ++sb) {
       int sc;
       k4_scale_min(m, sb, sc, mv[sb]);
-      scr[((rt * 8 + sb) * 8 + (ri & 7)) * 2 + (ri >> 3)] = d * (float)sc;
+      scr[((rt * 8 + sb) * 8 + (ri & 7)) * 2 + (ri >> 3)] = d * (float)sc * rs;
     }
     uint32_t* mw = reinterpret_cast<uint32_t*>(scr + 256);
 #pragma unroll
@@ -199,8 +207,13 @@ SPEC_DEV void tile_q45k(const uint8_t* tp, const uint8_t* xs, const float* scr, 
           const int i = 2 * sb + h;
           a_from_nibbles(wv[i], a[h]);
           if (q5) {
+            // The fifth bit: weight 16 (bit 4) in rows g, 256 (bit 8) in the
+            // x16 rows g+8.
 #pragma unroll
-            for (int jj = 0; jj < 4; ++jj) a[h][jj] = lop3_or_and(a[h][jj], shift_signed(hw, 4 * i + jj - 4), 0x00100010u);
+            for (int jj = 0; jj < 4; jj += 2) {
+              a[h][jj] = lop3_or_and(a[h][jj], shift_signed(hw, 4 * i + jj - 4), 0x00100010u);
+              a[h][jj + 1] = lop3_or_and(a[h][jj + 1], shift_signed(hw, 4 * i + jj + 1 - 8), 0x01000100u);
+            }
           }
         }
 #pragma unroll
