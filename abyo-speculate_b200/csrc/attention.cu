@@ -16,7 +16,12 @@ template <int HD, bool BF16>
 __global__ void __launch_bounds__(128) attn_split_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ __align__(128) uint8_t smem_raw[];
   pdl_launch_dependents();
-  attn::split_unit<HD, BF16>(p, blockIdx.x, blockIdx.y, smem_raw, p.chunk, [] { pdl_wait(); });
+  // Up to two 16-row tiles, warp pairs split the head columns (all four
+  // warps busy); more tiles take one warp each (S formed once per tile).
+  if (p.M * p.G <= 32)
+    attn::split_unit<HD, BF16, 2>(p, blockIdx.x, blockIdx.y, smem_raw, p.chunk, [] { pdl_wait(); });
+  else
+    attn::split_unit<HD, BF16, 1>(p, blockIdx.x, blockIdx.y, smem_raw, p.chunk, [] { pdl_wait(); });
 }
 
 template <int HD>

@@ -46,8 +46,12 @@ SPEC_DEV void sync128() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 // once by all 128 threads, after the prefix keys' loads are issued and before
 // any load of what the QKV projection of this forward wrote (new keys, q
 // rows).  Returns false when the split holds no key (nothing written).
-template <int HD, bool BF16, class Wait>
+// DS = warps per 16-row tile (1 or 2), each accumulating P.V for HD/DS head
+// columns; S and the softmax state are formed the same way by each, so the
+// result does not depend on DS.
+template <int HD, bool BF16, int DS, class Wait>
 SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem, int kp, Wait&& wait_inputs) {
+  static_assert(DS == 1 || DS == 2, "one or two warps per row tile");
   constexpr int STR = Smem<HD>::STRIDE;
   constexpr int CH = HD / 8;  // 16-byte chunks per row
   const int C = p.chunk;
@@ -102,14 +106,15 @@ SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem,
     }
   };
 
-  // Warps 2i and 2i+1 share row tile rt0 + i: both form S and the softmax
-  // state (identical arithmetic), each accumulates P.V for half of the head
-  // dimensions (dims [dh*HD/2, dh*HD/2 + HD/2)).
-  constexpr int HALF = HD / 16;  // 8-column blocks per half
-  const int dh = warp & 1;
+  // With DS = 2, warps 2i and 2i+1 share row tile rt0 + i: both form S and
+  // the softmax state (identical arithmetic), each accumulates P.V for half
+  // of the head dimensions (dims [dh*HD/2, dh*HD/2 + HD/2)).
+  constexpr int HALF = HD / 8 / DS;  // 8-column blocks per warp
+  constexpr int TPR = kWarps / DS;   // row tiles per round
+  const int dh = DS == 2 ? (warp & 1) : 0;
   bool first_load = true;
-  for (int rt0 = 0; rt0 < RT; rt0 += kWarps / 2) {
-    const int rt = rt0 + (warp >> 1);  // this warp's 16-row tile (idle when >= RT)
+  for (int rt0 = 0; rt0 < RT; rt0 += TPR) {
+    const int rt = rt0 + warp / DS;  // this warp's 16-row tile (idle when >= RT)
     unsigned long long anc[2];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
@@ -278,14 +283,14 @@ SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem,
             p.part_ml[base * 2 + 0] = mrow[h];
             p.part_ml[base * 2 + 1] = lrow[h];
           }
-          float* po = p.part_o + base * HD + dh * (HD / 2);
+          float* po = p.part_o + base * HD + dh * (HD / DS);
 #pragma unroll
           for (int j = 0; j < HALF; ++j)
             *reinterpret_cast<float2*>(po + j * 8 + 2 * t) = make_float2(o[j][2 * h], o[j][2 * h + 1]);
         }
       }
     }
-    if (rt0 + kWarps / 2 < RT) sync128();  // the next round restages the q rows
+    if (rt0 + TPR < RT) sync128();  // the next round restages the q rows
   }
   return true;
 }

@@ -1051,11 +1051,11 @@ SPEC_DEV void attn_op_unit(const FwdOp* ops, int* done, const int* gflags, int f
     };
     const int kp = attn_keys_per_pass(ring_bytes, a.hd, a.chunk);
     if (a.hd == 128) {
-      if (a.act_bf16) attn::split_unit<128, true>(a, split, kvh, ring, kp, wait_inputs);
-      else attn::split_unit<128, false>(a, split, kvh, ring, kp, wait_inputs);
+      if (a.act_bf16) attn::split_unit<128, true, 2>(a, split, kvh, ring, kp, wait_inputs);
+      else attn::split_unit<128, false, 2>(a, split, kvh, ring, kp, wait_inputs);
     } else {
-      if (a.act_bf16) attn::split_unit<64, true>(a, split, kvh, ring, kp, wait_inputs);
-      else attn::split_unit<64, false>(a, split, kvh, ring, kp, wait_inputs);
+      if (a.act_bf16) attn::split_unit<64, true, 2>(a, split, kvh, ring, kp, wait_inputs);
+      else attn::split_unit<64, false, 2>(a, split, kvh, ring, kp, wait_inputs);
     }
     consumer_sync();  // every thread's partial stores are issued
     if (tid == 0) {
