@@ -77,6 +77,13 @@ class EagleWeights(ctypes.Structure):
         ("rope_theta", ctypes.c_float)]
 
 
+class MedusaWeights(ctypes.Structure):
+    """spec_medusa_weights (include/spec_b200.h)."""
+
+    _fields_ = [("n_heads", ctypes.c_int), ("residual_layers", ctypes.c_int), ("res_w", ctypes.c_void_p),
+                ("res_b", ctypes.c_void_p), ("out_w", ctypes.c_void_p)]
+
+
 class LoadOpts(ctypes.Structure):
     _fields_ = [("device", ctypes.c_int), ("max_ctx", ctypes.c_int), ("use_graphs", ctypes.c_int),
                 ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int), ("reserved", ctypes.c_int * 3)]
@@ -120,6 +127,11 @@ SIGNATURES = [
     ("spec_eagle_draft", ctypes.c_int,
      [ctypes.c_void_p, c_f32_p, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_int,
       ctypes.POINTER(ctypes.c_int32), c_f32_p]),
+    ("spec_medusa_attach", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    ("spec_medusa_attach_synthetic", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_uint64]),
+    ("spec_medusa_topk", ctypes.c_int,
+     [ctypes.c_void_p, c_f32_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int32), c_f32_p]),
+    ("spec_medusa_num_heads", ctypes.c_int, [ctypes.c_void_p]),
     ("spec_sd_greedy_round", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_int)]),
     ("spec_apply_lm_head_topk", ctypes.c_int,

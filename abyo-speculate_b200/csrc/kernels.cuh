@@ -314,6 +314,8 @@ cudaError_t launch_eagle_resid_norm(const float* t, const float* h, const float*
                                     float* xn, cudaStream_t s);
 cudaError_t launch_eagle_add(const float* a, const float* b, float* out, int n, cudaStream_t s);
 cudaError_t launch_row_lse(const float* x, int V, float* out, cudaStream_t s);
+// Medusa residual block update: out = x + SiLU(y) (methods/medusa.rs:571-575).
+cudaError_t launch_medusa_res(const float* x, const float* y, float* out, int n, cudaStream_t s);
 
 // ---- synthetic weight generation (seeded N(0, sigma) then quantized) -------
 cudaError_t launch_synth_quant(uint8_t* raw, int fmt, int rows, int K, uint64_t seed, float sigma,

@@ -333,6 +333,16 @@ __global__ void eagle_add_kernel(const float* a, const float* b, float* out, int
   if (i < n) out[i] = a[i] + b[i];
 }
 
+// A Medusa residual block's update (methods/medusa.rs:571-575):
+// out = x + SiLU(y), y = the block's linear output (bias included).
+__global__ void medusa_res_kernel(const float* x, const float* y, float* out, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) {
+    const float v = y[i];
+    out[i] = x[i] + v / (1.f + expf(-v));
+  }
+}
+
 // log(sum(exp(x - max))) + max over one row (NaN entries skipped).  One CTA.
 __global__ void __launch_bounds__(1024) row_lse_kernel(const float* x, int V, float* out) {
   __shared__ float red[32];
@@ -600,6 +610,10 @@ cudaError_t launch_eagle_resid_norm(const float* t, const float* h, const float*
 }
 cudaError_t launch_eagle_add(const float* a, const float* b, float* out, int n, cudaStream_t s) {
   eagle_add_kernel<<<(n + 255) / 256, 256, 0, s>>>(a, b, out, n);
+  return cudaGetLastError();
+}
+cudaError_t launch_medusa_res(const float* x, const float* y, float* out, int n, cudaStream_t s) {
+  medusa_res_kernel<<<(n + 255) / 256, 256, 0, s>>>(x, y, out, n);
   return cudaGetLastError();
 }
 cudaError_t launch_row_lse(const float* x, int V, float* out, cudaStream_t s) {

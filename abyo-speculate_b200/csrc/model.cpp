@@ -91,6 +91,7 @@ float bf_round(float f) {
 }  // namespace
 
 struct EagleHead;  // the EAGLE draft block attached to a target (spec_eagle_*)
+struct MedusaHeads;  // Medusa draft heads attached to a target (spec_medusa_*)
 
 struct spec_model {
   ModelCfg cfg;
@@ -148,6 +149,7 @@ struct spec_model {
   int* argmax_dev = nullptr;
   unsigned long long* argmax_slots = nullptr;  // row argmax scratch (self-clearing)
   std::shared_ptr<EagleHead> eagle;            // spec_eagle_attach*: device memory owned via dalloc
+  std::shared_ptr<MedusaHeads> medusa;         // spec_medusa_attach*: device memory owned via dalloc
   unsigned long long* topk_part = nullptr;     // row top-k scratch (allocated on first use)
   int* topk_ids = nullptr;
   float* topk_vals = nullptr;
@@ -235,7 +237,13 @@ struct spec_model {
     if (e != cudaSuccess) return e;
     dev_allocs.push_back(q);
     *p = static_cast<T*>(q);
-    return cudaMemsetAsync(q, 0, bytes ? bytes : 16, stream);
+    // Zeroed before returning: the synchronous uploads that often follow run
+    // on the legacy stream, which is not ordered after this non-blocking one.
+    // (Never called during stream capture: graphs are captured only after a
+    // first eager forward has made every buffer.)
+    e = cudaMemsetAsync(q, 0, bytes ? bytes : 16, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    return e;
   }
   template <class T>
   cudaError_t halloc(T** p, size_t bytes) {
@@ -2041,7 +2049,7 @@ enum : int { EOP_FC = 0, EOP_QKV, EOP_O, EOP_GU, EOP_DOWN, EOP_LM, EOP_N };
 // RoPE tables of the draft: eagle.rs:134-147 computes inv_freq in f32, then
 // positions and inv_freq in the checkpoint dtype (BF16), their product in
 // BF16, and cos/sin of that in BF16; the same roundings here.
-int eagle_rope(spec_model* m, EagleHead& e, float theta) {
+static int eagle_rope(spec_model* m, EagleHead& e, float theta) {
   const ModelCfg& c = m->cfg;
   const int half = c.head_dim / 2, T = m->t_max + kEagleMaxSteps;
   std::vector<float> cs((size_t)T * half), sn((size_t)T * half);
@@ -2062,7 +2070,7 @@ int eagle_rope(spec_model* m, EagleHead& e, float theta) {
 }
 
 // Buffers and the six single-op descriptors, once the matrices exist.
-int eagle_finish(spec_model* m, EagleHead& e) {
+static int eagle_finish(spec_model* m, EagleHead& e) {
   const ModelCfg& c = m->cfg;
   const int H = c.hidden, F = c.ffn, hd = c.head_dim, V = c.vocab, G = c.n_heads / c.n_kv;
   const int Kq = c.n_heads * hd;
@@ -2210,7 +2218,7 @@ int eagle_finish(spec_model* m, EagleHead& e) {
   return SPEC_OK;
 }
 
-int eagle_build(spec_model* m, const Part& fc, const Part& q, const Part& k, const Part& v, const Part& o,
+static int eagle_build(spec_model* m, const Part& fc, const Part& q, const Part& k, const Part& v, const Part& o,
                 const Part& g, const Part& u, const Part& d, float theta, std::shared_ptr<EagleHead>& out) {
   const ModelCfg& c = m->cfg;
   auto e = std::make_shared<EagleHead>();
@@ -2227,7 +2235,7 @@ int eagle_build(spec_model* m, const Part& fc, const Part& q, const Part& k, con
   return rc;
 }
 
-int eagle_check_target(spec_model* m) {
+static int eagle_check_target(spec_model* m) {
   const ModelCfg& c = m->cfg;
   if (m->tp_size > 1) return m->fail(SPEC_ERR_UNSUPPORTED, "EAGLE draft on a tensor-parallel handle");
   if ((2 * c.hidden) % 128 || c.hidden % 128 || c.ffn % 128 || (c.n_heads * c.head_dim) % 128)
@@ -2381,6 +2389,242 @@ int spec_eagle_draft(spec_model* m, const float* hidden, uint32_t root, int posi
     for (int i = 0; i < depth * k; ++i) logprobs_out[i] = e->vals_host[i] - e->lse_host[i / k];
   return SPEC_OK;
 }
+
+// ---------------------------------------------------------------------------
+// Medusa draft heads on the device (methods/medusa.rs:509-584, 706-734)
+// ---------------------------------------------------------------------------
+struct MedusaHeads {
+  int n_heads = 0, layers = 0;
+  std::vector<Mat> res;        // [head][layer] BF16 [H][H]
+  std::vector<float*> res_b;   // [head][layer] f32 [H]
+  std::vector<Mat> out;        // [head] BF16 [V][H]
+  float *hin = nullptr, *x = nullptr, *y = nullptr, *logits = nullptr;
+  uint32_t* xa = nullptr;
+  float *xa16 = nullptr, *xa32 = nullptr;
+  float* gpart = nullptr;
+  int* gcounters = nullptr;
+  FwdOp* ops = nullptr;        // [head][layer] residual linears, then [head] output projections
+  int* done = nullptr;
+  int* ids = nullptr;
+  float* vals = nullptr;
+  float* lse = nullptr;
+  int* ids_host = nullptr;
+  float* vals_host = nullptr;
+  float* lse_host = nullptr;
+  int set_bf = 0;
+};
+
+namespace {
+
+constexpr int kMedusaMaxHeads = 8;
+constexpr int kMedusaMaxLayers = 4;
+
+static int medusa_check(spec_model* m, int n_heads, int layers) {
+  const ModelCfg& c = m->cfg;
+  if (n_heads < 1 || n_heads > kMedusaMaxHeads || layers < 0 || layers > kMedusaMaxLayers)
+    return m->fail(SPEC_ERR_INVALID, "Medusa heads: 1..8 heads of 0..4 residual layers");
+  if (m->tp_size > 1) return m->fail(SPEC_ERR_UNSUPPORTED, "Medusa heads on a tensor-parallel handle");
+  if (c.hidden % 128 || c.vocab % 128) return m->fail(SPEC_ERR_UNSUPPORTED, "Medusa head shapes are not multiples of 128");
+  return SPEC_OK;
+}
+
+// Builds the heads' matrices from parts ([head][layer] residual weights, then
+// [head] output projections) and their buffers and op descriptors.
+static int medusa_build(spec_model* m, int n_heads, int layers, const std::vector<Part>& res, const std::vector<Part>& outp,
+                 std::shared_ptr<MedusaHeads>& out) {
+  const ModelCfg& c = m->cfg;
+  const int H = c.hidden, V = c.vocab;
+  auto h = std::make_shared<MedusaHeads>();
+  h->n_heads = n_heads;
+  h->layers = layers;
+  h->res.resize((size_t)n_heads * layers);
+  h->res_b.assign((size_t)n_heads * layers, nullptr);
+  h->out.resize(n_heads);
+  const int saved_bits = m->fmt_bits;  // the heads' BF16 does not join the target's format set
+  int rc = SPEC_OK;
+  for (size_t i = 0; i < h->res.size() && rc == SPEC_OK; ++i) rc = build_mat(m, {res[i]}, H, false, h->res[i]);
+  for (int i = 0; i < n_heads && rc == SPEC_OK; ++i) rc = build_mat(m, {outp[i]}, H, false, h->out[i]);
+  m->fmt_bits = saved_bits;
+  if (rc != SPEC_OK) return rc;
+  cudaError_t er = cudaSuccess;
+#define MALLOC(ptr, bytes)                                                     \
+  do {                                                                         \
+    if (er == cudaSuccess) er = m->dalloc(&(ptr), (bytes));                    \
+  } while (0)
+  MALLOC(h->hin, (size_t)H * 4);
+  MALLOC(h->x, (size_t)H * 4);
+  MALLOC(h->y, (size_t)H * 4);
+  MALLOC(h->logits, (size_t)V * 4);
+  MALLOC(h->xa, (size_t)H * 16);  // one row's operand: H/16 k-steps x 256 bytes (NT = 1)
+  MALLOC(h->xa16, (size_t)(H / 16) * 8 * 4);
+  MALLOC(h->xa32, (size_t)(H / 32) * 8 * 4);
+  size_t part = 0;
+  int groups = 0;
+  for (const auto* v : {&h->res, &h->out})
+    for (const Mat& mt : *v) {
+      part = std::max(part, (size_t)partial_slots(mt) * kGroupRows * 8);
+      groups = std::max(groups, mt.seg[0].groups + mt.seg[1].groups);
+    }
+  MALLOC(h->gpart, part * 4);
+  MALLOC(h->gcounters, (size_t)groups * 4);
+  const int n_ops = n_heads * (layers + 1);
+  MALLOC(h->ops, sizeof(FwdOp) * n_ops);
+  MALLOC(h->done, sizeof(int) * n_ops);
+  MALLOC(h->ids, (size_t)n_heads * kMaxTopK * 4);
+  MALLOC(h->vals, (size_t)n_heads * kMaxTopK * 4);
+  MALLOC(h->lse, (size_t)n_heads * 4);
+  if (!m->topk_part) MALLOC(m->topk_part, (size_t)kMaxRows * kTopKMaxChunks * kMaxTopK * 8);
+#undef MALLOC
+  if (er == cudaSuccess) er = m->halloc(&h->ids_host, (size_t)n_heads * kMaxTopK * 4);
+  if (er == cudaSuccess) er = m->halloc(&h->vals_host, (size_t)n_heads * kMaxTopK * 4);
+  if (er == cudaSuccess) er = m->halloc(&h->lse_host, (size_t)n_heads * 4);
+  if (er != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(er, "Medusa buffers"));
+  h->set_bf = fwd_fmt_set_for(fmt_bit(WF_BF16));
+  out = h;
+  // The caller fills the residual biases (res_b), then uploads the op
+  // descriptors (medusa_upload_ops).
+  return SPEC_OK;
+}
+
+static int medusa_upload_ops(spec_model* m, MedusaHeads& h) {
+  const int n_ops = h.n_heads * (h.layers + 1);
+  std::vector<FwdOp> ops(n_ops);
+  const ModelCfg& c = m->cfg;
+  for (int i = 0; i < n_ops; ++i) {
+    const bool res = i < h.n_heads * h.layers;
+    const Mat& mt = res ? h.res[i] : h.out[i - h.n_heads * h.layers];
+    QmvParams p = base_params(m, mt, 1);
+    p.part = h.gpart;
+    p.counters = h.gcounters;
+    p.act_bf16 = 1;
+    p.xfrag = h.xa;
+    p.xsum16 = h.xa16;
+    p.xsum32 = h.xa32;
+    p.epi = EPI_STORE;
+    p.out = res ? h.y : h.logits;
+    p.ld_out = res ? c.hidden : c.vocab;
+    p.bias = res ? h.res_b[i] : nullptr;
+    ops[i].q = p;
+    ops[i].dep = -1;
+  }
+  cudaError_t er = cudaMemcpy(h.ops, ops.data(), sizeof(FwdOp) * n_ops, cudaMemcpyHostToDevice);
+  if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "Medusa descriptors"));
+  return SPEC_OK;
+}
+
+}  // namespace
+
+int spec_medusa_attach(spec_model* m, const spec_medusa_weights* w) {
+  if (!m || !w || (w->residual_layers > 0 && (!w->res_w || !w->res_b)) || !w->out_w) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (int rc = medusa_check(m, w->n_heads, w->residual_layers)) return rc;
+  const ModelCfg& c = m->cfg;
+  const int n_res = w->n_heads * w->residual_layers;
+  for (int i = 0; i < n_res; ++i)
+    if (!w->res_w[i] || !w->res_b[i]) return SPEC_ERR_INVALID;
+  for (int i = 0; i < w->n_heads; ++i)
+    if (!w->out_w[i]) return SPEC_ERR_INVALID;
+  auto host = [](const void* src, int rows) {
+    Part p;
+    p.src = static_cast<const uint8_t*>(src);
+    p.on_device = false;
+    p.fmt = WF_BF16;
+    p.rows = rows;
+    return p;
+  };
+  std::vector<Part> res, outp;
+  for (int i = 0; i < n_res; ++i) res.push_back(host(w->res_w[i], c.hidden));
+  for (int i = 0; i < w->n_heads; ++i) outp.push_back(host(w->out_w[i], c.vocab));
+  std::shared_ptr<MedusaHeads> h;
+  int rc = medusa_build(m, w->n_heads, w->residual_layers, res, outp, h);
+  if (rc != SPEC_OK) return rc;
+  for (int i = 0; i < n_res; ++i) {
+    cudaError_t er = m->dalloc(&h->res_b[i], (size_t)c.hidden * 4);
+    if (er == cudaSuccess) er = cudaMemcpy(h->res_b[i], w->res_b[i], (size_t)c.hidden * 4, cudaMemcpyHostToDevice);
+    if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "Medusa biases"));
+  }
+  if ((rc = medusa_upload_ops(m, *h)) != SPEC_OK) return rc;
+  m->medusa = h;
+  return SPEC_OK;
+}
+
+int spec_medusa_attach_synthetic(spec_model* m, int n_heads, int residual_layers, uint64_t seed) {
+  if (!m) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  if (int rc = medusa_check(m, n_heads, residual_layers)) return rc;
+  const ModelCfg& c = m->cfg;
+  std::vector<void*> temps;
+  uint64_t st = seed * 0x9E3779B97F4A7C15ull + 0x3ED05Aull;
+  auto tseed = [&]() { return st += 0x632BE59BD9B4E019ull; };
+  std::vector<Part> res(n_heads * residual_layers), outp(n_heads);
+  int rc = SPEC_OK;
+  for (auto& p : res)
+    if (rc == SPEC_OK) rc = synth_part(m, temps, WF_BF16, c.hidden, c.hidden, tseed(), p);
+  for (auto& p : outp)
+    if (rc == SPEC_OK) rc = synth_part(m, temps, WF_BF16, c.vocab, c.hidden, tseed(), p);
+  std::shared_ptr<MedusaHeads> h;
+  if (rc == SPEC_OK) rc = medusa_build(m, n_heads, residual_layers, res, outp, h);
+  for (int i = 0; rc == SPEC_OK && i < n_heads * residual_layers; ++i)
+    rc = synth_vec(m, &h->res_b[i], c.hidden, tseed(), 0.f);
+  cudaStreamSynchronize(m->stream);
+  for (void* t : temps) cudaFree(t);
+  if (rc == SPEC_OK) rc = medusa_upload_ops(m, *h);
+  if (rc != SPEC_OK) return rc;
+  m->medusa = h;
+  return SPEC_OK;
+}
+
+int spec_medusa_topk(spec_model* m, const float* hidden, int k, int32_t* ids_out, float* logprobs_out) {
+  if (!m || !hidden || !ids_out) return SPEC_ERR_INVALID;
+  cudaSetDevice(m->device);
+  MedusaHeads* h = m->medusa.get();
+  if (!h) return m->fail(SPEC_ERR_INVALID, "no Medusa heads attached (spec_medusa_attach)");
+  const ModelCfg& c = m->cfg;
+  const int H = c.hidden, V = c.vocab;
+  if (k < 1 || k > kMaxTopK || k > V) return m->fail(SPEC_ERR_INVALID, "top-k size out of range");
+  cudaStream_t s = m->stream;
+  cudaError_t er = cudaMemcpyAsync(h->hin, hidden, (size_t)H * 4, cudaMemcpyHostToDevice, s);
+  if (er == cudaSuccess) er = cudaMemsetAsync(m->err_dev, 0, 16, s);
+  auto gemv = [&](int op) {
+    FwdParams fp;
+    fp.ops = h->ops + op;
+    fp.n_ops = 1;
+    fp.done = h->done + op;
+    fp.err = m->err_dev;
+    return launch_fwd(fp, h->set_bf, 1, s, false);
+  };
+  // Every head reads the same hidden row (medusa.rs:706-708).
+  for (int hd = 0; hd < h->n_heads && er == cudaSuccess; ++hd) {
+    const float* x = h->hin;
+    for (int l = 0; l < h->layers && er == cudaSuccess; ++l) {
+      // x' = x + SiLU(W x + b) (medusa.rs:571-575)
+      er = launch_make_operand(x, 1, H, 1, h->xa, h->xa16, h->xa32, 1, s);
+      if (er == cudaSuccess) er = gemv(hd * h->layers + l);
+      if (er == cudaSuccess) er = launch_medusa_res(x, h->y, h->x, H, s);
+      x = h->x;
+    }
+    if (er == cudaSuccess) er = launch_make_operand(x, 1, H, 1, h->xa, h->xa16, h->xa32, 1, s);
+    if (er == cudaSuccess) er = gemv(h->n_heads * h->layers + hd);
+    // top_k_indices over the head's logits (medusa.rs:713-734, 477-487)
+    if (er == cudaSuccess)
+      er = launch_row_topk(h->logits, 1, V, k, m->topk_part, h->ids + (size_t)hd * k, h->vals + (size_t)hd * k, s);
+    if (er == cudaSuccess) er = launch_row_lse(h->logits, V, h->lse + hd, s);
+  }
+  const int n = h->n_heads;
+  if (er == cudaSuccess) er = cudaMemcpyAsync(h->ids_host, h->ids, (size_t)n * k * 4, cudaMemcpyDeviceToHost, s);
+  if (er == cudaSuccess) er = cudaMemcpyAsync(h->vals_host, h->vals, (size_t)n * k * 4, cudaMemcpyDeviceToHost, s);
+  if (er == cudaSuccess) er = cudaMemcpyAsync(h->lse_host, h->lse, (size_t)n * 4, cudaMemcpyDeviceToHost, s);
+  if (er == cudaSuccess) er = cudaMemcpyAsync(m->err_host, m->err_dev, 16, cudaMemcpyDeviceToHost, s);
+  if (er == cudaSuccess) er = cudaStreamSynchronize(s);
+  if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "Medusa heads"));
+  if (m->err_host[0]) return m->fail(SPEC_ERR_TIMEOUT, "device error during the Medusa heads");
+  memcpy(ids_out, h->ids_host, (size_t)n * k * 4);
+  if (logprobs_out)
+    for (int i = 0; i < n * k; ++i) logprobs_out[i] = h->vals_host[i] - h->lse_host[i / k];
+  return SPEC_OK;
+}
+
+int spec_medusa_num_heads(const spec_model* m) { return (m && m->medusa) ? m->medusa->n_heads : 0; }
 
 int spec_embed_tokens(spec_model* m, const uint32_t* ids, int n, float* out) {
   if (!m || !ids || !out || n < 0) return SPEC_ERR_INVALID;

@@ -248,6 +248,45 @@ class B200Decoder:
                                                _ptr(ids, ctypes.c_int32), _ptr(lp, ctypes.c_float)))
         return ids, lp
 
+    def medusa_attach(self, res_w: Sequence[Sequence[np.ndarray]], res_b: Sequence[Sequence[np.ndarray]],
+                      out_w: Sequence[np.ndarray]) -> None:
+        """Medusa heads (medusa.rs:509-584): res_w[head][layer] uint16 BF16 bits
+        [H, H], res_b[head][layer] f32 [H], out_w[head] uint16 BF16 bits [V, H]."""
+        n = len(out_w)
+        layers = len(res_w[0]) if n and len(res_w) else 0
+        if len(res_w) != n or len(res_b) != n or any(len(r) != layers for r in res_w) or \
+                any(len(b) != layers for b in res_b):
+            raise _lib.SamplingError(_lib.SPEC_ERR_INVALID, "res_w / res_b must be [n_heads][residual_layers]")
+        keep = []
+
+        def arr(a, dt):
+            a = np.ascontiguousarray(a, dtype=dt)
+            keep.append(a)
+            return a.ctypes.data
+        rw = (ctypes.c_void_p * max(n * layers, 1))(*[arr(w, np.uint16) for r in res_w for w in r])
+        rb = (ctypes.c_void_p * max(n * layers, 1))(*[arr(b, np.float32) for r in res_b for b in r])
+        ow = (ctypes.c_void_p * max(n, 1))(*[arr(w, np.uint16) for w in out_w])
+        ws = _lib.MedusaWeights(n, layers, ctypes.cast(rw, ctypes.c_void_p), ctypes.cast(rb, ctypes.c_void_p),
+                                ctypes.cast(ow, ctypes.c_void_p))
+        self._check(self._lib.spec_medusa_attach(self._h, ctypes.byref(ws)))
+
+    def medusa_attach_synthetic(self, n_heads: int, residual_layers: int = 1, seed: int = 0) -> None:
+        self._check(self._lib.spec_medusa_attach_synthetic(self._h, int(n_heads), int(residual_layers), int(seed)))
+
+    def medusa_num_heads(self) -> int:
+        return self._lib.spec_medusa_num_heads(self._h)
+
+    def medusa_topk(self, hidden: np.ndarray, k: int) -> Tuple[np.ndarray, np.ndarray]:
+        """MedusaHeadsCandle::top_k_per_head (medusa.rs:713-734) on the device:
+        (ids [n_heads, k], log-probs [n_heads, k])."""
+        n = self.medusa_num_heads()
+        h = np.ascontiguousarray(np.asarray(hidden, dtype=np.float32).reshape(-1))
+        ids = np.empty((max(n, 1), k), dtype=np.int32)
+        lp = np.empty((max(n, 1), k), dtype=np.float32)
+        self._check(self._lib.spec_medusa_topk(self._h, _ptr(h, ctypes.c_float), int(k), _ptr(ids, ctypes.c_int32),
+                                               _ptr(lp, ctypes.c_float)))
+        return ids[:n], lp[:n]
+
     def embed_tokens(self, ids: Sequence[int]) -> np.ndarray:
         a = _u32(ids)
         out = np.empty((a.size, self._hidden), dtype=np.float32)

@@ -199,6 +199,31 @@ int spec_eagle_attach_synthetic(spec_model* m, uint64_t seed);
 int spec_eagle_draft(spec_model* m, const float* hidden, uint32_t root, int position, int depth, int k,
                      int32_t* ids_out, float* logprobs_out);
 
+/* ---- Medusa draft heads on the device (methods/medusa.rs) -------------------
+ * Each head (MedusaHeadModule, medusa.rs:509-584) maps the target's last
+ * hidden row through residual_layers blocks x' = x + SiLU(W x + b)
+ * (W [H][H], b [H]) and an output projection [V][H] without bias; weights are
+ * BF16 (row-major [out][in] bits), biases f32.  1 <= n_heads <= 8,
+ * 0 <= residual_layers <= 4.  res_w / res_b list [head][layer]. */
+typedef struct spec_medusa_weights {
+  int n_heads;
+  int residual_layers;
+  const uint16_t* const* res_w;  /* [n_heads * residual_layers] -> [H][H] */
+  const float* const* res_b;     /* [n_heads * residual_layers] -> [H] */
+  const uint16_t* const* out_w;  /* [n_heads] -> [V][H] */
+} spec_medusa_weights;
+int spec_medusa_attach(spec_model* m, const spec_medusa_weights* w);
+/* Seeded N(0, 0.02) BF16 weights and biases made on the device (benchmarks). */
+int spec_medusa_attach_synthetic(spec_model* m, int n_heads, int residual_layers, uint64_t seed);
+/* MedusaHeadsCandle::top_k_per_head (medusa.rs:713-734): every head applied to
+ * hidden [H], then top_k_indices (medusa.rs:477-487) over its logits on the
+ * device.  Writes ids_out[n_heads][k] (descending logit, ties by ascending
+ * index) and, when non-NULL, logprobs_out[n_heads][k] = logit - logsumexp.
+ * 1 <= k <= 64. */
+int spec_medusa_topk(spec_model* m, const float* hidden, int k, int32_t* ids_out, float* logprobs_out);
+/* Number of attached Medusa heads (0 when none). */
+int spec_medusa_num_heads(const spec_model* m);
+
 /* ---- device-side acceptance ------------------------------------------------
  * Greedy (temperature 0) vanilla verify: one batched forward of [last]+drafts
  * (same protocol and state change as spec_batched_logits), then the argmax of

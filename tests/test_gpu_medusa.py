@@ -1,0 +1,67 @@
+"""Medusa heads on the device (spec_medusa_topk) against the restated
+medusa.rs heads (oracle/medusa.py) on the same BF16 weights.
+
+Every head maps the target's hidden row through its residual blocks and its
+output projection; a device top-k and log-softmax follow.  The check: the
+device's k ids are a top-k of the oracle's logits row within the tolerance,
+and their log-probs match within it.  The tolerance is 2 % of the row's
+scale (BF16 operands into each linear, as in the reference's BF16 heads)."""
+
+import importlib
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+REL = 2e-2
+
+
+def _bf(rng, shape, s):
+    eo = importlib.import_module("oracle.eagle")
+    return eo.bf16_bits(rng.standard_normal(shape).astype(np.float32) * np.float32(s))
+
+
+@pytest.mark.parametrize("name,heads,layers", [("llama_q4km", 4, 1), ("qwen_q4km", 3, 2), ("llama_bf16", 2, 0)])
+def test_medusa_topk_matches_oracle(pkg, tiny_gguf, name, heads, layers):
+    mo = importlib.import_module("oracle.medusa")
+    dec = pkg.B200Decoder.from_gguf(tiny_gguf(name), max_ctx=128)
+    H, V = dec.hidden_size(), dec.vocab_size()
+    rng = np.random.default_rng(11)
+    res_w = [[_bf(rng, (H, H), 0.05) for _ in range(layers)] for _ in range(heads)]
+    res_b = [[(0.1 * rng.standard_normal(H)).astype(np.float32) for _ in range(layers)] for _ in range(heads)]
+    out_w = [_bf(rng, (V, H), 0.05) for _ in range(heads)]
+    dec.medusa_attach(res_w, res_b, out_w)
+    assert dec.medusa_num_heads() == heads
+    hidden = rng.standard_normal(H).astype(np.float32)
+    k = 10
+    ids, lp = dec.medusa_topk(hidden, k)
+    assert ids.shape == (heads, k) and lp.shape == (heads, k)
+    _, rows = mo.MedusaOracle(res_w, res_b, out_w).top_k_per_head(hidden, k)
+    for h in range(heads):
+        row = rows[h]
+        tol = REL * max(1.0, float(np.max(np.abs(row))))
+        mx = np.max(row)
+        lse = np.log(np.sum(np.exp(row - mx))) + mx
+        kth = np.sort(row)[::-1][k - 1]
+        assert np.all(row[ids[h]] >= kth - 2 * tol), h
+        err = float(np.abs(lp[h] - (row[ids[h]] - lse)).max())
+        assert err <= tol, (h, err, tol)
+        assert np.all(np.diff(lp[h]) <= 0)
+    # the same call again gives the same bits
+    ids2, lp2 = dec.medusa_topk(hidden, k)
+    assert np.array_equal(ids, ids2) and np.array_equal(lp, lp2)
+
+
+def test_medusa_errors_and_synthetic(pkg, tiny_gguf):
+    dec = pkg.B200Decoder.from_gguf(tiny_gguf("llama_q4km"), max_ctx=128)
+    h = np.zeros(dec.hidden_size(), np.float32)
+    with pytest.raises(pkg.SamplingError):
+        dec.medusa_topk(h, 4)  # nothing attached
+    with pytest.raises(pkg.SamplingError):
+        dec.medusa_attach_synthetic(9, 1, 0)  # more than 8 heads
+    dec.medusa_attach_synthetic(4, 1, 5)
+    ids, lp = dec.medusa_topk(h + 0.5, 8)
+    assert ids.shape == (4, 8) and np.isfinite(lp).all() and (ids >= 0).all() and (ids < dec.vocab_size()).all()
+    with pytest.raises(pkg.SamplingError):
+        dec.medusa_topk(h, 65)
