@@ -245,6 +245,14 @@ struct spec_model {
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     return e;
   }
+  // Host -> device copy that has landed when it returns.  A plain cudaMemcpy
+  // from pageable memory may return before its DMA completes, and kernels on
+  // this non-blocking stream are not ordered after the legacy stream.
+  cudaError_t upload(void* dst, const void* src, size_t bytes) {
+    cudaError_t e = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    return e;
+  }
   template <class T>
   cudaError_t halloc(T** p, size_t bytes) {
     void* q = nullptr;
@@ -517,8 +525,8 @@ int build_rope(spec_model* m) {
     }
   cudaError_t e = m->dalloc(&m->rope_cos, n * 4);
   if (e == cudaSuccess) e = m->dalloc(&m->rope_sin, n * 4);
-  if (e == cudaSuccess) e = cudaMemcpy(m->rope_cos, cs.data(), n * 4, cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMemcpy(m->rope_sin, sn.data(), n * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = m->upload(m->rope_cos, cs.data(), n * 4);
+  if (e == cudaSuccess) e = m->upload(m->rope_sin, sn.data(), n * 4);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "rope tables"));
   return SPEC_OK;
 }
@@ -791,13 +799,13 @@ int get_schedule(spec_model* m, int M, int flags, spec_model::Schedule** out) {
   cudaError_t e = m->dalloc(&sc.ops, sizeof(FwdOp) * ops.size());
   if (e == cudaSuccess) e = m->dalloc(&sc.done, sizeof(int) * ops.size());
   if (e == cudaSuccess) e = m->dalloc(&sc.gflags, sizeof(int) * ops.size() * m->counter_set);
-  if (e == cudaSuccess) e = cudaMemcpy(sc.ops, ops.data(), sizeof(FwdOp) * ops.size(), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = m->upload(sc.ops, ops.data(), sizeof(FwdOp) * ops.size());
   if (e == cudaSuccess) {
     std::vector<FwdOp> solo = ops;
     for (auto& o : solo) o.dep = -1;
     e = m->dalloc(&sc.solo, sizeof(FwdOp) * solo.size());
     if (e == cudaSuccess)
-      e = cudaMemcpy(sc.solo, solo.data(), sizeof(FwdOp) * solo.size(), cudaMemcpyHostToDevice);
+      e = m->upload(sc.solo, solo.data(), sizeof(FwdOp) * solo.size());
   }
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "schedule upload"));
   auto res = m->schedules.emplace(key, std::move(sc));
@@ -1155,7 +1163,7 @@ int init_device(spec_model* m, const spec_load_opts* opts) {
 
 int upload_vec(spec_model* m, float** dst, const float* src, int n) {
   cudaError_t e = m->dalloc(dst, (size_t)n * 4);
-  if (e == cudaSuccess) e = cudaMemcpy(*dst, src, (size_t)n * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = m->upload(*dst, src, (size_t)n * 4);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "upload vector"));
   return SPEC_OK;
 }
@@ -1415,7 +1423,7 @@ int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) 
     return m->fail(SPEC_ERR_UNSUPPORTED, "unsupported token_embd format");
   {
     cudaError_t e = m->dalloc(&m->embed_raw, te->nbytes);
-    if (e == cudaSuccess) e = cudaMemcpy(m->embed_raw, f.data(*te), te->nbytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = m->upload(m->embed_raw, f.data(*te), te->nbytes);
     if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, "embedding upload"));
   }
   Part outp;
@@ -1656,7 +1664,7 @@ int spec_tp_connect(spec_model* m, const void* handles, int n) {
   std::vector<void*> ptrs((size_t)2 * n);
   for (int set = 0; set < 2; ++set)
     for (int r = 0; r < n; ++r) ptrs[(size_t)set * n + r] = base[r] + set * m->tp_set_bytes;
-  const cudaError_t e = cudaMemcpy(m->tp_ptrs_dev, ptrs.data(), ptrs.size() * sizeof(void*), cudaMemcpyHostToDevice);
+  const cudaError_t e = m->upload(m->tp_ptrs_dev, ptrs.data(), ptrs.size() * sizeof(void*));
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "peer pointer table"));
   m->tp_connected = true;
   return SPEC_OK;
@@ -2063,8 +2071,8 @@ static int eagle_rope(spec_model* m, EagleHead& e, float theta) {
   }
   cudaError_t er = m->dalloc(&e.rope_cos, cs.size() * 4);
   if (er == cudaSuccess) er = m->dalloc(&e.rope_sin, sn.size() * 4);
-  if (er == cudaSuccess) er = cudaMemcpy(e.rope_cos, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice);
-  if (er == cudaSuccess) er = cudaMemcpy(e.rope_sin, sn.data(), sn.size() * 4, cudaMemcpyHostToDevice);
+  if (er == cudaSuccess) er = m->upload(e.rope_cos, cs.data(), cs.size() * 4);
+  if (er == cudaSuccess) er = m->upload(e.rope_sin, sn.data(), sn.size() * 4);
   if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "eagle rope tables"));
   return SPEC_OK;
 }
@@ -2129,7 +2137,7 @@ static int eagle_finish(spec_model* m, EagleHead& e) {
   if (er == cudaSuccess) er = m->halloc(&e.lse_host, (size_t)kEagleMaxSteps * 4);
   if (er != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(er, "eagle buffers"));
   const unsigned long long one = 1ull;
-  er = cudaMemcpy(e.anc, &one, 8, cudaMemcpyHostToDevice);
+  er = m->upload(e.anc, &one, 8);
 
   auto base = [&](const Mat& mt) {
     QmvParams p = base_params(m, mt, 1);
@@ -2212,7 +2220,7 @@ static int eagle_finish(spec_model* m, EagleHead& e) {
     p.ld_out = V;
   }
   for (auto& op : ops) op.dep = -1;
-  if (er == cudaSuccess) er = cudaMemcpy(e.ops, ops, sizeof(ops), cudaMemcpyHostToDevice);
+  if (er == cudaSuccess) er = m->upload(e.ops, ops, sizeof(ops));
   if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "eagle descriptors"));
   e.set_bf = fwd_fmt_set_for(fmt_bit(WF_BF16));
   return SPEC_OK;
@@ -2266,7 +2274,7 @@ int spec_eagle_attach(spec_model* m, const spec_eagle_weights* w) {
                        host(w->down, c.hidden), w->rope_theta > 0.f ? w->rope_theta : c.rope_theta, e);
   if (rc != SPEC_OK) return rc;
   cudaError_t er = m->dalloc(&e->post_norm, (size_t)c.hidden * 4);
-  if (er == cudaSuccess) er = cudaMemcpy(e->post_norm, w->post_norm, (size_t)c.hidden * 4, cudaMemcpyHostToDevice);
+  if (er == cudaSuccess) er = m->upload(e->post_norm, w->post_norm, (size_t)c.hidden * 4);
   if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "eagle norm"));
   m->eagle = e;
   return SPEC_OK;
@@ -2507,7 +2515,7 @@ static int medusa_upload_ops(spec_model* m, MedusaHeads& h) {
     ops[i].q = p;
     ops[i].dep = -1;
   }
-  cudaError_t er = cudaMemcpy(h.ops, ops.data(), sizeof(FwdOp) * n_ops, cudaMemcpyHostToDevice);
+  cudaError_t er = m->upload(h.ops, ops.data(), sizeof(FwdOp) * n_ops);
   if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "Medusa descriptors"));
   return SPEC_OK;
 }
@@ -2540,7 +2548,7 @@ int spec_medusa_attach(spec_model* m, const spec_medusa_weights* w) {
   if (rc != SPEC_OK) return rc;
   for (int i = 0; i < n_res; ++i) {
     cudaError_t er = m->dalloc(&h->res_b[i], (size_t)c.hidden * 4);
-    if (er == cudaSuccess) er = cudaMemcpy(h->res_b[i], w->res_b[i], (size_t)c.hidden * 4, cudaMemcpyHostToDevice);
+    if (er == cudaSuccess) er = m->upload(h->res_b[i], w->res_b[i], (size_t)c.hidden * 4);
     if (er != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(er, "Medusa biases"));
   }
   if ((rc = medusa_upload_ops(m, *h)) != SPEC_OK) return rc;
@@ -2994,7 +3002,7 @@ static int qmatmul_enqueue(spec_qweight* w, int M, float* y_dev, cudaStream_t s)
     // New descriptor: the slot may still feed a launch in flight (on any
     // stream), so drain the device first.  Happens once per (M, output).
     e = cudaDeviceSynchronize();
-    if (e == cudaSuccess) e = cudaMemcpy(w->op_dev, &op, sizeof(FwdOp), cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = m->upload(w->op_dev, &op, sizeof(FwdOp));
     if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "qmatmul op upload"));
     w->op_M = M;
     w->op_out = y_dev;
