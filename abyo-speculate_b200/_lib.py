@@ -101,6 +101,12 @@ SIGNATURES = [
     ("spec_load_gguf", ctypes.c_int, [ctypes.c_char_p, ctypes.POINTER(LoadOpts), ctypes.POINTER(ctypes.c_void_p)]),
     ("spec_create_synthetic", ctypes.c_int,
      [ctypes.POINTER(ModelDesc), ctypes.c_uint64, ctypes.POINTER(LoadOpts), ctypes.POINTER(ctypes.c_void_p)]),
+    ("spec_synthetic_seed", ctypes.c_uint64, [ctypes.c_uint64, ctypes.c_uint64]),
+    ("spec_synthetic_tensor", ctypes.c_int,
+     [ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_float, ctypes.c_void_p,
+      ctypes.c_int64]),
+    ("spec_synthetic_vector", ctypes.c_int,
+     [ctypes.c_int, ctypes.c_int, ctypes.c_uint64, ctypes.c_float, ctypes.c_float, c_f32_p]),
     ("spec_free", None, [ctypes.c_void_p]),
     ("spec_last_error", ctypes.c_char_p, [ctypes.c_void_p]),
     ("spec_vocab_size", ctypes.c_int, [ctypes.c_void_p]),

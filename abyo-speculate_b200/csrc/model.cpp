@@ -213,7 +213,7 @@ struct spec_model {
   int* single_done = nullptr;
 
   ~spec_model() {
-    cudaSetDevice(device);
+    DeviceGuard dg_(device);
     if (stream) cudaStreamSynchronize(stream);
     for (auto& kv : graphs)
       if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
@@ -1517,7 +1517,7 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
   if (int rc0 = check_tp_shape(m, c.n_heads, c.n_kv, c.head_dim, c.ffn, c.n_layers)) return rc0;
   const int H = c.hidden, F = c.ffn, hd = c.head_dim;
   uint64_t tid = 0;
-  auto tseed = [&]() { return mix64(seed * 0x100000001B3ull + (++tid)); };
+  auto tseed = [&]() { return spec_synthetic_seed(seed, ++tid); };  // tensor numbering: spec_b200.h
   m->layers.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
     Layer& L = m->layers[l];
@@ -1596,6 +1596,7 @@ int spec_load_gguf(const char* path, const spec_load_opts* opts, spec_model** ou
   *out = nullptr;
   std::unique_ptr<spec_model> m(new (std::nothrow) spec_model());
   if (!m) return SPEC_ERR_OOM;
+  DeviceGuard dg_(opts ? opts->device : 0);
   int rc = init_device(m.get(), opts);
   if (rc == SPEC_OK) rc = load_from_gguf(m.get(), path, opts);
   if (rc != SPEC_OK) {
@@ -1615,6 +1616,7 @@ int spec_create_synthetic(const spec_model_desc* desc, uint64_t seed, const spec
   *out = nullptr;
   std::unique_ptr<spec_model> m(new (std::nothrow) spec_model());
   if (!m) return SPEC_ERR_OOM;
+  DeviceGuard dg_(opts ? opts->device : 0);
   int rc = init_device(m.get(), opts);
   if (rc == SPEC_OK) rc = create_synthetic(m.get(), desc, seed, opts);
   if (rc != SPEC_OK) {
@@ -1627,11 +1629,59 @@ int spec_create_synthetic(const spec_model_desc* desc, uint64_t seed, const spec
 
 void spec_free(spec_model* m) { delete m; }
 
+uint64_t spec_synthetic_seed(uint64_t model_seed, uint64_t index) {
+  return mix64(model_seed * 0x100000001B3ull + index);
+}
+
+int spec_synthetic_tensor(int device, int ggml_type, int rows, int k_cols, uint64_t seed, float sigma,
+                          void* host_out, int64_t out_bytes) {
+  const bool known = ggml_type == WF_Q4_K || ggml_type == WF_Q5_K || ggml_type == WF_Q6_K ||
+                     ggml_type == WF_Q8_0 || ggml_type == WF_BF16 || ggml_type == WF_F16 || ggml_type == WF_F32;
+  if (!host_out || rows <= 0 || k_cols <= 0 || !known || k_cols % fmt_block_elems(ggml_type)) {
+    g_load_error = "spec_synthetic_tensor: null output, bad shape or unsupported type";
+    return SPEC_ERR_INVALID;
+  }
+  const size_t bytes = (size_t)rows * (size_t)(k_cols / fmt_block_elems(ggml_type)) * fmt_block_bytes(ggml_type);
+  if (out_bytes < (int64_t)bytes) {
+    g_load_error = "spec_synthetic_tensor: output buffer too small";
+    return SPEC_ERR_INVALID;
+  }
+  DeviceGuard dg_(device);
+  void* buf = nullptr;
+  cudaError_t e = cudaMalloc(&buf, bytes);
+  if (e == cudaSuccess) e = launch_synth_quant(static_cast<uint8_t*>(buf), ggml_type, rows, k_cols, seed, sigma, 0, 0);
+  if (e == cudaSuccess) e = cudaMemcpy(host_out, buf, bytes, cudaMemcpyDeviceToHost);
+  if (buf) cudaFree(buf);
+  if (e != cudaSuccess) {
+    g_load_error = cuda_msg(e, "spec_synthetic_tensor");
+    return SPEC_ERR_CUDA;
+  }
+  return SPEC_OK;
+}
+
+int spec_synthetic_vector(int device, int n, uint64_t seed, float base, float sigma, float* host_out) {
+  if (!host_out || n <= 0) {
+    g_load_error = "spec_synthetic_vector: null output or n <= 0";
+    return SPEC_ERR_INVALID;
+  }
+  DeviceGuard dg_(device);
+  float* buf = nullptr;
+  cudaError_t e = cudaMalloc(&buf, (size_t)n * 4);
+  if (e == cudaSuccess) e = launch_synth_vec(buf, n, seed, base, sigma, 0);
+  if (e == cudaSuccess) e = cudaMemcpy(host_out, buf, (size_t)n * 4, cudaMemcpyDeviceToHost);
+  if (buf) cudaFree(buf);
+  if (e != cudaSuccess) {
+    g_load_error = cuda_msg(e, "spec_synthetic_vector");
+    return SPEC_ERR_CUDA;
+  }
+  return SPEC_OK;
+}
+
 int spec_tp_handle(spec_model* m, void* out, int cap) {
   if (!m || !out) return -SPEC_ERR_INVALID;
   if (m->tp_size <= 1 || !m->tp_buf) return -m->fail(SPEC_ERR_INVALID, "not a tensor-parallel handle");
   if (cap < (int)sizeof(cudaIpcMemHandle_t)) return -m->fail(SPEC_ERR_INVALID, "handle buffer too small");
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   // The zeroed counters must be in place before any peer can write to them.
   cudaError_t e = cudaStreamSynchronize(m->stream);
   if (e != cudaSuccess) return -m->fail(SPEC_ERR_CUDA, cuda_msg(e, "stream"));
@@ -1646,7 +1696,7 @@ int spec_tp_connect(spec_model* m, const void* handles, int n) {
   if (!m || !handles) return SPEC_ERR_INVALID;
   if (m->tp_size <= 1 || n != m->tp_size) return m->fail(SPEC_ERR_INVALID, "handle count differs from tp_size");
   if (m->tp_connected) return m->fail(SPEC_ERR_INVALID, "already connected");
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   std::vector<uint8_t*> base(n);
   for (int r = 0; r < n; ++r) {
     if (r == m->tp_rank) {
@@ -1710,7 +1760,7 @@ int spec_reset(spec_model* m) {
 int spec_observe(spec_model* m, const uint32_t* ids, int n) {
   if (!m || (n > 0 && !ids) || n < 0) return SPEC_ERR_INVALID;
   if (n == 0) return SPEC_OK;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   for (int i = 0; i < n; ++i)
     if (ids[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
   const int size = (int)m->history.size();
@@ -1731,7 +1781,7 @@ int spec_observe(spec_model* m, const uint32_t* ids, int n) {
 
 int spec_next_logits(spec_model* m, float* out) {
   if (!m || !out) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "next_logits called with empty history");
   if (m->last_valid) return copy_last_row(m, out);
   const uint32_t last = m->history.back();
@@ -1749,7 +1799,7 @@ int spec_next_logits(spec_model* m, float* out) {
 
 int spec_batched_logits(spec_model* m, const uint32_t* drafts, int k, float* out) {
   if (!m || !out || k < 0 || (k > 0 && !drafts)) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (k == 0) return spec_next_logits(m, out);
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "batched_logits with empty history");
   std::vector<uint32_t> combined(k + 1);
@@ -1789,7 +1839,7 @@ int spec_rollback_to(spec_model* m, int len) {
 
 int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out) {
   if (!m || !tokens || !parents || !out) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
   int rc = check_tree(m, tokens, parents, n);
   if (rc != SPEC_OK) return rc;
@@ -1822,7 +1872,7 @@ int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* paren
 int spec_tree_logits_keep_kv(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
                              float* logits_out, float* hidden_out) {
   if (!m || !tokens || !parents) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   m->last_valid = false;
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
   int rc = check_tree(m, tokens, parents, n);
@@ -1852,7 +1902,7 @@ int spec_tree_logits_keep_kv(spec_model* m, const uint32_t* tokens, const int32_
 int spec_commit_tree_path(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
                           const int32_t* accepted, int n_acc) {
   if (!m || !tokens || !parents || !accepted) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   m->last_valid = false;
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "commit_tree_path with empty history");
   int rc = check_tree(m, tokens, parents, n);
@@ -1890,7 +1940,7 @@ int spec_commit_tree_path(spec_model* m, const uint32_t* tokens, const int32_t* 
 
 int spec_last_hidden_state(spec_model* m, float* out) {
   if (!m || !out) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "last_hidden_state with empty history");
   const uint32_t last = m->history.back();
   const int target = (int)m->history.size() - 1;
@@ -1912,7 +1962,7 @@ int spec_last_hidden_state(spec_model* m, float* out) {
 
 int spec_observe_returning_last_hidden(spec_model* m, const uint32_t* ids, int n, float* hidden_out) {
   if (!m || !ids || !hidden_out) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (n <= 0) return m->fail(SPEC_ERR_INVALID, "observe_returning_last_hidden with empty ids");
   for (int i = 0; i < n; ++i)
     if (ids[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
@@ -1951,7 +2001,7 @@ int spec_observe_returning_last_hidden(spec_model* m, const uint32_t* ids, int n
 
 int spec_apply_lm_head(spec_model* m, const float* hidden, int rows, float* out) {
   if (!m || !hidden || !out || rows < 0) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   const int H = m->cfg.hidden, V = m->cfg.vocab;
   for (int r0 = 0; r0 < rows; r0 += kMaxRows) {
     const int M = std::min(kMaxRows, rows - r0);
@@ -1979,7 +2029,7 @@ int spec_apply_lm_head(spec_model* m, const float* hidden, int rows, float* out)
 int spec_apply_lm_head_topk(spec_model* m, const float* hidden, int rows, int k, int32_t* ids_out, float* vals_out) {
   if (!m || !hidden || !ids_out || rows < 0) return SPEC_ERR_INVALID;
   if (k < 1 || k > kMaxTopK || k > m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "top-k size out of range");
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   const int H = m->cfg.hidden, V = m->cfg.vocab;
   cudaError_t e = cudaSuccess;
   if (!m->topk_part) {
@@ -2256,7 +2306,7 @@ static int eagle_check_target(spec_model* m) {
 int spec_eagle_attach(spec_model* m, const spec_eagle_weights* w) {
   if (!m || !w || !w->fc || !w->q || !w->k || !w->v || !w->o || !w->gate || !w->up || !w->down || !w->post_norm)
     return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (int rc = eagle_check_target(m)) return rc;
   const ModelCfg& c = m->cfg;
   const int hd = c.head_dim;
@@ -2282,7 +2332,7 @@ int spec_eagle_attach(spec_model* m, const spec_eagle_weights* w) {
 
 int spec_eagle_attach_synthetic(spec_model* m, uint64_t seed) {
   if (!m) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (int rc = eagle_check_target(m)) return rc;
   const ModelCfg& c = m->cfg;
   const int H = c.hidden, hd = c.head_dim, F = c.ffn;
@@ -2311,7 +2361,7 @@ int spec_eagle_attach_synthetic(spec_model* m, uint64_t seed) {
 int spec_eagle_draft(spec_model* m, const float* hidden, uint32_t root, int position, int depth, int k,
                      int32_t* ids_out, float* logprobs_out) {
   if (!m || !hidden || !ids_out || depth < 1) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   EagleHead* e = m->eagle.get();
   if (!e) return m->fail(SPEC_ERR_INVALID, "no EAGLE draft attached (spec_eagle_attach)");
   const ModelCfg& c = m->cfg;
@@ -2524,7 +2574,7 @@ static int medusa_upload_ops(spec_model* m, MedusaHeads& h) {
 
 int spec_medusa_attach(spec_model* m, const spec_medusa_weights* w) {
   if (!m || !w || (w->residual_layers > 0 && (!w->res_w || !w->res_b)) || !w->out_w) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (int rc = medusa_check(m, w->n_heads, w->residual_layers)) return rc;
   const ModelCfg& c = m->cfg;
   const int n_res = w->n_heads * w->residual_layers;
@@ -2558,7 +2608,7 @@ int spec_medusa_attach(spec_model* m, const spec_medusa_weights* w) {
 
 int spec_medusa_attach_synthetic(spec_model* m, int n_heads, int residual_layers, uint64_t seed) {
   if (!m) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (int rc = medusa_check(m, n_heads, residual_layers)) return rc;
   const ModelCfg& c = m->cfg;
   std::vector<void*> temps;
@@ -2584,7 +2634,7 @@ int spec_medusa_attach_synthetic(spec_model* m, int n_heads, int residual_layers
 
 int spec_medusa_topk(spec_model* m, const float* hidden, int k, int32_t* ids_out, float* logprobs_out) {
   if (!m || !hidden || !ids_out) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   MedusaHeads* h = m->medusa.get();
   if (!h) return m->fail(SPEC_ERR_INVALID, "no Medusa heads attached (spec_medusa_attach)");
   const ModelCfg& c = m->cfg;
@@ -2636,7 +2686,7 @@ int spec_medusa_num_heads(const spec_model* m) { return (m && m->medusa) ? m->me
 
 int spec_embed_tokens(spec_model* m, const uint32_t* ids, int n, float* out) {
   if (!m || !ids || !out || n < 0) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   const int H = m->cfg.hidden;
   for (int i = 0; i < n; ++i)
     if (ids[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
@@ -2671,7 +2721,7 @@ int spec_embed_tokens(spec_model* m, const uint32_t* ids, int n, float* out) {
 int spec_last_hidden_states_multi(spec_model* m, const int32_t* layers, int n_sel, float* final_out,
                                   float* layer_outs) {
   if (!m || !final_out || n_sel < 0 || (n_sel > 0 && (!layers || !layer_outs))) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "last_hidden_states_multi with empty history");
   for (int i = 0; i < n_sel; ++i)
     if (layers[i] < 0 || layers[i] >= m->cfg.n_layers)
@@ -2708,7 +2758,7 @@ int spec_last_hidden_states_multi(spec_model* m, const int32_t* layers, int n_se
 int spec_verify_greedy(spec_model* m, const uint32_t* drafts, int k, int* n_accepted, uint32_t* next_token,
                        int32_t* argmax_out) {
   if (!m || !n_accepted || !next_token || k < 0 || (k > 0 && !drafts)) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "batched_logits with empty history");
   if (k + 1 > kMaxRows) return m->fail(SPEC_ERR_UNSUPPORTED, "k+1 exceeds SPEC_MAX_ROWS");
   for (int i = 0; i < k; ++i)
@@ -2788,7 +2838,7 @@ int spec_verify_rejection(spec_model* m, const uint32_t* drafts, int k, const fl
   if (!m || !commits || !n_commits || k < 0 || (k > 0 && (!drafts || !draft_probs)) || n_uniforms < 0 ||
       (n_uniforms > 0 && !uniforms))
     return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (!std::isfinite(temperature) || temperature < 0.f) return m->fail(SPEC_ERR_INVALID, "invalid temperature");
   if (budget < 1) return m->fail(SPEC_ERR_INVALID, "token budget must be >= 1");
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "batched_logits with empty history");
@@ -2853,7 +2903,7 @@ int spec_verify_rejection(spec_model* m, const uint32_t* drafts, int k, const fl
 int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
                             int32_t* best_path, int* path_len, uint32_t* bonus) {
   if (!m || !tokens || !parents || !best_path || !path_len || !bonus) return SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   m->last_valid = false;
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
   int rc = check_tree(m, tokens, parents, n);
@@ -2933,6 +2983,7 @@ int spec_qweight_upload(int ggml_type, const void* gguf_blocks, int n_rows, int 
   spec_model* m = w->ctx.get();
   spec_load_opts o = {};
   o.device = device;
+  DeviceGuard dg_(device);
   int rc = init_device(m, &o);
   if (rc != SPEC_OK) {
     g_load_error = m->err;
@@ -2971,7 +3022,7 @@ int spec_qweight_upload(int ggml_type, const void* gguf_blocks, int n_rows, int 
 void spec_qweight_free(spec_qweight* w) {
   if (!w) return;
   if (w->flush) {
-    cudaSetDevice(w->ctx->device);
+    DeviceGuard dg_(w->ctx->device);
     cudaFree(w->flush);
   }
   delete w;
@@ -3036,20 +3087,42 @@ bool qweight_launch_desc(spec_qweight* w, int M, float* y_dev, QmatmulLaunch* ou
   out->p = p;
   out->fmt_set = m->fmt_set ? m->fmt_set : fwd_fmt_set_for(m->fmt_bits);
   out->device = m->device;
+  out->l2_ahead = m->l2_ahead;
   out->stream = m->stream;
   return true;
 }
 
 void set_thread_error(const char* msg) { g_load_error = msg; }
 
+int take_device_error(unsigned* err_dev, cudaStream_t s, char* msg, size_t cap) {
+  unsigned h[4] = {0u, 0u, 0u, 0u};
+  cudaError_t e = cudaMemcpyAsync(h, err_dev, sizeof h, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) {
+    snprintf(msg, cap, "reading the device error word: %s", cudaGetErrorString(e));
+    return SPEC_ERR_CUDA;
+  }
+  if (!h[0]) return SPEC_OK;
+  e = cudaMemsetAsync(err_dev, 0, sizeof h, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (h[0] & DEV_ERR_MBAR_TIMEOUT) {
+    snprintf(msg, cap,
+             "a device wait gave up (mbarrier timeout): site %u op %u cta %u, stage/pos %u (0x%x), counter %d; "
+             "the output is incomplete",
+             h[1] & 0xffu, (h[1] >> 8) & 0xffu, h[1] >> 16, h[2], h[2], (int)h[3]);
+    return SPEC_ERR_TIMEOUT;
+  }
+  snprintf(msg, cap, "a kernel rejected an argument (device error bits 0x%x)", h[0]);
+  return SPEC_ERR_INVALID;
+}
+
 }  // namespace specb200
 
 extern "C" {
 
-int spec_qmatmul(spec_qweight* w, const float* x_dev, int M, float* y_dev, void* stream) {
-  if (!w || !x_dev || !y_dev || M < 1 || M > kMaxRows) return SPEC_ERR_INVALID;
+static int qmatmul_call(spec_qweight* w, const float* x_dev, int M, float* y_dev, void* stream) {
   spec_model* m = w->ctx.get();
-  cudaSetDevice(m->device);
+  DeviceGuard dg(m->device);
   cudaStream_t s = stream ? static_cast<cudaStream_t>(stream) : m->stream;
   const int nt = nt_for_rows(M);
   cudaError_t e = launch_make_operand(x_dev, M, w->mat.K, nt, w->frag, w->x16, w->x32,
@@ -3059,16 +3132,30 @@ int spec_qmatmul(spec_qweight* w, const float* x_dev, int M, float* y_dev, void*
   int rc = qmatmul_enqueue(w, M, y_dev, s);
   if (rc != SPEC_OK) return rc;
   if (!stream) {
-    e = cudaStreamSynchronize(s);
-    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "qmatmul"));
+    // Synchronous call: a bounded wait that gave up inside the kernel left
+    // y incomplete; report it (and clear the word) instead of SPEC_OK.
+    char msg[256];
+    rc = take_device_error(m->err_dev, s, msg, sizeof msg);
+    if (rc != SPEC_OK) return m->fail(rc, msg);
   }
   return SPEC_OK;
+}
+
+int spec_qmatmul(spec_qweight* w, const float* x_dev, int M, float* y_dev, void* stream) {
+  if (!w || !x_dev || !y_dev || M < 1 || M > kMaxRows) {
+    g_load_error = "spec_qmatmul: null argument or M outside [1, 64]";
+    return SPEC_ERR_INVALID;
+  }
+  const int rc = qmatmul_call(w, x_dev, M, y_dev, stream);
+  // Weight calls report through spec_last_error(NULL) (this thread).
+  if (rc != SPEC_OK) g_load_error = "spec_qmatmul: " + w->ctx->err;
+  return rc;
 }
 
 int spec_qmatmul_time(spec_qweight* w, int M, int iters, int flush_l2, float* avg_ms) {
   if (!w || !avg_ms || iters < 1 || M != w->last_M) return SPEC_ERR_INVALID;
   spec_model* m = w->ctx.get();
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   cudaError_t e = cudaSuccess;
   if (flush_l2 && !w->flush) {
     w->flush_bytes = (size_t)512 << 20;
@@ -3107,7 +3194,7 @@ void* spec_cuda_stream(const spec_model* m) { return m ? static_cast<void*>(m->s
 int spec_profile_forward(spec_model* m, const uint32_t* drafts, int k, float* ms_out, int* kind_out,
                          int64_t* bytes_out, int cap) {
   if (!m || k < 0 || (k > 0 && !drafts) || !ms_out || !kind_out || !bytes_out) return -SPEC_ERR_INVALID;
-  cudaSetDevice(m->device);
+  DeviceGuard dg_(m->device);
   if (m->history.empty()) return -m->fail(SPEC_ERR_INVALID, "profile with empty history");
   const int target = (int)m->history.size() - 1;
   if (target > m->cache_len || target + k + 1 > m->t_max) return -m->fail(SPEC_ERR_INVALID, "bad cache state");

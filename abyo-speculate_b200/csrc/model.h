@@ -73,8 +73,32 @@ struct QmatmulLaunch {
   QmvParams p;           // weight segments, rows, splits, M, output; scratch pointers null
   int fmt_set = 0;       // forward-kernel format set of the weight
   int device = 0;
+  int l2_ahead = 0;      // L2 run-ahead stages of the weight's context (SPEC_B200_L2_AHEAD)
   cudaStream_t stream = nullptr;  // the weight's own stream
 };
+
+// Makes `device` current for the lifetime of the guard and restores the
+// caller's current device afterwards.
+struct DeviceGuard {
+  int prev = -1;
+  explicit DeviceGuard(int device) {
+    if (cudaGetDevice(&prev) != cudaSuccess) prev = -1;
+    if (prev != device) cudaSetDevice(device);
+  }
+  ~DeviceGuard() {
+    int cur = -1;
+    if (prev >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != prev) cudaSetDevice(prev);
+  }
+  DeviceGuard(const DeviceGuard&) = delete;
+  DeviceGuard& operator=(const DeviceGuard&) = delete;
+};
+
+// Reads the 16-byte device error word `err_dev` after the work on `s` (the
+// stream is synchronised here), clears it on the device, and turns a
+// recorded wait timeout into SPEC_ERR_TIMEOUT (an index a kernel rejected
+// into SPEC_ERR_INVALID) with the record written into msg[cap].  Allocates
+// nothing.
+int take_device_error(unsigned* err_dev, cudaStream_t s, char* msg, size_t cap);
 
 }  // namespace specb200
 

@@ -95,9 +95,14 @@ extern "C" int spec_qmatmul_noalloc(spec_qweight* w, const float* x_dev, int M, 
   }
   QmatmulLaunch q;
   if (!qweight_launch_desc(w, M, y_dev, &q)) return SPEC_ERR_INVALID;
-  if (cudaSetDevice(q.device) != cudaSuccess) {
-    set_thread_error("spec_qmatmul_noalloc: cudaSetDevice failed");
-    return SPEC_ERR_CUDA;
+  // The weight's device is current for the call; the caller's comes back on return.
+  DeviceGuard dg(q.device);
+  {
+    int cur = -1;
+    if (cudaGetDevice(&cur) != cudaSuccess || cur != q.device) {
+      set_thread_error("spec_qmatmul_noalloc: cudaSetDevice failed");
+      return SPEC_ERR_CUDA;
+    }
   }
   const int nt = nt_for_rows(M);
   const int groups = q.p.seg[0].groups + q.p.seg[1].groups;
@@ -123,6 +128,9 @@ extern "C" int spec_qmatmul_noalloc(spec_qweight* w, const float* x_dev, int M, 
   op.dep = -1;
 
   cudaError_t e = cudaMemsetAsync(base + L.zero_begin, 0, L.zero_end - L.zero_begin, s);
+  // The weight's 16-byte error word starts clear, so a synchronous call
+  // reports only its own launch.
+  if (e == cudaSuccess) e = cudaMemsetAsync(q.p.err, 0, 16, s);
   if (e == cudaSuccess)
     e = launch_make_operand(x_dev, M, q.p.K, nt, reinterpret_cast<uint32_t*>(base + L.frag),
                             reinterpret_cast<float*>(base + L.x16), reinterpret_cast<float*>(base + L.x32),
@@ -137,12 +145,22 @@ extern "C" int spec_qmatmul_noalloc(spec_qweight* w, const float* x_dev, int M, 
     fp.n_ops = 1;
     fp.done = reinterpret_cast<int*>(base + L.done);
     fp.err = q.p.err;
+    fp.l2_ahead = q.l2_ahead;
     e = launch_fwd(fp, q.fmt_set, M, s, false);
   }
-  if (e == cudaSuccess && !stream) e = cudaStreamSynchronize(s);
   if (e != cudaSuccess) {
-    set_thread_error("spec_qmatmul_noalloc: CUDA launch or synchronize failed");
+    set_thread_error("spec_qmatmul_noalloc: CUDA launch failed");
     return SPEC_ERR_CUDA;
+  }
+  if (!stream) {
+    // Synchronous call: a bounded wait inside the kernel that gave up left y
+    // incomplete; that is reported here (and the word cleared).
+    char msg[256];
+    const int rc2 = take_device_error(q.p.err, s, msg, sizeof msg);
+    if (rc2 != SPEC_OK) {
+      set_thread_error(msg);
+      return rc2;
+    }
   }
   return SPEC_OK;
 }

@@ -135,6 +135,10 @@ class B200Decoder:
         """The reference decoder's `cache_len`."""
         return self._lib.spec_kv_len(self._h)
 
+    def max_ctx(self) -> int:
+        """KV capacity in tokens (the load's max_ctx)."""
+        return self._lib.spec_max_ctx(self._h)
+
     def eos_token_ids(self) -> List[int]:
         return list(self._eos)
 

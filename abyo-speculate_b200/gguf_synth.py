@@ -290,9 +290,80 @@ def write_gguf(path: str, spec: ModelSpec, seed: int, rope_style: Optional[str] 
     llama_local.rs); ``llama3_scaling`` records Llama-3.1 frequency scaling
     (factor 8, low 1, high 4, original context 8192; llama_local.rs:47-75).
     """
+    tensors = synth_tensors(spec, seed, sigma)
+    write_gguf_tensors(path, spec, tensors, seed, rope_style, llama3_scaling)
+    return tensors
+
+
+def device_synthetic_tensors(spec: ModelSpec, seed: int, device: int = 0) -> Dict[str, Tuple[np.ndarray, int]]:
+    """The tensors of ``B200Decoder.synthetic(..., seed=seed)`` (spec_create_synthetic),
+    rebuilt one by one with the same device generator, numbering and seeds
+    (spec_synthetic_seed / spec_synthetic_tensor / spec_synthetic_vector), as
+    name -> (raw GGUF data, ggml type).  Writing them with write_gguf_tensors
+    gives a GGUF file holding exactly the weights the device model runs on."""
+    import ctypes
+    from . import _lib
+    lib = _lib.load()
+    out: Dict[str, Tuple[np.ndarray, int]] = {}
+    counter = [0]
+
+    def next_seed() -> int:
+        counter[0] += 1
+        return int(lib.spec_synthetic_seed(seed, counter[0]))
+
+    def mat(name: str, rows: int, k: int, layer: Optional[int]) -> None:
+        qt = tensor_qtype(spec, name, k, layer)
+        nbytes = rows * (k // BLOCK_ELEMS[qt]) * BLOCK_BYTES[qt] if qt in BLOCK_ELEMS else rows * k * 2
+        buf = np.empty(nbytes, dtype=np.uint8)
+        _lib.check(lib.spec_synthetic_tensor(device, qt, rows, k, next_seed(), 0.02, buf.ctypes.data, nbytes))
+        if qt == BF16:
+            out[name] = (buf.view(np.uint16).reshape(rows, k), qt)
+        else:
+            out[name] = (buf.reshape(rows, -1), qt)
+
+    def vec(name: str, n: int, base: float) -> np.ndarray:
+        v = np.empty(n, dtype=np.float32)
+        _lib.check(lib.spec_synthetic_vector(device, n, next_seed(), base, 0.02,
+                                             v.ctypes.data_as(ctypes.POINTER(ctypes.c_float))))
+        if name:
+            out[name] = (v, F32)
+        return v
+
+    hd = spec.head_dim
+    for i in range(spec.n_layers):
+        for suffix, (rows, k) in layer_tensor_shapes(spec):
+            mat(f"blk.{i}.{suffix}", rows, k, i)
+        vec(f"blk.{i}.attn_norm.weight", spec.hidden, 1.0)
+        vec(f"blk.{i}.ffn_norm.weight", spec.hidden, 1.0)
+        if spec.arch == "qwen2":
+            b = vec("", (spec.n_heads + 2 * spec.n_kv_heads) * hd, 0.0)
+            nq, nk = spec.n_heads * hd, spec.n_kv_heads * hd
+            out[f"blk.{i}.attn_q.bias"] = (b[:nq].copy(), F32)
+            out[f"blk.{i}.attn_k.bias"] = (b[nq:nq + nk].copy(), F32)
+            out[f"blk.{i}.attn_v.bias"] = (b[nq + nk:].copy(), F32)
+    vec("output_norm.weight", spec.hidden, 1.0)
+    mat("token_embd.weight", spec.vocab, spec.hidden, None)
+    mat("output.weight", spec.vocab, spec.hidden, None)
+    return out
+
+
+def write_device_synthetic_gguf(path: str, spec: ModelSpec, seed: int, device: int = 0,
+                                rope_half: bool = False) -> Dict[str, Tuple[np.ndarray, int]]:
+    """GGUF file of the device-synthesized model ``B200Decoder.synthetic(spec, seed)``
+    (same RoPE style and, for BF16 Llama, the Llama-3.1 scaling that
+    spec_create_synthetic applies)."""
+    tensors = device_synthetic_tensors(spec, seed, device)
+    bf16_llama = spec.quant_mix == "BF16" and spec.arch == "llama"
+    rope_style = "half" if (spec.arch == "llama" and rope_half) else None
+    write_gguf_tensors(path, spec, tensors, seed, rope_style, bf16_llama)
+    return tensors
+
+
+def write_gguf_tensors(path: str, spec: ModelSpec, tensors: Dict[str, Tuple[np.ndarray, int]], seed: int,
+                       rope_style: Optional[str] = None, llama3_scaling: bool = False) -> None:
+    """Write ``tensors`` (name -> (raw data, ggml type)) with the model metadata of ``spec``."""
     import gguf
 
-    tensors = synth_tensors(spec, seed, sigma)
     arch = spec.arch
     w = gguf.GGUFWriter(path, arch)
     w.add_uint32(f"{arch}.attention.head_count", spec.n_heads)
@@ -327,7 +398,6 @@ def write_gguf(path: str, spec: ModelSpec, seed: int, rope_style: Optional[str] 
     w.write_kv_data_to_file()
     w.write_tensors_to_file()
     w.close()
-    return tensors
 
 
 def spec_to_json(spec: ModelSpec) -> str:

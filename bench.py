@@ -10,19 +10,20 @@ the library's stream over K back-to-back device-side greedy verifies
 whole forward, device argmax, k+1 ints back).  `e2e` = the same metric through
 spec_batched_logits with host draft tokens in and the 5 x 128256 f32 logits
 rows copied back to host every step (the reference-facing Decoder call).
-Multi-GPU: one process per GPU, time = max over ranks.  By default each rank
-is an independent replica of the verify step (no collective; value = all
-ranks' steps / that time).  `--tp T` shards each model over T GPUs instead
-(tensor parallelism: each rank holds its heads and FFN slice, the o and down
-outputs are summed across the T ranks inside the GEMV epilogue over NVLink);
-the N GPUs then run N/T such models and value = their steps / the time.
+Multi-GPU: one process per GPU, time = max over ranks.  By default the N
+GPUs hold ONE model, tensor parallel (each rank holds its heads and FFN slice;
+the o and down outputs are summed across the ranks inside the GEMV epilogue
+over NVLink), and value = that model's verify steps/s (strong scaling).
+`--tp T` shards each model over T GPUs instead, so the N GPUs run N/T models
+(`--tp 1`: N independent replicas) and value = their steps / the time.
 
 `--impl reference` times the reference's CPU path for the same workload.  The
 reference is Rust over candle and cannot be built here (no cargo/rustc, candle
-not vendored), so this arm runs the CPU restatement in oracle/ (a multi-threaded
-C dequant-matmul over the same GGUF block formats, numpy attention) on a
-bounded per-step sample (one transformer layer at M=5) extrapolated to the
-full 32-layer verify plus LM head.
+not vendored), so this arm runs the CPU restatement in oracle/ (the C
+dequant-matmul over the same GGUF block formats and the C causal attention,
+OpenMP over every host thread): each step is one whole 32-layer verify plus
+the LM head, nothing extrapolated; steps run until --steps or the
+--reference-budget seconds are used up, and the line reports the steps timed.
 """
 
 from __future__ import annotations
@@ -145,69 +146,120 @@ class ClockSampler:
 
 
 # ---------------------------------------------------------------------------
-# CPU path (oracle port): one layer at M = k+1 rows, extrapolated.
+# CPU path (oracle port): whole 32-layer verifies, nothing extrapolated.
 # ---------------------------------------------------------------------------
-class CpuVerifySample:
-    def __init__(self, seed: int = 0, lm_fraction: int = 16):
+class CpuVerify:
+    """The verify step of configs[1] on the host cores, restated by the oracle
+    (oracle/quants.c: the quantized matmul straight from GGUF blocks and the
+    causal attention, both OpenMP over all host threads; RMSNorm, RoPE and the
+    SiLU gate in numpy on 5 x 4096 rows).  One call of verify_seconds() runs a
+    whole verify: 32 layers of 7 dequant-matmuls at M = k+1 = 5 plus attention
+    over 2053 keys, and the full 128256-row Q6_K LM head.
+
+    Weights: two distinct layers (an even and an odd layer of the Q4_K_M mix:
+    Q6_K attn_v / ffn_down on the even one) that the 32 layers alternate
+    between; 248 MB of packed blocks, so no layer's weights are cache-resident
+    when it runs again.  The LM head is half the vocabulary's rows, run twice
+    (the full head's bytes and work).  Each layer has its own f32 KV cache of
+    2053 keys (the reference's quantized model keeps f32 K/V)."""
+
+    def __init__(self, seed: int = 0):
+        import concurrent.futures as cf
         synth = importlib.import_module("abyo-speculate_b200.gguf_synth")
         self.om = importlib.import_module("oracle.model")
-        rng = np.random.default_rng(seed)
-        H, F, hd = CFG["hidden"], CFG["ffn"], CFG["hidden"] // CFG["n_heads"]
-        nkv = CFG["n_kv_heads"]
-
-        def q(shape, qt):
-            w = rng.standard_normal(shape, dtype=np.float32) * np.float32(0.02)
-            return synth.quantize(w, qt).view(np.uint8).reshape(shape[0], -1), qt
-
-        # layer 0 of the Q4_K_M mix: v and down are Q6_K on even layers
-        self.mats = [(q((4096, H), 12), 4096, H), (q((1024, H), 12), 1024, H), (q((1024, H), 14), 1024, H),
-                     (q((H, 4096), 12), H, 4096), (q((F, H), 12), F, H), (q((F, H), 12), F, H),
-                     (q((H, F), 14), H, F)]
-        self.lm_rows = CFG["vocab"] // lm_fraction
-        self.lm = q((self.lm_rows, H), 14)
-        self.lm_fraction = lm_fraction
-        self.x = rng.standard_normal((K_DRAFT + 1, H), dtype=np.float32)
-        self.xf = rng.standard_normal((K_DRAFT + 1, F), dtype=np.float32)
-        self.kc = rng.standard_normal((nkv, KV_LEN + K_DRAFT + 1, hd)).astype(np.float32)
-        self.vc = rng.standard_normal((nkv, KV_LEN + K_DRAFT + 1, hd)).astype(np.float32)
         self.threads = os.cpu_count() or 1
+        spec = synth.ModelSpec("llama", CFG["n_layers"], CFG["hidden"], CFG["n_heads"], CFG["n_kv_heads"],
+                               CFG["ffn"], CFG["vocab"], CFG["rope_theta"], 8192, CFG["eps"], "Q4_K_M")
+        H, F, nq, nkv = CFG["hidden"], CFG["ffn"], CFG["n_heads"], CFG["n_kv_heads"]
+        self.hd = hd = H // nq
+        M, T = K_DRAFT + 1, KV_LEN + K_DRAFT + 1
+        pool = cf.ThreadPoolExecutor(self.threads)
 
-    def layer_seconds(self) -> float:
+        def quant(rows, k, qt, tag):
+            def block(r0):
+                g = np.random.default_rng([seed, tag, r0])
+                w = g.standard_normal((min(1024, rows - r0), k), dtype=np.float32) * np.float32(0.02)
+                return synth.quantize(w, qt).view(np.uint8).reshape(w.shape[0], -1)
+            return np.concatenate(list(pool.map(block, range(0, rows, 1024)))), qt, rows, k
+
+        rng = np.random.default_rng(seed)
+        self.layers = []
+        for li in (0, 1):
+            L = {}
+            for name, (rows, k) in synth.layer_tensor_shapes(spec):
+                L[name.split(".")[0]] = quant(rows, k, synth.tensor_qtype(spec, "blk.%d.%s" % (li, name), k, li),
+                                              li * 16 + len(L))
+            L["attn_norm"] = (1 + 0.02 * rng.standard_normal(H)).astype(np.float32)
+            L["ffn_norm"] = (1 + 0.02 * rng.standard_normal(H)).astype(np.float32)
+            self.layers.append(L)
+        self.lm_half = quant(CFG["vocab"] // 2, H, synth.Q6_K, 99)
+        pool.shutdown()
+        self.out_norm = (1 + 0.02 * rng.standard_normal(H)).astype(np.float32)
+        self.kc = rng.standard_normal((CFG["n_layers"], nkv, T, hd), dtype=np.float32)
+        self.vc = rng.standard_normal((CFG["n_layers"], nkv, T, hd), dtype=np.float32)
+        self.x0 = rng.standard_normal((M, H), dtype=np.float32)
+        inv = 1.0 / np.power(np.float32(CFG["rope_theta"]), np.arange(0, hd, 2, dtype=np.float32) / hd)
+        ang = np.arange(KV_LEN, T, dtype=np.float32)[:, None] * inv[None, :]
+        self.cos, self.sin = np.cos(ang).astype(np.float32), np.sin(ang).astype(np.float32)
+
+    def _mm(self, w, x):
+        raw, qt, n, k = w
+        return self.om.qmatmul(qt, raw, n, k, x, threads=self.threads, acc_double=False)
+
+    def _rms(self, x, w):
+        return (x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + np.float32(CFG["eps"])) * w).astype(np.float32)
+
+    def _rope(self, x):  # x [M, heads, hd], interleaved pairs (rope_i)
+        a, b = x[..., 0::2], x[..., 1::2]
+        c, s = self.cos[:, None, :], self.sin[:, None, :]
+        out = np.empty_like(x)
+        out[..., 0::2] = a * c - b * s
+        out[..., 1::2] = a * s + b * c
+        return out
+
+    def verify_seconds(self) -> float:
+        M, nq, nkv, hd = K_DRAFT + 1, CFG["n_heads"], CFG["n_kv_heads"], self.hd
         t0 = time.perf_counter()
-        for (raw, qt), n, k in self.mats:
-            x = self.xf if k == CFG["ffn"] else self.x
-            self.om.qmatmul(qt, raw, n, k, x, threads=self.threads, acc_double=False)
-        # attention for one layer: 32 heads x 5 rows over 2053 keys
-        qh = self.x[:, :4096].reshape(K_DRAFT + 1, 32, 128)
-        for h in range(32):
-            s = qh[:, h] @ self.kc[h // 4].T / np.float32(np.sqrt(128))
-            s = np.exp(s - s.max(axis=-1, keepdims=True))
-            _ = (s / s.sum(axis=-1, keepdims=True)) @ self.vc[h // 4]
+        x = self.x0.copy()
+        for li in range(CFG["n_layers"]):
+            L = self.layers[li % 2]
+            xn = self._rms(x, L["attn_norm"])
+            q = self._rope(self._mm(L["attn_q"], xn).reshape(M, nq, hd))
+            k = self._rope(self._mm(L["attn_k"], xn).reshape(M, nkv, hd))
+            v = self._mm(L["attn_v"], xn).reshape(M, nkv, hd)
+            self.kc[li][:, KV_LEN:] = k.transpose(1, 0, 2)
+            self.vc[li][:, KV_LEN:] = v.transpose(1, 0, 2)
+            att = self.om.attention(q.transpose(1, 0, 2), self.kc[li], self.vc[li], threads=self.threads)
+            x = x + self._mm(L["attn_output"], att)
+            xn = self._rms(x, L["ffn_norm"])
+            g, u = self._mm(L["ffn_gate"], xn), self._mm(L["ffn_up"], xn)
+            x = x + self._mm(L["ffn_down"], (g / (1 + np.exp(-g)) * u).astype(np.float32))
+        h = self._rms(x, self.out_norm)
+        logits = np.concatenate([self._mm(self.lm_half, h), self._mm(self.lm_half, h)], axis=1)
+        assert logits.shape == (M, CFG["vocab"])
         return time.perf_counter() - t0
 
-    def lm_seconds(self) -> float:
-        (raw, qt) = self.lm
-        t0 = time.perf_counter()
-        self.om.qmatmul(qt, raw, self.lm_rows, CFG["hidden"], self.x, threads=self.threads, acc_double=False)
-        return (time.perf_counter() - t0) * self.lm_fraction
 
-    def verify_seconds(self, layer_s: float, lm_s: float) -> float:
-        return CFG["n_layers"] * layer_s + lm_s
+def time_cpu_verifies(cpu: CpuVerify, warmup: int, steps: int, budget_s: float):
+    """Warm-up verifies, then up to `steps` timed verifies while the budget lasts."""
+    for _ in range(warmup):
+        cpu.verify_seconds()
+    times = []
+    t_end = time.perf_counter() + budget_s
+    while len(times) < steps and (not times or time.perf_counter() < t_end):
+        times.append(cpu.verify_seconds())
+    return times
 
 
 def cpu_baseline_block(budget_s: float = 20.0):
-    s = CpuVerifySample()
-    lm = s.lm_seconds()
-    layers = []
-    t_end = time.perf_counter() + budget_s
-    while time.perf_counter() < t_end or len(layers) < 2:
-        layers.append(s.layer_seconds())
-    med = statistics.median(layers)
-    v = s.verify_seconds(med, lm)
-    return {"value": round(1.0 / v, 4), "unit": UNIT, "cores": s.threads, "kind": "port",
-            "sample": f"{len(layers)} single-layer CPU forwards (7 dequant-matmuls at M=5 + attention over "
-                      f"{KV_LEN + 5} keys) and 1/{s.lm_fraction} of the Q6_K LM head, extrapolated to 32 layers + "
-                      f"full head: {v * 1e3:.1f} ms per verify"}
+    cpu = CpuVerify()
+    times = time_cpu_verifies(cpu, 1, 1000, budget_s)
+    med = statistics.median(times)
+    return {"value": round(1.0 / med, 4), "unit": UNIT, "cores": cpu.threads, "kind": "port",
+            "sample": f"{len(times)} whole CPU verifies after 1 warm-up (32 layers x 7 dequant-matmuls at M=5 "
+                      f"+ attention over {KV_LEN + K_DRAFT + 1} keys + the 128256-row LM head, nothing "
+                      f"extrapolated): median {med * 1e3:.1f} ms, min {min(times) * 1e3:.1f}, "
+                      f"max {max(times) * 1e3:.1f}"}
 
 
 # ---- the other BASELINE.json configs (opt-in: --config cfg1|cfg4|cfg5) ----------
@@ -336,7 +388,7 @@ def run_config(args, ws, rank, local, dist):
     elif args.config == "cfg5":
         T = 16384
         k = 8
-        tp = args.tp
+        tp = args.tp if args.tp else ws
         res = {}
         for mix in ("Q5_K", "Q8_0"):
             dec = pkg.B200Decoder.synthetic(**CFG5_TARGET, quant_mix=mix, seed=15, device=local, max_ctx=T + 64,
@@ -371,29 +423,24 @@ def run_config(args, ws, rank, local, dist):
 def run_reference(args, ws, rank):
     if rank != 0:
         return
-    s = CpuVerifySample()
-    lm = s.lm_seconds()
-    for _ in range(max(args.warmup, 0)):
-        s.layer_seconds()
-    times = []
-    t_start = time.perf_counter()
-    for _ in range(args.steps):
-        times.append(s.layer_seconds())
-        if time.perf_counter() - t_start > args.reference_budget:
-            break
-    layer = statistics.mean(times)
-    v = s.verify_seconds(layer, lm)
-    value = 1.0 / v
+    cpu = CpuVerify()
+    times = time_cpu_verifies(cpu, min(args.warmup, 2), max(args.steps, 1), args.reference_budget)
+    ms = statistics.mean(times) * 1e3
+    value = 1e3 / ms
     out = {"metric": METRIC, "value": round(value, 4), "unit": UNIT, "impl": "reference", "n_gpus": ws,
-           "steps": args.steps, "steps_timed": len(times), "warmup": args.warmup,
-           "ms_per_step": round(v * 1e3, 3), "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "steps": len(times), "steps_requested": args.steps, "warmup": min(args.warmup, 2),
+           "ms_per_step": round(ms, 3), "ms_median": round(statistics.median(times) * 1e3, 3),
+           "ms_min": round(min(times) * 1e3, 3), "ms_max": round(max(times) * 1e3, 3),
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": "q4_k/q6_k x f32 -> f32 (CPU)", "data": "synthetic",
            "config": {"workload": "Llama-3-8B-shaped Q4_K_M verify step, k=4 (5 rows), 2048-token KV, batch 1",
                       "rows": K_DRAFT + 1, "kv_len": KV_LEN},
-           "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": s.threads, "kind": "port",
-                            "sample": "per step: one layer (7 dequant-matmuls at M=5 + attention), "
-                                      "extrapolated x32 + LM head; reference Rust/candle path unavailable "
-                                      "(no cargo/rustc on this image, candle not vendored)"},
+           "cpu_baseline": {"value": round(value, 4), "unit": UNIT, "cores": cpu.threads, "kind": "port",
+                            "sample": f"per step one whole 32-layer verify (7 dequant-matmuls per layer at M=5, "
+                                      f"attention over {KV_LEN + K_DRAFT + 1} keys, full LM head; OpenMP over "
+                                      f"{cpu.threads} threads); {len(times)} steps timed within a "
+                                      f"{args.reference_budget:.0f} s budget; reference Rust/candle path "
+                                      "unavailable (no cargo/rustc on this image, candle not vendored)"},
            "e2e": {"value": round(value, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(out), flush=True)
 
@@ -489,7 +536,7 @@ def run_b200(args, ws, rank, local, dist):
     pkg = importlib.import_module("abyo-speculate_b200")
     torch.cuda.set_device(local)
     cfg = dict(CFG, n_layers=args.layers)
-    tp = args.tp
+    tp = args.tp if args.tp else ws  # default: one model over all N GPUs (tensor parallel)
     if tp < 1 or ws % tp:
         raise SystemExit(f"--tp {tp} must divide the number of ranks ({ws})")
     models = ws // tp
@@ -562,8 +609,11 @@ def run_b200(args, ws, rank, local, dist):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(dist, f0.elapsed_time(f1))
     sd_block = run_sd_greedy(pkg, dec, prompt, local) if (tp == 1 and not args.no_sd) else None
-    micro = run_microbench(pkg, local) if (rank == 0 and not args.no_microbench) else None
+    # The single-GPU microbench runs only at N=1 (under tensor parallelism the
+    # other ranks would wait inside the next forward's exchange meanwhile).
+    micro = run_microbench(pkg, local) if (ws == 1 and not args.no_microbench) else None
     # per-kernel profile of one eager verify forward (roofline)
+    barrier(dist)
     kinds, kms, kbytes = dec.profile_forward(drafts_all[0].tolist())
     dec.rollback_to(KV_LEN)
     peak, peak_kind = measured_peaks()
@@ -597,7 +647,8 @@ def run_b200(args, ws, rank, local, dist):
     out = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "q4_k/q6_k x f16 -> f32", "data": "synthetic",
+        "scaling": "strong" if tp > 1 else "weak", "vs_baseline": None, "dtype": "q4_k/q6_k x f16 -> f32",
+        "data": "synthetic",
         "config": {"workload": "Llama-3-8B-shaped Q4_K_M verify step, k=4 (5 rows), 2048-token KV, batch 1"
                    + ("" if args.layers == CFG["n_layers"] else f" ({args.layers} of 32 layers: profiling case)"),
                    "rows": K_DRAFT + 1, "kv_len": KV_LEN, "quant_mix": "Q4_K_M (Q6_K v/down on even layers, Q6_K head)",
@@ -640,14 +691,16 @@ def main():
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
-    ap.add_argument("--reference-budget", type=float, default=120.0)
+    ap.add_argument("--reference-budget", type=float, default=60.0,
+                    help="seconds of timed CPU verifies in the --impl reference arm (at least one runs)")
     ap.add_argument("--config", default="cfg2", choices=["cfg1", "cfg2", "cfg4", "cfg5"],
                     help="BASELINE.json config: cfg2 (default, the headline line), cfg1 = configs[0] SD loop, "
                          "cfg4 = configs[3] BF16 tree verify, cfg5 = configs[4] Qwen2.5-7B k=8 16K KV")
     ap.add_argument("--no-sd", action="store_true", help="skip the greedy SD-loop tokens/s measurement")
     ap.add_argument("--no-microbench", action="store_true", help="skip the dequant-matmul microbench (configs[2])")
-    ap.add_argument("--tp", type=int, default=1,
-                    help="tensor-parallel ranks per model (divides --gpus); 1 = one whole model per GPU")
+    ap.add_argument("--tp", type=int, default=0,
+                    help="tensor-parallel ranks per model (divides --gpus); default: all N GPUs hold one model "
+                         "(strong scaling of one verify stream); 1 = one whole model per GPU (N replicas)")
     ap.add_argument("--layers", type=int, default=CFG["n_layers"],
                     help="transformer layers of the synthetic target (32 = the benchmark; fewer only for ncu captures)")
     args = ap.parse_args()

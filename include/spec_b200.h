@@ -79,6 +79,27 @@ int spec_load_gguf(const char* path, const spec_load_opts* opts, spec_model** ou
 /* Synthetic model: seeded N(0, 0.02) weights quantized on the device. */
 int spec_create_synthetic(const spec_model_desc* desc, uint64_t seed, const spec_load_opts* opts,
                           spec_model** out);
+/* The device generator behind spec_create_synthetic, one tensor at a time,
+ * so a test or a CPU checker can rebuild the exact weights a synthetic model
+ * (and the benchmark) runs on.  spec_create_synthetic numbers its tensors
+ * 1, 2, ... in this order and seeds tensor i with
+ * spec_synthetic_seed(model_seed, i):
+ *   per layer: attn_q, attn_k, attn_v, attn_output, ffn_gate, ffn_up,
+ *              ffn_down (N(0, 0.02) matrices, [rows][K] GGUF blocks),
+ *              attn_norm, ffn_norm (1 + N(0, 0.02)), and for qwen2 one
+ *              q|k|v bias vector (N(0, 0.02));
+ *   then output_norm (1 + N(0, 0.02)), token_embd, output.
+ * Types follow the quant mix: Q4_K_M = Q4_K, with Q6_K for attn_v and
+ * ffn_down on even layers and for output; Q8_0 wherever K % 256 != 0.
+ * No counterpart in the reference (its weights come from checkpoints). */
+uint64_t spec_synthetic_seed(uint64_t model_seed, uint64_t index);
+/* Raw GGUF blocks of one N(0, sigma) tensor of `rows` x `k_cols`, generated on
+ * `device` and copied to host_out (out_bytes >= rows * k_cols / block elements
+ * * block bytes). */
+int spec_synthetic_tensor(int device, int ggml_type, int rows, int k_cols, uint64_t seed, float sigma,
+                          void* host_out, int64_t out_bytes);
+/* base + N(0, sigma) f32 vector of n elements (norm weights, biases). */
+int spec_synthetic_vector(int device, int n, uint64_t seed, float base, float sigma, float* host_out);
 void spec_free(spec_model* m);
 
 /* ---- tensor parallelism (one process per GPU) ----------------------------
@@ -299,7 +320,13 @@ typedef struct spec_qweight spec_qweight;
 int spec_qweight_upload(int ggml_type, const void* gguf_blocks, int n_rows, int k_cols, int device,
                         spec_qweight** out);
 void spec_qweight_free(spec_qweight* w);
-/* x_dev: M x K f32 (device), y_dev: M x N f32 (device); stream may be NULL. */
+/* x_dev: M x K f32 (device), y_dev: M x N f32 (device); stream may be NULL
+ * (the weight's own stream, synchronised on return).  The weight's device is
+ * current during the call and the caller's current device is restored.  With
+ * stream == NULL a device wait that gave up inside the kernel (y incomplete)
+ * returns SPEC_ERR_TIMEOUT and clears the weight's error word; with a caller
+ * stream nothing is synchronised and such a timeout is reported by the next
+ * synchronous call on the same weight.  Messages: spec_last_error(NULL). */
 int spec_qmatmul(spec_qweight* w, const float* x_dev, int M, float* y_dev, void* stream);
 /* Weight bytes of the packed matrix (equal to the GGUF byte count). */
 int64_t spec_qweight_bytes(const spec_qweight* w);
@@ -337,7 +364,13 @@ int spec_qmatmul_time(spec_qweight* w, int M, int iters, int flush_l2, float* av
  *     several host threads) race on it and corrupt each other's results;
  *   - each call zeroes the counters it uses (an async memset on `stream`)
  *     and rewrites everything else it reads before reading it;
- *   - stream may be NULL (the weight's own stream, synchronised on return).
+ *   - stream may be NULL (the weight's own stream, synchronised on return);
+ *     a synchronous call reports a device wait that gave up as
+ *     SPEC_ERR_TIMEOUT, like spec_qmatmul; with a caller stream the next
+ *     synchronous call on the weight reports it;
+ *   - the looked-up address belongs to the device's primary context: calls
+ *     must not cross a cudaDeviceReset of that device;
+ *   - the caller's current device is restored on return.
  * Error messages are thread-local (spec_last_error(NULL)). */
 #define SPEC_NOALLOC_SCRATCH_BYTES (16u << 20)
 int spec_qmatmul_noalloc(spec_qweight* w, const float* x_dev, int M, float* y_dev, void* stream);

@@ -79,6 +79,25 @@ def qmatmul(qtype: int, raw: np.ndarray, n: int, k: int, x: np.ndarray, threads:
     return y
 
 
+def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, threads: int = 0) -> np.ndarray:
+    """Causal attention of M new rows (oracle/quants.c oq_attention, f32):
+    q [n_heads, M, hd], k/v [n_kv, T, hd] with the M new keys last -> [M, n_heads * hd]."""
+    lib = oracle_lib()
+    if not getattr(lib, "_attn_bound", False):
+        lib.oq_attention.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int] * 5 + [ctypes.c_void_p, ctypes.c_int]
+        lib.oq_attention.restype = ctypes.c_int
+        lib._attn_bound = True
+    q = np.ascontiguousarray(q, dtype=np.float32)
+    k = np.ascontiguousarray(k, dtype=np.float32)
+    v = np.ascontiguousarray(v, dtype=np.float32)
+    nh, M, hd = q.shape
+    nkv, T, _ = k.shape
+    out = np.empty((M, nh * hd), dtype=np.float32)
+    if lib.oq_attention(q.ctypes.data, k.ctypes.data, v.ctypes.data, nh, nkv, M, T, hd, out.ctypes.data, threads):
+        raise ValueError("oracle attention: bad shape")
+    return out
+
+
 def bf16_round(a: np.ndarray) -> np.ndarray:
     u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
     r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
@@ -214,9 +233,12 @@ class OracleModel:
         total = prefix + n
         vis = np.zeros((n, total), dtype=bool)
         vis[:, :prefix] = True
-        for i in range(n):
-            for j in range(n):
-                vis[i, prefix + j] = bool((anc[i] >> j) & 1)
+        if list(anc) == causal_anc(n):
+            vis[:, prefix:] = np.tril(np.ones((n, n), dtype=bool))
+        else:
+            for i in range(n):
+                for j in range(n):
+                    vis[i, prefix + j] = bool((anc[i] >> j) & 1)
         collected = []
         for li in range(self.n_layers):
             p = f"blk.{li}."
@@ -254,8 +276,15 @@ class OracleModel:
         return hfin, collected
 
     def lm_head(self, hfin: np.ndarray) -> np.ndarray:
+        # In row blocks, so a vocabulary-sized head is never materialised in
+        # float64 at once (same products; each logit is one dot product).
         name = "output.weight" if "output.weight" in self.tensors else "token_embd.weight"
-        return hfin @ self.W(name)[: self.vocab].T
+        w = self.tensors[name]
+        out = np.empty((hfin.shape[0], self.vocab), dtype=np.float64)
+        for r0 in range(0, self.vocab, 16384):
+            r1 = min(r0 + 16384, self.vocab)
+            out[:, r0:r1] = hfin @ w[r0:r1].astype(np.float64).T
+        return out
 
 
 def causal_anc(n: int) -> List[int]:
@@ -295,11 +324,13 @@ class OracleDecoder:
         self.cache_len = 0
         self.last_logits = None
 
-    def _advance(self, tokens: Sequence[int]) -> np.ndarray:
+    def _advance(self, tokens: Sequence[int], last_only: bool = False) -> np.ndarray:
+        # last_only: the caller reads only the last row's logits (observe),
+        # so the LM head runs on that row alone; the result is the same row.
         n = len(tokens)
         P = self.cache_len
         h, _ = self.m.forward(tokens, list(range(P, P + n)), list(range(P, P + n)), P, causal_anc(n))
-        logits = self.m.lm_head(h)
+        logits = self.m.lm_head(h[-1:] if last_only else h)
         self.cache_len += n
         self.last_logits = logits[-1].copy()
         return logits
@@ -307,7 +338,7 @@ class OracleDecoder:
     def observe(self, ids: Sequence[int]) -> None:
         if len(ids) == 0:
             return
-        self._advance(ids)
+        self._advance(ids, last_only=True)
         self.history.extend(int(t) for t in ids)
 
     def next_logits(self) -> np.ndarray:
@@ -315,7 +346,7 @@ class OracleDecoder:
             return self.last_logits.copy()
         last = self.history[-1]
         self.cache_len = len(self.history) - 1
-        return self._advance([last])[-1]
+        return self._advance([last], last_only=True)[-1]
 
     def batched_logits(self, drafts: Sequence[int]) -> np.ndarray:
         if len(drafts) == 0:

@@ -249,3 +249,64 @@ int oq_qmatmul(int fmt, const uint8_t* W, int64_t N, int64_t K, const float* x, 
     }
     return err ? -1 : 0;
 }
+
+/*
+ * oq_attention: the attention core of one layer for M new rows, the CPU leg
+ * of the verify-step timing (bench.py cpu_baseline / --impl reference).
+ * Restates run_attn (crates/speculate/src/model/quantized_llama_local.rs:
+ * 107-136): scores q . k^T / sqrt(hd) plus the causal bias (causal_bias,
+ * :332-350: the T - M prefix keys are visible to every row, new key j to new
+ * row i iff j <= i), softmax over the keys, times v; the G = n_heads / n_kv
+ * query heads of a KV head share it (repeat_kv, :115-123).
+ *   q   [n_heads][M][hd]   (rows already rotated)
+ *   k,v [n_kv][T][hd]      (T = prefix + M keys, the new rows last)
+ *   out [M][n_heads * hd]
+ * f32 throughout (the reference's quantized model keeps f32 activations);
+ * heads run in parallel with OpenMP.
+ */
+int oq_attention(const float* q, const float* k, const float* v, int n_heads, int n_kv, int M, int T, int hd,
+                 float* out, int nthreads) {
+    if (n_heads <= 0 || n_kv <= 0 || n_heads % n_kv || M <= 0 || T < M || hd <= 0) return -1;
+    const int G = n_heads / n_kv, prefix = T - M;
+    const float scale = 1.0f / sqrtf((float)hd);
+#ifdef _OPENMP
+    if (nthreads > 0) omp_set_num_threads(nthreads);
+#else
+    (void)nthreads;
+#endif
+    int err = 0;
+#pragma omp parallel reduction(| : err)
+    {
+        float* s = (float*)malloc(sizeof(float) * (size_t)T);
+        if (!s) err |= 1;
+#pragma omp for schedule(static)
+        for (int hm = 0; hm < n_heads * M; hm++) {
+            if (!s) continue;
+            const int h = hm / M, i = hm % M, kvh = h / G;
+            const float* qi = q + ((size_t)h * M + i) * hd;
+            const float* kh = k + (size_t)kvh * T * hd;
+            const float* vh = v + (size_t)kvh * T * hd;
+            const int visible = prefix + i + 1;
+            float mx = -INFINITY;
+            for (int j = 0; j < visible; j++) {
+                float acc = 0.f;
+                for (int d = 0; d < hd; d++) acc += qi[d] * kh[(size_t)j * hd + d];
+                s[j] = acc * scale;
+                if (s[j] > mx) mx = s[j];
+            }
+            float sum = 0.f;
+            for (int j = 0; j < visible; j++) {
+                s[j] = expf(s[j] - mx);
+                sum += s[j];
+            }
+            float* o = out + (size_t)i * n_heads * hd + (size_t)h * hd;
+            for (int d = 0; d < hd; d++) o[d] = 0.f;
+            for (int j = 0; j < visible; j++) {
+                const float p = s[j] / sum;
+                for (int d = 0; d < hd; d++) o[d] += p * vh[(size_t)j * hd + d];
+            }
+        }
+        free(s);
+    }
+    return err ? -1 : 0;
+}

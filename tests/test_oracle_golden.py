@@ -47,3 +47,27 @@ def test_oracle_qmatmul_matches_dense(oracle, synth, name):
     deq = oracle.dequant(TYPES[name], raw, w.size).reshape(w.shape).astype(np.float64)
     y = oracle.qmatmul(TYPES[name], raw, 64, 512, x)
     assert np.allclose(y, x.astype(np.float64) @ deq.T, atol=1e-5, rtol=1e-5)
+
+
+def test_oracle_c_attention_matches_float64_model(oracle):
+    """oq_attention (the C attention the CPU baseline times) against the
+    float64 attention of oracle/model.py's forward: causal bias over the new
+    rows, prefix keys visible, GQA head sharing."""
+    rng = np.random.default_rng(9)
+    nh, nkv, M, T, hd = 8, 2, 5, 70, 64
+    q = rng.standard_normal((nh, M, hd)).astype(np.float32)
+    k = rng.standard_normal((nkv, T, hd)).astype(np.float32)
+    v = rng.standard_normal((nkv, T, hd)).astype(np.float32)
+    got = oracle.attention(q, k, v, threads=2)
+    G = nh // nkv
+    vis = np.zeros((M, T), dtype=bool)
+    vis[:, :T - M] = True
+    vis[:, T - M:] = np.tril(np.ones((M, M), dtype=bool))
+    want = np.empty((M, nh, hd))
+    for h in range(nh):
+        sc = q[h].astype(np.float64) @ k[h // G].astype(np.float64).T / np.sqrt(hd)
+        sc = np.where(vis, sc, -np.inf)
+        p = np.exp(sc - sc.max(axis=-1, keepdims=True))
+        p /= p.sum(axis=-1, keepdims=True)
+        want[:, h] = p @ v[h // G]
+    assert np.abs(got - want.reshape(M, -1)).max() <= 1e-5
