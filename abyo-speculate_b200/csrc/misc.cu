@@ -391,6 +391,26 @@ SPEC_DEV float gauss(uint64_t seed, uint64_t idx) {
 
 SPEC_DEV uint16_t f2h_bits(float f) { return __half_as_ushort(__float2half_rn(f)); }
 
+// One GGUF block assembled in registers (up to 212 bytes as 53 words), then
+// written out with 16-bit stores: every block base is 2-byte aligned
+// (cudaMalloc alignment, even block sizes) and no byte of global memory is
+// read back or written twice.  (Building the block with byte read-modify-
+// writes in global memory left the low byte of Q6_K's d and of Q4_K's dmin
+// wrong on B200, which scaled Q6_K weights by about 0.79 and biased Q4_K
+// weights by +0.003.)
+struct BlockBytes {
+  uint32_t w[53];
+  SPEC_DEV void clear() {
+#pragma unroll
+    for (int i = 0; i < 53; ++i) w[i] = 0u;
+  }
+  SPEC_DEV void set(int i, uint32_t v) { w[i >> 2] |= (v & 0xffu) << (8 * (i & 3)); }
+  SPEC_DEV void store(uint8_t* out, int bytes) const {
+    uint16_t* o = reinterpret_cast<uint16_t*>(out);
+    for (int i = 0; i < bytes / 2; ++i) o[i] = (uint16_t)(w[i >> 1] >> (16 * (i & 1)));
+  }
+};
+
 // One thread per block of the row-major [rows][K] matrix.
 __global__ void synth_quant_kernel(uint8_t* raw, int fmt, int rows, int K, uint64_t seed, float sigma,
                                    int row_offset) {
@@ -401,6 +421,19 @@ __global__ void synth_quant_kernel(uint8_t* raw, int fmt, int rows, int K, uint6
   const int r = (int)(blk / nbr), c = (int)(blk % nbr);
   uint8_t* out = raw + blk * bb;
   const uint64_t base = ((uint64_t)(r + row_offset) * (uint64_t)K) + (uint64_t)c * be;
+  if (fmt == WF_BF16 || fmt == WF_F16 || fmt == WF_F32) {
+    const float x = sigma * gauss(seed, base);
+    if (fmt == WF_BF16) {
+      *reinterpret_cast<uint16_t*>(out) = __bfloat16_as_ushort(__float2bfloat16_rn(x));
+    } else if (fmt == WF_F16) {
+      *reinterpret_cast<uint16_t*>(out) = f2h_bits(x);
+    } else {
+      *reinterpret_cast<float*>(out) = x;
+    }
+    return;
+  }
+  BlockBytes B;
+  B.clear();
   if (fmt == WF_Q8_0) {
     float x[32], amax = 0.f;
     for (int i = 0; i < 32; ++i) {
@@ -409,32 +442,17 @@ __global__ void synth_quant_kernel(uint8_t* raw, int fmt, int rows, int K, uint6
     }
     const uint16_t db = f2h_bits(amax / 127.f);
     const float d = h2f16(db);
-    out[0] = db & 0xff;
-    out[1] = db >> 8;
+    B.set(0, db & 0xff);
+    B.set(1, db >> 8);
     for (int i = 0; i < 32; ++i) {
       const float q = d > 0.f ? rintf(x[i] / d) : 0.f;
-      out[2 + i] = (uint8_t)(int8_t)fminf(fmaxf(q, -127.f), 127.f);
+      B.set(2 + i, (uint8_t)(int8_t)fminf(fmaxf(q, -127.f), 127.f));
     }
-    return;
-  }
-  if (fmt == WF_BF16 || fmt == WF_F16 || fmt == WF_F32) {
-    const float x = sigma * gauss(seed, base);
-    if (fmt == WF_BF16) {
-      const uint16_t b = __bfloat16_as_ushort(__float2bfloat16_rn(x));
-      out[0] = b & 0xff;
-      out[1] = b >> 8;
-    } else if (fmt == WF_F16) {
-      const uint16_t b = f2h_bits(x);
-      out[0] = b & 0xff;
-      out[1] = b >> 8;
-    } else {
-      *reinterpret_cast<float*>(out) = x;
-    }
+    B.store(out, bb);
     return;
   }
   float x[256];
   for (int i = 0; i < 256; ++i) x[i] = sigma * gauss(seed, base + i);
-  for (int i = 0; i < bb; ++i) out[i] = 0;
   if (fmt == WF_Q6_K) {
     float scale[16], dmax = 0.f;
     for (int s = 0; s < 16; ++s) {
@@ -445,22 +463,25 @@ __global__ void synth_quant_kernel(uint8_t* raw, int fmt, int rows, int K, uint6
     }
     const uint16_t db = f2h_bits(dmax / 127.f);
     const float d = h2f16(db);
-    out[208] = db & 0xff;
-    out[209] = db >> 8;
+    B.set(208, db & 0xff);
+    B.set(209, db >> 8);
     for (int s = 0; s < 16; ++s) {
       const int sc = d > 0.f ? (int)fminf(fmaxf(rintf(scale[s] / d), 0.f), 127.f) : 0;
-      out[192 + s] = (uint8_t)(int8_t)sc;
+      B.set(192 + s, (uint8_t)(int8_t)sc);
       const float se = d * (float)sc;
       for (int i = 0; i < 16; ++i) {
         const int k = 16 * s + i;
         int q = se > 0.f ? (int)fminf(fmaxf(rintf(x[k] / se), -32.f), 31.f) : 0;
         q += 32;
+        // GGUF Q6_K: half n = k / 128; within it quarter j = (k % 128) / 32 and
+        // lane l: low nibble in ql[64 n + l + 32 (j & 1)] (high nibble for
+        // j >= 2), top 2 bits in qh[32 n + l] at bit 2 j.
         const int n = k >> 7, rr = k & 127, j = rr >> 5, l = rr & 31;
-        uint8_t& lb = out[64 * n + l + (j & 1) * 32];
-        lb |= (j < 2) ? (q & 15) : ((q & 15) << 4);
-        out[128 + 32 * n + l] |= (uint8_t)(((q >> 4) & 3) << (2 * j));
+        B.set(64 * n + l + (j & 1) * 32, (j < 2) ? (q & 15) : ((q & 15) << 4));
+        B.set(128 + 32 * n + l, ((q >> 4) & 3) << (2 * j));
       }
     }
+    B.store(out, bb);
     return;
   }
   // Q4_K / Q5_K
@@ -479,30 +500,33 @@ __global__ void synth_quant_kernel(uint8_t* raw, int fmt, int rows, int K, uint6
   }
   const uint16_t db = f2h_bits(smax / 63.f), dmb = f2h_bits(mmax / 63.f);
   const float d = h2f16(db), dm = h2f16(dmb);
-  out[0] = db & 0xff;
-  out[1] = db >> 8;
-  out[2] = dmb & 0xff;
-  out[3] = dmb >> 8;
+  B.set(0, db & 0xff);
+  B.set(1, db >> 8);
+  B.set(2, dmb & 0xff);
+  B.set(3, dmb >> 8);
   int sc[8], mq[8];
   for (int s = 0; s < 8; ++s) {
     sc[s] = d > 0.f ? (int)fminf(fmaxf(rintf(scale[s] / d), 0.f), 63.f) : 0;
     mq[s] = dm > 0.f ? (int)fminf(fmaxf(rintf(mins[s] / dm), 0.f), 63.f) : 0;
   }
-  uint8_t* sp = out + 4;
+  // 6-bit (scale, min) packing of the GGUF K-quants: sub-blocks 0-3 in the low
+  // 6 bits of bytes 4-7 / 8-11; sub-blocks 4-7 as low nibbles in bytes 12-15
+  // and their top 2 bits in the high bits of bytes 4-11.
   for (int j = 0; j < 4; ++j) {
-    sp[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
-    sp[j + 4] = (uint8_t)((mq[j] & 63) | ((mq[j + 4] >> 4) << 6));
-    sp[j + 8] = (uint8_t)((sc[j + 4] & 15) | ((mq[j + 4] & 15) << 4));
+    B.set(4 + j, (sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+    B.set(8 + j, (mq[j] & 63) | ((mq[j + 4] >> 4) << 6));
+    B.set(12 + j, (sc[j + 4] & 15) | ((mq[j + 4] & 15) << 4));
   }
   const int qoff = fmt == WF_Q4_K ? 16 : 48;
   for (int k = 0; k < 256; ++k) {
     const int s = k >> 5;
     const float se = d * (float)sc[s], ce = dm * (float)mq[s];
-    int q = se > 0.f ? (int)fminf(fmaxf(rintf((x[k] + ce) / se), 0.f), (float)levels) : 0;
-    const int c = k >> 6, l = k & 31, hi = (k & 63) >> 5;
-    out[qoff + 32 * c + l] |= (uint8_t)((q & 15) << (hi ? 4 : 0));
-    if (fmt == WF_Q5_K && (q >> 4)) out[16 + l] |= (uint8_t)(1u << (2 * c + hi));
+    const int q = se > 0.f ? (int)fminf(fmaxf(rintf((x[k] + ce) / se), 0.f), (float)levels) : 0;
+    const int cc = k >> 6, l = k & 31, hi = (k & 63) >> 5;
+    B.set(qoff + 32 * cc + l, (q & 15) << (hi ? 4 : 0));
+    if (fmt == WF_Q5_K && (q >> 4)) B.set(16 + l, 1u << (2 * cc + hi));
   }
+  B.store(out, bb);
 }
 
 // grid (ceil(K/128), M): f32 row-major activations -> operand fragments.
