@@ -30,7 +30,14 @@ enum DevError : unsigned {
 // err[3] = the counter value it last saw.
 // (Site 2 was the consumers' per-op dependency wait, which per-group flags
 // made unnecessary; the number stays retired.)
-enum WaitSite : unsigned { WAIT_CONSUMER_FULL = 1, WAIT_PRODUCER_IDLE = 3, WAIT_TP_PEERS = 4, WAIT_ATTN_DEP = 5 };
+// Site 6: the producer's last wait for its own copies to land before exit.
+enum WaitSite : unsigned {
+  WAIT_CONSUMER_FULL = 1,
+  WAIT_PRODUCER_IDLE = 3,
+  WAIT_TP_PEERS = 4,
+  WAIT_ATTN_DEP = 5,
+  WAIT_PRODUCER_DRAIN = 6
+};
 
 // GGML type ids (public GGUF specification) of the weight formats handled.
 enum WFmt : int { WF_F32 = 0, WF_F16 = 1, WF_Q8_0 = 8, WF_Q4_K = 12, WF_Q5_K = 13, WF_Q6_K = 14, WF_BF16 = 30 };
@@ -195,6 +202,15 @@ struct FwdParams {
   const FwdOp* ops = nullptr;  // device array (16-byte aligned)
   int n_ops = 0;
   int* done = nullptr;         // [n_ops] completion counters, zero at launch
+  // Work claiming.  The launch's GEMV work is the list of (op, stream-K
+  // chunk) items in op order.  With `claim` set (a counter, zero at launch)
+  // CTAs take items from it with atomicAdd in that order, so an item whose
+  // inputs another item produces is only ever waited on after that item was
+  // claimed by a running CTA: progress needs no CTA to be resident, and a CTA
+  // that runs late (an epilogue, a slow SM) simply takes fewer items.  Null:
+  // CTA c takes chunks c, c + grid, ... of every op (the single-op launches,
+  // where no item waits on another).
+  int* claim = nullptr;
   unsigned* err = nullptr;
   int l2_ahead = 0;            // stages of this CTA's weights prefetched into L2 ahead of the ring
   // Per-group completion flags [n_ops][flag_stride]: a group's epilogue

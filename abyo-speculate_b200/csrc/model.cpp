@@ -208,6 +208,7 @@ struct spec_model {
   bool fused_attn = false;          // attention as ops of the forward kernel (else its own kernels)
   bool attn_trigger = true;         // a launch's attention tail overlaps the next launch (PDL trigger)
   bool attn_kernels_pdl = true;     // programmatic launch of the standalone attention kernels
+  bool static_claim = false;        // forward launches walk chunks c, c + grid, ... (SPEC_B200_STATIC_CLAIM)
   FwdOp* single_op = nullptr;       // device slot for one-op launches
   FwdOp* single_op_host = nullptr;  // pinned staging
   int* single_done = nullptr;
@@ -797,7 +798,8 @@ int get_schedule(spec_model* m, int M, int flags, spec_model::Schedule** out) {
   sc.n_ops = (int)ops.size();
   sc.host_ops = ops;
   cudaError_t e = m->dalloc(&sc.ops, sizeof(FwdOp) * ops.size());
-  if (e == cudaSuccess) e = m->dalloc(&sc.done, sizeof(int) * ops.size());
+  // done: one completion counter per op, then one work-claim counter per launch
+  if (e == cudaSuccess) e = m->dalloc(&sc.done, sizeof(int) * (ops.size() + sc.launches.size()));
   if (e == cudaSuccess) e = m->dalloc(&sc.gflags, sizeof(int) * ops.size() * m->counter_set);
   if (e == cudaSuccess) e = m->upload(sc.ops, ops.data(), sizeof(FwdOp) * ops.size());
   if (e == cudaSuccess) {
@@ -818,6 +820,7 @@ cudaError_t launch_slice(spec_model* m, const spec_model::Schedule& sc, int li, 
   fp.ops = sc.ops + sc.launches[li].first;
   fp.n_ops = sc.launches[li].second - sc.launches[li].first;
   fp.done = sc.done + sc.launches[li].first;
+  fp.claim = m->static_claim ? nullptr : sc.done + sc.n_ops + li;
   fp.err = m->err_dev;
   fp.l2_ahead = m->l2_ahead;
   fp.gflags = sc.gflags + (size_t)sc.launches[li].first * m->counter_set;
@@ -876,7 +879,7 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
   if (get_schedule(m, M, flags, &sc) != SPEC_OK) return cudaErrorMemoryAllocation;
   cudaError_t e = cudaMemcpyAsync(m->step_dev, m->step_host, sizeof(StepDev), cudaMemcpyHostToDevice, s);
   if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(sc->done, 0, sizeof(int) * sc->n_ops, s);
+  e = cudaMemsetAsync(sc->done, 0, sizeof(int) * (sc->n_ops + sc->launches.size()), s);
   if (e != cudaSuccess) return e;
   EmbedParams ep;
   ep.table = m->embed_raw;
@@ -1148,6 +1151,7 @@ int init_device(spec_model* m, const spec_load_opts* opts) {
   if (getenv("SPEC_B200_FUSED_ATTN")) m->fused_attn = true;
   if (getenv("SPEC_B200_NO_ATTN_TRIGGER")) m->attn_trigger = false;
   if (getenv("SPEC_B200_ATTN_KERNELS_NO_PDL")) m->attn_kernels_pdl = false;
+  if (getenv("SPEC_B200_STATIC_CLAIM")) m->static_claim = true;
   if (const char* env = getenv("SPEC_B200_L2_AHEAD")) m->l2_ahead = atoi(env);
   cudaError_t e = cudaSetDevice(m->device);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "cudaSetDevice"));
