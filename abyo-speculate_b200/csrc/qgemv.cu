@@ -1358,11 +1358,12 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
           }
         }
       }
-      // Every issued copy must land before this CTA can retire.  The end
-      // mark reused the slot of position wpos - D (sent only after the
-      // consumers released that stage, so its copy has landed) and moved that
-      // barrier one phase on: that position is not waited for again.
-      const int first = wpos > D ? wpos - D + (end_sent ? 1 : 0) : 0;
+      // Every issued copy must land before this CTA can retire: positions
+      // [wpos - D, wpos).  An end mark sent at position wpos >= D reused the
+      // slot of position wpos - D (sent only after the consumers released
+      // that stage, so its copy has landed) and moved that barrier one phase
+      // on: that position is not waited for again.
+      const int first = wpos >= D ? wpos - D + (end_sent ? 1 : 0) : 0;
       for (int pos = first; pos < wpos; ++pos)
         if (!mbar_wait_bounded(&full[pos % D], (uint32_t)((pos / D) & 1), nullptr))
           wait_gave_up(P.err, WAIT_PRODUCER_DRAIN, 255, pos, wpos);
