@@ -208,7 +208,8 @@ struct spec_model {
   bool fused_attn = false;          // attention as ops of the forward kernel (else its own kernels)
   bool attn_trigger = true;         // a launch's attention tail overlaps the next launch (PDL trigger)
   bool attn_kernels_pdl = true;     // programmatic launch of the standalone attention kernels
-  bool static_claim = false;        // forward launches walk chunks c, c + grid, ... (SPEC_B200_STATIC_CLAIM)
+  bool dynamic_claim = false;       // forward launches claim chunks from a counter (SPEC_B200_DYNAMIC_CLAIM)
+  bool coop = true;                 // multi-op forward launches are cooperative (SPEC_B200_NO_COOP clears)
   FwdOp* single_op = nullptr;       // device slot for one-op launches
   FwdOp* single_op_host = nullptr;  // pinned staging
   int* single_done = nullptr;
@@ -820,7 +821,11 @@ cudaError_t launch_slice(spec_model* m, const spec_model::Schedule& sc, int li, 
   fp.ops = sc.ops + sc.launches[li].first;
   fp.n_ops = sc.launches[li].second - sc.launches[li].first;
   fp.done = sc.done + sc.launches[li].first;
-  fp.claim = m->static_claim ? nullptr : sc.done + sc.n_ops + li;
+  // Static chunk assignment with a cooperative launch (every CTA resident,
+  // so no CTA waits on a group whose CTA has not started), or claims from the
+  // launch's counter (no residency needed).
+  fp.claim = m->dynamic_claim ? sc.done + sc.n_ops + li : nullptr;
+  fp.cooperative = (!m->dynamic_claim && m->coop && fp.n_ops > 1) ? 1 : 0;
   fp.err = m->err_dev;
   fp.l2_ahead = m->l2_ahead;
   fp.gflags = sc.gflags + (size_t)sc.launches[li].first * m->counter_set;
@@ -1151,7 +1156,8 @@ int init_device(spec_model* m, const spec_load_opts* opts) {
   if (getenv("SPEC_B200_FUSED_ATTN")) m->fused_attn = true;
   if (getenv("SPEC_B200_NO_ATTN_TRIGGER")) m->attn_trigger = false;
   if (getenv("SPEC_B200_ATTN_KERNELS_NO_PDL")) m->attn_kernels_pdl = false;
-  if (getenv("SPEC_B200_STATIC_CLAIM")) m->static_claim = true;
+  if (getenv("SPEC_B200_DYNAMIC_CLAIM")) m->dynamic_claim = true;
+  if (getenv("SPEC_B200_NO_COOP")) m->coop = false;
   if (const char* env = getenv("SPEC_B200_L2_AHEAD")) m->l2_ahead = atoi(env);
   cudaError_t e = cudaSetDevice(m->device);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "cudaSetDevice"));

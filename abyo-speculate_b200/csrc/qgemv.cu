@@ -1669,11 +1669,16 @@ struct FwdInst {
     cfg.blockDim = dim3((kGemvWarps + 1) * 32, 1, 1);
     cfg.dynamicSmemBytes = FGeo<SET, NT>::SMEM;
     cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
+    if (p.cooperative) {
+      attr[1].id = cudaLaunchAttributeCooperative;
+      attr[1].val.cooperative = 1;
+      cfg.numAttrs = 2;
+    }
     return cudaLaunchKernelEx(&cfg, fwd_kernel<SET, NT>, p);
   }
 };
