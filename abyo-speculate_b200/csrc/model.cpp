@@ -941,10 +941,13 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
       a.xsum32 = m->xb32;
       a.act_bf16 = c.bf16 ? 1 : 0;
       a.err = m->err_dev;
-      // 64-key splits launch 512+ small split CTAs; chained programmatically
-      // ahead of the next forward kernel they lost a GEMV group's completion
-      // on B200 (a bounded wait fired), so they run without the early launch.
-      const bool attn_pdl = pdl && m->attn_kernels_pdl && m->attn_chunk >= 128;
+      // 64-key splits launch 512+ small split CTAs.  Chained programmatically
+      // ahead of a forward kernel whose CTAs could start before all of them
+      // fit, they lost a GEMV group's completion on B200 (a bounded wait
+      // fired).  A cooperative forward launch, or counter claims, cannot be
+      // caught that way; otherwise they run without the early launch.
+      const bool fwd_safe = m->dynamic_claim || m->coop;
+      const bool attn_pdl = pdl && m->attn_kernels_pdl && (m->attn_chunk >= 128 || fwd_safe);
       if ((e = launch_attention(a, nt, s, attn_pdl)) != cudaSuccess) return e;
       if ((e = prof_mark(pr, s, K_ATTN, attn_bytes)) != cudaSuccess) return e;
     }
