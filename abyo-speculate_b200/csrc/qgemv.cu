@@ -1321,8 +1321,17 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
       while (xi.valid || !end_sent) {
         bool progressed = false;
         if (xi.valid && xpos < wpos) {
-          if (xi.op <= ready_op || stage_ready(xi)) {
-            fence_proxy_async_global();
+          bool rdy = xi.op <= ready_op;
+          if (!rdy && stage_ready(xi)) {
+            rdy = true;
+            // stage_ready acquired the producing groups' generic-proxy writes;
+            // one proxy fence orders them before this thread's bulk copies
+            // that read them.  Stages of an op whose inputs were acquired
+            // already, and inputs written by the previous kernel (ordered by
+            // griddepcontrol.wait), need no fence.
+            if (P.ops[xi.op].dep >= 0) fence_proxy_async_global();
+          }
+          if (rdy) {
             issue_x(xi, xpos);
             cur_next(xi);
             ++xpos;
