@@ -1163,18 +1163,22 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], kGemvWarps);
     }
-    // From the global descriptors: s_ops is still being filled by the other threads.
+  }
+  fence_mbar_init();
+  __syncthreads();
+  // From the shared copy of the descriptors (complete after the barrier; a
+  // walk over the global ones would chain one memory round trip per op).
+  if (threadIdx.x == 0) {
     int n = 0, b = 0;
-    const int nops = Pg.n_ops < kMaxLaunchOps ? Pg.n_ops : kMaxLaunchOps;
-    while (n < nops && Pg.ops[n].kind == OPK_GEMV) {
+    const int nops = P.n_ops < kMaxLaunchOps ? P.n_ops : kMaxLaunchOps;
+    while (n < nops && s_ops[n].kind == OPK_GEMV) {
       s_base[n] = b;
-      b += Pg.ops[n].q.chunks;
+      b += s_ops[n].q.chunks;
       ++n;
     }
     s_base[n] = b;
     s_n_gemv = n;
   }
-  fence_mbar_init();
   __syncthreads();
   const int n_gemv = s_n_gemv;
 
