@@ -202,18 +202,9 @@ struct FwdParams {
   const FwdOp* ops = nullptr;  // device array (16-byte aligned)
   int n_ops = 0;
   int* done = nullptr;         // [n_ops] completion counters, zero at launch
-  // Work assignment.  The launch's GEMV work is the list of (op, stream-K
-  // chunk) items in op order.  Null `claim` (the default): CTA c takes chunks
-  // c, c + grid, ... of every op.  An item of a later op waits for groups
-  // other CTAs produce, so a multi-op launch then needs every CTA resident at
-  // once: it is launched cooperative (`cooperative`), which the hardware
-  // guarantees or refuses.  With `claim` set (a counter, zero at launch) CTAs
-  // take items from it with atomicAdd in op order instead, so an item is only
-  // ever waited on after a running CTA claimed it: progress needs no CTA to
-  // be resident.  That is slower at one chunk per CTA and op (a CTA that
-  // claims ahead can hold two chunks of an op while another holds none), so
-  // it is opt-in (SPEC_B200_DYNAMIC_CLAIM).
-  int* claim = nullptr;
+  // Launch attribute (host side): all CTAs co-resident.  Multi-op launches
+  // need it: CTA c takes chunks c, c + grid, ... of every op, and a chunk of a
+  // later op waits for groups other CTAs produce.
   int cooperative = 0;  // launch attribute (host side): all CTAs co-resident
   unsigned* err = nullptr;
   int l2_ahead = 0;            // stages of this CTA's weights prefetched into L2 ahead of the ring

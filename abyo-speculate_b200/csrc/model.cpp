@@ -208,7 +208,6 @@ struct spec_model {
   bool fused_attn = false;          // attention as ops of the forward kernel (else its own kernels)
   bool attn_trigger = true;         // a launch's attention tail overlaps the next launch (PDL trigger)
   bool attn_kernels_pdl = true;     // programmatic launch of the standalone attention kernels
-  bool dynamic_claim = false;       // forward launches claim chunks from a counter (SPEC_B200_DYNAMIC_CLAIM)
   bool coop = true;                 // multi-op forward launches are cooperative (SPEC_B200_NO_COOP clears)
   FwdOp* single_op = nullptr;       // device slot for one-op launches
   FwdOp* single_op_host = nullptr;  // pinned staging
@@ -799,8 +798,7 @@ int get_schedule(spec_model* m, int M, int flags, spec_model::Schedule** out) {
   sc.n_ops = (int)ops.size();
   sc.host_ops = ops;
   cudaError_t e = m->dalloc(&sc.ops, sizeof(FwdOp) * ops.size());
-  // done: one completion counter per op, then one work-claim counter per launch
-  if (e == cudaSuccess) e = m->dalloc(&sc.done, sizeof(int) * (ops.size() + sc.launches.size()));
+  if (e == cudaSuccess) e = m->dalloc(&sc.done, sizeof(int) * ops.size());
   if (e == cudaSuccess) e = m->dalloc(&sc.gflags, sizeof(int) * ops.size() * m->counter_set);
   if (e == cudaSuccess) e = m->upload(sc.ops, ops.data(), sizeof(FwdOp) * ops.size());
   if (e == cudaSuccess) {
@@ -821,11 +819,9 @@ cudaError_t launch_slice(spec_model* m, const spec_model::Schedule& sc, int li, 
   fp.ops = sc.ops + sc.launches[li].first;
   fp.n_ops = sc.launches[li].second - sc.launches[li].first;
   fp.done = sc.done + sc.launches[li].first;
-  // Static chunk assignment with a cooperative launch (every CTA resident,
-  // so no CTA waits on a group whose CTA has not started), or claims from the
-  // launch's counter (no residency needed).
-  fp.claim = m->dynamic_claim ? sc.done + sc.n_ops + li : nullptr;
-  fp.cooperative = (!m->dynamic_claim && m->coop && fp.n_ops > 1) ? 1 : 0;
+  // A cooperative launch: every CTA resident, so no CTA waits on a group
+  // whose CTA has not started.
+  fp.cooperative = (m->coop && fp.n_ops > 1) ? 1 : 0;
   fp.err = m->err_dev;
   fp.l2_ahead = m->l2_ahead;
   fp.gflags = sc.gflags + (size_t)sc.launches[li].first * m->counter_set;
@@ -884,7 +880,7 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
   if (get_schedule(m, M, flags, &sc) != SPEC_OK) return cudaErrorMemoryAllocation;
   cudaError_t e = cudaMemcpyAsync(m->step_dev, m->step_host, sizeof(StepDev), cudaMemcpyHostToDevice, s);
   if (e != cudaSuccess) return e;
-  e = cudaMemsetAsync(sc->done, 0, sizeof(int) * (sc->n_ops + sc->launches.size()), s);
+  e = cudaMemsetAsync(sc->done, 0, sizeof(int) * sc->n_ops, s);
   if (e != cudaSuccess) return e;
   EmbedParams ep;
   ep.table = m->embed_raw;
@@ -944,10 +940,9 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
       // 64-key splits launch 512+ small split CTAs.  Chained programmatically
       // ahead of a forward kernel whose CTAs could start before all of them
       // fit, they lost a GEMV group's completion on B200 (a bounded wait
-      // fired).  A cooperative forward launch, or counter claims, cannot be
-      // caught that way; otherwise they run without the early launch.
-      const bool fwd_safe = m->dynamic_claim || m->coop;
-      const bool attn_pdl = pdl && m->attn_kernels_pdl && (m->attn_chunk >= 128 || fwd_safe);
+      // fired).  A cooperative forward launch cannot be caught that way;
+      // without it they run without the early launch.
+      const bool attn_pdl = pdl && m->attn_kernels_pdl && (m->attn_chunk >= 128 || m->coop);
       if ((e = launch_attention(a, nt, s, attn_pdl)) != cudaSuccess) return e;
       if ((e = prof_mark(pr, s, K_ATTN, attn_bytes)) != cudaSuccess) return e;
     }
@@ -1159,7 +1154,6 @@ int init_device(spec_model* m, const spec_load_opts* opts) {
   if (getenv("SPEC_B200_FUSED_ATTN")) m->fused_attn = true;
   if (getenv("SPEC_B200_NO_ATTN_TRIGGER")) m->attn_trigger = false;
   if (getenv("SPEC_B200_ATTN_KERNELS_NO_PDL")) m->attn_kernels_pdl = false;
-  if (getenv("SPEC_B200_DYNAMIC_CLAIM")) m->dynamic_claim = true;
   if (getenv("SPEC_B200_NO_COOP")) m->coop = false;
   if (const char* env = getenv("SPEC_B200_L2_AHEAD")) m->l2_ahead = atoi(env);
   cudaError_t e = cudaSetDevice(m->device);

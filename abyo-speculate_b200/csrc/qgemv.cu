@@ -913,35 +913,6 @@ SPEC_DEV void seq_next(const FwdParams& P, int c, int G, SeqIt& it) {
   seq_settle(P, c, G, it);
 }
 
-// ---------------------------------------------------------------------------
-// Work items of a launch: (GEMV op, stream-K chunk) in op order, numbered
-// t = base[op] + chunk.  Each CTA's producer claims items (FwdParams::claim)
-// into a shared-memory queue; its own cursors (L2 prefetch, weights,
-// operands) and the consumers walk that queue in order.  The queue holds the
-// items between the consumers (up to D stages behind the weight cursor) and
-// the prefetch cursor (up to D + l2_ahead stages ahead of it); an item has at
-// least one stage, so kItemQueue >= 2 D + l2_ahead + 2 entries suffice.
-// ---------------------------------------------------------------------------
-constexpr int kItemQueue = 32;
-constexpr int kItemEnd = -1;  // queue entry: no more GEMV items for this CTA
-
-struct ItemCur {
-  int j = 0;  // position in this CTA's item sequence
-  int op = 0, chunk = 0, s = 0, s_end = 0;
-  bool valid = false;
-};
-
-SPEC_DEV void item_decode(const FwdParams& P, const int* base, int n_gemv, int t, ItemCur& k) {
-  int op = 0;
-  while (op + 1 < n_gemv && t >= base[op + 1]) ++op;
-  const QmvParams& q = P.ops[op].q;
-  k.op = op;
-  k.chunk = t - base[op];
-  k.s = chunk_start(q, k.chunk);
-  k.s_end = chunk_start(q, k.chunk + 1);
-  k.valid = true;
-}
-
 SPEC_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
@@ -1111,6 +1082,11 @@ SPEC_DEV void attn_op_unit(const FwdOp* ops, int* done, const int* gflags, int f
   }
 }
 
+// CTA c takes chunks c, c + G, ... of every op.  A stage of a later op waits
+// for groups that other CTAs of the launch produce, so a multi-op launch needs
+// every CTA resident at once: it is launched cooperative (FwdParams::
+// cooperative), which the hardware guarantees or refuses.
+//
 // Persistent, warp-specialized multi-op GEMV (see FwdOp).  Warp 4 lane 0 is
 // the producer: it keeps a weight cursor up to D stages ahead of the
 // consumers (never blocked by op dependencies) and an operand cursor that
@@ -1151,13 +1127,6 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, c = blockIdx.x;
 
-  // Item bookkeeping (see ItemCur): the first item number of each GEMV op
-  // (s_base[n_gemv] = the launch's item count), this CTA's claimed items in
-  // order, and the item the consumers run (broadcast by consumer thread 0).
-  __shared__ int s_base[kMaxLaunchOps + 1];
-  __shared__ int s_items[kItemQueue];
-  __shared__ int s_cur[2];
-  __shared__ int s_n_gemv;
   if (threadIdx.x == 0) {
     for (int s = 0; s < D; ++s) {
       mbar_init(&full[s], 1);
@@ -1166,76 +1135,12 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
   }
   fence_mbar_init();
   __syncthreads();
-  // From the shared copy of the descriptors (complete after the barrier; a
-  // walk over the global ones would chain one memory round trip per op).
-  if (threadIdx.x == 0) {
-    int n = 0, b = 0;
-    const int nops = P.n_ops < kMaxLaunchOps ? P.n_ops : kMaxLaunchOps;
-    while (n < nops && s_ops[n].kind == OPK_GEMV) {
-      s_base[n] = b;
-      b += s_ops[n].q.chunks;
-      ++n;
-    }
-    s_base[n] = b;
-    s_n_gemv = n;
-  }
-  __syncthreads();
-  const int n_gemv = s_n_gemv;
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
       // Weights are read once per forward: evict them from L2 first.
       const uint64_t wpol = l2_policy_evict_first();
-      const int total = s_base[n_gemv];
-      // Claiming: with P.claim the next claim's atomicAdd is issued as soon
-      // as the previous one is used, so its round trip overlaps the copies
-      // issued meanwhile.  Without it: chunks c, c + G, ... of each op.
-      int pending = (P.claim && total > 0) ? atomicAdd(P.claim, 1) : 0;
-      int st_op = 0, st_k = 0;
-      auto next_ticket = [&]() -> int {
-        if (P.claim) {
-          const int t = pending;
-          if (t >= total) return kItemEnd;
-          pending = atomicAdd(P.claim, 1);
-          return t;
-        }
-        while (st_op < n_gemv) {
-          const int i = c + st_k * G;
-          if (i < P.ops[st_op].q.chunks) {
-            ++st_k;
-            return s_base[st_op] + i;
-          }
-          ++st_op;
-          st_k = 0;
-        }
-        return kItemEnd;
-      };
-      int n_pushed = 0;
-      bool ended = false;
-      // Item j of this CTA's sequence, claimed when a cursor first reaches it.
-      auto item_at = [&](int j) -> int {
-        while (n_pushed <= j) {
-          const int t = ended ? kItemEnd : next_ticket();
-          ended = ended || t == kItemEnd;
-          s_items[n_pushed % kItemQueue] = t;
-          ++n_pushed;
-        }
-        return s_items[j % kItemQueue];
-      };
-      auto cur_load = [&](ItemCur& k) {
-        const int t = item_at(k.j);
-        if (t == kItemEnd) {
-          k.valid = false;
-          return;
-        }
-        item_decode(P, s_base, n_gemv, t, k);
-      };
-      auto cur_next = [&](ItemCur& k) {
-        if (++k.s < k.s_end) return;
-        ++k.j;
-        cur_load(k);
-      };
-      auto issue_w = [&](const ItemCur& it, int pos) {
+      auto issue_w = [&](const SeqIt& it, int pos) {
         const QmvParams& q = P.ops[it.op].q;
         const StageLoc L = locate(q, it.s);
         const WSeg& sg = q.seg[L.seg];
@@ -1248,7 +1153,7 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
         tma_bulk_g2s_hint(dst, sg.w + ((size_t)L.lgrp * sg.k_tiles + L.kt) * kGemvWarps * pair, kGemvWarps * pair,
                           &full[st], wpol);
       };
-      auto issue_x = [&](const ItemCur& it, int pos) {
+      auto issue_x = [&](const SeqIt& it, int pos) {
         const QmvParams& q = P.ops[it.op].q;
         const StageLoc L = locate(q, it.s);
         const int fmt = q.seg[L.seg].fmt;
@@ -1265,29 +1170,26 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
       // into L2 while the ring is still `l2_ahead` stages behind, so HBM keeps
       // streaming while ops wait on their inputs (and before pdl_wait, while
       // the previous kernel still runs).
-      auto issue_pf = [&](const ItemCur& it) {
+      auto issue_pf = [&](const SeqIt& it) {
         const QmvParams& q = P.ops[it.op].q;
         const StageLoc L = locate(q, it.s);
         const WSeg& sg = q.seg[L.seg];
         const int pair = fmt_pair_bytes(sg.fmt);
         tma_prefetch_l2(sg.w + ((size_t)L.lgrp * sg.k_tiles + L.kt) * kGemvWarps * pair, kGemvWarps * pair);
       };
-      ItemCur wi, xi, pi;
-      cur_load(wi);
+      SeqIt wi, xi, pi;
+      seq_begin(P, c, G, wi, true);
       xi = wi;
       pi = wi;
       int wpos = 0, xpos = 0, ppos = 0;
-      // The prefetch cursor leads the weight cursor by D + ahead stages; the
-      // item queue must span that lead plus the consumers' lag of D stages.
-      const int ahead_cap = kItemQueue - 2 * D - 2;
-      const int ahead = P.l2_ahead < ahead_cap ? P.l2_ahead : ahead_cap;
+      const int ahead = P.l2_ahead;
       for (; pi.valid && ppos < D + ahead; ++ppos) {
         if (ppos >= D) issue_pf(pi);
-        cur_next(pi);
+        seq_next(P, c, G, pi);
       }
       for (; wi.valid && wpos < D; ++wpos) {  // weights only depend on nothing
         issue_w(wi, wpos);
-        cur_next(wi);
+        seq_next(P, c, G, wi);
       }
       pdl_wait();  // operands and counters come from the previous kernel
       int ready_op = -1;
@@ -1296,7 +1198,7 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
       // activations per group after the SiLU epilogue) must carry this
       // forward's epoch.  The dependency's `done` count is read alongside;
       // once it is full, the rest of the op needs no more checks.
-      auto stage_ready = [&](const ItemCur& it) -> bool {
+      auto stage_ready = [&](const SeqIt& it) -> bool {
         const int dep = P.ops[it.op].dep;
         if (dep < 0) return true;
         const QmvParams& d = P.ops[dep].q;
@@ -1318,45 +1220,28 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
         if (ok) fence_acq_rel_gpu();
         return ok;
       };
-      // After the last item, ring position wpos carries no copy: one plain
-      // arrival completes its phase and the consumers read kItemEnd there.
-      bool end_sent = false;
       unsigned long long t_idle = 0;
-      while (xi.valid || !end_sent) {
+      while (xi.valid) {
         bool progressed = false;
-        if (xi.valid && xpos < wpos) {
-          bool rdy = xi.op <= ready_op;
-          if (!rdy && stage_ready(xi)) {
-            rdy = true;
-            // stage_ready acquired the producing groups' generic-proxy writes;
-            // one proxy fence orders them before this thread's bulk copies
-            // that read them.  Stages of an op whose inputs were acquired
-            // already, and inputs written by the previous kernel (ordered by
-            // griddepcontrol.wait), need no fence.
-            if (P.ops[xi.op].dep >= 0) fence_proxy_async_global();
-          }
-          if (rdy) {
+        if (xpos < wpos) {
+          if (xi.op <= ready_op || stage_ready(xi)) {
+            fence_proxy_async_global();
             issue_x(xi, xpos);
-            cur_next(xi);
+            seq_next(P, c, G, xi);
             ++xpos;
             progressed = true;
           }
         }
-        if (!end_sent && (wpos < D || mbar_test_wait(&empty[wpos % D], (uint32_t)(((wpos / D) - 1) & 1)))) {
-          if (wi.valid) {
-            issue_w(wi, wpos);
-            cur_next(wi);
-            ++wpos;
-            if (pi.valid && ppos < wpos + D + ahead) {
-              issue_pf(pi);
-              cur_next(pi);
-              ++ppos;
-            }
-          } else {
-            mbar_arrive(&full[wpos % D]);
-            end_sent = true;
-          }
+        if (wi.valid && mbar_test_wait(&empty[wpos % D], (uint32_t)(((wpos / D) - 1) & 1))) {
+          issue_w(wi, wpos);
+          seq_next(P, c, G, wi);
+          ++wpos;
           progressed = true;
+          if (pi.valid && ppos < wpos + D + ahead) {
+            issue_pf(pi);
+            seq_next(P, c, G, pi);
+            ++ppos;
+          }
         }
         if (progressed) {
           t_idle = 0;
@@ -1364,22 +1249,17 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
           const unsigned long long now = global_timer_ns();
           if (t_idle == 0) t_idle = now;
           else if (now - t_idle > kMbarTimeoutNs) {
-            const int dep = xi.valid ? P.ops[xi.op].dep : -1;
-            wait_gave_up(P.err, WAIT_PRODUCER_IDLE, xi.valid ? xi.op : 255, xpos | (wpos << 16),
-                         dep >= 0 ? ld_acquire(P.done + dep) : -1);
+            const int dep = P.ops[xi.op].dep;
+            wait_gave_up(P.err, WAIT_PRODUCER_IDLE, xi.op, xpos | (wpos << 16), dep >= 0 ? ld_acquire(P.done + dep) : -1);
             break;
           }
         }
       }
-      // Every issued copy must land before this CTA can retire: positions
-      // [wpos - D, wpos).  An end mark sent at position wpos >= D reused the
-      // slot of position wpos - D (sent only after the consumers released
-      // that stage, so its copy has landed) and moved that barrier one phase
-      // on: that position is not waited for again.
-      const int first = wpos >= D ? wpos - D + (end_sent ? 1 : 0) : 0;
+      // Every issued copy must land before this CTA can retire.
+      const int first = wpos > D ? wpos - D : 0;
       for (int pos = first; pos < wpos; ++pos)
         if (!mbar_wait_bounded(&full[pos % D], (uint32_t)((pos / D) & 1), nullptr))
-          wait_gave_up(P.err, WAIT_PRODUCER_DRAIN, 255, pos, wpos);
+          wait_gave_up(P.err, WAIT_PRODUCER_DRAIN, xi.valid ? xi.op : 255, pos, wpos);
     }
     return;
   }
@@ -1390,27 +1270,13 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
   float acc[2][NT][4];
   bool ok = true;
   int pos = 0;
-  for (int j = 0;; ++j) {
-    // Item j starts at ring position pos: consumer thread 0 waits for that
-    // stage (or the end mark), reads the item and hands it to all consumers,
-    // so every consumer warp takes the same path through the barriers below.
-    if (threadIdx.x == 0) {
-      int t = kItemEnd;
-      if (ok) {
-        ok = mbar_wait_bounded(&full[pos % D], (uint32_t)((pos / D) & 1), nullptr);
-        if (ok) t = s_items[j % kItemQueue];
-        else wait_gave_up(P.err, WAIT_CONSUMER_FULL, 255, j, pos);
-      }
-      s_cur[j & 1] = t;
-    }
-    consumer_sync();
-    const int t = s_cur[j & 1];
-    if (t == kItemEnd) break;
-    ItemCur it;
-    item_decode(P, s_base, n_gemv, t, it);
+  SeqIt it;
+  seq_begin(P, c, G, it, false);
+  while (it.valid) {
     const int op = it.op;
+    if (P.ops[op].kind != OPK_GEMV) break;  // the attention ops, below
     const QmvParams& q = P.ops[op].q;
-    const int own = it.chunk;
+    const int own = c + it.k * G;
 #pragma unroll
     for (int rt = 0; rt < 2; ++rt)
 #pragma unroll
@@ -1452,12 +1318,9 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
             for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
       }
     }
+    it.s = it.s_end - 1;
+    seq_next(P, c, G, it);
   }
-  // The launch's attention ops (fused attention only) keep the static
-  // assignment: CTA c runs units c, c + G, ... of each.
-  SeqIt it;
-  it.op = n_gemv;
-  seq_settle(P, c, G, it);
   // Attention ops follow every GEMV op of the launch: one chunk = one unit.
   // Every GEMV piece of this CTA is done: the next forward kernel may be
   // scheduled (its CTAs take the slots of CTAs that exit, stream their first
@@ -1687,7 +1550,7 @@ struct FwdInst {
     attr[0].val.programmaticStreamSerializationAllowed = pdl ? 1 : 0;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (p.cooperative) {
+    if (p.cooperative) {  // every CTA resident at once, or the launch fails
       attr[1].id = cudaLaunchAttributeCooperative;
       attr[1].val.cooperative = 1;
       cfg.numAttrs = 2;

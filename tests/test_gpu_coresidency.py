@@ -4,9 +4,7 @@ Inside one forward-kernel launch, chunks of a later op wait for the groups
 that other CTAs of the same launch produce, so no such CTA may wait for a CTA
 that has not started.  Multi-op launches therefore run cooperative (the
 hardware starts the grid only when every CTA fits, and refuses a grid that
-never could), or, with SPEC_B200_DYNAMIC_CLAIM, take their chunks from a
-counter in op order (a chunk is only waited on after a running CTA claimed
-it).
+never could).
 
 Here a kernel of the test's own (compiled with NVRTC; it spins on
 %globaltimer for 3 s, so it always ends) takes the shared memory of 74 of the
@@ -15,11 +13,10 @@ Llama-3-8B layer shapes (444-chunk ops) is issued on the decoder's stream
 meanwhile.  Every device wait of the forward gives up after 2 s, so a forward
 whose resident CTAs waited on CTAs that cannot start would fail with
 SPEC_ERR_TIMEOUT.  It must instead return logits bit-identical to an
-undisturbed run, for both assignment modes.
+undisturbed run.
 """
 
 import ctypes
-import os
 import time
 
 import numpy as np
@@ -69,16 +66,10 @@ def _occupier():
     return cu, fn
 
 
-@pytest.mark.parametrize("mode", ["cooperative", "dynamic_claim"])
-def test_verify_while_half_the_sms_are_held(pkg, mode):
+def test_verify_while_half_the_sms_are_held(pkg):
     import torch
     torch.cuda.init()
-    if mode == "dynamic_claim":
-        os.environ["SPEC_B200_DYNAMIC_CLAIM"] = "1"
-    try:
-        dec = pkg.B200Decoder.synthetic(**LLAMA8B_2L, quant_mix="Q4_K_M", seed=5, max_ctx=512)
-    finally:
-        os.environ.pop("SPEC_B200_DYNAMIC_CLAIM", None)
+    dec = pkg.B200Decoder.synthetic(**LLAMA8B_2L, quant_mix="Q4_K_M", seed=5, max_ctx=512)
     rng = np.random.default_rng(4)
     prompt = rng.integers(0, LLAMA8B_2L["vocab"], size=64).tolist()
     drafts = rng.integers(0, LLAMA8B_2L["vocab"], size=4).tolist()
@@ -103,5 +94,5 @@ def test_verify_while_half_the_sms_are_held(pkg, mode):
     elapsed = time.perf_counter() - t0
     side.synchronize()
     assert int(done.item()) == blocks, "the occupying kernel did not run to its end"
-    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"logits differ ({mode}, {elapsed:.2f} s)"
+    assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), f"logits differ ({elapsed:.2f} s)"
     dec.close()
