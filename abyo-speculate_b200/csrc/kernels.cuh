@@ -218,6 +218,9 @@ struct FwdParams {
   // Consumers that reach the launch's attention ops first signal the next
   // kernel's programmatic launch (griddepcontrol.launch_dependents).
   int trigger_after_gemv = 0;
+  // griddepcontrol.launch_dependents at kernel entry (cooperative forward
+  // launches only; see fwd_kernel).
+  int trigger_at_start = 0;
 };
 
 // The instantiation is picked by (format set, nt_for_rows(M)); all ops of

@@ -1102,12 +1102,16 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
   __shared__ __align__(8) uint64_t full[D];
   __shared__ __align__(8) uint64_t empty[D];
   __shared__ __align__(16) FwdOp s_ops[kMaxLaunchOps];
-  // No griddepcontrol.launch_dependents here: the kernels after this one
-  // (attention, then the next forward kernel) are only scheduled as its CTAs
-  // exit.  Letting them launch while these persistent CTAs still wait on one
-  // another lost a split-K group's completion on B200 (a bounded wait fired);
-  // the next forward kernel still overlaps attention through the attention
-  // kernels' own early trigger.
+  // Dependent launch.  Without a cooperative launch the kernels after this
+  // one (attention, then the next forward kernel) are only scheduled as its
+  // CTAs exit: letting them launch early let CTAs of the next forward kernel
+  // become resident before their siblings and wait on them, and a split-K
+  // group's completion was lost on B200 (a bounded wait fired).  When the
+  // forward kernels are cooperative that cannot happen (the next one starts
+  // only when all of its CTAs fit), so they trigger at entry: the attention
+  // CTAs take the slots of exiting CTAs at once and stage the older keys
+  // while this launch's tail finishes.
+  if (Pg.trigger_at_start) pdl_launch_dependents();
   // Op descriptors live in shared memory for the whole launch (the producer
   // walks them per tile).  They were uploaded long before this launch.
   {
