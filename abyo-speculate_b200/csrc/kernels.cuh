@@ -67,6 +67,7 @@ constexpr float kXSum16Seed = -1056.f;
 constexpr float kXSum32Seed = -1024.f;
 constexpr int kTpSlot = kMaxRows * 128;  // words per (source rank, group) receive slot
 constexpr int kTpMaxLayers = 256;        // tp_tag = 2 x layer + set stays below 512
+constexpr int kTpMaxRanks = 8;           // tensor-parallel ranks per model
 __host__ __device__ inline unsigned tp_flag_of(unsigned epoch, int tag) { return (epoch << 9) | (unsigned)tag; }
 
 // Number of 8-row fragment columns (n-tiles) the kernels use for M rows: the
@@ -126,6 +127,14 @@ struct QmvParams {
   const unsigned* tp_epoch = nullptr;                // forward counter, identical on every rank
   unsigned long long* const* tp_recv = nullptr;      // [tp_size] device: rank r's receive set
   const unsigned long long* tp_recv_local = nullptr; // this rank's set [src rank][group][kTpSlot]
+  // Vocabulary-parallel LM head (EPI_STORE under tensor parallelism): each
+  // rank computes its own rows of the logits and stores them into every
+  // rank's logits buffer (out_peers[r] = rank r's buffer at this rank's first
+  // row), then adds each finished group to every rank's arrival counter
+  // (out_counters[r]); tp_logits_wait() holds a rank's stream until all
+  // ranks' groups of this forward have arrived.
+  float* const* out_peers = nullptr;                   // [tp_size] device
+  unsigned long long* const* out_counters = nullptr;   // [tp_size] device
   int ss_groups = 0;
   float ss_inv_dim = 0.f;
   float eps = 0.f;
@@ -234,6 +243,11 @@ int fwd_fmt_set_for(int fmt_bits);
 // (format set, M rows, head dim, keys per split); below kAttnKeyBlock,
 // attention does not fit the instantiation's ring and runs as its own kernels.
 int fwd_attn_keys_per_pass(int fmt_set, int M, int hd, int chunk);
+
+// Vocabulary-parallel LM head: holds the stream until *counter >= *target
+// (every rank's logits rows of this forward have arrived); bounded wait.
+cudaError_t launch_tp_logits_wait(const unsigned long long* counter, const unsigned long long* target, unsigned* err,
+                                  cudaStream_t s);
 
 // Repack raw GGUF blocks (device, row-major [N][K/be][bb]) into pair tiles.
 cudaError_t launch_repack(const uint8_t* raw, int fmt, int N, int K, uint8_t* tiles, cudaStream_t s);

@@ -200,6 +200,18 @@ struct spec_model {
   uint8_t* tp_buf = nullptr;
   size_t tp_set_bytes = 0;
   void** tp_ptrs_dev = nullptr;     // [set][rank] device pointers to every rank's sets
+  // Vocabulary-parallel LM head: this rank owns head rows [lm_row0, lm_row0 +
+  // lm.N) of lm_groups_total 128-row groups.  Its logits buffer and arrival
+  // counter live in tp_buf (so peers can write them); tp_out_peers_dev[r] is
+  // rank r's logits buffer offset to this rank's first row, and
+  // tp_out_counters_dev[r] rank r's counter.
+  int lm_row0 = 0;
+  int lm_groups_total = 0;
+  size_t tp_logits_off = 0, tp_counter_off = 0;
+  unsigned long long* tp_counter = nullptr;
+  float** tp_out_peers_dev = nullptr;
+  unsigned long long** tp_out_counters_dev = nullptr;
+  unsigned long long logits_forwards = 0;  // forwards with logits (the same count on every rank)
   unsigned epoch = 0;               // forwards run (the same count on every tensor-parallel rank)
   std::vector<void*> tp_peer_bases; // opened IPC mappings (closed at free)
   bool tp_connected = false;
@@ -451,11 +463,21 @@ int alloc_runtime(spec_model* m) {
   ALLOC(m->gemv_part, 2 * part * 4);
   ALLOC(m->counters, (size_t)2 * max_groups * 4);
   if (m->tp_size > 1) {
-    m->tp_set_bytes = (size_t)m->tp_size * groups_h * kTpSlot * 8;
-    ALLOC(m->tp_buf, 2 * m->tp_set_bytes);
+    // [o set][down set][logits kMaxRows x V][arrival counter]: one exported
+    // allocation, the same layout on every rank.
+    auto up256 = [](size_t v) { return (v + 255) / 256 * 256; };
+    m->tp_set_bytes = up256((size_t)m->tp_size * groups_h * kTpSlot * 8);
+    m->tp_logits_off = 2 * m->tp_set_bytes;
+    m->tp_counter_off = m->tp_logits_off + up256((size_t)kMaxRows * V * 4);
+    ALLOC(m->tp_buf, m->tp_counter_off + 256);
     ALLOC(m->tp_ptrs_dev, (size_t)2 * m->tp_size * sizeof(void*));
+    ALLOC(m->tp_out_peers_dev, (size_t)m->tp_size * sizeof(float*));
+    ALLOC(m->tp_out_counters_dev, (size_t)m->tp_size * sizeof(unsigned long long*));
+    m->logits = reinterpret_cast<float*>(m->tp_buf + m->tp_logits_off);
+    m->tp_counter = reinterpret_cast<unsigned long long*>(m->tp_buf + m->tp_counter_off);
+  } else {
+    ALLOC(m->logits, (size_t)kMaxRows * V * 4);
   }
-  ALLOC(m->logits, (size_t)kMaxRows * V * 4);
   ALLOC(m->last_row, (size_t)V * 4);
   ALLOC(m->hidden_out, (size_t)kMaxRows * H * 4);
   ALLOC(m->err_dev, 16);
@@ -745,8 +767,14 @@ FwdOp op_lm(spec_model* m, int M, float* out) {
   p.ss_inv_dim = 1.f / (float)c.hidden;
   p.eps = c.eps;
   p.epi = EPI_STORE;
-  p.out = out;
+  p.out = out + m->lm_row0;  // this rank's rows of the head (all rows without tensor parallelism)
   p.ld_out = c.vocab;
+  if (m->tp_size > 1 && out == m->logits) {
+    p.tp_size = m->tp_size;
+    p.tp_rank = m->tp_rank;
+    p.out_peers = m->tp_out_peers_dev;
+    p.out_counters = m->tp_out_counters_dev;
+  }
   return o;
 }
 
@@ -972,6 +1000,12 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
     const bool has_attn = sc->fused_attn && l + 1 < c.n_layers;
     if ((e = prof_mark(pr, s, K_FWD, sc->launch_bytes[l + 1] + (has_attn ? attn_bytes : 0))) != cudaSuccess) return e;
   }
+  if ((flags & F_LOGITS) && m->tp_size > 1) {
+    // Vocabulary-parallel head: every rank's rows must be in this rank's
+    // logits before anything reads them.
+    e = launch_tp_logits_wait(m->tp_counter, &m->step_dev->logits_target, m->err_dev, s);
+    if (e != cudaSuccess) return e;
+  }
   if (flags & F_LOGITS) {
     e = cudaMemcpyAsync(m->last_row, m->logits + (size_t)(M - 1) * c.vocab, (size_t)c.vocab * 4,
                         cudaMemcpyDeviceToDevice, s);
@@ -986,10 +1020,19 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
 
 // Runs one forward of M rows described by m->step_host.  Graph-replayed per
 // (M, flags) after a first eager run.
+// Numbers the forward about to be enqueued: its completion-flag / exchange
+// epoch and, with logits under tensor parallelism, the arrival count that
+// says every rank's LM-head rows are in.
+void begin_step(spec_model* m, int flags) {
+  m->step_host->epoch = ++m->epoch;
+  if (flags & F_LOGITS) ++m->logits_forwards;
+  m->step_host->logits_target = m->logits_forwards * (unsigned long long)m->lm_groups_total;
+}
+
 int run_forward(spec_model* m, int M, int flags, const std::vector<int>* collect = nullptr) {
   if (m->tp_size > 1 && !m->tp_connected)
     return m->fail(SPEC_ERR_INVALID, "tensor-parallel handle used before spec_tp_connect");
-  m->step_host->epoch = ++m->epoch;
+  begin_step(m, flags);
   cudaError_t e = cudaSuccess;
   const int key = M | (flags << 8);
   const bool graphable = m->use_graphs && collect == nullptr;
@@ -1228,10 +1271,27 @@ int check_tp_shape(spec_model* m, int nq, int nkv, int hd, int F, int n_layers) 
   const int N = m->tp_size;
   if (N == 1) return SPEC_OK;
   if (n_layers > kTpMaxLayers) return m->fail(SPEC_ERR_UNSUPPORTED, "too many layers for tensor parallelism");
+  if (N > kTpMaxRanks) return m->fail(SPEC_ERR_UNSUPPORTED, "more than 8 tensor-parallel ranks");
   if (nq % N || nkv % N || F % N || (F / N) % kGroupRows || ((nq / N) * hd) % 256 || (F / N) % 256 ||
       ((nkv / N) * hd) % kGroupRows)
     return m->fail(SPEC_ERR_UNSUPPORTED, "model does not split into tp_size tensor-parallel shards");
   return SPEC_OK;
+}
+
+// Vocabulary-parallel LM head: rank r keeps 128-row groups
+// [r G / T, (r + 1) G / T) of the head's G groups (V rows of K columns in
+// GGUF blocks); the other ranks compute the rest and every rank receives all
+// rows (EPI_STORE with out_peers).  Records the rank's first row.
+void shard_lm(spec_model* m, Part& p, int V, int K) {
+  m->lm_groups_total = V / kGroupRows;
+  m->lm_row0 = 0;
+  if (m->tp_size <= 1) return;
+  const int G = m->lm_groups_total, T = m->tp_size, r = m->tp_rank;
+  const int g0 = (int)((long long)r * G / T), g1 = (int)((long long)(r + 1) * G / T);
+  const size_t row_bytes = (size_t)(K / fmt_block_elems(p.fmt)) * fmt_block_bytes(p.fmt);
+  p.src += (size_t)g0 * kGroupRows * row_bytes;
+  p.rows = (g1 - g0) * kGroupRows;
+  m->lm_row0 = g0 * kGroupRows;
 }
 
 // The tensor-parallel shard of one layer for this rank: q/k/v rows of the
@@ -1446,6 +1506,7 @@ int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) 
   if (outp.rows < c.vocab) return m->fail(SPEC_ERR_IO, "output.weight has fewer rows than the vocabulary");
   if (c.vocab % kGroupRows) return m->fail(SPEC_ERR_UNSUPPORTED, "vocabulary not a multiple of 128");
   outp.rows = c.vocab;
+  shard_lm(m, outp, c.vocab, H);
   rc = build_mat(m, {outp}, H, false, m->lm);
   if (rc != SPEC_OK) return rc;
   set_local_dims(m);
@@ -1582,7 +1643,10 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
       if (e != cudaSuccess) rc = m->fail(SPEC_ERR_OOM, cuda_msg(e, "embedding"));
     }
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(d->quant_mix, true, false, -1, H), c.vocab, H, tseed(), op);
-    if (rc == SPEC_OK) rc = build_mat(m, {op}, H, false, m->lm);
+    if (rc == SPEC_OK) {
+      shard_lm(m, op, c.vocab, H);
+      rc = build_mat(m, {op}, H, false, m->lm);
+    }
     cudaStreamSynchronize(m->stream);
     for (void* t : temps) cudaFree(t);
     if (rc != SPEC_OK) return rc;
@@ -1724,7 +1788,15 @@ int spec_tp_connect(spec_model* m, const void* handles, int n) {
   std::vector<void*> ptrs((size_t)2 * n);
   for (int set = 0; set < 2; ++set)
     for (int r = 0; r < n; ++r) ptrs[(size_t)set * n + r] = base[r] + set * m->tp_set_bytes;
-  const cudaError_t e = m->upload(m->tp_ptrs_dev, ptrs.data(), ptrs.size() * sizeof(void*));
+  std::vector<float*> outs(n);
+  std::vector<unsigned long long*> ctrs(n);
+  for (int r = 0; r < n; ++r) {
+    outs[r] = reinterpret_cast<float*>(base[r] + m->tp_logits_off) + m->lm_row0;
+    ctrs[r] = reinterpret_cast<unsigned long long*>(base[r] + m->tp_counter_off);
+  }
+  cudaError_t e = m->upload(m->tp_ptrs_dev, ptrs.data(), ptrs.size() * sizeof(void*));
+  if (e == cudaSuccess) e = m->upload(m->tp_out_peers_dev, outs.data(), outs.size() * sizeof(float*));
+  if (e == cudaSuccess) e = m->upload(m->tp_out_counters_dev, ctrs.data(), ctrs.size() * sizeof(void*));
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "peer pointer table"));
   m->tp_connected = true;
   return SPEC_OK;
@@ -2011,6 +2083,7 @@ int spec_observe_returning_last_hidden(spec_model* m, const uint32_t* ids, int n
 
 int spec_apply_lm_head(spec_model* m, const float* hidden, int rows, float* out) {
   if (!m || !hidden || !out || rows < 0) return SPEC_ERR_INVALID;
+  if (m->tp_size > 1) return m->fail(SPEC_ERR_UNSUPPORTED, "apply_lm_head on a tensor-parallel handle (vocabulary-parallel head)");
   DeviceGuard dg_(m->device);
   const int H = m->cfg.hidden, V = m->cfg.vocab;
   for (int r0 = 0; r0 < rows; r0 += kMaxRows) {
@@ -2038,6 +2111,8 @@ int spec_apply_lm_head(spec_model* m, const float* hidden, int rows, float* out)
 
 int spec_apply_lm_head_topk(spec_model* m, const float* hidden, int rows, int k, int32_t* ids_out, float* vals_out) {
   if (!m || !hidden || !ids_out || rows < 0) return SPEC_ERR_INVALID;
+  if (m->tp_size > 1)
+    return m->fail(SPEC_ERR_UNSUPPORTED, "apply_lm_head_topk on a tensor-parallel handle (vocabulary-parallel head)");
   if (k < 1 || k > kMaxTopK || k > m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "top-k size out of range");
   DeviceGuard dg_(m->device);
   const int H = m->cfg.hidden, V = m->cfg.vocab;
@@ -3212,6 +3287,9 @@ int spec_profile_forward(spec_model* m, const uint32_t* drafts, int k, float* ms
   combined[0] = m->history.back();
   if (k) memcpy(combined.data() + 1, drafts, (size_t)k * 4);
   fill_step_causal(m, combined.data(), k + 1, target);
+  if (m->tp_size > 1 && !m->tp_connected)
+    return -m->fail(SPEC_ERR_INVALID, "tensor-parallel handle used before spec_tp_connect");
+  begin_step(m, F_LOGITS);
   ProfRec pr;
   cudaError_t e = enqueue_forward(m, k + 1, F_LOGITS, nullptr, &pr);
   if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);

@@ -50,6 +50,10 @@ struct StepDev {
   int step[2];  // P (keys before the new rows), P + M
   unsigned epoch;  // forward counter: value of this forward's completion flags and exchanged words
   int pad;
+  // Tensor parallelism: value every rank's logits arrival counter reaches
+  // once this forward's LM-head rows have all arrived (forwards with logits
+  // so far x the head's 128-row groups).
+  unsigned long long logits_target;
 };
 
 // Source of one weight part while building a fused matrix.

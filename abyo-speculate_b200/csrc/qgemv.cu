@@ -474,6 +474,10 @@ SPEC_DEV void cp_async4(void* smem_dst, const void* gsrc) {
 }
 SPEC_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 SPEC_DEV void fence_acq_rel_gpu() { asm volatile("fence.acq_rel.gpu;" ::: "memory"); }
+SPEC_DEV void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+SPEC_DEV void red_add_release_sys_u64(unsigned long long* ptr, unsigned long long v) {
+  asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+}
 SPEC_DEV void st_relaxed_gpu(int* ptr, int v) {
   asm volatile("st.relaxed.gpu.global.b32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
@@ -684,11 +688,24 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
   consumer_sync();
 
   if (p.epi == EPI_STORE) {
-    for (int idx = tid; idx < M * kGroupRows; idx += kGemvWarps * 32) {
-      const int m = idx / kGroupRows, j = idx % kGroupRows, n = n0 + j;
-      float v = ys[m * kGroupRows + j] * s_rinv[m];
-      if (p.bias) v += p.bias[n];
-      p.out[(size_t)m * p.ld_out + n] = v;
+    if (p.out_peers) {
+      // Vocabulary-parallel head: the rows go to every rank's logits buffer.
+      float* dst[kTpMaxRanks];
+      const int T = p.tp_size < kTpMaxRanks ? p.tp_size : kTpMaxRanks;
+      for (int r = 0; r < T; ++r) dst[r] = p.out_peers[r];
+      for (int idx = tid; idx < M * kGroupRows; idx += kGemvWarps * 32) {
+        const int m = idx / kGroupRows, j = idx % kGroupRows, n = n0 + j;
+        float v = ys[m * kGroupRows + j] * s_rinv[m];
+        if (p.bias) v += p.bias[n];
+        for (int r = 0; r < T; ++r) dst[r][(size_t)m * p.ld_out + n] = v;
+      }
+    } else {
+      for (int idx = tid; idx < M * kGroupRows; idx += kGemvWarps * 32) {
+        const int m = idx / kGroupRows, j = idx % kGroupRows, n = n0 + j;
+        float v = ys[m * kGroupRows + j] * s_rinv[m];
+        if (p.bias) v += p.bias[n];
+        p.out[(size_t)m * p.ld_out + n] = v;
+      }
     }
   } else if (p.epi == EPI_QKV) {
     const int hd = p.head_dim, nq = p.n_q_heads, nkv = p.n_kv_heads;
@@ -804,6 +821,13 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
     }
   }
   consumer_sync();  // ys aliases the scale scratch of the next unit
+  if (p.out_counters && tid == 0) {
+    // Every thread's peer stores are ordered before this by the barrier; the
+    // system-scope fence makes them visible to the other GPUs before the
+    // arrivals they wait on.
+    fence_acq_rel_sys();
+    for (int r = 0; r < p.tp_size; ++r) red_add_release_sys_u64(p.out_counters[r], 1ull);
+  }
   if (done && tid == 0) {
     if (gflag) {  // one release fence covers the group flag and the op count
       fence_acq_rel_gpu();
@@ -1625,6 +1649,33 @@ cudaError_t launch_fwd(const FwdParams& p, int fmt_set, int M, cudaStream_t s, b
   if (fmt_set == kSetK5) return launch_set<kSetK5>(p, M, s, pdl);
   if (fmt_set == kSetBF) return launch_set<kSetBF>(p, M, s, pdl);
   return cudaErrorNotSupported;
+}
+
+namespace {
+// One thread: waits until this rank's logits arrival counter reaches the
+// forward's target (every rank's LM-head groups stored), bounded by the
+// usual 2 s; on timeout it records WAIT_TP_PEERS and returns.
+__global__ void tp_logits_wait_kernel(const unsigned long long* counter, const unsigned long long* target,
+                                      unsigned* err) {
+  if (threadIdx.x != 0) return;
+  const unsigned long long want = *target;
+  const unsigned long long t0 = global_timer_ns();
+  for (unsigned i = 0;; ++i) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(counter) : "memory");
+    if (v >= want) return;
+    if ((i & 255u) == 255u && global_timer_ns() - t0 > kMbarTimeoutNs) {
+      wait_gave_up(err, WAIT_TP_PEERS, 255, 0, (int)(v & 0x7fffffff));
+      return;
+    }
+  }
+}
+}  // namespace
+
+cudaError_t launch_tp_logits_wait(const unsigned long long* counter, const unsigned long long* target, unsigned* err,
+                                  cudaStream_t s) {
+  tp_logits_wait_kernel<<<1, 32, 0, s>>>(counter, target, err);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_repack(const uint8_t* raw, int fmt, int N, int K, uint8_t* tiles, cudaStream_t s) {
