@@ -133,8 +133,11 @@ struct QmvParams {
   // row), then adds each finished group to every rank's arrival counter
   // (out_counters[r]); tp_logits_wait() holds a rank's stream until all
   // ranks' groups of this forward have arrived.
-  float* const* out_peers = nullptr;                   // [tp_size] device
-  unsigned long long* const* out_counters = nullptr;   // [tp_size] device
+  // Set only on the head op, whose tp_size stays 1 (tp_size > 1 selects the
+  // row-parallel exchange above).
+  int out_ranks = 0;                                   // ranks of out_peers / out_counters
+  float* const* out_peers = nullptr;                   // [out_ranks] device
+  unsigned long long* const* out_counters = nullptr;   // [out_ranks] device
   int ss_groups = 0;
   float ss_inv_dim = 0.f;
   float eps = 0.f;

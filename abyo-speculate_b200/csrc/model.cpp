@@ -770,8 +770,7 @@ FwdOp op_lm(spec_model* m, int M, float* out) {
   p.out = out + m->lm_row0;  // this rank's rows of the head (all rows without tensor parallelism)
   p.ld_out = c.vocab;
   if (m->tp_size > 1 && out == m->logits) {
-    p.tp_size = m->tp_size;
-    p.tp_rank = m->tp_rank;
+    p.out_ranks = m->tp_size;
     p.out_peers = m->tp_out_peers_dev;
     p.out_counters = m->tp_out_counters_dev;
   }

@@ -691,7 +691,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
     if (p.out_peers) {
       // Vocabulary-parallel head: the rows go to every rank's logits buffer.
       float* dst[kTpMaxRanks];
-      const int T = p.tp_size < kTpMaxRanks ? p.tp_size : kTpMaxRanks;
+      const int T = p.out_ranks < kTpMaxRanks ? p.out_ranks : kTpMaxRanks;
       for (int r = 0; r < T; ++r) dst[r] = p.out_peers[r];
       for (int idx = tid; idx < M * kGroupRows; idx += kGemvWarps * 32) {
         const int m = idx / kGroupRows, j = idx % kGroupRows, n = n0 + j;
@@ -826,7 +826,8 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
     // system-scope fence makes them visible to the other GPUs before the
     // arrivals they wait on.
     fence_acq_rel_sys();
-    for (int r = 0; r < p.tp_size; ++r) red_add_release_sys_u64(p.out_counters[r], 1ull);
+    const int T = p.out_ranks < kTpMaxRanks ? p.out_ranks : kTpMaxRanks;
+    for (int r = 0; r < T; ++r) red_add_release_sys_u64(p.out_counters[r], 1ull);
   }
   if (done && tid == 0) {
     if (gflag) {  // one release fence covers the group flag and the op count
