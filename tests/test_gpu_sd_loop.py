@@ -48,3 +48,51 @@ def test_self_draft_accepts_everything(pkg, accept, tiny_gguf):
     toks, acc = sd.vanilla_greedy_generate(target, draft, prompt, 30, 4)
     assert all(a == 4 for a in acc)
     assert toks == _greedy_plain(pkg, accept, path, prompt, len(toks))
+
+
+def test_sampled_stream_replays_with_stdrng(pkg, accept, tiny_gguf):
+    """Temperature-1.0 vanilla SD seeded like StdRng::seed_from_u64(7)
+    (engine.rs:320-326): the device rounds (spec_verify_rejection fed from the
+    restated ChaCha12 stream in the reference's draw order) produce the same
+    token stream and acceptance counts as a host replay of vanilla.rs:285-369
+    with the oracle's acceptance functions on the same decoders' logits rows
+    and the same stream."""
+    sd = importlib.import_module("abyo-speculate_b200.sd_loop")
+    rng_mod = importlib.import_module("abyo-speculate_b200.rng")
+    tpath, dpath = tiny_gguf("llama_q4km"), tiny_gguf("llama_hd128")
+    prompt = np.random.default_rng(43).integers(0, 1024, size=20).tolist()
+    T, k, n_new = 1.0, 4, 40
+    target = pkg.B200Decoder.from_gguf(tpath, max_ctx=512)
+    draft = pkg.B200Decoder.from_gguf(dpath, max_ctx=512)
+    toks, accs = sd.vanilla_sampled_generate(target, draft, prompt, n_new, k, T, seed=7)
+    assert len(toks) == n_new and sum(accs) > 0
+
+    # Host replay: the same calls and draws, acceptance by the oracle.
+    tr = pkg.B200Decoder.from_gguf(tpath, max_ctx=512)
+    dr = pkg.B200Decoder.from_gguf(dpath, max_ctx=512)
+    tr.observe(prompt)
+    dr.observe(prompt)
+    rng = rng_mod.StdRng(7)
+    out, racc = [], []
+    while len(out) < n_new:
+        kk = min(k, n_new - len(out))
+        pre_t, pre_d = tr.history_len(), dr.history_len()
+        drafts, dists = [], []
+        for _ in range(kk):
+            probs = accept.softmax_with_temperature(dr.next_logits(), T)
+            tok = accept.sample_from_distribution(rng.gen_f32(), probs)
+            drafts.append(tok)
+            dists.append(probs)
+            dr.observe([tok])
+        rows = tr.batched_logits(drafts)
+        commits, used = accept.vanilla_round(rows, drafts, dists, T, list(rng.peek_f32(kk + 1)), len(out), n_new)
+        rng.advance(used)
+        racc.append(len(commits) if (used == len(commits) and len(commits) <= kk) else len(commits) - 1)
+        a = min(len(commits), kk)
+        tr.rollback_to(pre_t + a)
+        tr.observe(commits[a:])
+        dr.rollback_to(pre_d + a)
+        dr.observe(commits[a:])
+        out.extend(commits)
+    assert toks == out
+    assert accs == racc
