@@ -93,7 +93,8 @@ class ModelDesc(ctypes.Structure):
     _fields_ = [("arch", ctypes.c_int), ("n_layers", ctypes.c_int), ("hidden", ctypes.c_int),
                 ("n_heads", ctypes.c_int), ("n_kv_heads", ctypes.c_int), ("ffn", ctypes.c_int),
                 ("vocab", ctypes.c_int), ("rope_theta", ctypes.c_float), ("eps", ctypes.c_float),
-                ("quant_mix", ctypes.c_int), ("rope_half", ctypes.c_int), ("reserved", ctypes.c_int * 6)]
+                ("quant_mix", ctypes.c_int), ("rope_half", ctypes.c_int), ("damp_from_layer", ctypes.c_int),
+                ("damp_e4", ctypes.c_int), ("reserved", ctypes.c_int * 4)]
 
 
 # (name, restype, argtypes) of every function declared in include/spec_b200.h

@@ -1538,13 +1538,14 @@ uint64_t mix64(uint64_t x) {
 }
 
 // Raw GGUF blocks for one seeded tensor, generated on the device.
-int synth_part(spec_model* m, std::vector<void*>& temps, int fmt, int rows, int K, uint64_t seed, Part& p) {
+int synth_part(spec_model* m, std::vector<void*>& temps, int fmt, int rows, int K, uint64_t seed, Part& p,
+               float sigma = 0.02f) {
   const size_t bytes = (size_t)rows * (K / fmt_block_elems(fmt)) * fmt_block_bytes(fmt);
   void* buf = nullptr;
   cudaError_t e = cudaMalloc(&buf, bytes);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_OOM, cuda_msg(e, "synthetic staging"));
   temps.push_back(buf);
-  e = launch_synth_quant(static_cast<uint8_t*>(buf), fmt, rows, K, seed, 0.02f, 0, m->stream);
+  e = launch_synth_quant(static_cast<uint8_t*>(buf), fmt, rows, K, seed, sigma, 0, m->stream);
   if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "synthetic weights"));
   p.src = static_cast<const uint8_t*>(buf);
   p.on_device = true;
@@ -1588,6 +1589,34 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
   const int H = c.hidden, F = c.ffn, hd = c.head_dim;
   uint64_t tid = 0;
   auto tseed = [&]() { return spec_synthetic_seed(seed, ++tid); };  // tensor numbering: spec_b200.h
+  // Output norm, embedding and head first, so a shallower model with the
+  // same seed shares them.
+  {
+    const int rc0 = synth_vec(m, &m->out_norm, H, tseed(), 1.f);
+    if (rc0 != SPEC_OK) return rc0;
+  }
+  {
+    std::vector<void*> temps;
+    Part ep, op;
+    m->embed_fmt = mix_type(d->quant_mix, false, false, -1, H);
+    int rc = synth_part(m, temps, m->embed_fmt, c.vocab, H, tseed(), ep);
+    if (rc == SPEC_OK) {
+      const size_t bytes = (size_t)c.vocab * (H / fmt_block_elems(m->embed_fmt)) * fmt_block_bytes(m->embed_fmt);
+      cudaError_t e = m->dalloc(&m->embed_raw, bytes);
+      if (e == cudaSuccess) e = cudaMemcpyAsync(m->embed_raw, ep.src, bytes, cudaMemcpyDeviceToDevice, m->stream);
+      if (e != cudaSuccess) rc = m->fail(SPEC_ERR_OOM, cuda_msg(e, "embedding"));
+    }
+    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(d->quant_mix, true, false, -1, H), c.vocab, H, tseed(), op);
+    if (rc == SPEC_OK) {
+      shard_lm(m, op, c.vocab, H);
+      rc = build_mat(m, {op}, H, false, m->lm);
+    }
+    cudaStreamSynchronize(m->stream);
+    for (void* t : temps) cudaFree(t);
+    if (rc != SPEC_OK) return rc;
+  }
+  const bool damp_on = d->damp_from_layer > 0;
+  const float damp_sigma = 0.02f * (float)d->damp_e4 / 10000.f;
   m->layers.resize(c.n_layers);
   for (int l = 0; l < c.n_layers; ++l) {
     Layer& L = m->layers[l];
@@ -1597,10 +1626,12 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
     int rc = synth_part(m, temps, mix_type(mix, false, false, l, H), c.n_heads * hd, H, tseed(), q);
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, H), c.n_kv * hd, H, tseed(), k);
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, true, l, H), c.n_kv * hd, H, tseed(), v);
-    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, c.n_heads * hd), H, c.n_heads * hd, tseed(), o);
+    const float sig_od = (damp_on && l >= d->damp_from_layer) ? damp_sigma : 0.02f;
+    if (rc == SPEC_OK)
+      rc = synth_part(m, temps, mix_type(mix, false, false, l, c.n_heads * hd), H, c.n_heads * hd, tseed(), o, sig_od);
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, H), F, H, tseed(), g);
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, H), F, H, tseed(), u);
-    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, true, l, F), H, F, tseed(), dn);
+    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, true, l, F), H, F, tseed(), dn, sig_od);
     if (rc == SPEC_OK) rc = shard_layer(m, temps, c.n_heads, c.n_kv, hd, H, F, q, k, v, o, g, u, dn);
     const int Kl_o = c.n_heads / m->tp_size * hd, Fl = F / m->tp_size;
     if (rc == SPEC_OK) rc = build_mat(m, {q, k, v}, H, false, L.qkv);
@@ -1623,28 +1654,6 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
       } else {
         L.bqkv = full;
       }
-    }
-    cudaStreamSynchronize(m->stream);
-    for (void* t : temps) cudaFree(t);
-    if (rc != SPEC_OK) return rc;
-  }
-  int rc = synth_vec(m, &m->out_norm, H, tseed(), 1.f);
-  if (rc != SPEC_OK) return rc;
-  {
-    std::vector<void*> temps;
-    Part ep, op;
-    m->embed_fmt = mix_type(d->quant_mix, false, false, -1, H);
-    rc = synth_part(m, temps, m->embed_fmt, c.vocab, H, tseed(), ep);
-    if (rc == SPEC_OK) {
-      const size_t bytes = (size_t)c.vocab * (H / fmt_block_elems(m->embed_fmt)) * fmt_block_bytes(m->embed_fmt);
-      cudaError_t e = m->dalloc(&m->embed_raw, bytes);
-      if (e == cudaSuccess) e = cudaMemcpyAsync(m->embed_raw, ep.src, bytes, cudaMemcpyDeviceToDevice, m->stream);
-      if (e != cudaSuccess) rc = m->fail(SPEC_ERR_OOM, cuda_msg(e, "embedding"));
-    }
-    if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(d->quant_mix, true, false, -1, H), c.vocab, H, tseed(), op);
-    if (rc == SPEC_OK) {
-      shard_lm(m, op, c.vocab, H);
-      rc = build_mat(m, {op}, H, false, m->lm);
     }
     cudaStreamSynchronize(m->stream);
     for (void* t : temps) cudaFree(t);

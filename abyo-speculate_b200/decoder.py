@@ -67,13 +67,18 @@ class B200Decoder:
     def synthetic(cls, arch: str, n_layers: int, hidden: int, n_heads: int, n_kv_heads: int, ffn: int,
                   vocab: int, rope_theta: float, eps: float, quant_mix: str = "Q4_K_M", seed: int = 0,
                   device: int = 0, max_ctx: int = 0, use_graphs: bool = True, rope_half: bool = False,
-                  eos_token_ids: Sequence[int] = (), tp_rank: int = 0, tp_size: int = 1) -> "B200Decoder":
+                  eos_token_ids: Sequence[int] = (), tp_rank: int = 0, tp_size: int = 1,
+                  damp_from_layer: int = 0, damp: float = 1.0) -> "B200Decoder":
         """A seeded synthetic model whose weights are generated on the device
-        (the same weights for every tp_size; a tensor-parallel rank keeps its shard)."""
+        (the same weights for every tp_size; a tensor-parallel rank keeps its shard).
+        Layers from damp_from_layer on (0 = none) draw attn_output / ffn_down
+        with sigma 0.02 * damp: a model with the same seed and only the first
+        damp_from_layer layers then predicts like this one (see spec_model_desc)."""
         lib = _lib.load()
         mixes = {"Q4_K_M": 0, "Q5_K": 1, "Q8_0": 2, "BF16": 3}
         d = _lib.ModelDesc(0 if arch == "llama" else 1, n_layers, hidden, n_heads, n_kv_heads, ffn, vocab,
-                           rope_theta, eps, mixes[quant_mix], 1 if rope_half else 0)
+                           rope_theta, eps, mixes[quant_mix], 1 if rope_half else 0, int(damp_from_layer),
+                           int(round(damp * 10000)))
         opts = _lib.LoadOpts(device, max_ctx, 1 if use_graphs else 0, tp_rank, tp_size)
         h = ctypes.c_void_p()
         _lib.check(lib.spec_create_synthetic(ctypes.byref(d), seed, ctypes.byref(opts), ctypes.byref(h)), None)

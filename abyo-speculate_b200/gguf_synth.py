@@ -295,7 +295,8 @@ def write_gguf(path: str, spec: ModelSpec, seed: int, rope_style: Optional[str] 
     return tensors
 
 
-def device_synthetic_tensors(spec: ModelSpec, seed: int, device: int = 0) -> Dict[str, Tuple[np.ndarray, int]]:
+def device_synthetic_tensors(spec: ModelSpec, seed: int, device: int = 0, damp_from_layer: int = 0,
+                             damp: float = 1.0) -> Dict[str, Tuple[np.ndarray, int]]:
     """The tensors of ``B200Decoder.synthetic(..., seed=seed)`` (spec_create_synthetic),
     rebuilt one by one with the same device generator, numbering and seeds
     (spec_synthetic_seed / spec_synthetic_tensor / spec_synthetic_vector), as
@@ -311,11 +312,11 @@ def device_synthetic_tensors(spec: ModelSpec, seed: int, device: int = 0) -> Dic
         counter[0] += 1
         return int(lib.spec_synthetic_seed(seed, counter[0]))
 
-    def mat(name: str, rows: int, k: int, layer: Optional[int]) -> None:
+    def mat(name: str, rows: int, k: int, layer: Optional[int], sigma: float = 0.02) -> None:
         qt = tensor_qtype(spec, name, k, layer)
         nbytes = rows * (k // BLOCK_ELEMS[qt]) * BLOCK_BYTES[qt] if qt in BLOCK_ELEMS else rows * k * 2
         buf = np.empty(nbytes, dtype=np.uint8)
-        _lib.check(lib.spec_synthetic_tensor(device, qt, rows, k, next_seed(), 0.02, buf.ctypes.data, nbytes))
+        _lib.check(lib.spec_synthetic_tensor(device, qt, rows, k, next_seed(), sigma, buf.ctypes.data, nbytes))
         if qt == BF16:
             out[name] = (buf.view(np.uint16).reshape(rows, k), qt)
         else:
@@ -330,9 +331,15 @@ def device_synthetic_tensors(spec: ModelSpec, seed: int, device: int = 0) -> Dic
         return v
 
     hd = spec.head_dim
+    vec("output_norm.weight", spec.hidden, 1.0)
+    mat("token_embd.weight", spec.vocab, spec.hidden, None)
+    mat("output.weight", spec.vocab, spec.hidden, None)
+    damp_sigma = np.float32(0.02) * np.float32(int(round(damp * 10000))) / np.float32(10000)
     for i in range(spec.n_layers):
         for suffix, (rows, k) in layer_tensor_shapes(spec):
-            mat(f"blk.{i}.{suffix}", rows, k, i)
+            damped = damp_from_layer > 0 and i >= damp_from_layer and suffix in ("attn_output.weight",
+                                                                                 "ffn_down.weight")
+            mat(f"blk.{i}.{suffix}", rows, k, i, float(damp_sigma) if damped else 0.02)
         vec(f"blk.{i}.attn_norm.weight", spec.hidden, 1.0)
         vec(f"blk.{i}.ffn_norm.weight", spec.hidden, 1.0)
         if spec.arch == "qwen2":
@@ -341,9 +348,6 @@ def device_synthetic_tensors(spec: ModelSpec, seed: int, device: int = 0) -> Dic
             out[f"blk.{i}.attn_q.bias"] = (b[:nq].copy(), F32)
             out[f"blk.{i}.attn_k.bias"] = (b[nq:nq + nk].copy(), F32)
             out[f"blk.{i}.attn_v.bias"] = (b[nq + nk:].copy(), F32)
-    vec("output_norm.weight", spec.hidden, 1.0)
-    mat("token_embd.weight", spec.vocab, spec.hidden, None)
-    mat("output.weight", spec.vocab, spec.hidden, None)
     return out
 
 

@@ -312,16 +312,23 @@ def run_config(args, ws, rank, local, dist):
     out = {"impl": "b200", "n_gpus": ws, "data": "synthetic", "higher_is_better": True, "steps": args.steps,
            "warmup": args.warmup}
     if args.config == "cfg1":
-        tgt = pkg.B200Decoder.synthetic(**CFG1_TARGET, quant_mix="Q4_K_M", seed=11, device=local, max_ctx=1024)
-        drf = pkg.B200Decoder.synthetic(**CFG1_DRAFT, quant_mix="Q4_K_M", seed=12, device=local, max_ctx=1024)
+        # The 2-layer draft shares the target's embedding, first two layers,
+        # final norm and head (same seed); the target's layers 2-23 draw
+        # their o / down weights at sigma 0.02 x SHARED_DAMP, so the draft
+        # predicts like it (independent random weights accept nothing).
+        tgt = pkg.B200Decoder.synthetic(**CFG1_TARGET, quant_mix="Q4_K_M", seed=11, device=local, max_ctx=1024,
+                                        damp_from_layer=2, damp=SHARED_DAMP)
+        drf = pkg.B200Decoder.synthetic(**CFG1_DRAFT, quant_mix="Q4_K_M", seed=11, device=local, max_ctx=1024)
         prompt = rng.integers(0, CFG1_TARGET["vocab"], size=128).tolist()
         for _ in range(args.warmup):
             sd.vanilla_greedy_generate(tgt, drf, prompt, 16, K_DRAFT)
         t0 = time.perf_counter()
         n_tok = 0
+        accs = []
         for _ in range(max(1, args.steps // 50)):
             toks, acc = sd.vanilla_greedy_generate(tgt, drf, prompt, 128, K_DRAFT)
             n_tok += len(toks)
+            accs += acc
         el = time.perf_counter() - t0
         tgt.rollback_to(128)
         stream = torch.cuda.ExternalStream(tgt.cuda_stream(), device=f"cuda:{local}")
@@ -338,6 +345,9 @@ def run_config(args, ws, rank, local, dist):
                     "config": {"workload": "configs[0]: prompt 128 uniform ids, 128 new tokens, greedy, batch 1",
                                "k": K_DRAFT, "quant_mix": "Q4_K_M (Q8_0 where K=896 is not a multiple of 256)"},
                     "verify_us": round(ms / args.steps * 1e3, 2),
+                    "mean_accepted": round(float(np.mean(accs)), 3),
+                    "draft": "2 layers sharing the target's embedding, layers 0-1, norm and head (same seed); "
+                             f"target layers 2-23 o/down at sigma 0.02 x {SHARED_DAMP}",
                     "note": "wall clock per generation incl. prefill of target and draft"})
     elif args.config == "cfg4":
         T = 4096
@@ -531,6 +541,44 @@ def run_sd_greedy(pkg, target, prompt, local):
                     "random-init models accept ~0 drafts"}
 
 
+SHARED_DAMP = 0.05  # attn_output / ffn_down sigma scale of the target's layers >= 2 (spec_model_desc)
+
+
+def run_sd_shared(pkg, local, prompt):
+    """Greedy vanilla SD (k=4) with a draft that shares the target's embedding,
+    first two layers, final norm and LM head: the target is the configs[1]
+    Llama-3-8B shape with every layer's bytes, but layers 2-31 draw their o and
+    down weights with sigma 0.02 x 0.05, so their residual updates are small
+    and a 2-layer model with the same seed predicts like it (independent
+    random weights accept nothing: there is nothing a draft could learn).
+    Reports tok/s with the acceptance it measures."""
+    sd = importlib.import_module("abyo-speculate_b200.sd_loop")
+    seed = 2468
+    target = pkg.B200Decoder.synthetic(**CFG, quant_mix="Q4_K_M", seed=seed, device=local, max_ctx=4096,
+                                       damp_from_layer=2, damp=SHARED_DAMP)
+    draft = pkg.B200Decoder.synthetic(**dict(CFG, n_layers=2), quant_mix="Q4_K_M", seed=seed, device=local,
+                                      max_ctx=4096)
+    target.observe(prompt)
+    draft.observe(prompt)
+    for _ in range(3):  # warm-up rounds (graph capture)
+        sd.vanilla_greedy_round_native(target, draft, K_DRAFT)
+    target.rollback_to(KV_LEN)
+    draft.rollback_to(KV_LEN)
+    t0 = time.perf_counter()
+    toks, acc = sd.vanilla_greedy_generate(target, draft, prompt, SD_NEW_TOKENS, K_DRAFT, observe_prompt=False)
+    el = time.perf_counter() - t0
+    target.close()
+    draft.close()
+    return {"tok_per_s": round(len(toks) / el, 2), "tokens": len(toks), "rounds": len(acc),
+            "ms_per_round": round(el / len(acc) * 1e3, 3), "mean_accepted": round(float(np.mean(acc)), 3),
+            "acceptance_rate": round(float(np.mean(acc)) / K_DRAFT, 3), "k": K_DRAFT,
+            "draft": "2-layer model sharing the target's embedding, layers 0-1, final norm and Q6_K head "
+                     "(same seed); target = configs[1] shape with layers 2-31's o/down weights at sigma 0.02 x "
+                     f"{SHARED_DAMP}",
+            "note": "greedy vanilla SD (spec_sd_greedy_round), 2048-token prompt, wall clock per round incl. "
+                    "host calls"}
+
+
 def run_b200(args, ws, rank, local, dist):
     import torch
     pkg = importlib.import_module("abyo-speculate_b200")
@@ -609,6 +657,7 @@ def run_b200(args, ws, rank, local, dist):
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(dist, f0.elapsed_time(f1))
     sd_block = run_sd_greedy(pkg, dec, prompt, local) if (tp == 1 and not args.no_sd) else None
+    sd_shared = run_sd_shared(pkg, local, prompt) if (tp == 1 and not args.no_sd) else None
     # The single-GPU microbench runs only at N=1 (under tensor parallelism the
     # other ranks would wait inside the next forward's exchange meanwhile).
     micro = run_microbench(pkg, local) if (ws == 1 and not args.no_microbench) else None
@@ -674,6 +723,7 @@ def run_b200(args, ws, rank, local, dist):
                          "mean_commits": round(rj_commits / max(args.steps, 1), 3),
                          "note": "spec_verify_rejection, temperature 1.0, seeded draft distributions and uniforms"},
         "sd_greedy": sd_block,
+        "sd_greedy_shared_draft": sd_shared,
         "dequant_microbench": micro,
         "gpu_launches": launches_per_step * args.steps,
         "clocks": sampler.summary(),

@@ -68,7 +68,15 @@ typedef struct spec_model_desc {
   float eps;
   int quant_mix;  /* 0 = Q4_K_M, 1 = Q5_K, 2 = Q8_0, 3 = BF16 */
   int rope_half;  /* llama only: 1 = rotate-half RoPE (BF16 checkpoints), 0 = interleaved */
-  int reserved[6];
+  /* Layers from damp_from_layer on (0 = none) draw their attn_output and
+   * ffn_down weights with sigma 0.02 * damp_e4 / 10000: their updates to the
+   * residual are small, so a model with the first damp_from_layer layers and
+   * the same seed (which shares the embedding, the first layers, the final
+   * norm and the head) predicts like this one -- a draft with realistic
+   * acceptance for random-weight benchmarks.  Byte counts do not change. */
+  int damp_from_layer;
+  int damp_e4;
+  int reserved[4];
 } spec_model_desc;
 
 /* ---- lifetime -------------------------------------------------------------
@@ -84,11 +92,13 @@ int spec_create_synthetic(const spec_model_desc* desc, uint64_t seed, const spec
  * (and the benchmark) runs on.  spec_create_synthetic numbers its tensors
  * 1, 2, ... in this order and seeds tensor i with
  * spec_synthetic_seed(model_seed, i):
- *   per layer: attn_q, attn_k, attn_v, attn_output, ffn_gate, ffn_up,
- *              ffn_down (N(0, 0.02) matrices, [rows][K] GGUF blocks),
- *              attn_norm, ffn_norm (1 + N(0, 0.02)), and for qwen2 one
- *              q|k|v bias vector (N(0, 0.02));
- *   then output_norm (1 + N(0, 0.02)), token_embd, output.
+ *   output_norm (1 + N(0, 0.02)), token_embd, output (N(0, 0.02) matrices,
+ *   [rows][K] GGUF blocks), then per layer: attn_q, attn_k, attn_v,
+ *   attn_output, ffn_gate, ffn_up, ffn_down (N(0, 0.02); attn_output and
+ *   ffn_down of damped layers N(0, 0.02 * damp_e4 / 10000)), attn_norm,
+ *   ffn_norm (1 + N(0, 0.02)), and for qwen2 one q|k|v bias vector
+ *   (N(0, 0.02)).  Models with the same seed and shape but fewer layers
+ *   therefore share the embedding, head, final norm and first layers.
  * Types follow the quant mix: Q4_K_M = Q4_K, with Q6_K for attn_v and
  * ffn_down on even layers and for output; Q8_0 wherever K % 256 != 0.
  * No counterpart in the reference (its weights come from checkpoints). */
@@ -106,7 +116,10 @@ void spec_free(spec_model* m);
  * No counterpart in the reference (candle runs the model on one device).  A
  * handle loaded with tp_size > 1 holds rank tp_rank's shard: its q/kv heads
  * and FFN slice (column-parallel q/k/v and gate/up, row-parallel o and down,
- * KV cache of its heads; embedding, norms and LM head whole).  The sums of
+ * KV cache of its heads; embedding and norms whole) and its 128-row-aligned
+ * slice of the LM head (vocabulary-parallel: each rank computes its rows of
+ * the logits and stores them into every rank's logits buffer, so every rank
+ * returns the full rows).  The sums of
  * the row-parallel projections are exchanged inside the forward kernel over
  * NVLink peer memory.  Before the first forward every rank exports its
  * receive buffer (spec_tp_handle: writes an opaque handle, returns its byte
