@@ -148,3 +148,23 @@ def test_qwen7b_shapes_long_context_256_key_splits(pkg, synth, oracle, tmp_path)
     assert np.abs(got - want).max() <= TOL
     assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
     dec.close()
+
+
+def test_shallow_same_seed_model_shares_tensors(synth):
+    """spec_create_synthetic numbers the output norm, embedding and head first,
+    so a 2-layer model with the target's seed shares them and layers 0-1
+    exactly (the bench's shared-prefix draft); damped layers draw o / down at
+    sigma 0.02 x damp."""
+    spec4 = synth.ModelSpec("llama", 4, 256, 4, 2, 512, 1024, 5e5, 2048, 1e-5, "Q4_K_M")
+    spec2 = synth.ModelSpec("llama", 2, 256, 4, 2, 512, 1024, 5e5, 2048, 1e-5, "Q4_K_M")
+    t4 = synth.device_synthetic_tensors(spec4, 77, damp_from_layer=2, damp=0.05)
+    t2 = synth.device_synthetic_tensors(spec2, 77)
+    assert set(t2) <= set(t4)
+    for name, (data, qt) in t2.items():
+        assert qt == t4[name][1] and np.array_equal(np.asarray(data), np.asarray(t4[name][0])), name
+    import importlib
+    om = importlib.import_module("oracle.model")
+    for layer, want in ((1, 0.02), (2, 0.001), (3, 0.001)):
+        raw, qt = t4[f"blk.{layer}.attn_output.weight"]
+        w = om.dequant(qt, raw, 256 * 256)
+        assert abs(float(w.std()) - want) < 0.15 * want, (layer, float(w.std()))
