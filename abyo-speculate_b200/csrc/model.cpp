@@ -1280,17 +1280,20 @@ int check_tp_shape(spec_model* m, int nq, int nkv, int hd, int F, int n_layers) 
 // Vocabulary-parallel LM head: rank r keeps 128-row groups
 // [r G / T, (r + 1) G / T) of the head's G groups (V rows of K columns in
 // GGUF blocks); the other ranks compute the rest and every rank receives all
-// rows (EPI_STORE with out_peers).  Records the rank's first row.
-void shard_lm(spec_model* m, Part& p, int V, int K) {
+// rows (EPI_STORE with out_peers).  Records the rank's first row.  Every rank
+// needs at least one group.
+int shard_lm(spec_model* m, Part& p, int V, int K) {
   m->lm_groups_total = V / kGroupRows;
   m->lm_row0 = 0;
-  if (m->tp_size <= 1) return;
+  if (m->tp_size <= 1) return SPEC_OK;
   const int G = m->lm_groups_total, T = m->tp_size, r = m->tp_rank;
+  if (G < T) return m->fail(SPEC_ERR_UNSUPPORTED, "vocabulary has fewer 128-row groups than tensor-parallel ranks");
   const int g0 = (int)((long long)r * G / T), g1 = (int)((long long)(r + 1) * G / T);
   const size_t row_bytes = (size_t)(K / fmt_block_elems(p.fmt)) * fmt_block_bytes(p.fmt);
   p.src += (size_t)g0 * kGroupRows * row_bytes;
   p.rows = (g1 - g0) * kGroupRows;
   m->lm_row0 = g0 * kGroupRows;
+  return SPEC_OK;
 }
 
 // The tensor-parallel shard of one layer for this rank: q/k/v rows of the
@@ -1505,8 +1508,8 @@ int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) 
   if (outp.rows < c.vocab) return m->fail(SPEC_ERR_IO, "output.weight has fewer rows than the vocabulary");
   if (c.vocab % kGroupRows) return m->fail(SPEC_ERR_UNSUPPORTED, "vocabulary not a multiple of 128");
   outp.rows = c.vocab;
-  shard_lm(m, outp, c.vocab, H);
-  rc = build_mat(m, {outp}, H, false, m->lm);
+  rc = shard_lm(m, outp, c.vocab, H);
+  if (rc == SPEC_OK) rc = build_mat(m, {outp}, H, false, m->lm);
   if (rc != SPEC_OK) return rc;
   set_local_dims(m);
   return finalize_model(m, opts, c.ctx_len);
@@ -1608,8 +1611,8 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
     }
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(d->quant_mix, true, false, -1, H), c.vocab, H, tseed(), op);
     if (rc == SPEC_OK) {
-      shard_lm(m, op, c.vocab, H);
-      rc = build_mat(m, {op}, H, false, m->lm);
+      rc = shard_lm(m, op, c.vocab, H);
+      if (rc == SPEC_OK) rc = build_mat(m, {op}, H, false, m->lm);
     }
     cudaStreamSynchronize(m->stream);
     for (void* t : temps) cudaFree(t);
