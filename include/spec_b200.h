@@ -378,9 +378,10 @@ int spec_qmatmul_time(spec_qweight* w, int M, int iters, int flush_l2, float* av
  *   - each call zeroes the counters it uses (an async memset on `stream`)
  *     and rewrites everything else it reads before reading it;
  *   - stream may be NULL (the weight's own stream, synchronised on return);
- *     a synchronous call reports a device wait that gave up as
- *     SPEC_ERR_TIMEOUT, like spec_qmatmul; with a caller stream the next
- *     synchronous call on the weight reports it;
+ *     each call clears the weight's error word before its launch, so a
+ *     synchronous call reports a device wait that gave up in its own launch
+ *     as SPEC_ERR_TIMEOUT; with a caller stream such a timeout is not
+ *     reported (the next call clears the word first);
  *   - the looked-up address belongs to the device's primary context: calls
  *     must not cross a cudaDeviceReset of that device;
  *   - the caller's current device is restored on return.
