@@ -354,7 +354,7 @@ SPEC_DEV void combine_item(const AttnParams& p, int nt_total, int item, int lane
   }
   const float inv = (lsum > 0.f) ? 1.f / lsum : 0.f;
   const int head = kvh * p.G + gq;
-  const int k = head * HD + col;
+  const int k = p.col_off + head * HD + col;
   const float v = acc * inv;
   float back;
   uint16_t bits;

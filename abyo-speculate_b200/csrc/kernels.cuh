@@ -169,6 +169,11 @@ struct QmvParams {
   uint32_t* next_frag = nullptr;
   float* next_xsum16 = nullptr;
   float* next_xsum32 = nullptr;
+  // Operand column of this op's first output (EPI_SILU; attention ops): under
+  // tensor parallelism a rank's slice of the down / O-projection K may start
+  // inside a 256-column superblock; the rank then streams whole superblocks
+  // and its slice sits at this offset in the wider operand, zeros around it.
+  int next_col_off = 0;
   int act_bf16 = 0;                 // operand dtype: 0 f16, 1 bf16
   // Attention ops (FwdOp::kind != OPK_GEMV) use qbuf / kcache / vcache /
   // t_max / head counts above, next_frag / next_xsum* as the O-projection
@@ -289,6 +294,7 @@ struct AttnParams {
   uint32_t* frag = nullptr;
   float* xsum16 = nullptr;
   float* xsum32 = nullptr;
+  int col_off = 0;                 // operand column of head 0, column 0 (QmvParams::next_col_off)
   int act_bf16 = 0;
   unsigned* err = nullptr;
 };

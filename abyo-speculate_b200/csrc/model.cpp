@@ -195,6 +195,12 @@ struct spec_model {
   };
   std::map<int, Schedule> schedules;
   int tp_rank = 0, tp_size = 1;     // tensor-parallel position (1 = whole model on this GPU)
+  // K of the O-projection and down matrices as this rank streams them, and
+  // where the rank's own columns start inside that window.  Without tensor
+  // parallelism: the whole K at offset 0.  With it, a rank's column slice
+  // that does not start and end on 256-column superblocks is widened to whole
+  // superblocks; the extra columns meet zero activations.
+  int o_kwin = 0, o_koff = 0, d_kwin = 0, d_koff = 0;
   // Tensor-parallel receive buffer (exported to the other ranks by CUDA IPC):
   // two sets (o, down), each [tp_size][groups][kTpSlot] flagged 8-byte words.
   uint8_t* tp_buf = nullptr;
@@ -417,7 +423,9 @@ int alloc_runtime(spec_model* m) {
   // projection, ss1 = after each o-projection (each residual epilogue scales
   // its emitted operand by the other table's rinv).
   ALLOC(m->ss, (size_t)2 * groups_h * kSsStride * 4);
-  const int Kq = c.n_heads * hd;
+  // O-projection and down operands span the K windows the rank streams; the
+  // columns outside its own slice are never written and stay zero.
+  const int Kq = m->o_kwin, Kd = m->d_kwin;
   auto frag_bytes = [](int K) { return (size_t)K * kMaxRows * 2; };
   ALLOC(m->xa, frag_bytes(H));
   ALLOC(m->xa16, (size_t)(H / 16) * kMaxRows * 4);
@@ -425,9 +433,9 @@ int alloc_runtime(spec_model* m) {
   ALLOC(m->xb, frag_bytes(Kq));
   ALLOC(m->xb16, (size_t)(Kq / 16) * kMaxRows * 4);
   ALLOC(m->xb32, (size_t)(Kq / 32) * kMaxRows * 4);
-  ALLOC(m->xc, frag_bytes(F));
-  ALLOC(m->xc16, (size_t)(F / 16) * kMaxRows * 4);
-  ALLOC(m->xc32, (size_t)(F / 32) * kMaxRows * 4);
+  ALLOC(m->xc, frag_bytes(Kd));
+  ALLOC(m->xc16, (size_t)(Kd / 16) * kMaxRows * 4);
+  ALLOC(m->xc32, (size_t)(Kd / 32) * kMaxRows * 4);
   ALLOC(m->qbuf, (size_t)c.n_heads * kMaxRows * hd * 2);
   // Keys per attention split (fixed per model: splits are aligned to absolute
   // key positions, which keeps every row's arithmetic independent of M).
@@ -674,6 +682,7 @@ FwdOp op_attn(spec_model* m, int l, int M, int kind) {
   p.next_frag = m->xb;
   p.next_xsum16 = m->xb16;
   p.next_xsum32 = m->xb32;
+  p.next_col_off = m->o_koff;
   const int R = M * (c.n_heads / c.n_kv);
   p.stages = p.chunks = kind == OPK_ATTN_SPLIT
                             ? c.n_kv * m->attn_max_splits
@@ -729,6 +738,7 @@ FwdOp op_gu(spec_model* m, int l, int M) {
   p.next_frag = m->xc;
   p.next_xsum16 = m->xc16;
   p.next_xsum32 = m->xc32;
+  p.next_col_off = m->d_koff;
   return o;
 }
 FwdOp op_down(spec_model* m, int l, int M) {
@@ -964,6 +974,7 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
       a.frag = m->xb;
       a.xsum16 = m->xb16;
       a.xsum32 = m->xb32;
+      a.col_off = m->o_koff;
       a.act_bf16 = c.bf16 ? 1 : 0;
       a.err = m->err_dev;
       // 64-key splits launch 512+ small split CTAs.  Chained programmatically
@@ -1271,8 +1282,10 @@ int check_tp_shape(spec_model* m, int nq, int nkv, int hd, int F, int n_layers) 
   if (N == 1) return SPEC_OK;
   if (n_layers > kTpMaxLayers) return m->fail(SPEC_ERR_UNSUPPORTED, "too many layers for tensor parallelism");
   if (N > kTpMaxRanks) return m->fail(SPEC_ERR_UNSUPPORTED, "more than 8 tensor-parallel ranks");
-  if (nq % N || nkv % N || F % N || (F / N) % kGroupRows || ((nq / N) * hd) % 256 || (F / N) % 256 ||
-      ((nkv / N) * hd) % kGroupRows)
+  if (nkv % N)
+    return m->fail(SPEC_ERR_UNSUPPORTED,
+                   "tp_size does not divide the KV heads (KV-head replication across ranks is not built)");
+  if (nq % N || F % N || (F / N) % kGroupRows || ((nq / N) * hd) % kGroupRows || ((nkv / N) * hd) % kGroupRows)
     return m->fail(SPEC_ERR_UNSUPPORTED, "model does not split into tp_size tensor-parallel shards");
   return SPEC_OK;
 }
@@ -1311,9 +1324,20 @@ int shard_layer(spec_model* m, std::vector<void*>& temps, int nq, int nkv, int h
   v = part_rows(v, H, r * nkvl * hd, nkvl * hd);
   g = part_rows(g, H, r * Fl, Fl);
   u = part_rows(u, H, r * Fl, Fl);
+  // Row-parallel K slices, widened to whole 256-column superblocks (every
+  // layer gets the same windows, so the operand layout is per model).
+  auto window = [](int K, int k0, int kn, int& lo, int& width, int& off) {
+    lo = k0 / 256 * 256;
+    const int hi = std::min(K, (k0 + kn + 255) / 256 * 256);
+    width = hi - lo;
+    off = k0 - lo;
+  };
+  int o_lo, d_lo;
+  window(nq * hd, r * nql * hd, nql * hd, o_lo, m->o_kwin, m->o_koff);
+  window(F, r * Fl, Fl, d_lo, m->d_kwin, m->d_koff);
   Part o2, d2;
-  int rc = part_cols(m, temps, o, nq * hd, r * nql * hd, nql * hd, o2);
-  if (rc == SPEC_OK) rc = part_cols(m, temps, d, F, r * Fl, Fl, d2);
+  int rc = part_cols(m, temps, o, nq * hd, o_lo, m->o_kwin, o2);
+  if (rc == SPEC_OK) rc = part_cols(m, temps, d, F, d_lo, m->d_kwin, d2);
   if (rc != SPEC_OK) return rc;
   o = o2;
   d = d2;
@@ -1454,12 +1478,13 @@ int load_from_gguf(spec_model* m, const char* path, const spec_load_opts* opts) 
         g.rows != F || u.rows != F || d.rows != H)
       return m->fail(SPEC_ERR_IO, "layer " + std::to_string(l) + " has inconsistent shapes");
     std::vector<void*> temps;
+    m->o_kwin = c.n_heads * hd;  // shard_layer narrows them under tensor parallelism
+    m->d_kwin = F;
     int rc = shard_layer(m, temps, c.n_heads, c.n_kv, hd, H, F, q, k, v, o, g, u, d);
-    const int Kl_o = c.n_heads / m->tp_size * hd, Fl = F / m->tp_size;
     if (rc == SPEC_OK) rc = build_mat(m, {q, k, v}, H, false, L.qkv);
-    if (rc == SPEC_OK) rc = build_mat(m, {o}, Kl_o, false, L.o);
+    if (rc == SPEC_OK) rc = build_mat(m, {o}, m->o_kwin, false, L.o);
     if (rc == SPEC_OK) rc = build_mat(m, {g, u}, H, true, L.gu);
-    if (rc == SPEC_OK) rc = build_mat(m, {d}, Fl, false, L.down);
+    if (rc == SPEC_OK) rc = build_mat(m, {d}, m->d_kwin, false, L.down);
     cudaStreamSynchronize(m->stream);
     for (void* t : temps) cudaFree(t);
     if (rc == SPEC_OK) rc = vec_of(pre + "attn_norm.weight", H, &L.attn_norm);
@@ -1635,12 +1660,13 @@ int create_synthetic(spec_model* m, const spec_model_desc* d, uint64_t seed, con
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, H), F, H, tseed(), g);
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, false, l, H), F, H, tseed(), u);
     if (rc == SPEC_OK) rc = synth_part(m, temps, mix_type(mix, false, true, l, F), H, F, tseed(), dn, sig_od);
+    m->o_kwin = c.n_heads * hd;  // shard_layer narrows them under tensor parallelism
+    m->d_kwin = F;
     if (rc == SPEC_OK) rc = shard_layer(m, temps, c.n_heads, c.n_kv, hd, H, F, q, k, v, o, g, u, dn);
-    const int Kl_o = c.n_heads / m->tp_size * hd, Fl = F / m->tp_size;
     if (rc == SPEC_OK) rc = build_mat(m, {q, k, v}, H, false, L.qkv);
-    if (rc == SPEC_OK) rc = build_mat(m, {o}, Kl_o, false, L.o);
+    if (rc == SPEC_OK) rc = build_mat(m, {o}, m->o_kwin, false, L.o);
     if (rc == SPEC_OK) rc = build_mat(m, {g, u}, H, true, L.gu);
-    if (rc == SPEC_OK) rc = build_mat(m, {dn}, Fl, false, L.down);
+    if (rc == SPEC_OK) rc = build_mat(m, {dn}, m->d_kwin, false, L.down);
     if (rc == SPEC_OK) rc = synth_vec(m, &L.attn_norm, H, tseed(), 1.f);
     if (rc == SPEC_OK) rc = synth_vec(m, &L.ffn_norm, H, tseed(), 1.f);
     if (rc == SPEC_OK && c.has_bias) {
@@ -2800,9 +2826,11 @@ int spec_embed_tokens(spec_model* m, const uint32_t* ids, int n, float* out) {
     ep.h = m->op_in;
     ep.ss_out = m->ss;
     ep.norm = nullptr;
-    ep.frag = m->xb;  // scratch operand; not consumed
-    ep.xsum16 = m->xb16;
-    ep.xsum32 = m->xb32;
+    // Scratch operand, not consumed: the H-wide one (the O-projection
+    // operand may be narrower than H, and its zero columns must stay zero).
+    ep.frag = m->xa;
+    ep.xsum16 = m->xa16;
+    ep.xsum32 = m->xa32;
     ep.act_bf16 = m->cfg.bf16 ? 1 : 0;
     ep.err = m->err_dev;
     if (e == cudaSuccess) e = launch_embed(ep, nt_for_rows(M), m->stream, false);

@@ -811,7 +811,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
     }
   } else if (p.epi == EPI_SILU) {
     if (tid < 64) {
-      const int f = group * 64 + tid;
+      const int f = p.next_col_off + group * 64 + tid;
       for (int m = 0; m < M; ++m) {
         const float gv = ys[m * kGroupRows + tid] * s_rinv[m];
         const float uv = ys[m * kGroupRows + tid + 64] * s_rinv[m];
@@ -1035,6 +1035,7 @@ SPEC_DEV void attn_op_unit(const FwdOp* ops, int* done, const int* gflags, int f
     a.frag = q.next_frag;
     a.xsum16 = q.next_xsum16;
     a.xsum32 = q.next_xsum32;
+    a.col_off = q.next_col_off;
     a.act_bf16 = q.act_bf16;
     a.err = q.err;
   }

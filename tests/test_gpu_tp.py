@@ -29,8 +29,17 @@ TP_SPECS = {
     # Llama-3-8B's head layout (32 q / 8 kv heads of 128): 8 ranks hold one kv head each.
     "llama_tp8": dict(arch="llama", n_layers=2, hidden=4096, n_heads=32, n_kv_heads=8, ffn=4096, vocab=1024,
                       rope_theta=5e5, eps=1e-5, quant_mix="Q4_K_M"),
+    # Slices that start inside a 256-column superblock (Qwen2.5-7B's case: 28
+    # heads and FFN 18944 give 896 q columns and 4736 FFN columns per rank at
+    # 4 ranks).  Here 3 heads (384 columns) and 384 FFN columns per rank: each
+    # rank streams whole superblocks around its slice, zeros elsewhere.
+    "qwen_tp2_uneven": dict(arch="qwen2", n_layers=2, hidden=768, n_heads=6, n_kv_heads=2, ffn=768, vocab=1024,
+                            rope_theta=1e6, eps=1e-6, quant_mix="Q4_K_M"),
+    "qwen_tp4_uneven": dict(arch="qwen2", n_layers=2, hidden=1536, n_heads=12, n_kv_heads=4, ffn=1536, vocab=1024,
+                            rope_theta=1e6, eps=1e-6, quant_mix="Q4_K_M"),
 }
-CASES = [("llama_tp", 2), ("qwen_tp_q80", 2), ("llama_tp4", 2), ("llama_tp4", 4), ("llama_tp8", 8)]
+CASES = [("llama_tp", 2), ("qwen_tp_q80", 2), ("llama_tp4", 2), ("llama_tp4", 4), ("llama_tp8", 8),
+         ("qwen_tp2_uneven", 2), ("qwen_tp4_uneven", 4)]
 
 
 def _prompt(vocab, n, seed):
