@@ -23,6 +23,16 @@ restatement in oracle/quants.c, itself pinned against gguf 0.19.0):
   next_logits (:528-551), batched_logits (:553-583), rollback_to (:585-599).
 
 RMSNorm is candle's x / sqrt(mean(x^2) + eps) * w.  SiLU is x / (1 + exp(-x)).
+
+Activation quantization (OracleModel(act_quant="q8_1")): the reference's
+headline runs candle on CUDA, whose quantized matmul for batches of at most 8
+rows first quantizes the activations to ggml's Q8_1 blocks (32 values, scale
+d = max|x| / 127 kept as f16, codes round(x / d)) and takes integer dot
+products with the weight codes.  That equals the dot product of the
+dequantized weights with the Q8_1 round trip of the activations, up to the
+float summation order, so this mode applies q8_1_roundtrip to the input of
+every quantized matmul (not to BF16 weights, which candle multiplies
+directly).  The default ("none") keeps f32 activations.
 """
 
 from __future__ import annotations
@@ -98,6 +108,22 @@ def attention(q: np.ndarray, k: np.ndarray, v: np.ndarray, threads: int = 0) -> 
     return out
 
 
+def q8_1_roundtrip(x: np.ndarray) -> np.ndarray:
+    """Rows of x through ggml's Q8_1 block format and back (the last axis in
+    blocks of 32): d = max|x| / 127 rounded to f16, q = round-half-away(x / d)
+    with the f32 scale, value = f16(d) * q."""
+    a = np.asarray(x, dtype=np.float32)
+    shp = a.shape
+    b = a.reshape(-1, 32)
+    amax = np.max(np.abs(b), axis=1, keepdims=True)
+    d = (amax / np.float32(127.0)).astype(np.float32)
+    safe = np.where(d > 0, d, np.float32(1.0))
+    r = b / safe
+    q = np.where(d > 0, np.sign(r) * np.floor(np.abs(r) + np.float32(0.5)), np.float32(0.0)).astype(np.float32)
+    d16 = d.astype(np.float16).astype(np.float32)
+    return (d16 * q).reshape(shp).astype(np.float64)
+
+
 def bf16_round(a: np.ndarray) -> np.ndarray:
     u = np.ascontiguousarray(a, dtype=np.float32).view(np.uint32)
     r = ((u + 0x7FFF + ((u >> 16) & 1)) & 0xFFFF0000).astype(np.uint32)
@@ -107,8 +133,12 @@ def bf16_round(a: np.ndarray) -> np.ndarray:
 class OracleModel:
     """Quantized Llama / Qwen2 (or BF16 Llama) from a GGUF file, float64 math."""
 
-    def __init__(self, path: str, max_ctx: int = 512):
+    def __init__(self, path: str, max_ctx: int = 512, act_quant: str = "none"):
         import gguf
+
+        if act_quant not in ("none", "q8_1"):
+            raise ValueError("act_quant must be 'none' or 'q8_1'")
+        self.act_quant = act_quant
 
         r = gguf.GGUFReader(path)
         kv = {f.name: f for f in r.fields.values()}
@@ -199,6 +229,15 @@ class OracleModel:
     def W(self, name: str) -> np.ndarray:
         return self.tensors[name].astype(np.float64)
 
+    def act(self, x: np.ndarray, name: str) -> np.ndarray:
+        """The activations as the matmul with weight `name` sees them."""
+        if self.act_quant == "q8_1" and self.types.get(name) not in (0, 30):
+            return q8_1_roundtrip(x)
+        return x
+
+    def mm(self, x: np.ndarray, name: str) -> np.ndarray:
+        return self.act(x, name) @ self.W(name).T
+
     def rms(self, x: np.ndarray, w: np.ndarray) -> np.ndarray:
         ms = np.mean(x * x, axis=-1, keepdims=True)
         return x / np.sqrt(ms + self.eps) * w
@@ -243,9 +282,9 @@ class OracleModel:
         for li in range(self.n_layers):
             p = f"blk.{li}."
             xn = self.rms(x, self.W(p + "attn_norm.weight"))
-            q = xn @ self.W(p + "attn_q.weight").T
-            k = xn @ self.W(p + "attn_k.weight").T
-            v = xn @ self.W(p + "attn_v.weight").T
+            q = self.mm(xn, p + "attn_q.weight")
+            k = self.mm(xn, p + "attn_k.weight")
+            v = self.mm(xn, p + "attn_v.weight")
             if self.arch == "qwen2":
                 q = q + self.W(p + "attn_q.bias")
                 k = k + self.W(p + "attn_k.bias")
@@ -265,11 +304,11 @@ class OracleModel:
                 pr = np.exp(sc)
                 pr /= pr.sum(axis=-1, keepdims=True)
                 out[:, h] = pr @ vv[h // G]
-            x = x + out.reshape(n, nq * hd) @ self.W(p + "attn_output.weight").T
+            x = x + self.mm(out.reshape(n, nq * hd), p + "attn_output.weight")
             xn = self.rms(x, self.W(p + "ffn_norm.weight"))
-            g = xn @ self.W(p + "ffn_gate.weight").T
-            u = xn @ self.W(p + "ffn_up.weight").T
-            x = x + (g / (1.0 + np.exp(-g)) * u) @ self.W(p + "ffn_down.weight").T
+            g = self.mm(xn, p + "ffn_gate.weight")
+            u = self.mm(xn, p + "ffn_up.weight")
+            x = x + self.mm(g / (1.0 + np.exp(-g)) * u, p + "ffn_down.weight")
             if li in collect:
                 collected.append(x.copy())
         hfin = self.rms(x, self.W("output_norm.weight"))
@@ -280,6 +319,7 @@ class OracleModel:
         # float64 at once (same products; each logit is one dot product).
         name = "output.weight" if "output.weight" in self.tensors else "token_embd.weight"
         w = self.tensors[name]
+        hfin = self.act(hfin, name)
         out = np.empty((hfin.shape[0], self.vocab), dtype=np.float64)
         for r0 in range(0, self.vocab, 16384):
             r1 = min(r0 + 16384, self.vocab)

@@ -46,6 +46,30 @@ def test_observe_next_and_batched_logits(pkg, oracle, tiny_gguf, name):
     assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
 
 
+@pytest.mark.parametrize("name", ["llama_q4km", "qwen_q5k", "qwen_q80"])
+def test_logits_against_q8_1_activation_oracle(pkg, oracle, tiny_gguf, name):
+    """The reference's CUDA matmul quantizes activations to Q8_1 (restated by
+    OracleModel(act_quant="q8_1")); that alone moves logits by 0.015-0.023
+    from the f32 restatement on these models (tests/test_oracle_act_quant.py).
+    The device logits must sit within the same distance of it: 3e-2, and the
+    device's distance to the f32 oracle stays within 2e-2."""
+    path = tiny_gguf(name)
+    dec = pkg.B200Decoder.from_gguf(path, max_ctx=512)
+    q8 = oracle.OracleDecoder(oracle.OracleModel(path, max_ctx=512, act_quant="q8_1"))
+    f32 = oracle.OracleDecoder(oracle.OracleModel(path, max_ctx=512))
+    prompt = _prompt(dec.vocab_size(), 60, 11)
+    drafts = _prompt(dec.vocab_size(), 4, 3)
+    rows = []
+    for d in (dec, q8, f32):
+        d.observe(prompt)
+        rows.append(np.concatenate([d.next_logits()[None], d.batched_logits(drafts)]))
+    got, ref_q8, ref_f32 = rows
+    print(f"{name}: device vs Q8_1 oracle {np.abs(got - ref_q8).max():.4f}, "
+          f"vs f32 oracle {np.abs(got - ref_f32).max():.4f}")
+    assert np.abs(got - ref_q8).max() <= 3e-2
+    assert np.abs(got - ref_f32).max() <= TOL
+
+
 @pytest.mark.parametrize("name", ["llama_q4km", "qwen_q4km", "llama_bf16"])
 def test_long_observe_chunks(pkg, oracle, tiny_gguf, name):
     dec, ref = _pair(pkg, oracle, tiny_gguf(name))

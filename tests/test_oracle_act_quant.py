@@ -1,0 +1,59 @@
+"""The reference's activation quantization, restated, and how far it moves logits.
+
+candle on CUDA (the reference's headline device) runs a quantized matmul of
+at most 8 rows by quantizing the activations to ggml's Q8_1 blocks first; the
+oracle's default keeps f32 activations and the device kernels use f16
+operands.  oracle.model.OracleModel(act_quant="q8_1") restates the Q8_1 path.
+These CPU tests pin the round trip and measure the distance between the two
+oracle modes on the tiny models: that distance is the reference's own
+deviation from the f32 restatement, against which the device's 2e-2 logit
+bound (to the f32 oracle) should be read.
+"""
+
+import numpy as np
+import pytest
+
+from conftest import make_tiny_gguf
+
+
+def test_q8_1_roundtrip_blocks(oracle):
+    rng = np.random.default_rng(0)
+    x = rng.standard_normal((3, 128)).astype(np.float32)
+    x[1, 32:64] = 0.0
+    y = oracle.q8_1_roundtrip(x)
+    for r in range(3):
+        for b in range(4):
+            blk = x[r, 32 * b:32 * b + 32]
+            out = y[r, 32 * b:32 * b + 32]
+            amax = np.abs(blk).max()
+            if amax == 0:
+                assert np.all(out == 0)
+                continue
+            d = np.float32(amax / np.float32(127.0))
+            d16 = float(np.float16(d))
+            q = out / d16
+            assert np.allclose(q, np.round(q)) and np.abs(q).max() == 127  # the extreme value maps to +-127
+            assert np.abs(out - blk).max() <= 0.5 * d16 + abs(d16 - d) * 127 + 1e-7
+    # round half away from zero
+    z = np.zeros(32, dtype=np.float32)
+    z[0], z[1], z[2] = 127.0, 0.5, -2.5
+    w = oracle.q8_1_roundtrip(z)
+    assert w[1] == 1.0 and w[2] == -3.0
+
+
+@pytest.mark.parametrize("name", ["llama_q4km", "qwen_q5k", "qwen_q80"])
+def test_q8_1_activations_move_logits_by_about_the_bound(oracle, synth, tiny_dir, name):
+    path = make_tiny_gguf(synth, name, tiny_dir)
+    rows = {}
+    for mode in ("none", "q8_1"):
+        od = oracle.OracleDecoder(oracle.OracleModel(path, max_ctx=512, act_quant=mode))
+        od.observe(np.random.default_rng(11).integers(0, 1024, size=60).tolist())
+        nxt = od.next_logits()
+        bat = od.batched_logits(np.random.default_rng(3).integers(0, 1024, size=4).tolist())
+        rows[mode] = np.concatenate([nxt[None], bat])
+    diff = float(np.abs(rows["none"] - rows["q8_1"]).max())
+    agree = float((rows["none"].argmax(-1) == rows["q8_1"].argmax(-1)).mean())
+    print(f"{name}: Q8_1 activations move the logits by up to {diff:.4f} "
+          f"(logit std {rows['none'].std():.3f}); argmax agreement {agree:.2f}")
+    # Measured 0.015-0.023 on these models: the same order as the 2e-2 bound.
+    assert 5e-3 < diff < 5e-2
