@@ -25,10 +25,11 @@ restatement in oracle/quants.c, itself pinned against gguf 0.19.0):
 RMSNorm is candle's x / sqrt(mean(x^2) + eps) * w.  SiLU is x / (1 + exp(-x)).
 
 Activation quantization (OracleModel(act_quant="q8_1")): the reference's
-headline runs candle on CUDA, whose quantized matmul for batches of at most 8
-rows first quantizes the activations to ggml's Q8_1 blocks (32 values, scale
-d = max|x| / 127 kept as f16, codes round(x / d)) and takes integer dot
-products with the weight codes.  That equals the dot product of the
+headline runs candle on CUDA, whose quantized matmuls follow ggml's CUDA
+design (candle's source is not vendored here, so this is expected, not
+verified): for small batches the activations are first quantized to ggml's
+Q8_1 blocks (32 values, scale d = max|x| / 127 kept as f16, codes
+round(x / d)) and dotted with the weight codes in integers.  That equals the dot product of the
 dequantized weights with the Q8_1 round trip of the activations, up to the
 float summation order, so this mode applies q8_1_roundtrip to the input of
 every quantized matmul (not to BF16 weights, which candle multiplies

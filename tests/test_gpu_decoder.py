@@ -48,8 +48,8 @@ def test_observe_next_and_batched_logits(pkg, oracle, tiny_gguf, name):
 
 @pytest.mark.parametrize("name", ["llama_q4km", "qwen_q5k", "qwen_q80"])
 def test_logits_against_q8_1_activation_oracle(pkg, oracle, tiny_gguf, name):
-    """The reference's CUDA matmul quantizes activations to Q8_1 (restated by
-    OracleModel(act_quant="q8_1")); that alone moves logits by 0.015-0.023
+    """The reference's CUDA matmul is expected to quantize activations to Q8_1
+    (restated by OracleModel(act_quant="q8_1")); that alone moves logits by 0.015-0.023
     from the f32 restatement on these models (tests/test_oracle_act_quant.py).
     The device logits must sit within the same distance of it: 3e-2, and the
     device's distance to the f32 oracle stays within 2e-2."""

@@ -1,7 +1,8 @@
 """The reference's activation quantization, restated, and how far it moves logits.
 
-candle on CUDA (the reference's headline device) runs a quantized matmul of
-at most 8 rows by quantizing the activations to ggml's Q8_1 blocks first; the
+candle on CUDA (the reference's headline device) follows ggml's CUDA design,
+which quantizes a small batch's activations to Q8_1 blocks before the
+integer dot products (expected; candle's source is not vendored here); the
 oracle's default keeps f32 activations and the device kernels use f16
 operands.  oracle.model.OracleModel(act_quant="q8_1") restates the Q8_1 path.
 These CPU tests pin the round trip and measure the distance between the two
