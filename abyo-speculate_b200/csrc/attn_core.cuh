@@ -295,11 +295,8 @@ SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem,
   return true;
 }
 
-SPEC_DEV void frag_store_a(uint32_t* frag, int nt_total, int m, int k, uint16_t bits) {
-  const int s = k >> 4, kk = k & 15, nt = m >> 3, g = m & 7;
-  const int t = (kk & 7) >> 1, slot = kk >> 3, lo = kk & 1;
-  const size_t hidx = ((size_t)((s * nt_total + nt) * 32 + g * 4 + t)) * 4 + slot * 2 + lo;
-  reinterpret_cast<uint16_t*>(frag)[hidx] = bits;
+SPEC_DEV void frag_store_a(uint32_t* frag, int nt_total, int m, int k, uint16_t bits, int bf16) {
+  reinterpret_cast<uint16_t*>(frag)[operand_half_index(nt_total, m, k, bf16 != 0)] = bits;
 }
 
 // One warp per item = (KV head, row r, columns [32q, 32q + 32) of the head):
@@ -367,7 +364,7 @@ SPEC_DEV void combine_item(const AttnParams& p, int nt_total, int item, int lane
     back = __half2float(h);
     bits = __half_as_ushort(h);
   }
-  frag_store_a(p.frag, nt_total, m, k, bits);
+  frag_store_a(p.frag, nt_total, m, k, bits, p.act_bf16);
   float s16 = back;
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);

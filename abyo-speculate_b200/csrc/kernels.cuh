@@ -3,10 +3,13 @@
 // Data layout in HBM (one model):
 //   * weights: every quantized matrix is repacked at load into "pair tiles"
 //     of 32 rows x KT columns laid out in mma-fragment order (see qgemv.cu);
-//     the byte count equals the GGUF byte count (same bits per weight).
+//     the byte count equals the GGUF byte count (same bits per weight).  BF16
+//     matrices are repacked per 128-row x 128-column stage into the tensor
+//     core's K-major no-swizzle canonical layout (tcgen05 operands).
 //   * residual stream h: f32 [M][H].
-//   * activation operand of every GEMV: f16 (bf16 for BF16 models) values in
-//     m16n8k16 B-fragment order, plus per-16 / per-32 column sums of those
+//   * activation operand of every GEMV: f16 values in m16n8k16 B-fragment
+//     order, or bf16 values (BF16 models) in the canonical layout
+//     (operand_half_index), plus per-16 / per-32 column sums of those
 //     rounded values, stored already multiplied by the tiles' accumulator
 //     seeds: xsum16 = -1056 x (sum of 16), xsum32 = -1024 x (sum of 32)
 //     (kXSum16Seed / kXSum32Seed), so a tile loads its MMA's C operand.
@@ -74,6 +77,23 @@ __host__ __device__ inline unsigned tp_flag_of(unsigned epoch, int tag) { return
 // GEMV is instantiated for 1, 2, 4 and 8, and every producer of an operand
 // must lay it out for the same count.
 __host__ __device__ constexpr int nt_for_rows(int M) { return M <= 8 ? 1 : M <= 16 ? 2 : M <= 32 ? 4 : 8; }
+
+// Position (in 16-bit elements) of operand element (row m, column k) of an
+// operand laid out for nt_total n-tiles.  Both layouts spend 256 bytes per
+// (16-column k-step, n-tile), k-steps outermost:
+//  * f16 operands (consumed by the mma.sync tiles of the quantized formats):
+//    m16n8k16 B-fragment order, lane (g = m % 8, t) holding columns 2t, 2t+1,
+//    2t+8, 2t+9 of row g in one 8-byte word;
+//  * bf16 operands (consumed by the tcgen05 path of BF16 weights): the K-major
+//    no-swizzle canonical layout of the tensor core's shared-memory
+//    descriptors, two 8x8 core matrices per (k-step, n-tile) (columns 0-7,
+//    then 8-15), each 8 rows of 16 bytes.
+__host__ __device__ inline size_t operand_half_index(int nt_total, int m, int k, bool bf16) {
+  const int s = k >> 4, kk = k & 15, nt = m >> 3, g = m & 7;
+  if (bf16) return ((size_t)((s * nt_total + nt) * 2 + (kk >> 3))) * 64 + g * 8 + (kk & 7);
+  const int t = (kk & 7) >> 1, slot = kk >> 3, lo = kk & 1;
+  return ((size_t)((s * nt_total + nt) * 32 + g * 4 + t)) * 4 + slot * 2 + lo;
+}
 
 // Epilogue applied by the CTA that owns the final sum of a 128-row group.
 enum Epi : int {

@@ -75,11 +75,8 @@ SPEC_DEV float deq_elem(const uint8_t* row, int fmt, int k) {
   return 0.f;
 }
 
-SPEC_DEV void frag_store_m(uint32_t* frag, int nt_total, int m, int k, uint16_t bits) {
-  const int s = k >> 4, kk = k & 15, nt = m >> 3, g = m & 7;
-  const int t = (kk & 7) >> 1, slot = kk >> 3, lo = kk & 1;
-  const size_t hidx = ((size_t)((s * nt_total + nt) * 32 + g * 4 + t)) * 4 + slot * 2 + lo;
-  reinterpret_cast<uint16_t*>(frag)[hidx] = bits;
+SPEC_DEV void frag_store_m(uint32_t* frag, int nt_total, int m, int k, uint16_t bits, int bf16) {
+  reinterpret_cast<uint16_t*>(frag)[operand_half_index(nt_total, m, k, bf16 != 0)] = bits;
 }
 
 // grid (H/128, M), 128 threads: one column each.
@@ -114,7 +111,7 @@ __global__ void __launch_bounds__(128) embed_kernel(const __grid_constant__ Embe
     back = __half2float(h);
     bits = __half_as_ushort(h);
   }
-  frag_store_m(p.frag, nt_total, m, n, bits);
+  frag_store_m(p.frag, nt_total, m, n, bits, p.act_bf16);
   float s16 = back;
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
@@ -548,7 +545,7 @@ __global__ void __launch_bounds__(128) make_operand_kernel(const float* x, int K
     back = __half2float(h);
     bits = __half_as_ushort(h);
   }
-  frag_store_m(frag, nt_total, m, k, bits);
+  frag_store_m(frag, nt_total, m, k, bits, bf16);
   float s16 = back;
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);

@@ -344,52 +344,23 @@ SPEC_DEV void tile_q80(const uint8_t* tp, const uint8_t* xs, const float* scr, i
   }
 }
 
-template <int NT>
-SPEC_DEV void tile_bf16(const uint8_t* tp, const uint8_t* xs, int lane, float (&acc)[2][NT][4]) {
-  constexpr int TB = 4096;
-#pragma unroll
-  for (int s = 0; s < 8; ++s) {
-    uint32_t bq[NT][2];
-    load_bfrag<NT>(xs, s, lane, bq);
-#pragma unroll
-    for (int rt = 0; rt < 2; ++rt) {
-      const uint4 a = *reinterpret_cast<const uint4*>(tp + rt * TB + s * 512 + lane * 16);
-#pragma unroll
-      for (int nt = 0; nt < NT; ++nt) {
-        float* ac = acc[rt][nt];
-        float d[4] = {ac[0], ac[1], ac[2], ac[3]};
-        mma_bf16(d, a.x, a.y, a.z, a.w, bq[nt][0], bq[nt][1], d[0], d[1], d[2], d[3]);
-        ac[0] = d[0];
-        ac[1] = d[1];
-        ac[2] = d[2];
-        ac[3] = d[3];
-      }
-    }
-  }
-}
-
+// BF16 weights never come here: they run on the tcgen05 path of fwd_kernel.
 template <int F, int NT>
 SPEC_DEV void process_tile(const uint8_t* tp, const uint8_t* xs, float* scr, int lane, float (&acc)[2][NT][4]) {
-  if constexpr (F != WF_BF16) {
-    decode_scales<F>(tp, scr, lane);
-    __syncwarp();
-  }
+  decode_scales<F>(tp, scr, lane);
+  __syncwarp();
   if constexpr (F == WF_Q4_K) tile_q45k<NT>(tp, xs, scr, lane, false, acc);
   else if constexpr (F == WF_Q5_K) tile_q45k<NT>(tp, xs, scr, lane, true, acc);
   else if constexpr (F == WF_Q6_K) tile_q6k<NT>(tp, xs, scr, lane, acc);
   else if constexpr (F == WF_Q8_0) tile_q80<NT>(tp, xs, scr, lane, acc);
-  else tile_bf16<NT>(tp, xs, lane, acc);
   __syncwarp();
 }
 
 // ---------------------------------------------------------------------------
 // Operand-fragment writer used by the producing epilogues.
 // ---------------------------------------------------------------------------
-SPEC_DEV void frag_store(uint32_t* frag, int nt_total, int m, int k, uint16_t bits) {
-  const int s = k >> 4, kk = k & 15, nt = m >> 3, g = m & 7;
-  const int t = (kk & 7) >> 1, slot = kk >> 3, lo = kk & 1;
-  const size_t hidx = ((size_t)((s * nt_total + nt) * 32 + g * 4 + t)) * 4 + slot * 2 + lo;
-  reinterpret_cast<uint16_t*>(frag)[hidx] = bits;
+SPEC_DEV void frag_store(uint32_t* frag, int nt_total, int m, int k, uint16_t bits, int bf16) {
+  reinterpret_cast<uint16_t*>(frag)[operand_half_index(nt_total, m, k, bf16 != 0)] = bits;
 }
 
 SPEC_DEV uint16_t round_act(float v, int bf16, float& back) {
@@ -403,49 +374,33 @@ SPEC_DEV uint16_t round_act(float v, int bf16, float& back) {
   return __half_as_ushort(h);
 }
 
-// Writes value v for (row m, column k) of the next operand and accumulates
-// the per-16 / per-32 column sums.  Called by a full warp whose lanes hold 32
-// consecutive columns starting at a multiple of 32 (k = k0 + lane).
-SPEC_DEV void emit_operand_warp(uint32_t* frag, float* xs16, float* xs32, int nt_total, int m, int k, float v,
-                                int bf16, int lane) {
-  float back;
-  const uint16_t bits = round_act(v, bf16, back);
-  frag_store(frag, nt_total, m, k, bits);
-  float s16 = back;
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1) s16 += __shfl_xor_sync(0xffffffffu, s16, o);
-  const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 16);
-  const int w16 = 8 * nt_total;
-  if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m] = kXSum16Seed * s16;
-  if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = kXSum32Seed * s32;
-}
-
-// emit_operand_warp for rows 0..M-1 (M <= 8) of one column at once; the
-// rows' shuffle chains are independent, so they overlap.  Same arithmetic per
-// row as emit_operand_warp.
-SPEC_DEV void emit_rows_warp8(uint32_t* frag, float* xs16, float* xs32, int nt_total, int M, int k, const float (&v)[8],
-                              int bf16, int lane) {
+// Writes the values v[q] of rows m0 .. m0 + cnt - 1 (cnt <= 8) at column k of
+// the next operand and their per-16 / per-32 column sums.  Called by a full
+// warp whose lanes hold 32 consecutive columns starting at a multiple of 32
+// (k = k0 + lane); the rows' shuffle chains are independent, so they overlap.
+SPEC_DEV void emit_rows_warp8(uint32_t* frag, float* xs16, float* xs32, int nt_total, int m0, int cnt, int k,
+                              const float (&v)[8], int bf16, int lane) {
   float s16[8];
 #pragma unroll
-  for (int m = 0; m < 8; ++m) {
+  for (int q = 0; q < 8; ++q) {
     float back = 0.f;
-    if (m < M) {
-      const uint16_t bits = round_act(v[m], bf16, back);
-      frag_store(frag, nt_total, m, k, bits);
+    if (q < cnt) {
+      const uint16_t bits = round_act(v[q], bf16, back);
+      frag_store(frag, nt_total, m0 + q, k, bits, bf16);
     }
-    s16[m] = back;
+    s16[q] = back;
   }
 #pragma unroll
   for (int o = 8; o > 0; o >>= 1)
 #pragma unroll
-    for (int m = 0; m < 8; ++m) s16[m] += __shfl_xor_sync(0xffffffffu, s16[m], o);
+    for (int q = 0; q < 8; ++q) s16[q] += __shfl_xor_sync(0xffffffffu, s16[q], o);
   const int w16 = 8 * nt_total;
 #pragma unroll
-  for (int m = 0; m < 8; ++m) {
-    const float s32 = s16[m] + __shfl_xor_sync(0xffffffffu, s16[m], 16);
-    if (m < M) {
-      if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m] = kXSum16Seed * s16[m];
-      if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m] = kXSum32Seed * s32;
+  for (int q = 0; q < 8; ++q) {
+    const float s32 = s16[q] + __shfl_xor_sync(0xffffffffu, s16[q], 16);
+    if (q < cnt) {
+      if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m0 + q] = kXSum16Seed * s16[q];
+      if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m0 + q] = kXSum32Seed * s32;
     }
   }
 }
@@ -503,7 +458,11 @@ SPEC_DEV unsigned long long ld_relaxed_sys_u64(const unsigned long long* ptr) {
 // cut across chunks i0..i1 leaves one partial per piece in slot (chunk +
 // group); the CTA that delivers the last piece sums the slots in chunk order
 // and runs the epilogue.  The CTA that ran the epilogue bumps `done`.
-template <int NT>
+// UM: acc came from tensor memory (tcgen05 path): thread `lane` of warp w holds
+// row 32w + lane, acc[rt][nt][i] = column (rt * NT + nt) * 4 + i; otherwise acc
+// is in m16n8k16 accumulator order.  Partials are stored and summed
+// position-wise, so only the final placement into ys depends on it.
+template <int NT, bool UM>
 SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0, int i1, float (&acc)[2][NT][4],
                                   float* ys, int* done, int* gflag = nullptr, unsigned epoch = 0) {
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -613,9 +572,14 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
     for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int row = warp * 32 + rt * 16 + g + ((i >> 1) ? 8 : 0);
-        const int col = nt * 8 + 2 * t + (i & 1);
-        if (col < M) ys[col * kGroupRows + row] = acc[rt][nt][i];
+        if constexpr (UM) {
+          const int col = (rt * NT + nt) * 4 + i;
+          if (col < M) ys[col * kGroupRows + warp * 32 + lane] = acc[rt][nt][i];
+        } else {
+          const int row = warp * 32 + rt * 16 + g + ((i >> 1) ? 8 : 0);
+          const int col = nt * 8 + 2 * t + (i & 1);
+          if (col < M) ys[col * kGroupRows + row] = acc[rt][nt][i];
+        }
       }
   if (p.tp_size > 1) {
     // Tensor parallelism: this rank's sum of the group goes to every rank's
@@ -708,42 +672,66 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       }
     }
   } else if (p.epi == EPI_QKV) {
+    // Thread j owns column j of the group for every row; rows go 8 at a time
+    // so the RoPE table loads of 8 rows are in flight together.
     const int hd = p.head_dim, nq = p.n_q_heads, nkv = p.n_kv_heads;
     const int G = nq / nkv, R = M * G, half = hd / 2;
-    for (int idx = tid; idx < M * kGroupRows; idx += kGemvWarps * 32) {
-      const int m = idx / kGroupRows, j = idx % kGroupRows, n = n0 + j;
-      const int d = n % hd, head = n / hd;
-      float x = ys[m * kGroupRows + j] * s_rinv[m];
-      if (p.bias) x += p.bias[n];
-      const bool is_v = head >= nq + nkv;
-      float out = x;
-      if (!is_v) {
-        int jp, ci;
-        if (p.rope_interleaved) {
-          jp = j ^ 1;
-          ci = d >> 1;
-        } else {
-          jp = d < half ? j + half : j - half;
-          ci = d < half ? d : d - half;
-        }
-        float y = ys[m * kGroupRows + jp] * s_rinv[m];
-        if (p.bias) y += p.bias[n0 + jp];
-        const int pos = s_pos[m];
-        const float cs = p.rope_cos[(size_t)pos * half + ci], sn = p.rope_sin[(size_t)pos * half + ci];
-        const bool first = p.rope_interleaved ? ((d & 1) == 0) : (d < half);
-        out = first ? (x * cs - y * sn) : (y * sn + x * cs);
-      }
-      float back;
-      const uint16_t bits = round_act(out, p.act_bf16, back);
-      if (head < nq) {
-        const int kvh = head / G, gq = head % G, r = m * G + gq;
-        reinterpret_cast<uint16_t*>(p.qbuf)[((size_t)kvh * R + r) * hd + d] = bits;
-      } else if (!is_v) {
-        const int kvh = head - nq;
-        reinterpret_cast<uint16_t*>(p.kcache)[((size_t)kvh * p.t_max + s_slot[m]) * hd + d] = bits;
+    const int j = tid, n = n0 + j;
+    const int d = n % hd, head = n / hd;
+    const bool is_v = head >= nq + nkv;
+    int jp = j, ci = 0;
+    if (!is_v) {
+      if (p.rope_interleaved) {
+        jp = j ^ 1;
+        ci = d >> 1;
       } else {
-        const int kvh = head - nq - nkv;
-        reinterpret_cast<uint16_t*>(p.vcache)[((size_t)kvh * p.t_max + s_slot[m]) * hd + d] = bits;
+        jp = d < half ? j + half : j - half;
+        ci = d < half ? d : d - half;
+      }
+    }
+    const bool first = p.rope_interleaved ? ((d & 1) == 0) : (d < half);
+    const float bx = p.bias ? p.bias[n] : 0.f, by = (p.bias && !is_v) ? p.bias[n0 + jp] : 0.f;
+    uint16_t* dst;
+    size_t stride_m;  // per row m: q rows move by G * hd; cache rows by the slot
+    if (head < nq) {
+      const int kvh = head / G, gq = head % G;
+      dst = reinterpret_cast<uint16_t*>(p.qbuf) + ((size_t)kvh * R + gq) * hd + d;
+      stride_m = (size_t)G * hd;
+    } else if (!is_v) {
+      dst = reinterpret_cast<uint16_t*>(p.kcache) + (size_t)(head - nq) * p.t_max * hd + d;
+      stride_m = 0;
+    } else {
+      dst = reinterpret_cast<uint16_t*>(p.vcache) + (size_t)(head - nq - nkv) * p.t_max * hd + d;
+      stride_m = 0;
+    }
+    for (int m0 = 0; m0 < M; m0 += 8) {
+      float cs[8], sn[8];
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        cs[q] = 1.f;
+        sn[q] = 0.f;
+        if (!is_v && m0 + q < M) {
+          const size_t ti = (size_t)s_pos[m0 + q] * half + ci;
+          cs[q] = p.rope_cos[ti];
+          sn[q] = p.rope_sin[ti];
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int m = m0 + q;
+        if (m < M) {
+          float x = ys[m * kGroupRows + j] * s_rinv[m];
+          if (p.bias) x += bx;
+          float out = x;
+          if (!is_v) {
+            float y = ys[m * kGroupRows + jp] * s_rinv[m];
+            if (p.bias) y += by;
+            out = first ? (x * cs[q] - y * sn[q]) : (y * sn[q] + x * cs[q]);
+          }
+          float back;
+          const uint16_t bits = round_act(out, p.act_bf16, back);
+          dst[stride_m ? (size_t)m * stride_m : (size_t)s_slot[m] * hd] = bits;
+        }
       }
     }
   } else if (p.epi == EPI_RESID) {
@@ -768,38 +756,30 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       }
     }
     const float nw = resid_pre ? nwpre : (p.next_norm ? __ldg(p.next_norm + n) : 1.f);
-    // s_rinv[m] = rinv of the residual before this update (or 1).
-    if (M <= 8) {
-      // All rows at once: their shuffle chains are independent and overlap.
+    // s_rinv[m] = rinv of the residual before this update (or 1).  Rows go 8
+    // at a time: their shuffle chains are independent and overlap.
+    for (int m0 = 0; m0 < M; m0 += 8) {
+      const int cnt = M - m0 < 8 ? M - m0 : 8;
       float hv[8], sq[8];
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        hv[m] = m < M ? ys[m * kGroupRows + tid] : 0.f;
-        sq[m] = hv[m] * hv[m];
+      for (int q = 0; q < 8; ++q) {
+        hv[q] = q < cnt ? ys[(m0 + q) * kGroupRows + tid] : 0.f;
+        sq[q] = hv[q] * hv[q];
       }
 #pragma unroll
       for (int o = 16; o > 0; o >>= 1)
 #pragma unroll
-        for (int m = 0; m < 8; ++m) sq[m] += __shfl_xor_sync(0xffffffffu, sq[m], o);
+        for (int q = 0; q < 8; ++q) sq[q] += __shfl_xor_sync(0xffffffffu, sq[q], o);
       if (lane == 0) {
 #pragma unroll
-        for (int m = 0; m < 8; ++m)
-          if (m < M) s_red[warp][m] = sq[m];
+        for (int q = 0; q < 8; ++q)
+          if (q < cnt) s_red[warp][m0 + q] = sq[q];
       }
       if (p.next_frag) {
         float v[8];
 #pragma unroll
-        for (int m = 0; m < 8; ++m) v[m] = m < M ? hv[m] * nw * s_rinv[m] : 0.f;
-        emit_rows_warp8(p.next_frag, p.next_xsum16, p.next_xsum32, NT, M, n, v, p.act_bf16, lane);
-      }
-    } else {
-      for (int m = 0; m < M; ++m) {
-        const float hv = ys[m * kGroupRows + tid];
-        const float sq = warp_sum(hv * hv);
-        if (lane == 0) s_red[warp][m] = sq;
-        if (p.next_frag)
-          emit_operand_warp(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m, n, hv * nw * s_rinv[m], p.act_bf16,
-                            lane);
+        for (int q = 0; q < 8; ++q) v[q] = q < cnt ? hv[q] * nw * s_rinv[m0 + q] : 0.f;
+        emit_rows_warp8(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m0, cnt, n, v, p.act_bf16, lane);
       }
     }
     consumer_sync();
@@ -812,11 +792,19 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
   } else if (p.epi == EPI_SILU) {
     if (tid < 64) {
       const int f = p.next_col_off + group * 64 + tid;
-      for (int m = 0; m < M; ++m) {
-        const float gv = ys[m * kGroupRows + tid] * s_rinv[m];
-        const float uv = ys[m * kGroupRows + tid + 64] * s_rinv[m];
-        const float a = gv / (1.f + expf(-gv)) * uv;
-        emit_operand_warp(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m, f, a, p.act_bf16, lane);
+      for (int m0 = 0; m0 < M; m0 += 8) {
+        const int cnt = M - m0 < 8 ? M - m0 : 8;
+        float a[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          a[q] = 0.f;
+          if (q < cnt) {
+            const float gv = ys[(m0 + q) * kGroupRows + tid] * s_rinv[m0 + q];
+            const float uv = ys[(m0 + q) * kGroupRows + tid + 64] * s_rinv[m0 + q];
+            a[q] = gv / (1.f + expf(-gv)) * uv;
+          }
+        }
+        emit_rows_warp8(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m0, cnt, f, a, p.act_bf16, lane);
       }
     }
   }
@@ -845,7 +833,9 @@ SPEC_DEV void mbar_arrive(uint64_t* bar) {
 }
 
 constexpr int kProducerWarp = kGemvWarps;  // warp 4
+constexpr int kMmaWarp = kGemvWarps + 1;    // warp 5 (tcgen05 path only): issues the MMAs
 constexpr int kStageBudget = 64 * 1024;    // ring bytes per CTA (3 CTAs / SM at M <= 8)
+constexpr int kUmmaSmemBudget = 215 * 1024;  // dynamic shared memory of a tcgen05 CTA (one per SM)
 
 template <int SET, int F, int NT>
 struct GeoIf {
@@ -864,14 +854,24 @@ struct FGeo {
   static constexpr int XBMAX = cmax(cmax(cmax(GeoIf<SET, WF_Q4_K, NT>::XB, GeoIf<SET, WF_Q5_K, NT>::XB),
                                          cmax(GeoIf<SET, WF_Q6_K, NT>::XB, GeoIf<SET, WF_Q8_0, NT>::XB)),
                                     GeoIf<SET, WF_BF16, NT>::XB);
+  // BF16 (the only format of its set) runs on tcgen05: one CTA per SM, whose
+  // MMAs are issued by one thread, so the ring takes most of shared memory.
+  static constexpr bool UM = SET == FS_BF16;
   static constexpr int STAGE = kGemvWarps * PAIRMAX + XBMAX;
-  static constexpr int D0 = kStageBudget / STAGE;
-  static constexpr int D = D0 < 2 ? 2 : (D0 > 6 ? 6 : D0);
-  static constexpr int RING = D * STAGE;
   static constexpr int SCR = kGemvWarps * kScratch;
   static constexpr int YS = (8 * NT * kGroupRows + 2 * kMaxSsGroups * 8 * NT) * 4;
   static constexpr int TAIL = SCR > YS ? SCR : YS;
+  static constexpr int D0 = (UM ? kUmmaSmemBudget - TAIL : kStageBudget) / STAGE;
+  static constexpr int D = D0 < 2 ? 2 : (D0 > 6 ? 6 : D0);
+  static constexpr int RING = D * STAGE;
   static constexpr int SMEM = RING + TAIL;
+  // tcgen05 MMA shape: M = 128 rows of a group, N = the operand's rows
+  // (at least 16; one n-tile is read twice through a zero row-group stride).
+  // Two accumulators in TMEM: the MMAs of one piece run while the consumer
+  // warps drain the previous one.
+  static constexpr int UN = NT < 2 ? 16 : 8 * NT;
+  static constexpr uint32_t TCOLS = 2 * UN <= 32 ? 32u : (uint32_t)(2 * UN);  // TMEM columns allocated
+  static constexpr int THREADS = (kGemvWarps + (UM ? 2 : 1)) * 32;
 };
 
 // Stage s of an op: segment, group (within the segment and overall), k-tile.
@@ -980,9 +980,6 @@ SPEC_DEV void process_any(int fmt, const uint8_t* tp, const uint8_t* xs, float* 
   }
   if constexpr ((SET & FS_Q80) != 0) {
     if (fmt == WF_Q8_0) return process_tile<WF_Q8_0, NT>(tp, xs, scr, lane, acc);
-  }
-  if constexpr ((SET & FS_BF16) != 0) {
-    if (fmt == WF_BF16) return process_tile<WF_BF16, NT>(tp, xs, scr, lane, acc);
   }
 }
 
@@ -1119,14 +1116,29 @@ SPEC_DEV void attn_op_unit(const FwdOp* ops, int* done, const int* gflags, int f
 // fills each stage's activation tile once that stage's op has its inputs.
 // Warps 0-3 consume stages, run the per-unit split-K epilogue and publish
 // op completion.
+//
+// BF16 weights (SET == FS_BF16) run on the 5th-generation tensor core
+// instead: warp 5 lane 0 issues, per stage, the tcgen05.mma of the group's
+// 128 rows x the operand's rows over the stage's 128 columns (8 K-steps of
+// 16) into one of two TMEM accumulators, and its tcgen05.commit frees the
+// ring slot once the MMAs have read it.  At the end of a piece it commits the
+// accumulator to the consumer warps, which read their 32 rows (TMEM lanes)
+// with tcgen05.ld, hand the accumulator back and run the same split-K
+// reduction and epilogues while the next piece's MMAs proceed.
 template <int SET, int NT>
-__global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2 : 1)))
+__global__ void __launch_bounds__(FGeo<SET, NT>::THREADS,
+                                  SET == FS_BF16 ? 1 : (NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2 : 1))))
     fwd_kernel(const __grid_constant__ FwdParams Pg) {
   using FG = FGeo<SET, NT>;
   constexpr int D = FG::D;
+  constexpr bool UM = FG::UM;
   extern __shared__ __align__(128) uint8_t smem[];
   __shared__ __align__(8) uint64_t full[D];
   __shared__ __align__(8) uint64_t empty[D];
+  __shared__ __align__(8) uint64_t accfull[2];   // tcgen05 path: a piece's MMAs are complete
+  __shared__ __align__(8) uint64_t accempty[2];  // tcgen05 path: the consumers have read the accumulator
+  __shared__ __align__(8) uint64_t issdone;      // tcgen05 path: every MMA the issuer started is complete
+  __shared__ uint32_t s_tmem;                    // tcgen05 path: TMEM base address
   __shared__ __align__(16) FwdOp s_ops[kMaxLaunchOps];
   // Dependent launch.  Without a cooperative launch the kernels after this
   // one (attention, then the next forward kernel) are only scheduled as its
@@ -1160,11 +1172,22 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
   if (threadIdx.x == 0) {
     for (int s = 0; s < D; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kGemvWarps);
+      // tcgen05 path: the slot is freed by the one commit after its MMAs.
+      mbar_init(&empty[s], UM ? 1 : kGemvWarps);
     }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&accfull[b], 1);
+      mbar_init(&accempty[b], kGemvWarps);
+    }
+    mbar_init(&issdone, 1);
   }
   fence_mbar_init();
+  if constexpr (UM) {
+    if (warp == 0) tmem_alloc(&s_tmem, FG::TCOLS);
+    tc_fence_before();
+  }
   __syncthreads();
+  if constexpr (UM) tc_fence_after();
 
   if (warp == kProducerWarp) {
     if (lane == 0) {
@@ -1294,12 +1317,73 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
     return;
   }
 
+  if constexpr (UM) {
+    if (warp == kMmaWarp) {
+      // ---- tcgen05 issuer: walks the GEMV stages in the consumers' order ----
+      if (lane == 0) {
+        constexpr uint32_t kIdesc = umma_idesc_bf16(128, FG::UN);
+        bool ok = true, fresh = true;
+        int pos = 0, buf = 0;
+        unsigned uses[2] = {0u, 0u};  // pieces accumulated in each TMEM buffer so far
+        SeqIt it;
+        seq_begin(P, c, G, it, true);
+        while (it.valid) {
+          const QmvParams& q = P.ops[it.op].q;
+          for (int s = it.s; s < it.s_end; ++s, ++pos) {
+            const StageLoc L = locate(q, s);
+            const int st = pos % D;
+            if (fresh && uses[buf] > 0 && ok) {
+              // The consumers must have read this buffer's previous piece.
+              ok = mbar_wait_bounded(&accempty[buf], (uses[buf] - 1) & 1u, nullptr);
+              if (!ok) wait_gave_up(P.err, WAIT_CONSUMER_FULL, it.op, s, -2);
+            }
+            if (ok) {
+              ok = mbar_wait_bounded(&full[st], (uint32_t)((pos / D) & 1), nullptr);
+              if (!ok) wait_gave_up(P.err, WAIT_CONSUMER_FULL, it.op, s, pos);
+            }
+            if (ok) {
+              tc_fence_after();
+              // Weights: 8 K-steps of [16 row groups][2 core matrices] (4 KB
+              // each); operand: 8 K-steps of [NT row groups][2 core matrices].
+              const uint32_t wa = smem_u32(ring + (size_t)st * FG::STAGE);
+              const uint32_t xa = wa + kGemvWarps * FG::PAIRMAX;
+              const uint32_t td = s_tmem + (uint32_t)(buf * FG::UN);
+#pragma unroll
+              for (int kk = 0; kk < 8; ++kk) {
+                const uint64_t ad = umma_desc_kmajor(wa + kk * 4096, 128, 256);
+                const uint64_t bd = umma_desc_kmajor(xa + kk * NT * 256, 128, NT < 2 ? 0 : 256);
+                umma_bf16(td, ad, bd, kIdesc, (fresh && kk == 0) ? 0u : 1u);
+              }
+              umma_commit(&empty[st]);
+            } else {
+              mbar_arrive(&empty[st]);
+            }
+            fresh = false;
+            if (L.kt == q.seg[L.seg].k_tiles - 1 || s == it.s_end - 1) {  // end of a piece
+              umma_commit(&accfull[buf]);
+              ++uses[buf];
+              buf ^= 1;
+              fresh = true;
+            }
+          }
+          it.s = it.s_end - 1;
+          seq_next(P, c, G, it);
+        }
+        umma_commit(&issdone);
+      }
+      return;
+    }
+  }
+
   // ---- consumers ----
   pdl_wait();
   float* scr = tail + warp * (kScratch / 4);
   float acc[2][NT][4];
   bool ok = true;
   int pos = 0;
+  // tcgen05 path: the TMEM buffer of the next piece and each buffer's use count.
+  int cbuf = 0;
+  unsigned cuses[2] = {0u, 0u};
   SeqIt it;
   seq_begin(P, c, G, it, false);
   while (it.valid) {
@@ -1317,19 +1401,49 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
       const StageLoc L = locate(q, s);
       const int kts = q.seg[L.seg].k_tiles;
       const int st = pos % D;
-      if (ok) {
-        ok = mbar_wait_bounded(&full[st], (uint32_t)((pos / D) & 1), nullptr);
-        if (!ok) wait_gave_up(P.err, WAIT_CONSUMER_FULL, op, s, pos);
+      if constexpr (UM) {
+        // Stages are the issuer warp's: nothing to do per stage here.
+      } else {
+        if (ok) {
+          ok = mbar_wait_bounded(&full[st], (uint32_t)((pos / D) & 1), nullptr);
+          if (!ok) wait_gave_up(P.err, WAIT_CONSUMER_FULL, op, s, pos);
+        }
+        if (ok) {
+          const uint8_t* stage = ring + (size_t)st * FG::STAGE;
+          const int fmt = q.seg[L.seg].fmt;
+          process_any<SET, NT>(fmt, stage + warp * fmt_pair_bytes(fmt), stage + kGemvWarps * FG::PAIRMAX, scr, lane,
+                               acc);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[st]);
       }
-      if (ok) {
-        const uint8_t* stage = ring + (size_t)st * FG::STAGE;
-        const int fmt = q.seg[L.seg].fmt;
-        process_any<SET, NT>(fmt, stage + warp * fmt_pair_bytes(fmt), stage + kGemvWarps * FG::PAIRMAX, scr, lane,
-                             acc);
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&empty[st]);
       if (L.kt == kts - 1 || s == it.s_end - 1) {  // end of a piece
+        if constexpr (UM) {
+          // The piece's accumulator: wait for its MMAs, read this warp's 32
+          // rows, and hand the buffer back to the issuer.  A piece whose MMAs
+          // were skipped (a wait gave up) yields whatever TMEM holds; the
+          // error word reports it.
+          bool got = mbar_wait_bounded(&accfull[cbuf], cuses[cbuf] & 1u, nullptr);
+          if (!got && lane == 0) wait_gave_up(P.err, WAIT_CONSUMER_FULL, op, s, -1);
+          ++cuses[cbuf];
+          tc_fence_after();
+          const uint32_t ta = s_tmem + ((uint32_t)(warp * 32) << 16) + (uint32_t)(cbuf * FG::UN);
+#pragma unroll
+          for (int c0 = 0; c0 < 8 * NT; c0 += 16) {
+            uint32_t r[16];
+            tmem_ld16(ta + (uint32_t)c0, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const int col = c0 + j;
+              if (col < 8 * NT) acc[col / (4 * NT)][(col / 4) % NT][col % 4] = __uint_as_float(r[j]);
+            }
+          }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&accempty[cbuf]);
+          cbuf ^= 1;
+        }
         // What the epilogue reads of earlier ops (norm tables, residual) is
         // ordered before it without a wait here: a group is reduced only
         // after every K stage of it ran, each stage's inputs were acquired
@@ -1337,8 +1451,8 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
         // and the split arrivals release / acquire those CTAs' work.  Every
         // K stage of a group covers every group of the dependency.
         const int i0 = chunk_of(q, L.gstart), i1 = chunk_of(q, L.gstart + kts - 1);
-        reduce_and_epilogue<NT>(q, L.grp, own, i0, i1, acc, tail, P.done + op,
-                                P.gflags ? P.gflags + (size_t)op * P.flag_stride : nullptr, epoch);
+        reduce_and_epilogue<NT, UM>(q, L.grp, own, i0, i1, acc, tail, P.done + op,
+                                    P.gflags ? P.gflags + (size_t)op * P.flag_stride : nullptr, epoch);
         consumer_sync();
 #pragma unroll
         for (int rt = 0; rt < 2; ++rt)
@@ -1350,6 +1464,19 @@ __global__ void __launch_bounds__(160, NT == 1 ? 3 : (NT == 2 ? 3 : (NT == 4 ? 2
     }
     it.s = it.s_end - 1;
     seq_next(P, c, G, it);
+  }
+  if constexpr (UM) {
+    // Every consumer warp's TMEM reads are done and every MMA the issuer
+    // started has completed (its waits are bounded, so it always gets here):
+    // free the columns.
+    tc_fence_before();
+    consumer_sync();
+    if (warp == 0) {
+      if (!mbar_wait_bounded(&issdone, 0u, nullptr) && lane == 0)
+        wait_gave_up(P.err, WAIT_CONSUMER_FULL, it.valid ? it.op : 255, -3, -3);
+      tc_fence_after();
+      tmem_dealloc(s_tmem, FG::TCOLS);
+    }
   }
   // Attention ops follow every GEMV op of the launch: one chunk = one unit.
   // Every GEMV piece of this CTA is done: the next forward kernel may be
@@ -1431,17 +1558,20 @@ __global__ void repack_kernel(const uint8_t* raw, int fmt, int N, int K, uint8_t
   const int r0 = rt16 * 16;
   const int kbase = kt * KT;
   if (fmt == WF_BF16) {
-    for (int s = 0; s < KT / 16; ++s) {
-      uint16_t v[8];
-      for (int p = 0; p < 8; ++p) {
-        // a0: (g, 2t..2t+1), a1: (g+8, 2t..), a2: (g, 2t+8..), a3: (g+8, 2t+8..)
-        const int reg = p >> 1, lo = p & 1;
-        const int row = g + ((reg & 1) ? 8 : 0), col = 2 * t + ((reg & 2) ? 8 : 0) + lo;
-        const uint8_t* src = raw + (size_t)(r0 + row) * row_bytes + (size_t)(kbase + 16 * s + col) * 2;
-        v[p] = (uint16_t)(src[0] | (src[1] << 8));
-      }
-      uint32_t* dst = reinterpret_cast<uint32_t*>(out + s * 512 + lane * 16);
-      for (int r = 0; r < 4; ++r) dst[r] = (uint32_t)v[2 * r] | ((uint32_t)v[2 * r + 1] << 16);
+    // A stage (128 rows x 128 columns, 32 KB) in the tensor core's K-major
+    // no-swizzle canonical layout: [K-step of 16][8-row group][8-column
+    // half][8 rows x 16 bytes].  This warp writes its 16 rows, 16 bytes
+    // (8 columns of one row) per lane and step.
+    uint8_t* stage = tiles + ((size_t)(rt16 >> 3) * k_tiles + kt) * (kGemvWarps * 2 * TB);
+    const int rbase = (rt16 & 7) * 16;
+    for (int i = lane; i < 16 * (KT / 8); i += 32) {
+      const int row = i / (KT / 8), c8 = i % (KT / 8);
+      const int rr = rbase + row, k0 = c8 * 8;
+      const uint8_t* src = raw + (size_t)(r0 + row) * row_bytes + (size_t)(kbase + k0) * 2;
+      uint4 v;
+      uint8_t* vb = reinterpret_cast<uint8_t*>(&v);
+      for (int b = 0; b < 16; ++b) vb[b] = src[b];
+      *reinterpret_cast<uint4*>(stage + ((k0 >> 4) * 16 + (rr >> 3)) * 256 + ((k0 >> 3) & 1) * 128 + (rr & 7) * 16) = v;
     }
     return;
   }
@@ -1548,7 +1678,7 @@ struct FwdInst {
     cudaError_t e = cudaFuncSetAttribute(fwd_kernel<SET, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
     int b = 0;
-    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fwd_kernel<SET, NT>, (kGemvWarps + 1) * 32, smem);
+    e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, fwd_kernel<SET, NT>, FGeo<SET, NT>::THREADS, smem);
     if (e != cudaSuccess) return e;
     int n = 0;
     e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
@@ -1572,7 +1702,7 @@ struct FwdInst {
     }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid, 1, 1);
-    cfg.blockDim = dim3((kGemvWarps + 1) * 32, 1, 1);
+    cfg.blockDim = dim3(FGeo<SET, NT>::THREADS, 1, 1);
     cfg.dynamicSmemBytes = FGeo<SET, NT>::SMEM;
     cfg.stream = stream;
     cudaLaunchAttribute attr[2];

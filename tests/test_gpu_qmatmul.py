@@ -71,6 +71,26 @@ def test_qmatmul_split_k_and_m_invariance(pkg, synth, oracle, name):
         assert np.array_equal(ym.view(np.uint32), y9[:m].view(np.uint32))
 
 
+def test_bf16_tcgen05_split_k_and_m_invariance(pkg, synth, oracle):
+    """BF16 weights run on tcgen05 with a TMEM accumulator at every M (MMA N =
+    16, 16, 32, 64 for 1-8, 9-16, 17-32 and 33-64 rows).  A split-K shape at
+    M = 64 against the oracle, and rows bit-identical for every smaller M, so
+    the accumulator's arithmetic does not depend on the MMA's N."""
+    fmt = FMTS["BF16"]
+    rng = np.random.default_rng(8)
+    n, k = 1024, 4096
+    w = rng.standard_normal((n, k), dtype=np.float32) * np.float32(0.02)
+    raw = synth.quantize(w, fmt).view(np.uint8).reshape(n, -1)
+    x = rng.standard_normal((64, k), dtype=np.float32)
+    y64, _ = _run(pkg, fmt, raw, n, k, x)
+    deq = oracle.bf16_round(w).astype(np.float64)
+    ref = _round_operand(x, fmt).astype(np.float64) @ deq.T
+    assert np.abs(y64 - ref).max() <= 2e-4 * np.abs(ref).max()
+    for m in (1, 5, 9, 16, 33):
+        ym, _ = _run(pkg, fmt, raw, n, k, x[:m])
+        assert np.array_equal(ym.view(np.uint32), y64[:m].view(np.uint32)), f"M={m} rows differ from M=64"
+
+
 def test_qmatmul_lm_head_shape(pkg, synth, oracle):
     """A vocabulary-sized Q6_K head (many 128-row groups, no split)."""
     rng = np.random.default_rng(11)
