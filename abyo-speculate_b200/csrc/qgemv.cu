@@ -478,8 +478,8 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
   // issued (by the CTA that runs the epilogue only) before the partial sums,
   // so their latency overlaps the partial-sum round trips: the sum-of-squares
   // tables and the rows' positions / cache slots go to shared memory by
-  // cp.async (no registers held), and for EPI_RESID at M <= 8 this thread's
-  // residual column and norm weight go to registers.
+  // cp.async (no registers held), and for EPI_RESID this thread's residual
+  // column (every row) and norm weight go to registers.
   // EPI_QKV's row positions / cache slots share s_red's storage (EPI_RESID only).
   int* s_pos = reinterpret_cast<int*>(&s_red[0][0]);
   int* s_slot = s_pos + kMaxRows;
@@ -487,8 +487,8 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
   const int n_ss = p.ss_groups * M;
   const float* ss_t1 = p.ss_in ? p.ss_pre : nullptr;
   const float* ss_t0 = p.ss_in ? p.ss_in : p.ss_scale;
-  const bool resid_pre = p.epi == EPI_RESID && M <= 8;
-  float hpre[8];
+  const bool resid_pre = p.epi == EPI_RESID;
+  float hpre[8 * NT];
   float nwpre = 1.f;
   auto epi_loads = [&]() {
     if (ss_t0) {
@@ -504,7 +504,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
     }
     if (resid_pre) {
 #pragma unroll
-      for (int m = 0; m < 8; ++m) hpre[m] = m < M ? __ldcg(p.h + (size_t)m * H + n0 + tid) : 0.f;
+      for (int m = 0; m < 8 * NT; ++m) hpre[m] = m < M ? __ldcg(p.h + (size_t)m * H + n0 + tid) : 0.f;
       if (p.next_norm) nwpre = __ldg(p.next_norm + n0 + tid);
     }
   };
@@ -626,25 +626,27 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
   }
   cp_async_wait_all();  // sst, s_pos, s_slot
   if (ss_t0) {
-    // Per-group sums of squares of the residual rows -> RMSNorm scale: warp w
-    // takes rows w, w+4, ...; lane l adds groups l, l+32, ..., then a fixed
-    // butterfly (the same order for every M).
+    // Per-group sums of squares of the residual rows -> RMSNorm scale: thread
+    // m adds row m's groups in group order (the same order for every M, and
+    // the final-norm kernel's); threads 64 + m do the pre-scale table.
     consumer_sync();
-    for (int m = warp; m < M; m += kGemvWarps) {
-      float ms = 0.f, mp = 0.f;
-      for (int q = lane; q < p.ss_groups; q += 32) {
-        ms += sst[q * M + m];
-        if (ss_t1) mp += sst[n_ss + q * M + m];
-      }
-      ms = warp_sum(ms);
-      if (ss_t1) mp = warp_sum(mp);
-      if (lane == 0) {
-        float r = 1.f / sqrtf(ms * p.ss_inv_dim + p.eps);
-        // undo the pre-scale the operand was emitted with: x (1/r_pre) r
-        if (ss_t1) r *= sqrtf(mp * p.ss_inv_dim + p.eps);
-        // EPI_RESID (ss_scale): s_rinv is the pre-scale of the emitted operand.
-        s_rinv[m] = r;
-      }
+    const bool t1 = ss_t1 && tid >= kMaxRows && tid - kMaxRows < M;
+    if (tid < M || t1) {
+      const float* col = t1 ? sst + n_ss + (tid - kMaxRows) : sst + tid;
+      float ms = 0.f;
+#pragma unroll 8
+      for (int q = 0; q < p.ss_groups; ++q) ms += col[q * M];
+      // s_red[3] is free until the epilogue body (s_pos / s_slot use rows 0-1).
+      if (t1) s_red[3][tid - kMaxRows] = ms;
+      else s_rinv[tid] = ms;
+    }
+    consumer_sync();
+    if (tid < M) {
+      float r = 1.f / sqrtf(s_rinv[tid] * p.ss_inv_dim + p.eps);
+      // undo the pre-scale the operand was emitted with: x (1/r_pre) r
+      if (ss_t1) r *= sqrtf(s_red[3][tid] * p.ss_inv_dim + p.eps);
+      // EPI_RESID (ss_scale): s_rinv is the pre-scale of the emitted operand.
+      s_rinv[tid] = r;
     }
   } else if (tid < M) {
     s_rinv[tid] = 1.f;
@@ -672,8 +674,9 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       }
     }
   } else if (p.epi == EPI_QKV) {
-    // Thread j owns column j of the group for every row; rows go 8 at a time
-    // so the RoPE table loads of 8 rows are in flight together.
+    // Thread j owns column j of the group for every row; every row's RoPE
+    // table entries are loaded before any is used, so they are in flight
+    // together.
     const int hd = p.head_dim, nq = p.n_q_heads, nkv = p.n_kv_heads;
     const int G = nq / nkv, R = M * G, half = hd / 2;
     const int j = tid, n = n0 + j;
@@ -704,58 +707,45 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       dst = reinterpret_cast<uint16_t*>(p.vcache) + (size_t)(head - nq - nkv) * p.t_max * hd + d;
       stride_m = 0;
     }
-    for (int m0 = 0; m0 < M; m0 += 8) {
-      float cs[8], sn[8];
+    float cs[8 * NT], sn[8 * NT];
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        cs[q] = 1.f;
-        sn[q] = 0.f;
-        if (!is_v && m0 + q < M) {
-          const size_t ti = (size_t)s_pos[m0 + q] * half + ci;
-          cs[q] = p.rope_cos[ti];
-          sn[q] = p.rope_sin[ti];
-        }
+    for (int m = 0; m < 8 * NT; ++m) {
+      cs[m] = 1.f;
+      sn[m] = 0.f;
+      if (!is_v && m < M) {
+        const size_t ti = (size_t)s_pos[m] * half + ci;
+        cs[m] = p.rope_cos[ti];
+        sn[m] = p.rope_sin[ti];
       }
+    }
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int m = m0 + q;
-        if (m < M) {
-          float x = ys[m * kGroupRows + j] * s_rinv[m];
-          if (p.bias) x += bx;
-          float out = x;
-          if (!is_v) {
-            float y = ys[m * kGroupRows + jp] * s_rinv[m];
-            if (p.bias) y += by;
-            out = first ? (x * cs[q] - y * sn[q]) : (y * sn[q] + x * cs[q]);
-          }
-          float back;
-          const uint16_t bits = round_act(out, p.act_bf16, back);
-          dst[stride_m ? (size_t)m * stride_m : (size_t)s_slot[m] * hd] = bits;
+    for (int m = 0; m < 8 * NT; ++m) {
+      if (m < M) {
+        float x = ys[m * kGroupRows + j] * s_rinv[m];
+        if (p.bias) x += bx;
+        float out = x;
+        if (!is_v) {
+          float y = ys[m * kGroupRows + jp] * s_rinv[m];
+          if (p.bias) y += by;
+          out = first ? (x * cs[m] - y * sn[m]) : (y * sn[m] + x * cs[m]);
         }
+        float back;
+        const uint16_t bits = round_act(out, p.act_bf16, back);
+        dst[stride_m ? (size_t)m * stride_m : (size_t)s_slot[m] * hd] = bits;
       }
     }
   } else if (p.epi == EPI_RESID) {
     const int n = n0 + tid;  // 128 threads, one column each
-    // Issue every row's residual load before using any of them (prefetched
-    // above at M <= 8).
-    for (int m0 = 0; m0 < M; m0 += 8) {
-      float hv[8];
+    // Every row's residual was loaded into registers before the partial sums.
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        if (resid_pre) hv[q] = hpre[q];
-        else if (m0 + q < M) hv[q] = __ldcg(p.h + (size_t)(m0 + q) * H + n);
-      }
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int m = m0 + q;
-        if (m < M) {
-          const float v = hv[q] + ys[m * kGroupRows + tid];
-          p.h[(size_t)m * H + n] = v;
-          ys[m * kGroupRows + tid] = v;
-        }
+    for (int m = 0; m < 8 * NT; ++m) {
+      if (m < M) {
+        const float v = hpre[m] + ys[m * kGroupRows + tid];
+        p.h[(size_t)m * H + n] = v;
+        ys[m * kGroupRows + tid] = v;
       }
     }
-    const float nw = resid_pre ? nwpre : (p.next_norm ? __ldg(p.next_norm + n) : 1.f);
+    const float nw = nwpre;  // 1 without a next norm
     // s_rinv[m] = rinv of the residual before this update (or 1).  Rows go 8
     // at a time: their shuffle chains are independent and overlap.
     for (int m0 = 0; m0 < M; m0 += 8) {
@@ -790,17 +780,18 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       p.ss_out[group * kSsStride + tid] = ss;
     }
   } else if (p.epi == EPI_SILU) {
-    if (tid < 64) {
-      const int f = p.next_col_off + group * 64 + tid;
-      for (int m0 = 0; m0 < M; m0 += 8) {
+    // Warps 0-1 take rows 0-31, warps 2-3 rows 32-63, of the same 64 columns.
+    {
+      const int f = p.next_col_off + group * 64 + (tid & 63);
+      for (int m0 = (tid >> 6) * 32; m0 < M && m0 < (tid >> 6) * 32 + 32; m0 += 8) {
         const int cnt = M - m0 < 8 ? M - m0 : 8;
         float a[8];
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           a[q] = 0.f;
           if (q < cnt) {
-            const float gv = ys[(m0 + q) * kGroupRows + tid] * s_rinv[m0 + q];
-            const float uv = ys[(m0 + q) * kGroupRows + tid + 64] * s_rinv[m0 + q];
+            const float gv = ys[(m0 + q) * kGroupRows + (tid & 63)] * s_rinv[m0 + q];
+            const float uv = ys[(m0 + q) * kGroupRows + (tid & 63) + 64] * s_rinv[m0 + q];
             a[q] = gv / (1.f + expf(-gv)) * uv;
           }
         }
