@@ -374,34 +374,36 @@ SPEC_DEV uint16_t round_act(float v, int bf16, float& back) {
   return __half_as_ushort(h);
 }
 
-// Writes the values v[q] of rows m0 .. m0 + cnt - 1 (cnt <= 8) at column k of
-// the next operand and their per-16 / per-32 column sums.  Called by a full
-// warp whose lanes hold 32 consecutive columns starting at a multiple of 32
-// (k = k0 + lane); the rows' shuffle chains are independent, so they overlap.
-SPEC_DEV void emit_rows_warp8(uint32_t* frag, float* xs16, float* xs32, int nt_total, int m0, int cnt, int k,
-                              const float (&v)[8], int bf16, int lane) {
-  float s16[8];
+// Writes the values v[0..3] of row m at columns k0 .. k0 + 3 of the next
+// operand (one 8-byte or two 4-byte stores) and the per-16 / per-32 column
+// sums of the rounded values.  Called by a full warp: every lane owns 4
+// consecutive columns (k0 a multiple of 4), lanes 4i .. 4i + 3 one aligned
+// 16-column run; lanes with ok == false store nothing but take part in the
+// shuffles.
+SPEC_DEV void emit_operand4(uint32_t* frag, float* xs16, float* xs32, int nt_total, int m, int k0, const float (&v)[4],
+                            int bf16, int lane, bool ok) {
+  float back[4];
+  uint16_t b[4];
 #pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    float back = 0.f;
-    if (q < cnt) {
-      const uint16_t bits = round_act(v[q], bf16, back);
-      frag_store(frag, nt_total, m0 + q, k, bits, bf16);
+  for (int e = 0; e < 4; ++e) b[e] = round_act(v[e], bf16, back[e]);
+  if (ok) {
+    const uint32_t lo = (uint32_t)b[0] | ((uint32_t)b[1] << 16), hi = (uint32_t)b[2] | ((uint32_t)b[3] << 16);
+    uint16_t* hp = reinterpret_cast<uint16_t*>(frag);
+    if (bf16) {
+      *reinterpret_cast<uint2*>(hp + operand_half_index(nt_total, m, k0, true)) = make_uint2(lo, hi);
+    } else {
+      *reinterpret_cast<uint32_t*>(hp + operand_half_index(nt_total, m, k0, false)) = lo;
+      *reinterpret_cast<uint32_t*>(hp + operand_half_index(nt_total, m, k0 + 2, false)) = hi;
     }
-    s16[q] = back;
   }
-#pragma unroll
-  for (int o = 8; o > 0; o >>= 1)
-#pragma unroll
-    for (int q = 0; q < 8; ++q) s16[q] += __shfl_xor_sync(0xffffffffu, s16[q], o);
-  const int w16 = 8 * nt_total;
-#pragma unroll
-  for (int q = 0; q < 8; ++q) {
-    const float s32 = s16[q] + __shfl_xor_sync(0xffffffffu, s16[q], 16);
-    if (q < cnt) {
-      if ((lane & 15) == 0) xs16[(size_t)(k >> 4) * w16 + m0 + q] = kXSum16Seed * s16[q];
-      if (lane == 0) xs32[(size_t)(k >> 5) * w16 + m0 + q] = kXSum32Seed * s32;
-    }
+  float s16 = ((back[0] + back[1]) + back[2]) + back[3];
+  s16 += __shfl_xor_sync(0xffffffffu, s16, 1);
+  s16 += __shfl_xor_sync(0xffffffffu, s16, 2);
+  const float s32 = s16 + __shfl_xor_sync(0xffffffffu, s16, 4);
+  if (ok) {
+    const int w16 = 8 * nt_total;
+    if ((lane & 3) == 0) xs16[(size_t)(k0 >> 4) * w16 + m] = kXSum16Seed * s16;
+    if ((lane & 7) == 0) xs32[(size_t)(k0 >> 5) * w16 + m] = kXSum32Seed * s32;
   }
 }
 
@@ -480,7 +482,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
   // tables and the rows' positions / cache slots go to shared memory by
   // cp.async (no registers held), and for EPI_RESID this thread's residual
   // column (every row) and norm weight go to registers.
-  // EPI_QKV's row positions / cache slots share s_red's storage (EPI_RESID only).
+  // EPI_QKV's row positions / cache slots live in s_red's rows 0-1.
   int* s_pos = reinterpret_cast<int*>(&s_red[0][0]);
   int* s_slot = s_pos + kMaxRows;
   float* sst = ys + M * kGroupRows;
@@ -488,8 +490,8 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
   const float* ss_t1 = p.ss_in ? p.ss_pre : nullptr;
   const float* ss_t0 = p.ss_in ? p.ss_in : p.ss_scale;
   const bool resid_pre = p.epi == EPI_RESID;
-  float hpre[8 * NT];
-  float nwpre = 1.f;
+  float4 hpre4[2 * NT];  // EPI_RESID: rows warp + 4i, columns 4 lane .. 4 lane + 3
+  float4 nwpre4 = make_float4(1.f, 1.f, 1.f, 1.f);
   auto epi_loads = [&]() {
     if (ss_t0) {
       for (int i = tid; i < n_ss; i += kGemvWarps * 32) {
@@ -503,9 +505,13 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       cp_async4(s_slot + tid, p.kv_slots + tid);
     }
     if (resid_pre) {
+      const int k0 = n0 + lane * 4;
 #pragma unroll
-      for (int m = 0; m < 8 * NT; ++m) hpre[m] = m < M ? __ldcg(p.h + (size_t)m * H + n0 + tid) : 0.f;
-      if (p.next_norm) nwpre = __ldg(p.next_norm + n0 + tid);
+      for (int i = 0; i < 2 * NT; ++i) {
+        const int m = warp + 4 * i;
+        hpre4[i] = m < M ? __ldcg(reinterpret_cast<const float4*>(p.h + (size_t)m * H + k0)) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+      if (p.next_norm) nwpre4 = __ldg(reinterpret_cast<const float4*>(p.next_norm + k0));
     }
   };
   if (i0 == i1) epi_loads();
@@ -636,7 +642,7 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       float ms = 0.f;
 #pragma unroll 8
       for (int q = 0; q < p.ss_groups; ++q) ms += col[q * M];
-      // s_red[3] is free until the epilogue body (s_pos / s_slot use rows 0-1).
+      // s_red[3] is free (s_pos / s_slot use rows 0-1).
       if (t1) s_red[3][tid - kMaxRows] = ms;
       else s_rinv[tid] = ms;
     }
@@ -674,129 +680,124 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
       }
     }
   } else if (p.epi == EPI_QKV) {
-    // Thread j owns column j of the group for every row; every row's RoPE
-    // table entries are loaded before any is used, so they are in flight
-    // together.
+    // Thread t owns columns [j0, j0 + 8), j0 = 8 (t % 16), of rows t / 16,
+    // t / 16 + 8, ...: one 16-byte store per row.  (Each 2-byte store is an
+    // instruction of its own, and under the weight stream every store
+    // instruction costs about a memory round trip of issue time.)
     const int hd = p.head_dim, nq = p.n_q_heads, nkv = p.n_kv_heads;
     const int G = nq / nkv, R = M * G, half = hd / 2;
-    const int j = tid, n = n0 + j;
-    const int d = n % hd, head = n / hd;
+    const int j0 = (tid & 15) * 8, n = n0 + j0;
+    const int d0 = n % hd, head = n / hd;  // the 8 columns lie in one head (hd % 8 == 0)
     const bool is_v = head >= nq + nkv;
-    int jp = j, ci = 0;
-    if (!is_v) {
-      if (p.rope_interleaved) {
-        jp = j ^ 1;
-        ci = d >> 1;
-      } else {
-        jp = d < half ? j + half : j - half;
-        ci = d < half ? d : d - half;
-      }
+    const bool ilv = p.rope_interleaved != 0;
+    // Partner column of column j0 + e (RoPE pairs): e ^ 1 within the block
+    // (interleaved pairs), or j0 + e -/+ half (rotate-half); table column of
+    // the block's first pair.
+    const int jq = ilv ? j0 : (d0 < half ? j0 + half : j0 - half);
+    const int ci0 = ilv ? (d0 >> 1) : (d0 < half ? d0 : d0 - half);
+    const bool lowhalf = d0 < half;
+    float bx[8], by[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      bx[e] = p.bias ? p.bias[n + e] : 0.f;
+      by[e] = (p.bias && !is_v) ? p.bias[n0 + (ilv ? (j0 + (e ^ 1)) : (jq + e))] : 0.f;
     }
-    const bool first = p.rope_interleaved ? ((d & 1) == 0) : (d < half);
-    const float bx = p.bias ? p.bias[n] : 0.f, by = (p.bias && !is_v) ? p.bias[n0 + jp] : 0.f;
     uint16_t* dst;
     size_t stride_m;  // per row m: q rows move by G * hd; cache rows by the slot
     if (head < nq) {
       const int kvh = head / G, gq = head % G;
-      dst = reinterpret_cast<uint16_t*>(p.qbuf) + ((size_t)kvh * R + gq) * hd + d;
+      dst = reinterpret_cast<uint16_t*>(p.qbuf) + ((size_t)kvh * R + gq) * hd + d0;
       stride_m = (size_t)G * hd;
     } else if (!is_v) {
-      dst = reinterpret_cast<uint16_t*>(p.kcache) + (size_t)(head - nq) * p.t_max * hd + d;
+      dst = reinterpret_cast<uint16_t*>(p.kcache) + (size_t)(head - nq) * p.t_max * hd + d0;
       stride_m = 0;
     } else {
-      dst = reinterpret_cast<uint16_t*>(p.vcache) + (size_t)(head - nq - nkv) * p.t_max * hd + d;
+      dst = reinterpret_cast<uint16_t*>(p.vcache) + (size_t)(head - nq - nkv) * p.t_max * hd + d0;
       stride_m = 0;
     }
-    float cs[8 * NT], sn[8 * NT];
+    for (int m = tid >> 4; m < M; m += 8) {
+      const float rinv = s_rinv[m];
+      float x[8], y[8], cs[8], sn[8];
 #pragma unroll
-    for (int m = 0; m < 8 * NT; ++m) {
-      cs[m] = 1.f;
-      sn[m] = 0.f;
-      if (!is_v && m < M) {
-        const size_t ti = (size_t)s_pos[m] * half + ci;
-        cs[m] = p.rope_cos[ti];
-        sn[m] = p.rope_sin[ti];
+      for (int e = 0; e < 8; ++e) {
+        x[e] = ys[m * kGroupRows + j0 + e] * rinv;
+        if (p.bias) x[e] += bx[e];
+        cs[e] = 1.f;
+        sn[e] = 0.f;
+        y[e] = 0.f;
       }
-    }
+      if (!is_v) {
+        const size_t tb = (size_t)s_pos[m] * half + ci0;
 #pragma unroll
-    for (int m = 0; m < 8 * NT; ++m) {
-      if (m < M) {
-        float x = ys[m * kGroupRows + j] * s_rinv[m];
-        if (p.bias) x += bx;
-        float out = x;
-        if (!is_v) {
-          float y = ys[m * kGroupRows + jp] * s_rinv[m];
-          if (p.bias) y += by;
-          out = first ? (x * cs[m] - y * sn[m]) : (y * sn[m] + x * cs[m]);
+        for (int e = 0; e < 8; ++e) {
+          y[e] = ys[m * kGroupRows + (ilv ? j0 + (e ^ 1) : jq + e)] * rinv;
+          if (p.bias) y[e] += by[e];
+          const size_t ti = tb + (ilv ? (e >> 1) : e);
+          cs[e] = p.rope_cos[ti];
+          sn[e] = p.rope_sin[ti];
+        }
+      }
+      uint32_t w[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        float o2[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int ee = e + h;
+          const bool first = ilv ? ((ee & 1) == 0) : lowhalf;
+          o2[h] = is_v ? x[ee] : (first ? (x[ee] * cs[ee] - y[ee] * sn[ee]) : (y[ee] * sn[ee] + x[ee] * cs[ee]));
         }
         float back;
-        const uint16_t bits = round_act(out, p.act_bf16, back);
-        dst[stride_m ? (size_t)m * stride_m : (size_t)s_slot[m] * hd] = bits;
+        w[e >> 1] = (uint32_t)round_act(o2[0], p.act_bf16, back) | ((uint32_t)round_act(o2[1], p.act_bf16, back) << 16);
       }
+      *reinterpret_cast<uint4*>(dst + (stride_m ? (size_t)m * stride_m : (size_t)s_slot[m] * hd)) =
+          make_uint4(w[0], w[1], w[2], w[3]);
     }
   } else if (p.epi == EPI_RESID) {
-    const int n = n0 + tid;  // 128 threads, one column each
-    // Every row's residual was loaded into registers before the partial sums.
+    // Warp w owns rows w, w + 4, ...; lane l owns columns [4l, 4l + 4) of the
+    // group: float4 residual updates (rows loaded before the partial sums), a
+    // row's sum of squares in one warp reduction, 4 operand values per store.
+    // s_rinv[m] = rinv of the residual before this update (or 1).
+    const int k0 = n0 + lane * 4;
+    const float4 nw = nwpre4;  // 1 without a next norm
 #pragma unroll
-    for (int m = 0; m < 8 * NT; ++m) {
-      if (m < M) {
-        const float v = hpre[m] + ys[m * kGroupRows + tid];
-        p.h[(size_t)m * H + n] = v;
-        ys[m * kGroupRows + tid] = v;
+    for (int i = 0; i < 2 * NT; ++i) {
+      const int m = warp + 4 * i;
+      if (m < M) {  // uniform across the warp
+        const float4 y = *reinterpret_cast<const float4*>(ys + m * kGroupRows + lane * 4);
+        float4 hv = hpre4[i];
+        hv.x += y.x;
+        hv.y += y.y;
+        hv.z += y.z;
+        hv.w += y.w;
+        *reinterpret_cast<float4*>(p.h + (size_t)m * H + k0) = hv;
+        const float sq = warp_sum(((hv.x * hv.x + hv.y * hv.y) + hv.z * hv.z) + hv.w * hv.w);
+        if (lane == 0) p.ss_out[group * kSsStride + m] = sq;
+        if (p.next_frag) {
+          const float r = s_rinv[m];
+          const float v[4] = {hv.x * nw.x * r, hv.y * nw.y * r, hv.z * nw.z * r, hv.w * nw.w * r};
+          emit_operand4(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m, k0, v, p.act_bf16, lane, true);
+        }
       }
-    }
-    const float nw = nwpre;  // 1 without a next norm
-    // s_rinv[m] = rinv of the residual before this update (or 1).  Rows go 8
-    // at a time: their shuffle chains are independent and overlap.
-    for (int m0 = 0; m0 < M; m0 += 8) {
-      const int cnt = M - m0 < 8 ? M - m0 : 8;
-      float hv[8], sq[8];
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        hv[q] = q < cnt ? ys[(m0 + q) * kGroupRows + tid] : 0.f;
-        sq[q] = hv[q] * hv[q];
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1)
-#pragma unroll
-        for (int q = 0; q < 8; ++q) sq[q] += __shfl_xor_sync(0xffffffffu, sq[q], o);
-      if (lane == 0) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          if (q < cnt) s_red[warp][m0 + q] = sq[q];
-      }
-      if (p.next_frag) {
-        float v[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) v[q] = q < cnt ? hv[q] * nw * s_rinv[m0 + q] : 0.f;
-        emit_rows_warp8(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m0, cnt, n, v, p.act_bf16, lane);
-      }
-    }
-    consumer_sync();
-    if (tid < M) {
-      float ss = 0.f;
-#pragma unroll
-      for (int w = 0; w < kGemvWarps; ++w) ss += s_red[w][tid];
-      p.ss_out[group * kSsStride + tid] = ss;
     }
   } else if (p.epi == EPI_SILU) {
-    // Warps 0-1 take rows 0-31, warps 2-3 rows 32-63, of the same 64 columns.
-    {
-      const int f = p.next_col_off + group * 64 + (tid & 63);
-      for (int m0 = (tid >> 6) * 32; m0 < M && m0 < (tid >> 6) * 32 + 32; m0 += 8) {
-        const int cnt = M - m0 < 8 ? M - m0 : 8;
-        float a[8];
+    // Thread t owns gate/up columns [4c, 4c + 4) (c = t % 16) of rows t / 16,
+    // t / 16 + 8, ...: 4 operand values per store.
+    const int c = (tid & 15) * 4, f0 = p.next_col_off + group * 64 + c;
+    for (int mb = 0; mb < M; mb += 8) {  // uniform across the CTA
+      const int m = mb + (tid >> 4);
+      const bool ok = m < M;
+      float a[4] = {0.f, 0.f, 0.f, 0.f};
+      if (ok) {
+        const float r = s_rinv[m];
+        const float4 g4 = *reinterpret_cast<const float4*>(ys + m * kGroupRows + c);
+        const float4 u4 = *reinterpret_cast<const float4*>(ys + m * kGroupRows + 64 + c);
+        const float gv[4] = {g4.x * r, g4.y * r, g4.z * r, g4.w * r};
+        const float uv[4] = {u4.x * r, u4.y * r, u4.z * r, u4.w * r};
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          a[q] = 0.f;
-          if (q < cnt) {
-            const float gv = ys[(m0 + q) * kGroupRows + (tid & 63)] * s_rinv[m0 + q];
-            const float uv = ys[(m0 + q) * kGroupRows + (tid & 63) + 64] * s_rinv[m0 + q];
-            a[q] = gv / (1.f + expf(-gv)) * uv;
-          }
-        }
-        emit_rows_warp8(p.next_frag, p.next_xsum16, p.next_xsum32, NT, m0, cnt, f, a, p.act_bf16, lane);
+        for (int e = 0; e < 4; ++e) a[e] = gv[e] / (1.f + expf(-gv[e])) * uv[e];
       }
+      emit_operand4(p.next_frag, p.next_xsum16, p.next_xsum32, NT, ok ? m : 0, f0, a, p.act_bf16, lane, ok);
     }
   }
   consumer_sync();  // ys aliases the scale scratch of the next unit
