@@ -351,7 +351,9 @@ def run_config(args, ws, rank, local, dist):
                     "note": "wall clock per generation incl. prefill of target and draft"})
     elif args.config == "cfg4":
         T = 4096
-        tgt = pkg.B200Decoder.synthetic(**CFG4_TARGET, quant_mix="BF16", seed=13, device=local, max_ctx=T + 128,
+        # --layers gives the same shapes with fewer layers (profiling cases).
+        tgt = pkg.B200Decoder.synthetic(**dict(CFG4_TARGET, n_layers=args.layers), quant_mix="BF16", seed=13,
+                                        device=local, max_ctx=T + 128,
                                         rope_half=True)
         prompt = rng.integers(0, CFG4_TARGET["vocab"], size=T).tolist()
         tgt.observe(prompt)
