@@ -27,7 +27,7 @@
 namespace specb200 {
 namespace attn {
 
-constexpr int kWarps = 4;                  // 128 threads take part in a split unit
+constexpr int kWarps = 4;                  // warps of a split unit (128 threads); tree verifies use 8
 constexpr int kKeyBlock = kAttnKeyBlock;   // keys per online-softmax step (two 16-key MMA tiles)
 
 template <int HD>
@@ -35,21 +35,29 @@ struct Smem {
   static constexpr int STRIDE = HD + 8;  // halves; padding breaks bank conflicts
 };
 
-// Shared-memory bytes of a split unit that stages `kp` keys per pass.
-__host__ __device__ constexpr int unit_smem_bytes(int hd, int kp) { return (2 * kp + kWarps * 16) * (hd + 8) * 2; }
+// Shared-memory bytes of a split unit of `w` warps that stages `kp` keys per pass.
+__host__ __device__ constexpr int unit_smem_bytes(int hd, int kp, int w = kWarps) {
+  return (2 * kp + w * 16) * (hd + 8) * 2;
+}
 
 SPEC_DEV void sync128() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Barrier 1 over the W warps of a split unit.
+template <int W>
+SPEC_DEV void sync_unit() {
+  if constexpr (W == 4) sync128();
+  else asm volatile("bar.sync 1, %0;" ::"n"(W * 32) : "memory");
+}
 
-// One split unit, run by threads 0-127 of the CTA (all of them call it with
-// the same arguments).  `kp` keys (a multiple of kKeyBlock) are staged per
-// pass in `smem` (unit_smem_bytes(HD, kp) bytes).  wait_inputs() is called
-// once by all 128 threads, after the prefix keys' loads are issued and before
+// One split unit, run by threads 0 .. 32W-1 of the CTA (all of them call it
+// with the same arguments).  `kp` keys (a multiple of kKeyBlock) are staged
+// per pass in `smem` (unit_smem_bytes(HD, kp, W) bytes).  wait_inputs() is called
+// once by all the unit's threads, after the prefix keys' loads are issued and before
 // any load of what the QKV projection of this forward wrote (new keys, q
 // rows).  Returns false when the split holds no key (nothing written).
 // DS = warps per 16-row tile (1 or 2), each accumulating P.V for HD/DS head
 // columns; S and the softmax state are formed the same way by each, so the
 // result does not depend on DS.
-template <int HD, bool BF16, int DS, class Wait>
+template <int HD, bool BF16, int DS, int W = kWarps, class Wait>
 SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem, int kp, Wait&& wait_inputs) {
   static_assert(DS == 1 || DS == 2, "one or two warps per row tile");
   constexpr int STR = Smem<HD>::STRIDE;
@@ -85,7 +93,7 @@ SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem,
     const int n = (b - a) * CH;
     const bool first = !waited;
     if (first) {
-      for (int i = tid; i < n; i += kWarps * 32) {
+      for (int i = tid; i < n; i += W * 32) {
         const int kr = i / CH, c = i % CH, key = k0 + a + kr;
         if (key < P) {
           cp_async16(Ks + kr * STR + c * 8, kbase + (size_t)key * HD + c * 8, true);
@@ -96,7 +104,7 @@ SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem,
       wait_inputs();
       waited = true;
     }
-    for (int i = tid; i < n; i += kWarps * 32) {
+    for (int i = tid; i < n; i += W * 32) {
       const int kr = i / CH, c = i % CH, key = k0 + a + kr;
       if (!first || key >= P) {
         const bool ok = key < Ttot;
@@ -110,7 +118,7 @@ SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem,
   // the softmax state (identical arithmetic), each accumulates P.V for half
   // of the head dimensions (dims [dh*HD/2, dh*HD/2 + HD/2)).
   constexpr int HALF = HD / 8 / DS;  // 8-column blocks per warp
-  constexpr int TPR = kWarps / DS;   // row tiles per round
+  constexpr int TPR = W / DS;        // row tiles per round
   const int dh = DS == 2 ? (warp & 1) : 0;
   bool first_load = true;
   for (int rt0 = 0; rt0 < RT; rt0 += TPR) {
@@ -132,7 +140,7 @@ SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem,
         load_kv(a, b);
         first_load = false;
       } else if (npass > 1) {
-        sync128();  // every warp is done with the previous pass's keys
+        sync_unit<W>();  // every warp is done with the previous pass's keys
         load_kv(a, b);
       }
       if (ps == 0 && rt < RT) {
@@ -145,7 +153,7 @@ SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem,
       }
       cp_async_commit();
       cp_async_wait<0>();
-      sync128();
+      sync_unit<W>();
       if (rt >= RT) continue;
 
       for (int kb = a; kb < b; kb += kKeyBlock) {
@@ -290,7 +298,7 @@ SPEC_DEV bool split_unit(const AttnParams& p, int split, int kvh, uint8_t* smem,
         }
       }
     }
-    if (rt0 + TPR < RT) sync128();  // the next round restages the q rows
+    if (rt0 + TPR < RT) sync_unit<W>();  // the next round restages the q rows
   }
   return true;
 }
