@@ -424,7 +424,8 @@ int alloc_runtime(spec_model* m) {
   // its emitted operand by the other table's rinv).
   ALLOC(m->ss, (size_t)2 * groups_h * kSsStride * 4);
   // O-projection and down operands span the K windows the rank streams; the
-  // columns outside its own slice are never written and stay zero.
+  // columns outside its own slice are cleared for each forward's layout
+  // (zero_window_edges).
   const int Kq = m->o_kwin, Kd = m->d_kwin;
   auto frag_bytes = [](int K) { return (size_t)K * kMaxRows * 2; };
   ALLOC(m->xa, frag_bytes(H));
@@ -909,6 +910,28 @@ cudaError_t launch_solo(spec_model* m, spec_model::Schedule* sc, int q, int M, c
   return launch_fwd(fp, m->fmt_set, M, s, false);
 }
 
+// Under tensor parallelism a rank's O-projection / down operand spans a
+// window of whole superblocks around its own columns [off, off + len), and
+// the columns outside its slice must read as zero.  Where those columns sit
+// in memory depends on the operand layout of the forward's row count (n-tiles
+// per k-step), so a forward with another row count may have written there:
+// each forward clears them for its own layout.  off, len and win are
+// multiples of 128 columns (whole k-steps and 32-column sum blocks).
+cudaError_t zero_window_edges(uint32_t* frag, float* x16, float* x32, int win, int off, int len, int nt,
+                              cudaStream_t s) {
+  auto clear = [&](int k0, int k1) -> cudaError_t {
+    if (k1 <= k0) return cudaSuccess;
+    cudaError_t e = cudaMemsetAsync(reinterpret_cast<uint8_t*>(frag) + (size_t)(k0 / 16) * nt * 256, 0,
+                                    (size_t)(k1 - k0) / 16 * nt * 256, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(x16 + (size_t)(k0 / 16) * 8 * nt, 0, (size_t)(k1 - k0) / 16 * 8 * nt * 4, s);
+    if (e == cudaSuccess) e = cudaMemsetAsync(x32 + (size_t)(k0 / 32) * 8 * nt, 0, (size_t)(k1 - k0) / 32 * 8 * nt * 4, s);
+    return e;
+  };
+  cudaError_t e = clear(0, off);
+  if (e == cudaSuccess) e = clear(off + len, win);
+  return e;
+}
+
 cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<int>* collect,
                             ProfRec* pr = nullptr) {
   const ModelCfg& c = m->cfg;
@@ -921,6 +944,11 @@ cudaError_t enqueue_forward(spec_model* m, int M, int flags, const std::vector<i
   if (e != cudaSuccess) return e;
   e = cudaMemsetAsync(sc->done, 0, sizeof(int) * sc->n_ops, s);
   if (e != cudaSuccess) return e;
+  if (m->tp_size > 1) {  // c holds this rank's head and FFN counts
+    e = zero_window_edges(m->xb, m->xb16, m->xb32, m->o_kwin, m->o_koff, c.n_heads * hd, nt, s);
+    if (e == cudaSuccess) e = zero_window_edges(m->xc, m->xc16, m->xc32, m->d_kwin, m->d_koff, c.ffn, nt, s);
+    if (e != cudaSuccess) return e;
+  }
   EmbedParams ep;
   ep.table = m->embed_raw;
   ep.fmt = m->embed_fmt;

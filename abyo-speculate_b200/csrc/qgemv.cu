@@ -446,13 +446,11 @@ SPEC_DEV int ld_relaxed_gpu(const int* ptr) {
 SPEC_DEV void red_add_relaxed(int* ptr, int v) {
   asm volatile("red.relaxed.gpu.global.add.s32 [%0], %1;" ::"l"(ptr), "r"(v) : "memory");
 }
-SPEC_DEV void st_relaxed_sys_u64(unsigned long long* ptr, unsigned long long v) {
-  asm volatile("st.relaxed.sys.global.b64 [%0], %1;" ::"l"(ptr), "l"(v) : "memory");
+SPEC_DEV void st_relaxed_sys_u64x2(unsigned long long* ptr, unsigned long long a, unsigned long long b) {
+  asm volatile("st.relaxed.sys.global.v2.b64 [%0], {%1, %2};" ::"l"(ptr), "l"(a), "l"(b) : "memory");
 }
-SPEC_DEV unsigned long long ld_relaxed_sys_u64(const unsigned long long* ptr) {
-  unsigned long long v;
-  asm volatile("ld.relaxed.sys.global.b64 %0, [%1];" : "=l"(v) : "l"(ptr) : "memory");
-  return v;
+SPEC_DEV void ld_relaxed_sys_u64x2(const unsigned long long* ptr, unsigned long long& a, unsigned long long& b) {
+  asm volatile("ld.relaxed.sys.global.v2.b64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(ptr) : "memory");
 }
 
 // Finishes one piece (the part of a 128-row group inside one chunk).  A
@@ -594,24 +592,28 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
     // rank order (the same arithmetic on every rank, so h stays identical).
     // Each thread reads back only the elements it stored, so ys needs no
     // barrier between the two loops.
+    // Two words per 16-byte store / load (each 8-byte word is read and
+    // checked on its own, so a pair need not arrive together).
     consumer_sync();
     const int ng = p.seg[0].groups + p.seg[1].groups;
-    const int n = M * kGroupRows;
+    const int n = M * kGroupRows;  // even
     const unsigned flag = tp_flag_of(*p.tp_epoch, p.tp_tag);
     const unsigned long long hi = (unsigned long long)flag << 32;
     for (int i = 1; i <= p.tp_size; ++i) {
       const int r = (p.tp_rank + i) % p.tp_size;
       unsigned long long* dst = p.tp_recv[r] + ((size_t)p.tp_rank * ng + group) * kTpSlot;
-      for (int e = tid; e < n; e += kGemvWarps * 32) st_relaxed_sys_u64(dst + e, hi | __float_as_uint(ys[e]));
+      for (int e = 2 * tid; e < n; e += 2 * kGemvWarps * 32)
+        st_relaxed_sys_u64x2(dst + e, hi | __float_as_uint(ys[e]), hi | __float_as_uint(ys[e + 1]));
     }
     bool live = true;
     const unsigned long long t0 = global_timer_ns();
-    for (int e = tid; e < n; e += kGemvWarps * 32) {
-      float sum = 0.f;
+    for (int e = 2 * tid; e < n; e += 2 * kGemvWarps * 32) {
+      float sum0 = 0.f, sum1 = 0.f;
       for (int r = 0; r < p.tp_size; ++r) {
         const unsigned long long* src = p.tp_recv_local + ((size_t)r * ng + group) * kTpSlot + e;
-        unsigned long long w = ld_relaxed_sys_u64(src);
-        for (unsigned spin = 0; live && (unsigned)(w >> 32) != flag; ++spin) {
+        unsigned long long w0, w1;
+        ld_relaxed_sys_u64x2(src, w0, w1);
+        for (unsigned spin = 0; live && ((unsigned)(w0 >> 32) != flag || (unsigned)(w1 >> 32) != flag); ++spin) {
           if ((spin & 255u) == 255u &&
               ((*(volatile unsigned*)p.err & DEV_ERR_MBAR_TIMEOUT) || global_timer_ns() - t0 > kMbarTimeoutNs)) {
             live = false;
@@ -619,15 +621,17 @@ SPEC_DEV void reduce_and_epilogue(const QmvParams& p, int group, int own, int i0
             if (atomicCAS(p.err + 1, 0u, WAIT_TP_PEERS | ((unsigned)group << 8) | ((unsigned)blockIdx.x << 16)) ==
                 0u) {
               p.err[2] = (unsigned)r;
-              p.err[3] = (unsigned)(w >> 32);
+              p.err[3] = (unsigned)(((unsigned)(w0 >> 32) != flag ? w0 : w1) >> 32);
             }
             break;
           }
-          w = ld_relaxed_sys_u64(src);
+          ld_relaxed_sys_u64x2(src, w0, w1);
         }
-        sum += __uint_as_float((unsigned)w);
+        sum0 += __uint_as_float((unsigned)w0);
+        sum1 += __uint_as_float((unsigned)w1);
       }
-      ys[e] = sum;
+      ys[e] = sum0;
+      ys[e + 1] = sum1;
     }
   }
   cp_async_wait_all();  // sst, s_pos, s_slot
