@@ -149,6 +149,12 @@ SIGNATURES = [
     ("spec_verify_rejection", ctypes.c_int,
      [ctypes.c_void_p, c_u32_p, ctypes.c_int, c_f32_p, ctypes.c_float, c_f32_p, ctypes.c_int, ctypes.c_int, c_u32_p,
       c_int_p, c_int_p]),
+    ("spec_rng_create", ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]),
+    ("spec_rng_free", None, [ctypes.c_void_p]),
+    ("spec_rng_next_f32", ctypes.c_int, [ctypes.c_void_p, c_f32_p, ctypes.c_int]),
+    ("spec_sd_sampled_round", ctypes.c_int,
+     [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_float, ctypes.c_void_p, ctypes.c_int,
+      ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     ("spec_verify_tree_greedy", ctypes.c_int,
      [ctypes.c_void_p, c_u32_p, c_i32_p, ctypes.c_int, c_i32_p, c_int_p, c_u32_p]),
     ("spec_last_forward_ms", ctypes.c_float, [ctypes.c_void_p]),

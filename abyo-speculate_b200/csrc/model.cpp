@@ -19,6 +19,7 @@
 
 #include <algorithm>
 #include <memory>
+#include <new>
 #include <numeric>
 #include <string>
 #include <vector>
@@ -2984,12 +2985,12 @@ int spec_sd_greedy_round(spec_model* target, spec_model* draft, int k, uint32_t*
   return SPEC_OK;
 }
 
-int spec_verify_rejection(spec_model* m, const uint32_t* drafts, int k, const float* draft_probs,
-                          float temperature, const float* uniforms, int n_uniforms, int budget, uint32_t* commits,
-                          int* n_commits, int* n_uniforms_used) {
-  if (!m || !commits || !n_commits || k < 0 || (k > 0 && (!drafts || !draft_probs)) || n_uniforms < 0 ||
-      (n_uniforms > 0 && !uniforms))
-    return SPEC_ERR_INVALID;
+// spec_verify_rejection with the draft rows either on the host (draft_probs)
+// or already in m->rej_q (draft_probs null; the sampled round puts them
+// there on the device).
+int verify_rejection_core(spec_model* m, const uint32_t* drafts, int k, const float* draft_probs, float temperature,
+                          const float* uniforms, int n_uniforms, int budget, uint32_t* commits, int* n_commits,
+                          int* n_uniforms_used) {
   DeviceGuard dg_(m->device);
   if (!std::isfinite(temperature) || temperature < 0.f) return m->fail(SPEC_ERR_INVALID, "invalid temperature");
   if (budget < 1) return m->fail(SPEC_ERR_INVALID, "token budget must be >= 1");
@@ -3013,9 +3014,10 @@ int spec_verify_rejection(spec_model* m, const uint32_t* drafts, int k, const fl
   st->n_uniforms = std::min(n_uniforms, kMaxRows + 1);
   for (int i = 0; i < k; ++i) st->drafts[i] = (int)drafts[i];
   for (int i = 0; i < st->n_uniforms; ++i) st->uniforms[i] = uniforms[i];
-  if (k) memcpy(m->rej_q_host, draft_probs, (size_t)k * V * 4);
+  if (k && draft_probs) memcpy(m->rej_q_host, draft_probs, (size_t)k * V * 4);
   cudaError_t e0 = cudaSuccess;
-  if (k) e0 = cudaMemcpyAsync(m->rej_q, m->rej_q_host, (size_t)k * V * 4, cudaMemcpyHostToDevice, m->stream);
+  if (k && draft_probs)
+    e0 = cudaMemcpyAsync(m->rej_q, m->rej_q_host, (size_t)k * V * 4, cudaMemcpyHostToDevice, m->stream);
   if (e0 == cudaSuccess)
     e0 = cudaMemcpyAsync(m->rej_step_dev, st, sizeof(RejStep), cudaMemcpyHostToDevice, m->stream);
   if (e0 != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e0, "rejection inputs"));
@@ -3049,6 +3051,162 @@ int spec_verify_rejection(spec_model* m, const uint32_t* drafts, int k, const fl
   for (int i = 0; i < n; ++i) commits[i] = (uint32_t)m->rej_out_host[4 + i];
   *n_commits = n;
   if (n_uniforms_used) *n_uniforms_used = m->rej_out_host[1];
+  return SPEC_OK;
+}
+
+int spec_verify_rejection(spec_model* m, const uint32_t* drafts, int k, const float* draft_probs,
+                          float temperature, const float* uniforms, int n_uniforms, int budget, uint32_t* commits,
+                          int* n_commits, int* n_uniforms_used) {
+  if (!m || !commits || !n_commits || k < 0 || (k > 0 && (!drafts || !draft_probs)) || n_uniforms < 0 ||
+      (n_uniforms > 0 && !uniforms))
+    return SPEC_ERR_INVALID;
+  return verify_rejection_core(m, drafts, k, draft_probs, temperature, uniforms, n_uniforms, budget, commits,
+                               n_commits, n_uniforms_used);
+}
+
+// ---------------------------------------------------------------------------
+// The reference's seeded sampling stream (rand 0.8 StdRng, restated from the
+// published algorithms; see include/spec_b200.h) and the sampled SD round.
+// ---------------------------------------------------------------------------
+struct spec_rng {
+  uint32_t key[8];
+  uint64_t block = 0;  // counter of the next block to generate
+  uint32_t buf[64];    // four blocks, as rand_chacha buffers them (the order is the stream's)
+  int pos = 64;
+};
+
+namespace {
+
+inline uint32_t rotl32(uint32_t x, int n) { return (x << n) | (x >> (32 - n)); }
+
+// One ChaCha block with `rounds` rounds: a 64-bit block counter in words
+// 12-13 and a zero 64-bit stream id in words 14-15 (rand_chacha's layout).
+void chacha_block(const uint32_t key[8], uint64_t ctr, int rounds, uint32_t out[16]) {
+  uint32_t st[16] = {0x61707865u, 0x3320646Eu, 0x79622D32u, 0x6B206574u};
+  for (int i = 0; i < 8; ++i) st[4 + i] = key[i];
+  st[12] = (uint32_t)ctr;
+  st[13] = (uint32_t)(ctr >> 32);
+  st[14] = 0;
+  st[15] = 0;
+  uint32_t x[16];
+  memcpy(x, st, sizeof x);
+  auto qr = [&](int a, int b, int c, int d) {
+    x[a] += x[b]; x[d] = rotl32(x[d] ^ x[a], 16);
+    x[c] += x[d]; x[b] = rotl32(x[b] ^ x[c], 12);
+    x[a] += x[b]; x[d] = rotl32(x[d] ^ x[a], 8);
+    x[c] += x[d]; x[b] = rotl32(x[b] ^ x[c], 7);
+  };
+  for (int r = 0; r < rounds; r += 2) {
+    qr(0, 4, 8, 12); qr(1, 5, 9, 13); qr(2, 6, 10, 14); qr(3, 7, 11, 15);
+    qr(0, 5, 10, 15); qr(1, 6, 11, 12); qr(2, 7, 8, 13); qr(3, 4, 9, 14);
+  }
+  for (int i = 0; i < 16; ++i) out[i] = x[i] + st[i];
+}
+
+uint32_t rng_next_u32(spec_rng* r) {
+  if (r->pos >= 64) {
+    for (int b = 0; b < 4; ++b) chacha_block(r->key, r->block + b, 12, r->buf + 16 * b);
+    r->block += 4;
+    r->pos = 0;
+  }
+  return r->buf[r->pos++];
+}
+
+// gen::<f32>(): the top 24 bits scaled by 2^-24 (exact in f32).
+float rng_next_f32(spec_rng* r) { return (float)(rng_next_u32(r) >> 8) * (1.0f / 16777216.0f); }
+
+void rng_peek_f32(const spec_rng* r, int n, float* out) {
+  spec_rng c = *r;
+  for (int i = 0; i < n; ++i) out[i] = rng_next_f32(&c);
+}
+
+}  // namespace
+
+int spec_rng_create(uint64_t seed, spec_rng** out) {
+  if (!out) return SPEC_ERR_INVALID;
+  spec_rng* r = new (std::nothrow) spec_rng();
+  if (!r) return SPEC_ERR_OOM;
+  // rand_core 0.6 seed_from_u64: eight PCG32 outputs, little-endian.
+  uint64_t state = seed;
+  for (int i = 0; i < 8; ++i) {
+    state = state * 6364136223846793005ull + 11634580027462260723ull;
+    const uint32_t xs = (uint32_t)(((state >> 18) ^ state) >> 27);
+    const int rot = (int)(state >> 59);
+    r->key[i] = (xs >> rot) | (xs << ((32 - rot) & 31));
+  }
+  *out = r;
+  return SPEC_OK;
+}
+
+void spec_rng_free(spec_rng* r) { delete r; }
+
+int spec_rng_next_f32(spec_rng* r, float* out, int n) {
+  if (!r || (n > 0 && !out) || n < 0) return SPEC_ERR_INVALID;
+  for (int i = 0; i < n; ++i) out[i] = rng_next_f32(r);
+  return SPEC_OK;
+}
+
+int spec_sd_sampled_round(spec_model* target, spec_model* draft, int k, float temperature, spec_rng* rng, int budget,
+                          uint32_t* commits_out, int* n_out, int* n_accepted) {
+  if (!target || !draft || !rng || !commits_out || !n_out || k < 0 || k + 1 > kMaxRows) return SPEC_ERR_INVALID;
+  if (budget < 1) return target->fail(SPEC_ERR_INVALID, "token budget must be >= 1");
+  if (target->history.size() != draft->history.size())
+    return target->fail(SPEC_ERR_INVALID, "target and draft histories differ in length");
+  if (target->cfg.vocab != draft->cfg.vocab) return target->fail(SPEC_ERR_INVALID, "target and draft vocabularies differ");
+  const int V = target->cfg.vocab;
+  k = std::min(k, budget);
+  const int pre = (int)target->history.size();
+  uint32_t drafts[kMaxRows];
+  auto draft_fail = [&](int rc) {
+    if (draft != target) target->err = draft->err;
+    return rc;
+  };
+  for (int i = 0; i < k; ++i) {
+    // A zero-draft rejection round on the draft is its sampling step: one
+    // forward of the pending token, softmax_t of the row (left in its logits
+    // buffer as probabilities), a sample with the next draw.
+    float u;
+    rng_peek_f32(rng, 1, &u);
+    uint32_t tok = 0;
+    int nc = 0, used = 0;
+    int rc = verify_rejection_core(draft, nullptr, 0, nullptr, temperature, &u, 1, 1, &tok, &nc, &used);
+    if (rc == SPEC_OK && (nc != 1 || used != 1)) rc = draft->fail(SPEC_ERR_INVALID, "draft sampling step");
+    if (rc != SPEC_OK) return draft_fail(rc);
+    for (int j = 0; j < used; ++j) rng_next_f32(rng);
+    // The row goes to the target's q buffer on the draft's stream: the next
+    // draft step (same stream) overwrites the row only after the copy.
+    DeviceGuard dg_(draft->device);
+    cudaError_t e = cudaMemcpyAsync(target->rej_q + (size_t)i * V, draft->logits, (size_t)V * 4, cudaMemcpyDefault,
+                                    draft->stream);
+    if (e != cudaSuccess) return draft_fail(draft->fail(SPEC_ERR_CUDA, cuda_msg(e, "draft distribution copy")));
+    rc = spec_observe(draft, &tok, 1);
+    if (rc != SPEC_OK) return draft_fail(rc);
+    drafts[i] = tok;
+  }
+  {
+    DeviceGuard dg_(draft->device);
+    const cudaError_t e = cudaStreamSynchronize(draft->stream);
+    if (e != cudaSuccess) return draft_fail(draft->fail(SPEC_ERR_CUDA, cuda_msg(e, "draft distribution copy")));
+  }
+  float u[kMaxRows + 1];
+  rng_peek_f32(rng, k + 1, u);
+  uint32_t commits[kMaxRows];
+  int n = 0, used = 0;
+  int rc = verify_rejection_core(target, drafts, k, nullptr, temperature, u, k + 1, budget, commits, &n, &used);
+  if (rc != SPEC_OK) return rc;
+  for (int j = 0; j < used; ++j) rng_next_f32(rng);
+  // Drafts accepted: a rejection or the bonus adds one commit beyond them; a
+  // budget cut-off does not (then every draw was an accept test).
+  const int n_acc = (used == n && n <= k) ? n : n - 1;
+  const int acc = std::min(n, k);
+  rc = spec_rollback_to(target, pre + acc);
+  if (rc == SPEC_OK && n > acc) rc = spec_observe(target, commits + acc, n - acc);
+  if (rc == SPEC_OK) rc = spec_rollback_to(draft, pre + acc);
+  if (rc == SPEC_OK && n > acc) rc = spec_observe(draft, commits + acc, n - acc);
+  if (rc != SPEC_OK) return rc;
+  for (int i = 0; i < n; ++i) commits_out[i] = commits[i];
+  *n_out = n;
+  if (n_accepted) *n_accepted = n_acc;
   return SPEC_OK;
 }
 

@@ -142,12 +142,56 @@ def vanilla_sampled_round(target, draft, k: int, temperature: float, rng, budget
     return commits, n_acc
 
 
+class NativeRng:
+    """The same seeded stream held by the library (spec_rng): what
+    spec_sd_sampled_round draws from."""
+
+    def __init__(self, seed: int):
+        import ctypes
+        from . import _lib
+        self._lib = _lib.load()
+        h = ctypes.c_void_p()
+        _lib.check(self._lib.spec_rng_create(ctypes.c_uint64(seed & 0xFFFFFFFFFFFFFFFF), ctypes.byref(h)), None)
+        self.h = h
+
+    def next_f32(self, n: int):
+        import numpy as np
+        out = np.zeros(n, dtype=np.float32)
+        from . import _lib
+        _lib.check(self._lib.spec_rng_next_f32(self.h, out.ctypes.data_as(_lib.c_f32_p), n), None)
+        return out
+
+    def close(self) -> None:
+        if self.h:
+            self._lib.spec_rng_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def vanilla_sampled_round_native(target, draft, k: int, temperature: float, rng: NativeRng,
+                                 budget: int) -> Tuple[List[int], int]:
+    """The same round as one C call (spec_sd_sampled_round): draft sampling
+    and both distributions stay on the device."""
+    import ctypes
+    out = (ctypes.c_uint32 * (k + 1))()
+    n, n_acc = ctypes.c_int(), ctypes.c_int()
+    target._check(target._lib.spec_sd_sampled_round(target._h, draft._h, k, ctypes.c_float(temperature), rng.h,
+                                                     budget, out, ctypes.byref(n), ctypes.byref(n_acc)))
+    return [int(out[i]) for i in range(n.value)], int(n_acc.value)
+
+
 def vanilla_sampled_generate(target, draft, prompt: Sequence[int], n_new: int, k: int, temperature: float,
-                             seed: int) -> Tuple[List[int], List[int]]:
+                             seed: int, native: bool = False) -> Tuple[List[int], List[int]]:
     """run_vanilla_sd at temperature > 0 with StdRng::seed_from_u64(seed)
-    (engine.rs:320-326); returns (tokens, accepted drafts per round)."""
+    (engine.rs:320-326); returns (tokens, accepted drafts per round).
+    native: each round is one spec_sd_sampled_round call."""
     from .rng import StdRng
-    rng = StdRng(seed)
+    rng = NativeRng(seed) if native else StdRng(seed)
     target.reset()
     draft.reset()
     target.observe(list(prompt))
@@ -157,7 +201,8 @@ def vanilla_sampled_generate(target, draft, prompt: Sequence[int], n_new: int, k
     while len(out) < n_new:
         budget = n_new - len(out)
         kk = min(k, budget)
-        c, n_acc = vanilla_sampled_round(target, draft, kk, temperature, rng, budget)
+        rnd = vanilla_sampled_round_native if native else vanilla_sampled_round
+        c, n_acc = rnd(target, draft, kk, temperature, rng, budget)
         out.extend(c)
         accepted.append(n_acc)
     return out, accepted

@@ -305,6 +305,33 @@ int spec_verify_rejection(spec_model* m, const uint32_t* drafts, int k, const fl
                           float temperature, const float* uniforms, int n_uniforms, int budget, uint32_t* commits,
                           int* n_commits, int* n_uniforms_used);
 
+/* ---- seeded sampling stream and the sampled SD round --------------------- */
+/* The reference's sampling RNG, StdRng::seed_from_u64(seed)
+ * (crates/speculate/src/engine.rs:320-326; rand 0.8.6 StdRng = ChaCha12 of
+ * rand_chacha 0.3.1, seeded by rand_core 0.6's PCG32 fill), drawn with
+ * gen::<f32>() = (next_u32 >> 8) * 2^-24 (sampling/tokens.rs:99-120).  Host
+ * state only: usable without a GPU. */
+typedef struct spec_rng spec_rng;
+int spec_rng_create(uint64_t seed, spec_rng** out);
+void spec_rng_free(spec_rng* r);
+/* The next n gen::<f32>() draws (consumed). */
+int spec_rng_next_f32(spec_rng* r, float* out, int n);
+/* One vanilla SD round at temperature >= 0 as one native call
+ * (methods/vanilla.rs:285-369 with the engine's seeded stream):
+ *   k' = min(k, budget) draft steps, each a forward of the draft's pending
+ *     token, softmax_t of its row and a sample with the next draw
+ *     (sampling/tokens.rs:14-55, 99-120), observed lazily; the draft's
+ *     probability rows stay on the device;
+ *   spec_verify_rejection on the target with those rows and the next draws
+ *     (one per verified position, then one for the resample or the bonus);
+ *   the stream advances by the draws used; both decoders roll back to
+ *     pre + min(n_commits, k') and observe the commits past it
+ *     (vanilla.rs:352-362: a resampled token is emitted, not observed).
+ * Writes the committed tokens (room for k+1), their count and the number of
+ * drafts accepted.  The histories must be equal on entry. */
+int spec_sd_sampled_round(spec_model* target, spec_model* draft, int k, float temperature, spec_rng* rng, int budget,
+                          uint32_t* commits_out, int* n_out, int* n_accepted);
+
 /* ---- diagnostics -------------------------------------------------------- */
 /* Device time (ms, CUDA events) of the most recent forward. */
 float spec_last_forward_ms(const spec_model* m);

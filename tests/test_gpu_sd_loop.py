@@ -96,3 +96,24 @@ def test_sampled_stream_replays_with_stdrng(pkg, accept, tiny_gguf):
         out.extend(commits)
     assert toks == out
     assert accs == racc
+
+
+@pytest.mark.parametrize("T", [1.0, 0.7])
+def test_native_sampled_round_equals_host_orchestrated(pkg, tiny_gguf, T):
+    """spec_sd_sampled_round (draft sampling and both distributions on the
+    device, the stream in the library) commits the same tokens and accepts
+    the same drafts as the same rounds orchestrated from Python (host
+    softmax and sampling of the draft rows, spec_verify_rejection fed host
+    distributions), seeded like StdRng::seed_from_u64(11)."""
+    sd = importlib.import_module("abyo-speculate_b200.sd_loop")
+    tpath, dpath = tiny_gguf("llama_q4km"), tiny_gguf("llama_hd128")
+    prompt = np.random.default_rng(44).integers(0, 1024, size=18).tolist()
+    k, n_new = 4, 40
+    runs = []
+    for native in (False, True):
+        target = pkg.B200Decoder.from_gguf(tpath, max_ctx=512)
+        draft = pkg.B200Decoder.from_gguf(dpath, max_ctx=512)
+        toks, accs = sd.vanilla_sampled_generate(target, draft, prompt, n_new, k, T, seed=11, native=native)
+        runs.append((toks, accs, target.history(), draft.history(), target.kv_len()))
+    assert len(runs[0][0]) == n_new and sum(runs[0][1]) > 0
+    assert runs[0] == runs[1]

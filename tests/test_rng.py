@@ -66,3 +66,16 @@ def test_seed_from_u64_pcg32_fill():
     a, b = r.StdRng(42), r.StdRng(42)
     assert [a.next_u32() for _ in range(70)] == [b.next_u32() for _ in range(70)]
     assert r.StdRng(43).next_u32() != r.StdRng(42).next_u32()
+
+
+def test_library_stream_equals_restatement(pkg):
+    """spec_rng (the C++ stream spec_sd_sampled_round draws from) gives the
+    same gen::<f32>() values as rng.StdRng for several seeds, across the
+    four-block refills."""
+    sd = importlib.import_module("abyo-speculate_b200.sd_loop")
+    for seed in (0, 7, 42, 2**63 + 12345):
+        want = _rng().StdRng(seed).peek_f32(300)
+        r = sd.NativeRng(seed)
+        got = np.concatenate([r.next_f32(1), r.next_f32(63), r.next_f32(236)])
+        r.close()
+        assert np.array_equal(got.view(np.uint32), want.view(np.uint32)), seed
