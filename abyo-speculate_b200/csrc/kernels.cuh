@@ -258,6 +258,9 @@ struct FwdParams {
   // griddepcontrol.launch_dependents at kernel entry (cooperative forward
   // launches only; see fwd_kernel).
   int trigger_at_start = 0;
+  // Walk a chunk that starts inside a group from the next group's start and
+  // take the piece ending the first group last (see SeqIt in qgemv.cu).
+  int rotate = 1;
 };
 
 // The instantiation is picked by (format set, nt_for_rows(M)); all ops of

@@ -228,6 +228,7 @@ struct spec_model {
   bool attn_trigger = true;         // a launch's attention tail overlaps the next launch (PDL trigger)
   bool attn_kernels_pdl = true;     // programmatic launch of the standalone attention kernels
   bool coop = true;                 // multi-op forward launches are cooperative (SPEC_B200_NO_COOP clears)
+  bool rotate = true;               // chunk walks take a group's tail piece last (SPEC_B200_NO_ROTATE clears)
   bool early_trigger = true;        // cooperative forward launches trigger dependents at entry (SPEC_B200_NO_EARLY_TRIGGER)
   FwdOp* single_op = nullptr;       // device slot for one-op launches
   FwdOp* single_op_host = nullptr;  // pinned staging
@@ -869,6 +870,7 @@ cudaError_t launch_slice(spec_model* m, const spec_model::Schedule& sc, int li, 
   fp.epoch = &m->step_dev->epoch;
   fp.trigger_after_gemv = (pdl && m->attn_trigger) ? 1 : 0;
   fp.trigger_at_start = (pdl && fp.cooperative && m->early_trigger) ? 1 : 0;
+  fp.rotate = m->rotate ? 1 : 0;
   return launch_fwd(fp, m->fmt_set, M, m->stream, pdl);
 }
 
@@ -1239,6 +1241,7 @@ int init_device(spec_model* m, const spec_load_opts* opts) {
   if (getenv("SPEC_B200_NO_ATTN_TRIGGER")) m->attn_trigger = false;
   if (getenv("SPEC_B200_ATTN_KERNELS_NO_PDL")) m->attn_kernels_pdl = false;
   if (getenv("SPEC_B200_NO_COOP")) m->coop = false;
+  if (getenv("SPEC_B200_NO_ROTATE")) m->rotate = false;
   if (getenv("SPEC_B200_NO_EARLY_TRIGGER")) m->early_trigger = false;
   if (const char* env = getenv("SPEC_B200_L2_AHEAD")) m->l2_ahead = atoi(env);
   cudaError_t e = cudaSetDevice(m->device);

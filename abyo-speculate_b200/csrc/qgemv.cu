@@ -892,11 +892,23 @@ SPEC_DEV int chunk_of(const QmvParams& q, int s) { return (int)(((long long)(s +
 
 // Walks (op, chunk, stage) for CTA c in schedule order: chunks c, c+G, ...
 // The producer's walks skip the attention ops (no weight stream).
+// A GEMV chunk [s0, s_end) that starts inside a group and reaches the next
+// group's start b is walked [b, s_end) then [s0, b) (FwdParams::rotate): the
+// piece that ends the first group -- the one whose CTA most likely arrives
+// last and runs the group's reduction and epilogue -- comes after this
+// CTA's other pieces of the op, so that epilogue delays none of them.  Each
+// piece's own stages stay in order, so no sum changes.
 struct SeqIt {
   int op = 0, k = 0, s = 0, s_end = 0;
+  int s0 = 0, b = 0, v = 0, len = 0;  // chunk start, walk start, position in the walk, chunk length
   bool valid = false;
   bool gemv_only = false;
 };
+// Stage at position v of the chunk's walk.
+SPEC_DEV int seq_stage(const SeqIt& it, int v) {
+  const int l1 = it.s_end - it.b;
+  return v < l1 ? it.b + v : it.s0 + (v - l1);
+}
 
 SPEC_DEV void seq_settle(const FwdParams& P, int c, int G, SeqIt& it) {
   // Move to the first non-empty chunk at or after (it.op, it.k).
@@ -909,9 +921,18 @@ SPEC_DEV void seq_settle(const FwdParams& P, int c, int G, SeqIt& it) {
     const QmvParams& q = P.ops[it.op].q;
     const int i = c + it.k * G;
     if (i < q.chunks) {
-      it.s = chunk_start(q, i);
+      it.s0 = chunk_start(q, i);
       it.s_end = chunk_start(q, i + 1);
-      if (it.s < it.s_end) {
+      if (it.s0 < it.s_end) {
+        it.b = it.s0;
+        if (P.rotate && P.ops[it.op].kind == OPK_GEMV) {
+          const StageLoc L = locate(q, it.s0);
+          const int nb = L.gstart + q.seg[L.seg].k_tiles;  // the next group's first stage
+          if (L.kt != 0 && nb < it.s_end) it.b = nb;
+        }
+        it.v = 0;
+        it.len = it.s_end - it.s0;
+        it.s = seq_stage(it, 0);
         it.valid = true;
         return;
       }
@@ -929,9 +950,17 @@ SPEC_DEV void seq_begin(const FwdParams& P, int c, int G, SeqIt& it, bool gemv_o
   seq_settle(P, c, G, it);
 }
 SPEC_DEV void seq_next(const FwdParams& P, int c, int G, SeqIt& it) {
-  if (++it.s < it.s_end) return;
+  if (++it.v < it.len) {
+    it.s = seq_stage(it, it.v);
+    return;
+  }
   ++it.k;
   seq_settle(P, c, G, it);
+}
+// Moves past the rest of the current chunk.
+SPEC_DEV void seq_next_chunk(const FwdParams& P, int c, int G, SeqIt& it) {
+  it.v = it.len - 1;
+  seq_next(P, c, G, it);
 }
 
 SPEC_DEV bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
@@ -1325,7 +1354,8 @@ __global__ void __launch_bounds__(FGeo<SET, NT>::THREADS,
         seq_begin(P, c, G, it, true);
         while (it.valid) {
           const QmvParams& q = P.ops[it.op].q;
-          for (int s = it.s; s < it.s_end; ++s, ++pos) {
+          for (int v = 0; v < it.len; ++v, ++pos) {
+            const int s = seq_stage(it, v);
             const StageLoc L = locate(q, s);
             const int st = pos % D;
             if (fresh && uses[buf] > 0 && ok) {
@@ -1355,15 +1385,14 @@ __global__ void __launch_bounds__(FGeo<SET, NT>::THREADS,
               mbar_arrive(&empty[st]);
             }
             fresh = false;
-            if (L.kt == q.seg[L.seg].k_tiles - 1 || s == it.s_end - 1) {  // end of a piece
+            if (L.kt == q.seg[L.seg].k_tiles - 1 || s == it.s_end - 1 || v == it.len - 1) {  // end of a piece
               umma_commit(&accfull[buf]);
               ++uses[buf];
               buf ^= 1;
               fresh = true;
             }
           }
-          it.s = it.s_end - 1;
-          seq_next(P, c, G, it);
+          seq_next_chunk(P, c, G, it);
         }
         umma_commit(&issdone);
       }
@@ -1393,7 +1422,8 @@ __global__ void __launch_bounds__(FGeo<SET, NT>::THREADS,
       for (int nt = 0; nt < NT; ++nt)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
-    for (int s = it.s; s < it.s_end; ++s, ++pos) {
+    for (int v = 0; v < it.len; ++v, ++pos) {
+      const int s = seq_stage(it, v);
       const StageLoc L = locate(q, s);
       const int kts = q.seg[L.seg].k_tiles;
       const int st = pos % D;
@@ -1413,7 +1443,7 @@ __global__ void __launch_bounds__(FGeo<SET, NT>::THREADS,
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[st]);
       }
-      if (L.kt == kts - 1 || s == it.s_end - 1) {  // end of a piece
+      if (L.kt == kts - 1 || s == it.s_end - 1 || v == it.len - 1) {  // end of a piece
         if constexpr (UM) {
           // The piece's accumulator: wait for its MMAs, read this warp's 32
           // rows, and hand the buffer back to the issuer.  A piece whose MMAs
@@ -1458,8 +1488,7 @@ __global__ void __launch_bounds__(FGeo<SET, NT>::THREADS,
             for (int i = 0; i < 4; ++i) acc[rt][nt][i] = 0.f;
       }
     }
-    it.s = it.s_end - 1;
-    seq_next(P, c, G, it);
+    seq_next_chunk(P, c, G, it);
   }
   if constexpr (UM) {
     // Every consumer warp's TMEM reads are done and every MMA the issuer
@@ -1486,10 +1515,9 @@ __global__ void __launch_bounds__(FGeo<SET, NT>::THREADS,
       if (threadIdx.x == 0) atomicOr(Pg.err, DEV_ERR_BAD_ARGUMENT);
       break;
     }
-    for (int u = it.s; u < it.s_end; ++u)
+    for (int u = it.s0; u < it.s_end; ++u)
       attn_op_unit<NT>(s_ops, Pg.done, Pg.gflags, Pg.flag_stride, Pg.err, it.op, u, ring, FG::RING, epoch);
-    it.s = it.s_end - 1;
-    seq_next(P, c, G, it);
+    seq_next_chunk(P, c, G, it);
   }
 }
 

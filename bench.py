@@ -569,6 +569,25 @@ def run_sd_shared(pkg, local, prompt):
     t0 = time.perf_counter()
     toks, acc = sd.vanilla_greedy_generate(target, draft, prompt, SD_NEW_TOKENS, K_DRAFT, observe_prompt=False)
     el = time.perf_counter() - t0
+    # The seeded temperature-1.0 round: StdRng::seed_from_u64(7)
+    # in the library, each round one spec_sd_sampled_round call.
+    target.rollback_to(KV_LEN)
+    draft.rollback_to(KV_LEN)
+    rng = sd.NativeRng(7)
+    for _ in range(3):  # warm-up rounds (graph capture of the draft's M=1 forward)
+        sd.vanilla_sampled_round_native(target, draft, K_DRAFT, 1.0, rng, K_DRAFT + 1)
+    target.rollback_to(KV_LEN)
+    draft.rollback_to(KV_LEN)
+    rng = sd.NativeRng(7)
+    s_toks, s_acc = [], []
+    t1 = time.perf_counter()
+    while len(s_toks) < SD_NEW_TOKENS:
+        budget = SD_NEW_TOKENS - len(s_toks)
+        c, na = sd.vanilla_sampled_round_native(target, draft, min(K_DRAFT, budget), 1.0, rng, budget)
+        s_toks += c
+        s_acc.append(na)
+    el_s = time.perf_counter() - t1
+    rng.close()
     target.close()
     draft.close()
     return {"tok_per_s": round(len(toks) / el, 2), "tokens": len(toks), "rounds": len(acc),
@@ -578,7 +597,12 @@ def run_sd_shared(pkg, local, prompt):
                      "(same seed); target = configs[1] shape with layers 2-31's o/down weights at sigma 0.02 x "
                      f"{SHARED_DAMP}",
             "note": "greedy vanilla SD (spec_sd_greedy_round), 2048-token prompt, wall clock per round incl. "
-                    "host calls"}
+                    "host calls",
+            "sampled_t1": {"tok_per_s": round(len(s_toks) / el_s, 2), "tokens": len(s_toks), "rounds": len(s_acc),
+                           "ms_per_round": round(el_s / len(s_acc) * 1e3, 3),
+                           "mean_accepted": round(float(np.mean(s_acc)), 3),
+                           "note": "temperature 1.0, seed 7 (StdRng::seed_from_u64 restated in the library), one "
+                                   "spec_sd_sampled_round per round, same models and prompt"}}
 
 
 def run_b200(args, ws, rank, local, dist):
