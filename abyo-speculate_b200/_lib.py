@@ -134,6 +134,12 @@ SIGNATURES = [
     ("spec_eagle_draft", ctypes.c_int,
      [ctypes.c_void_p, c_f32_p, ctypes.c_uint32, ctypes.c_int, ctypes.c_int, ctypes.c_int,
       ctypes.POINTER(ctypes.c_int32), c_f32_p]),
+    ("spec_eagle_build_tree", ctypes.c_int,
+     [ctypes.c_uint32, c_i32_p, c_f32_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, c_u32_p, c_i32_p, ctypes.c_int,
+      c_int_p]),
+    ("spec_eagle_round", ctypes.c_int,
+     [ctypes.c_void_p, c_f32_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int, c_u32_p, ctypes.c_int,
+      c_u32_p, c_int_p, c_f32_p, c_int_p]),
     ("spec_medusa_attach", ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
     ("spec_medusa_attach_synthetic", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_uint64]),
     ("spec_medusa_topk", ctypes.c_int,

@@ -3213,9 +3213,10 @@ int spec_sd_sampled_round(spec_model* target, spec_model* draft, int k, float te
   return SPEC_OK;
 }
 
-int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
-                            int32_t* best_path, int* path_len, uint32_t* bonus) {
-  if (!m || !tokens || !parents || !best_path || !path_len || !bonus) return SPEC_ERR_INVALID;
+// spec_verify_tree_greedy; with `hidden` the tree forward also leaves every
+// node's final hidden row in m->hidden_out (device).
+int verify_tree_greedy_core(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, int32_t* best_path,
+                            int* path_len, uint32_t* bonus, bool hidden) {
   DeviceGuard dg_(m->device);
   m->last_valid = false;
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
@@ -3227,7 +3228,7 @@ int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t
   const int pre = m->cache_len;
   const int prefix = (int)m->history.size() - 1;
   if (prefix > pre) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
-  rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS);
+  rc = tree_forward(m, tokens, parents, n, prefix, hidden ? (F_LOGITS | F_HIDDEN) : F_LOGITS);
   if (rc == SPEC_OK) {
     cudaError_t e = launch_row_argmax(m->logits, n, m->cfg.vocab, m->argmax_dev, nullptr,
                                       m->argmax_slots, m->argmax_counters, m->stream);
@@ -3262,6 +3263,170 @@ int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t
   *path_len = (int)best.size();
   *bonus = (uint32_t)m->argmax_host[best.back()];
   return SPEC_OK;
+}
+
+int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
+                            int32_t* best_path, int* path_len, uint32_t* bonus) {
+  if (!m || !tokens || !parents || !best_path || !path_len || !bonus) return SPEC_ERR_INVALID;
+  return verify_tree_greedy_core(m, tokens, parents, n, best_path, path_len, bonus, false);
+}
+
+// The EAGLE-2 round tree (eagle.rs:584-593): the Cartesian product of the
+// draft steps' top-k (medusa.rs:172-189: BFS layers, every candidate of step
+// d under every node of layer d, parents in layer order), pruned to at most
+// max_nodes by path log-prob (eagle.rs:763-843).  In that tree node p of
+// layer D (0-based position) has parent p / k of layer D-1 and candidate
+// p % k of step D-1, so nothing is materialised but the scores.  The score
+// is the f32 sum of the candidates' log-probs deepest step first (:800-812);
+// the first max_nodes - 1 of the stable descending sort (:815) are the
+// max_nodes - 1 largest under (score desc, index asc); their ancestors are
+// added (:822-827) and the kept nodes keep their BFS order, which is the
+// depth order (:829-842).
+int spec_eagle_build_tree(uint32_t root, const int32_t* ids, const float* logprobs, int depth, int k, int max_nodes,
+                          uint32_t* tokens_out, int32_t* parents_out, int cap, int* n_out) {
+  if (!ids || !tokens_out || !parents_out || !n_out || depth < 0 || k < 1 || cap < 1 ||
+      (max_nodes > 0 && !logprobs))
+    return SPEC_ERR_INVALID;
+  std::vector<int64_t> start(depth + 2, 0);  // first index of each layer
+  int64_t width = 1;
+  for (int d = 0; d <= depth; ++d) {
+    start[d + 1] = start[d] + width;
+    if (start[d + 1] > (int64_t)1 << 26) {
+      set_thread_error("spec_eagle_build_tree: the Cartesian tree exceeds 2^26 nodes");
+      return SPEC_ERR_UNSUPPORTED;
+    }
+    width *= k;
+  }
+  const int64_t N = start[depth + 1];
+  auto layer_of = [&](int64_t i) {
+    int d = 0;
+    while (start[d + 1] <= i) ++d;
+    return d;
+  };
+  std::vector<char> keep;
+  if (max_nodes > 0 && N > max_nodes) {
+    std::vector<float> score((size_t)(N - 1));
+    for (int D = 1; D <= depth; ++D)
+      for (int64_t p = 0; p < start[D + 1] - start[D]; ++p) {
+        float sc = 0.f;
+        int64_t q = p;
+        for (int d = D - 1; d >= 0; --d) {
+          sc += logprobs[(size_t)d * k + (q % k)];
+          q /= k;
+        }
+        score[(size_t)(start[D] + p - 1)] = sc;
+      }
+    std::vector<int32_t> order((size_t)(N - 1));
+    std::iota(order.begin(), order.end(), 1);
+    const int64_t want = std::min<int64_t>(max_nodes - 1, N - 1);
+    auto before = [&](int32_t a, int32_t b) {
+      const float sa = score[(size_t)a - 1], sb = score[(size_t)b - 1];
+      return sa > sb || (!(sb > sa) && a < b);
+    };
+    std::nth_element(order.begin(), order.begin() + want, order.end(), before);
+    keep.assign((size_t)N, 0);
+    keep[0] = 1;
+    for (int64_t j = 0; j < want; ++j) keep[(size_t)order[(size_t)j]] = 1;
+    for (int64_t i = N - 1; i >= 1; --i)
+      if (keep[(size_t)i]) {
+        const int D = layer_of(i);
+        keep[(size_t)(start[D - 1] + (i - start[D]) / k)] = 1;
+      }
+  } else {
+    keep.assign((size_t)N, 1);
+  }
+  std::vector<int64_t> new_index((size_t)N, -1);
+  int n = 0;
+  for (int64_t i = 0; i < N; ++i) {
+    if (!keep[(size_t)i]) continue;
+    if (n >= cap) {
+      set_thread_error("spec_eagle_build_tree: the tree has more nodes than the output capacity");
+      return SPEC_ERR_UNSUPPORTED;
+    }
+    new_index[(size_t)i] = n;
+    if (i == 0) {
+      tokens_out[0] = root;
+      parents_out[0] = 0;
+    } else {
+      const int D = layer_of(i);
+      const int64_t p = i - start[D];
+      tokens_out[n] = (uint32_t)ids[(size_t)(D - 1) * k + (p % k)];
+      parents_out[n] = (int32_t)new_index[(size_t)(start[D - 1] + p / k)];
+    }
+    ++n;
+  }
+  *n_out = n;
+  return SPEC_OK;
+}
+
+int spec_eagle_round(spec_model* m, const float* hidden, int depth, int top_k, int max_tree_nodes, int strict_root,
+                     const uint32_t* eos_ids, int n_eos, uint32_t* commits_out, int* n_out, float* hidden_out,
+                     int* stop) {
+  if (!m || !hidden || !commits_out || !n_out || !hidden_out || !stop || depth < 1 || top_k < 1 || n_eos < 0 ||
+      (n_eos > 0 && !eos_ids))
+    return SPEC_ERR_INVALID;
+  DeviceGuard dg_(m->device);
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "EAGLE round with empty history");
+  const uint32_t root = m->history.back();
+  // 1-2. Draft loop from the target's hidden row at the history length.
+  std::vector<int32_t> ids((size_t)depth * top_k);
+  std::vector<float> lps((size_t)depth * top_k);
+  int rc = spec_eagle_draft(m, hidden, root, (int)m->history.size(), depth, top_k, ids.data(), lps.data());
+  if (rc != SPEC_OK) return rc;
+  // 3. The tree.
+  uint32_t tok[kMaxRows];
+  int32_t par[kMaxRows];
+  int n = 0;
+  rc = spec_eagle_build_tree(root, ids.data(), lps.data(), depth, top_k, max_tree_nodes, tok, par, kMaxRows, &n);
+  if (rc != SPEC_OK) return m->fail(rc, g_load_error.empty() ? "EAGLE tree" : g_load_error);
+  // 4-6. Tree forward keeping KV, greedy walk, bonus (per-node hidden kept).
+  int32_t best[kMaxRows];
+  int len = 0;
+  uint32_t bonus = 0;
+  rc = verify_tree_greedy_core(m, tok, par, n, best, &len, &bonus, true);
+  if (rc != SPEC_OK) return rc;
+  auto is_eos = [&](uint32_t t) {
+    for (int i = 0; i < n_eos; ++i)
+      if (eos_ids[i] == t) return true;
+    return false;
+  };
+  int nc = 0;
+  for (int i = 1; i < len; ++i) commits_out[nc++] = tok[best[i]];
+  commits_out[nc++] = bonus;
+  int eos_at = -1;
+  for (int i = 0; i < nc; ++i)
+    if (is_eos(commits_out[i])) {
+      eos_at = i;
+      break;
+    }
+  if (eos_at >= 0) nc = eos_at + 1;
+  *n_out = nc;
+  *stop = eos_at >= 0 ? 1 : 0;
+  // 7. Commit the accepted path.
+  if (eos_at >= 0 && eos_at < len - 1) {
+    // An EOS on the accepted path: keep the root and the path up to it.
+    return spec_commit_tree_path(m, tok, par, n, best, eos_at + 2);
+  }
+  const int deepest = best[len - 1];
+  int bn = -1;
+  if (!strict_root)
+    for (int i = 1; i < n; ++i)
+      if (par[i] == deepest && tok[i] == bonus) {
+        bn = i;
+        break;
+      }
+  if (bn >= 0) {
+    // The bonus is a child of the deepest accepted node: its KV row is in
+    // the cache already and its hidden row comes from the tree forward.
+    const cudaError_t e = cudaMemcpy(hidden_out, m->hidden_out + (size_t)bn * m->cfg.hidden,
+                                     (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "tree hidden row"));
+    best[len++] = bn;
+    return spec_commit_tree_path(m, tok, par, n, best, len);
+  }
+  rc = spec_commit_tree_path(m, tok, par, n, best, len);
+  if (rc == SPEC_OK) rc = spec_observe_returning_last_hidden(m, &bonus, 1, hidden_out);
+  return rc;
 }
 
 float spec_last_forward_ms(const spec_model* m) { return m ? m->last_ms : 0.f; }

@@ -257,6 +257,21 @@ class B200Decoder:
                                                _ptr(ids, ctypes.c_int32), _ptr(lp, ctypes.c_float)))
         return ids, lp
 
+    def eagle_round(self, hidden: np.ndarray, depth: int, top_k: int, max_tree_nodes: int = 0,
+                    strict_root: bool = False, eos: Sequence[int] = ()) -> Tuple[List[int], np.ndarray, bool]:
+        """One greedy EAGLE-2 round (eagle.rs:531-731) in one call:
+        (committed tokens, the next round's hidden row, stop)."""
+        h = np.ascontiguousarray(np.asarray(hidden, dtype=np.float32).reshape(-1))
+        e = np.ascontiguousarray(np.asarray(list(eos), dtype=np.uint32))
+        out = np.zeros(depth + 1, dtype=np.uint32)
+        nxt = np.zeros(self.hidden_size(), dtype=np.float32)
+        n, stop = ctypes.c_int(), ctypes.c_int()
+        self._check(self._lib.spec_eagle_round(self._h, _ptr(h, ctypes.c_float), depth, top_k, max_tree_nodes,
+                                               1 if strict_root else 0, _ptr(e, ctypes.c_uint32), int(e.size),
+                                               _ptr(out, ctypes.c_uint32), ctypes.byref(n), _ptr(nxt, ctypes.c_float),
+                                               ctypes.byref(stop)))
+        return [int(t) for t in out[:n.value]], nxt, bool(stop.value)
+
     def medusa_attach(self, res_w: Sequence[Sequence[np.ndarray]], res_b: Sequence[Sequence[np.ndarray]],
                       out_w: Sequence[np.ndarray]) -> None:
         """Medusa heads (medusa.rs:509-584): res_w[head][layer] uint16 BF16 bits

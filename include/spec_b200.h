@@ -232,6 +232,35 @@ int spec_eagle_attach_synthetic(spec_model* m, uint64_t seed);
  * logprobs_out[depth][k] = logit - logsumexp(row).  depth <= 64. */
 int spec_eagle_draft(spec_model* m, const float* hidden, uint32_t root, int position, int depth, int k,
                      int32_t* ids_out, float* logprobs_out);
+/* The round's draft tree (methods/eagle.rs:584-593, host code): the
+ * Cartesian product of the depth steps' top-k (medusa.rs:172-189, BFS
+ * layers), and when max_nodes > 0 and the product is larger, its pruning by
+ * path log-prob (eagle.rs:763-843: f32 sums deepest step first, stable
+ * descending order, the best max_nodes - 1 plus their ancestors, BFS order).
+ * ids / logprobs: [depth][k] as spec_eagle_draft writes them.  Writes the
+ * tree as tokens / parents (parents[0] = 0) and its size; a tree larger than
+ * cap, or a product above 2^26 nodes, returns SPEC_ERR_UNSUPPORTED. */
+int spec_eagle_build_tree(uint32_t root, const int32_t* ids, const float* logprobs, int depth, int k, int max_nodes,
+                          uint32_t* tokens_out, int32_t* parents_out, int cap, int* n_out);
+/* One EAGLE-2 round at temperature 0 as one native call (run_eagle's loop
+ * body, methods/eagle.rs:531-731), on a target with an attached EAGLE head:
+ *   the draft loop from `hidden` (the target's last hidden row [H]) with the
+ *   last committed token as root; the tree of spec_eagle_build_tree (at most
+ *   SPEC_MAX_ROWS nodes); the tree forward keeping KV and the greedy walk of
+ *   spec_verify_tree_greedy; committed = the accepted path's tokens + the
+ *   bonus, cut after the first token of eos_ids;
+ *   the KV commit (:680-727): an EOS on the path keeps the path up to it;
+ *   otherwise, unless strict_root, a child of the deepest accepted node
+ *   holding the bonus joins the commit and its tree hidden row is the next
+ *   hidden; else the path is committed and the bonus observed.
+ * strict_root only disables that shortcut: the backend's tree row 0 equals
+ * next_logits bit for bit, so the reference's strict root logits change
+ * nothing else.  Writes commits_out (room for depth + 1), *n_out,
+ * hidden_out [H] (the next round's hidden; not written when an EOS on the
+ * path stops the round) and *stop (an EOS was committed). */
+int spec_eagle_round(spec_model* m, const float* hidden, int depth, int top_k, int max_tree_nodes, int strict_root,
+                     const uint32_t* eos_ids, int n_eos, uint32_t* commits_out, int* n_out, float* hidden_out,
+                     int* stop);
 
 /* ---- Medusa draft heads on the device (methods/medusa.rs) -------------------
  * Each head (MedusaHeadModule, medusa.rs:509-584) maps the target's last

@@ -140,3 +140,76 @@ class EagleOracle:
         if self.t.bf16:
             return self._op(x)
         return np.asarray(x, dtype=np.float32).astype(np.float16).astype(np.float64)
+
+
+# ---------------------------------------------------------------------------
+# EAGLE-2 round tree: Cartesian product of the draft steps' top-k, pruned by
+# path log-prob (test infrastructure: the checker of spec_eagle_build_tree).
+# ---------------------------------------------------------------------------
+def build_cartesian_tree(root: int, step_top_k: Sequence[Sequence[int]]) -> List[Tuple[int, int]]:
+    """medusa.rs:172-189 (build_cartesian_tree): BFS parent table; layer h+1 =
+    every candidate of step h under every node of layer h, parents in layer
+    order, candidates in their order.  Entries are (parent, token); entry 0
+    is (0, root)."""
+    nodes = [(0, int(root))]
+    prev = [0]
+    for cands in step_top_k:
+        nxt = []
+        for p in prev:
+            for c in cands:
+                nodes.append((p, int(c)))
+                nxt.append(len(nodes) - 1)
+        prev = nxt
+    return nodes
+
+
+def prune_cartesian_tree(nodes: List[Tuple[int, int]], step_log_probs: Sequence[Sequence[float]],
+                         max_total_nodes: int) -> List[Tuple[int, int]]:
+    """eagle.rs:763-843 (prune_cartesian_tree): a tree of at most
+    max_total_nodes entries returned as is; otherwise every non-root node is
+    scored by the f32 sum of the per-step log-probs of its candidates,
+    deepest step first (:800-812), nodes are stably sorted by descending
+    score (:815), the root and the first max_total_nodes - 1 are kept, every
+    kept node's ancestors are added (:822-827), and the kept nodes are
+    re-emitted ordered by depth, index order within a depth (:829-842)."""
+    n = len(nodes)
+    if n <= max_total_nodes:
+        return list(nodes)
+    parent = np.array([p for p, _ in nodes], dtype=np.int64)
+    depth = np.zeros(n, dtype=np.int64)
+    for i in range(1, n):  # parents precede their children
+        depth[i] = depth[parent[i]] + 1
+    # Candidate index = rank among the parent's children in index order.
+    cand = np.zeros(n, dtype=np.int64)
+    seen: Dict[int, int] = {}
+    for i in range(1, n):
+        p = int(parent[i])
+        cand[i] = seen.get(p, 0)
+        seen[p] = cand[i] + 1
+    width = max(len(v) for v in step_log_probs)
+    lp = np.full((len(step_log_probs), width), np.nan, dtype=np.float32)
+    for d, v in enumerate(step_log_probs):
+        lp[d, :len(v)] = np.asarray(v, dtype=np.float32)
+    # s = ((0 + lp[D-1][c_i]) + lp[D-2][c_parent]) + ...: one f32 add per
+    # level, every node at once.
+    idx = np.arange(1, n)
+    cur = idx.copy()
+    dep = depth[idx]
+    s = np.zeros(n - 1, dtype=np.float32)
+    for t in range(int(dep.max())):
+        live = dep > t
+        s[live] = (s[live] + lp[dep[live] - 1 - t, cand[cur[live]]]).astype(np.float32)
+        cur[live] = parent[cur[live]]
+    order_by_score = np.argsort(-s, kind="stable")  # stable: equal scores keep index order
+    want = min(max_total_nodes - 1, n - 1)
+    keep = np.zeros(n, dtype=bool)
+    keep[0] = True
+    keep[idx[order_by_score[:want]]] = True
+    for i in range(n - 1, 0, -1):
+        if keep[i]:
+            keep[parent[i]] = True
+    depth = depth.tolist()
+    parent = parent.tolist()
+    order = sorted((i for i in range(n) if keep[i]), key=lambda i: depth[i])
+    new_index = {old: new for new, old in enumerate(order)}
+    return [(new_index[parent[old] if old else 0], nodes[old][1]) for old in order]

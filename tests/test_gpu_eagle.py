@@ -75,3 +75,74 @@ def test_eagle_errors_and_synthetic(pkg, tiny_gguf):
         dec.eagle_draft(h, 1, 0, 65, 8)
     with pytest.raises(pkg.SamplingError):
         dec.eagle_draft(h, 10 ** 6, 0, 2, 8)
+
+
+def _py_eagle_round(pkg, dec, hidden, depth, k, max_nodes, strict, eos):
+    """run_eagle's loop body (eagle.rs:531-731, greedy) written over the
+    trait calls, with the tree of oracle/eagle.py: the counterpart of
+    spec_eagle_round."""
+    eo = importlib.import_module("oracle.eagle")
+    root, pos = dec.history()[-1], dec.history_len()
+    ids, lp = dec.eagle_draft(hidden, root, pos, depth, k)
+    nodes = eo.build_cartesian_tree(root, ids.tolist())
+    if max_nodes:
+        nodes = eo.prune_cartesian_tree(nodes, lp.tolist(), max_nodes)
+    tree = pkg.DraftTree.from_parent_table(nodes)
+    _, hid = dec.tree_logits_keep_kv(tree)
+    best, bonus = dec.verify_tree_greedy(tree)  # the same tree forward again, then the walk
+    committed = [tree.token_at(i) for i in best[1:]] + [int(bonus)]
+    eos_at = next((i for i, t in enumerate(committed) if t in eos), None)
+    if eos_at is not None:
+        committed = committed[:eos_at + 1]
+    if eos_at is not None and eos_at < len(best) - 1:
+        dec.commit_tree_path(tree, best[:eos_at + 2])
+        return committed, None, True, False
+    bn = None
+    if not strict:
+        bn = next((i for i in range(1, len(tree)) if tree.parent_of(i) == best[-1] and tree.token_at(i) == bonus),
+                  None)
+    if bn is not None:
+        dec.commit_tree_path(tree, list(best) + [bn])
+        return committed, hid[bn].copy(), eos_at is not None, True
+    dec.commit_tree_path(tree, best)
+    return committed, dec.observe_returning_last_hidden([int(bonus)]), eos_at is not None, False
+
+
+@pytest.mark.parametrize("depth,k,max_nodes,strict", [(2, 4, 0, False), (4, 4, 40, False), (3, 8, 60, True)])
+def test_native_eagle_round_equals_trait_calls(pkg, tiny_gguf, depth, k, max_nodes, strict):
+    """spec_eagle_round (draft loop, tree, tree forward, walk, KV commit in
+    one call) against the same round made of the trait calls in the
+    reference's order: identical commits, next hidden rows (bit for bit),
+    histories and KV lengths over several rounds, with an EOS id taken from
+    a dry run so one round stops on it."""
+    path = tiny_gguf("llama_q4km")
+    rng = np.random.default_rng(5)
+    prompt = rng.integers(0, 1024, size=21).tolist()
+    dec_probe = pkg.B200Decoder.from_gguf(path, max_ctx=256)
+    dec_probe.eagle_attach_synthetic(99)
+    hid = dec_probe.observe_returning_last_hidden(prompt)
+    dry = []
+    for _ in range(6):
+        c, hid, _ = dec_probe.eagle_round(hid, depth, k, max_nodes, strict)
+        dry.append(c)
+    eos = {dry[3][-1]}
+    runs = []
+    for native in (True, False):
+        dec = pkg.B200Decoder.from_gguf(path, max_ctx=256)
+        dec.eagle_attach_synthetic(99)
+        hid = dec.observe_returning_last_hidden(prompt)
+        rec = []
+        for _ in range(6):
+            if native:
+                c, nh, stop = dec.eagle_round(hid, depth, k, max_nodes, strict, eos)
+            else:
+                c, nh, stop, _ = _py_eagle_round(pkg, dec, hid, depth, k, max_nodes, strict, eos)
+            rec.append((c, stop, dec.history(), dec.kv_len()))
+            if stop:
+                break
+            assert nh is not None
+            rec.append(nh.view(np.uint32).tolist())
+            hid = nh
+        runs.append(rec)
+    assert runs[0] == runs[1]
+    assert any(r[1] for r in runs[0] if isinstance(r, tuple)), "the EOS round stops"
