@@ -163,6 +163,8 @@ SIGNATURES = [
       ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     ("spec_verify_tree_greedy", ctypes.c_int,
      [ctypes.c_void_p, c_u32_p, c_i32_p, ctypes.c_int, c_i32_p, c_int_p, c_u32_p]),
+    ("spec_verify_tree_typical", ctypes.c_int,
+     [ctypes.c_void_p, c_u32_p, c_i32_p, ctypes.c_int, ctypes.c_float, ctypes.c_float, c_i32_p, c_int_p, c_u32_p]),
     ("spec_last_forward_ms", ctypes.c_float, [ctypes.c_void_p]),
     ("spec_kernels_per_forward", ctypes.c_int, [ctypes.c_void_p, ctypes.c_int]),
     ("spec_cuda_stream", ctypes.c_void_p, [ctypes.c_void_p]),

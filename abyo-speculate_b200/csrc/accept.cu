@@ -90,65 +90,98 @@ SPEC_DEV float block_seq_sum(const float* x, int n, float* buf, float* bcast) {
   return s;
 }
 
+// Thread 0: s += buf[0..len) in order, every partial sum stored to
+// out[0..len) (16-byte aligned).  Same add sequence as add_chunk.
+SPEC_DEV float add_chunk_pref(float s, const float* buf, int len, float* out) {
+  const int n16 = len & ~15;
+  if (n16) {
+    float4 a0 = *reinterpret_cast<const float4*>(buf), a1 = *reinterpret_cast<const float4*>(buf + 4),
+           a2 = *reinterpret_cast<const float4*>(buf + 8), a3 = *reinterpret_cast<const float4*>(buf + 12);
+    for (int i = 0; i < n16; i += 16) {
+      const float4 b[4] = {a0, a1, a2, a3};
+      if (i + 16 < n16) {
+        a0 = *reinterpret_cast<const float4*>(buf + i + 16);
+        a1 = *reinterpret_cast<const float4*>(buf + i + 20);
+        a2 = *reinterpret_cast<const float4*>(buf + i + 24);
+        a3 = *reinterpret_cast<const float4*>(buf + i + 28);
+      }
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float4 o;
+        s = __fadd_rn(s, b[q].x); o.x = s;
+        s = __fadd_rn(s, b[q].y); o.y = s;
+        s = __fadd_rn(s, b[q].z); o.z = s;
+        s = __fadd_rn(s, b[q].w); o.w = s;
+        *reinterpret_cast<float4*>(out + i + 4 * q) = o;
+      }
+    }
+  }
+  for (int i = n16; i < len; ++i) {
+    s = __fadd_rn(s, buf[i]);
+    out[i] = s;
+  }
+  return s;
+}
+
 // tokens.rs:99-120 over probs[0..n) with the uniform u01 (block-wide; every
-// thread receives the index); -1 on an invalid distribution.
-SPEC_DEV int block_sample(const float* probs, int n, float u01, float* buf, float* bcast, int* ibcast) {
-  const float sum = block_seq_sum(probs, n, buf, bcast);
-  if (!(sum > 0.f) || !isfinite(sum)) return -1;
-  const float u = __fmul_rn(u01, sum);
-  float acc = 0.f;
+// thread receives the index); -1 on an invalid distribution.  The reference
+// sums the row, then scans it again accumulating from 0 in the same order:
+// the scan's running sums are exactly the sum's partial sums.  So one
+// sequential pass (thread 0, chunks staged by the other warps as in
+// block_seq_sum) stores every partial sum to pref[0..n), the staging threads
+// note the first invalid element (non-finite or negative; the reference
+// checks each before adding it), and the first index whose partial sum
+// exceeds u = u01 * sum is then found by all threads at once.  pref may be
+// probs itself (a chunk is overwritten only after it has been staged).
+SPEC_DEV int block_sample(const float* probs, int n, float u01, float* pref, float* buf, float* bcast,
+                          int* ibcast, int* ibad) {
+  if (threadIdx.x == 0) {
+    *ibcast = INT_MAX;
+    *ibad = INT_MAX;
+  }
+  __syncthreads();
+  auto stage = [&](int base, int len, float* dst, bool skip_warp0) {
+    const int t0 = skip_warp0 ? 32 : 0;
+    if ((int)threadIdx.x < t0) return;
+    for (int i = threadIdx.x - t0; i < len; i += blockDim.x - t0) {
+      const float v = probs[base + i];
+      if (!isfinite(v) || v < 0.f) atomicMin(ibad, base + i);
+      dst[i] = v;
+    }
+  };
+  float s = 0.f;
   const int nc = (n + kSeqChunk - 1) / kSeqChunk;
-  stage_chunk(probs, 0, min(kSeqChunk, n), buf, false);
-  if (threadIdx.x == 0) *ibcast = -2;  // -2: not found yet
+  if (nc > 0) stage(0, min(kSeqChunk, n), buf, false);
   __syncthreads();
   for (int c = 0; c < nc; ++c) {
     const int base = c * kSeqChunk, len = min(kSeqChunk, n - base);
-    const float* cur = buf + (c & 1) * kSeqChunk;
-    if (c + 1 < nc)
-      stage_chunk(probs, base + kSeqChunk, min(kSeqChunk, n - base - kSeqChunk), buf + ((c + 1) & 1) * kSeqChunk,
-                  true);
-    if (threadIdx.x == 0) {
-      // 16 elements per step, the next 16 loaded ahead.  The running sum
-      // advances unconditionally; the answer is the first
-      // index whose running sum exceeds u, unless an invalid element comes at
-      // or before it (the reference checks each element before adding it).
-      // Neither record feeds back into the add chain.
-      int hit = -1, bad = -1;
-      auto step = [&](float p, int idx) {
-        const bool invalid = !isfinite(p) || p < 0.f;
-        bad = (bad < 0 && invalid) ? idx : bad;
-        acc = __fadd_rn(acc, p);
-        hit = (hit < 0 && u < acc) ? idx : hit;
-      };
-      const int n16 = len & ~15;
-      int i = 0;
-      if (n16) {
-        float4 a0 = *reinterpret_cast<const float4*>(cur), a1 = *reinterpret_cast<const float4*>(cur + 4),
-               a2 = *reinterpret_cast<const float4*>(cur + 8), a3 = *reinterpret_cast<const float4*>(cur + 12);
-        for (; i < n16 && (bad | hit) < 0; i += 16) {
-          const float4 b0 = a0, b1 = a1, b2 = a2, b3 = a3;
-          if (i + 16 < n16) {
-            a0 = *reinterpret_cast<const float4*>(cur + i + 16);
-            a1 = *reinterpret_cast<const float4*>(cur + i + 20);
-            a2 = *reinterpret_cast<const float4*>(cur + i + 24);
-            a3 = *reinterpret_cast<const float4*>(cur + i + 28);
-          }
-          step(b0.x, i + 0); step(b0.y, i + 1); step(b0.z, i + 2); step(b0.w, i + 3);
-          step(b1.x, i + 4); step(b1.y, i + 5); step(b1.z, i + 6); step(b1.w, i + 7);
-          step(b2.x, i + 8); step(b2.y, i + 9); step(b2.z, i + 10); step(b2.w, i + 11);
-          step(b3.x, i + 12); step(b3.y, i + 13); step(b3.z, i + 14); step(b3.w, i + 15);
-        }
-      }
-      for (; i < len && (bad | hit) < 0; ++i) step(cur[i], i);
-      if (bad >= 0 && (hit < 0 || bad <= hit)) *ibcast = -1;
-      else if (hit >= 0) *ibcast = base + hit;
-    }
-    __syncthreads();
-    const int found = *ibcast;
-    if (found != -2) return found;  // uniform: read after the barrier by every thread
+    float* cur = buf + (c & 1) * kSeqChunk;
+    if (c + 1 < nc) stage(base + kSeqChunk, min(kSeqChunk, n - base - kSeqChunk), buf + ((c + 1) & 1) * kSeqChunk, true);
+    if (threadIdx.x == 0) s = add_chunk_pref(s, cur, len, pref + base);
     __syncthreads();
   }
-  return n - 1;
+  if (threadIdx.x == 0) *bcast = s;
+  __syncthreads();
+  const float sum = *bcast;
+  const int bad = *ibad;
+  if (!(sum > 0.f) || !isfinite(sum)) {
+    __syncthreads();
+    return -1;
+  }
+  const float u = __fmul_rn(u01, sum);
+  // First index with u < partial sum; a thread stops at its first hit, and
+  // no index at or beyond the block's current best is worth reading.
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    if (u < pref[i]) {
+      atomicMin(ibcast, i);
+      break;
+    }
+  }
+  __syncthreads();
+  const int hit = *ibcast;
+  __syncthreads();
+  if (bad != INT_MAX && (hit == INT_MAX || bad <= hit)) return -1;
+  return hit != INT_MAX ? hit : n - 1;
 }
 
 // Block-wide first-max argmax (tokens.rs:26-36 fold) of row[0..V).
@@ -223,7 +256,7 @@ __global__ void __launch_bounds__(kRejThreads) target_softmax_kernel(float* rows
 // q: [k][V] draft probabilities, r: [V] scratch.
 __global__ void __launch_bounds__(kRejThreads) rejection_walk_kernel(const float* p, const float* q, float* r,
                                                                      const RejStep* st, int V, int* out) {
-  __shared__ int s_i, s_n, s_used, s_status, s_reject, s_idx;
+  __shared__ int s_i, s_n, s_used, s_status, s_reject, s_idx, s_bad;
   __shared__ float s_sum;
   __shared__ __align__(16) float s_buf[2 * kSeqChunk];
   const int k = st->k;
@@ -279,7 +312,7 @@ __global__ void __launch_bounds__(kRejThreads) rejection_walk_kernel(const float
       if (s_used >= st->n_uniforms) {
         if (threadIdx.x == 0) s_status = REJ_ERR_UNIFORMS;
       } else {
-        const int idx = block_sample(r, V, st->uniforms[s_used], s_buf, &s_sum, &s_idx);
+        const int idx = block_sample(r, V, st->uniforms[s_used], r, s_buf, &s_sum, &s_idx, &s_bad);
         if (threadIdx.x == 0) {
           ++s_used;
           if (idx < 0) s_status = REJ_ERR_DISTRIBUTION;
@@ -292,7 +325,7 @@ __global__ void __launch_bounds__(kRejThreads) rejection_walk_kernel(const float
     if (s_used >= st->n_uniforms) {
       if (threadIdx.x == 0) s_status = REJ_ERR_UNIFORMS;
     } else {
-      const int idx = block_sample(p + (size_t)k * V, V, st->uniforms[s_used], s_buf, &s_sum, &s_idx);
+      const int idx = block_sample(p + (size_t)k * V, V, st->uniforms[s_used], r, s_buf, &s_sum, &s_idx, &s_bad);
       if (threadIdx.x == 0) {
         ++s_used;
         if (idx < 0) s_status = REJ_ERR_DISTRIBUTION;
@@ -308,7 +341,87 @@ __global__ void __launch_bounds__(kRejThreads) rejection_walk_kernel(const float
   }
 }
 
+// ---- typical acceptance (methods/medusa.rs:424-445) -----------------------
+// f32::ln modelled as the correctly rounded log of the f32 argument (log in
+// double, one rounding), as exp is above.
+SPEC_DEV float ln_f32_cr(float x) { return (float)log((double)x); }
+
+// block_seq_sum over values computed while they are staged: f(i) for
+// i in [0, n).  Same chunking and add order as block_seq_sum.
+template <class F>
+SPEC_DEV void stage_chunk_of(F f, int base, int len, float* buf, bool skip_warp0) {
+  const int t0 = skip_warp0 ? 32 : 0;
+  if ((int)threadIdx.x < t0) return;
+  for (int i = threadIdx.x - t0; i < len; i += blockDim.x - t0) buf[i] = f(base + i);
+}
+
+template <class F>
+SPEC_DEV float block_seq_sum_of(F f, int n, float* buf, float* bcast) {
+  float s = 0.f;
+  const int nc = (n + kSeqChunk - 1) / kSeqChunk;
+  if (nc > 0) stage_chunk_of(f, 0, min(kSeqChunk, n), buf, false);
+  __syncthreads();
+  for (int c = 0; c < nc; ++c) {
+    const int base = c * kSeqChunk, len = min(kSeqChunk, n - base);
+    float* cur = buf + (c & 1) * kSeqChunk;
+    if (c + 1 < nc)
+      stage_chunk_of(f, base + kSeqChunk, min(kSeqChunk, n - base - kSeqChunk), buf + ((c + 1) & 1) * kSeqChunk,
+                     true);
+    if (threadIdx.x == 0) s = add_chunk(s, cur, len);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *bcast = s;
+  __syncthreads();
+  s = *bcast;
+  __syncthreads();
+  return s;
+}
+
+// One CTA per tree row that has children.  softmax: NaN-skipping max, then
+// e_i = exp(l_i - max) and their sequential f32 sum; p_i = e_i / sum.
+// entropy: sequential f32 sum of (-p) * ln(p) over p > 0 (skipped elements
+// contribute -0.0, which leaves every partial sum unchanged).  threshold =
+// max(epsilon, delta * exp(-entropy)); a child passes iff p(token) >=
+// threshold.  A row whose mass is non-positive or non-finite rejects every
+// child (the reference returns false).  Nothing is stored but the flags.
+__global__ void __launch_bounds__(kRejThreads) typical_accept_kernel(const float* rows, int V, TypicalTree t,
+                                                                     int* accept) {
+  const int r = blockIdx.x;
+  bool has_child = false;
+  for (int i = 1; i < t.n; ++i) has_child |= t.par[i] == r;
+  if (!has_child) return;  // uniform across the block
+  const float* row = rows + (size_t)r * V;
+  __shared__ float red[kRejThreads / 32];
+  __shared__ float s_sum;
+  __shared__ __align__(16) float s_buf[2 * kSeqChunk];
+  const float mx = block_max(row, V, red);
+  const float s = block_seq_sum_of([&](int i) { return exp_f32_cr(__fsub_rn(row[i], mx)); }, V, s_buf, &s_sum);
+  const bool valid = s > 0.f && isfinite(s);
+  float thr = 0.f;
+  if (valid) {
+    const float h = block_seq_sum_of(
+        [&](int i) {
+          const float p = __fdiv_rn(exp_f32_cr(__fsub_rn(row[i], mx)), s);
+          return p > 0.f ? __fmul_rn(-p, ln_f32_cr(p)) : -0.f;
+        },
+        V, s_buf, &s_sum);
+    thr = fmaxf(t.epsilon, __fmul_rn(t.delta, exp_f32_cr(-h)));
+  }
+  for (int i = threadIdx.x; i < t.n; i += blockDim.x) {
+    if (i < 1 || t.par[i] != r) continue;
+    int ok = 0;
+    if (valid) ok = __fdiv_rn(exp_f32_cr(__fsub_rn(row[t.tok[i]], mx)), s) >= thr;
+    accept[i] = ok;
+  }
+}
+
 }  // namespace
+
+cudaError_t launch_typical_accept(const float* rows, int V, const TypicalTree& t, int* accept, cudaStream_t s) {
+  if (t.n < 1 || t.n > kMaxRows || V < 1) return cudaErrorInvalidValue;
+  typical_accept_kernel<<<t.n, kRejThreads, 0, s>>>(rows, V, t, accept);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_rejection(float* rows, const float* q, float* r, const RejStep* st, int k, int V,
                              float temperature, int* out, cudaStream_t s) {

@@ -354,6 +354,17 @@ struct RejStep {
 cudaError_t launch_rejection(float* rows, const float* q, float* r, const RejStep* st, int k, int V,
                              float temperature, int* out, cudaStream_t s);
 
+// ---- typical acceptance over a tree forward (accept.cu) --------------------
+struct TypicalTree {
+  int n = 0;
+  float epsilon = 0.f, delta = 0.f;
+  uint32_t tok[kMaxRows];
+  int32_t par[kMaxRows];
+};
+// rows: [n][V] node logits (unchanged).  accept[i] (1 <= i < n) = 1 when
+// node i's token passes the typical rule against its parent's row, else 0.
+cudaError_t launch_typical_accept(const float* rows, int V, const TypicalTree& t, int* accept, cudaStream_t s);
+
 // Per-row argmax (first-max tie break).  slots / counters: kMaxRows each,
 // zero before the first call; every call leaves them zero again.
 cudaError_t launch_row_argmax(const float* logits, int rows, int V, int* out_idx, float* out_val,

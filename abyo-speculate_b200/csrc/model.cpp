@@ -3271,6 +3271,71 @@ int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t
   return verify_tree_greedy_core(m, tokens, parents, n, best_path, path_len, bonus, false);
 }
 
+// Medusa's typical acceptance (medusa.rs:290-326 with Acceptance::Typical,
+// :391-445) over one tree forward with the KV kept: the per-node pass/fail
+// flags come from the device (typical_accept_kernel, the reference's f32
+// operations in its order), the path walk and the argmax bonus are those of
+// spec_verify_tree_greedy.
+int spec_verify_tree_typical(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float epsilon,
+                             float delta, int32_t* best_path, int* path_len, uint32_t* bonus) {
+  if (!m || !tokens || !parents || !best_path || !path_len || !bonus) return SPEC_ERR_INVALID;
+  DeviceGuard dg_(m->device);
+  m->last_valid = false;
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
+  int rc = check_tree(m, tokens, parents, n);
+  if (rc != SPEC_OK) return rc;
+  if (tokens[0] != m->history.back()) return m->fail(SPEC_ERR_INVALID, "tree root must equal last committed token");
+  const int pre = m->cache_len;
+  const int prefix = (int)m->history.size() - 1;
+  if (prefix > pre) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
+  TypicalTree tt;
+  tt.n = n;
+  tt.epsilon = epsilon;
+  tt.delta = delta;
+  for (int i = 0; i < n; ++i) {
+    tt.tok[i] = tokens[i];
+    tt.par[i] = i ? parents[i] : 0;
+  }
+  int* flags_dev = m->rej_out_dev + 4;  // kMaxRows ints
+  int* flags_host = m->rej_out_host + 4;
+  rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS);
+  if (rc == SPEC_OK) {
+    cudaError_t e = launch_row_argmax(m->logits, n, m->cfg.vocab, m->argmax_dev, nullptr, m->argmax_slots,
+                                      m->argmax_counters, m->stream);
+    if (e == cudaSuccess) e = cudaMemsetAsync(flags_dev, 0, (size_t)n * 4, m->stream);
+    if (e == cudaSuccess) e = launch_typical_accept(m->logits, m->cfg.vocab, tt, flags_dev, m->stream);
+    if (e == cudaSuccess)
+      e = cudaMemcpyAsync(m->argmax_host, m->argmax_dev, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(flags_host, flags_dev, (size_t)n * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "typical acceptance"));
+  }
+  if (rc == SPEC_OK) rc = finish(m);
+  if (rc != SPEC_OK) return rc;
+  m->cache_len = prefix + n;
+  std::vector<char> is_leaf(n, 1);
+  for (int i = 1; i < n; ++i) is_leaf[parents[i]] = 0;
+  std::vector<int> best = {0};
+  for (int leaf = 0; leaf < n; ++leaf) {
+    if (!is_leaf[leaf]) continue;
+    std::vector<int> chain;
+    for (int cur = leaf;; cur = parents[cur]) {
+      chain.push_back(cur);
+      if (cur == 0) break;
+    }
+    std::reverse(chain.begin(), chain.end());
+    int accepted = 0;
+    for (size_t w = 0; w + 1 < chain.size(); ++w) {
+      if (flags_host[chain[w + 1]]) ++accepted;
+      else break;
+    }
+    if (accepted + 1 > (int)best.size()) best.assign(chain.begin(), chain.begin() + accepted + 1);
+  }
+  for (size_t i = 0; i < best.size(); ++i) best_path[i] = best[i];
+  *path_len = (int)best.size();
+  *bonus = (uint32_t)m->argmax_host[best.back()];
+  return SPEC_OK;
+}
+
 // The EAGLE-2 round tree (eagle.rs:584-593): the Cartesian product of the
 // draft steps' top-k (medusa.rs:172-189: BFS layers, every candidate of step
 // d under every node of layer d, parents in layer order), pruned to at most

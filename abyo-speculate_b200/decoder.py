@@ -374,6 +374,19 @@ class B200Decoder:
                                                       ctypes.byref(bonus)))
         return [int(x) for x in best[:plen.value]], bonus.value
 
+    def verify_tree_typical(self, tree: DraftTree, epsilon: float, delta: float) -> Tuple[List[int], int]:
+        """Tree verify (KV kept) + Medusa typical acceptance (medusa.rs:290-326,
+        :424-445: p(x) >= max(epsilon, delta * exp(-H(p))) against the parent's
+        row, first longest accepted path) + the argmax bonus of its deepest node."""
+        t, p = self._tree_arrays(tree)
+        best = np.empty(t.size, dtype=np.int32)
+        plen = ctypes.c_int()
+        bonus = ctypes.c_uint32()
+        self._check(self._lib.spec_verify_tree_typical(self._h, _ptr(t, ctypes.c_uint32), _ptr(p, ctypes.c_int32),
+                                                       t.size, float(epsilon), float(delta), _ptr(best, ctypes.c_int32),
+                                                       ctypes.byref(plen), ctypes.byref(bonus)))
+        return [int(x) for x in best[:plen.value]], bonus.value
+
     # ---- diagnostics -----------------------------------------------------------------
     def last_forward_ms(self) -> float:
         return float(self._lib.spec_last_forward_ms(self._h))

@@ -311,6 +311,17 @@ int spec_sd_greedy_round(spec_model* target, spec_model* draft, int k, uint32_t*
  * *bonus the argmax of the deepest accepted node. */
 int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
                             int32_t* best_path, int* path_len, uint32_t* bonus);
+/* Medusa typical acceptance (crates/speculate/src/methods/medusa.rs:290-326
+ * with Acceptance::Typical { epsilon, delta }, accept_one at :424-445) over
+ * the same tree forward (KV kept): node i passes iff, under its parent's
+ * row, p(token_i) >= max(epsilon, delta * exp(-H(p))), with the softmax and
+ * the entropy in the reference's f32 operations and sequential order (max,
+ * exp(l - max), sequential sum, division; sequential sum of (-p) * ln(p) over
+ * p > 0); a row with non-positive or non-finite mass rejects every child.
+ * Walk, outputs and state change as spec_verify_tree_greedy; the bonus is the
+ * argmax of the deepest accepted node (medusa.rs:311-316, :451-470). */
+int spec_verify_tree_typical(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float epsilon,
+                             float delta, int32_t* best_path, int* path_len, uint32_t* bonus);
 /* Rejection-sampling vanilla round (methods/vanilla.rs:172-210 steps 3-4) on
  * the device: one batched forward of [last]+drafts (same protocol and state
  * change as spec_batched_logits), then, with the reference's float32

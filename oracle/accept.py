@@ -14,6 +14,9 @@ Restates, with float32 arithmetic in the reference's sequential order:
 * crates/speculate/src/methods/eagle.rs:618-661 greedy tree acceptance
   (walk every root-to-leaf path in leaf-index order, count leading
   argmax matches, first longest wins; bonus = argmax of the deepest node);
+* crates/speculate/src/methods/medusa.rs:424-445 typical acceptance
+  (p(x) >= max(epsilon, delta * exp(-H(p)))) and the same tree walk with it
+  (:290-326, :391-411);
 * crates/speculate/src/model/mock.rs:164-180 fixed_distribution.
 
 Uniforms are explicit inputs so decisions can be compared bit-exactly with
@@ -206,6 +209,69 @@ def greedy_tree_accept(tokens: Sequence[int], parents: Sequence[int], rows: np.n
         if accepted + 1 > len(best):
             best = path[: accepted + 1]
     return best, am[best[-1]]
+
+
+def ln_f32(x: np.ndarray) -> np.ndarray:
+    """f32::ln as modelled here: the correctly rounded natural log of the f32
+    argument (log in double, one rounding to f32).  Rust calls the platform
+    libm's logf; tests/test_exp_model.py measures how often glibc's differs
+    from this model and whether a typical-acceptance decision does."""
+    return np.log(np.asarray(x, dtype=np.float32).astype(np.float64)).astype(np.float32)
+
+
+def typical_threshold(logits: np.ndarray, epsilon: float, delta: float):
+    """medusa.rs:424-443 up to the comparison: (probs, threshold), or None
+    where the reference returns false for a non-positive / non-finite softmax
+    mass.  softmax: max by the NaN-skipping f32::max fold, exp(l - max),
+    sequential f32 sum, p = e / sum; entropy = sequential f32 sum of
+    (-p) * ln(p) over p > 0; threshold = epsilon.max(delta * exp(-entropy))."""
+    lg = np.asarray(logits, dtype=np.float32)
+    finite = lg[~np.isnan(lg)]
+    mx = np.float32(np.max(finite)) if finite.size else np.float32(-np.inf)
+    with np.errstate(invalid="ignore", over="ignore"):
+        e = exp_f32(lg - mx)
+        s = seq_sum_f32(e)
+        if not (s > 0) or not np.isfinite(s):
+            return None
+        p = (e / s).astype(np.float32)
+        pos = p[p > 0]
+        ent = seq_sum_f32(((-pos) * ln_f32(pos)).astype(np.float32))
+        t = np.float32(np.float32(delta) * exp_f32(np.float32(-ent)))
+    return p, np.float32(np.fmax(np.float32(epsilon), t))  # f32::max: a NaN side yields the other
+
+
+def typical_accept_one(logits: np.ndarray, candidate: int, epsilon: float, delta: float) -> bool:
+    """medusa.rs:424-445 (Acceptance::Typical): p(candidate) >= threshold."""
+    r = typical_threshold(logits, epsilon, delta)
+    if r is None:
+        return False
+    p, thr = r
+    return bool(p[int(candidate)] >= thr)
+
+
+def typical_tree_accept(tokens: Sequence[int], parents: Sequence[int], rows: np.ndarray, epsilon: float,
+                        delta: float) -> Tuple[List[int], int]:
+    """medusa.rs:290-326 with Acceptance::Typical: every root-to-leaf path
+    (leaves in index order) accepts while typical_accept_one holds against the
+    parent's row (:391-411); the first longest accepted prefix wins (:296-301)
+    and the bonus is the argmax of its deepest node (:311-316, :451-470)."""
+    thr = [typical_threshold(r, epsilon, delta) for r in rows]
+
+    def ok(parent: int, child: int) -> bool:
+        t = thr[parent]
+        return t is not None and bool(t[0][int(tokens[child])] >= t[1])
+
+    best = [0]
+    for path in tree_paths(parents):
+        accepted = 0
+        for parent, child in zip(path[:-1], path[1:]):
+            if ok(parent, child):
+                accepted += 1
+            else:
+                break
+        if accepted + 1 > len(best):
+            best = path[: accepted + 1]
+    return best, argmax_first_fast(rows[best[-1]])
 
 
 def top2_margin(row: np.ndarray) -> float:

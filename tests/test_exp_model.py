@@ -87,3 +87,63 @@ def test_vanilla_round_decisions_with_libm_expf(accept, monkeypatch):
     print(f"{differ} of {len(rounds)} rounds differ between the exp model and libm expf "
           f"({accepted} drafts accepted in total)")
     assert differ == 0
+
+
+def _libm_logf():
+    name = ctypes.util.find_library("m") or "libm.so.6"
+    try:
+        lib = ctypes.CDLL(name)
+    except OSError:
+        pytest.skip("no C math library to call")
+    f = lib.logf
+    f.restype = ctypes.c_float
+    f.argtypes = [ctypes.c_float]
+    return f
+
+
+def test_libm_logf_against_the_correctly_rounded_model(accept):
+    """Typical acceptance (medusa.rs:424-445) takes ln of every probability;
+    the oracle and the device model f32::ln as the correctly rounded log."""
+    logf = _libm_logf()
+    rng = np.random.default_rng(2)
+    x = np.exp(-rng.random(300_000) * 25.0).astype(np.float32)  # probabilities in (e^-25, 1]
+    got = _vec(logf)(x)
+    model = accept.ln_f32(x)
+    exact = np.log(x.astype(np.longdouble)).astype(np.float32)
+    assert np.array_equal(model, exact)
+    diff = got != model
+    ulps = np.abs(got.view(np.int32).astype(np.int64) - model.view(np.int32).astype(np.int64))
+    print(f"libm logf differs from the correctly rounded log on {int(diff.sum())} of {x.size} arguments "
+          f"({float(diff.mean()):.3%}), by at most {int(ulps.max())} ulp")
+    assert int(ulps.max()) <= 1
+    assert float(diff.mean()) < 2e-3
+
+
+def test_typical_decisions_with_libm(accept, monkeypatch):
+    """200 seeded typical-acceptance trees (V = 4096, 15 nodes) decided with
+    the exp/ln models and again with the host libm's expf and logf: the
+    accepted paths and bonus tokens are compared tree by tree."""
+    expf, logf = _vec(_libm_expf()), _vec(_libm_logf())
+    rng = np.random.default_rng(11)
+    V, n = 4096, 15
+    parents = [0] + [(i - 1) // 2 for i in range(1, n)]
+    cases = []
+    for _ in range(200):
+        rows = (rng.standard_normal((n, V)) * rng.choice([1.0, 3.0, 6.0])).astype(np.float32)
+        toks = [0] + [int(np.argsort(rows[parents[i]])[-1 - int(rng.integers(0, 3))]) for i in range(1, n)]
+        eps, delta = float(rng.choice([0.01, 0.05, 0.1])), float(rng.choice([0.1, 0.3, 0.6]))
+        cases.append((toks, rows, eps, delta))
+
+    def play(exp_fn, ln_fn):
+        monkeypatch.setattr(accept, "exp_f32", exp_fn)
+        monkeypatch.setattr(accept, "ln_f32", ln_fn)
+        return [accept.typical_tree_accept(t, parents, r, e, d) for t, r, e, d in cases]
+
+    model = play(accept.exp_f32, accept.ln_f32)
+    libm = play(expf, logf)
+    differ = sum(a != b for a, b in zip(model, libm))
+    accepted = sum(len(b) - 1 for b, _ in model)
+    print(f"{differ} of {len(cases)} typical trees differ between the models and libm "
+          f"({accepted} nodes accepted in total)")
+    assert accepted > 0
+    assert differ == 0

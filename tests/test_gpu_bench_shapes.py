@@ -126,6 +126,35 @@ def test_llama8b_shapes_prefill_and_verify(pkg, oracle, llama8b):
     other.close()
 
 
+def test_llama8b_vocab_typical_tree(pkg, accept, llama8b):
+    """Medusa typical acceptance (spec_verify_tree_typical) over 128256-wide
+    node rows of the Llama-3-8B-shaped model: the device's softmax and
+    entropy (33 sequential chunks per row) decide every node as the
+    restated rule does on the same rows."""
+    dec, _, _ = llama8b
+    V = LLAMA8B["vocab"]
+    rng = np.random.default_rng(13)
+    dec.reset()
+    prompt = rng.integers(0, V, size=64).tolist()
+    dec.observe(prompt)
+    tokens, parents = [prompt[-1]], [0]
+    rows, _ = dec.tree_logits_keep_kv(pkg.DraftTree(tokens, parents))
+    for t in np.argsort(-rows[0], kind="stable")[:3].tolist() + [int(rng.integers(0, V))]:
+        tokens.append(int(t))
+        parents.append(0)
+    rows, _ = dec.tree_logits_keep_kv(pkg.DraftTree(tokens, parents))
+    for f in range(1, 5):
+        for t in np.argsort(-rows[f], kind="stable")[:2].tolist():
+            tokens.append(int(t))
+            parents.append(f)
+    tree = pkg.DraftTree(tokens, parents)
+    rows, _ = dec.tree_logits_keep_kv(tree)
+    for eps, delta in [(0.0, 1.0), (1e-5, 0.5), (1e-3, 3.0), (0.5, 0.5)]:
+        want = accept.typical_tree_accept(tokens, parents, rows, eps, delta)
+        assert dec.verify_tree_typical(tree, eps, delta) == want, (eps, delta)
+    dec.reset()
+
+
 QWEN7B_1L = dict(arch="qwen2", n_layers=1, hidden=3584, n_heads=28, n_kv_heads=4, ffn=18944, vocab=4096,
                  rope_theta=1e6, eps=1e-6)
 

@@ -65,3 +65,55 @@ def test_medusa_errors_and_synthetic(pkg, tiny_gguf):
     assert ids.shape == (4, 8) and np.isfinite(lp).all() and (ids >= 0).all() and (ids < dec.vocab_size()).all()
     with pytest.raises(pkg.SamplingError):
         dec.medusa_topk(h, 65)
+
+
+def _grown_tree(pkg, dec, root, rng, depth, V):
+    """A tree whose children are, per node, its row's top two tokens and one
+    random token (rows from tree forwards of the tree grown so far), so that
+    the typical rule both passes and fails along its paths."""
+    tokens, parents = [int(root)], [0]
+    frontier = [0]
+    for _ in range(depth):
+        rows, _ = dec.tree_logits_keep_kv(pkg.DraftTree(tokens, parents))
+        nxt = []
+        for f in frontier:
+            top = np.argsort(-rows[f], kind="stable")[:2].tolist()
+            for t in top + [int(rng.integers(0, V))]:
+                if len(tokens) < 40:
+                    tokens.append(int(t))
+                    parents.append(f)
+                    nxt.append(len(tokens) - 1)
+        frontier = nxt
+    return pkg.DraftTree(tokens, parents)
+
+
+@pytest.mark.parametrize("name", ["llama_q4km", "qwen_q4km", "llama_bf16"])
+def test_verify_tree_typical_matches_oracle(pkg, tiny_gguf, accept, name):
+    """spec_verify_tree_typical (device softmax/entropy per node row, host
+    walk) against medusa.rs typical acceptance restated on the same node rows
+    (oracle.accept.typical_tree_accept): identical accepted paths and bonus
+    tokens, bit for bit, for several (epsilon, delta), and the KV/history
+    state of spec_verify_tree_greedy."""
+    dec = pkg.B200Decoder.from_gguf(tiny_gguf(name), max_ctx=256)
+    V = dec.vocab_size()
+    rng = np.random.default_rng(21)
+    prompt = rng.integers(0, V, size=17).tolist()
+    dec.observe(prompt)
+    tree = _grown_tree(pkg, dec, prompt[-1], rng, 3, V)
+    rows, _ = dec.tree_logits_keep_kv(tree)
+    lengths = set()
+    for eps, delta in [(0.0, 1.0), (0.001, 0.5), (0.01, 0.3), (0.05, 2.0), (0.3, 0.3), (1.0, 0.0)]:
+        want_best, want_bonus = accept.typical_tree_accept(tree.tokens(), tree.parents(), rows, eps, delta)
+        best, bonus = dec.verify_tree_typical(tree, eps, delta)
+        assert best == want_best and bonus == want_bonus, (eps, delta)
+        assert dec.kv_len() == len(prompt) - 1 + len(tree) and dec.history() == prompt
+        lengths.add(len(best))
+    assert 1 in lengths and max(lengths) >= 3, lengths
+    # Greedy and typical share the forward and the walk: with epsilon above
+    # every probability nothing passes, as a greedy walk on a root whose
+    # argmax is not a child.
+    best, bonus = dec.verify_tree_typical(tree, 2.0, 0.0)
+    assert best == [0] and bonus == int(accept.argmax_first_fast(rows[0]))
+    with pytest.raises(pkg.SamplingError):
+        dec.verify_tree_typical(pkg.DraftTree([prompt[-1] + 1 if prompt[-1] + 1 < V else 0], [0]), 0.1, 0.1)
+    dec.close()
