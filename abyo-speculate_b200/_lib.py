@@ -145,6 +145,9 @@ SIGNATURES = [
     ("spec_medusa_topk", ctypes.c_int,
      [ctypes.c_void_p, c_f32_p, ctypes.c_int, ctypes.POINTER(ctypes.c_int32), c_f32_p]),
     ("spec_medusa_num_heads", ctypes.c_int, [ctypes.c_void_p]),
+    ("spec_medusa_round", ctypes.c_int,
+     [ctypes.c_void_p, c_f32_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+      c_u32_p, c_int_p, c_f32_p]),
     ("spec_sd_greedy_round", ctypes.c_int,
      [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.POINTER(ctypes.c_uint32), ctypes.POINTER(ctypes.c_int)]),
     ("spec_apply_lm_head_topk", ctypes.c_int,

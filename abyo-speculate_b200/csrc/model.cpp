@@ -3276,9 +3276,10 @@ int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t
 // flags come from the device (typical_accept_kernel, the reference's f32
 // operations in its order), the path walk and the argmax bonus are those of
 // spec_verify_tree_greedy.
-int spec_verify_tree_typical(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float epsilon,
-                             float delta, int32_t* best_path, int* path_len, uint32_t* bonus) {
-  if (!m || !tokens || !parents || !best_path || !path_len || !bonus) return SPEC_ERR_INVALID;
+// With `hidden` the tree forward also leaves every node's final hidden row in
+// m->hidden_out (device).
+int verify_tree_typical_core(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float epsilon,
+                             float delta, int32_t* best_path, int* path_len, uint32_t* bonus, bool hidden) {
   DeviceGuard dg_(m->device);
   m->last_valid = false;
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
@@ -3298,7 +3299,7 @@ int spec_verify_tree_typical(spec_model* m, const uint32_t* tokens, const int32_
   }
   int* flags_dev = m->rej_out_dev + 4;  // kMaxRows ints
   int* flags_host = m->rej_out_host + 4;
-  rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS);
+  rc = tree_forward(m, tokens, parents, n, prefix, hidden ? (F_LOGITS | F_HIDDEN) : F_LOGITS);
   if (rc == SPEC_OK) {
     cudaError_t e = launch_row_argmax(m->logits, n, m->cfg.vocab, m->argmax_dev, nullptr, m->argmax_slots,
                                       m->argmax_counters, m->stream);
@@ -3334,6 +3335,12 @@ int spec_verify_tree_typical(spec_model* m, const uint32_t* tokens, const int32_
   *path_len = (int)best.size();
   *bonus = (uint32_t)m->argmax_host[best.back()];
   return SPEC_OK;
+}
+
+int spec_verify_tree_typical(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float epsilon,
+                             float delta, int32_t* best_path, int* path_len, uint32_t* bonus) {
+  if (!m || !tokens || !parents || !best_path || !path_len || !bonus) return SPEC_ERR_INVALID;
+  return verify_tree_typical_core(m, tokens, parents, n, epsilon, delta, best_path, path_len, bonus, false);
 }
 
 // The EAGLE-2 round tree (eagle.rs:584-593): the Cartesian product of the
@@ -3487,6 +3494,86 @@ int spec_eagle_round(spec_model* m, const float* hidden, int depth, int top_k, i
                                      (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "tree hidden row"));
     best[len++] = bn;
+    return spec_commit_tree_path(m, tok, par, n, best, len);
+  }
+  rc = spec_commit_tree_path(m, tok, par, n, best, len);
+  if (rc == SPEC_OK) rc = spec_observe_returning_last_hidden(m, &bonus, 1, hidden_out);
+  return rc;
+}
+
+// One Medusa round: the body of run_medusa_real's loop (medusa.rs:761-810).
+// The reference's tree_logits restores the state and observe(committed)
+// recomputes the accepted rows; here the tree forward keeps its KV rows and
+// the accepted path is committed in place (spec_commit_tree_path), then the
+// bonus is observed, which leaves the same history and KV rows.
+int spec_medusa_round(spec_model* m, const float* hidden, int top_k, int topology, int acceptance, float epsilon,
+                      float delta, int budget, uint32_t* commits_out, int* n_out, float* hidden_out) {
+  if (!m || !hidden || !commits_out || !n_out || !hidden_out || top_k < 1 || (topology != 0 && topology != 1) ||
+      (acceptance != 0 && acceptance != 1))
+    return SPEC_ERR_INVALID;
+  DeviceGuard dg_(m->device);
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "Medusa requires non-empty prompt");
+  if (budget < 1) return m->fail(SPEC_ERR_INVALID, "token budget must be >= 1");
+  MedusaHeads* h = m->medusa.get();
+  if (!h) return m->fail(SPEC_ERR_INVALID, "no Medusa heads attached (spec_medusa_attach)");
+  const int nh = h->n_heads;
+  const uint32_t root = m->history.back();
+  // 1. Per-head top-k from the target's last hidden row (:766-768).
+  std::vector<int32_t> ids((size_t)nh * top_k);
+  int rc = spec_medusa_topk(m, hidden, top_k, ids.data(), nullptr);
+  if (rc != SPEC_OK) return rc;
+  // 2. The tree (:771): a chain of each head's top-1 (:167-170), or BFS
+  // layers with every candidate of head d under every node of layer d
+  // (:172-189).
+  uint32_t tok[kMaxRows];
+  int32_t par[kMaxRows];
+  int n = 1;
+  tok[0] = root;
+  par[0] = 0;
+  if (topology == 0) {
+    if (nh + 1 > kMaxRows) return m->fail(SPEC_ERR_UNSUPPORTED, "Medusa tree larger than SPEC_MAX_ROWS nodes");
+    for (int d = 0; d < nh; ++d) {
+      tok[n] = (uint32_t)ids[(size_t)d * top_k];
+      par[n] = n - 1;
+      ++n;
+    }
+  } else {
+    int64_t total = 1, width = 1;
+    for (int d = 0; d < nh; ++d) {
+      width *= top_k;
+      total += width;
+      if (total > kMaxRows) return m->fail(SPEC_ERR_UNSUPPORTED, "Medusa tree larger than SPEC_MAX_ROWS nodes");
+    }
+    int lo = 0, hi = 1;  // the previous layer's node range
+    for (int d = 0; d < nh; ++d) {
+      const int start = n;
+      for (int p = lo; p < hi; ++p)
+        for (int c = 0; c < top_k; ++c) {
+          tok[n] = (uint32_t)ids[(size_t)d * top_k + c];
+          par[n] = p;
+          ++n;
+        }
+      lo = start;
+      hi = n;
+    }
+  }
+  // 3-4. Tree forward (KV and per-node hidden rows kept) and the walk.
+  int32_t best[kMaxRows];
+  int len = 0;
+  uint32_t bonus = 0;
+  rc = acceptance == 0 ? verify_tree_greedy_core(m, tok, par, n, best, &len, &bonus, true)
+                       : verify_tree_typical_core(m, tok, par, n, epsilon, delta, best, &len, &bonus, true);
+  if (rc != SPEC_OK) return rc;
+  // 5. Commit, with the bonus while the budget allows (:786-800).
+  int nc = 0;
+  for (int i = 1; i < len; ++i) commits_out[nc++] = tok[best[i]];
+  const bool with_bonus = nc < budget;
+  if (with_bonus) commits_out[nc++] = bonus;
+  *n_out = nc;
+  if (!with_bonus) {
+    const cudaError_t e = cudaMemcpy(hidden_out, m->hidden_out + (size_t)best[len - 1] * m->cfg.hidden,
+                                     (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "tree hidden row"));
     return spec_commit_tree_path(m, tok, par, n, best, len);
   }
   rc = spec_commit_tree_path(m, tok, par, n, best, len);

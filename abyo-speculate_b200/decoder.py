@@ -311,6 +311,22 @@ class B200Decoder:
                                                _ptr(lp, ctypes.c_float)))
         return ids[:n], lp[:n]
 
+    def medusa_round(self, hidden: np.ndarray, top_k: int, topology: str = "cartesian", acceptance: str = "greedy",
+                     epsilon: float = 0.0, delta: float = 0.0, budget: int = 1 << 30) -> Tuple[List[int], np.ndarray]:
+        """One Medusa round (medusa.rs:761-810) in one call: (committed tokens,
+        the hidden row of the last one).  topology: "greedy" | "cartesian";
+        acceptance: "greedy" | "typical" (with epsilon, delta)."""
+        topo = {"greedy": 0, "cartesian": 1}[topology]
+        acc = {"greedy": 0, "typical": 1}[acceptance]
+        h = np.ascontiguousarray(np.asarray(hidden, dtype=np.float32).reshape(-1))
+        out = np.zeros(self.medusa_num_heads() + 1, dtype=np.uint32)
+        nxt = np.zeros(self.hidden_size(), dtype=np.float32)
+        n = ctypes.c_int()
+        self._check(self._lib.spec_medusa_round(self._h, _ptr(h, ctypes.c_float), int(top_k), topo, acc,
+                                                float(epsilon), float(delta), int(budget), _ptr(out, ctypes.c_uint32),
+                                                ctypes.byref(n), _ptr(nxt, ctypes.c_float)))
+        return [int(t) for t in out[:n.value]], nxt
+
     def embed_tokens(self, ids: Sequence[int]) -> np.ndarray:
         a = _u32(ids)
         out = np.empty((a.size, self._hidden), dtype=np.float32)

@@ -286,6 +286,23 @@ int spec_medusa_attach_synthetic(spec_model* m, int n_heads, int residual_layers
 int spec_medusa_topk(spec_model* m, const float* hidden, int k, int32_t* ids_out, float* logprobs_out);
 /* Number of attached Medusa heads (0 when none). */
 int spec_medusa_num_heads(const spec_model* m);
+/* One Medusa round, the body of run_medusa_real's loop
+ * (crates/speculate/src/methods/medusa.rs:761-810), in one call: the heads'
+ * top_k from `hidden` (the target's last hidden row, host, hidden_size
+ * floats), the draft tree of `topology` (0 = Greedy: each head's top-1 as a
+ * chain, :167-170; 1 = CartesianProduct: BFS layers, every candidate of head
+ * d under every node of layer d, :172-189), the tree forward keeping KV, the
+ * walk with `acceptance` (0 = Greedy, as spec_verify_tree_greedy; 1 =
+ * Typical {epsilon, delta}, as spec_verify_tree_typical), the commit of the
+ * accepted path and, while fewer than `budget` (max_new_tokens - generated)
+ * tokens are committed, the argmax bonus of the deepest accepted node.
+ * commits_out (room for n_heads + 1) receives the committed tokens, *n_out
+ * their count, hidden_out (hidden_size floats) the hidden row of the last
+ * committed token: the next round's `hidden`.  History and KV afterwards are
+ * those of the reference's observe(committed).  A tree over SPEC_MAX_ROWS
+ * nodes returns SPEC_ERR_UNSUPPORTED with the state unchanged. */
+int spec_medusa_round(spec_model* m, const float* hidden, int top_k, int topology, int acceptance, float epsilon,
+                      float delta, int budget, uint32_t* commits_out, int* n_out, float* hidden_out);
 
 /* ---- device-side acceptance ------------------------------------------------
  * Greedy (temperature 0) vanilla verify: one batched forward of [last]+drafts

@@ -117,3 +117,82 @@ def test_verify_tree_typical_matches_oracle(pkg, tiny_gguf, accept, name):
     with pytest.raises(pkg.SamplingError):
         dec.verify_tree_typical(pkg.DraftTree([prompt[-1] + 1 if prompt[-1] + 1 < V else 0], [0]), 0.1, 0.1)
     dec.close()
+
+
+def _medusa_tree(pkg, root, ids, topology):
+    """medusa.rs:167-189: the greedy chain of each head's top-1, or the
+    Cartesian product in BFS layers."""
+    if topology == "greedy":
+        return pkg.DraftTree.linear(int(root), [int(c[0]) for c in ids])
+    tokens, parents, prev = [int(root)], [0], [0]
+    for cands in ids:
+        nxt = []
+        for p in prev:
+            for c in cands:
+                tokens.append(int(c))
+                parents.append(p)
+                nxt.append(len(tokens) - 1)
+        prev = nxt
+    return pkg.DraftTree(tokens, parents)
+
+
+def _medusa_round_by_trait_calls(pkg, dec, hidden, k, topology, acceptance, eps, delta, budget):
+    """run_medusa_real's loop body (medusa.rs:761-810) from the trait calls:
+    heads' top-k, tree, tree forward + walk, commit of the path, bonus."""
+    root = dec.history()[-1]
+    ids, _ = dec.medusa_topk(hidden, k)
+    tree = _medusa_tree(pkg, root, ids, topology)
+    if acceptance == "greedy":
+        best, bonus = dec.verify_tree_greedy(tree)
+    else:
+        best, bonus = dec.verify_tree_typical(tree, eps, delta)
+    committed = [tree.token_at(i) for i in best[1:]]
+    dec.commit_tree_path(tree, best)
+    if len(committed) < budget:
+        committed.append(int(bonus))
+        return committed, dec.observe_returning_last_hidden([int(bonus)])
+    return committed, None
+
+
+@pytest.mark.parametrize("name,heads,k,topology,acceptance", [
+    ("llama_q4km", 4, 2, "cartesian", "greedy"),
+    ("qwen_q4km", 3, 3, "cartesian", "typical"),
+    ("llama_bf16", 4, 2, "greedy", "typical"),
+])
+def test_native_medusa_round_equals_trait_calls(pkg, tiny_gguf, name, heads, k, topology, acceptance):
+    """spec_medusa_round against the same rounds made of trait calls: equal
+    commits, histories, KV lengths and next hidden rows (bit for bit) over
+    several rounds, the last one cut by the token budget."""
+    path = tiny_gguf(name)
+    a = pkg.B200Decoder.from_gguf(path, max_ctx=256)
+    b = pkg.B200Decoder.from_gguf(path, max_ctx=256)
+    for d in (a, b):
+        d.medusa_attach_synthetic(heads, 1, 17)
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, a.vocab_size(), size=19).tolist()
+    ha = a.observe_returning_last_hidden(prompt)
+    hb = b.observe_returning_last_hidden(prompt)
+    assert np.array_equal(ha.view(np.uint32), hb.view(np.uint32))
+    eps, delta = 0.002, 0.3
+    total, max_new = 0, 14
+    while total < max_new:
+        budget = max_new - total
+        ca, ha = a.medusa_round(ha, k, topology, acceptance, eps, delta, budget)
+        cb, hb = _medusa_round_by_trait_calls(pkg, b, hb, k, topology, acceptance, eps, delta, budget)
+        assert ca == cb
+        assert a.history() == b.history() and a.kv_len() == b.kv_len()
+        if hb is not None:
+            assert np.array_equal(ha.view(np.uint32), hb.view(np.uint32))
+        total += len(ca)
+        if hb is None:
+            break
+    # The accepted path is committed whole; the budget only withholds the bonus (:786-800).
+    assert total >= max_new and len(a.history()) == len(prompt) + total
+    # A Cartesian tree over SPEC_MAX_ROWS nodes is refused with the state unchanged.
+    if topology == "cartesian":
+        hist, kv = a.history(), a.kv_len()
+        with pytest.raises(pkg.SpecError):
+            a.medusa_round(ha, 8, "cartesian")
+        assert a.history() == hist and a.kv_len() == kv
+    a.close()
+    b.close()
