@@ -1988,10 +1988,107 @@ int spec_rollback_to(spec_model* m, int len) {
   return SPEC_OK;
 }
 
+// A tree of more than kMaxRows nodes, cut into forwards of at most kMaxRows
+// rows.  Nodes are taken in index order; each joins the current chunk with
+// every ancestor it lacks there, or, when they do not fit, starts the next
+// chunk with its ancestor chain.  A chunk is closed under ancestors, so it is
+// itself a tree rooted at node 0 in which every row attends to exactly its
+// own ancestors (and, as in one forward, to the whole prefix); its RoPE
+// positions are prefix + depth as before.  A node's logits come from the
+// chunk that took it as `primary`; ancestors repeated in later chunks only
+// provide keys.
+struct TreeChunk {
+  std::vector<int> nodes;    // global node indices, ascending
+  std::vector<int> primary;  // global nodes whose logits this chunk provides
+};
+
+static int plan_tree_chunks(spec_model* m, const int32_t* parents, int n, std::vector<TreeChunk>& chunks) {
+  chunks.clear();
+  std::vector<char> in(n, 0);
+  std::vector<int> chain;
+  TreeChunk cur;
+  for (int i = 0; i < n; ++i) {
+    chain.clear();
+    for (int a = i;; a = parents[a]) {
+      chain.push_back(a);
+      if (a == 0) break;
+    }
+    if ((int)chain.size() > kMaxRows) return m->fail(SPEC_ERR_UNSUPPORTED, "tree deeper than SPEC_MAX_ROWS - 1");
+    int missing = 0;
+    for (int a : chain) missing += !in[a];
+    if ((int)cur.nodes.size() + missing > kMaxRows) {
+      for (int g : cur.nodes) in[g] = 0;
+      chunks.push_back(std::move(cur));
+      cur = TreeChunk();
+    }
+    for (int a : chain)
+      if (!in[a]) {
+        in[a] = 1;
+        cur.nodes.push_back(a);
+      }
+    cur.primary.push_back(i);
+  }
+  if (!cur.nodes.empty()) chunks.push_back(std::move(cur));
+  for (TreeChunk& c : chunks) std::sort(c.nodes.begin(), c.nodes.end());
+  return SPEC_OK;
+}
+
+// spec_tree_logits for trees over kMaxRows nodes: one forward per chunk (each
+// overwrites the tree's KV window), the primary rows copied out, then the
+// same restore as the single-forward path.
+static int big_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out) {
+  for (int i = 1; i < n; ++i)
+    if (parents[i] < 0 || parents[i] >= i)
+      return m->fail(SPEC_ERR_INVALID, "node " + std::to_string(i) + " has parent index " +
+                                           std::to_string(parents[i]) + ", which is not strictly smaller");
+  for (int i = 0; i < n; ++i)
+    if (tokens[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  const uint32_t last = m->history.back();
+  if (tokens[0] != last)
+    return m->fail(SPEC_ERR_INVALID, "tree root (" + std::to_string(tokens[0]) +
+                                         ") must equal last committed token (" + std::to_string(last) + ")");
+  const int pre = m->cache_len;
+  const int prefix = (int)m->history.size() - 1;
+  if (prefix > pre) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
+  std::vector<TreeChunk> chunks;
+  int rc = plan_tree_chunks(m, parents, n, chunks);
+  if (rc != SPEC_OK) return rc;
+  const size_t V = (size_t)m->cfg.vocab;
+  std::vector<int> local(n, -1);
+  uint32_t lt[kMaxRows];
+  int32_t lp[kMaxRows];
+  for (const TreeChunk& c : chunks) {
+    const int cn = (int)c.nodes.size();
+    for (int j = 0; j < cn; ++j) local[c.nodes[j]] = j;
+    for (int j = 0; j < cn; ++j) {
+      const int g = c.nodes[j];
+      lt[j] = tokens[g];
+      lp[j] = j ? local[parents[g]] : 0;
+    }
+    rc = tree_forward(m, lt, lp, cn, prefix, F_LOGITS);
+    if (rc == SPEC_OK) {
+      const cudaError_t e =
+          cudaMemcpyAsync(m->logits_host, m->logits, (size_t)cn * V * 4, cudaMemcpyDeviceToHost, m->stream);
+      if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "tree logits"));
+    }
+    if (rc == SPEC_OK) rc = finish(m);
+    if (rc != SPEC_OK) return rc;
+    for (int g : c.primary) memcpy(out + (size_t)g * V, m->logits_host + (size_t)local[g] * V, V * 4);
+  }
+  m->cache_len = prefix;
+  rc = forward_advance(m, &last, 1, nullptr);
+  if (rc != SPEC_OK) {
+    m->cache_len = pre;
+    return rc;
+  }
+  return copy_last_row(m, out);
+}
+
 int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out) {
   if (!m || !tokens || !parents || !out) return SPEC_ERR_INVALID;
   DeviceGuard dg_(m->device);
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
+  if (n > kMaxRows) return big_tree_logits(m, tokens, parents, n, out);
   int rc = check_tree(m, tokens, parents, n);
   if (rc != SPEC_OK) return rc;
   const uint32_t last = m->history.back();

@@ -57,6 +57,43 @@ KIND_NAMES = {0: "embed", 2: "attention (split + combine)", 8: "fwd_kernel (pers
 GEMV_KINDS = (8,)
 
 
+def run_tree_acceptance(pkg, dec, stream, args):
+    """Tree verify with greedy and with Medusa typical acceptance
+    (spec_verify_tree_greedy / spec_verify_tree_typical) on the target: the
+    31-node Cartesian tree of Medusa's default 4 heads x top-2, seeded draft
+    tokens, KV kept; CUDA events around `steps` back-to-back calls each."""
+    import torch
+
+    rng = np.random.default_rng(23)
+    hist = dec.history()
+    tokens, parents, prev = [int(hist[-1])], [0], [0]
+    for _ in range(4):
+        nxt = []
+        for p in prev:
+            for t in rng.integers(0, CFG["vocab"], size=2).tolist():
+                tokens.append(int(t))
+                parents.append(p)
+                nxt.append(len(tokens) - 1)
+        prev = nxt
+    tree = pkg.DraftTree(tokens, parents)
+    out = {"nodes": len(tokens)}
+    for name, call in (("greedy", lambda: dec.verify_tree_greedy(tree)),
+                       ("typical", lambda: dec.verify_tree_typical(tree, 0.09, 0.3))):
+        for _ in range(args.warmup):
+            call()
+        torch.cuda.synchronize()
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            call()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        out[f"{name}_us"] = round(t0.elapsed_time(t1) / args.steps * 1e3, 2)
+    out["note"] = ("tree forward (KV kept) + acceptance: greedy = device argmax + walk; typical = medusa.rs:424-445 "
+                   "(epsilon 0.09, delta 0.3; per-row softmax and entropy in sequential f32 order) + walk")
+    return out
+
+
 def dist_env():
     ws = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -682,6 +719,7 @@ def run_b200(args, ws, rank, local, dist):
     f1.record(stream)
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(dist, f0.elapsed_time(f1))
+    tree_block = run_tree_acceptance(pkg, dec, stream, args) if tp == 1 else None
     sd_block = run_sd_greedy(pkg, dec, prompt, local) if (tp == 1 and not args.no_sd) else None
     sd_shared = run_sd_shared(pkg, local, prompt) if (tp == 1 and not args.no_sd) else None
     # The single-GPU microbench runs only at N=1 (under tensor parallelism the
@@ -744,6 +782,7 @@ def run_b200(args, ws, rank, local, dist):
         "kernels": per_kind,
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": 1296 + 4 * K_DRAFT,
                 "d2h_bytes_per_step": (K_DRAFT + 1) * CFG["vocab"] * 4 + 4},
+        "tree_acceptance_31": tree_block,
         "rejection_t1": {"value": round(models * args.steps / (rj_ms / 1e3), 3), "unit": UNIT,
                          "verify_us": round(rj_ms / args.steps * 1e3, 2),
                          "mean_commits": round(rj_commits / max(args.steps, 1), 3),

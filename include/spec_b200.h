@@ -169,7 +169,11 @@ int spec_rollback_to(spec_model* m, int len);
  * A draft tree is (tokens[n], parents[n]) in BFS order with parents[0]
  * ignored and parents[i] < i (crates/speculate/src/tree.rs:38-74).          */
 /* TreeDecoder::tree_logits (mod.rs:135-144; quantized_llama.rs:262-325);
- * out: n x V.  History and KV are restored. */
+ * out: n x V.  History and KV are restored.  A tree of more than
+ * SPEC_MAX_ROWS nodes runs as several forwards over ancestor-closed chunks
+ * (each node with all its ancestors, at most SPEC_MAX_ROWS rows); only a node
+ * more than SPEC_MAX_ROWS - 1 levels deep is refused (SPEC_ERR_UNSUPPORTED).
+ * The other tree calls take at most SPEC_MAX_ROWS nodes. */
 int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out);
 /* TreeDecoder::tree_logits_keep_kv (mod.rs:196-210; quantized_llama.rs:341-394);
  * logits_out: n x V (may be NULL), hidden_out: n x hidden (may be NULL).

@@ -121,6 +121,57 @@ def test_tree_logits_and_restore(pkg, oracle, tiny_gguf, name):
     assert np.array_equal(dec.next_logits().view(np.uint32), nxt.view(np.uint32))
 
 
+@pytest.mark.parametrize("name", ["llama_q4km", "qwen_q4km", "llama_bf16"])
+def test_tree_logits_over_max_rows(pkg, oracle, tiny_gguf, name):
+    """Trees over SPEC_MAX_ROWS nodes (the reference's DraftTree has no cap):
+    a 121-node Cartesian tree (4 levels of 3, Medusa's 4 heads x top-3) and a
+    deep 70-node chain with side branches run as ancestor-closed chunks of at
+    most 64 rows.  Every node's row matches the oracle's single tree forward,
+    each node's row equals its own ancestor chain's tree forward, and the
+    state is restored as for a small tree."""
+    dec, ref = _pair(pkg, oracle, tiny_gguf(name))
+    V = dec.vocab_size()
+    rng = np.random.default_rng(31)
+    prompt = _prompt(V, 23, 12)
+    dec.observe(prompt)
+    ref.observe(prompt)
+    nxt = dec.next_logits()
+    tokens, parents, prev = [prompt[-1]], [0], [0]
+    for _ in range(4):
+        layer = []
+        cands = rng.integers(0, V, size=3).tolist()
+        for p in prev:
+            for c in cands:
+                tokens.append(int(c))
+                parents.append(p)
+                layer.append(len(tokens) - 1)
+        prev = layer
+    chain_t, chain_p = [prompt[-1]], [0]
+    for i in range(1, 70):
+        chain_t.append(int(rng.integers(0, V)))
+        chain_p.append(i - 1 if i % 5 else max(0, i - 3))
+    for tt, pp in ((tokens, parents), (chain_t, chain_p)):
+        tree = pkg.DraftTree(tt, pp)
+        a = dec.tree_logits(tree)
+        b = ref.tree_logits(tt, pp)
+        assert a.shape == (len(tt), V)
+        assert np.abs(a - b).max() <= TOL
+        assert np.array_equal(a[0].view(np.uint32), nxt.view(np.uint32))
+        assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+        assert np.array_equal(dec.next_logits().view(np.uint32), nxt.view(np.uint32))
+        for i in (len(tt) - 1, len(tt) // 2, 40):
+            anc = tree.path_to(i)
+            if len(anc) > 64:
+                continue
+            row = dec.tree_logits(pkg.DraftTree([tt[j] for j in anc], [0] + list(range(len(anc) - 1))))[-1]
+            assert np.abs(row - a[i]).max() <= TOL
+    # A chain deeper than 64 nodes cannot be cut into ancestor-closed chunks.
+    deep = pkg.DraftTree([prompt[-1]] + [5] * 64, [0] + list(range(64)))
+    with pytest.raises(pkg.SpecError):
+        dec.tree_logits(deep)
+    assert np.array_equal(dec.next_logits().view(np.uint32), nxt.view(np.uint32))
+
+
 @pytest.mark.parametrize("name", MODELS)
 def test_tree_keep_kv_commit_path(pkg, oracle, tiny_gguf, name):
     dec, ref = _pair(pkg, oracle, tiny_gguf(name))
