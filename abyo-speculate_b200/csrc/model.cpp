@@ -151,6 +151,12 @@ struct spec_model {
   unsigned long long* argmax_slots = nullptr;  // row argmax scratch (self-clearing)
   std::shared_ptr<EagleHead> eagle;            // spec_eagle_attach*: device memory owned via dalloc
   std::shared_ptr<MedusaHeads> medusa;         // spec_medusa_attach*: device memory owned via dalloc
+  // A tree over kMaxRows nodes leaves only its last chunk's KV rows in the
+  // tree window: tree_window lists that chunk's nodes in slot order, for the
+  // tree whose signature is tree_window_sig (0: no such tree; every forward
+  // clears it).
+  std::vector<int> tree_window;
+  uint64_t tree_window_sig = 0;
   unsigned long long* topk_part = nullptr;     // row top-k scratch (allocated on first use)
   int* topk_ids = nullptr;
   float* topk_vals = nullptr;
@@ -1073,6 +1079,7 @@ void begin_step(spec_model* m, int flags) {
 int run_forward(spec_model* m, int M, int flags, const std::vector<int>* collect = nullptr) {
   if (m->tp_size > 1 && !m->tp_connected)
     return m->fail(SPEC_ERR_INVALID, "tensor-parallel handle used before spec_tp_connect");
+  m->tree_window_sig = 0;
   begin_step(m, flags);
   cudaError_t e = cudaSuccess;
   const int key = M | (flags << 8);
@@ -2033,16 +2040,95 @@ static int plan_tree_chunks(spec_model* m, const int32_t* parents, int n, std::v
   return SPEC_OK;
 }
 
-// spec_tree_logits for trees over kMaxRows nodes: one forward per chunk (each
-// overwrites the tree's KV window), the primary rows copied out, then the
-// same restore as the single-forward path.
-static int big_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out) {
+// FNV-1a over a tree's size, tokens and parents: identifies the tree whose
+// last chunk is in the KV window.
+static uint64_t tree_signature(const uint32_t* tokens, const int32_t* parents, int n) {
+  uint64_t h = 1469598103934665603ull;
+  auto mix = [&](uint32_t v) {
+    for (int b = 0; b < 4; ++b) {
+      h ^= (v >> (8 * b)) & 0xffu;
+      h *= 1099511628211ull;
+    }
+  };
+  mix((uint32_t)n);
+  for (int i = 0; i < n; ++i) {
+    mix(tokens[i]);
+    mix((uint32_t)(i ? parents[i] : 0));
+  }
+  return h ? h : 1;
+}
+
+static int check_big_tree(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n) {
   for (int i = 1; i < n; ++i)
     if (parents[i] < 0 || parents[i] >= i)
       return m->fail(SPEC_ERR_INVALID, "node " + std::to_string(i) + " has parent index " +
                                            std::to_string(parents[i]) + ", which is not strictly smaller");
   for (int i = 0; i < n; ++i)
     if (tokens[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
+  return SPEC_OK;
+}
+
+// Tokens and local parents of one chunk; local[] maps global -> slot.
+static void chunk_arrays(const TreeChunk& c, const uint32_t* tokens, const int32_t* parents, std::vector<int>& local,
+                         uint32_t* lt, int32_t* lp) {
+  const int cn = (int)c.nodes.size();
+  for (int j = 0; j < cn; ++j) local[c.nodes[j]] = j;
+  for (int j = 0; j < cn; ++j) {
+    const int g = c.nodes[j];
+    lt[j] = tokens[g];
+    lp[j] = j ? local[parents[g]] : 0;
+  }
+}
+
+// The forwards of a tree over kMaxRows nodes at `prefix`, one per chunk: the
+// primary rows' logits (logits_out, n x V), final hidden rows (hidden_out,
+// n x H) and argmaxes (argmax_out, n) go to the host, any of them NULL.  The
+// last chunk's KV rows stay in the tree window and are recorded.
+static int big_tree_run(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, int prefix,
+                        float* logits_out, float* hidden_out, int32_t* argmax_out) {
+  std::vector<TreeChunk> chunks;
+  int rc = plan_tree_chunks(m, parents, n, chunks);
+  if (rc != SPEC_OK) return rc;
+  const size_t V = (size_t)m->cfg.vocab, H = (size_t)m->cfg.hidden;
+  const int flags = (logits_out || argmax_out ? F_LOGITS : 0) | (hidden_out ? F_HIDDEN : 0);
+  std::vector<int> local(n, -1);
+  uint32_t lt[kMaxRows];
+  int32_t lp[kMaxRows];
+  for (const TreeChunk& c : chunks) {
+    const int cn = (int)c.nodes.size();
+    chunk_arrays(c, tokens, parents, local, lt, lp);
+    rc = tree_forward(m, lt, lp, cn, prefix, flags);
+    cudaError_t e = cudaSuccess;
+    if (rc == SPEC_OK && logits_out)
+      e = cudaMemcpyAsync(m->logits_host, m->logits, (size_t)cn * V * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (rc == SPEC_OK && hidden_out && e == cudaSuccess)
+      e = cudaMemcpyAsync(m->hidden_host, m->hidden_out, (size_t)cn * H * 4, cudaMemcpyDeviceToHost, m->stream);
+    if (rc == SPEC_OK && argmax_out && e == cudaSuccess) {
+      e = launch_row_argmax(m->logits, cn, (int)V, m->argmax_dev, nullptr, m->argmax_slots, m->argmax_counters,
+                            m->stream);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(m->argmax_host, m->argmax_dev, (size_t)cn * 4, cudaMemcpyDeviceToHost, m->stream);
+    }
+    if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "tree chunk outputs"));
+    if (rc == SPEC_OK) rc = finish(m);
+    if (rc != SPEC_OK) return rc;
+    for (int g : c.primary) {
+      const int j = local[g];
+      if (logits_out) memcpy(logits_out + (size_t)g * V, m->logits_host + (size_t)j * V, V * 4);
+      if (hidden_out) memcpy(hidden_out + (size_t)g * H, m->hidden_host + (size_t)j * H, H * 4);
+      if (argmax_out) argmax_out[g] = m->argmax_host[j];
+    }
+  }
+  m->tree_window = chunks.back().nodes;
+  m->tree_window_sig = tree_signature(tokens, parents, n);
+  return SPEC_OK;
+}
+
+// spec_tree_logits for trees over kMaxRows nodes: the chunk forwards, then
+// the same restore as the single-forward path.
+static int big_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out) {
+  int rc = check_big_tree(m, tokens, parents, n);
+  if (rc != SPEC_OK) return rc;
   const uint32_t last = m->history.back();
   if (tokens[0] != last)
     return m->fail(SPEC_ERR_INVALID, "tree root (" + std::to_string(tokens[0]) +
@@ -2050,31 +2136,9 @@ static int big_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t*
   const int pre = m->cache_len;
   const int prefix = (int)m->history.size() - 1;
   if (prefix > pre) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
-  std::vector<TreeChunk> chunks;
-  int rc = plan_tree_chunks(m, parents, n, chunks);
+  if (prefix + kMaxRows > m->t_max) return m->fail(SPEC_ERR_INVALID, "KV capacity exceeded");
+  rc = big_tree_run(m, tokens, parents, n, prefix, out, nullptr, nullptr);
   if (rc != SPEC_OK) return rc;
-  const size_t V = (size_t)m->cfg.vocab;
-  std::vector<int> local(n, -1);
-  uint32_t lt[kMaxRows];
-  int32_t lp[kMaxRows];
-  for (const TreeChunk& c : chunks) {
-    const int cn = (int)c.nodes.size();
-    for (int j = 0; j < cn; ++j) local[c.nodes[j]] = j;
-    for (int j = 0; j < cn; ++j) {
-      const int g = c.nodes[j];
-      lt[j] = tokens[g];
-      lp[j] = j ? local[parents[g]] : 0;
-    }
-    rc = tree_forward(m, lt, lp, cn, prefix, F_LOGITS);
-    if (rc == SPEC_OK) {
-      const cudaError_t e =
-          cudaMemcpyAsync(m->logits_host, m->logits, (size_t)cn * V * 4, cudaMemcpyDeviceToHost, m->stream);
-      if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "tree logits"));
-    }
-    if (rc == SPEC_OK) rc = finish(m);
-    if (rc != SPEC_OK) return rc;
-    for (int g : c.primary) memcpy(out + (size_t)g * V, m->logits_host + (size_t)local[g] * V, V * 4);
-  }
   m->cache_len = prefix;
   rc = forward_advance(m, &last, 1, nullptr);
   if (rc != SPEC_OK) {
@@ -2117,12 +2181,33 @@ int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* paren
   return copy_last_row(m, out);
 }
 
+// Over kMaxRows nodes: the chunk forwards; the KV window keeps the last
+// chunk's rows (cache_len = prefix + its size) and spec_commit_tree_path
+// brings the accepted path's chunk back when it is another one.
+static int big_tree_keep_kv(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* logits_out,
+                            float* hidden_out, int32_t* argmax_out) {
+  int rc = check_big_tree(m, tokens, parents, n);
+  if (rc != SPEC_OK) return rc;
+  const uint32_t last = m->history.back();
+  if (tokens[0] != last)
+    return m->fail(SPEC_ERR_INVALID, "tree root (" + std::to_string(tokens[0]) +
+                                         ") must equal last committed token (" + std::to_string(last) + ")");
+  const int prefix = (int)m->history.size() - 1;
+  if (prefix > m->cache_len) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
+  if (prefix + kMaxRows > m->t_max) return m->fail(SPEC_ERR_INVALID, "KV capacity exceeded");
+  rc = big_tree_run(m, tokens, parents, n, prefix, logits_out, hidden_out, argmax_out);
+  if (rc != SPEC_OK) return rc;
+  m->cache_len = prefix + (int)m->tree_window.size();
+  return SPEC_OK;
+}
+
 int spec_tree_logits_keep_kv(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
                              float* logits_out, float* hidden_out) {
   if (!m || !tokens || !parents) return SPEC_ERR_INVALID;
   DeviceGuard dg_(m->device);
   m->last_valid = false;
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
+  if (n > kMaxRows) return big_tree_keep_kv(m, tokens, parents, n, logits_out, hidden_out, nullptr);
   int rc = check_tree(m, tokens, parents, n);
   if (rc != SPEC_OK) return rc;
   const uint32_t last = m->history.back();
@@ -2153,20 +2238,61 @@ int spec_commit_tree_path(spec_model* m, const uint32_t* tokens, const int32_t* 
   DeviceGuard dg_(m->device);
   m->last_valid = false;
   if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "commit_tree_path with empty history");
-  int rc = check_tree(m, tokens, parents, n);
+  const bool big = n > kMaxRows;
+  int rc = big ? check_big_tree(m, tokens, parents, n) : check_tree(m, tokens, parents, n);
   if (rc != SPEC_OK) return rc;
   if (n_acc < 1 || accepted[0] != 0) return m->fail(SPEC_ERR_INVALID, "accepted path must start at the root (0)");
   const int prefix = (int)m->history.size() - 1;
-  for (int i = 0; i < n_acc; ++i) {
+  for (int i = 0; i < n_acc; ++i)
     if (accepted[i] < 0 || accepted[i] >= n) return m->fail(SPEC_ERR_INVALID, "accepted index out of range");
-    if (prefix + accepted[i] >= m->cache_len)
+  // slot[i]: the tree-window slot holding accepted[i]'s KV row.
+  std::vector<int> slot(n_acc);
+  if (!big) {
+    for (int i = 0; i < n_acc; ++i) {
+      if (prefix + accepted[i] >= m->cache_len)
+        return m->fail(SPEC_ERR_INVALID, "accepted node is not in the KV cache");
+      slot[i] = accepted[i];
+    }
+  } else {
+    // A tree over kMaxRows nodes: the path must be a chain from the root
+    // (its nodes are then in one chunk), and that chunk's rows must be in the
+    // window, brought back by its forward if the window holds another one.
+    for (int i = 1; i < n_acc; ++i)
+      if (parents[accepted[i]] != accepted[i - 1])
+        return m->fail(SPEC_ERR_UNSUPPORTED, "over SPEC_MAX_ROWS nodes the accepted nodes must form a root path");
+    if (m->tree_window_sig == 0 || m->tree_window_sig != tree_signature(tokens, parents, n) ||
+        prefix + (int)m->tree_window.size() != m->cache_len)
       return m->fail(SPEC_ERR_INVALID, "accepted node is not in the KV cache");
+    std::vector<int> local(n, -1);
+    for (size_t j = 0; j < m->tree_window.size(); ++j) local[m->tree_window[j]] = (int)j;
+    bool in_window = true;
+    for (int i = 0; i < n_acc; ++i) in_window &= local[accepted[i]] >= 0;
+    if (!in_window) {
+      std::vector<TreeChunk> chunks;
+      rc = plan_tree_chunks(m, parents, n, chunks);
+      if (rc != SPEC_OK) return rc;
+      const int want = accepted[n_acc - 1];
+      const TreeChunk* hit = nullptr;
+      for (const TreeChunk& c : chunks)
+        if (std::find(c.primary.begin(), c.primary.end(), want) != c.primary.end()) hit = &c;
+      uint32_t lt[kMaxRows];
+      int32_t lp[kMaxRows];
+      std::fill(local.begin(), local.end(), -1);
+      chunk_arrays(*hit, tokens, parents, local, lt, lp);
+      rc = tree_forward(m, lt, lp, (int)hit->nodes.size(), prefix, 0);
+      if (rc == SPEC_OK) rc = finish(m);
+      if (rc != SPEC_OK) return rc;
+      m->tree_window = hit->nodes;
+      m->tree_window_sig = tree_signature(tokens, parents, n);
+      m->cache_len = prefix + (int)hit->nodes.size();
+    }
+    for (int i = 0; i < n_acc; ++i) slot[i] = local[accepted[i]];
   }
   // keep = [0..prefix) ++ [prefix + ti]: the prefix is the identity, so only
   // the accepted tree rows move (quantized_llama.rs:426-433).
   int nmove = 0;
   for (int i = 0; i < n_acc; ++i) {
-    const int src = prefix + accepted[i], dst = prefix + i;
+    const int src = prefix + slot[i], dst = prefix + i;
     if (src != dst) {
       m->idx_host[nmove] = src;
       m->idx_host[kMaxRows + nmove] = dst;
@@ -3365,7 +3491,36 @@ int verify_tree_greedy_core(spec_model* m, const uint32_t* tokens, const int32_t
 int spec_verify_tree_greedy(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
                             int32_t* best_path, int* path_len, uint32_t* bonus) {
   if (!m || !tokens || !parents || !best_path || !path_len || !bonus) return SPEC_ERR_INVALID;
-  return verify_tree_greedy_core(m, tokens, parents, n, best_path, path_len, bonus, false);
+  if (n <= kMaxRows) return verify_tree_greedy_core(m, tokens, parents, n, best_path, path_len, bonus, false);
+  // Over kMaxRows nodes: the chunk forwards' argmaxes, the same walk.
+  DeviceGuard dg_(m->device);
+  m->last_valid = false;
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
+  std::vector<int32_t> am(n);
+  int rc = big_tree_keep_kv(m, tokens, parents, n, nullptr, nullptr, am.data());
+  if (rc != SPEC_OK) return rc;
+  std::vector<char> is_leaf(n, 1);
+  for (int i = 1; i < n; ++i) is_leaf[parents[i]] = 0;
+  std::vector<int> best = {0}, chain;
+  for (int leaf = 0; leaf < n; ++leaf) {
+    if (!is_leaf[leaf]) continue;
+    chain.clear();
+    for (int cur = leaf;; cur = parents[cur]) {
+      chain.push_back(cur);
+      if (cur == 0) break;
+    }
+    std::reverse(chain.begin(), chain.end());
+    int accepted = 0;
+    for (size_t w = 0; w + 1 < chain.size(); ++w) {
+      if ((uint32_t)am[chain[w]] == tokens[chain[w + 1]]) ++accepted;
+      else break;
+    }
+    if (accepted + 1 > (int)best.size()) best.assign(chain.begin(), chain.begin() + accepted + 1);
+  }
+  for (size_t i = 0; i < best.size(); ++i) best_path[i] = best[i];
+  *path_len = (int)best.size();
+  *bonus = (uint32_t)am[best.back()];
+  return SPEC_OK;
 }
 
 // Medusa's typical acceptance (medusa.rs:290-326 with Acceptance::Typical,

@@ -173,7 +173,12 @@ int spec_rollback_to(spec_model* m, int len);
  * SPEC_MAX_ROWS nodes runs as several forwards over ancestor-closed chunks
  * (each node with all its ancestors, at most SPEC_MAX_ROWS rows); only a node
  * more than SPEC_MAX_ROWS - 1 levels deep is refused (SPEC_ERR_UNSUPPORTED).
- * The other tree calls take at most SPEC_MAX_ROWS nodes. */
+ * spec_tree_logits_keep_kv, spec_verify_tree_greedy and spec_commit_tree_path
+ * take such trees too: the KV window then holds the last chunk's rows
+ * (spec_kv_len = prefix + that chunk's size), and the commit, whose accepted
+ * nodes must then form a path from the root, re-runs the path's chunk when
+ * the window holds another.  spec_verify_tree_typical and the EAGLE / Medusa
+ * rounds take at most SPEC_MAX_ROWS nodes. */
 int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out);
 /* TreeDecoder::tree_logits_keep_kv (mod.rs:196-210; quantized_llama.rs:341-394);
  * logits_out: n x V (may be NULL), hidden_out: n x hidden (may be NULL).

@@ -172,6 +172,64 @@ def test_tree_logits_over_max_rows(pkg, oracle, tiny_gguf, name):
     assert np.array_equal(dec.next_logits().view(np.uint32), nxt.view(np.uint32))
 
 
+def _cartesian(root, V, rng, levels=4, width=3):
+    tokens, parents, prev = [int(root)], [0], [0]
+    for _ in range(levels):
+        layer = []
+        cands = rng.integers(0, V, size=width).tolist()
+        for p in prev:
+            for c in cands:
+                tokens.append(int(c))
+                parents.append(p)
+                layer.append(len(tokens) - 1)
+        prev = layer
+    return tokens, parents
+
+
+@pytest.mark.parametrize("name", ["llama_q4km", "qwen_q4km"])
+def test_tree_over_max_rows_keep_kv_verify_commit(pkg, oracle, accept, tiny_gguf, name):
+    """A 121-node tree with the KV kept: logits and hidden rows against the
+    oracle; committing a path whose nodes are not in the last chunk's KV
+    rows (the chunk is brought back) and then the greedy verify's own best
+    path leave the KV the oracle's commit leaves (next logits after a
+    further token)."""
+    dec, ref = _pair(pkg, oracle, tiny_gguf(name))
+    V = dec.vocab_size()
+    rng = np.random.default_rng(41)
+    prompt = _prompt(V, 21, 14)
+    dec.observe(prompt)
+    ref.observe(prompt)
+    tt, pp = _cartesian(prompt[-1], V, rng)
+    tree = pkg.DraftTree(tt, pp)
+    lo, hi = dec.tree_logits_keep_kv(tree)
+    rlo, rhi = ref.tree_logits_keep_kv(tt, pp)
+    assert np.abs(lo - rlo).max() <= TOL and np.abs(hi - rhi).max() <= TOL
+    path = tree.path_to(5)  # nodes 0 -> 1 -> 5, all in the first chunk
+    dec.commit_tree_path(tree, path)
+    ref.commit_tree_path(tt, pp, path)
+    assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+    dec.observe([7])
+    ref.observe([7])
+    assert np.abs(dec.next_logits() - ref.next_logits()).max() <= TOL
+    # Greedy verify over the big tree: decisions from the device's own rows.
+    tt, pp = _cartesian(dec.history()[-1], V, rng)
+    tree = pkg.DraftTree(tt, pp)
+    rows, _ = dec.tree_logits_keep_kv(tree)
+    best, bonus = dec.verify_tree_greedy(tree)
+    assert (best, bonus) == accept.greedy_tree_accept(tt, pp, rows)
+    # A non-path commit is refused over 64 nodes; a path commit works.
+    with pytest.raises(pkg.SpecError):
+        dec.commit_tree_path(tree, [0, 1, 2])
+    deep = max(tree.paths(), key=len)
+    ref.tree_logits_keep_kv(tt, pp)
+    dec.commit_tree_path(tree, deep)
+    ref.commit_tree_path(tt, pp, deep)
+    assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+    dec.observe([int(bonus)])
+    ref.observe([int(bonus)])
+    assert np.abs(dec.next_logits() - ref.next_logits()).max() <= TOL
+
+
 @pytest.mark.parametrize("name", MODELS)
 def test_tree_keep_kv_commit_path(pkg, oracle, tiny_gguf, name):
     dec, ref = _pair(pkg, oracle, tiny_gguf(name))
