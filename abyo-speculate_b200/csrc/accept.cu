@@ -90,6 +90,37 @@ SPEC_DEV float block_seq_sum(const float* x, int n, float* buf, float* bcast) {
   return s;
 }
 
+// block_seq_sum over values computed while they are staged: f(i) for
+// i in [0, n).  Same chunking and add order as block_seq_sum.
+template <class F>
+SPEC_DEV void stage_chunk_of(F f, int base, int len, float* buf, bool skip_warp0) {
+  const int t0 = skip_warp0 ? 32 : 0;
+  if ((int)threadIdx.x < t0) return;
+  for (int i = threadIdx.x - t0; i < len; i += blockDim.x - t0) buf[i] = f(base + i);
+}
+
+template <class F>
+SPEC_DEV float block_seq_sum_of(F f, int n, float* buf, float* bcast) {
+  float s = 0.f;
+  const int nc = (n + kSeqChunk - 1) / kSeqChunk;
+  if (nc > 0) stage_chunk_of(f, 0, min(kSeqChunk, n), buf, false);
+  __syncthreads();
+  for (int c = 0; c < nc; ++c) {
+    const int base = c * kSeqChunk, len = min(kSeqChunk, n - base);
+    float* cur = buf + (c & 1) * kSeqChunk;
+    if (c + 1 < nc)
+      stage_chunk_of(f, base + kSeqChunk, min(kSeqChunk, n - base - kSeqChunk), buf + ((c + 1) & 1) * kSeqChunk,
+                     true);
+    if (threadIdx.x == 0) s = add_chunk(s, cur, len);
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *bcast = s;
+  __syncthreads();
+  s = *bcast;
+  __syncthreads();
+  return s;
+}
+
 // Thread 0: s += buf[0..len) in order, every partial sum stored to
 // out[0..len) (16-byte aligned).  Same add sequence as add_chunk.
 SPEC_DEV float add_chunk_pref(float s, const float* buf, int len, float* out) {
@@ -245,9 +276,15 @@ __global__ void __launch_bounds__(kRejThreads) target_softmax_kernel(float* rows
   }
   const float inv_t = __fdiv_rn(1.f, temperature);
   const float mx = block_max(row, V, red);
-  for (int i = threadIdx.x; i < V; i += blockDim.x) row[i] = exp_f32_cr(__fmul_rn(__fsub_rn(row[i], mx), inv_t));
-  __syncthreads();
-  const float s = block_seq_sum(row, V, s_buf, &s_sum);
+  // The exponentials are computed (and kept in the row) by the warps that
+  // stage each chunk for thread 0's sequential sum.
+  const float s = block_seq_sum_of(
+      [&](int i) {
+        const float e = exp_f32_cr(__fmul_rn(__fsub_rn(row[i], mx), inv_t));
+        row[i] = e;
+        return e;
+      },
+      V, s_buf, &s_sum);
   if (threadIdx.x == 0 && (!(s > 0.f) || !isfinite(s))) atomicCAS(status, 0, REJ_ERR_SOFTMAX);
   for (int i = threadIdx.x; i < V; i += blockDim.x) row[i] = __fdiv_rn(row[i], s);
 }
@@ -345,37 +382,6 @@ __global__ void __launch_bounds__(kRejThreads) rejection_walk_kernel(const float
 // f32::ln modelled as the correctly rounded log of the f32 argument (log in
 // double, one rounding), as exp is above.
 SPEC_DEV float ln_f32_cr(float x) { return (float)log((double)x); }
-
-// block_seq_sum over values computed while they are staged: f(i) for
-// i in [0, n).  Same chunking and add order as block_seq_sum.
-template <class F>
-SPEC_DEV void stage_chunk_of(F f, int base, int len, float* buf, bool skip_warp0) {
-  const int t0 = skip_warp0 ? 32 : 0;
-  if ((int)threadIdx.x < t0) return;
-  for (int i = threadIdx.x - t0; i < len; i += blockDim.x - t0) buf[i] = f(base + i);
-}
-
-template <class F>
-SPEC_DEV float block_seq_sum_of(F f, int n, float* buf, float* bcast) {
-  float s = 0.f;
-  const int nc = (n + kSeqChunk - 1) / kSeqChunk;
-  if (nc > 0) stage_chunk_of(f, 0, min(kSeqChunk, n), buf, false);
-  __syncthreads();
-  for (int c = 0; c < nc; ++c) {
-    const int base = c * kSeqChunk, len = min(kSeqChunk, n - base);
-    float* cur = buf + (c & 1) * kSeqChunk;
-    if (c + 1 < nc)
-      stage_chunk_of(f, base + kSeqChunk, min(kSeqChunk, n - base - kSeqChunk), buf + ((c + 1) & 1) * kSeqChunk,
-                     true);
-    if (threadIdx.x == 0) s = add_chunk(s, cur, len);
-    __syncthreads();
-  }
-  if (threadIdx.x == 0) *bcast = s;
-  __syncthreads();
-  s = *bcast;
-  __syncthreads();
-  return s;
-}
 
 // One CTA per tree row that has children.  softmax: NaN-skipping max, then
 // e_i = exp(l_i - max) and their sequential f32 sum; p_i = e_i / sum.
