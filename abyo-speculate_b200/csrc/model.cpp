@@ -18,6 +18,7 @@
 #include <string.h>
 
 #include <algorithm>
+#include <functional>
 #include <memory>
 #include <new>
 #include <numeric>
@@ -2084,13 +2085,18 @@ static void chunk_arrays(const TreeChunk& c, const uint32_t* tokens, const int32
 // primary rows' logits (logits_out, n x V), final hidden rows (hidden_out,
 // n x H) and argmaxes (argmax_out, n) go to the host, any of them NULL.  The
 // last chunk's KV rows stay in the tree window and are recorded.
+// `per_chunk`, when given, runs after each chunk's forward on the model's
+// stream with the chunk's rows in m->logits (`local`: global -> row).
+using ChunkHook = std::function<int(const TreeChunk&, const std::vector<int>&)>;
+
 static int big_tree_run(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, int prefix,
-                        float* logits_out, float* hidden_out, int32_t* argmax_out) {
+                        float* logits_out, float* hidden_out, int32_t* argmax_out,
+                        const ChunkHook& per_chunk = nullptr) {
   std::vector<TreeChunk> chunks;
   int rc = plan_tree_chunks(m, parents, n, chunks);
   if (rc != SPEC_OK) return rc;
   const size_t V = (size_t)m->cfg.vocab, H = (size_t)m->cfg.hidden;
-  const int flags = (logits_out || argmax_out ? F_LOGITS : 0) | (hidden_out ? F_HIDDEN : 0);
+  const int flags = (logits_out || argmax_out || per_chunk ? F_LOGITS : 0) | (hidden_out ? F_HIDDEN : 0);
   std::vector<int> local(n, -1);
   uint32_t lt[kMaxRows];
   int32_t lp[kMaxRows];
@@ -2110,6 +2116,7 @@ static int big_tree_run(spec_model* m, const uint32_t* tokens, const int32_t* pa
         e = cudaMemcpyAsync(m->argmax_host, m->argmax_dev, (size_t)cn * 4, cudaMemcpyDeviceToHost, m->stream);
     }
     if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "tree chunk outputs"));
+    if (rc == SPEC_OK && per_chunk) rc = per_chunk(c, local);
     if (rc == SPEC_OK) rc = finish(m);
     if (rc != SPEC_OK) return rc;
     for (int g : c.primary) {
@@ -2185,7 +2192,7 @@ int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* paren
 // chunk's rows (cache_len = prefix + its size) and spec_commit_tree_path
 // brings the accepted path's chunk back when it is another one.
 static int big_tree_keep_kv(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* logits_out,
-                            float* hidden_out, int32_t* argmax_out) {
+                            float* hidden_out, int32_t* argmax_out, const ChunkHook& per_chunk = nullptr) {
   int rc = check_big_tree(m, tokens, parents, n);
   if (rc != SPEC_OK) return rc;
   const uint32_t last = m->history.back();
@@ -2195,7 +2202,7 @@ static int big_tree_keep_kv(spec_model* m, const uint32_t* tokens, const int32_t
   const int prefix = (int)m->history.size() - 1;
   if (prefix > m->cache_len) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
   if (prefix + kMaxRows > m->t_max) return m->fail(SPEC_ERR_INVALID, "KV capacity exceeded");
-  rc = big_tree_run(m, tokens, parents, n, prefix, logits_out, hidden_out, argmax_out);
+  rc = big_tree_run(m, tokens, parents, n, prefix, logits_out, hidden_out, argmax_out, per_chunk);
   if (rc != SPEC_OK) return rc;
   m->cache_len = prefix + (int)m->tree_window.size();
   return SPEC_OK;
@@ -3589,10 +3596,83 @@ int verify_tree_typical_core(spec_model* m, const uint32_t* tokens, const int32_
   return SPEC_OK;
 }
 
+// Over kMaxRows nodes: after each chunk's forward, the children of the
+// chunk's primary nodes are decided against their parents' rows, up to
+// kMaxRows - 1 at a time (kernel slots 1.., parent = the parent's row in the
+// chunk, -1 in unused slots); then the walk of the small-tree path.
+static int big_verify_tree_typical(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n,
+                                   float epsilon, float delta, int32_t* best_path, int* path_len, uint32_t* bonus) {
+  std::vector<int32_t> am(n);
+  std::vector<char> pass(n, 0);
+  std::vector<std::vector<int>> kids(n);
+  for (int i = 1; i < n; ++i)
+    if (parents[i] >= 0 && parents[i] < i) kids[parents[i]].push_back(i);
+  int* flags_dev = m->rej_out_dev + 4;  // kMaxRows ints
+  int* flags_host = m->rej_out_host + 4;
+  auto decide = [&](const TreeChunk& c, const std::vector<int>& local) -> int {
+    std::vector<std::pair<int, int>> q;  // (row in the chunk, child node)
+    for (int p : c.primary)
+      for (int ch : kids[p]) q.push_back({local[p], ch});
+    const int cn = (int)c.nodes.size();
+    for (size_t b = 0; b < q.size(); b += kMaxRows - 1) {
+      const int nq = (int)std::min<size_t>(kMaxRows - 1, q.size() - b);
+      TypicalTree tt;
+      tt.n = std::max(cn, nq + 1);
+      tt.epsilon = epsilon;
+      tt.delta = delta;
+      for (int i = 0; i < tt.n; ++i) {
+        tt.tok[i] = 0;
+        tt.par[i] = -1;
+      }
+      for (int j = 0; j < nq; ++j) {
+        tt.par[j + 1] = q[b + j].first;
+        tt.tok[j + 1] = tokens[q[b + j].second];
+      }
+      cudaError_t e = cudaMemsetAsync(flags_dev, 0, (size_t)tt.n * 4, m->stream);
+      if (e == cudaSuccess) e = launch_typical_accept(m->logits, m->cfg.vocab, tt, flags_dev, m->stream);
+      if (e == cudaSuccess)
+        e = cudaMemcpyAsync(flags_host, flags_dev, (size_t)tt.n * 4, cudaMemcpyDeviceToHost, m->stream);
+      if (e == cudaSuccess) e = cudaStreamSynchronize(m->stream);
+      if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "typical acceptance"));
+      for (int j = 0; j < nq; ++j) pass[q[b + j].second] = flags_host[j + 1] != 0;
+    }
+    return SPEC_OK;
+  };
+  int rc = big_tree_keep_kv(m, tokens, parents, n, nullptr, nullptr, am.data(), decide);
+  if (rc != SPEC_OK) return rc;
+  std::vector<char> is_leaf(n, 1);
+  for (int i = 1; i < n; ++i) is_leaf[parents[i]] = 0;
+  std::vector<int> best = {0}, chain;
+  for (int leaf = 0; leaf < n; ++leaf) {
+    if (!is_leaf[leaf]) continue;
+    chain.clear();
+    for (int cur = leaf;; cur = parents[cur]) {
+      chain.push_back(cur);
+      if (cur == 0) break;
+    }
+    std::reverse(chain.begin(), chain.end());
+    int accepted = 0;
+    for (size_t w = 0; w + 1 < chain.size(); ++w) {
+      if (pass[chain[w + 1]]) ++accepted;
+      else break;
+    }
+    if (accepted + 1 > (int)best.size()) best.assign(chain.begin(), chain.begin() + accepted + 1);
+  }
+  for (size_t i = 0; i < best.size(); ++i) best_path[i] = best[i];
+  *path_len = (int)best.size();
+  *bonus = (uint32_t)am[best.back()];
+  return SPEC_OK;
+}
+
 int spec_verify_tree_typical(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float epsilon,
                              float delta, int32_t* best_path, int* path_len, uint32_t* bonus) {
   if (!m || !tokens || !parents || !best_path || !path_len || !bonus) return SPEC_ERR_INVALID;
-  return verify_tree_typical_core(m, tokens, parents, n, epsilon, delta, best_path, path_len, bonus, false);
+  if (n <= kMaxRows)
+    return verify_tree_typical_core(m, tokens, parents, n, epsilon, delta, best_path, path_len, bonus, false);
+  DeviceGuard dg_(m->device);
+  m->last_valid = false;
+  if (m->history.empty()) return m->fail(SPEC_ERR_INVALID, "tree_logits with empty history");
+  return big_verify_tree_typical(m, tokens, parents, n, epsilon, delta, best_path, path_len, bonus);
 }
 
 // The EAGLE-2 round tree (eagle.rs:584-593): the Cartesian product of the
@@ -3776,26 +3856,32 @@ int spec_medusa_round(spec_model* m, const float* hidden, int top_k, int topolog
   if (rc != SPEC_OK) return rc;
   // 2. The tree (:771): a chain of each head's top-1 (:167-170), or BFS
   // layers with every candidate of head d under every node of layer d
-  // (:172-189).
-  uint32_t tok[kMaxRows];
-  int32_t par[kMaxRows];
+  // (:172-189).  Over kMaxRows nodes it runs as ancestor-closed chunks.
+  constexpr int64_t kMaxMedusaNodes = 1 << 14;
+  int64_t total = 1;
+  if (topology == 0) {
+    total = 1 + nh;
+  } else {
+    int64_t width = 1;
+    for (int d = 0; d < nh; ++d) {
+      width *= top_k;
+      total += width;
+      if (total > kMaxMedusaNodes) break;
+    }
+  }
+  if (total > kMaxMedusaNodes) return m->fail(SPEC_ERR_UNSUPPORTED, "Medusa tree larger than 16384 nodes");
+  std::vector<uint32_t> tok((size_t)total);
+  std::vector<int32_t> par((size_t)total);
   int n = 1;
   tok[0] = root;
   par[0] = 0;
   if (topology == 0) {
-    if (nh + 1 > kMaxRows) return m->fail(SPEC_ERR_UNSUPPORTED, "Medusa tree larger than SPEC_MAX_ROWS nodes");
     for (int d = 0; d < nh; ++d) {
       tok[n] = (uint32_t)ids[(size_t)d * top_k];
       par[n] = n - 1;
       ++n;
     }
   } else {
-    int64_t total = 1, width = 1;
-    for (int d = 0; d < nh; ++d) {
-      width *= top_k;
-      total += width;
-      if (total > kMaxRows) return m->fail(SPEC_ERR_UNSUPPORTED, "Medusa tree larger than SPEC_MAX_ROWS nodes");
-    }
     int lo = 0, hi = 1;  // the previous layer's node range
     for (int d = 0; d < nh; ++d) {
       const int start = n;
@@ -3809,12 +3895,20 @@ int spec_medusa_round(spec_model* m, const float* hidden, int top_k, int topolog
       hi = n;
     }
   }
-  // 3-4. Tree forward (KV and per-node hidden rows kept) and the walk.
-  int32_t best[kMaxRows];
+  // 3-4. Tree forward (KV kept; per-node hidden rows too up to kMaxRows
+  // nodes) and the walk.
+  const bool small = n <= kMaxRows;
+  std::vector<int32_t> best((size_t)n);
   int len = 0;
   uint32_t bonus = 0;
-  rc = acceptance == 0 ? verify_tree_greedy_core(m, tok, par, n, best, &len, &bonus, true)
-                       : verify_tree_typical_core(m, tok, par, n, epsilon, delta, best, &len, &bonus, true);
+  if (small)
+    rc = acceptance == 0 ? verify_tree_greedy_core(m, tok.data(), par.data(), n, best.data(), &len, &bonus, true)
+                         : verify_tree_typical_core(m, tok.data(), par.data(), n, epsilon, delta, best.data(), &len,
+                                                    &bonus, true);
+  else
+    rc = acceptance == 0 ? spec_verify_tree_greedy(m, tok.data(), par.data(), n, best.data(), &len, &bonus)
+                         : spec_verify_tree_typical(m, tok.data(), par.data(), n, epsilon, delta, best.data(), &len,
+                                                    &bonus);
   if (rc != SPEC_OK) return rc;
   // 5. Commit, with the bonus while the budget allows (:786-800).
   int nc = 0;
@@ -3823,12 +3917,16 @@ int spec_medusa_round(spec_model* m, const float* hidden, int top_k, int topolog
   if (with_bonus) commits_out[nc++] = bonus;
   *n_out = nc;
   if (!with_bonus) {
-    const cudaError_t e = cudaMemcpy(hidden_out, m->hidden_out + (size_t)best[len - 1] * m->cfg.hidden,
-                                     (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost);
-    if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "tree hidden row"));
-    return spec_commit_tree_path(m, tok, par, n, best, len);
+    if (small) {
+      const cudaError_t e = cudaMemcpy(hidden_out, m->hidden_out + (size_t)best[len - 1] * m->cfg.hidden,
+                                       (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost);
+      if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "tree hidden row"));
+    }
+    rc = spec_commit_tree_path(m, tok.data(), par.data(), n, best.data(), len);
+    if (rc == SPEC_OK && !small) rc = spec_last_hidden_state(m, hidden_out);
+    return rc;
   }
-  rc = spec_commit_tree_path(m, tok, par, n, best, len);
+  rc = spec_commit_tree_path(m, tok.data(), par.data(), n, best.data(), len);
   if (rc == SPEC_OK) rc = spec_observe_returning_last_hidden(m, &bonus, 1, hidden_out);
   return rc;
 }

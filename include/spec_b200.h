@@ -177,8 +177,8 @@ int spec_rollback_to(spec_model* m, int len);
  * take such trees too: the KV window then holds the last chunk's rows
  * (spec_kv_len = prefix + that chunk's size), and the commit, whose accepted
  * nodes must then form a path from the root, re-runs the path's chunk when
- * the window holds another.  spec_verify_tree_typical and the EAGLE / Medusa
- * rounds take at most SPEC_MAX_ROWS nodes. */
+ * the window holds another.  spec_verify_tree_typical and spec_medusa_round
+ * do the same; spec_eagle_round takes at most SPEC_MAX_ROWS nodes. */
 int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out);
 /* TreeDecoder::tree_logits_keep_kv (mod.rs:196-210; quantized_llama.rs:341-394);
  * logits_out: n x V (may be NULL), hidden_out: n x hidden (may be NULL).
@@ -308,7 +308,8 @@ int spec_medusa_num_heads(const spec_model* m);
  * commits_out (room for n_heads + 1) receives the committed tokens, *n_out
  * their count, hidden_out (hidden_size floats) the hidden row of the last
  * committed token: the next round's `hidden`.  History and KV afterwards are
- * those of the reference's observe(committed).  A tree over SPEC_MAX_ROWS
+ * those of the reference's observe(committed).  Trees over SPEC_MAX_ROWS
+ * nodes run as ancestor-closed chunks (spec_tree_logits); one over 16384
  * nodes returns SPEC_ERR_UNSUPPORTED with the state unchanged. */
 int spec_medusa_round(spec_model* m, const float* hidden, int top_k, int topology, int acceptance, float epsilon,
                       float delta, int budget, uint32_t* commits_out, int* n_out, float* hidden_out);

@@ -158,6 +158,8 @@ def _medusa_round_by_trait_calls(pkg, dec, hidden, k, topology, acceptance, eps,
     ("llama_q4km", 4, 2, "cartesian", "greedy"),
     ("qwen_q4km", 3, 3, "cartesian", "typical"),
     ("llama_bf16", 4, 2, "greedy", "typical"),
+    ("llama_q4km", 4, 3, "cartesian", "greedy"),   # 121 nodes: ancestor-closed chunks
+    ("qwen_q4km", 4, 3, "cartesian", "typical"),
 ])
 def test_native_medusa_round_equals_trait_calls(pkg, tiny_gguf, name, heads, k, topology, acceptance):
     """spec_medusa_round against the same rounds made of trait calls: equal
@@ -188,11 +190,42 @@ def test_native_medusa_round_equals_trait_calls(pkg, tiny_gguf, name, heads, k, 
             break
     # The accepted path is committed whole; the budget only withholds the bonus (:786-800).
     assert total >= max_new and len(a.history()) == len(prompt) + total
-    # A Cartesian tree over SPEC_MAX_ROWS nodes is refused with the state unchanged.
+    # A Cartesian tree over 16384 nodes is refused with the state unchanged.
     if topology == "cartesian":
         hist, kv = a.history(), a.kv_len()
         with pytest.raises(pkg.SpecError):
-            a.medusa_round(ha, 8, "cartesian")
+            a.medusa_round(ha, 64, "cartesian")
         assert a.history() == hist and a.kv_len() == kv
     a.close()
     b.close()
+
+
+@pytest.mark.parametrize("name", ["llama_q4km", "qwen_q4km"])
+def test_verify_tree_typical_over_max_rows(pkg, tiny_gguf, accept, name):
+    """Typical acceptance over a 121-node tree (chunks of at most 64 rows):
+    the same decisions as the restated rule on the chunked forward's rows."""
+    dec = pkg.B200Decoder.from_gguf(tiny_gguf(name), max_ctx=256)
+    V = dec.vocab_size()
+    rng = np.random.default_rng(43)
+    prompt = rng.integers(0, V, size=15).tolist()
+    dec.observe(prompt)
+    tokens, parents, frontier = [prompt[-1]], [0], [0]
+    for _ in range(4):  # every node: its row's top two tokens and a random one
+        rows, _ = dec.tree_logits_keep_kv(pkg.DraftTree(tokens, parents))
+        nxt = []
+        for f in frontier:
+            for t in np.argsort(-rows[f], kind="stable")[:2].tolist() + [int(rng.integers(0, V))]:
+                tokens.append(int(t))
+                parents.append(f)
+                nxt.append(len(tokens) - 1)
+        frontier = nxt
+    tree = pkg.DraftTree(tokens, parents)
+    assert len(tree) > 64
+    rows, _ = dec.tree_logits_keep_kv(tree)
+    lengths = set()
+    for eps, delta in [(0.0, 1.0), (0.001, 0.5), (0.01, 0.3), (0.3, 0.3)]:
+        want = accept.typical_tree_accept(tokens, parents, rows, eps, delta)
+        assert dec.verify_tree_typical(tree, eps, delta) == want, (eps, delta)
+        lengths.add(len(want[0]))
+    assert max(lengths) >= 3, lengths
+    dec.close()
