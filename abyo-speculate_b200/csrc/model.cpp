@@ -3777,17 +3777,23 @@ int spec_eagle_round(spec_model* m, const float* hidden, int depth, int top_k, i
   std::vector<float> lps((size_t)depth * top_k);
   int rc = spec_eagle_draft(m, hidden, root, (int)m->history.size(), depth, top_k, ids.data(), lps.data());
   if (rc != SPEC_OK) return rc;
-  // 3. The tree.
-  uint32_t tok[kMaxRows];
-  int32_t par[kMaxRows];
+  // 3. The tree.  Over kMaxRows nodes the tree forward runs as
+  // ancestor-closed chunks (spec_verify_tree_greedy) and the bonus is always
+  // observed (no per-node hidden rows are kept).
+  constexpr int kMaxEagleNodes = 1 << 14;
+  std::vector<uint32_t> tok(kMaxEagleNodes);
+  std::vector<int32_t> par(kMaxEagleNodes);
   int n = 0;
-  rc = spec_eagle_build_tree(root, ids.data(), lps.data(), depth, top_k, max_tree_nodes, tok, par, kMaxRows, &n);
+  rc = spec_eagle_build_tree(root, ids.data(), lps.data(), depth, top_k, max_tree_nodes, tok.data(), par.data(),
+                             kMaxEagleNodes, &n);
   if (rc != SPEC_OK) return m->fail(rc, g_load_error.empty() ? "EAGLE tree" : g_load_error);
+  const bool small = n <= kMaxRows;
   // 4-6. Tree forward keeping KV, greedy walk, bonus (per-node hidden kept).
-  int32_t best[kMaxRows];
+  std::vector<int32_t> best((size_t)n + 1);
   int len = 0;
   uint32_t bonus = 0;
-  rc = verify_tree_greedy_core(m, tok, par, n, best, &len, &bonus, true);
+  rc = small ? verify_tree_greedy_core(m, tok.data(), par.data(), n, best.data(), &len, &bonus, true)
+             : spec_verify_tree_greedy(m, tok.data(), par.data(), n, best.data(), &len, &bonus);
   if (rc != SPEC_OK) return rc;
   auto is_eos = [&](uint32_t t) {
     for (int i = 0; i < n_eos; ++i)
@@ -3809,11 +3815,11 @@ int spec_eagle_round(spec_model* m, const float* hidden, int depth, int top_k, i
   // 7. Commit the accepted path.
   if (eos_at >= 0 && eos_at < len - 1) {
     // An EOS on the accepted path: keep the root and the path up to it.
-    return spec_commit_tree_path(m, tok, par, n, best, eos_at + 2);
+    return spec_commit_tree_path(m, tok.data(), par.data(), n, best.data(), eos_at + 2);
   }
   const int deepest = best[len - 1];
   int bn = -1;
-  if (!strict_root)
+  if (!strict_root && small)
     for (int i = 1; i < n; ++i)
       if (par[i] == deepest && tok[i] == bonus) {
         bn = i;
@@ -3826,9 +3832,9 @@ int spec_eagle_round(spec_model* m, const float* hidden, int depth, int top_k, i
                                      (size_t)m->cfg.hidden * 4, cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return m->fail(SPEC_ERR_CUDA, cuda_msg(e, "tree hidden row"));
     best[len++] = bn;
-    return spec_commit_tree_path(m, tok, par, n, best, len);
+    return spec_commit_tree_path(m, tok.data(), par.data(), n, best.data(), len);
   }
-  rc = spec_commit_tree_path(m, tok, par, n, best, len);
+  rc = spec_commit_tree_path(m, tok.data(), par.data(), n, best.data(), len);
   if (rc == SPEC_OK) rc = spec_observe_returning_last_hidden(m, &bonus, 1, hidden_out);
   return rc;
 }

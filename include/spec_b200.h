@@ -177,8 +177,8 @@ int spec_rollback_to(spec_model* m, int len);
  * take such trees too: the KV window then holds the last chunk's rows
  * (spec_kv_len = prefix + that chunk's size), and the commit, whose accepted
  * nodes must then form a path from the root, re-runs the path's chunk when
- * the window holds another.  spec_verify_tree_typical and spec_medusa_round
- * do the same; spec_eagle_round takes at most SPEC_MAX_ROWS nodes. */
+ * the window holds another.  spec_verify_tree_typical, spec_medusa_round
+ * and spec_eagle_round do the same. */
 int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* parents, int n, float* out);
 /* TreeDecoder::tree_logits_keep_kv (mod.rs:196-210; quantized_llama.rs:341-394);
  * logits_out: n x V (may be NULL), hidden_out: n x hidden (may be NULL).
@@ -254,8 +254,10 @@ int spec_eagle_build_tree(uint32_t root, const int32_t* ids, const float* logpro
 /* One EAGLE-2 round at temperature 0 as one native call (run_eagle's loop
  * body, methods/eagle.rs:531-731), on a target with an attached EAGLE head:
  *   the draft loop from `hidden` (the target's last hidden row [H]) with the
- *   last committed token as root; the tree of spec_eagle_build_tree (at most
- *   SPEC_MAX_ROWS nodes); the tree forward keeping KV and the greedy walk of
+ *   last committed token as root; the tree of spec_eagle_build_tree (up to
+ *   16384 nodes; over SPEC_MAX_ROWS it runs as ancestor-closed chunks, as
+ *   spec_tree_logits does, and the bonus is always observed); the tree
+ *   forward keeping KV and the greedy walk of
  *   spec_verify_tree_greedy; committed = the accepted path's tokens + the
  *   bonus, cut after the first token of eos_ids;
  *   the KV commit (:680-727): an EOS on the path keeps the path up to it;

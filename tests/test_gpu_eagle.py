@@ -108,7 +108,8 @@ def _py_eagle_round(pkg, dec, hidden, depth, k, max_nodes, strict, eos):
     return committed, dec.observe_returning_last_hidden([int(bonus)]), eos_at is not None, False
 
 
-@pytest.mark.parametrize("depth,k,max_nodes,strict", [(2, 4, 0, False), (4, 4, 40, False), (3, 8, 60, True)])
+@pytest.mark.parametrize("depth,k,max_nodes,strict", [(2, 4, 0, False), (4, 4, 40, False), (3, 8, 60, True),
+                                                      (3, 6, 0, True)])  # 259 nodes: ancestor-closed chunks
 def test_native_eagle_round_equals_trait_calls(pkg, tiny_gguf, depth, k, max_nodes, strict):
     """spec_eagle_round (draft loop, tree, tree forward, walk, KV commit in
     one call) against the same round made of the trait calls in the
