@@ -1155,6 +1155,20 @@ void fill_step_causal(spec_model* m, const uint32_t* toks, int M, int P) {
 // forward_advance_logits (quantized_llama.rs:137-158): forwards `n` tokens
 // at cache_len, chunked by kMaxRows; when rows_out != nullptr it receives
 // all n logits rows.  On success cache_len += n and the last row is cached.
+// True when [p, p + bytes) is page-locked host memory the GPU can copy into
+// directly (cudaHostAlloc / cudaHostRegister / a pinned torch tensor).
+bool host_pinned(const void* p, size_t bytes) {
+  auto one = [](const void* q) {
+    cudaPointerAttributes a;
+    if (cudaPointerGetAttributes(&a, q) != cudaSuccess) {
+      cudaGetLastError();
+      return false;
+    }
+    return a.type == cudaMemoryTypeHost;
+  };
+  return one(p) && one(static_cast<const uint8_t*>(p) + bytes - 1);
+}
+
 int forward_advance(spec_model* m, const uint32_t* ids, int n, float* rows_out, bool want_logits = true) {
   if (n <= 0) return m->fail(SPEC_ERR_INVALID, "forward_advance with empty tokens");
   if (m->cache_len + n > m->t_max)
@@ -1163,6 +1177,10 @@ int forward_advance(spec_model* m, const uint32_t* ids, int n, float* rows_out, 
   for (int i = 0; i < n; ++i)
     if (ids[i] >= (uint32_t)m->cfg.vocab) return m->fail(SPEC_ERR_INVALID, "token id out of range");
   const int start = m->cache_len;
+  const size_t V = (size_t)m->cfg.vocab;
+  // Logits rows go straight into a pinned caller buffer; otherwise through
+  // the model's pinned staging rows.
+  const bool direct = rows_out && host_pinned(rows_out, (size_t)n * V * 4);
   int done = 0;
   while (done < n) {
     const int M = std::min(kMaxRows, n - done);
@@ -1171,14 +1189,16 @@ int forward_advance(spec_model* m, const uint32_t* ids, int n, float* rows_out, 
     const int flags = (rows_out || (last_chunk && want_logits)) ? F_LOGITS : 0;
     int rc = run_forward(m, M, flags);
     if (rc == SPEC_OK && rows_out) {
-      cudaMemcpyAsync(m->logits_host, m->logits, (size_t)M * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+      float* dst = direct ? rows_out + (size_t)done * V : m->logits_host;
+      const cudaError_t e = cudaMemcpyAsync(dst, m->logits, (size_t)M * V * 4, cudaMemcpyDeviceToHost, m->stream);
+      if (e != cudaSuccess) rc = m->fail(SPEC_ERR_CUDA, cuda_msg(e, "logits rows"));
     }
     if (rc == SPEC_OK) rc = finish(m);
     if (rc != SPEC_OK) {
       m->cache_len = start;  // KV rows beyond cache_len are ignored: state unchanged
       return rc;
     }
-    if (rows_out) memcpy(rows_out + (size_t)done * m->cfg.vocab, m->logits_host, (size_t)M * m->cfg.vocab * 4);
+    if (rows_out && !direct) memcpy(rows_out + (size_t)done * V, m->logits_host, (size_t)M * V * 4);
     done += M;
   }
   m->cache_len = start + n;

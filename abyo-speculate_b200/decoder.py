@@ -159,9 +159,16 @@ class B200Decoder:
         self._check(self._lib.spec_next_logits(self._h, _ptr(out, ctypes.c_float)))
         return out
 
-    def batched_logits(self, drafts: Sequence[int]) -> np.ndarray:
+    def batched_logits(self, drafts: Sequence[int], out: Optional[np.ndarray] = None) -> np.ndarray:
+        """Decoder::batched_logits.  `out` (optional): a C-contiguous float32
+        (k+1, V) array to fill; when it is page-locked (e.g. a pinned torch
+        tensor's .numpy()), the rows are copied into it by DMA directly."""
         a = _u32(drafts)
-        out = np.empty((a.size + 1, self._vocab), dtype=np.float32)
+        shape = (a.size + 1, self._vocab)
+        if out is None:
+            out = np.empty(shape, dtype=np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags["C_CONTIGUOUS"]:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {shape}")
         self._check(self._lib.spec_batched_logits(self._h, _ptr(a, ctypes.c_uint32), a.size,
                                                   _ptr(out, ctypes.c_float)))
         return out

@@ -9,7 +9,8 @@ the library's stream over K back-to-back device-side greedy verifies
 (spec_verify_greedy: H2D of the step parameters, one CUDA-graph replay of the
 whole forward, device argmax, k+1 ints back).  `e2e` = the same metric through
 spec_batched_logits with host draft tokens in and the 5 x 128256 f32 logits
-rows copied back to host every step (the reference-facing Decoder call).
+rows copied back every step into a pinned host array (the reference-facing
+Decoder call).
 Multi-GPU: one process per GPU, time = max over ranks.  By default the N
 GPUs hold ONE model, tensor parallel (each rank holds its heads and FFN slice;
 the o and down outputs are summed across the ranks inside the GEMV epilogue
@@ -708,13 +709,15 @@ def run_b200(args, ws, rank, local, dist):
     r1.record(stream)
     torch.cuda.synchronize()
     rj_ms = max_over_ranks(dist, r0.elapsed_time(r1))
-    # e2e: host drafts in, host logits rows out (spec_batched_logits)
+    # e2e: host drafts in, host logits rows out (spec_batched_logits) into a
+    # pinned host buffer, which the library fills by DMA
+    e2e_rows = torch.empty((K_DRAFT + 1, CFG["vocab"]), dtype=torch.float32, pin_memory=True).numpy()
     barrier(dist)
     torch.cuda.synchronize()
     f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     f0.record(stream)
     for i in range(args.steps):
-        dec.batched_logits(drafts_all[i])
+        dec.batched_logits(drafts_all[i], out=e2e_rows)
         dec.rollback_to(KV_LEN)
     f1.record(stream)
     torch.cuda.synchronize()
@@ -781,7 +784,9 @@ def run_b200(args, ws, rank, local, dist):
                      "peak_kind": peak_kind},
         "kernels": per_kind,
         "e2e": {"value": round(e2e_value, 3), "unit": UNIT, "h2d_bytes_per_step": 1296 + 4 * K_DRAFT,
-                "d2h_bytes_per_step": (K_DRAFT + 1) * CFG["vocab"] * 4 + 4},
+                "d2h_bytes_per_step": (K_DRAFT + 1) * CFG["vocab"] * 4 + 4,
+                "note": "spec_batched_logits per step: host draft ids in, the 5 logits rows DMA'd into a pinned "
+                        "host array (B200Decoder.batched_logits(drafts, out=pinned))"},
         "tree_acceptance_31": tree_block,
         "rejection_t1": {"value": round(models * args.steps / (rj_ms / 1e3), 3), "unit": UNIT,
                          "verify_us": round(rj_ms / args.steps * 1e3, 2),

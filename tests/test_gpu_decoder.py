@@ -462,3 +462,25 @@ def test_fused_attention_matches_attention_kernels(pkg, tiny_gguf, name, monkeyp
     assert fused.kernels_per_forward(5) < sep.kernels_per_forward(5)
     fused.close()
     sep.close()
+
+
+def test_batched_logits_into_pinned_buffer(pkg, tiny_gguf):
+    """Logits rows DMA'd into a page-locked caller array equal the rows copied
+    through the library's staging buffer, bit for bit; a wrongly shaped
+    array is refused before the call."""
+    torch = pytest.importorskip("torch")
+    dec = pkg.B200Decoder.from_gguf(tiny_gguf("llama_q4km"), max_ctx=256)
+    V = dec.vocab_size()
+    prompt = _prompt(V, 20, 3)
+    dec.observe(prompt)
+    drafts = [5, 6, 7, 8]
+    a = dec.batched_logits(drafts)
+    dec.rollback_to(len(prompt))
+    buf = torch.empty((5, V), dtype=torch.float32, pin_memory=True).numpy()
+    b = dec.batched_logits(drafts, out=buf)
+    assert b is buf and np.array_equal(a.view(np.uint32), buf.view(np.uint32))
+    dec.rollback_to(len(prompt))
+    with pytest.raises(ValueError):
+        dec.batched_logits(drafts, out=np.empty((4, V), dtype=np.float32))
+    assert dec.history() == prompt
+    dec.close()
