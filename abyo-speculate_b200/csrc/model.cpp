@@ -2192,11 +2192,13 @@ int spec_tree_logits(spec_model* m, const uint32_t* tokens, const int32_t* paren
   const int prefix = (int)m->history.size() - 1;
   if (prefix > pre) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
   rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS);
+  const size_t lbytes = (size_t)n * m->cfg.vocab * 4;
+  const bool direct = host_pinned(out, lbytes);  // DMA straight into a pinned caller array
   if (rc == SPEC_OK)
-    cudaMemcpyAsync(m->logits_host, m->logits, (size_t)n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+    cudaMemcpyAsync(direct ? out : m->logits_host, m->logits, lbytes, cudaMemcpyDeviceToHost, m->stream);
   if (rc == SPEC_OK) rc = finish(m);
   if (rc != SPEC_OK) return rc;
-  memcpy(out, m->logits_host, (size_t)n * m->cfg.vocab * 4);
+  if (!direct) memcpy(out, m->logits_host, lbytes);
   // Restore (quantized_llama.rs:306-323): truncate to prefix and re-forward
   // the root; its logits replace row 0 and become the cached next logits.
   m->cache_len = prefix;
@@ -2247,15 +2249,18 @@ int spec_tree_logits_keep_kv(spec_model* m, const uint32_t* tokens, const int32_
   const int prefix = (int)m->history.size() - 1;
   if (prefix > pre) return m->fail(SPEC_ERR_CACHE_ROLLBACK, "truncate beyond cache length");
   rc = tree_forward(m, tokens, parents, n, prefix, F_LOGITS | F_HIDDEN);
+  const size_t lbytes = (size_t)n * m->cfg.vocab * 4, hbytes = (size_t)n * m->cfg.hidden * 4;
+  const bool ldirect = logits_out && host_pinned(logits_out, lbytes);  // DMA into pinned caller arrays
+  const bool hdirect = hidden_out && host_pinned(hidden_out, hbytes);
   if (rc == SPEC_OK && logits_out)
-    cudaMemcpyAsync(m->logits_host, m->logits, (size_t)n * m->cfg.vocab * 4, cudaMemcpyDeviceToHost, m->stream);
+    cudaMemcpyAsync(ldirect ? logits_out : m->logits_host, m->logits, lbytes, cudaMemcpyDeviceToHost, m->stream);
   if (rc == SPEC_OK && hidden_out)
-    cudaMemcpyAsync(m->hidden_host, m->hidden_out, (size_t)n * m->cfg.hidden * 4, cudaMemcpyDeviceToHost, m->stream);
+    cudaMemcpyAsync(hdirect ? hidden_out : m->hidden_host, m->hidden_out, hbytes, cudaMemcpyDeviceToHost, m->stream);
   if (rc == SPEC_OK) rc = finish(m);
   if (rc != SPEC_OK) return rc;
   m->cache_len = prefix + n;
-  if (logits_out) memcpy(logits_out, m->logits_host, (size_t)n * m->cfg.vocab * 4);
-  if (hidden_out) memcpy(hidden_out, m->hidden_host, (size_t)n * m->cfg.hidden * 4);
+  if (logits_out && !ldirect) memcpy(logits_out, m->logits_host, lbytes);
+  if (hidden_out && !hdirect) memcpy(hidden_out, m->hidden_host, hbytes);
   return SPEC_OK;
 }
 

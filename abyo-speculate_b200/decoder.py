@@ -181,9 +181,15 @@ class B200Decoder:
     def _tree_arrays(tree: DraftTree) -> Tuple[np.ndarray, np.ndarray]:
         return _u32(tree.tokens()), np.ascontiguousarray(np.asarray(tree.parents(), dtype=np.int32))
 
-    def tree_logits(self, tree: DraftTree) -> np.ndarray:
+    def tree_logits(self, tree: DraftTree, out: Optional[np.ndarray] = None) -> np.ndarray:
+        """TreeDecoder::tree_logits; `out` as for batched_logits ((n, V) float32,
+        filled by DMA when page-locked and the tree fits one forward)."""
         t, p = self._tree_arrays(tree)
-        out = np.empty((t.size, self._vocab), dtype=np.float32)
+        shape = (t.size, self._vocab)
+        if out is None:
+            out = np.empty(shape, dtype=np.float32)
+        elif out.shape != shape or out.dtype != np.float32 or not out.flags["C_CONTIGUOUS"]:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {shape}")
         self._check(self._lib.spec_tree_logits(self._h, _ptr(t, ctypes.c_uint32), _ptr(p, ctypes.c_int32), t.size,
                                                _ptr(out, ctypes.c_float)))
         return out

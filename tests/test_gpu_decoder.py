@@ -483,4 +483,9 @@ def test_batched_logits_into_pinned_buffer(pkg, tiny_gguf):
     with pytest.raises(ValueError):
         dec.batched_logits(drafts, out=np.empty((4, V), dtype=np.float32))
     assert dec.history() == prompt
+    tree = pkg.DraftTree([prompt[-1], 5, 6, 7, 8, 9], [0, 0, 0, 1, 1, 2])
+    t0 = dec.tree_logits(tree)
+    tbuf = torch.empty((6, V), dtype=torch.float32, pin_memory=True).numpy()
+    t1 = dec.tree_logits(tree, out=tbuf)
+    assert t1 is tbuf and np.array_equal(t0.view(np.uint32), tbuf.view(np.uint32))
     dec.close()
