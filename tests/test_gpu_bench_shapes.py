@@ -155,6 +155,47 @@ def test_llama8b_vocab_typical_tree(pkg, accept, llama8b):
     dec.reset()
 
 
+def test_llama8b_shapes_tree_over_max_rows(pkg, oracle, llama8b):
+    """A 121-node tree (4 levels of 3: Medusa's 4 heads x top-3) over the
+    Llama-3-8B-shaped model, 128256-wide rows: ancestor-closed chunks of at
+    most 64 rows against the oracle's single tree forward, then a kept-KV
+    forward, the greedy verify and the commit of its path (next logits after
+    the bonus against the oracle)."""
+    dec, ref, _ = llama8b
+    V = LLAMA8B["vocab"]
+    rng = np.random.default_rng(17)
+    dec.reset()
+    ref.reset()
+    prompt = rng.integers(0, V, size=96).tolist()
+    dec.observe(prompt)
+    ref.observe(prompt)
+    tokens, parents, prev = [prompt[-1]], [0], [0]
+    for _ in range(4):
+        layer = []
+        cands = rng.integers(0, V, size=3).tolist()
+        for p in prev:
+            for c in cands:
+                tokens.append(int(c))
+                parents.append(p)
+                layer.append(len(tokens) - 1)
+        prev = layer
+    tree = pkg.DraftTree(tokens, parents)
+    a = dec.tree_logits(tree)
+    b = ref.tree_logits(tokens, parents)
+    assert np.abs(a - b).max() <= TOL
+    assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+    best, bonus = dec.verify_tree_greedy(tree)
+    ref.tree_logits_keep_kv(tokens, parents)
+    dec.commit_tree_path(tree, best)
+    ref.commit_tree_path(tokens, parents, best)
+    assert dec.history() == ref.history and dec.kv_len() == ref.cache_len
+    dec.observe([int(bonus)])
+    ref.observe([int(bonus)])
+    assert np.abs(dec.next_logits() - ref.next_logits()).max() <= TOL
+    dec.reset()
+    ref.reset()
+
+
 QWEN7B_1L = dict(arch="qwen2", n_layers=1, hidden=3584, n_heads=28, n_kv_heads=4, ffn=18944, vocab=4096,
                  rope_theta=1e6, eps=1e-6)
 
